@@ -1,0 +1,347 @@
+// Python bindings for the flare_b200 native kernels. Kernels take raw device
+// pointers (Python passes tensor.data_ptr()) and run on PyTorch's current CUDA
+// stream, so they compose with torch streams, events and CUDA graph capture.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <pybind11/stl.h>
+
+#include "common.cuh"
+#include "dense.cuh"
+#include "embedding.cuh"
+#include "gemm.cuh"
+#include "sparse_ops.cuh"
+
+namespace flare {
+void* dev_malloc(size_t bytes);
+void dev_free(void* p);
+std::vector<char> ipc_get_handle(void* p);
+void* ipc_open_handle(const std::vector<char>& bytes);
+void ipc_close_handle(void* p);
+bool can_access_peer(int dev, int peer);
+}  // namespace flare
+
+namespace py = pybind11;
+using flare::kBF16;
+
+namespace {
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+template <typename T>
+T* P(uintptr_t v) {
+  return reinterpret_cast<T*>(v);
+}
+
+template <typename T>
+T get(const py::dict& d, const char* k) {
+  if (!d.contains(k)) throw std::runtime_error(std::string("missing parameter: ") + k);
+  return d[k].cast<T>();
+}
+
+template <typename T>
+T get_or(const py::dict& d, const char* k, T dflt) {
+  return d.contains(k) ? d[k].cast<T>() : dflt;
+}
+
+flare::SparseOptParams parse_sparse_opt(const py::dict& d) {
+  flare::SparseOptParams o{};
+  o.kind = get<int>(d, "kind");
+  o.lr = get<float>(d, "lr");
+  o.beta1 = get_or<float>(d, "beta1", 0.9f);
+  o.beta2 = get_or<float>(d, "beta2", 0.999f);
+  o.eps = get_or<float>(d, "eps", 1e-8f);
+  o.weight_decay = get_or<float>(d, "weight_decay", 0.f);
+  o.bias_corr1 = get_or<float>(d, "bias_corr1", 1.f);
+  o.bias_corr2 = get_or<float>(d, "bias_corr2", 1.f);
+  o.lr_policy = get_or<int>(d, "lr_policy", 0);
+  o.policy_a = get_or<float>(d, "policy_a", 0.f);
+  o.policy_b = get_or<float>(d, "policy_b", 1.f);
+  o.lut = P<const float>(get_or<uintptr_t>(d, "lut", 0));
+  o.lut_len = get_or<int>(d, "lut_len", 0);
+  o.state_row = P<float>(get_or<uintptr_t>(d, "state_row", 0));
+  o.state_m = P<float>(get_or<uintptr_t>(d, "state_m", 0));
+  o.state_v = P<float>(get_or<uintptr_t>(d, "state_v", 0));
+  o.score = P<float>(get_or<uintptr_t>(d, "score", 0));
+  o.step_ptr = P<const int>(get_or<uintptr_t>(d, "step_ptr", 0));
+  return o;
+}
+
+flare::AdamParams parse_adam(const py::dict& d) {
+  flare::AdamParams o{};
+  o.kind = get_or<int>(d, "kind", 0);
+  o.lr = get<float>(d, "lr");
+  o.beta1 = get_or<float>(d, "beta1", 0.9f);
+  o.beta2 = get_or<float>(d, "beta2", 0.999f);
+  o.eps = get_or<float>(d, "eps", 1e-8f);
+  o.weight_decay = get_or<float>(d, "weight_decay", 0.f);
+  o.decoupled = get_or<int>(d, "decoupled", 0);
+  o.nesterov = get_or<int>(d, "nesterov", 0);
+  o.bias_corr1 = get_or<float>(d, "bias_corr1", 1.f);
+  o.bias_corr2 = get_or<float>(d, "bias_corr2", 1.f);
+  o.step_ptr = P<const int>(get_or<uintptr_t>(d, "step_ptr", 0));
+  return o;
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "flare_b200 native kernels (sm_100a)";
+
+  m.def("device_sm_count", &flare::device_sm_count);
+  m.def("launch_count", &flare::launch_count);
+  m.def("increment_counter", [](uintptr_t p) { flare::increment_counter(P<int>(p), cur_stream()); });
+
+  m.def(
+      "gemm",
+      [](uintptr_t A, int64_t lda, bool a_mn, uintptr_t B, int64_t ldb, bool b_mn, int M, int N, int K, uintptr_t C,
+         int64_t ldc, int c_dtype, bool accumulate, uintptr_t bias, int act, float alpha, uintptr_t mask,
+         int64_t ldm, uintptr_t colsum, uintptr_t status, uint64_t timeout_ns, int bn) {
+        flare::GemmArgs a{};
+        a.A = P<const void>(A);
+        a.lda = lda;
+        a.a_mn = a_mn;
+        a.B = P<const void>(B);
+        a.ldb = ldb;
+        a.b_mn = b_mn;
+        a.M = M;
+        a.N = N;
+        a.K = K;
+        a.C = P<void>(C);
+        a.ldc = ldc;
+        a.c_dtype = c_dtype;
+        a.accumulate = accumulate;
+        a.bias = P<const __nv_bfloat16>(bias);
+        a.act = act;
+        a.alpha = alpha;
+        a.mask = P<const void>(mask);
+        a.ldm = ldm;
+        a.colsum = P<float>(colsum);
+        a.status = P<int>(status);
+        a.timeout_ns = timeout_ns;
+        flare::gemm_bf16_tcgen05(a, bn, cur_stream());
+      },
+      py::arg("A"), py::arg("lda"), py::arg("a_mn"), py::arg("B"), py::arg("ldb"), py::arg("b_mn"), py::arg("M"),
+      py::arg("N"), py::arg("K"), py::arg("C"), py::arg("ldc"), py::arg("c_dtype"), py::arg("accumulate"),
+      py::arg("bias"), py::arg("act"), py::arg("alpha"), py::arg("mask"), py::arg("ldm"), py::arg("colsum"),
+      py::arg("status"), py::arg("timeout_ns"), py::arg("bn") = 0);
+
+  m.def("emb_forward", [](const py::dict& d) {
+    flare::EmbFwdParams p{};
+    p.shards = P<const flare::ShardDesc>(get<uintptr_t>(d, "shards"));
+    p.num_shards = get<int>(d, "num_shards");
+    p.world = get<int>(d, "world");
+    p.rank = get<int>(d, "rank");
+    p.Bl = get<int>(d, "Bl");
+    p.F = get<int>(d, "F");
+    p.peer_offsets = P<const int* const>(get<uintptr_t>(d, "peer_offsets"));
+    p.peer_values = P<const int* const>(get<uintptr_t>(d, "peer_values"));
+    p.peer_out = P<void* const>(get<uintptr_t>(d, "peer_out"));
+    p.out_stride = get<int64_t>(d, "out_stride");
+    p.weights = P<const void>(get<uintptr_t>(d, "weights"));
+    p.w_dtype = get<int>(d, "w_dtype");
+    p.out_dtype = get_or<int>(d, "out_dtype", kBF16);
+    p.vec = get_or<int>(d, "vec", 1);
+    p.stage_ids = P<int>(get<uintptr_t>(d, "stage_ids"));
+    p.stage_bag = P<int>(get<uintptr_t>(d, "stage_bag"));
+    p.stage_count = P<int>(get<uintptr_t>(d, "stage_count"));
+    p.stage_len = P<int>(get<uintptr_t>(d, "stage_len"));
+    p.stage_cap = get<int64_t>(d, "stage_cap");
+    p.flags_local = P<uint32_t>(get_or<uintptr_t>(d, "flags_local", 0));
+    p.peer_flags = P<uint32_t* const>(get_or<uintptr_t>(d, "peer_flags", 0));
+    p.flag_in = get_or<int>(d, "flag_in", 0);
+    p.flag_out = get_or<int>(d, "flag_out", 0);
+    p.epoch_ctr = P<uint32_t>(get_or<uintptr_t>(d, "epoch_ctr", 0));
+    p.block_counter = P<unsigned>(get_or<uintptr_t>(d, "block_counter", 0));
+    p.status = P<int>(get_or<uintptr_t>(d, "status", 0));
+    p.timeout_ns = get_or<uint64_t>(d, "timeout_ns", 2000000000ull);
+    flare::emb_forward(p, get<int>(d, "grid"), cur_stream());
+  });
+
+  m.def("emb_backward", [](const py::dict& d) {
+    flare::EmbBwdParams p{};
+    p.shards = P<const flare::ShardDesc>(get<uintptr_t>(d, "shards"));
+    p.num_shards = get<int>(d, "num_shards");
+    p.world = get<int>(d, "world");
+    p.rank = get<int>(d, "rank");
+    p.Bl = get<int>(d, "Bl");
+    p.peer_grad = P<const void* const>(get<uintptr_t>(d, "peer_grad"));
+    p.out_stride = get<int64_t>(d, "out_stride");
+    p.grad_dtype = get_or<int>(d, "grad_dtype", kBF16);
+    p.grad_stage = P<void>(get<uintptr_t>(d, "grad_stage"));
+    p.grad_stage_ld = get<int64_t>(d, "grad_stage_ld");
+    p.stage_ids = P<const int>(get<uintptr_t>(d, "stage_ids"));
+    p.stage_bag = P<const int>(get<uintptr_t>(d, "stage_bag"));
+    p.stage_count = P<const int>(get<uintptr_t>(d, "stage_count"));
+    p.stage_len = P<const int>(get<uintptr_t>(d, "stage_len"));
+    p.stage_cap = get<int64_t>(d, "stage_cap");
+    p.weights = P<void>(get<uintptr_t>(d, "weights"));
+    p.w_dtype = get<int>(d, "w_dtype");
+    p.row_count = P<int>(get<uintptr_t>(d, "row_count"));
+    p.row2u = P<int>(get<uintptr_t>(d, "row2u"));
+    p.uniq_row = P<int64_t>(get<uintptr_t>(d, "uniq_row"));
+    p.uniq_shard = P<int>(get<uintptr_t>(d, "uniq_shard"));
+    p.num_unique = P<int>(get<uintptr_t>(d, "num_unique"));
+    p.seg_start = P<int>(get<uintptr_t>(d, "seg_start"));
+    p.block_sums = P<int>(get<uintptr_t>(d, "block_sums"));
+    p.occ = P<int>(get<uintptr_t>(d, "occ"));
+    p.carry = P<float>(get<uintptr_t>(d, "carry"));
+    p.span_u = P<int>(get<uintptr_t>(d, "span_u"));
+    p.chunk = get<int>(d, "chunk");
+    p.max_occ = get<int64_t>(d, "max_occ");
+    p.opt = parse_sparse_opt(get<py::dict>(d, "opt"));
+    p.flags_local = P<uint32_t>(get_or<uintptr_t>(d, "flags_local", 0));
+    p.peer_flags = P<uint32_t* const>(get_or<uintptr_t>(d, "peer_flags", 0));
+    p.flag_in = get_or<int>(d, "flag_in", 0);
+    p.epoch_ctr = P<uint32_t>(get_or<uintptr_t>(d, "epoch_ctr", 0));
+    p.block_counter = P<unsigned>(get_or<uintptr_t>(d, "block_counter", 0));
+    p.status = P<int>(get_or<uintptr_t>(d, "status", 0));
+    p.timeout_ns = get_or<uint64_t>(d, "timeout_ns", 2000000000ull);
+    flare::emb_backward(p, get<int>(d, "ncols_max"), get<int>(d, "grid"), cur_stream());
+  });
+
+  auto parse_inter = [](const py::dict& d) {
+    flare::InteractionParams p{};
+    p.B = get<int>(d, "B");
+    p.F = get<int>(d, "F");
+    p.D = get<int>(d, "D");
+    p.bot = P<const __nv_bfloat16>(get<uintptr_t>(d, "bot"));
+    p.bot_ld = get<int64_t>(d, "bot_ld");
+    p.emb = P<const __nv_bfloat16>(get<uintptr_t>(d, "emb"));
+    p.emb_ld = get<int64_t>(d, "emb_ld");
+    p.out = P<__nv_bfloat16>(get_or<uintptr_t>(d, "out", 0));
+    p.dout = P<const __nv_bfloat16>(get_or<uintptr_t>(d, "dout", 0));
+    p.out_ld = get<int64_t>(d, "out_ld");
+    p.dbot = P<__nv_bfloat16>(get_or<uintptr_t>(d, "dbot", 0));
+    p.dbot_ld = get_or<int64_t>(d, "dbot_ld", 0);
+    p.demb = P<__nv_bfloat16>(get_or<uintptr_t>(d, "demb", 0));
+    p.demb_ld = get_or<int64_t>(d, "demb_ld", 0);
+    p.relu_mask_bot = get_or<int>(d, "relu_mask_bot", 1);
+    return p;
+  };
+  m.def("interaction_forward", [parse_inter](const py::dict& d) { flare::interaction_forward(parse_inter(d), cur_stream()); });
+  m.def("interaction_backward", [parse_inter](const py::dict& d) { flare::interaction_backward(parse_inter(d), cur_stream()); });
+
+  m.def("head_bce", [](const py::dict& d) {
+    flare::HeadBceParams p{};
+    p.B = get<int>(d, "B");
+    p.H = get<int>(d, "H");
+    p.T = get<int>(d, "T");
+    p.h = P<const __nv_bfloat16>(get<uintptr_t>(d, "h"));
+    p.h_ld = get<int64_t>(d, "h_ld");
+    p.w = P<const __nv_bfloat16>(get<uintptr_t>(d, "w"));
+    p.bias = P<const __nv_bfloat16>(get<uintptr_t>(d, "bias"));
+    p.labels = P<const float>(get<uintptr_t>(d, "labels"));
+    p.label_ld = get<int64_t>(d, "label_ld");
+    p.target_weights = P<const float>(get_or<uintptr_t>(d, "target_weights", 0));
+    p.sample_weights = P<const float>(get_or<uintptr_t>(d, "sample_weights", 0));
+    p.valid_count = get_or<int>(d, "valid_count", -1);
+    p.grad_scale = get<float>(d, "grad_scale");
+    p.logits = P<float>(get<uintptr_t>(d, "logits"));
+    p.loss_sum = P<float>(get<uintptr_t>(d, "loss_sum"));
+    p.dh = P<__nv_bfloat16>(get<uintptr_t>(d, "dh"));
+    p.dh_ld = get<int64_t>(d, "dh_ld");
+    p.dw = P<float>(get<uintptr_t>(d, "dw"));
+    p.db = P<float>(get<uintptr_t>(d, "db"));
+    flare::head_bce(p, cur_stream());
+  });
+
+  m.def("adam_flat", [](const py::dict& d) {
+    flare::AdamFlatParams p{};
+    p.master = P<float>(get<uintptr_t>(d, "master"));
+    p.grad = P<float>(get<uintptr_t>(d, "grad"));
+    p.m = P<float>(get<uintptr_t>(d, "m"));
+    p.v = P<float>(get<uintptr_t>(d, "v"));
+    p.compute_copy = P<__nv_bfloat16>(get_or<uintptr_t>(d, "compute_copy", 0));
+    p.n = get<int64_t>(d, "n");
+    p.grad_scale = get_or<float>(d, "grad_scale", 1.f);
+    p.zero_grad = get_or<int>(d, "zero_grad", 1);
+    p.opt = parse_adam(get<py::dict>(d, "opt"));
+    flare::adam_flat(p, cur_stream());
+  });
+
+  m.def("adam_dp_fused", [](const py::dict& d) {
+    flare::AdamDpParams p{};
+    p.world = get<int>(d, "world");
+    p.rank = get<int>(d, "rank");
+    p.lo = get<int64_t>(d, "lo");
+    p.hi = get<int64_t>(d, "hi");
+    p.peer_grad = P<float* const>(get<uintptr_t>(d, "peer_grad"));
+    p.peer_param = P<void* const>(get<uintptr_t>(d, "peer_param"));
+    p.master_shard = P<float>(get<uintptr_t>(d, "master_shard"));
+    p.m_shard = P<float>(get<uintptr_t>(d, "m_shard"));
+    p.v_shard = P<float>(get<uintptr_t>(d, "v_shard"));
+    p.grad_scale = get_or<float>(d, "grad_scale", 1.f);
+    p.opt = parse_adam(get<py::dict>(d, "opt"));
+    p.flags_local = P<uint32_t>(get<uintptr_t>(d, "flags_local"));
+    p.peer_flags = P<uint32_t* const>(get<uintptr_t>(d, "peer_flags"));
+    p.flag_in = get<int>(d, "flag_in");
+    p.flag_out = get<int>(d, "flag_out");
+    p.epoch_ctr = P<uint32_t>(get<uintptr_t>(d, "epoch_ctr"));
+    p.block_counter = P<unsigned>(get<uintptr_t>(d, "block_counter"));
+    p.status = P<int>(get_or<uintptr_t>(d, "status", 0));
+    p.timeout_ns = get_or<uint64_t>(d, "timeout_ns", 2000000000ull);
+    flare::adam_dp_fused(p, cur_stream());
+  });
+
+  m.def("colsum_bf16", [](uintptr_t x, int64_t rows, int cols, int64_t ldx, uintptr_t out) {
+    flare::colsum_bf16(P<const __nv_bfloat16>(x), rows, cols, ldx, P<float>(out), cur_stream());
+  });
+  m.def("cast_pad_bf16", [](uintptr_t x, int64_t rows, int cols, int64_t ldx, uintptr_t y, int ldy) {
+    flare::cast_pad_bf16(P<const float>(x), rows, cols, ldx, P<__nv_bfloat16>(y), ldy, cur_stream());
+  });
+  m.def("init_uniform", [](uintptr_t out, int dtype, int64_t n, float lo, float hi, uint64_t seed, int64_t off) {
+    flare::init_uniform(P<void>(out), dtype, n, lo, hi, seed, off, cur_stream());
+  });
+
+  m.def("sparse_gather", [](uintptr_t emb, int dtype, uintptr_t inv, int64_t slots, int dim, int pad, uintptr_t out) {
+    flare::sparse_gather(P<const void>(emb), dtype, P<const int>(inv), slots, dim, pad, P<void>(out), cur_stream());
+  });
+  m.def("sparse_gather_pooled", [](uintptr_t emb, int dtype, uintptr_t inv, int64_t bags, int E, int dim, int pad,
+                                   uintptr_t out) {
+    flare::sparse_gather_pooled(P<const void>(emb), dtype, P<const int>(inv), bags, E, dim, pad, P<void>(out),
+                                cur_stream());
+  });
+  m.def("sparse_scatter", [](uintptr_t g, int dtype, uintptr_t inv, int64_t slots, int dim, int pad, uintptr_t out) {
+    flare::sparse_scatter(P<const void>(g), dtype, P<const int>(inv), slots, dim, pad, P<float>(out), cur_stream());
+  });
+  m.def("sparse_scatter_pooled", [](uintptr_t g, int dtype, uintptr_t inv, int64_t bags, int E, int dim, int pad,
+                                    uintptr_t out) {
+    flare::sparse_scatter_pooled(P<const void>(g), dtype, P<const int>(inv), bags, E, dim, pad, P<float>(out),
+                                 cur_stream());
+  });
+  m.def("unique_first_occurrence", [](uintptr_t keys, int64_t n, const py::dict& w, uintptr_t unique,
+                                      uintptr_t inverse, uintptr_t first_idx) {
+    flare::UniqueScratch s{};
+    s.tab_keys = P<unsigned long long>(get<uintptr_t>(w, "tab_keys"));
+    s.tab_first = P<int>(get<uintptr_t>(w, "tab_first"));
+    s.cap = get<int64_t>(w, "cap");
+    s.slot_of = P<int64_t>(get<uintptr_t>(w, "slot_of"));
+    s.is_first = P<int>(get<uintptr_t>(w, "is_first"));
+    s.pos = P<int>(get<uintptr_t>(w, "pos"));
+    s.block_sums = P<int>(get<uintptr_t>(w, "block_sums"));
+    flare::unique_first_occurrence(P<const int64_t>(keys), n, s, P<int64_t>(unique), P<int>(inverse),
+                                   P<int64_t>(first_idx), cur_stream());
+  });
+  m.def("exclusive_scan_int", [](uintptr_t in, int64_t n, uintptr_t out, uintptr_t block_sums) {
+    flare::exclusive_scan_int(P<const int>(in), n, P<int>(out), P<int>(block_sums), cur_stream());
+  });
+
+  // ---- symmetric memory plumbing ----
+  m.def("dev_malloc", [](size_t bytes) { return reinterpret_cast<uintptr_t>(flare::dev_malloc(bytes)); });
+  m.def("dev_free", [](uintptr_t p) { flare::dev_free(P<void>(p)); });
+  m.def("ipc_get_handle", [](uintptr_t p) {
+    auto v = flare::ipc_get_handle(P<void>(p));
+    return py::bytes(v.data(), v.size());
+  });
+  m.def("ipc_open_handle", [](py::bytes b) {
+    std::string s = b;
+    std::vector<char> v(s.begin(), s.end());
+    return reinterpret_cast<uintptr_t>(flare::ipc_open_handle(v));
+  });
+  m.def("ipc_close_handle", [](uintptr_t p) { flare::ipc_close_handle(P<void>(p)); });
+  m.def("can_access_peer", &flare::can_access_peer);
+  m.def("tensor_from_ptr", [](uintptr_t ptr, std::vector<int64_t> sizes, at::ScalarType dtype, int device) {
+    auto opts = at::TensorOptions().dtype(dtype).device(at::Device(at::kCUDA, device));
+    return torch::from_blob(reinterpret_cast<void*>(ptr), sizes, [](void*) {}, opts);
+  });
+}

@@ -1,0 +1,481 @@
+// Dense-tower kernels other than the GEMM (sm_100a):
+//   * DLRM pairwise dot interaction, forward and backward (one warp/sample)
+//   * fused prediction head + multi-target weighted sigmoid BCE, forward and
+//     backward in one pass (replaces optax sigmoid_binary_cross_entropy used by
+//     recipes/recsys/ranking/losses.py:69-95 of the reference)
+//   * flat fused Adam / AdamW / SGD over fp32 master weights that also writes
+//     the bf16 compute copy
+//   * data-parallel fused reduce-scatter -> Adam -> all-gather over NVLink peer
+//     memory (ZeRO-1 semantics of src/flare/training/zero/contracts.py:40-48)
+//   * small helpers: fp32 -> bf16 cast with padding, counter-based uniform init
+#include "dense.cuh"
+
+#include <algorithm>
+
+namespace flare {
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+// ------------------------------- interaction -------------------------------
+// Vector index pairs (i > j) enumerated row by row: p = i*(i-1)/2 + j.
+__device__ __forceinline__ void pair_of(int p, int& i, int& j) {
+  int r = static_cast<int>((1.f + sqrtf(1.f + 8.f * static_cast<float>(p))) * 0.5f);
+  while (r * (r - 1) / 2 > p) --r;
+  while ((r + 1) * r / 2 <= p) ++r;
+  i = r;
+  j = p - r * (r - 1) / 2;
+}
+
+constexpr int kInterWarps = 4;
+
+// Z = [bot, emb_0..emb_{F-1}] (T = F+1 vectors of width D, D % 64 == 0, D <= 256)
+// out[b] = [bot (D), dots (T(T-1)/2), zero padding up to out_ld]
+__global__ void __launch_bounds__(kInterWarps * 32) interaction_fwd_kernel(InteractionParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int T = p.F + 1;
+  const int rowp = p.D / 2 + 1;  // row pitch in 32-bit words (+1 word breaks bank conflicts)
+  uint32_t* z = reinterpret_cast<uint32_t*>(smem) + warp_id() * T * rowp;
+  const int lane = lane_id();
+  const int npairs = T * (T - 1) / 2;
+  for (int b = blockIdx.x * kInterWarps + warp_id(); b < p.B; b += gridDim.x * kInterWarps) {
+    const __nv_bfloat16* bot = p.bot + static_cast<int64_t>(b) * p.bot_ld;
+    const __nv_bfloat16* emb = p.emb + static_cast<int64_t>(b) * p.emb_ld;
+    __nv_bfloat16* out = p.out + static_cast<int64_t>(b) * p.out_ld;
+    // stage Z (bf16 pairs) into shared memory; copy bot to the output head
+    for (int w = lane; w < T * (p.D / 2); w += 32) {
+      const int r = w / (p.D / 2), c = w - r * (p.D / 2);
+      const uint32_t v = r == 0 ? reinterpret_cast<const uint32_t*>(bot)[c]
+                                : reinterpret_cast<const uint32_t*>(emb + (r - 1) * p.D)[c];
+      z[r * rowp + c] = v;
+      if (r == 0) reinterpret_cast<uint32_t*>(out)[c] = v;
+    }
+    __syncwarp();
+    for (int q = lane; q < npairs; q += 32) {
+      int i, j;
+      pair_of(q, i, j);
+      const uint32_t* zi = z + i * rowp;
+      const uint32_t* zj = z + j * rowp;
+      float acc = 0.f;
+#pragma unroll 8
+      for (int c = 0; c < p.D / 2; ++c) {
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(zi + c));
+        const float2 bb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(zj + c));
+        acc = fmaf(a.x, bb.x, acc);
+        acc = fmaf(a.y, bb.y, acc);
+      }
+      out[p.D + q] = __float2bfloat16_rn(acc);
+    }
+    for (int c = p.D + npairs + lane; c < p.out_ld; c += 32) out[c] = __float2bfloat16_rn(0.f);
+    __syncwarp();
+  }
+}
+
+// dZ_i = sum_{j != i} dDot(i,j) Z_j ; d(bot) += dOut[:, :D]; ReLU mask of bot.
+__global__ void __launch_bounds__(kInterWarps * 32) interaction_bwd_kernel(InteractionParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int T = p.F + 1;
+  const int rowp = p.D / 2 + 1;
+  uint32_t* z = reinterpret_cast<uint32_t*>(smem) + warp_id() * (T * rowp + T * T);
+  float* S = reinterpret_cast<float*>(z + T * rowp);
+  const int lane = lane_id();
+  const int npairs = T * (T - 1) / 2;
+  const int per_lane = p.D / 32;  // columns per lane (2, 4 or 8)
+  for (int b = blockIdx.x * kInterWarps + warp_id(); b < p.B; b += gridDim.x * kInterWarps) {
+    const __nv_bfloat16* bot = p.bot + static_cast<int64_t>(b) * p.bot_ld;
+    const __nv_bfloat16* emb = p.emb + static_cast<int64_t>(b) * p.emb_ld;
+    const __nv_bfloat16* dout = p.dout + static_cast<int64_t>(b) * p.out_ld;
+    for (int w = lane; w < T * (p.D / 2); w += 32) {
+      const int r = w / (p.D / 2), c = w - r * (p.D / 2);
+      z[r * rowp + c] = r == 0 ? reinterpret_cast<const uint32_t*>(bot)[c]
+                               : reinterpret_cast<const uint32_t*>(emb + (r - 1) * p.D)[c];
+    }
+    for (int q = lane; q < T * T; q += 32) S[q] = 0.f;
+    __syncwarp();
+    for (int q = lane; q < npairs; q += 32) {
+      int i, j;
+      pair_of(q, i, j);
+      const float g = __bfloat162float(dout[p.D + q]);
+      S[i * T + j] = g;
+      S[j * T + i] = g;
+    }
+    __syncwarp();
+    // lane owns columns [lane*per_lane, (lane+1)*per_lane)
+    const int c0 = lane * per_lane;
+    for (int i = 0; i < T; ++i) {
+      float acc[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+      for (int j = 0; j < T; ++j) {
+        const float s = S[i * T + j];
+        const uint32_t* zj = z + j * rowp + c0 / 2;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (2 * e < per_lane) {
+            const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(zj + e));
+            acc[2 * e] = fmaf(s, v.x, acc[2 * e]);
+            acc[2 * e + 1] = fmaf(s, v.y, acc[2 * e + 1]);
+          }
+        }
+      }
+      if (i == 0) {
+        __nv_bfloat16* dbot = p.dbot + static_cast<int64_t>(b) * p.dbot_ld;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (e < per_lane) {
+            const int c = c0 + e;
+            float v = acc[e] + __bfloat162float(dout[c]);
+            if (p.relu_mask_bot && __bfloat162float(bot[c]) <= 0.f) v = 0.f;
+            dbot[c] = __float2bfloat16_rn(v);
+          }
+        }
+      } else {
+        __nv_bfloat16* demb = p.demb + static_cast<int64_t>(b) * p.demb_ld + (i - 1) * p.D;
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          if (e < per_lane)
+            *reinterpret_cast<__nv_bfloat162*>(demb + c0 + e) = __floats2bfloat162_rn(acc[e], acc[e + 1]);
+        }
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// --------------------------- fused head + BCE ------------------------------
+// logits[b,t] = h[b,:] . w[t,:] + bias[t]
+// loss = sum_b sum_t weight[b,t] * (softplus(x) - y*x)  (accumulated into loss_sum)
+// dlogit = weight * (sigmoid(x) - y) * grad_scale
+// dh = sum_t dlogit[b,t] * w[t,:] masked by (h > 0) ; dw[t,:] += sum_b dlogit h ; db[t] += sum_b dlogit
+constexpr int kHeadWarps = 8;
+template <int PER>
+__global__ void __launch_bounds__(kHeadWarps * 32) head_bce_kernel(HeadBceParams p) {
+  extern __shared__ __align__(16) float hs[];  // per warp: [T][H] dw partials, then [T] db partials
+  const int H = p.H, T = p.T;
+  const int lane = lane_id();
+  float* mine = hs + warp_id() * T * (H + 1);
+  for (int i = lane; i < T * (H + 1); i += 32) mine[i] = 0.f;
+  __syncwarp();
+  float loss_acc = 0.f;
+  for (int b = blockIdx.x * kHeadWarps + warp_id(); b < p.B; b += gridDim.x * kHeadWarps) {
+    const __nv_bfloat16* h = p.h + static_cast<int64_t>(b) * p.h_ld + lane * PER;
+    float hv[PER], dh[PER];
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+      hv[e] = __bfloat162float(h[e]);
+      dh[e] = 0.f;
+    }
+    for (int t = 0; t < T; ++t) {
+      const __nv_bfloat16* wrow = p.w + static_cast<int64_t>(t) * H + lane * PER;
+      float w[PER];
+#pragma unroll
+      for (int e = 0; e < PER; ++e) w[e] = __bfloat162float(wrow[e]);
+      float acc = 0.f;
+#pragma unroll
+      for (int e = 0; e < PER; ++e) acc = fmaf(hv[e], w[e], acc);
+      const float x = warp_sum(acc) + __bfloat162float(p.bias[t]);
+      if (lane == 0) p.logits[static_cast<int64_t>(b) * T + t] = x;
+      const float y = p.labels[static_cast<int64_t>(b) * p.label_ld + t];
+      float wt = p.target_weights ? p.target_weights[t] : 1.f;
+      if (p.sample_weights) wt *= p.sample_weights[b];
+      if (p.valid_count >= 0 && b >= p.valid_count) wt = 0.f;
+      // softplus(x) - y*x = max(x,0) - x*y + log1p(exp(-|x|))
+      const float l = fmaxf(x, 0.f) - x * y + log1pf(__expf(-fabsf(x)));
+      loss_acc += wt * l;
+      const float sg = 1.f / (1.f + __expf(-x));
+      const float dl = wt * (sg - y) * p.grad_scale;
+      float* dwp = mine + t * H + lane * PER;
+#pragma unroll
+      for (int e = 0; e < PER; ++e) {
+        dh[e] = fmaf(dl, w[e], dh[e]);
+        dwp[e] = fmaf(dl, hv[e], dwp[e]);
+      }
+      if (lane == 0) mine[T * H + t] += dl;
+    }
+    __nv_bfloat16* dho = p.dh + static_cast<int64_t>(b) * p.dh_ld + lane * PER;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) dho[e] = __float2bfloat16_rn(hv[e] > 0.f ? dh[e] : 0.f);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < T * (H + 1); i += blockDim.x) {
+    float acc = 0.f;
+    for (int w = 0; w < kHeadWarps; ++w) acc += hs[w * T * (H + 1) + i];
+    if (acc != 0.f) atomicAdd(i < T * H ? p.dw + i : p.db + (i - T * H), acc);
+  }
+  loss_acc = warp_sum(loss_acc);
+  if (lane == 0 && loss_acc != 0.f) atomicAdd(p.loss_sum, loss_acc);
+}
+
+// ------------------------------ optimizers --------------------------------
+__device__ __forceinline__ AdamParams resolve_step(AdamParams o) {
+  if (o.step_ptr != nullptr) {
+    const float t = static_cast<float>(*o.step_ptr);
+    o.bias_corr1 = 1.f - powf(o.beta1, t);
+    o.bias_corr2 = 1.f - powf(o.beta2, t);
+  }
+  return o;
+}
+
+__device__ __forceinline__ void adam_elem(const AdamParams& o, float& w, float& m, float& v, float g) {
+  if (o.weight_decay != 0.f) {
+    if (o.decoupled) w -= o.lr * o.weight_decay * w;
+    else g += o.weight_decay * w;
+  }
+  if (o.kind == kDenseSgd) {
+    if (o.beta1 != 0.f) {  // momentum
+      m = o.beta1 * m + g;
+      g = o.nesterov ? g + o.beta1 * m : m;
+    }
+    w -= o.lr * g;
+    return;
+  }
+  if (o.kind == kDenseAdagrad) {
+    m += g * g;
+    w -= o.lr * g / (sqrtf(m) + o.eps);
+    return;
+  }
+  if (o.kind == kDenseRmsprop) {
+    v = o.beta2 * v + (1.f - o.beta2) * g * g;
+    w -= o.lr * g / (sqrtf(v) + o.eps);
+    return;
+  }
+  m = o.beta1 * m + (1.f - o.beta1) * g;
+  v = o.beta2 * v + (1.f - o.beta2) * g * g;
+  w -= o.lr * (m / o.bias_corr1) / (sqrtf(v / o.bias_corr2) + o.eps);
+}
+
+__global__ void adam_flat_kernel(AdamFlatParams p) {
+  const AdamParams opt = resolve_step(p.opt);
+  const int64_t n4 = p.n / 4;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float4 w = reinterpret_cast<float4*>(p.master)[i];
+    float4 g = reinterpret_cast<const float4*>(p.grad)[i];
+    float4 m = reinterpret_cast<float4*>(p.m)[i];
+    float4 v = reinterpret_cast<float4*>(p.v)[i];
+    float* wp = reinterpret_cast<float*>(&w);
+    float* gp = reinterpret_cast<float*>(&g);
+    float* mp = reinterpret_cast<float*>(&m);
+    float* vp = reinterpret_cast<float*>(&v);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) adam_elem(opt, wp[e], mp[e], vp[e], gp[e] * p.grad_scale);
+    reinterpret_cast<float4*>(p.master)[i] = w;
+    reinterpret_cast<float4*>(p.m)[i] = m;
+    reinterpret_cast<float4*>(p.v)[i] = v;
+    if (p.compute_copy) store4<__nv_bfloat16>(p.compute_copy + 4 * i, w);
+    if (p.zero_grad) reinterpret_cast<float4*>(p.grad)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+// Data-parallel ZeRO-1 update in one launch: rank r owns [lo, hi) of the flat
+// buffer. Sum every peer's gradient slice over NVLink (reduce-scatter), run the
+// optimizer on the local fp32 master/state shard, push the new bf16 values
+// into every peer's compute copy (all-gather), zero the consumed gradient
+// slices, and finish with a barrier so every rank sees complete parameters.
+__global__ void adam_dp_fused_kernel(AdamDpParams p) {
+  __shared__ int ok_sh;
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(p.epoch_ctr) + 1u;
+  if (threadIdx.x == 0) {
+    ok_sh = 1;
+    if (blockIdx.x == 0) {
+      fence_sys();
+      for (int s = 0; s < p.world; ++s) st_release_sys(p.peer_flags[s] + p.flag_in + p.rank, epoch);
+    }
+    for (int s = 0; s < p.world && ok_sh; ++s)
+      ok_sh = wait_flag_geq(p.flags_local + p.flag_in + s, epoch, p.timeout_ns, p.status, s) ? 1 : 0;
+  }
+  __syncthreads();
+  if (!ok_sh) return;
+  const AdamParams opt = resolve_step(p.opt);
+  const int64_t lo4 = p.lo / 4, hi4 = p.hi / 4;
+  for (int64_t i = lo4 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < hi4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < p.world; ++s) {
+      float4* gs = reinterpret_cast<float4*>(p.peer_grad[s]) + i;
+      g = f4_add(g, *gs);
+      *gs = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const int64_t li = i - lo4;  // index into the local shard state
+    float4 w = reinterpret_cast<float4*>(p.master_shard)[li];
+    float4 m = reinterpret_cast<float4*>(p.m_shard)[li];
+    float4 v = reinterpret_cast<float4*>(p.v_shard)[li];
+    float* wp = reinterpret_cast<float*>(&w);
+    float* gp = reinterpret_cast<float*>(&g);
+    float* mp = reinterpret_cast<float*>(&m);
+    float* vp = reinterpret_cast<float*>(&v);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) adam_elem(opt, wp[e], mp[e], vp[e], gp[e] * p.grad_scale);
+    reinterpret_cast<float4*>(p.master_shard)[li] = w;
+    reinterpret_cast<float4*>(p.m_shard)[li] = m;
+    reinterpret_cast<float4*>(p.v_shard)[li] = v;
+    for (int s = 0; s < p.world; ++s)
+      store4<__nv_bfloat16>(reinterpret_cast<__nv_bfloat16*>(p.peer_param[s]) + 4 * i, w);
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(p.block_counter, 1u);
+    if (prev == gridDim.x - 1) {
+      *p.block_counter = 0u;
+      *p.epoch_ctr = epoch;
+      fence_sys();
+      for (int s = 0; s < p.world; ++s) st_release_sys(p.peer_flags[s] + p.flag_out + p.rank, epoch);
+      for (int s = 0; s < p.world; ++s)
+        if (!wait_flag_geq(p.flags_local + p.flag_out + s, epoch, p.timeout_ns, p.status, s)) break;
+    }
+  }
+}
+
+// ------------------------------- helpers -----------------------------------
+// out[c] += sum_r x[r, c]: block = 32 columns x 8 row-groups, one atomic per
+// column per block.
+__global__ void colsum_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int cols, int64_t ldx,
+                              float* __restrict__ out) {
+  __shared__ float part[8][33];
+  const int c = blockIdx.x * 32 + threadIdx.x;
+  float acc = 0.f;
+  if (c < cols) {
+    for (int64_t r = blockIdx.y * 8 + threadIdx.y; r < rows; r += static_cast<int64_t>(gridDim.y) * 8)
+      acc += __bfloat162float(x[r * ldx + c]);
+  }
+  part[threadIdx.y][threadIdx.x] = acc;
+  __syncthreads();
+  if (threadIdx.y == 0 && c < cols) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += part[i][threadIdx.x];
+    atomicAdd(out + c, s);
+  }
+}
+
+__global__ void cast_pad_kernel(const float* __restrict__ x, int64_t rows, int cols, int64_t ldx,
+                                __nv_bfloat16* __restrict__ y, int ldy) {
+  const int64_t n = rows * ldy;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / ldy;
+    const int c = static_cast<int>(i - r * ldy);
+    y[i] = __float2bfloat16_rn(c < cols ? x[r * ldx + c] : 0.f);
+  }
+}
+
+// splitmix64 finaliser as a counter-based generator: value i of stream `seed`.
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebULL;
+  return z ^ (z >> 31);
+}
+
+template <typename T>
+__global__ void init_uniform_kernel(T* __restrict__ out, int64_t n, float lo, float hi, uint64_t seed,
+                                    int64_t index_offset) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint64_t r = mix64(seed * 0x9e3779b97f4a7c15ULL + static_cast<uint64_t>(i + index_offset));
+    const float u = static_cast<float>(r >> 40) * (1.0f / 16777216.0f);  // 24 random bits in [0,1)
+    out[i] = from_f32<T>(lo + (hi - lo) * u);
+  }
+}
+
+}  // namespace
+
+int grid_for(int64_t n, int threads) {
+  const int64_t want = (n + threads - 1) / threads;
+  const int cap = 148 * 16;
+  return static_cast<int>(want < 1 ? 1 : (want > cap ? cap : want));
+}
+
+void interaction_forward(const InteractionParams& p, cudaStream_t s) {
+  FLARE_CHECK(p.D % 64 == 0 && p.D <= 256, "interaction width must be a multiple of 64 and <= 256");
+  const int T = p.F + 1;
+  FLARE_CHECK(p.out_ld >= p.D + T * (T - 1) / 2, "interaction output too narrow");
+  const size_t smem = static_cast<size_t>(kInterWarps) * T * (p.D / 2 + 1) * 4;
+  FLARE_CUDA_CHECK(cudaFuncSetAttribute(interaction_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(smem)));
+  const int grid = std::min(ceil_div(p.B, kInterWarps), 148 * 8);
+  interaction_fwd_kernel<<<grid, kInterWarps * 32, smem, s>>>(p);
+  FLARE_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void interaction_backward(const InteractionParams& p, cudaStream_t s) {
+  FLARE_CHECK(p.D % 64 == 0 && p.D <= 256, "interaction width must be a multiple of 64 and <= 256");
+  const int T = p.F + 1;
+  const size_t smem = static_cast<size_t>(kInterWarps) * (T * (p.D / 2 + 1) + T * T) * 4;
+  FLARE_CUDA_CHECK(cudaFuncSetAttribute(interaction_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(smem)));
+  const int grid = std::min(ceil_div(p.B, kInterWarps), 148 * 8);
+  interaction_bwd_kernel<<<grid, kInterWarps * 32, smem, s>>>(p);
+  FLARE_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+template <int PER>
+void head_bce_launch(const HeadBceParams& p, cudaStream_t s) {
+  const size_t smem = static_cast<size_t>(kHeadWarps) * p.T * (p.H + 1) * 4;
+  FLARE_CUDA_CHECK(cudaFuncSetAttribute(head_bce_kernel<PER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(smem)));
+  const int grid = std::min(ceil_div(p.B, kHeadWarps * 8), 148 * 2);
+  head_bce_kernel<PER><<<grid, kHeadWarps * 32, smem, s>>>(p);
+  count_launch();
+}
+
+void head_bce(const HeadBceParams& p, cudaStream_t s) {
+  FLARE_CHECK(p.H % 32 == 0 && p.H <= 1024, "head width must be a multiple of 32 and <= 1024");
+  FLARE_CHECK(p.T >= 1 && p.T * p.H <= 4096, "targets x head width must be <= 4096");
+  switch (p.H / 32) {
+    case 1: head_bce_launch<1>(p, s); break;
+    case 2: head_bce_launch<2>(p, s); break;
+    case 4: head_bce_launch<4>(p, s); break;
+    case 8: head_bce_launch<8>(p, s); break;
+    case 16: head_bce_launch<16>(p, s); break;
+    case 32: head_bce_launch<32>(p, s); break;
+    default: FLARE_CHECK(false, "head width / 32 must be a power of two");
+  }
+  FLARE_CUDA_CHECK(cudaGetLastError());
+}
+
+void adam_flat(const AdamFlatParams& p, cudaStream_t s) {
+  FLARE_CHECK(p.n % 4 == 0, "flat optimizer buffers must be padded to a multiple of 4");
+  adam_flat_kernel<<<grid_for(p.n / 4, 256), 256, 0, s>>>(p);
+  FLARE_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void adam_dp_fused(const AdamDpParams& p, cudaStream_t s) {
+  FLARE_CHECK(p.lo % 4 == 0 && p.hi % 4 == 0, "shard bounds must be multiples of 4");
+  const int grid = std::max(1, std::min(grid_for((p.hi - p.lo) / 4, 256), 148 * 4));
+  adam_dp_fused_kernel<<<grid, 256, 0, s>>>(p);
+  FLARE_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void colsum_bf16(const __nv_bfloat16* x, int64_t rows, int cols, int64_t ldx, float* out, cudaStream_t s) {
+  dim3 block(32, 8);
+  const int gx = ceil_div(cols, 32);
+  const int gy = std::max(1, std::min<int>(ceil_div(rows, 256), std::max(1, 148 * 8 / gx)));
+  colsum_kernel<<<dim3(gx, gy), block, 0, s>>>(x, rows, cols, ldx, out);
+  FLARE_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void cast_pad_bf16(const float* x, int64_t rows, int cols, int64_t ldx, __nv_bfloat16* y, int ldy,
+                   cudaStream_t s) {
+  cast_pad_kernel<<<grid_for(rows * ldy, 256), 256, 0, s>>>(x, rows, cols, ldx, y, ldy);
+  FLARE_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void init_uniform(void* out, int dtype, int64_t n, float lo, float hi, uint64_t seed, int64_t index_offset,
+                  cudaStream_t s) {
+  const int grid = grid_for(n, 256);
+  if (dtype == kF32) init_uniform_kernel<float><<<grid, 256, 0, s>>>(static_cast<float*>(out), n, lo, hi, seed, index_offset);
+  else if (dtype == kBF16)
+    init_uniform_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<__nv_bfloat16*>(out), n, lo, hi, seed, index_offset);
+  else init_uniform_kernel<__half><<<grid, 256, 0, s>>>(static_cast<__half*>(out), n, lo, hi, seed, index_offset);
+  FLARE_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+}  // namespace flare

@@ -1,0 +1,124 @@
+// Shared declarations for the sharded embedding-bag kernels.
+#pragma once
+
+#include "common.cuh"
+
+namespace flare {
+
+// One locally owned shard of a table: table-wise (all columns) or a
+// column-wise slice. Row ids index the shard directly (static vocabulary).
+struct ShardDesc {
+  int feature;         // index of the input feature (KJT key) feeding this table
+  int col_begin;       // first table column held by this shard
+  int ncols;           // number of columns held (multiple of 4)
+  int out_col;         // column of the pooled output row receiving col_begin
+  int64_t rows;        // rows held
+  int64_t weight_off;  // element offset of the shard in the weight buffer
+  int64_t row_base;    // offset of the shard's first row in per-row arrays
+  int pooling;         // 0 = sum, 1 = mean
+  int pad_;
+};
+
+enum SparseOptKind : int {
+  kOptSgd = 0,
+  kOptRowwiseAdagrad = 1,
+  kOptAdam = 2,
+  kOptRowwiseAdam = 3,
+  kOptAdagrad = 4,
+};
+
+enum LrPolicy : int {
+  kLrConstant = 0,
+  kLrSqrtDecay = 1,
+  kLrLogDecay = 2,
+  kLrInverseDecay = 3,
+  kLrCosineFrequency = 4,
+  kLrCustomLut = 5,
+};
+
+struct SparseOptParams {
+  int kind;
+  float lr, beta1, beta2, eps, weight_decay;
+  float bias_corr1, bias_corr2;  // 1 - beta^t for the current optimizer step (if step_ptr null)
+  const int* step_ptr;           // device step counter (1-based); bias corrections computed in-kernel
+  int lr_policy;
+  float policy_a, policy_b;  // cosine: min_lr_ratio, max_score
+  const float* lut;
+  int lut_len;
+  float* state_row;  // per-row fp32 state (row-wise adagrad sum, row-wise adam v)
+  float* state_m;    // per-element first moment (adam) / accumulator (adagrad)
+  float* state_v;    // per-element second moment (adam)
+  float* score;      // per-row access score for frequency-based LR policies (nullable)
+};
+
+struct EmbFwdParams {
+  const ShardDesc* shards;
+  int num_shards;
+  int world, rank, Bl, F;
+  const int* const* peer_offsets;  // [world] offsets buffers, int32[F*Bl+1]
+  const int* const* peer_values;   // [world] id buffers
+  void* const* peer_out;           // [world] pooled outputs (bf16 rows of out_stride)
+  int64_t out_stride;
+  const void* weights;
+  int w_dtype;
+  int out_dtype;  // kBF16 or kF32
+  int vec;        // float4 vectors per lane: 1 (shard width <= 128) or 2 (<= 256)
+  // staging for the backward pass
+  int* stage_ids;    // [(sh*world+s)*stage_cap + j]
+  int* stage_bag;    // same indexing: sample index of occurrence j
+  int* stage_count;  // [sh*world+s] occurrences staged
+  int* stage_len;    // [(sh*world+s)*Bl + b] bag length (for mean pooling)
+  int64_t stage_cap;
+  // cross-GPU barrier
+  uint32_t* flags_local;
+  uint32_t* const* peer_flags;
+  int flag_in, flag_out;  // slot-array offsets in the flag buffer
+  uint32_t* epoch_ctr;    // device-resident barrier epoch (advanced by the kernel)
+  unsigned* block_counter;
+  int* status;
+  uint64_t timeout_ns;
+};
+
+struct EmbBwdParams {
+  const ShardDesc* shards;
+  int num_shards;
+  int world, rank, Bl;
+  const void* const* peer_grad;  // [world] pooled-grad buffers (rows of out_stride)
+  int64_t out_stride;
+  int grad_dtype;                // kBF16 or kF32
+  void* grad_stage;              // [(sh*world+s)*Bl + b][ncols_max] (grad_dtype)
+  int64_t grad_stage_ld;
+  const int* stage_ids;
+  const int* stage_bag;
+  const int* stage_count;
+  const int* stage_len;
+  int64_t stage_cap;
+  void* weights;
+  int w_dtype;
+  // dedup / segment scratch
+  int* row_count;   // per-row occurrence counter (left at zero after the fill)
+  int* row2u;       // per-row unique index
+  int64_t* uniq_row;
+  int* uniq_shard;
+  int* num_unique;  // [0] = U, [1] = total occurrences T
+  int* seg_start;   // [U+1]
+  int* block_sums;
+  int* occ;         // [T] staged-grad row index per occurrence, grouped by unique row
+  float* carry;     // [num_chunks][ncols_max] partial sums of rows spanning chunks
+  int* span_u;      // [num_chunks]
+  int chunk;        // occurrences per reduce chunk
+  int64_t max_occ;  // capacity of occ / uniq arrays
+  SparseOptParams opt;
+  uint32_t* flags_local;
+  uint32_t* const* peer_flags;
+  int flag_in;
+  uint32_t* epoch_ctr;
+  unsigned* block_counter;
+  int* status;
+  uint64_t timeout_ns;
+};
+
+void emb_forward(const EmbFwdParams& p, int grid, cudaStream_t s);
+void emb_backward(const EmbBwdParams& p, int ncols_max, int grid, cudaStream_t s);
+
+}  // namespace flare

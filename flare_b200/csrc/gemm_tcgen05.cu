@@ -1,0 +1,362 @@
+// bf16 GEMM on the 5th-generation tensor cores (tcgen05) for sm_100a.
+//
+//   C[M,N] (+)= alpha * A[M,K] . B[N,K]^T   (+ bias[N]) -> act -> * mask -> C
+//
+// A and B may each be K-major (row-major [rows][K]) or MN-major (the
+// transpose is what is stored, row-major [K][rows]); MN-major operands are fed
+// to the tensor core with the descriptor's transpose bit, so the backward
+// GEMMs (dX = dY.W and dW = dY^T.X) never materialise a transpose.
+//
+// Structure (one 128 x BN output tile per CTA, 128 threads):
+//   warp 0 / lane 0 : TMA producer, STAGES-deep ring of 128-byte-swizzled tiles
+//   warp 1 / lane 0 : tcgen05.mma issuer; accumulator lives in TMEM
+//   warps 0..3      : epilogue, warp w reads TMEM lanes 32w..32w+31 (= rows)
+// Epilogue fusions used by the MLP towers:
+//   bias + ReLU (forward), ReLU-backward mask from the saved activation,
+//   per-column sums (bias gradient) via warp butterfly + one atomic per column,
+//   fp32 output with accumulate (gradient accumulation windows).
+//
+// This replaces the XLA/cuBLAS dense GEMMs of the reference's JAX engine
+// (src/flare/jax/training/engines/distributed.py:612-716 runs them via XLA).
+#include "gemm.cuh"
+#include "sm100.cuh"
+
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+namespace flare {
+
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;                 // one 128-byte swizzle atom of bf16 along K
+constexpr int kThreads = 128;
+constexpr int kTileBytesA = kBM * kBK * 2;  // 16 KiB
+
+struct EpiParams {
+  int M, N;
+  void* C;
+  int64_t ldc;
+  int c_dtype;
+  int accumulate;
+  const __nv_bfloat16* bias;
+  int act;
+  float alpha;
+  const __nv_bfloat16* mask;
+  int64_t ldm;
+  float* colsum;
+  int* status;
+  uint64_t timeout_ns;
+  int num_k_tiles;
+};
+
+template <int BN, int STAGES>
+struct SmemLayout {
+  static constexpr int kTileBytesB = BN * kBK * 2;
+  static constexpr int kOffA = 0;
+  static constexpr int kOffB = STAGES * kTileBytesA;
+  static constexpr int kOffBar = kOffB + STAGES * kTileBytesB;
+  static constexpr int kBytes = kOffBar + (2 * STAGES + 1) * 8 + 16;
+  static constexpr int kAlloc = kBytes + 1024;  // slack for manual 1 KiB alignment
+};
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                     EpiParams p) {
+  using L = SmemLayout<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* done_bar = empty_bar + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int m0 = blockIdx.x * kBM;
+  const int n0 = blockIdx.y * BN;
+
+  if (threadIdx.x == 0) {
+    sm100::tma_prefetch_desc(&tmap_a);
+    sm100::tma_prefetch_desc(&tmap_b);
+    for (int s = 0; s < STAGES; ++s) {
+      sm100::mbar_init(&full_bar[s], 1);
+      sm100::mbar_init(&empty_bar[s], 1);
+    }
+    sm100::mbar_init(done_bar, 1);
+    sm100::fence_mbar_init();
+  }
+  if (warp == 0) {
+    sm100::tmem_alloc(tmem_slot, BN);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int KT = p.num_k_tiles;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------ producer ------------------------------
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % STAGES;
+      if (kt >= STAGES) {
+        if (!sm100::mbar_wait(&empty_bar[s], ((kt / STAGES) - 1) & 1, p.timeout_ns, p.status, 100 + s)) break;
+      }
+      uint8_t* sa = smem + L::kOffA + s * kTileBytesA;
+      uint8_t* sb = smem + L::kOffB + s * L::kTileBytesB;
+      sm100::mbar_arrive_expect_tx(&full_bar[s], kTileBytesA + L::kTileBytesB);
+      const int k0 = kt * kBK;
+      if constexpr (!A_MN) {
+        sm100::tma_load_2d(sa, &tmap_a, &full_bar[s], k0, m0);
+      } else {
+#pragma unroll
+        for (int j = 0; j < kBM / 64; ++j) sm100::tma_load_2d(sa + j * 8192, &tmap_a, &full_bar[s], m0 + 64 * j, k0);
+      }
+      if constexpr (!B_MN) {
+        sm100::tma_load_2d(sb, &tmap_b, &full_bar[s], k0, n0);
+      } else {
+#pragma unroll
+        for (int j = 0; j < BN / 64; ++j) sm100::tma_load_2d(sb + j * 8192, &tmap_b, &full_bar[s], n0 + 64 * j, k0);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------ MMA issuer ----------------------------
+    constexpr uint32_t idesc = sm100::make_idesc_bf16(kBM, BN, A_MN, B_MN);
+    bool ok = true;
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % STAGES;
+      if (!sm100::mbar_wait(&full_bar[s], (kt / STAGES) & 1, p.timeout_ns, p.status, 200 + s)) {
+        ok = false;
+        break;
+      }
+      sm100::tc_fence_after();
+      const uint32_t sa = smem_u32(smem + L::kOffA + s * kTileBytesA);
+      const uint32_t sb = smem_u32(smem + L::kOffB + s * L::kTileBytesB);
+#pragma unroll
+      for (int k = 0; k < kBK / 16; ++k) {
+        // K-major: 16 bf16 = 32 bytes further along the swizzled 128-byte row.
+        // MN-major: 16 K-rows of 128 bytes further down the tile.
+        const uint64_t da = A_MN ? sm100::make_smem_desc(sa + k * 2048, 8192, 1024)
+                                 : sm100::make_smem_desc(sa + k * 32, 16, 1024);
+        const uint64_t db = B_MN ? sm100::make_smem_desc(sb + k * 2048, 8192, 1024)
+                                 : sm100::make_smem_desc(sb + k * 32, 16, 1024);
+        sm100::mma_f16_ss(tmem_base, da, db, idesc, (kt > 0 || k > 0) ? 1u : 0u);
+      }
+      sm100::mma_commit(&empty_bar[s]);
+    }
+    if (ok) sm100::mma_commit(done_bar);
+  }
+  __syncwarp();
+
+  // -------------------------------- epilogue --------------------------------
+  const bool done = sm100::mbar_wait(done_bar, 0, p.timeout_ns, p.status, 300);
+  sm100::tc_fence_after();
+  const int row = m0 + warp * 32 + lane;
+  const bool row_ok = row < p.M;
+  if (done) {
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      const int ncol = n0 + c;
+      if (ncol >= p.N) break;  // warp-uniform
+      uint32_t r[32];
+      sm100::tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + c, r);
+      sm100::tmem_ld_wait();
+      float v[32];
+      const bool full_chunk = (ncol + 32 <= p.N);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float x = __uint_as_float(r[j]) * p.alpha;
+        if (p.bias != nullptr && (full_chunk || ncol + j < p.N)) x += __bfloat162float(p.bias[ncol + j]);
+        if (p.act == 1) x = fmaxf(x, 0.f);
+        v[j] = x;
+      }
+      if (p.mask != nullptr && row_ok) {
+        const __nv_bfloat16* mrow = p.mask + static_cast<int64_t>(row) * p.ldm + ncol;
+        if (full_chunk) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 u = *reinterpret_cast<const uint4*>(mrow + q * 8);
+            const __nv_bfloat16* mb = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+            for (int t = 0; t < 8; ++t) v[q * 8 + t] = (__bfloat162float(mb[t]) > 0.f) ? v[q * 8 + t] : 0.f;
+          }
+        } else {
+          for (int j = 0; j < 32; ++j)
+            if (ncol + j < p.N) v[j] = (__bfloat162float(mrow[j]) > 0.f) ? v[j] : 0.f;
+        }
+      }
+      if (!row_ok) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = 0.f;
+      }
+      if (p.colsum != nullptr) {
+        // Butterfly reduce-scatter across the warp: afterwards lane l holds the
+        // sum over the warp's 32 rows of column (ncol + l).
+        float t[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) t[j] = v[j];
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+          const bool upper = (lane & o) != 0;
+#pragma unroll
+          for (int j = 0; j < o; ++j) {
+            const float send = upper ? t[j] : t[j + o];
+            const float keep = upper ? t[j + o] : t[j];
+            t[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+          }
+        }
+        if (ncol + lane < p.N) atomicAdd(p.colsum + ncol + lane, t[0]);
+      }
+      if (row_ok) {
+        if (p.c_dtype == kBF16) {
+          __nv_bfloat16* crow = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<int64_t>(row) * p.ldc + ncol;
+          if (full_chunk) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 u;
+              uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                __nv_bfloat162 h = __floats2bfloat162_rn(v[q * 8 + 2 * t], v[q * 8 + 2 * t + 1]);
+                w[t] = *reinterpret_cast<uint32_t*>(&h);
+              }
+              *reinterpret_cast<uint4*>(crow + q * 8) = u;
+            }
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (ncol + j < p.N) crow[j] = __float2bfloat16_rn(v[j]);
+          }
+        } else {
+          float* crow = reinterpret_cast<float*>(p.C) + static_cast<int64_t>(row) * p.ldc + ncol;
+          if (full_chunk) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              float4 o = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+              if (p.accumulate) o = f4_add(o, *reinterpret_cast<const float4*>(crow + 4 * q));
+              *reinterpret_cast<float4*>(crow + 4 * q) = o;
+            }
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (ncol + j < p.N) crow[j] = p.accumulate ? crow[j] + v[j] : v[j];
+          }
+        }
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) sm100::tmem_dealloc(tmem_base, BN);
+}
+
+// ----------------------------- host side ------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    FLARE_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q));
+    FLARE_CHECK(q == cudaDriverEntryPointSuccess && ptr != nullptr, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// Row-major bf16 matrix with `inner` contiguous elements per row and `outer`
+// rows, row pitch `ld` elements; box = 64 x box_outer with 128-byte swizzle.
+CUtensorMap make_tmap_bf16(const void* base, int64_t inner, int64_t outer, int64_t ld, int box_outer) {
+  FLARE_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base must be 16-byte aligned");
+  FLARE_CHECK((ld * 2) % 16 == 0, "TMA row pitch must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_outer)};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  FLARE_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (code " + std::to_string(static_cast<int>(r)) + ")");
+  return m;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+void launch_cfg(const GemmArgs& a, cudaStream_t stream) {
+  using L = SmemLayout<BN, STAGES>;
+  auto kern = gemm_bf16_kernel<BN, STAGES, A_MN, B_MN>;
+  static bool attr_set = false;  // one per instantiation; set before first launch
+  if (!attr_set) {
+    FLARE_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc));
+    attr_set = true;
+  }
+  // A: K-major -> inner K, outer M, box rows 128; MN-major -> inner M, outer K, box 64 rows of K.
+  CUtensorMap ta = A_MN ? make_tmap_bf16(a.A, a.M, a.K, a.lda, kBK) : make_tmap_bf16(a.A, a.K, a.M, a.lda, kBM);
+  CUtensorMap tb = B_MN ? make_tmap_bf16(a.B, a.N, a.K, a.ldb, kBK) : make_tmap_bf16(a.B, a.K, a.N, a.ldb, BN);
+  EpiParams p;
+  p.M = a.M;
+  p.N = a.N;
+  p.C = a.C;
+  p.ldc = a.ldc;
+  p.c_dtype = a.c_dtype;
+  p.accumulate = a.accumulate ? 1 : 0;
+  p.bias = a.bias;
+  p.act = a.act;
+  p.alpha = a.alpha;
+  p.mask = reinterpret_cast<const __nv_bfloat16*>(a.mask);
+  p.ldm = a.ldm;
+  p.colsum = a.colsum;
+  p.status = a.status;
+  p.timeout_ns = a.timeout_ns;
+  p.num_k_tiles = ceil_div(a.K, kBK);
+  dim3 grid(ceil_div(a.M, kBM), ceil_div(a.N, BN));
+  kern<<<grid, kThreads, L::kAlloc, stream>>>(ta, tb, p);
+  FLARE_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+template <int BN, int STAGES>
+void launch_majors(const GemmArgs& a, cudaStream_t s) {
+  if (!a.a_mn && !a.b_mn) launch_cfg<BN, STAGES, false, false>(a, s);
+  else if (!a.a_mn && a.b_mn) launch_cfg<BN, STAGES, false, true>(a, s);
+  else if (a.a_mn && !a.b_mn) launch_cfg<BN, STAGES, true, false>(a, s);
+  else launch_cfg<BN, STAGES, true, true>(a, s);
+}
+
+}  // namespace
+
+// Number of streaming multiprocessors on the current device (cached).
+int device_sm_count() {
+  static int count = 0;
+  if (count == 0) {
+    int dev = 0;
+    FLARE_CUDA_CHECK(cudaGetDevice(&dev));
+    FLARE_CUDA_CHECK(cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev));
+  }
+  return count;
+}
+
+void gemm_bf16_tcgen05(const GemmArgs& a, int bn_hint, cudaStream_t stream) {
+  FLARE_CHECK(a.M > 0 && a.N > 0 && a.K > 0, "GEMM dims must be positive");
+  FLARE_CHECK(a.c_dtype == kF32 || a.c_dtype == kBF16, "GEMM output must be fp32 or bf16");
+  FLARE_CHECK(a.ldm % 8 == 0 || a.mask == nullptr, "mask pitch must be a multiple of 8 elements");
+  FLARE_CHECK((reinterpret_cast<uintptr_t>(a.C) & 15) == 0, "C must be 16-byte aligned");
+  FLARE_CHECK(a.ldc % (a.c_dtype == kF32 ? 4 : 8) == 0, "C pitch must be a multiple of 16 bytes");
+  int bn = bn_hint;
+  if (bn == 0) {
+    // Pick the widest tile that still yields at least one wave of CTAs.
+    const int sms = device_sm_count();
+    const int mt = ceil_div(a.M, kBM);
+    bn = 256;
+    while (bn > 64 && static_cast<int64_t>(mt) * ceil_div(a.N, bn) < sms) bn >>= 1;
+    if (a.N <= 64) bn = 64;
+  }
+  if (bn == 64) launch_majors<64, 4>(a, stream);
+  else if (bn == 128) launch_majors<128, 3>(a, stream);
+  else launch_majors<256, 4>(a, stream);
+}
+
+}  // namespace flare

@@ -1,0 +1,227 @@
+"""DLRM-style ranking model: B200 fused path and a plain PyTorch reference.
+
+``DLRM`` (the product path) runs one training step as a fixed sequence of
+hand-written sm_100a kernels on static buffers, so the whole step can be
+captured in a CUDA graph:
+
+    cast(dense) -> bottom MLP (tcgen05 GEMMs, bias+ReLU epilogues)
+    sharded embedding forward (ids all-to-all + gather/pool + pooled all-to-all, one kernel)
+    pairwise dot interaction -> top MLP -> fused head + BCE (fwd + bwd)
+    top MLP backward (fused ReLU-mask / bias-grad epilogues) -> interaction backward
+    bottom MLP backward -> sharded embedding backward (grad all-to-all + dedup + row-wise optimizer)
+    dense optimizer (fused reduce-scatter + Adam + all-gather when data parallel)
+
+``DLRMTorch`` is the same model in plain PyTorch autograd (nn.EmbeddingBag,
+nn.Linear, torch optimizers): the CPU configuration, the numerics oracle and
+the library baseline arm (cuBLAS + NCCL through DDP) of the benchmark.
+
+The reference ships no concrete DLRM; applications build models from its MLP
+and embedding layers (src/flare/jax/layers/base.py:27,
+src/flare/jax/layers/embedding.py:13) and train them with row-wise sparse
+optimizers in its external store (src/flare/runtime/fluxway/workers/
+dynamic_embedding.py:69-106).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn as nn
+
+from ..ops.dense import cast_pad_bf16, head_bce, interaction_backward, interaction_forward, interaction_out_width
+from ..parallel.symm import SymmetricHeap
+from ..sparse.collection import ShardedEmbeddingBagCollection
+from ..sparse.config import SparseOptimizerConfig, SparseTableSpec
+from ..training.flat import DenseOptimizerConfig, DenseState, FlatParams
+from .mlp import MLPTower, pad_to
+
+
+@dataclass
+class DLRMConfig:
+    tables: list[SparseTableSpec]
+    num_dense: int = 13
+    bottom: tuple[int, ...] = (512, 256, 128)
+    top: tuple[int, ...] = (1024, 1024, 512, 256)
+    num_targets: int = 1
+    dense_optimizer: DenseOptimizerConfig = field(default_factory=DenseOptimizerConfig)
+    sparse_optimizer: SparseOptimizerConfig = field(default_factory=SparseOptimizerConfig)
+
+    def __post_init__(self):
+        dims = {t.embedding_dim for t in self.tables}
+        if dims != {self.bottom[-1]}:
+            raise ValueError("every table's embedding_dim must equal the bottom MLP output width")
+
+    @property
+    def embedding_dim(self) -> int:
+        return self.bottom[-1]
+
+    @property
+    def interaction_width(self) -> int:
+        return interaction_out_width(len(self.tables), self.embedding_dim)
+
+    def dense_flops_per_sample(self) -> float:
+        """Forward+backward FLOPs of the dense part (GEMMs + interaction), per sample."""
+        dims_b = [pad_to(self.num_dense)] + list(self.bottom)
+        dims_t = [self.interaction_width] + list(self.top)
+        f = sum(2 * a * b for a, b in zip(dims_b[:-1], dims_b[1:]))
+        f += sum(2 * a * b for a, b in zip(dims_t[:-1], dims_t[1:]))
+        T = len(self.tables) + 1
+        f += 2 * T * T * self.embedding_dim // 2
+        return 3.0 * f
+
+
+def dlrm_benchmark_tables(vocab_sizes: list[int], dim: int = 128, optimizer: SparseOptimizerConfig | None = None,
+                          value_dtype: str = "float32") -> list[SparseTableSpec]:
+    opt = optimizer or SparseOptimizerConfig(kind="rowwise_adagrad", learning_rate=0.01)
+    return [SparseTableSpec(f"t{i}", int(v), dim, optimizer=opt, value_dtype=value_dtype)
+            for i, v in enumerate(vocab_sizes)]
+
+
+class DLRM:
+    """Fused B200 DLRM for one rank's local batch."""
+
+    def __init__(self, cfg: DLRMConfig, batch_size: int, *, max_bag_size: int, rank: int = 0, world_size: int = 1,
+                 device: torch.device | None = None, heap: SymmetricHeap | None = None, seed: int = 0,
+                 global_batch_size: int | None = None, values_capacity: int | None = None):
+        self.cfg = cfg
+        self.B = int(batch_size)
+        self.global_B = int(global_batch_size or batch_size * world_size)
+        self.rank, self.world = rank, world_size
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        dev = self.device
+        D = cfg.embedding_dim
+        F = len(cfg.tables)
+        self.F = F
+
+        params = FlatParams()
+        self.bottom = MLPTower("bottom", [cfg.num_dense] + list(cfg.bottom), params, relu_last=True)
+        self.top = MLPTower("top", [cfg.interaction_width] + list(cfg.top), params, relu_last=True)
+        H = cfg.top[-1]
+        params.register("head.weight", (cfg.num_targets, H), "normal", (2.0 / (H + 1)) ** 0.5)
+        params.register("head.bias", (cfg.num_targets,), "zeros")
+        self.params = params
+        self.dense = DenseState(params, cfg.dense_optimizer, device=dev, rank=rank, world_size=world_size,
+                                heap=heap, seed=seed)
+        self.bottom.bind(self.dense, self.B)
+        self.top.bind(self.dense, self.B)
+        self.head_w = self.dense.compute_view("head.weight")
+        self.head_b = self.dense.compute_view("head.bias")
+        self.head_dw = self.dense.grad_view("head.weight")
+        self.head_db = self.dense.grad_view("head.bias")
+
+        self.emb = ShardedEmbeddingBagCollection(
+            cfg.tables, self.B, max_bag_size=max_bag_size, rank=rank, world_size=world_size, device=dev, heap=heap,
+            optimizer=cfg.sparse_optimizer, seed=seed, values_capacity=values_capacity)
+
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        self.dense_in = torch.zeros(self.B, cfg.num_dense, dtype=torch.float32, device=dev)
+        self.labels = torch.zeros(self.B, cfg.num_targets, dtype=torch.float32, device=dev)
+        self.xd = torch.zeros(self.B, self.bottom.in_dim, **bf)
+        self.inter = torch.zeros(self.B, cfg.interaction_width, **bf)
+        self.dbot = torch.empty(self.B, D, **bf)
+        self.dh = torch.empty(self.B, H, **bf)
+        self.logits = torch.zeros(self.B, cfg.num_targets, dtype=torch.float32, device=dev)
+        self.loss_sum = torch.zeros(1, dtype=torch.float32, device=dev)
+
+    # ------------------------------------------------------------------ data
+    def set_batch(self, dense: torch.Tensor, labels: torch.Tensor, offsets: torch.Tensor, values: torch.Tensor,
+                  non_blocking: bool = True) -> None:
+        self.dense_in.copy_(dense, non_blocking=non_blocking)
+        self.labels.copy_(labels.reshape(self.B, -1), non_blocking=non_blocking)
+        self.emb.set_input(offsets, values, non_blocking=non_blocking)
+
+    # ------------------------------------------------------------------ step
+    def forward_backward(self) -> torch.Tensor:
+        """Forward + backward of the local batch; gradients land in the flat/sparse buffers."""
+        cast_pad_bf16(self.dense_in, self.xd)
+        bot = self.bottom.forward(self.xd)
+        pooled = self.emb.forward()
+        interaction_forward(bot, pooled, self.F, self.inter)
+        h = self.top.forward(self.inter)
+        self.loss_sum.zero_()
+        head_bce(h, self.head_w, self.head_b, self.labels, grad_scale=1.0 / self.global_B, logits=self.logits,
+                 loss_sum=self.loss_sum, dh=self.dh, dw=self.head_dw, db=self.head_db)
+        dinter = self.top.backward(self.dh, need_input_grad=True)
+        interaction_backward(dinter, bot, pooled, self.F, self.dbot, self.emb.grad_input, relu_mask_bot=True)
+        self.bottom.backward(self.dbot, need_input_grad=False)
+        return self.loss_sum
+
+    def train_step(self) -> torch.Tensor:
+        """One full optimizer step; returns the device scalar sum of per-sample losses."""
+        loss = self.forward_backward()
+        self.emb.backward()
+        self.dense.apply()
+        return loss
+
+    def predict(self) -> torch.Tensor:
+        """Forward only (eval): sigmoid probabilities [B, T]; no state changes besides staging."""
+        cast_pad_bf16(self.dense_in, self.xd)
+        bot = self.bottom.forward(self.xd)
+        pooled = self.emb.forward()
+        interaction_forward(bot, pooled, self.F, self.inter)
+        h = self.top.forward(self.inter)
+        x = h.float() @ self.head_w.float().t() + self.head_b.float()
+        return torch.sigmoid(x)
+
+    def check(self) -> None:
+        self.emb.check()
+        if self.dense.status is not None:
+            self.dense.status.check("dense optimizer")
+
+
+# ---------------------------------------------------------------------------
+# Plain PyTorch reference / baseline
+# ---------------------------------------------------------------------------
+class DLRMTorch(nn.Module):
+    """DLRM in plain PyTorch: nn.EmbeddingBag (sum), nn.Linear towers, dot interaction."""
+
+    def __init__(self, cfg: DLRMConfig, *, dtype: torch.dtype = torch.float32, sparse_grad: bool = True):
+        super().__init__()
+        self.cfg = cfg
+        D = cfg.embedding_dim
+        self.embs = nn.ModuleList(
+            nn.EmbeddingBag(t.num_embeddings, t.embedding_dim, mode=t.pooling, sparse=sparse_grad)
+            for t in cfg.tables)
+        for e, t in zip(self.embs, cfg.tables):
+            nn.init.uniform_(e.weight, -t.init_scale, t.init_scale)
+
+        def mlp(dims):
+            layers = []
+            for a, b in zip(dims[:-1], dims[1:]):
+                layers += [nn.Linear(a, b), nn.ReLU()]
+            return nn.Sequential(*layers)
+
+        self.bottom = mlp([cfg.num_dense] + list(cfg.bottom))
+        T = len(cfg.tables) + 1
+        self.npairs = T * (T - 1) // 2
+        self.top = mlp([D + self.npairs] + list(cfg.top))
+        self.head = nn.Linear(cfg.top[-1], cfg.num_targets)
+        ii, jj = torch.tril_indices(T, T, offset=-1)
+        self.register_buffer("ii", ii, persistent=False)
+        self.register_buffer("jj", jj, persistent=False)
+        self.compute_dtype = dtype
+
+    def pooled(self, offsets: torch.Tensor, values: torch.Tensor, B: int) -> torch.Tensor:
+        outs = []
+        offs = offsets.long()
+        vals = values.long()
+        for f, e in enumerate(self.embs):
+            beg = offs[f * B:(f + 1) * B + 1]
+            ids = vals[beg[0]:beg[-1]]
+            outs.append(e(ids, beg[:-1] - beg[0]))
+        return torch.stack(outs, 1)
+
+    def forward(self, dense: torch.Tensor, offsets: torch.Tensor, values: torch.Tensor) -> torch.Tensor:
+        B = dense.shape[0]
+        with torch.autocast(device_type=dense.device.type, dtype=self.compute_dtype,
+                            enabled=self.compute_dtype != torch.float32):
+            bot = self.bottom(dense)
+            emb = self.pooled(offsets, values, B).to(bot.dtype)
+            z = torch.cat([bot.unsqueeze(1), emb], 1)
+            zz = torch.bmm(z, z.transpose(1, 2))
+            inter = torch.cat([bot, zz[:, self.ii, self.jj]], 1)
+            h = self.top(inter)
+            return self.head(h).float()
+
+
+__all__ = ["DLRM", "DLRMConfig", "DLRMTorch", "dlrm_benchmark_tables"]

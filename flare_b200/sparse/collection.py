@@ -1,0 +1,337 @@
+"""Sharded embedding-bag collection over the GPUs' HBM with fused all-to-alls.
+
+This is the B200 replacement of the reference's sparse-embedding role
+(DynamicSparseEmbeddingSPMD, src/flare/runtime/fluxway/workers/
+dynamic_embedding.py:134-716) together with the compute-side pooled gather /
+scatter (recipes/recsys/ranking/workers/train_worker.py:271-553).  Instead of
+routing ids and values between Ray roles, every rank owns the shards given by
+the sharding plan and one launch per direction does the exchange in-kernel:
+
+* ``forward()``: every owner reads the ids of each rank's local batch straight
+  from that rank's input buffer (NVLink P2P), gathers and pools its HBM rows
+  in fp32 and writes the pooled rows straight into the requesting rank's
+  pooled-output buffer.
+* ``backward()``: every owner pulls the pooled gradients of its columns from
+  each rank, deduplicates ids, reduces per row in fp32 and applies the
+  row-wise optimizer in place (the gradient never materialises as a dense
+  table gradient).
+
+Input layout (per rank, "keyed jagged"): ``offsets`` int32 ``[F*B+1]`` and
+``values`` int32 ids, feature-major: the ids of feature f for sample b are
+``values[offsets[f*B+b]:offsets[f*B+b+1]]``.  Ids index rows of the table
+directly (static vocabulary); negative ids are padding and are skipped.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from .._native import DEFAULT_TIMEOUT_NS, DeviceStatus, dtype_code, native
+from ..ops.dense import init_uniform_
+from ..parallel.symm import FlagRegion, SymmetricHeap
+from .config import SparseOptimizerConfig, SparseTableSpec
+from .planner import ShardingPlan, plan_sharding
+from .precision import TORCH_DTYPES
+
+# ShardDesc layout shared with embedding.cuh (int32 x4, int64 x3, int32 x2 = 48 bytes)
+_SHARD_DTYPE = np.dtype([
+    ("feature", "<i4"), ("col_begin", "<i4"), ("ncols", "<i4"), ("out_col", "<i4"),
+    ("rows", "<i8"), ("weight_off", "<i8"), ("row_base", "<i8"),
+    ("pooling", "<i4"), ("pad_", "<i4"),
+])
+assert _SHARD_DTYPE.itemsize == 48
+
+FLAG_FWD_IN, FLAG_FWD_OUT, FLAG_BWD_IN, NUM_FLAG_ARRAYS = 0, 1, 2, 3
+
+
+@dataclass
+class LocalShard:
+    table: int
+    spec: SparseTableSpec
+    col_begin: int
+    ncols: int
+    out_col: int
+    weight_off: int
+    row_base: int
+
+
+class ShardedEmbeddingBagCollection:
+    def __init__(
+        self,
+        tables: list[SparseTableSpec],
+        batch_size: int,
+        *,
+        max_bag_size: int,
+        rank: int = 0,
+        world_size: int = 1,
+        device: torch.device | None = None,
+        heap: SymmetricHeap | None = None,
+        plan: ShardingPlan | None = None,
+        optimizer: SparseOptimizerConfig | None = None,
+        seed: int = 0,
+        out_dtype: torch.dtype = torch.bfloat16,
+        grad_dtype: torch.dtype = torch.bfloat16,
+        chunk: int = 64,
+        values_capacity: int | None = None,
+        timeout_ns: int = DEFAULT_TIMEOUT_NS,
+        init: bool = True,
+    ):
+        if not tables:
+            raise ValueError("at least one table is required")
+        self.tables = list(tables)
+        self.features = [t.feature_name for t in tables]
+        if len(set(self.features)) != len(self.features):
+            raise ValueError("every table must read a distinct feature")
+        vdt = {t.value_dtype for t in tables}
+        if len(vdt) != 1:
+            raise ValueError("all tables of one collection share a value dtype")
+        self.value_dtype = TORCH_DTYPES[vdt.pop()]
+        self.optimizer = optimizer or tables[0].optimizer
+        self.B = int(batch_size)
+        self.F = len(tables)
+        self.rank, self.world = rank, world_size
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.plan = plan or plan_sharding(self.tables, world_size)
+        self.total_dim = self.plan.total_dim
+        self.max_bag = int(max_bag_size)
+        self.chunk = int(chunk)
+        self.timeout_ns = int(timeout_ns)
+        self.out_dtype, self.grad_dtype = out_dtype, grad_dtype
+        self.step = 0
+        dev = self.device
+
+        # ---- local shards ----
+        self.shards: list[LocalShard] = []
+        woff = 0
+        rbase = 0
+        for p in self.plan.for_rank(rank):
+            spec = self.tables[p.table]
+            self.shards.append(LocalShard(p.table, spec, p.col_begin, p.ncols, self.plan.out_cols[p.table] + p.col_begin,
+                                          woff, rbase))
+            woff += spec.num_embeddings * p.ncols
+            rbase += spec.num_embeddings
+        self.num_local_elems, self.num_local_rows = woff, rbase
+        self.ncols_max = max([s.ncols for s in self.shards], default=4)
+        self.vec = 2 if self.ncols_max > 128 else 1
+        for s in self.shards:
+            g = s.ncols // (4 * self.vec)
+            if g < 1 or g > 32 or (g & (g - 1)):
+                raise ValueError(f"shard width {s.ncols} unsupported with vec={self.vec}")
+
+        desc = np.zeros(max(len(self.shards), 1), dtype=_SHARD_DTYPE)
+        for i, s in enumerate(self.shards):
+            desc[i] = (self.features.index(s.spec.feature_name), s.col_begin, s.ncols, s.out_col,
+                       s.spec.num_embeddings, s.weight_off, s.row_base, 1 if s.spec.pooling == "mean" else 0, 0)
+        self.shard_desc = torch.from_numpy(desc.view(np.uint8).copy()).to(dev)
+
+        # ---- parameters and optimizer state (local HBM) ----
+        self.weights = torch.empty(max(woff, 4), dtype=self.value_dtype, device=dev)
+        if init:
+            for s in self.shards:
+                n = s.spec.num_embeddings * s.ncols
+                view = self.weights[s.weight_off:s.weight_off + n]
+                stream_seed = (seed * 1_000_003 + s.table * 7919 + s.col_begin) & 0x7FFFFFFF
+                init_uniform_(view, -s.spec.init_scale, s.spec.init_scale, stream_seed)
+        opt = self.optimizer
+        z32 = lambda n: torch.zeros(max(n, 4), dtype=torch.float32, device=dev)  # noqa: E731
+        self.state_row = z32(rbase) if opt.needs_row_state else None
+        self.state_m = z32(woff) if opt.needs_m else None
+        self.state_v = z32(woff) if opt.needs_v else None
+        self.score = z32(rbase) if opt.needs_score else None
+        self.lut = (torch.tensor(opt.custom_lut, dtype=torch.float32, device=dev)
+                    if opt.dynamic_lr_policy == "custom_lut" else None)
+
+        # ---- per-row dedup scratch (returns to zero after every backward) ----
+        self.row_count = torch.zeros(max(rbase, 4), dtype=torch.int32, device=dev)
+        self.row2u = torch.zeros(max(rbase, 4), dtype=torch.int32, device=dev)
+
+        # ---- staging ----
+        ns = max(len(self.shards), 1)
+        self.stage_cap = self.B * self.max_bag
+        nslot = ns * world_size
+        self.stage_ids = torch.empty(nslot * self.stage_cap, dtype=torch.int32, device=dev)
+        self.stage_bag = torch.empty(nslot * self.stage_cap, dtype=torch.int32, device=dev)
+        self.stage_count = torch.zeros(nslot, dtype=torch.int32, device=dev)
+        self.stage_len = torch.zeros(nslot * self.B, dtype=torch.int32, device=dev)
+        self.grad_stage_ld = self.ncols_max
+        self.grad_stage = torch.empty(nslot * self.B * self.ncols_max, dtype=grad_dtype, device=dev)
+        self.max_occ = nslot * self.stage_cap
+        self.uniq_row = torch.empty(self.max_occ, dtype=torch.int64, device=dev)
+        self.uniq_shard = torch.empty(self.max_occ, dtype=torch.int32, device=dev)
+        self.num_unique = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.seg_start = torch.empty(self.max_occ + 1, dtype=torch.int32, device=dev)
+        self.block_sums = torch.empty(512, dtype=torch.int32, device=dev)
+        self.occ = torch.empty(self.max_occ, dtype=torch.int32, device=dev)
+        nchunks = (self.max_occ + self.chunk - 1) // self.chunk
+        self.carry = torch.zeros(nchunks * 128 * self.vec, dtype=torch.float32, device=dev)
+        self.span_u = torch.full((nchunks,), -1, dtype=torch.int32, device=dev)
+
+        # ---- exchange buffers (symmetric when distributed) ----
+        self.values_capacity = int(values_capacity or self.F * self.B * self.max_bag)
+        if heap is None:
+            if world_size > 1:
+                raise ValueError("a SymmetricHeap is required for world_size > 1")
+            heap = SymmetricHeap(self._heap_bytes(), device=dev)
+            self._own_heap = heap
+        else:
+            self._own_heap = None
+        self.heap = heap
+        self.in_offsets = heap.alloc((self.F * self.B + 1,), torch.int32)
+        self.in_values = heap.alloc((self.values_capacity,), torch.int32)
+        self.pooled = heap.alloc((self.B, self.total_dim), out_dtype)
+        self.grad_in = heap.alloc((self.B, self.total_dim), grad_dtype)
+        self.flags = FlagRegion(heap, NUM_FLAG_ARRAYS)
+        self._peer = {
+            "offsets": self.in_offsets.peer_ptr_tensor(dev),
+            "values": self.in_values.peer_ptr_tensor(dev),
+            "out": self.pooled.peer_ptr_tensor(dev),
+            "grad": self.grad_in.peer_ptr_tensor(dev),
+        }
+        self.status = DeviceStatus(dev)
+        self.grid = native().device_sm_count() * 8
+        self.step_dev = torch.zeros(1, dtype=torch.int32, device=dev)  # device-resident optimizer step
+
+    def _heap_bytes(self) -> int:
+        b = (self.F * self.B + 1) * 4 + self.F * self.B * self.max_bag * 4
+        b += 2 * self.B * self.total_dim * 4 + NUM_FLAG_ARRAYS * 64 + 8 * 256
+        return b + (1 << 20)
+
+    # ------------------------------------------------------------------ API
+    @property
+    def pooled_output(self) -> torch.Tensor:
+        """[B, total_dim] pooled embeddings of this rank's local batch (bf16)."""
+        return self.pooled.local
+
+    @property
+    def grad_input(self) -> torch.Tensor:
+        """[B, total_dim] buffer the dense backward writes the pooled gradients into."""
+        return self.grad_in.local
+
+    def set_input(self, offsets: torch.Tensor, values: torch.Tensor, non_blocking: bool = True) -> None:
+        """Copy this rank's keyed-jagged batch into the exchange buffers."""
+        if offsets.numel() != self.F * self.B + 1:
+            raise ValueError(f"offsets must have F*B+1 = {self.F * self.B + 1} entries")
+        n = values.numel()
+        if n > self.values_capacity:
+            raise ValueError(f"{n} ids exceed the values capacity {self.values_capacity}")
+        self.in_offsets.local.copy_(offsets, non_blocking=non_blocking)
+        self.in_values.local[:n].copy_(values, non_blocking=non_blocking)
+
+    def forward(self) -> torch.Tensor:
+        d = dict(
+            shards=self.shard_desc.data_ptr(), num_shards=len(self.shards), world=self.world, rank=self.rank,
+            Bl=self.B, F=self.F, peer_offsets=self._peer["offsets"].data_ptr(),
+            peer_values=self._peer["values"].data_ptr(), peer_out=self._peer["out"].data_ptr(),
+            out_stride=self.total_dim, weights=self.weights.data_ptr(), w_dtype=dtype_code(self.value_dtype),
+            out_dtype=dtype_code(self.out_dtype), vec=self.vec, stage_ids=self.stage_ids.data_ptr(),
+            stage_bag=self.stage_bag.data_ptr(), stage_count=self.stage_count.data_ptr(),
+            stage_len=self.stage_len.data_ptr(), stage_cap=self.stage_cap,
+            flags_local=self.flags.local_ptr, peer_flags=self.flags.peer_ptrs.data_ptr(),
+            flag_in=self.flags.slots(FLAG_FWD_IN), flag_out=self.flags.slots(FLAG_FWD_OUT),
+            epoch_ctr=self.flags.epoch_ptr(FLAG_FWD_IN), block_counter=self.flags.block_counter_ptr(FLAG_FWD_IN),
+            status=self.status.ptr, timeout_ns=self.timeout_ns, grid=self.grid,
+        )
+        native().emb_forward(d)
+        return self.pooled.local
+
+    def backward(self, step: int | None = None) -> None:
+        """Consume ``grad_input`` (pooled gradients) and update the owned shards.
+
+        The optimizer step used for bias corrections is the device counter,
+        advanced by one per call (``step`` sets it explicitly first).
+        """
+        if step is not None:
+            self.step = int(step) - 1
+            self.step_dev.fill_(self.step)
+        self.step += 1
+        native().increment_counter(self.step_dev.data_ptr())
+        op = self.optimizer.kernel_params(self.step)
+        op.update(
+            step_ptr=self.step_dev.data_ptr(),
+            state_row=self.state_row.data_ptr() if self.state_row is not None else 0,
+            state_m=self.state_m.data_ptr() if self.state_m is not None else 0,
+            state_v=self.state_v.data_ptr() if self.state_v is not None else 0,
+            score=self.score.data_ptr() if self.score is not None else 0,
+            lut=self.lut.data_ptr() if self.lut is not None else 0,
+            lut_len=self.lut.numel() if self.lut is not None else 0,
+        )
+        d = dict(
+            shards=self.shard_desc.data_ptr(), num_shards=len(self.shards), world=self.world, rank=self.rank,
+            Bl=self.B, peer_grad=self._peer["grad"].data_ptr(), out_stride=self.total_dim,
+            grad_dtype=dtype_code(self.grad_dtype), grad_stage=self.grad_stage.data_ptr(),
+            grad_stage_ld=self.grad_stage_ld, stage_ids=self.stage_ids.data_ptr(),
+            stage_bag=self.stage_bag.data_ptr(), stage_count=self.stage_count.data_ptr(),
+            stage_len=self.stage_len.data_ptr(), stage_cap=self.stage_cap, weights=self.weights.data_ptr(),
+            w_dtype=dtype_code(self.value_dtype), row_count=self.row_count.data_ptr(),
+            row2u=self.row2u.data_ptr(), uniq_row=self.uniq_row.data_ptr(), uniq_shard=self.uniq_shard.data_ptr(),
+            num_unique=self.num_unique.data_ptr(), seg_start=self.seg_start.data_ptr(),
+            block_sums=self.block_sums.data_ptr(), occ=self.occ.data_ptr(), carry=self.carry.data_ptr(),
+            span_u=self.span_u.data_ptr(), chunk=self.chunk, max_occ=self.max_occ, opt=op,
+            flags_local=self.flags.local_ptr, peer_flags=self.flags.peer_ptrs.data_ptr(),
+            flag_in=self.flags.slots(FLAG_BWD_IN), epoch_ctr=self.flags.epoch_ptr(FLAG_BWD_IN),
+            block_counter=self.flags.block_counter_ptr(FLAG_BWD_IN), status=self.status.ptr,
+            timeout_ns=self.timeout_ns, ncols_max=self.ncols_max, grid=self.grid,
+        )
+        native().emb_backward(d)
+
+    def check(self) -> None:
+        self.status.check("sharded embedding")
+
+    # ------------------------------------------------------------ state I/O
+    def shard_view(self, i: int) -> torch.Tensor:
+        s = self.shards[i]
+        n = s.spec.num_embeddings * s.ncols
+        return self.weights[s.weight_off:s.weight_off + n].view(s.spec.num_embeddings, s.ncols)
+
+    def row_state_view(self, i: int) -> torch.Tensor | None:
+        if self.state_row is None:
+            return None
+        s = self.shards[i]
+        return self.state_row[s.row_base:s.row_base + s.spec.num_embeddings]
+
+    def local_state(self) -> dict:
+        """Owned shards with optimizer state (host copies), keyed by (table, col_begin)."""
+        out = {}
+        for i, s in enumerate(self.shards):
+            entry = {"weight": self.shard_view(i).cpu(), "ncols": s.ncols}
+            if self.state_row is not None:
+                entry["state_row"] = self.row_state_view(i).cpu()
+            n = s.spec.num_embeddings * s.ncols
+            if self.state_m is not None:
+                entry["state_m"] = self.state_m[s.weight_off:s.weight_off + n].view(-1, s.ncols).cpu()
+            if self.state_v is not None:
+                entry["state_v"] = self.state_v[s.weight_off:s.weight_off + n].view(-1, s.ncols).cpu()
+            if self.score is not None:
+                entry["score"] = self.score[s.row_base:s.row_base + s.spec.num_embeddings].cpu()
+            out[(s.spec.name, s.col_begin)] = entry
+        return out
+
+    def load_local_state(self, state: dict) -> None:
+        for i, s in enumerate(self.shards):
+            entry = state[(s.spec.name, s.col_begin)]
+            self.shard_view(i).copy_(entry["weight"])
+            n = s.spec.num_embeddings * s.ncols
+            if self.state_row is not None and "state_row" in entry:
+                self.row_state_view(i).copy_(entry["state_row"])
+            if self.state_m is not None and "state_m" in entry:
+                self.state_m[s.weight_off:s.weight_off + n].copy_(entry["state_m"].reshape(-1))
+            if self.state_v is not None and "state_v" in entry:
+                self.state_v[s.weight_off:s.weight_off + n].copy_(entry["state_v"].reshape(-1))
+            if self.score is not None and "score" in entry:
+                self.score[s.row_base:s.row_base + s.spec.num_embeddings].copy_(entry["score"])
+
+    def memory_bytes(self) -> int:
+        tensors = [self.weights, self.state_row, self.state_m, self.state_v, self.score, self.row_count,
+                   self.row2u, self.stage_ids, self.stage_bag, self.grad_stage, self.uniq_row, self.occ,
+                   self.seg_start, self.carry]
+        return sum(t.numel() * t.element_size() for t in tensors if t is not None)
+
+
+def expected_math_bytes(num_ids: int, dim: int, value_bytes: int = 4) -> float:
+    """Bytes a forward gather-pool must read at minimum (for roofline reports)."""
+    return float(num_ids) * dim * value_bytes
+
+
+__all__ = ["LocalShard", "ShardedEmbeddingBagCollection", "expected_math_bytes"]

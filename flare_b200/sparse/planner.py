@@ -1,0 +1,120 @@
+"""Embedding sharding planner: table-wise + column-wise placement over ranks.
+
+Every rank holds whole tables (table-wise) or column slices of tables
+(column-wise), so a shard produces complete columns of the pooled output and
+no partial sums cross NVLink.  Placement balances lookup work
+(``expected lookups x columns``) with a longest-processing-time greedy pass,
+splitting the heaviest piece on the most loaded rank in half (by columns)
+while that lowers the maximum load, subject to an HBM budget per rank.
+
+The reference shards tables by key with a modulo PartitionSpec across
+embedding workers (src/flare/runtime/fluxway/workers/dynamic_embedding.py:
+43-66, src/flare/mesh/topology.py:20-35); key-partitioned ("row-wise")
+placement is provided for the host-tier store, while the HBM fused path uses
+this plan.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+from .config import SparseTableSpec
+
+VALID_SHARD_WIDTHS = (4, 8, 16, 32, 64, 128, 256)
+
+
+@dataclass(frozen=True)
+class ShardPlacement:
+    table: int      # index into the table list
+    col_begin: int
+    ncols: int
+    rank: int
+
+
+@dataclass(frozen=True)
+class ShardingPlan:
+    world_size: int
+    placements: tuple[ShardPlacement, ...]
+    out_cols: tuple[int, ...]   # pooled-output column of each table's first column
+    total_dim: int
+
+    def for_rank(self, rank: int) -> list[ShardPlacement]:
+        return [p for p in self.placements if p.rank == rank]
+
+    def load(self, work) -> list[float]:
+        loads = [0.0] * self.world_size
+        for p in self.placements:
+            loads[p.rank] += work[p.table] * p.ncols
+        return loads
+
+
+def _bytes_per_elem(dtype: str) -> int:
+    return 4 if dtype == "float32" else 2
+
+
+def plan_sharding(
+    tables: list[SparseTableSpec],
+    world_size: int,
+    *,
+    expected_lookups: list[float] | None = None,
+    hbm_budget_bytes: float | None = None,
+    max_rounds: int = 64,
+) -> ShardingPlan:
+    if world_size < 1:
+        raise ValueError("world_size must be >= 1")
+    for t in tables:
+        if t.embedding_dim not in VALID_SHARD_WIDTHS:
+            raise ValueError(f"table {t.name}: embedding_dim must be one of {VALID_SHARD_WIDTHS}")
+    work = list(expected_lookups) if expected_lookups is not None else [1.0] * len(tables)
+    out_cols, c = [], 0
+    for t in tables:
+        out_cols.append(c)
+        c += t.embedding_dim
+    # pieces: (table, col_begin, ncols)
+    pieces = [(i, 0, t.embedding_dim) for i, t in enumerate(tables)]
+
+    def assign(pcs):
+        order = sorted(range(len(pcs)), key=lambda k: (-work[pcs[k][0]] * pcs[k][2], pcs[k][0], pcs[k][1]))
+        loads = [0.0] * world_size
+        mem = [0.0] * world_size
+        owner = [0] * len(pcs)
+        for k in order:
+            ti, _, nc = pcs[k]
+            nbytes = tables[ti].num_embeddings * nc * _bytes_per_elem(tables[ti].value_dtype)
+            cands = sorted(range(world_size), key=lambda r: (loads[r], mem[r], r))
+            chosen = cands[0]
+            if hbm_budget_bytes is not None:
+                fits = [r for r in cands if mem[r] + nbytes <= hbm_budget_bytes]
+                if not fits:
+                    raise MemoryError(f"table {tables[ti].name} piece does not fit the HBM budget on any rank")
+                chosen = fits[0]
+            owner[k] = chosen
+            loads[chosen] += work[ti] * nc
+            mem[chosen] += nbytes
+        return owner, loads
+
+    owner, loads = assign(pieces)
+
+    def score(ld):
+        top = max(ld)
+        return (round(top, 6), sum(1 for x in ld if abs(x - top) < 1e-9))
+
+    if world_size > 1:
+        best = (score(loads), pieces, owner, loads)
+        for _ in range(max_rounds):
+            hot = loads.index(max(loads))
+            cand = [k for k in range(len(pieces)) if owner[k] == hot and pieces[k][2] // 2 in VALID_SHARD_WIDTHS
+                    and pieces[k][2] >= 16]
+            if not cand:
+                break
+            k = max(cand, key=lambda k: (work[pieces[k][0]] * pieces[k][2], -k))
+            ti, cb, nc = pieces[k]
+            pieces = pieces[:k] + [(ti, cb, nc // 2), (ti, cb + nc // 2, nc // 2)] + pieces[k + 1:]
+            owner, loads = assign(pieces)
+            if score(loads) < best[0]:
+                best = (score(loads), pieces, owner, loads)
+        _, pieces, owner, loads = best
+    placements = tuple(ShardPlacement(ti, cb, nc, owner[k]) for k, (ti, cb, nc) in enumerate(pieces))
+    return ShardingPlan(world_size, placements, tuple(out_cols), c)
+
+
+__all__ = ["ShardPlacement", "ShardingPlan", "VALID_SHARD_WIDTHS", "plan_sharding"]

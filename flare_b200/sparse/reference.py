@@ -1,0 +1,175 @@
+"""CPU reference embedding-bag collection (PyTorch, fp32).
+
+Same keyed-jagged input contract and optimizer semantics as the fused GPU
+collection; used as the numerics oracle for the CUDA kernels and as the sparse
+backend of the CPU (gloo, world size 1) configuration.  Gather/pool semantics
+follow the reference's Numba ops (src/flare/ops/sparse_gather.py:40-99) and
+its pooled scatter (src/flare/ops/sparse_scatter.py:36-95).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .config import SparseOptimizerConfig, SparseTableSpec
+from .precision import TORCH_DTYPES
+
+
+def pool_reference(weights: list[torch.Tensor], tables: list[SparseTableSpec], offsets: torch.Tensor,
+                   values: torch.Tensor, B: int) -> torch.Tensor:
+    F = len(tables)
+    dims = [t.embedding_dim for t in tables]
+    out = torch.zeros(B, sum(dims), dtype=torch.float32)
+    offs = offsets.long()
+    vals = values.long()
+    col = 0
+    for f, t in enumerate(tables):
+        beg = offs[f * B:(f + 1) * B]
+        end = offs[f * B + 1:(f + 1) * B + 1]
+        lens = end - beg
+        ids = vals[beg[0]:end[-1]] if B else vals[:0]
+        bag = torch.repeat_interleave(torch.arange(B), lens)
+        keep = ids >= 0
+        rows = weights[f].float()[ids.clamp_min(0)] * keep.unsqueeze(1)
+        pooled = torch.zeros(B, dims[f])
+        pooled.index_add_(0, bag, rows)
+        if t.pooling == "mean":
+            pooled = pooled / lens.clamp_min(1).unsqueeze(1).float()
+        out[:, col:col + dims[f]] = pooled
+        col += dims[f]
+    return out
+
+
+def row_gradients(tables, offsets, values, grad_pooled, B):
+    """Per table: (unique rows, summed fp32 gradient rows, occurrence counts)."""
+    res = []
+    offs = offsets.long()
+    vals = values.long()
+    g = grad_pooled.float()
+    col = 0
+    for f, t in enumerate(tables):
+        d = t.embedding_dim
+        beg = offs[f * B:(f + 1) * B]
+        end = offs[f * B + 1:(f + 1) * B + 1]
+        lens = end - beg
+        ids = vals[beg[0]:end[-1]] if B else vals[:0]
+        bag = torch.repeat_interleave(torch.arange(B), lens)
+        gb = g[:, col:col + d]
+        if t.pooling == "mean":
+            gb = gb / lens.clamp_min(1).unsqueeze(1).float()
+        keep = ids >= 0
+        ids, bag = ids[keep], bag[keep]
+        uniq, inv = torch.unique(ids, return_inverse=True)
+        acc = torch.zeros(uniq.numel(), d)
+        acc.index_add_(0, inv, gb[bag])
+        cnt = torch.bincount(inv, minlength=uniq.numel()).float()
+        res.append((uniq, acc, cnt))
+        col += d
+    return res
+
+
+def lr_scale_reference(opt: SparseOptimizerConfig, score: torch.Tensor) -> torch.Tensor:
+    p = opt.dynamic_lr_policy
+    if p == "constant":
+        return torch.ones_like(score)
+    if p == "sqrt_decay":
+        return torch.rsqrt(score.clamp_min(1.0))
+    if p == "log_decay":
+        return 1.0 / (1.0 + torch.log1p(score.clamp_min(0.0)))
+    if p == "inverse_decay":
+        return 1.0 / score.clamp_min(1.0)
+    if p == "cosine_frequency":
+        S = max(opt.cosine_max_score, 1e-12)
+        x = score.clamp(0.0, opt.cosine_max_score) / S
+        r = opt.cosine_min_lr_ratio
+        return r + (1 - r) * 0.5 * (1 + torch.cos(math.pi * x))
+    lut = torch.tensor(opt.custom_lut, dtype=torch.float32)
+    idx = score.clamp_min(0).floor().long().clamp_max(len(opt.custom_lut) - 1)
+    return lut[idx]
+
+
+def apply_rows_reference(opt: SparseOptimizerConfig, step: int, w: torch.Tensor, rows: torch.Tensor,
+                         g: torch.Tensor, cnt: torch.Tensor, state: dict) -> None:
+    """In-place row update of table ``w`` (fp32 math) for the given unique rows."""
+    if rows.numel() == 0:
+        return
+    wr = w[rows].float()
+    g = g + opt.weight_decay * wr
+    lr = torch.full((rows.numel(), 1), opt.learning_rate)
+    if "score" in state:
+        sc = state["score"][rows] + cnt
+        state["score"][rows] = sc
+        lr = lr * lr_scale_reference(opt, sc).unsqueeze(1)
+    t = max(step, 1)
+    bc1, bc2 = 1 - opt.beta1 ** t, 1 - opt.beta2 ** t
+    k = opt.kind
+    if k == "sgd":
+        wr = wr - lr * g
+    elif k == "rowwise_adagrad":
+        s = state["row"][rows] + (g * g).mean(1)
+        state["row"][rows] = s
+        wr = wr - lr * g / (torch.sqrt(s).unsqueeze(1) + opt.eps)
+    elif k == "adagrad":
+        m = state["m"][rows] + g * g
+        state["m"][rows] = m
+        wr = wr - lr * g / (torch.sqrt(m) + opt.eps)
+    elif k == "adam":
+        m = opt.beta1 * state["m"][rows] + (1 - opt.beta1) * g
+        v = opt.beta2 * state["v"][rows] + (1 - opt.beta2) * g * g
+        state["m"][rows], state["v"][rows] = m, v
+        wr = wr - lr * (m / bc1) / (torch.sqrt(v / bc2) + opt.eps)
+    elif k == "rowwise_adam":
+        m = opt.beta1 * state["m"][rows] + (1 - opt.beta1) * g
+        v = opt.beta2 * state["row"][rows] + (1 - opt.beta2) * (g * g).mean(1)
+        state["m"][rows], state["row"][rows] = m, v
+        wr = wr - lr * (m / bc1) / (torch.sqrt(v / bc2).unsqueeze(1) + opt.eps)
+    w[rows] = wr.to(w.dtype)
+
+
+class CpuEmbeddingBagCollection:
+    """Whole tables on the host; same forward/backward contract as the GPU collection."""
+
+    def __init__(self, tables: list[SparseTableSpec], batch_size: int, *, optimizer: SparseOptimizerConfig | None = None,
+                 seed: int = 0, weights: list[torch.Tensor] | None = None):
+        self.tables = list(tables)
+        self.B = int(batch_size)
+        self.optimizer = optimizer or tables[0].optimizer
+        self.total_dim = sum(t.embedding_dim for t in tables)
+        g = torch.Generator().manual_seed(seed)
+        if weights is None:
+            weights = [((torch.rand(t.num_embeddings, t.embedding_dim, generator=g) * 2 - 1) * t.init_scale)
+                       .to(TORCH_DTYPES[t.value_dtype]) for t in tables]
+        self.weights = weights
+        opt = self.optimizer
+        self.state = []
+        for t in tables:
+            st = {}
+            if opt.needs_row_state:
+                st["row"] = torch.zeros(t.num_embeddings)
+            if opt.needs_m:
+                st["m"] = torch.zeros(t.num_embeddings, t.embedding_dim)
+            if opt.needs_v:
+                st["v"] = torch.zeros(t.num_embeddings, t.embedding_dim)
+            if opt.needs_score:
+                st["score"] = torch.zeros(t.num_embeddings)
+            self.state.append(st)
+        self.step = 0
+        self._offsets = None
+        self._values = None
+
+    def set_input(self, offsets: torch.Tensor, values: torch.Tensor, non_blocking: bool = False) -> None:
+        self._offsets, self._values = offsets.cpu(), values.cpu()
+
+    def forward(self) -> torch.Tensor:
+        return pool_reference(self.weights, self.tables, self._offsets, self._values, self.B)
+
+    def backward(self, grad_pooled: torch.Tensor, step: int | None = None) -> None:
+        self.step = self.step + 1 if step is None else int(step)
+        for f, (rows, g, cnt) in enumerate(row_gradients(self.tables, self._offsets, self._values, grad_pooled,
+                                                         self.B)):
+            apply_rows_reference(self.optimizer, self.step, self.weights[f], rows, g, cnt, self.state[f])
+
+
+__all__ = ["CpuEmbeddingBagCollection", "apply_rows_reference", "lr_scale_reference", "pool_reference",
+           "row_gradients"]

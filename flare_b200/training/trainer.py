@@ -1,0 +1,168 @@
+"""Public training API for the fused DLRM path.
+
+``DLRMTrainer.train_step(batch)`` is the call a user makes: it copies the
+step's inputs from (pinned) host memory to the device, runs the fused training
+step (replayed from a CUDA graph after the first call when ``use_graph``), and
+returns the step's loss read back to the host.  ``train_step_async`` overlaps
+the next batch's host->device copy with the current step on a side stream and
+returns the loss of the previous step (one-step lag), which is how a
+throughput-oriented loop uses it.
+
+The reference drives the same phases through Fluxway operators
+(recipes/recsys/ranking/workers/train_worker.py:271-664: prepare_sparse_
+materialize -> prepare_jax_bind -> train_core -> scatter_sparse_grads ->
+update -> materialize_train_metrics); ``prepare_execution`` there AOT-compiles
+per signature, here it captures a CUDA graph per static shape.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from .._native import native
+from ..data.synthetic import SparseBatch
+from ..models.dlrm import DLRM, DLRMConfig
+from ..parallel.symm import SymmetricHeap
+
+
+@dataclass
+class StepResult:
+    loss: float
+    step: int
+
+
+class DLRMTrainer:
+    def __init__(self, cfg: DLRMConfig, batch_size: int, *, max_bag_size: int, rank: int = 0, world_size: int = 1,
+                 device: torch.device | None = None, seed: int = 0, use_graph: bool = True,
+                 values_capacity: int | None = None, heap_bytes: int | None = None):
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.rank, self.world = rank, world_size
+        self.B = batch_size
+        heap = None
+        if world_size > 1:
+            cap = values_capacity or len(cfg.tables) * batch_size * max_bag_size
+            total_dim = sum(t.embedding_dim for t in cfg.tables)
+            exchange = 4 * (len(cfg.tables) * batch_size + 1) + 4 * cap + 2 * 2 * batch_size * total_dim
+            dense = 6 * 16 * 1024 * 1024  # flat fp32 grads + bf16 params for up to 16M parameters
+            need = heap_bytes or (exchange + dense + 64 * 1024 * 1024)
+            heap = SymmetricHeap(need, rank=rank, world_size=world_size, device=self.device)
+        self.heap = heap
+        self.model = DLRM(cfg, batch_size, max_bag_size=max_bag_size, rank=rank, world_size=world_size,
+                          device=self.device, heap=heap, seed=seed, values_capacity=values_capacity)
+        self.use_graph = use_graph
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.launches_per_step: int | None = None
+        self.steps = 0
+        self.copy_stream = torch.cuda.Stream(device=self.device)
+        self._staged: list[SparseBatch] = []
+        self._stage_idx = 0
+        self._loss_host = torch.zeros(2, dtype=torch.float32).pin_memory()
+        self._loss_event = [torch.cuda.Event(), torch.cuda.Event()]
+        self._copy_done = torch.cuda.Event()
+        self._stage_free = [torch.cuda.Event(), torch.cuda.Event()]
+        self._stage_used = [False, False]
+        self._pending = False
+
+    # ---------------------------------------------------------------- graph
+    EAGER_STEPS = 2  # steps run eagerly (module load, allocator warm-up) before capture
+
+    def prepare_execution(self) -> None:
+        """Capture the training step as a CUDA graph.
+
+        Capture records kernels without running them, so it changes no state;
+        the first replay performs the step.  Step counters used by the
+        optimizers are device-resident and advance inside the graph.
+        """
+        if not self.use_graph or self.graph is not None:
+            return
+        torch.cuda.synchronize(self.device)
+        before = native().launch_count()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.model.train_step()
+        self.launches_per_step = native().launch_count() - before
+        # train_step advanced the host mirrors while recording; undo that
+        self.model.dense.step -= 1
+        self.model.emb.step -= 1
+        self.graph = g
+
+    def _run_step(self) -> torch.Tensor:
+        if self.use_graph and self.graph is None and self.steps >= self.EAGER_STEPS:
+            self.prepare_execution()
+        if self.graph is not None:
+            self.graph.replay()
+            self.model.dense.step += 1
+            self.model.emb.step += 1
+            return self.model.loss_sum
+        before = native().launch_count()
+        loss = self.model.train_step()
+        self.launches_per_step = native().launch_count() - before
+        return loss
+
+    # ------------------------------------------------------------------ API
+    def train_step(self, batch: SparseBatch) -> StepResult:
+        """Copy ``batch`` (host or device) in, run one step, return the loss (host float)."""
+        m = self.model
+        m.set_batch(batch.dense, batch.labels, batch.offsets, batch.values, non_blocking=True)
+        loss = self._run_step()
+        self.steps += 1
+        return StepResult(float(loss.item()) / self.B, self.steps)
+
+    def train_step_async(self, batch: SparseBatch) -> StepResult | None:
+        """Pipelined step: H2D of this batch overlaps the previous step; returns the previous step's loss."""
+        m = self.model
+        cur = torch.cuda.current_stream(self.device)
+        if not self._staged:
+            self._staged = [self._alloc_stage(batch) for _ in range(2)]
+        idx = self._stage_idx
+        stage = self._staged[idx]
+        self._stage_idx ^= 1
+        with torch.cuda.stream(self.copy_stream):
+            if self._stage_used[idx]:
+                # do not overwrite a stage until the step that read it has copied it out
+                self.copy_stream.wait_event(self._stage_free[idx])
+            for dst, src in zip((stage.dense, stage.labels, stage.offsets), (batch.dense, batch.labels, batch.offsets)):
+                dst.copy_(src, non_blocking=True)
+            stage.values[:batch.values.numel()].copy_(batch.values, non_blocking=True)
+            self._copy_done.record(self.copy_stream)
+        prev = None
+        if self._pending:
+            ev = self._loss_event[self.steps % 2]
+            ev.synchronize()
+            prev = StepResult(float(self._loss_host[self.steps % 2]) / self.B, self.steps)
+        cur.wait_event(self._copy_done)
+        m.set_batch(stage.dense, stage.labels, stage.offsets, stage.values[:batch.values.numel()], non_blocking=True)
+        self._stage_free[idx].record(cur)
+        self._stage_used[idx] = True
+        loss = self._run_step()
+        self.steps += 1
+        slot = self.steps % 2
+        self._loss_host[slot:slot + 1].copy_(loss, non_blocking=True)
+        self._loss_event[slot].record(cur)
+        self._pending = True
+        return prev
+
+    def flush(self) -> StepResult | None:
+        if not self._pending:
+            return None
+        slot = self.steps % 2
+        self._loss_event[slot].synchronize()
+        self._pending = False
+        return StepResult(float(self._loss_host[slot]) / self.B, self.steps)
+
+    def _alloc_stage(self, batch: SparseBatch) -> SparseBatch:
+        dev = self.device
+        return SparseBatch(torch.empty_like(batch.dense, device=dev), torch.empty_like(batch.labels, device=dev),
+                           torch.empty_like(batch.offsets, device=dev),
+                           torch.empty(self.model.emb.values_capacity, dtype=torch.int32, device=dev))
+
+    def check(self) -> None:
+        self.model.check()
+
+    def close(self) -> None:
+        self.graph = None
+        torch.cuda.synchronize(self.device)
+
+
+__all__ = ["DLRMTrainer", "StepResult"]

@@ -1,0 +1,107 @@
+"""Fused sharded embedding collection (world size 1) vs the CPU reference store."""
+import pytest
+import torch
+
+from flare_b200.data.synthetic import make_jagged
+from flare_b200.sparse.collection import ShardedEmbeddingBagCollection
+from flare_b200.sparse.config import SparseOptimizerConfig, SparseTableSpec
+from flare_b200.sparse.planner import ShardingPlan, ShardPlacement
+from flare_b200.sparse.reference import CpuEmbeddingBagCollection
+
+pytestmark = pytest.mark.gpu
+
+
+def _batch(B, vocabs, max_bag, seed, zipf=1.05):
+    g = torch.Generator().manual_seed(seed)
+    lengths = torch.randint(0, max_bag + 1, (len(vocabs), B), generator=g)
+    return make_jagged(lengths, vocabs, zipf, g)
+
+
+def _export(coll, tables):
+    """Full host tables assembled from the GPU shards."""
+    ws = [torch.zeros(t.num_embeddings, t.embedding_dim) for t in tables]
+    for i, s in enumerate(coll.shards):
+        ws[s.table][:, s.col_begin:s.col_begin + s.ncols] = coll.shard_view(i).float().cpu()
+    return ws
+
+
+def _cw_plan(tables):
+    pl, out, c = [], [], 0
+    for i, t in enumerate(tables):
+        out.append(c)
+        c += t.embedding_dim
+        half = t.embedding_dim // 2
+        pl += [ShardPlacement(i, 0, half, 0), ShardPlacement(i, half, half, 0)]
+    return ShardingPlan(1, tuple(pl), tuple(out), c)
+
+
+@pytest.mark.parametrize("kind", ["rowwise_adagrad", "adam", "sgd", "adagrad", "rowwise_adam"])
+@pytest.mark.parametrize("column_split", [False, True])
+def test_forward_backward_matches_reference(cuda, kind, column_split):
+    torch.manual_seed(0)
+    opt = SparseOptimizerConfig(kind=kind, learning_rate=0.05, weight_decay=0.001)
+    vocabs = [50, 1000, 7]
+    tables = [SparseTableSpec(f"t{i}", v, 64, optimizer=opt, pooling="mean" if i == 1 else "sum")
+              for i, v in enumerate(vocabs)]
+    B, max_bag = 96, 20
+    plan = _cw_plan(tables) if column_split else None
+    coll = ShardedEmbeddingBagCollection(tables, B, max_bag_size=max_bag, device=cuda, plan=plan, optimizer=opt,
+                                         seed=3, chunk=8)
+    ref = CpuEmbeddingBagCollection(tables, B, optimizer=opt, weights=_export(coll, tables))
+    for step in range(1, 4):
+        offs, vals = _batch(B, vocabs, max_bag, seed=step)
+        coll.set_input(offs.to(cuda), vals.to(cuda), non_blocking=False)
+        ref.set_input(offs, vals)
+        pooled = coll.forward()
+        pooled_ref = ref.forward()
+        torch.testing.assert_close(pooled.float().cpu(), pooled_ref.to(torch.bfloat16).float(), rtol=2e-2, atol=1e-3)
+        grad = (torch.randn(B, coll.total_dim) * 0.1).to(torch.bfloat16)
+        coll.grad_input.copy_(grad.to(cuda))
+        coll.backward(step)
+        ref.backward(grad.float(), step)
+        torch.cuda.synchronize()
+        coll.check()
+        for w_gpu, w_ref in zip(_export(coll, tables), ref.weights):
+            torch.testing.assert_close(w_gpu, w_ref, rtol=1e-4, atol=1e-5)
+    assert int(coll.row_count.abs().max()) == 0  # per-row counters returned to zero
+
+
+def test_hot_rows_span_chunks(cuda):
+    """A few rows hit thousands of times (Zipf head) exercise the spanning-row carry path."""
+    opt = SparseOptimizerConfig(kind="rowwise_adagrad", learning_rate=0.1)
+    tables = [SparseTableSpec("hot", 4, 128, optimizer=opt)]
+    B, max_bag = 512, 32
+    coll = ShardedEmbeddingBagCollection(tables, B, max_bag_size=max_bag, device=cuda, optimizer=opt, chunk=64)
+    ref = CpuEmbeddingBagCollection(tables, B, optimizer=opt, weights=_export(coll, tables))
+    offs, vals = _batch(B, [4], max_bag, seed=11)
+    coll.set_input(offs.to(cuda), vals.to(cuda), non_blocking=False)
+    ref.set_input(offs, vals)
+    coll.forward()
+    grad = torch.randn(B, 128).to(torch.bfloat16)
+    coll.grad_input.copy_(grad.to(cuda))
+    coll.backward(1)
+    ref.backward(grad.float(), 1)
+    torch.cuda.synchronize()
+    coll.check()
+    torch.testing.assert_close(_export(coll, tables)[0], ref.weights[0], rtol=1e-4, atol=1e-5)
+    assert int(coll.span_u.max()) == -1 and float(coll.carry.abs().max()) == 0.0
+
+
+def test_lr_policies(cuda):
+    for pol, extra in [("sqrt_decay", {}), ("cosine_frequency", dict(cosine_min_lr_ratio=0.1, cosine_max_score=50.0)),
+                       ("custom_lut", dict(custom_lut=(1.0, 0.5, 0.25))), ("log_decay", {}), ("inverse_decay", {})]:
+        opt = SparseOptimizerConfig(kind="sgd", learning_rate=0.5, dynamic_lr_policy=pol, **extra)
+        tables = [SparseTableSpec("t", 30, 32, optimizer=opt)]
+        coll = ShardedEmbeddingBagCollection(tables, 16, max_bag_size=8, device=cuda, optimizer=opt)
+        ref = CpuEmbeddingBagCollection(tables, 16, optimizer=opt, weights=_export(coll, tables))
+        for step in (1, 2):
+            offs, vals = _batch(16, [30], 8, seed=20 + step)
+            coll.set_input(offs.to(cuda), vals.to(cuda), non_blocking=False)
+            ref.set_input(offs, vals)
+            coll.forward()
+            grad = torch.randn(16, 32).to(torch.bfloat16)
+            coll.grad_input.copy_(grad.to(cuda))
+            coll.backward(step)
+            ref.backward(grad.float(), step)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(_export(coll, tables)[0], ref.weights[0], rtol=1e-4, atol=1e-5, msg=pol)

@@ -1,0 +1,65 @@
+"""tcgen05 GEMM numerics against an fp32 PyTorch reference of the same op."""
+import pytest
+import torch
+
+from flare_b200.ops.gemm import gemm, gemm_reference
+
+pytestmark = pytest.mark.gpu
+
+
+def _rand(rows, cols, device):
+    """bf16 [rows, cols] view whose row pitch is padded to a multiple of 8 elements."""
+    ld = (cols + 7) // 8 * 8
+    full = (torch.randn(rows, ld, device=device) * 0.5).to(torch.bfloat16)
+    return full[:, :cols]
+
+
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (256, 192, 320), (300, 100, 200), (1024, 512, 1024)])
+def test_gemm_majors(cuda, a_t, b_t, M, N, K):
+    torch.manual_seed(0)
+    a = _rand(K, M, device=cuda) if a_t else _rand(M, K, device=cuda)
+    b = _rand(K, N, device=cuda) if b_t else _rand(N, K, device=cuda)
+    # pad leading dims to multiples of 8 as the kernels require 16-byte row pitch
+    out = torch.zeros(M, (N + 7) // 8 * 8, dtype=torch.float32, device=cuda)[:, :N]
+    gemm(a, b, a_t=a_t, b_t=b_t, out=out)
+    ref = gemm_reference(a, b, a_t=a_t, b_t=b_t)
+    torch.cuda.synchronize()
+    err = (out - ref).abs().max().item()
+    scale = ref.abs().max().item()
+    assert err <= 2e-3 * scale + 1e-3, (err, scale)
+
+
+@pytest.mark.parametrize("bn", [64, 128, 256])
+def test_gemm_tile_widths_bf16_out(cuda, bn):
+    torch.manual_seed(1)
+    M, N, K = 512, 512, 256
+    a, b = _rand(M, K, device=cuda), _rand(N, K, device=cuda)
+    bias = (torch.randn(N, device=cuda) * 0.1).to(torch.bfloat16)
+    out = gemm(a, b, bias=bias, relu=True, bn=bn)
+    ref = gemm_reference(a, b, bias=bias, relu=True)
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+
+
+def test_gemm_epilogue_mask_colsum_accumulate(cuda):
+    torch.manual_seed(2)
+    M, N, K = 384, 256, 192
+    a, b = _rand(M, K, device=cuda), _rand(K, N, device=cuda)
+    mask = _rand(M, N, device=cuda)
+    colsum = torch.zeros(N, device=cuda)
+    out = gemm(a, b, b_t=True, mask=mask, colsum=colsum)
+    ref = gemm_reference(a, b, b_t=True, mask=mask)
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(colsum, ref.sum(0), rtol=1e-2, atol=5e-2)
+    acc = torch.ones(M, N, device=cuda)
+    gemm(a, b, b_t=True, out=acc, accumulate=True, alpha=0.5)
+    torch.testing.assert_close(acc, 1 + 0.5 * gemm_reference(a, b, b_t=True), rtol=2e-3, atol=2e-3)
+
+
+def test_gemm_small_k_padded_input(cuda):
+    # bottom-MLP first layer: K = 16 (13 features padded)
+    torch.manual_seed(3)
+    x = _rand(1024, 16, device=cuda)
+    w = _rand(512, 16, device=cuda)
+    out = gemm(x, w, out_dtype=torch.float32)
+    torch.testing.assert_close(out, gemm_reference(x, w), rtol=2e-3, atol=2e-3)
