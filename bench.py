@@ -15,7 +15,7 @@ Timing: W untimed warm-up steps, then K steps bracketed by a barrier and
 training stream; the reported time is the max over ranks.  Each timed step
 reads a different pre-generated batch, and the embedding tables (>100 GB per
 node) are far larger than L2, so no L2 flush is needed.  SM clocks and throttle
-reasons are sampled with nvidia-smi during the timed region.  The e2e number
+reasons are sampled through NVML (read-only) during the timed region.  The e2e number
 goes through ``DLRMTrainer.train_step_async`` with inputs in pinned host memory:
 each step copies that step's inputs host->device and reads a loss back.
 """
@@ -24,8 +24,6 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import statistics
-import subprocess
 import sys
 import time
 
@@ -50,52 +48,6 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--seed", type=int, default=0)
     return p.parse_args()
-
-
-class ClockSampler:
-    """nvidia-smi sampler for SM clocks and throttle reasons during the timed region."""
-
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
-
-    def __init__(self, gpu_index: int):
-        self.gpu_index = gpu_index
-        self.proc = None
-
-    def start(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.gpu_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except (OSError, FileNotFoundError):
-            self.proc = None
-
-    def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 7:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                mx.append(float(parts[1]))
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[3:7]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
 
 
 def emit(obj):
@@ -131,6 +83,7 @@ def main():
     from flare_b200.parallel.dist import barrier, init_distributed, max_over_ranks, shutdown
     from flare_b200.sparse.config import SparseOptimizerConfig
     from flare_b200.training.flat import DenseOptimizerConfig
+    from flare_b200.utils.clocks import ClockSampler
 
     info = init_distributed(timeout_s=300)
     rank, world = info.rank, max(info.world_size, 1)
@@ -173,9 +126,7 @@ def main():
     launches_per_step = trainer.launches_per_step
     barrier()
     torch.cuda.synchronize()
-    clocks = ClockSampler(dev.index if os.environ.get("CUDA_VISIBLE_DEVICES") is None else
-                          int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[dev.index]))
-    clocks.start()
+    clocks = ClockSampler(dev.index).start()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(stream)
     for i in range(args.steps):

@@ -181,7 +181,7 @@ __global__ void __launch_bounds__(kHeadWarps * 32) head_bce_kernel(HeadBceParams
       if (p.valid_count >= 0 && b >= p.valid_count) wt = 0.f;
       // softplus(x) - y*x = max(x,0) - x*y + log1p(exp(-|x|))
       const float l = fmaxf(x, 0.f) - x * y + log1pf(__expf(-fabsf(x)));
-      loss_acc += wt * l;
+      if (lane == 0) loss_acc += wt * l;  // x is warp-uniform: count each sample once
       const float sg = 1.f / (1.f + __expf(-x));
       const float dl = wt * (sg - y) * p.grad_scale;
       float* dwp = mine + t * H + lane * PER;
@@ -202,7 +202,6 @@ __global__ void __launch_bounds__(kHeadWarps * 32) head_bce_kernel(HeadBceParams
     for (int w = 0; w < kHeadWarps; ++w) acc += hs[w * T * (H + 1) + i];
     if (acc != 0.f) atomicAdd(i < T * H ? p.dw + i : p.db + (i - T * H), acc);
   }
-  loss_acc = warp_sum(loss_acc);
   if (lane == 0 && loss_acc != 0.f) atomicAdd(p.loss_sum, loss_acc);
 }
 

@@ -201,6 +201,27 @@ class DLRMTorch(nn.Module):
         self.register_buffer("jj", jj, persistent=False)
         self.compute_dtype = dtype
 
+    @torch.no_grad()
+    def load_from_fused(self, fused: "DLRM") -> "DLRMTorch":
+        """Copy the fused model's compute weights and (exported) tables into this module."""
+        ds = fused.dense
+
+        def copy_tower(seq, tower):
+            lin = [m for m in seq if isinstance(m, nn.Linear)]
+            for layer, wn, bn in zip(lin, tower.wnames, tower.bnames):
+                w = ds.compute_view(wn).float()
+                layer.weight.copy_(w[:, :layer.weight.shape[1]])
+                layer.bias.copy_(ds.compute_view(bn).float())
+
+        copy_tower(self.bottom, fused.bottom)
+        copy_tower(self.top, fused.top)
+        self.head.weight.copy_(ds.compute_view("head.weight").float())
+        self.head.bias.copy_(ds.compute_view("head.bias").float())
+        for i, s in enumerate(fused.emb.shards):
+            self.embs[s.table].weight[:, s.col_begin:s.col_begin + s.ncols] = fused.emb.shard_view(i).float().to(
+                self.embs[s.table].weight.device)
+        return self
+
     def pooled(self, offsets: torch.Tensor, values: torch.Tensor, B: int) -> torch.Tensor:
         outs = []
         offs = offsets.long()

@@ -25,6 +25,60 @@ def _export(coll, tables):
     return ws
 
 
+class _PieceReference:
+    """CPU reference where every column shard is an independent table."""
+
+    def __init__(self, tables, coll, opt):
+        self.tables, self.pieces = tables, [(s.table, s.col_begin, s.ncols) for s in coll.shards]
+        full = _export(coll, tables)
+        specs = [SparseTableSpec(f"p{i}", tables[t].num_embeddings, n, optimizer=opt, pooling=tables[t].pooling,
+                                 feature=f"p{i}") for i, (t, c, n) in enumerate(self.pieces)]
+        self.inner = CpuEmbeddingBagCollection(specs, coll.B, optimizer=opt,
+                                               weights=[full[t][:, c:c + n].clone() for t, c, n in self.pieces])
+        self.B = coll.B
+
+    def _expand(self, offs, vals):
+        B = self.B
+        o, v, base = [0], [], 0
+        for t, _, _ in self.pieces:
+            seg = offs[t * B:(t + 1) * B + 1].long()
+            v.append(vals[seg[0]:seg[-1]])
+            o.extend((seg[1:] - seg[0] + base).tolist())
+            base += int(seg[-1] - seg[0])
+        return torch.tensor(o, dtype=torch.int32), torch.cat(v)
+
+    def set_input(self, offs, vals):
+        self.inner.set_input(*self._expand(offs, vals))
+
+    def forward(self):
+        out = self.inner.forward()
+        res = torch.zeros(self.B, sum(t.embedding_dim for t in self.tables))
+        col, starts = 0, []
+        for t in self.tables:
+            starts.append(col)
+            col += t.embedding_dim
+        k = 0
+        for t, c, n in self.pieces:
+            res[:, starts[t] + c:starts[t] + c + n] = out[:, k:k + n]
+            k += n
+        return res
+
+    def backward(self, grad, step):
+        starts, col = [], 0
+        for t in self.tables:
+            starts.append(col)
+            col += t.embedding_dim
+        g = torch.cat([grad[:, starts[t] + c:starts[t] + c + n] for t, c, n in self.pieces], 1)
+        self.inner.backward(g, step)
+
+    @property
+    def weights(self):
+        ws = [torch.zeros(t.num_embeddings, t.embedding_dim) for t in self.tables]
+        for (t, c, n), w in zip(self.pieces, self.inner.weights):
+            ws[t][:, c:c + n] = w
+        return ws
+
+
 def _cw_plan(tables):
     pl, out, c = [], [], 0
     for i, t in enumerate(tables):
@@ -48,6 +102,11 @@ def test_forward_backward_matches_reference(cuda, kind, column_split):
     coll = ShardedEmbeddingBagCollection(tables, B, max_bag_size=max_bag, device=cuda, plan=plan, optimizer=opt,
                                          seed=3, chunk=8)
     ref = CpuEmbeddingBagCollection(tables, B, optimizer=opt, weights=_export(coll, tables))
+    split_ref = column_split and opt.needs_row_state
+    if split_ref:
+        # Row-wise optimizer state is kept per (row, column shard): model every
+        # column piece as its own table in the reference.
+        ref = _PieceReference(tables, coll, opt)
     for step in range(1, 4):
         offs, vals = _batch(B, vocabs, max_bag, seed=step)
         coll.set_input(offs.to(cuda), vals.to(cuda), non_blocking=False)
