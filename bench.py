@@ -153,6 +153,7 @@ def main():
     torch.cuda.synchronize()
     barrier()
     embed_ms = max_over_ranks(e0.elapsed_time(e1) / 3)
+    emb_stats = model.emb.last_step_stats()
 
     # e2e through the public API: inputs in pinned host memory, loss read back every step
     e2e = None
@@ -197,6 +198,7 @@ def main():
                        "dense_optimizer": "adam", "l2": "inputs larger than L2 (tables > 100 GB, "
                        f"{args.num_batches} distinct batches cycled)", "cuda_graph": not args.no_graph},
             "embed_ms_per_step": embed_ms,
+            "embed_stats_rank0": emb_stats,
             "clocks": clk,
             "e2e": e2e,
             "gpu_launches": (launches_per_step or 0) * args.steps,

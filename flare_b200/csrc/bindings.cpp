@@ -171,6 +171,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.grad_stage_ld = get<int64_t>(d, "grad_stage_ld");
     p.stage_ids = P<const int>(get<uintptr_t>(d, "stage_ids"));
     p.stage_bag = P<const int>(get<uintptr_t>(d, "stage_bag"));
+    p.stage_rank = P<int>(get<uintptr_t>(d, "stage_rank"));
     p.stage_count = P<const int>(get<uintptr_t>(d, "stage_count"));
     p.stage_len = P<const int>(get<uintptr_t>(d, "stage_len"));
     p.stage_cap = get<int64_t>(d, "stage_cap");
@@ -178,15 +179,22 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.w_dtype = get<int>(d, "w_dtype");
     p.row_count = P<int>(get<uintptr_t>(d, "row_count"));
     p.row2u = P<int>(get<uintptr_t>(d, "row2u"));
+    p.flags = P<int>(get<uintptr_t>(d, "flags"));
+    p.pos = P<int>(get<uintptr_t>(d, "pos"));
     p.uniq_row = P<int64_t>(get<uintptr_t>(d, "uniq_row"));
     p.uniq_shard = P<int>(get<uintptr_t>(d, "uniq_shard"));
+    p.cnt_u = P<int>(get<uintptr_t>(d, "cnt_u"));
+    p.first_gidx = P<int>(get<uintptr_t>(d, "first_gidx"));
     p.num_unique = P<int>(get<uintptr_t>(d, "num_unique"));
     p.seg_start = P<int>(get<uintptr_t>(d, "seg_start"));
     p.block_sums = P<int>(get<uintptr_t>(d, "block_sums"));
     p.occ = P<int>(get<uintptr_t>(d, "occ"));
-    p.carry = P<float>(get<uintptr_t>(d, "carry"));
-    p.span_u = P<int>(get<uintptr_t>(d, "span_u"));
-    p.chunk = get<int>(d, "chunk");
+    p.heavy = P<int>(get<uintptr_t>(d, "heavy"));
+    p.heavy_start = P<int>(get<uintptr_t>(d, "heavy_start"));
+    p.hcnt = P<int>(get<uintptr_t>(d, "hcnt"));
+    p.heavy_acc = P<float>(get<uintptr_t>(d, "heavy_acc"));
+    p.max_heavy = get<int>(d, "max_heavy");
+    p.light_max = get_or<int>(d, "light_max", 64);
     p.max_occ = get<int64_t>(d, "max_occ");
     p.opt = parse_sparse_opt(get<py::dict>(d, "opt"));
     p.flags_local = P<uint32_t>(get_or<uintptr_t>(d, "flags_local", 0));
@@ -289,8 +297,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cast_pad_bf16", [](uintptr_t x, int64_t rows, int cols, int64_t ldx, uintptr_t y, int ldy) {
     flare::cast_pad_bf16(P<const float>(x), rows, cols, ldx, P<__nv_bfloat16>(y), ldy, cur_stream());
   });
-  m.def("init_uniform", [](uintptr_t out, int dtype, int64_t n, float lo, float hi, uint64_t seed, int64_t off) {
-    flare::init_uniform(P<void>(out), dtype, n, lo, hi, seed, off, cur_stream());
+  m.def("init_uniform", [](uintptr_t out, int dtype, int64_t n, float lo, float hi, uint64_t seed, int64_t off,
+                           int ncols, int dim, int col_begin) {
+    flare::init_uniform(P<void>(out), dtype, n, lo, hi, seed, off, ncols, dim, col_begin, cur_stream());
   });
 
   m.def("sparse_gather", [](uintptr_t emb, int dtype, uintptr_t inv, int64_t slots, int dim, int pad, uintptr_t out) {

@@ -29,49 +29,119 @@ __device__ __forceinline__ void pair_of(int p, int& i, int& j) {
 
 constexpr int kInterWarps = 4;
 
+// Stage Z = [bot, emb_0..emb_{F-1}] of one sample into shared memory (bf16
+// pairs, row pitch `rowp` words).  All 16-byte global loads of a lane are
+// issued before its shared-memory stores, so the staging costs about one
+// memory round trip instead of one per word.  Rows in [T, TP) are zeroed.
+__device__ __forceinline__ void stage_z(uint32_t* z, int rowp, const __nv_bfloat16* bot,
+                                        const __nv_bfloat16* emb, int T, int TP, int D) {
+  const int lane = lane_id();
+  const int qpr = D / 8;           // uint4 per row
+  constexpr int kBatch = 8;        // uint4 loads in flight per lane
+  const int total = T * qpr;
+  for (int q0 = 0; q0 < total; q0 += 32 * kBatch) {
+    uint4 buf[kBatch];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int q = q0 + lane + 32 * k;
+      if (q < total) {
+        const int r = q / qpr, c = q - r * qpr;
+        const __nv_bfloat16* src = r == 0 ? bot + 8 * c : emb + (r - 1) * D + 8 * c;
+        buf[k] = *reinterpret_cast<const uint4*>(src);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int q = q0 + lane + 32 * k;
+      if (q < total) {
+        const int r = q / qpr, c = q - r * qpr;
+        uint32_t* dst = z + r * rowp + 4 * c;
+        dst[0] = buf[k].x;
+        dst[1] = buf[k].y;
+        dst[2] = buf[k].z;
+        dst[3] = buf[k].w;
+      }
+    }
+  }
+  for (int w = T * (D / 2) + lane; w < TP * (D / 2); w += 32) {
+    const int r = w / (D / 2), c = w - r * (D / 2);
+    z[r * rowp + c] = 0u;
+  }
+}
+
 // Z = [bot, emb_0..emb_{F-1}] (T = F+1 vectors of width D, D % 64 == 0, D <= 256)
 // out[b] = [bot (D), dots (T(T-1)/2), zero padding up to out_ld]
+// One warp per sample; Z staged in shared memory as bf16 pairs with an odd
+// row pitch (conflict-free).  Each lane computes a 3x3 tile of Z.Z^T from the
+// lower triangle (i >= j blocks): 6 shared loads feed 18 FMAs per k-pair.
 __global__ void __launch_bounds__(kInterWarps * 32) interaction_fwd_kernel(InteractionParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int T = p.F + 1;
-  const int rowp = p.D / 2 + 1;  // row pitch in 32-bit words (+1 word breaks bank conflicts)
-  uint32_t* z = reinterpret_cast<uint32_t*>(smem) + warp_id() * T * rowp;
+  const int TB = (T + 2) / 3;          // 3-row blocks
+  const int TP = TB * 3;               // padded vector count
+  const int rowp = p.D / 2 + 1;        // row pitch in 32-bit words
+  const int orow_words = (p.out_ld + 1) / 2 + 4;
+  uint32_t* z = reinterpret_cast<uint32_t*>(smem) + warp_id() * (TP * rowp + orow_words);
+  // 16-byte aligned staging row for the output
+  __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(
+      reinterpret_cast<uintptr_t>(z + TP * rowp + 3) & ~static_cast<uintptr_t>(15));
   const int lane = lane_id();
-  const int npairs = T * (T - 1) / 2;
+  const int nblk = TB * (TB + 1) / 2;  // lower-triangle blocks incl. diagonal
+  const int KW = p.D / 2;
   for (int b = blockIdx.x * kInterWarps + warp_id(); b < p.B; b += gridDim.x * kInterWarps) {
     const __nv_bfloat16* bot = p.bot + static_cast<int64_t>(b) * p.bot_ld;
     const __nv_bfloat16* emb = p.emb + static_cast<int64_t>(b) * p.emb_ld;
     __nv_bfloat16* out = p.out + static_cast<int64_t>(b) * p.out_ld;
-    // stage Z (bf16 pairs) into shared memory; copy bot to the output head
-    for (int w = lane; w < T * (p.D / 2); w += 32) {
-      const int r = w / (p.D / 2), c = w - r * (p.D / 2);
-      const uint32_t v = r == 0 ? reinterpret_cast<const uint32_t*>(bot)[c]
-                                : reinterpret_cast<const uint32_t*>(emb + (r - 1) * p.D)[c];
-      z[r * rowp + c] = v;
-      if (r == 0) reinterpret_cast<uint32_t*>(out)[c] = v;
-    }
+    stage_z(z, rowp, bot, emb, T, TP, p.D);
     __syncwarp();
-    for (int q = lane; q < npairs; q += 32) {
-      int i, j;
-      pair_of(q, i, j);
-      const uint32_t* zi = z + i * rowp;
-      const uint32_t* zj = z + j * rowp;
-      float acc = 0.f;
-#pragma unroll 8
-      for (int c = 0; c < p.D / 2; ++c) {
-        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(zi + c));
-        const float2 bb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(zj + c));
-        acc = fmaf(a.x, bb.x, acc);
-        acc = fmaf(a.y, bb.y, acc);
+    for (int blk = lane; blk < nblk; blk += 32) {
+      // blk -> (I, J) with I >= J, row-major over the lower triangle
+      int I = static_cast<int>((sqrtf(8.f * blk + 1.f) - 1.f) * 0.5f);
+      while (I * (I + 1) / 2 > blk) --I;
+      while ((I + 1) * (I + 2) / 2 <= blk) ++I;
+      const int J = blk - I * (I + 1) / 2;
+      const uint32_t* zi = z + (3 * I) * rowp;
+      const uint32_t* zj = z + (3 * J) * rowp;
+      float acc[3][3];
+#pragma unroll
+      for (int x = 0; x < 3; ++x)
+#pragma unroll
+        for (int y = 0; y < 3; ++y) acc[x][y] = 0.f;
+#pragma unroll 4
+      for (int c = 0; c < KW; ++c) {
+        float2 a[3], bb[3];
+#pragma unroll
+        for (int x = 0; x < 3; ++x) {
+          a[x] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(zi + x * rowp + c));
+          bb[x] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(zj + x * rowp + c));
+        }
+#pragma unroll
+        for (int x = 0; x < 3; ++x)
+#pragma unroll
+          for (int y = 0; y < 3; ++y) acc[x][y] = fmaf(a[x].x, bb[y].x, fmaf(a[x].y, bb[y].y, acc[x][y]));
       }
-      out[p.D + q] = __float2bfloat16_rn(acc);
+#pragma unroll
+      for (int x = 0; x < 3; ++x)
+#pragma unroll
+        for (int y = 0; y < 3; ++y) {
+          const int i = 3 * I + x, j = 3 * J + y;
+          if (i < T && j < i) orow[p.D + i * (i - 1) / 2 + j] = __float2bfloat16_rn(acc[x][y]);
+        }
     }
-    for (int c = p.D + npairs + lane; c < p.out_ld; c += 32) out[c] = __float2bfloat16_rn(0.f);
+    const int npairs = T * (T - 1) / 2;
+    for (int c = lane; c < p.D / 2; c += 32) reinterpret_cast<uint32_t*>(orow)[c] = z[c];  // bot (row 0)
+    for (int c = p.D + npairs + lane; c < p.out_ld; c += 32) orow[c] = __float2bfloat16_rn(0.f);
+    __syncwarp();
+    for (int q = lane; q < p.out_ld / 8; q += 32)
+      reinterpret_cast<uint4*>(out)[q] = reinterpret_cast<const uint4*>(orow)[q];
     __syncwarp();
   }
 }
 
 // dZ_i = sum_{j != i} dDot(i,j) Z_j ; d(bot) += dOut[:, :D]; ReLU mask of bot.
+// One warp per sample: the symmetric T x T matrix S is built in shared memory;
+// a lane owns D/32 columns and accumulates 9 output rows at a time.
+template <int PER>
 __global__ void __launch_bounds__(kInterWarps * 32) interaction_bwd_kernel(InteractionParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int T = p.F + 1;
@@ -80,18 +150,14 @@ __global__ void __launch_bounds__(kInterWarps * 32) interaction_bwd_kernel(Inter
   float* S = reinterpret_cast<float*>(z + T * rowp);
   const int lane = lane_id();
   const int npairs = T * (T - 1) / 2;
-  const int per_lane = p.D / 32;  // columns per lane (2, 4 or 8)
+  constexpr int per_lane = PER;   // columns per lane (D / 32)
+  constexpr int wpl = PER / 2;     // 32-bit words per lane
   for (int b = blockIdx.x * kInterWarps + warp_id(); b < p.B; b += gridDim.x * kInterWarps) {
     const __nv_bfloat16* bot = p.bot + static_cast<int64_t>(b) * p.bot_ld;
     const __nv_bfloat16* emb = p.emb + static_cast<int64_t>(b) * p.emb_ld;
     const __nv_bfloat16* dout = p.dout + static_cast<int64_t>(b) * p.out_ld;
-    for (int w = lane; w < T * (p.D / 2); w += 32) {
-      const int r = w / (p.D / 2), c = w - r * (p.D / 2);
-      z[r * rowp + c] = r == 0 ? reinterpret_cast<const uint32_t*>(bot)[c]
-                               : reinterpret_cast<const uint32_t*>(emb + (r - 1) * p.D)[c];
-    }
-    for (int q = lane; q < T * T; q += 32) S[q] = 0.f;
-    __syncwarp();
+    stage_z(z, rowp, bot, emb, T, T, p.D);
+    for (int q = lane; q < T; q += 32) S[q * T + q] = 0.f;
     for (int q = lane; q < npairs; q += 32) {
       int i, j;
       pair_of(q, i, j);
@@ -100,41 +166,47 @@ __global__ void __launch_bounds__(kInterWarps * 32) interaction_bwd_kernel(Inter
       S[j * T + i] = g;
     }
     __syncwarp();
-    // lane owns columns [lane*per_lane, (lane+1)*per_lane)
-    const int c0 = lane * per_lane;
-    for (int i = 0; i < T; ++i) {
-      float acc[8];
+    const int w0 = lane * wpl;  // first word of this lane's columns
+    for (int i0 = 0; i0 < T; i0 += 9) {
+      float acc[9][PER];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+      for (int x = 0; x < 9; ++x)
+#pragma unroll
+        for (int e = 0; e < PER; ++e) acc[x][e] = 0.f;
       for (int j = 0; j < T; ++j) {
-        const float s = S[i * T + j];
-        const uint32_t* zj = z + j * rowp + c0 / 2;
+        float zv[PER];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          if (2 * e < per_lane) {
-            const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(zj + e));
-            acc[2 * e] = fmaf(s, v.x, acc[2 * e]);
-            acc[2 * e + 1] = fmaf(s, v.y, acc[2 * e + 1]);
-          }
+        for (int e = 0; e < wpl; ++e) {
+          const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(z + j * rowp + w0 + e));
+          zv[2 * e] = v.x;
+          zv[2 * e + 1] = v.y;
+        }
+#pragma unroll
+        for (int x = 0; x < 9; ++x) {
+          const float sv = (i0 + x < T) ? S[(i0 + x) * T + j] : 0.f;
+#pragma unroll
+          for (int e = 0; e < PER; ++e) acc[x][e] = fmaf(sv, zv[e], acc[x][e]);
         }
       }
-      if (i == 0) {
-        __nv_bfloat16* dbot = p.dbot + static_cast<int64_t>(b) * p.dbot_ld;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          if (e < per_lane) {
+      for (int x = 0; x < 9; ++x) {
+        const int i = i0 + x;
+        if (i >= T) break;
+        const int c0 = lane * per_lane;
+        if (i == 0) {
+          __nv_bfloat16* dbot = p.dbot + static_cast<int64_t>(b) * p.dbot_ld;
+#pragma unroll
+          for (int e = 0; e < PER; ++e) {
             const int c = c0 + e;
-            float v = acc[e] + __bfloat162float(dout[c]);
+            float v = acc[x][e] + __bfloat162float(dout[c]);
             if (p.relu_mask_bot && __bfloat162float(bot[c]) <= 0.f) v = 0.f;
             dbot[c] = __float2bfloat16_rn(v);
           }
-        }
-      } else {
-        __nv_bfloat16* demb = p.demb + static_cast<int64_t>(b) * p.demb_ld + (i - 1) * p.D;
+        } else {
+          __nv_bfloat16* demb = p.demb + static_cast<int64_t>(b) * p.demb_ld + (i - 1) * p.D;
 #pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          if (e < per_lane)
-            *reinterpret_cast<__nv_bfloat162*>(demb + c0 + e) = __floats2bfloat162_rn(acc[e], acc[e + 1]);
+          for (int e = 0; e < PER; e += 2)
+            *reinterpret_cast<__nv_bfloat162*>(demb + c0 + e) = __floats2bfloat162_rn(acc[x][e], acc[x][e + 1]);
         }
       }
     }
@@ -366,13 +438,19 @@ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
   return z ^ (z >> 31);
 }
 
+// Element i of a [rows, ncols] slice holding columns [col_begin, col_begin +
+// ncols) of a table with row length `dim` gets value index
+// (i / ncols) * dim + col_begin + i % ncols (+ index_offset) in the stream, so
+// a table initialised in column shards equals the table initialised whole.
 template <typename T>
 __global__ void init_uniform_kernel(T* __restrict__ out, int64_t n, float lo, float hi, uint64_t seed,
-                                    int64_t index_offset) {
+                                    int64_t index_offset, int ncols, int dim, int col_begin) {
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const uint64_t r = mix64(seed * 0x9e3779b97f4a7c15ULL + static_cast<uint64_t>(i + index_offset));
-    const float u = static_cast<float>(r >> 40) * (1.0f / 16777216.0f);  // 24 random bits in [0,1)
+    const int64_t r = i / ncols;
+    const int64_t idx = r * dim + col_begin + (i - r * ncols) + index_offset;
+    const uint64_t rnd = mix64(seed * 0x9e3779b97f4a7c15ULL + static_cast<uint64_t>(idx));
+    const float u = static_cast<float>(rnd >> 40) * (1.0f / 16777216.0f);  // 24 random bits in [0,1)
     out[i] = from_f32<T>(lo + (hi - lo) * u);
   }
 }
@@ -389,7 +467,9 @@ void interaction_forward(const InteractionParams& p, cudaStream_t s) {
   FLARE_CHECK(p.D % 64 == 0 && p.D <= 256, "interaction width must be a multiple of 64 and <= 256");
   const int T = p.F + 1;
   FLARE_CHECK(p.out_ld >= p.D + T * (T - 1) / 2, "interaction output too narrow");
-  const size_t smem = static_cast<size_t>(kInterWarps) * T * (p.D / 2 + 1) * 4;
+  const int TP = (T + 2) / 3 * 3;
+  FLARE_CHECK(p.out_ld % 8 == 0 && T <= 33, "interaction: out_ld must be a multiple of 8 and F <= 32");
+  const size_t smem = static_cast<size_t>(kInterWarps) * (TP * (p.D / 2 + 1) + (p.out_ld + 1) / 2 + 4) * 4;
   FLARE_CUDA_CHECK(cudaFuncSetAttribute(interaction_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(smem)));
   const int grid = std::min(ceil_div(p.B, kInterWarps), 148 * 8);
@@ -398,16 +478,24 @@ void interaction_forward(const InteractionParams& p, cudaStream_t s) {
   count_launch();
 }
 
-void interaction_backward(const InteractionParams& p, cudaStream_t s) {
-  FLARE_CHECK(p.D % 64 == 0 && p.D <= 256, "interaction width must be a multiple of 64 and <= 256");
+template <int PER>
+void interaction_bwd_launch(const InteractionParams& p, cudaStream_t s) {
   const int T = p.F + 1;
   const size_t smem = static_cast<size_t>(kInterWarps) * (T * (p.D / 2 + 1) + T * T) * 4;
-  FLARE_CUDA_CHECK(cudaFuncSetAttribute(interaction_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  FLARE_CUDA_CHECK(cudaFuncSetAttribute(interaction_bwd_kernel<PER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(smem)));
   const int grid = std::min(ceil_div(p.B, kInterWarps), 148 * 8);
-  interaction_bwd_kernel<<<grid, kInterWarps * 32, smem, s>>>(p);
+  interaction_bwd_kernel<PER><<<grid, kInterWarps * 32, smem, s>>>(p);
   FLARE_CUDA_CHECK(cudaGetLastError());
   count_launch();
+}
+
+void interaction_backward(const InteractionParams& p, cudaStream_t s) {
+  FLARE_CHECK(p.D % 64 == 0 && p.D <= 256, "interaction width must be a multiple of 64 and <= 256");
+  FLARE_CHECK(p.F + 1 <= 33, "interaction supports up to 32 embedded features");
+  if (p.D == 64) interaction_bwd_launch<2>(p, s);
+  else if (p.D == 128) interaction_bwd_launch<4>(p, s);
+  else interaction_bwd_launch<8>(p, s);
 }
 
 template <int PER>
@@ -467,12 +555,18 @@ void cast_pad_bf16(const float* x, int64_t rows, int cols, int64_t ldx, __nv_bfl
 }
 
 void init_uniform(void* out, int dtype, int64_t n, float lo, float hi, uint64_t seed, int64_t index_offset,
-                  cudaStream_t s) {
+                  int ncols, int dim, int col_begin, cudaStream_t s) {
+  FLARE_CHECK(ncols > 0 && dim >= ncols, "bad init slice");
   const int grid = grid_for(n, 256);
-  if (dtype == kF32) init_uniform_kernel<float><<<grid, 256, 0, s>>>(static_cast<float*>(out), n, lo, hi, seed, index_offset);
+  if (dtype == kF32)
+    init_uniform_kernel<float><<<grid, 256, 0, s>>>(static_cast<float*>(out), n, lo, hi, seed, index_offset, ncols,
+                                                     dim, col_begin);
   else if (dtype == kBF16)
-    init_uniform_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<__nv_bfloat16*>(out), n, lo, hi, seed, index_offset);
-  else init_uniform_kernel<__half><<<grid, 256, 0, s>>>(static_cast<__half*>(out), n, lo, hi, seed, index_offset);
+    init_uniform_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<__nv_bfloat16*>(out), n, lo, hi, seed,
+                                                             index_offset, ncols, dim, col_begin);
+  else
+    init_uniform_kernel<__half><<<grid, 256, 0, s>>>(static_cast<__half*>(out), n, lo, hi, seed, index_offset,
+                                                      ncols, dim, col_begin);
   FLARE_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

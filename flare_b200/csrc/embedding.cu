@@ -6,33 +6,48 @@
 //   (source rank, sample) bag: read the bag's ids straight from the source
 //   rank's memory over NVLink (the ids all-to-all), gather + sum/mean pool the
 //   local HBM rows in fp32, and store the pooled row straight into the source
-//   rank's pooled-output buffer (the pooled all-to-all) -> the ids are also
-//   staged locally for the backward -> exit barrier (every owner has written).
+//   rank's pooled-output buffer (the pooled all-to-all); the ids are staged
+//   locally for the backward -> exit barrier (every owner has written).
 //
-// Backward (one pass of six short launches, no host sync):
+// Backward (short launches, no host sync, no global hot counters):
 //   1. entry barrier; pull the pooled gradients of every (source, sample) bag
-//      for the owned shards (pooled-grad all-to-all) and, in the same launch,
-//      count occurrences per row with warp-aggregated atomics (dedup);
-//   2-3. exclusive scan of per-unique counts -> segment starts;
-//   4. fill: place every occurrence into its row's segment (counters return
-//      to zero, so no per-step clearing of the per-row arrays is needed);
-//   5. segment reduce in fp32 over fixed-size chunks of the occurrence list
-//      (balanced under Zipf skew) and apply the row-wise optimizer in place;
-//      rows spanning chunks accumulate into a small carry buffer;
-//   6. apply the optimizer to the spanning rows.
+//      of the owned columns (pooled-gradient all-to-all) and, in the same
+//      launch, count occurrences per row (warp-aggregated atomics), record
+//      each occurrence's rank within its row and flag rank 0;
+//   2. scan of the flags -> dense unique ids in occurrence order (deterministic);
+//   3. emit per-unique metadata (row, shard, count, first occurrence);
+//   4. scan of per-unique counts -> segment starts;
+//   5. fill: occ[seg_start[u] + rank] = staged-grad row (no atomics);
+//   6. light rows (<= light_max occurrences): one row per lane group, fp32
+//      segment sum + optimizer applied in place, per-row counter reset;
+//   7. heavy rows (Zipf head): their occurrences are cut into equal chunks
+//      across warps (balanced however skewed the counts are), partial fp32
+//      sums reduce into a per-heavy-row accumulator, then one warp per row
+//      applies the optimizer.
 //
 // Reference behaviour: gather/pool/scatter semantics of
 // src/flare/kernels/backends/gpu_cupy.py:52-252 and
 // src/flare/ops/sparse_gather.py:40-99 (sum, mean with max(len,1)); the
 // reference routes ids and values through Fluxway transport
-// (src/flare/runtime/fluxway/workers/dynamic_embedding.py:362-438, 551-681).
+// (src/flare/runtime/fluxway/workers/dynamic_embedding.py:362-438, 551-681)
+// and updates rows in its external native store.
 #include "embedding.cuh"
+#include "sparse_ops.cuh"
+
+#include <algorithm>
 
 namespace flare {
 namespace {
 
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kEmbThreads = 256;
+constexpr int kMaxShardsSmem = 96;
+
+__device__ __forceinline__ unsigned lanemask_lt() {
+  unsigned m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
 
 __device__ __forceinline__ void barrier_signal(uint32_t* const* peer_flags, int world, int rank, int slot_off,
                                                uint32_t epoch) {
@@ -60,6 +75,9 @@ __device__ __forceinline__ bool entry_barrier(uint32_t* flags_local, uint32_t* c
   return ok_sh != 0;
 }
 
+// ============================================================================
+// Forward
+// ============================================================================
 template <typename TW, int VEC>
 __global__ void __launch_bounds__(kEmbThreads) emb_fwd_kernel(EmbFwdParams p) {
   const uint32_t epoch = p.world > 1 ? *reinterpret_cast<volatile uint32_t*>(p.epoch_ctr) + 1u : 0u;
@@ -117,32 +135,33 @@ __global__ void __launch_bounds__(kEmbThreads) emb_fwd_kernel(EmbFwdParams p) {
       const int* vals = p.peer_values[s];
       for (int j = 0; j < maxlen; j += G) {
         int myid = -1;
-        if (active && j + l < len) {
+        const bool has = active && j + l < len;
+        if (has) {
           myid = vals[beg + j + l];
-          if (stage_ok) {
-            p.stage_ids[stage_base + j + l] = myid;
-            p.stage_bag[stage_base + j + l] = b;
-          }
           if (myid >= d.rows) {
             report_error(p.status, kIndexOutOfRange, d.feature);
             myid = -1;
           }
         }
+        if (has && stage_ok) {
+          p.stage_ids[stage_base + j + l] = myid;
+          p.stage_bag[stage_base + j + l] = b;
+        }
         const int cnt = min(G, maxlen - j);
         int t = 0;
-        for (; t + 4 <= cnt; t += 4) {
-          int id[4];
+        for (; t + 8 <= cnt; t += 8) {
+          int id[8];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) id[q] = __shfl_sync(kFull, myid, g * G + t + q);
-          float4 r[4][VEC];
+          for (int q = 0; q < 8; ++q) id[q] = __shfl_sync(kFull, myid, g * G + t + q);
+          float4 r[8][VEC];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
+          for (int q = 0; q < 8; ++q) {
             const TW* row = wshard + static_cast<int64_t>(id[q] < 0 ? 0 : id[q]) * d.ncols;
 #pragma unroll
             for (int v = 0; v < VEC; ++v) r[q][v] = load4<TW>(row + 4 * v);
           }
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
+          for (int q = 0; q < 8; ++q) {
             const float m = id[q] < 0 ? 0.f : 1.f;
 #pragma unroll
             for (int v = 0; v < VEC; ++v) acc[v] = f4_add(acc[v], f4_scale(r[q][v], m));
@@ -195,24 +214,18 @@ __global__ void __launch_bounds__(kEmbThreads) emb_fwd_kernel(EmbFwdParams p) {
   }
 }
 
-// --------------------------------------------------------------------------
+// ============================================================================
 // Backward
-// --------------------------------------------------------------------------
-__device__ __forceinline__ unsigned lanemask_lt() {
-  unsigned m;
-  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
-  return m;
-}
+// ============================================================================
 
-// Phase 1: pooled-gradient all-to-all (pull) fused with dedup counting.
+// 1. pooled-gradient all-to-all (pull) + occurrence counting, ranks, first-occurrence flags
 __global__ void __launch_bounds__(kEmbThreads) emb_bwd_pull_count_kernel(EmbBwdParams p) {
   if (p.world > 1) {
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(p.epoch_ctr) + 1u;
     const bool ok =
         entry_barrier(p.flags_local, p.peer_flags, p.world, p.rank, p.flag_in, epoch, p.timeout_ns, p.status);
     if (threadIdx.x == 0) {
-      // Advance the epoch once every block has read it.
-      if (atomicAdd(p.block_counter, 1u) == gridDim.x - 1) {
+      if (atomicAdd(p.block_counter, 1u) == gridDim.x - 1) {  // every block has read the epoch
         *p.block_counter = 0u;
         *p.epoch_ctr = epoch;
       }
@@ -222,7 +235,6 @@ __global__ void __launch_bounds__(kEmbThreads) emb_bwd_pull_count_kernel(EmbBwdP
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const int esize = p.grad_dtype == kBF16 ? 2 : 4;
-  // ---- pull gradient rows of every owned shard from every source ----
   for (int sh = 0; sh < p.num_shards; ++sh) {
     const ShardDesc d = p.shards[sh];
     const int chunks = d.ncols * esize / 16;
@@ -239,48 +251,74 @@ __global__ void __launch_bounds__(kEmbThreads) emb_bwd_pull_count_kernel(EmbBwdP
       *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
     }
   }
-  // ---- count occurrences per row (warp-aggregated) ----
+  __shared__ int block_total;
+  if (threadIdx.x == 0) block_total = 0;
+  __syncthreads();
+  // Count occurrences per row; this occurrence's rank within its row is the
+  // counter value before the add plus its position among equal-row lanes.
   const int lane = lane_id();
-  const int64_t gwarp = tid >> 5;
+  const int64_t N = static_cast<int64_t>(p.num_shards) * p.world * p.stage_cap;
   const int64_t nwarps = nthreads >> 5;
-  int local_total = 0;
-  for (int sh = 0; sh < p.num_shards; ++sh) {
-    const ShardDesc d = p.shards[sh];
-    for (int s = 0; s < p.world; ++s) {
-      const int slot = sh * p.world + s;
-      const int n = min(static_cast<int64_t>(p.stage_count[slot]), p.stage_cap);
-      const int* ids = p.stage_ids + static_cast<int64_t>(slot) * p.stage_cap;
-      for (int64_t j0 = gwarp * 32; j0 < n; j0 += nwarps * 32) {
-        const int64_t j = j0 + lane;
-        const int id = j < n ? ids[j] : -1;
-        const bool valid = id >= 0 && id < d.rows;
-        const unsigned vmask = __ballot_sync(kFull, valid);
-        bool fresh = false;
-        long long row = 0;
-        if (valid) {
-          row = d.row_base + id;
-          const unsigned peers = __match_any_sync(vmask, row);
-          const int leader = __ffs(peers) - 1;
-          if (lane == leader) fresh = atomicAdd(p.row_count + row, __popc(peers)) == 0;
-        }
-        const unsigned fmask = __ballot_sync(kFull, fresh);
-        if (fmask) {
-          int base = 0;
-          const int first = __ffs(fmask) - 1;
-          if (lane == first) base = atomicAdd(p.num_unique, __popc(fmask));
-          base = __shfl_sync(kFull, base, first);
-          if (fresh) {
-            const int u = base + __popc(fmask & lanemask_lt());
-            p.uniq_row[u] = row;
-            p.uniq_shard[u] = sh;
-            p.row2u[row] = u;
-          }
-        }
-        if (lane == 0) local_total += __popc(vmask);
+  int local = 0;
+  for (int64_t i0 = (tid >> 5) * 32; i0 < N; i0 += nwarps * 32) {
+    const int64_t i = i0 + lane;
+    int f = 0;
+    long long row = -1;
+    if (i < N) {
+      const int slot = static_cast<int>(i / p.stage_cap);
+      const int64_t j = i - static_cast<int64_t>(slot) * p.stage_cap;
+      if (j < p.stage_count[slot]) {
+        const int id = p.stage_ids[i];
+        if (id >= 0) row = p.shards[slot / p.world].row_base + id;
       }
     }
+    const bool valid = row >= 0;
+    const unsigned vmask = __ballot_sync(kFull, valid);
+    if (valid) {
+      ++local;
+      const unsigned peers = __match_any_sync(vmask, row);
+      const int leader = __ffs(peers) - 1;
+      int old = 0;
+      if (lane == leader) old = atomicAdd(p.row_count + row, __popc(peers));
+      old = __shfl_sync(peers, old, leader);
+      const int rank = old + __popc(peers & lanemask_lt());
+      p.stage_rank[i] = rank;
+      f = rank == 0 ? 1 : 0;
+    }
+    if (i < N) p.flags[i] = f;
   }
-  if (lane == 0 && local_total) atomicAdd(p.num_unique + 1, local_total);
+  local = __reduce_add_sync(kFull, local);
+  if (lane == 0 && local) atomicAdd(&block_total, local);
+  __syncthreads();
+  if (threadIdx.x == 0 && block_total) atomicAdd(p.num_unique + 1, block_total);
+}
+
+// 3. per-unique metadata
+__global__ void __launch_bounds__(kEmbThreads) emb_emit_kernel(EmbBwdParams p) {
+  const int64_t N = static_cast<int64_t>(p.num_shards) * p.world * p.stage_cap;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (tid == 0) p.num_unique[0] = p.pos[N];
+  for (int64_t i = tid; i < N; i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    if (!p.flags[i]) continue;
+    const int u = p.pos[i];
+    const int slot = static_cast<int>(i / p.stage_cap);
+    const int sh = slot / p.world;
+    const long long row = p.shards[sh].row_base + p.stage_ids[i];
+    p.uniq_row[u] = row;
+    p.uniq_shard[u] = sh;
+    p.row2u[row] = u;
+    const int c = p.row_count[row];
+    p.cnt_u[u] = c;
+    p.first_gidx[u] = slot * p.Bl + p.stage_bag[i];
+    if (c > p.light_max) {
+      const int h = atomicAdd(p.num_unique + 2, 1);
+      if (h < p.max_heavy) {
+        p.heavy[h] = u;
+        p.hcnt[h] = c;
+      }
+      else report_error(p.status, kCapacityOverflow, -1);
+    }
+  }
 }
 
 constexpr int kScanBlocks = 512;
@@ -304,30 +342,31 @@ __device__ __forceinline__ int block_reduce_sum(int v, int* sh) {
   return tot;
 }
 
-__global__ void __launch_bounds__(kScanThreads) emb_scan_partial_kernel(EmbBwdParams p) {
+// 4. exclusive scan of cnt_u[0..U) (U read on the device) -> seg_start
+__global__ void __launch_bounds__(kScanThreads) emb_seg_partial_kernel(EmbBwdParams p) {
   __shared__ int sh[32];
   const int U = p.num_unique[0];
   const int per = (U + kScanBlocks - 1) / kScanBlocks;
-  const int lo = min(U, blockIdx.x * per), hi = min(U, lo + per);
+  const int lo = min(U, static_cast<int>(blockIdx.x) * per), hi = min(U, lo + per);
   int acc = 0;
-  for (int u = lo + threadIdx.x; u < hi; u += blockDim.x) acc += p.row_count[p.uniq_row[u]];
+  for (int u = lo + threadIdx.x; u < hi; u += blockDim.x) acc += p.cnt_u[u];
   acc = block_reduce_sum(acc, sh);
   if (threadIdx.x == 0) p.block_sums[blockIdx.x] = acc;
 }
 
-__global__ void __launch_bounds__(kScanThreads) emb_scan_final_kernel(EmbBwdParams p) {
+__global__ void __launch_bounds__(kScanThreads) emb_seg_final_kernel(EmbBwdParams p) {
   __shared__ int sh[32];
   __shared__ int wsum[32];
   const int U = p.num_unique[0];
   const int per = (U + kScanBlocks - 1) / kScanBlocks;
-  const int lo = min(U, blockIdx.x * per), hi = min(U, lo + per);
+  const int lo = min(U, static_cast<int>(blockIdx.x) * per), hi = min(U, lo + per);
   int base = 0;
   for (int i = threadIdx.x; i < blockIdx.x; i += blockDim.x) base += p.block_sums[i];
   base = block_reduce_sum(base, sh);
   const int w = warp_id(), l = lane_id();
   for (int t0 = lo; t0 < hi; t0 += blockDim.x) {
     const int u = t0 + threadIdx.x;
-    const int c = u < hi ? p.row_count[p.uniq_row[u]] : 0;
+    const int c = u < hi ? p.cnt_u[u] : 0;
     int x = c;  // inclusive warp scan
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -343,7 +382,7 @@ __global__ void __launch_bounds__(kScanThreads) emb_scan_final_kernel(EmbBwdPara
         const int y = __shfl_up_sync(kFull, s, o);
         if (l >= o) s += y;
       }
-      wsum[l] = s;  // inclusive prefix over warps
+      wsum[l] = s;
     }
     __syncthreads();
     const int warp_base = w > 0 ? wsum[w - 1] : 0;
@@ -353,42 +392,24 @@ __global__ void __launch_bounds__(kScanThreads) emb_scan_final_kernel(EmbBwdPara
     base += tile_total;
   }
   // The last block's running base ends at the grand total (blocks past U own
-  // empty ranges), which is the sentinel seg_start[U] = T.
+  // empty ranges): the sentinel seg_start[U] = T.
   if (blockIdx.x == kScanBlocks - 1 && threadIdx.x == 0) p.seg_start[U] = base;
 }
 
-// Phase 4: scatter occurrences into their segments.
+// 5. occ[seg_start[u] + rank] = staged-grad row, for rows seen more than once
 __global__ void __launch_bounds__(kEmbThreads) emb_fill_kernel(EmbBwdParams p) {
-  const int lane = lane_id();
-  const int64_t gwarp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-  for (int sh = 0; sh < p.num_shards; ++sh) {
-    const ShardDesc d = p.shards[sh];
-    for (int s = 0; s < p.world; ++s) {
-      const int slot = sh * p.world + s;
-      const int n = min(static_cast<int64_t>(p.stage_count[slot]), p.stage_cap);
-      const int* ids = p.stage_ids + static_cast<int64_t>(slot) * p.stage_cap;
-      const int* bags = p.stage_bag + static_cast<int64_t>(slot) * p.stage_cap;
-      for (int64_t j0 = gwarp * 32; j0 < n; j0 += nwarps * 32) {
-        const int64_t j = j0 + lane;
-        const int id = j < n ? ids[j] : -1;
-        const bool valid = id >= 0 && id < d.rows;
-        const unsigned vmask = __ballot_sync(kFull, valid);
-        if (valid) {
-          const long long row = d.row_base + id;
-          const unsigned peers = __match_any_sync(vmask, row);
-          const int leader = __ffs(peers) - 1;
-          const int k = __popc(peers);
-          int old = 0;
-          if (lane == leader) old = atomicSub(p.row_count + row, k);
-          old = __shfl_sync(peers, old, leader);
-          const int u = p.row2u[row];
-          const int rank_in_group = __popc(peers & lanemask_lt());
-          const int pos = p.seg_start[u] + old - k + rank_in_group;
-          p.occ[pos] = (slot * p.Bl) + bags[j];
-        }
-      }
-    }
+  const int64_t N = static_cast<int64_t>(p.num_shards) * p.world * p.stage_cap;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < N;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int slot = static_cast<int>(i / p.stage_cap);
+    const int64_t j = i - static_cast<int64_t>(slot) * p.stage_cap;
+    if (j >= p.stage_count[slot]) continue;
+    const int id = p.stage_ids[i];
+    if (id < 0) continue;
+    const int sh = slot / p.world;
+    const int u = p.row2u[p.shards[sh].row_base + id];
+    if (p.cnt_u[u] <= 1) continue;
+    p.occ[p.seg_start[u] + p.stage_rank[i]] = slot * p.Bl + p.stage_bag[i];
   }
 }
 
@@ -414,104 +435,102 @@ __device__ __forceinline__ float lr_scale(const SparseOptParams& o, float score)
   }
 }
 
-// Apply the sparse optimizer to one row; called by a whole warp, lane covers
-// columns [col, col + 4*VEC) when col < ncols.
-template <typename TW, int VEC>
-__device__ __forceinline__ void apply_row_update(const EmbBwdParams& p, const ShardDesc& d, long long row, int col,
-                                                 float4 (&g)[VEC], int count) {
-  const SparseOptParams& o = p.opt;
-  const bool act = col < d.ncols;
-  const int64_t local = row - d.row_base;
-  const int64_t eoff = d.weight_off + local * d.ncols + col;
-  TW* w = reinterpret_cast<TW*>(p.weights) + eoff;
+__device__ __forceinline__ void resolve_sparse_step(SparseOptParams& o) {
+  if (o.step_ptr != nullptr) {
+    const float t = static_cast<float>(*o.step_ptr);
+    o.bias_corr1 = 1.f - powf(o.beta1, t);
+    o.bias_corr2 = 1.f - powf(o.beta2, t);
+  }
+}
+
+// Sum over the G lanes of an aligned lane group (G a power of two).
+__device__ __forceinline__ float group_sum(float v, int G) {
+  for (int o = G >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  return v;
+}
+
+// Apply the sparse optimizer to one row.  Called by every lane of the warp in
+// lockstep; a group of G lanes owns the row and lane `leader` is its first
+// lane; a lane covers columns [col, col + 4*NV) of the row when `act`.
+template <typename TW, int NV>
+__device__ __forceinline__ void apply_update(const SparseOptParams& o, TW* w, int64_t eoff, long long row,
+                                             bool row_ok, bool act, int ncols, float4 (&gv4)[NV],
+                                             float4 (&wv4)[NV], int count, int G, int leader) {
+  float* g = reinterpret_cast<float*>(gv4);
+  float* wv = reinterpret_cast<float*>(wv4);
   float lr = o.lr;
   if (o.score != nullptr) {
     float sc = 0.f;
-    if (lane_id() == 0) {
+    if (row_ok && lane_id() == leader) {
       sc = o.score[row] + static_cast<float>(count);
       o.score[row] = sc;
     }
-    sc = __shfl_sync(kFull, sc, 0);
+    sc = __shfl_sync(kFull, sc, leader);
     lr *= lr_scale(o, sc);
   }
-  float wv[VEC][4];
-  float gv[VEC][4];
 #pragma unroll
-  for (int v = 0; v < VEC; ++v) {
-    float4 x = act ? load4<TW>(w + 4 * v) : make_float4(0.f, 0.f, 0.f, 0.f);
-    wv[v][0] = x.x; wv[v][1] = x.y; wv[v][2] = x.z; wv[v][3] = x.w;
-    gv[v][0] = g[v].x; gv[v][1] = g[v].y; gv[v][2] = g[v].z; gv[v][3] = g[v].w;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) gv[v][e] += o.weight_decay * wv[v][e];
-  }
+  for (int e = 0; e < 4 * NV; ++e) g[e] += o.weight_decay * wv[e];
   if (o.kind == kOptRowwiseAdagrad || o.kind == kOptRowwiseAdam) {
     float sq = 0.f;
     if (act) {
 #pragma unroll
-      for (int v = 0; v < VEC; ++v)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) sq += gv[v][e] * gv[v][e];
+      for (int e = 0; e < 4 * NV; ++e) sq += g[e] * g[e];
     }
-    sq = warp_sum(sq) / static_cast<float>(d.ncols);
+    sq = group_sum(sq, G) / static_cast<float>(ncols);
     float st = 0.f;
-    if (lane_id() == 0) {
+    if (row_ok && lane_id() == leader) {
       const float old = o.state_row[row];
       st = o.kind == kOptRowwiseAdagrad ? old + sq : o.beta2 * old + (1.f - o.beta2) * sq;
       o.state_row[row] = st;
     }
-    st = __shfl_sync(kFull, st, 0);
+    st = __shfl_sync(kFull, st, leader);
     if (o.kind == kOptRowwiseAdagrad) {
       const float scale = lr / (sqrtf(st) + o.eps);
 #pragma unroll
-      for (int v = 0; v < VEC; ++v)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) wv[v][e] -= scale * gv[v][e];
-    } else {
+      for (int e = 0; e < 4 * NV; ++e) wv[e] -= scale * g[e];
+    } else if (act) {
       const float denom = sqrtf(st / o.bias_corr2) + o.eps;
-      if (act) {
 #pragma unroll
-        for (int v = 0; v < VEC; ++v) {
-          float4 m = *reinterpret_cast<float4*>(o.state_m + eoff + 4 * v);
-          float* mm = reinterpret_cast<float*>(&m);
+      for (int v = 0; v < NV; ++v) {
+        float4 m = *reinterpret_cast<float4*>(o.state_m + eoff + 4 * v);
+        float* mm = reinterpret_cast<float*>(&m);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            mm[e] = o.beta1 * mm[e] + (1.f - o.beta1) * gv[v][e];
-            wv[v][e] -= lr * (mm[e] / o.bias_corr1) / denom;
-          }
-          *reinterpret_cast<float4*>(o.state_m + eoff + 4 * v) = m;
+        for (int e = 0; e < 4; ++e) {
+          mm[e] = o.beta1 * mm[e] + (1.f - o.beta1) * g[4 * v + e];
+          wv[4 * v + e] -= lr * (mm[e] / o.bias_corr1) / denom;
         }
+        *reinterpret_cast<float4*>(o.state_m + eoff + 4 * v) = m;
       }
     }
   } else if (act) {
     if (o.kind == kOptSgd) {
 #pragma unroll
-      for (int v = 0; v < VEC; ++v)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) wv[v][e] -= lr * gv[v][e];
+      for (int e = 0; e < 4 * NV; ++e) wv[e] -= lr * g[e];
     } else if (o.kind == kOptAdagrad) {
 #pragma unroll
-      for (int v = 0; v < VEC; ++v) {
+      for (int v = 0; v < NV; ++v) {
         float4 m = *reinterpret_cast<float4*>(o.state_m + eoff + 4 * v);
         float* mm = reinterpret_cast<float*>(&m);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          mm[e] += gv[v][e] * gv[v][e];
-          wv[v][e] -= lr * gv[v][e] / (sqrtf(mm[e]) + o.eps);
+          mm[e] += g[4 * v + e] * g[4 * v + e];
+          wv[4 * v + e] -= lr * g[4 * v + e] / (sqrtf(mm[e]) + o.eps);
         }
         *reinterpret_cast<float4*>(o.state_m + eoff + 4 * v) = m;
       }
     } else if (o.kind == kOptAdam) {
 #pragma unroll
-      for (int v = 0; v < VEC; ++v) {
+      for (int v = 0; v < NV; ++v) {
         float4 m = *reinterpret_cast<float4*>(o.state_m + eoff + 4 * v);
         float4 s2 = *reinterpret_cast<float4*>(o.state_v + eoff + 4 * v);
         float* mm = reinterpret_cast<float*>(&m);
         float* vv = reinterpret_cast<float*>(&s2);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          mm[e] = o.beta1 * mm[e] + (1.f - o.beta1) * gv[v][e];
-          vv[e] = o.beta2 * vv[e] + (1.f - o.beta2) * gv[v][e] * gv[v][e];
-          wv[v][e] -= lr * (mm[e] / o.bias_corr1) / (sqrtf(vv[e] / o.bias_corr2) + o.eps);
+          const float ge = g[4 * v + e];
+          mm[e] = o.beta1 * mm[e] + (1.f - o.beta1) * ge;
+          vv[e] = o.beta2 * vv[e] + (1.f - o.beta2) * ge * ge;
+          wv[4 * v + e] -= lr * (mm[e] / o.bias_corr1) / (sqrtf(vv[e] / o.bias_corr2) + o.eps);
         }
         *reinterpret_cast<float4*>(o.state_m + eoff + 4 * v) = m;
         *reinterpret_cast<float4*>(o.state_v + eoff + 4 * v) = s2;
@@ -520,122 +539,254 @@ __device__ __forceinline__ void apply_row_update(const EmbBwdParams& p, const Sh
   }
   if (act) {
 #pragma unroll
-    for (int v = 0; v < VEC; ++v)
-      store4<TW>(w + 4 * v, make_float4(wv[v][0], wv[v][1], wv[v][2], wv[v][3]));
+    for (int v = 0; v < NV; ++v) store4<TW>(w + 4 * v, wv4[v]);
   }
 }
 
-template <typename TG, int VEC>
-__device__ __forceinline__ void add_grad_row(const EmbBwdParams& p, int gidx, int col, bool act, float scale,
-                                             float4 (&acc)[VEC]) {
-  if (!act) return;
-  const TG* src = reinterpret_cast<const TG*>(p.grad_stage) + static_cast<int64_t>(gidx) * p.grad_stage_ld + col;
-#pragma unroll
-  for (int v = 0; v < VEC; ++v) acc[v] = f4_add(acc[v], f4_scale(load4<TG>(src + 4 * v), scale));
-}
-
-// Phase 5: fixed-size chunks of the grouped occurrence list -> fp32 segment
-// sums -> optimizer (rows wholly inside the chunk) or carry (spanning rows).
-__device__ __forceinline__ void resolve_sparse_step(EmbBwdParams& p) {
-  if (p.opt.step_ptr != nullptr) {
-    const float t = static_cast<float>(*p.opt.step_ptr);
-    p.opt.bias_corr1 = 1.f - powf(p.opt.beta1, t);
-    p.opt.bias_corr2 = 1.f - powf(p.opt.beta2, t);
-  }
-}
-
-template <typename TW, typename TG, int VEC>
-__global__ void __launch_bounds__(kEmbThreads) emb_reduce_apply_kernel(EmbBwdParams p) {
-  resolve_sparse_step(p);
+// 6. light rows: a group of G lanes per unique row, NV float4 per lane.
+template <typename TW, typename TG, int NV>
+__global__ void __launch_bounds__(kEmbThreads, 4) emb_apply_light_kernel(EmbBwdParams p, int G) {
+  __shared__ ShardDesc sd[kMaxShardsSmem];
+  for (int i = threadIdx.x; i < p.num_shards; i += blockDim.x) sd[i] = p.shards[i];
+  __syncthreads();
+  SparseOptParams o = p.opt;
+  resolve_sparse_step(o);
   const int U = p.num_unique[0];
-  const int T = p.num_unique[1];
-  if (U == 0) return;
   const int lane = lane_id();
-  const int col = lane * 4 * VEC;
+  const int g = lane / G, gl = lane - (lane / G) * G;
+  const int leader = g * G;
+  const int gpw = 32 / G;
+  const int col = gl * 4 * NV;
   const int64_t gwarp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-  const int nchunks = (T + p.chunk - 1) / p.chunk;
+  for (int64_t base = gwarp * gpw; base < U; base += nwarps * gpw) {
+    const int u = static_cast<int>(base) + g;
+    const bool inr = u < U;
+    // independent per-row metadata, issued together
+    const int c = inr ? p.cnt_u[u] : 0;
+    const long long row = inr ? p.uniq_row[u] : 0;
+    const int sh = inr ? p.uniq_shard[u] : 0;
+    const int ss = inr ? p.seg_start[u] : 0;
+    const int g1 = inr ? p.first_gidx[u] : 0;
+    const bool mine = inr && c <= p.light_max && c > 0;
+    const ShardDesc& d = sd[sh];
+    const bool act = mine && col < d.ncols;
+    const int64_t eoff = d.weight_off + (row - d.row_base) * d.ncols + col;
+    TW* w = reinterpret_cast<TW*>(p.weights) + eoff;
+    float4 wv[NV], acc[NV];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      wv[v] = act ? load4<TW>(w + 4 * v) : make_float4(0.f, 0.f, 0.f, 0.f);
+      acc[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const bool mean = d.pooling == 1;
+    int cmax = mine ? c : 0;
+#pragma unroll
+    for (int o2 = 16; o2 > 0; o2 >>= 1) cmax = max(cmax, __shfl_xor_sync(kFull, cmax, o2));
+    for (int k0 = 0; k0 < cmax; k0 += G) {
+      // lane gl of the group loads occurrence k0 + gl of its row
+      int gidx = 0;
+      float sc = 1.f;
+      if (mine && k0 + gl < c) {
+        gidx = c == 1 ? g1 : p.occ[ss + k0 + gl];
+        if (mean) sc = 1.f / static_cast<float>(max(1, p.stage_len[gidx]));
+      }
+      const int n = min(G, cmax - k0);
+      int t = 0;
+      for (; t + 2 <= n; t += 2) {
+        float4 r[2][NV];
+        float s2[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const int gi = __shfl_sync(kFull, gidx, leader + t + q);
+          s2[q] = __shfl_sync(kFull, sc, leader + t + q);
+          const bool ok = act && k0 + t + q < c;
+          const TG* src =
+              reinterpret_cast<const TG*>(p.grad_stage) + static_cast<int64_t>(gi) * p.grad_stage_ld + col;
+#pragma unroll
+          for (int v = 0; v < NV; ++v) r[q][v] = ok ? load4<TG>(src + 4 * v) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+#pragma unroll
+          for (int v = 0; v < NV; ++v) acc[v] = f4_add(acc[v], f4_scale(r[q][v], s2[q]));
+      }
+      for (; t < n; ++t) {
+        const int gi = __shfl_sync(kFull, gidx, leader + t);
+        const float s = __shfl_sync(kFull, sc, leader + t);
+        if (act && k0 + t < c) {
+          const TG* src =
+              reinterpret_cast<const TG*>(p.grad_stage) + static_cast<int64_t>(gi) * p.grad_stage_ld + col;
+#pragma unroll
+          for (int v = 0; v < NV; ++v) acc[v] = f4_add(acc[v], f4_scale(load4<TG>(src + 4 * v), s));
+        }
+      }
+    }
+    apply_update<TW, NV>(o, w, eoff, row, mine, act, d.ncols, acc, wv, c, G, leader);
+    if (mine && gl == 0) p.row_count[row] = 0;
+  }
+}
+
+// 7a. exclusive scan of heavy-row counts hcnt[0..H) -> heavy_start (H on device)
+__global__ void __launch_bounds__(kScanThreads) emb_heavy_partial_kernel(EmbBwdParams p) {
+  __shared__ int sh[32];
+  const int H = min(p.num_unique[2], p.max_heavy);
+  const int per = (H + kScanBlocks - 1) / kScanBlocks;
+  const int lo = min(H, static_cast<int>(blockIdx.x) * per), hi = min(H, lo + per);
+  int acc = 0;
+  for (int h = lo + threadIdx.x; h < hi; h += blockDim.x) acc += p.hcnt[h];
+  acc = block_reduce_sum(acc, sh);
+  if (threadIdx.x == 0) p.block_sums[blockIdx.x] = acc;
+}
+
+__global__ void __launch_bounds__(kScanThreads) emb_heavy_final_kernel(EmbBwdParams p) {
+  __shared__ int sh[32];
+  __shared__ int wsum[32];
+  const int H = min(p.num_unique[2], p.max_heavy);
+  const int per = (H + kScanBlocks - 1) / kScanBlocks;
+  const int lo = min(H, static_cast<int>(blockIdx.x) * per), hi = min(H, lo + per);
+  int base = 0;
+  for (int i = threadIdx.x; i < blockIdx.x; i += blockDim.x) base += p.block_sums[i];
+  base = block_reduce_sum(base, sh);
+  const int w = warp_id(), l = lane_id();
+  for (int t0 = lo; t0 < hi; t0 += blockDim.x) {
+    const int h = t0 + threadIdx.x;
+    const int c = h < hi ? p.hcnt[h] : 0;
+    int x = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(kFull, x, o);
+      if (l >= o) x += y;
+    }
+    if (l == 31) wsum[w] = x;
+    __syncthreads();
+    if (w == 0) {
+      int s2 = l < blockDim.x / 32 ? wsum[l] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(kFull, s2, o);
+        if (l >= o) s2 += y;
+      }
+      wsum[l] = s2;
+    }
+    __syncthreads();
+    if (h < hi) p.heavy_start[h] = base + (w > 0 ? wsum[w - 1] : 0) + x - c;
+    const int tile_total = wsum[blockDim.x / 32 - 1];
+    __syncthreads();
+    base += tile_total;
+  }
+  if (blockIdx.x == kScanBlocks - 1 && threadIdx.x == 0) p.heavy_start[H] = base;
+}
+
+// 7b. heavy occurrences in fixed chunks of kHeavyChunk across warps: fp32
+// partial sums per heavy row, reduced into heavy_acc with vector atomics.
+constexpr int kHeavyChunk = 256;
+template <typename TG, int NV>
+__global__ void __launch_bounds__(kEmbThreads) emb_heavy_accumulate_kernel(EmbBwdParams p) {
+  const int H = min(p.num_unique[2], p.max_heavy);
+  if (H == 0) return;
+  const int total = p.heavy_start[H];
+  const int lane = lane_id();
+  const int col = lane * 4 * NV;
+  const int acc_ld = 32 * 4 * NV;
+  const int64_t gwarp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int nchunks = (total + kHeavyChunk - 1) / kHeavyChunk;
   for (int64_t c = gwarp; c < nchunks; c += nwarps) {
-    const int cb = static_cast<int>(c) * p.chunk;
-    const int ce = min(T, cb + p.chunk);
-    // largest u with seg_start[u] <= cb
-    int lo = 0, hi = U;  // invariant seg_start[lo] <= cb < seg_start[hi] (seg_start[U] = T > cb)
+    const int cb = static_cast<int>(c) * kHeavyChunk;
+    const int ce = min(total, cb + kHeavyChunk);
+    int lo = 0, hi = H;  // largest h with heavy_start[h] <= cb
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
-      if (p.seg_start[mid] <= cb) lo = mid; else hi = mid;
+      if (p.heavy_start[mid] <= cb) lo = mid; else hi = mid;
     }
-    for (int u = lo; u < U; ++u) {
-      const int ss = p.seg_start[u];
-      if (ss >= ce) break;
-      const int se = p.seg_start[u + 1];
-      const int a = max(ss, cb), e = min(se, ce);
+    for (int h = lo; h < H; ++h) {
+      const int hs = p.heavy_start[h];
+      if (hs >= ce) break;
+      const int he = p.heavy_start[h + 1];
+      const int a = max(hs, cb), e = min(he, ce);
+      const int u = p.heavy[h];
       const ShardDesc d = p.shards[p.uniq_shard[u]];
       const bool act = col < d.ncols;
       const bool mean = d.pooling == 1;
-      float4 acc[VEC];
+      const int ss = p.seg_start[u] - hs;  // occ index = ss + flat position
+      float4 acc[NV];
 #pragma unroll
-      for (int v = 0; v < VEC; ++v) acc[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int v = 0; v < NV; ++v) acc[v] = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int q0 = a; q0 < e; q0 += 32) {
-        const int mine = q0 + lane < e ? p.occ[q0 + lane] : 0;
-        float myscale = 1.f;
-        if (mean && q0 + lane < e) myscale = 1.f / static_cast<float>(max(1, p.stage_len[mine]));
-        const int cnt = min(32, e - q0);
+        int gidx = 0;
+        float sc = 1.f;
+        if (q0 + lane < e) {
+          gidx = p.occ[ss + q0 + lane];
+          if (mean) sc = 1.f / static_cast<float>(max(1, p.stage_len[gidx]));
+        }
+        const int n = min(32, e - q0);
         int t = 0;
-        for (; t + 2 <= cnt; t += 2) {
-          const int g0 = __shfl_sync(kFull, mine, t), g1 = __shfl_sync(kFull, mine, t + 1);
-          const float s0 = __shfl_sync(kFull, myscale, t), s1 = __shfl_sync(kFull, myscale, t + 1);
-          add_grad_row<TG, VEC>(p, g0, col, act, s0, acc);
-          add_grad_row<TG, VEC>(p, g1, col, act, s1, acc);
-        }
-        for (; t < cnt; ++t) {
-          const int g0 = __shfl_sync(kFull, mine, t);
-          const float s0 = __shfl_sync(kFull, myscale, t);
-          add_grad_row<TG, VEC>(p, g0, col, act, s0, acc);
-        }
-      }
-      if (ss >= cb && se <= ce) {
-        apply_row_update<TW, VEC>(p, d, p.uniq_row[u], col, acc, se - ss);
-      } else {
-        const int start_chunk = ss / p.chunk;
-        if (act) {
-          float* dst = p.carry + static_cast<int64_t>(start_chunk) * (128 * VEC) + col;
+        for (; t + 4 <= n; t += 4) {
+          float4 r[4][NV];
+          float s4[4];
 #pragma unroll
-          for (int v = 0; v < VEC; ++v) {
-            atomicAdd(dst + 4 * v + 0, acc[v].x);
-            atomicAdd(dst + 4 * v + 1, acc[v].y);
-            atomicAdd(dst + 4 * v + 2, acc[v].z);
-            atomicAdd(dst + 4 * v + 3, acc[v].w);
+          for (int q = 0; q < 4; ++q) {
+            const int gi = __shfl_sync(kFull, gidx, t + q);
+            s4[q] = __shfl_sync(kFull, sc, t + q);
+            const TG* src =
+                reinterpret_cast<const TG*>(p.grad_stage) + static_cast<int64_t>(gi) * p.grad_stage_ld + col;
+#pragma unroll
+            for (int v = 0; v < NV; ++v) r[q][v] = act ? load4<TG>(src + 4 * v) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int v = 0; v < NV; ++v) acc[v] = f4_add(acc[v], f4_scale(r[q][v], s4[q]));
+        }
+        for (; t < n; ++t) {
+          const int gi = __shfl_sync(kFull, gidx, t);
+          const float s1 = __shfl_sync(kFull, sc, t);
+          if (act) {
+            const TG* src =
+                reinterpret_cast<const TG*>(p.grad_stage) + static_cast<int64_t>(gi) * p.grad_stage_ld + col;
+#pragma unroll
+            for (int v = 0; v < NV; ++v) acc[v] = f4_add(acc[v], f4_scale(load4<TG>(src + 4 * v), s1));
           }
         }
-        if (ss >= cb && lane == 0) p.span_u[c] = u;
+      }
+      if (act) {
+        float* dst = p.heavy_acc + static_cast<int64_t>(h) * acc_ld + col;
+#pragma unroll
+        for (int v = 0; v < NV; ++v) atomicAdd(reinterpret_cast<float4*>(dst + 4 * v), acc[v]);
       }
     }
   }
 }
 
-// Phase 6: rows whose occurrences spanned several chunks.
-template <typename TW, int VEC>
-__global__ void __launch_bounds__(kEmbThreads) emb_finalize_spanning_kernel(EmbBwdParams p) {
-  resolve_sparse_step(p);
-  const int T = p.num_unique[1];
+// 7c. optimizer on the heavy rows (one warp per row), accumulators re-zeroed.
+template <typename TW, int NV>
+__global__ void __launch_bounds__(kEmbThreads) emb_heavy_apply_kernel(EmbBwdParams p) {
+  SparseOptParams o = p.opt;
+  resolve_sparse_step(o);
+  const int H = min(p.num_unique[2], p.max_heavy);
   const int lane = lane_id();
-  const int col = lane * 4 * VEC;
+  const int col = lane * 4 * NV;
+  const int acc_ld = 32 * 4 * NV;
   const int64_t gwarp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-  const int nchunks = (T + p.chunk - 1) / p.chunk;
-  for (int64_t c = gwarp; c < nchunks; c += nwarps) {
-    const int u = p.span_u[c];
-    if (u < 0) continue;
+  for (int64_t h = gwarp; h < H; h += nwarps) {
+    const int u = p.heavy[h];
+    const long long row = p.uniq_row[u];
     const ShardDesc d = p.shards[p.uniq_shard[u]];
-    float* src = p.carry + c * (128 * VEC) + col;
-    float4 acc[VEC];
+    const bool act = col < d.ncols;
+    float* src = p.heavy_acc + h * acc_ld + col;
+    float4 acc[NV], wv[NV];
+    const int64_t eoff = d.weight_off + (row - d.row_base) * d.ncols + col;
+    TW* wp = reinterpret_cast<TW*>(p.weights) + eoff;
 #pragma unroll
-    for (int v = 0; v < VEC; ++v) {
-      acc[v] = *reinterpret_cast<float4*>(src + 4 * v);
-      *reinterpret_cast<float4*>(src + 4 * v) = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int v = 0; v < NV; ++v) {
+      acc[v] = act ? reinterpret_cast<float4*>(src)[v] : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (act) reinterpret_cast<float4*>(src)[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+      wv[v] = act ? load4<TW>(wp + 4 * v) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    apply_row_update<TW, VEC>(p, d, p.uniq_row[u], col, acc, p.seg_start[u + 1] - p.seg_start[u]);
-    if (lane == 0) p.span_u[c] = -1;
+    apply_update<TW, NV>(o, wp, eoff, row, true, act, d.ncols, acc, wv, p.cnt_u[u], 32, 0);
+    if (lane == 0) p.row_count[row] = 0;
   }
 }
 
@@ -645,17 +796,27 @@ void fwd_dispatch(const EmbFwdParams& p, int grid, cudaStream_t s) {
   count_launch();
 }
 
-template <typename TW, typename TG, int VEC>
-void bwd_tail(const EmbBwdParams& p, int grid, cudaStream_t s) {
-  emb_reduce_apply_kernel<TW, TG, VEC><<<grid, kEmbThreads, 0, s>>>(p);
-  emb_finalize_spanning_kernel<TW, VEC><<<grid, kEmbThreads, 0, s>>>(p);
-  count_launch(2);
+template <typename TW, typename TG>
+void bwd_apply(const EmbBwdParams& p, int ncols_max, int grid, cudaStream_t s) {
+  // light rows: 2 float4 (8 columns) per lane -> ncols_max / 8 lanes per row
+  const int G = std::max(1, ncols_max / 8);
+  emb_apply_light_kernel<TW, TG, 2><<<grid, kEmbThreads, 0, s>>>(p, G);
+  emb_heavy_partial_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(p);
+  emb_heavy_final_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(p);
+  if (ncols_max > 128) {
+    emb_heavy_accumulate_kernel<TG, 2><<<grid, kEmbThreads, 0, s>>>(p);
+    emb_heavy_apply_kernel<TW, 2><<<grid, kEmbThreads, 0, s>>>(p);
+  } else {
+    emb_heavy_accumulate_kernel<TG, 1><<<grid, kEmbThreads, 0, s>>>(p);
+    emb_heavy_apply_kernel<TW, 1><<<grid, kEmbThreads, 0, s>>>(p);
+  }
+  count_launch(5);
 }
 
-template <typename TW, int VEC>
-void bwd_tail_g(const EmbBwdParams& p, int grid, cudaStream_t s) {
-  if (p.grad_dtype == kBF16) bwd_tail<TW, __nv_bfloat16, VEC>(p, grid, s);
-  else bwd_tail<TW, float, VEC>(p, grid, s);
+template <typename TW>
+void bwd_apply_g(const EmbBwdParams& p, int ncols_max, int grid, cudaStream_t s) {
+  if (p.grad_dtype == kBF16) bwd_apply<TW, __nv_bfloat16>(p, ncols_max, grid, s);
+  else bwd_apply<TW, float>(p, ncols_max, grid, s);
 }
 
 }  // namespace
@@ -674,21 +835,23 @@ void emb_forward(const EmbFwdParams& p, int grid, cudaStream_t s) {
 }
 
 void emb_backward(const EmbBwdParams& p, int ncols_max, int grid, cudaStream_t s) {
-  FLARE_CHECK(ncols_max > 0 && ncols_max <= 256, "embedding shard width must be in (0, 256]");
-  FLARE_CUDA_CHECK(cudaMemsetAsync(p.num_unique, 0, 2 * sizeof(int), s));
+  FLARE_CHECK(ncols_max >= 16 && ncols_max <= 256 && (ncols_max & (ncols_max - 1)) == 0,
+              "the backward needs a power-of-two widest shard in [16, 256] columns");
+  FLARE_CHECK(p.num_shards <= kMaxShardsSmem, "too many local shards");
+  const int64_t N = static_cast<int64_t>(p.num_shards) * p.world * p.stage_cap;
+  FLARE_CHECK(N < (1ll << 31) - 1, "staging space exceeds 2^31 occurrences");
+  FLARE_CUDA_CHECK(cudaMemsetAsync(p.num_unique, 0, 4 * sizeof(int), s));
   emb_bwd_pull_count_kernel<<<grid, kEmbThreads, 0, s>>>(p);
-  emb_scan_partial_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(p);
-  emb_scan_final_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(p);
+  count_launch();
+  exclusive_scan_int(p.flags, N, p.pos, p.block_sums, s);
+  emb_emit_kernel<<<grid, kEmbThreads, 0, s>>>(p);
+  emb_seg_partial_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(p);
+  emb_seg_final_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(p);
   emb_fill_kernel<<<grid, kEmbThreads, 0, s>>>(p);
   count_launch(4);
-  const int vec = ncols_max > 128 ? 2 : 1;
-  if (p.w_dtype == kF32) {
-    if (vec == 1) bwd_tail_g<float, 1>(p, grid, s); else bwd_tail_g<float, 2>(p, grid, s);
-  } else if (p.w_dtype == kF16) {
-    if (vec == 1) bwd_tail_g<__half, 1>(p, grid, s); else bwd_tail_g<__half, 2>(p, grid, s);
-  } else {
-    if (vec == 1) bwd_tail_g<__nv_bfloat16, 1>(p, grid, s); else bwd_tail_g<__nv_bfloat16, 2>(p, grid, s);
-  }
+  if (p.w_dtype == kF32) bwd_apply_g<float>(p, ncols_max, grid, s);
+  else if (p.w_dtype == kF16) bwd_apply_g<__half>(p, ncols_max, grid, s);
+  else bwd_apply_g<__nv_bfloat16>(p, ncols_max, grid, s);
   FLARE_CUDA_CHECK(cudaGetLastError());
 }
 

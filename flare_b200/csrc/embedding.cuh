@@ -86,28 +86,36 @@ struct EmbBwdParams {
   const void* const* peer_grad;  // [world] pooled-grad buffers (rows of out_stride)
   int64_t out_stride;
   int grad_dtype;                // kBF16 or kF32
-  void* grad_stage;              // [(sh*world+s)*Bl + b][ncols_max] (grad_dtype)
+  void* grad_stage;              // [(sh*world+s)*Bl + b][grad_stage_ld] (grad_dtype)
   int64_t grad_stage_ld;
   const int* stage_ids;
   const int* stage_bag;
+  int* stage_rank;   // written by the counting pass
   const int* stage_count;
   const int* stage_len;
   int64_t stage_cap;
   void* weights;
   int w_dtype;
   // dedup / segment scratch
-  int* row_count;   // per-row occurrence counter (left at zero after the fill)
+  int* row_count;   // per-row occurrence counter (reset to zero by the apply kernels)
   int* row2u;       // per-row unique index
+  int* flags;       // [nslot*stage_cap] 1 at each row's first occurrence
+  int* pos;         // [nslot*stage_cap + 1] exclusive scan of flags
   int64_t* uniq_row;
   int* uniq_shard;
-  int* num_unique;  // [0] = U, [1] = total occurrences T
+  int* cnt_u;       // occurrences of unique row u
+  int* first_gidx;  // staged-grad row of u's first occurrence
+  int* num_unique;  // [0] U, [1] T (valid occurrences), [2] heavy rows
   int* seg_start;   // [U+1]
   int* block_sums;
-  int* occ;         // [T] staged-grad row index per occurrence, grouped by unique row
-  float* carry;     // [num_chunks][ncols_max] partial sums of rows spanning chunks
-  int* span_u;      // [num_chunks]
-  int chunk;        // occurrences per reduce chunk
-  int64_t max_occ;  // capacity of occ / uniq arrays
+  int* occ;         // staged-grad row index per occurrence, grouped by unique row
+  int* heavy;       // unique rows with more than light_max occurrences
+  int* hcnt;        // [H] occurrence count of each heavy row
+  int* heavy_start; // [H+1] exclusive prefix of heavy-row counts
+  float* heavy_acc; // [max_heavy][32*4*NV] fp32 accumulators (kept zero between steps)
+  int max_heavy;
+  int light_max;
+  int64_t max_occ;  // capacity of the per-unique arrays
   SparseOptParams opt;
   uint32_t* flags_local;
   uint32_t* const* peer_flags;

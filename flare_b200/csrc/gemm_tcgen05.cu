@@ -23,6 +23,7 @@
 
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 namespace flare {
@@ -50,6 +51,7 @@ struct EpiParams {
   int* status;
   uint64_t timeout_ns;
   int num_k_tiles;
+  int splits;       // split-K factor (gridDim.z); > 1 reduces into fp32 C with atomics
 };
 
 template <int BN, int STAGES>
@@ -79,6 +81,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = lane_id();
   const int m0 = blockIdx.x * kBM;
   const int n0 = blockIdx.y * BN;
+  // split-K: this CTA owns k-tiles [kt_begin, kt_end)
+  const int kt_begin = static_cast<int>((static_cast<int64_t>(p.num_k_tiles) * blockIdx.z) / p.splits);
+  const int kt_end = static_cast<int>((static_cast<int64_t>(p.num_k_tiles) * (blockIdx.z + 1)) / p.splits);
 
   if (threadIdx.x == 0) {
     sm100::tma_prefetch_desc(&tmap_a);
@@ -98,7 +103,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int KT = p.num_k_tiles;
+  const int KT = kt_end - kt_begin;
 
   if (warp == 0 && lane == 0) {
     // ------------------------------ producer ------------------------------
@@ -110,7 +115,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint8_t* sa = smem + L::kOffA + s * kTileBytesA;
       uint8_t* sb = smem + L::kOffB + s * L::kTileBytesB;
       sm100::mbar_arrive_expect_tx(&full_bar[s], kTileBytesA + L::kTileBytesB);
-      const int k0 = kt * kBK;
+      const int k0 = (kt_begin + kt) * kBK;
       if constexpr (!A_MN) {
         sm100::tma_load_2d(sa, &tmap_a, &full_bar[s], k0, m0);
       } else {
@@ -212,7 +217,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (ncol + lane < p.N) atomicAdd(p.colsum + ncol + lane, t[0]);
       }
-      if (row_ok) {
+      if (row_ok && p.splits > 1) {
+        // split-K partial: reduce into the fp32 output
+        float* crow = reinterpret_cast<float*>(p.C) + static_cast<int64_t>(row) * p.ldc + ncol;
+        if (full_chunk) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            atomicAdd(reinterpret_cast<float4*>(crow + 4 * q), make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+        } else {
+          for (int j = 0; j < 32; ++j)
+            if (ncol + j < p.N) atomicAdd(crow + j, v[j]);
+        }
+      } else if (row_ok) {
         if (p.c_dtype == kBF16) {
           __nv_bfloat16* crow = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<int64_t>(row) * p.ldc + ncol;
           if (full_chunk) {
@@ -285,7 +301,7 @@ CUtensorMap make_tmap_bf16(const void* base, int64_t inner, int64_t outer, int64
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN>
-void launch_cfg(const GemmArgs& a, cudaStream_t stream) {
+void launch_cfg(const GemmArgs& a, int splits, cudaStream_t stream) {
   using L = SmemLayout<BN, STAGES>;
   auto kern = gemm_bf16_kernel<BN, STAGES, A_MN, B_MN>;
   static bool attr_set = false;  // one per instantiation; set before first launch
@@ -312,18 +328,19 @@ void launch_cfg(const GemmArgs& a, cudaStream_t stream) {
   p.status = a.status;
   p.timeout_ns = a.timeout_ns;
   p.num_k_tiles = ceil_div(a.K, kBK);
-  dim3 grid(ceil_div(a.M, kBM), ceil_div(a.N, BN));
+  p.splits = splits;
+  dim3 grid(ceil_div(a.M, kBM), ceil_div(a.N, BN), splits);
   kern<<<grid, kThreads, L::kAlloc, stream>>>(ta, tb, p);
   FLARE_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }
 
 template <int BN, int STAGES>
-void launch_majors(const GemmArgs& a, cudaStream_t s) {
-  if (!a.a_mn && !a.b_mn) launch_cfg<BN, STAGES, false, false>(a, s);
-  else if (!a.a_mn && a.b_mn) launch_cfg<BN, STAGES, false, true>(a, s);
-  else if (a.a_mn && !a.b_mn) launch_cfg<BN, STAGES, true, false>(a, s);
-  else launch_cfg<BN, STAGES, true, true>(a, s);
+void launch_majors(const GemmArgs& a, int splits, cudaStream_t s) {
+  if (!a.a_mn && !a.b_mn) launch_cfg<BN, STAGES, false, false>(a, splits, s);
+  else if (!a.a_mn && a.b_mn) launch_cfg<BN, STAGES, false, true>(a, splits, s);
+  else if (a.a_mn && !a.b_mn) launch_cfg<BN, STAGES, true, false>(a, splits, s);
+  else launch_cfg<BN, STAGES, true, true>(a, splits, s);
 }
 
 }  // namespace
@@ -345,18 +362,33 @@ void gemm_bf16_tcgen05(const GemmArgs& a, int bn_hint, cudaStream_t stream) {
   FLARE_CHECK(a.ldm % 8 == 0 || a.mask == nullptr, "mask pitch must be a multiple of 8 elements");
   FLARE_CHECK((reinterpret_cast<uintptr_t>(a.C) & 15) == 0, "C must be 16-byte aligned");
   FLARE_CHECK(a.ldc % (a.c_dtype == kF32 ? 4 : 8) == 0, "C pitch must be a multiple of 16 bytes");
+  const int sms = device_sm_count();
+  const int kt = ceil_div(a.K, kBK);
+  const bool can_split = a.c_dtype == kF32 && a.accumulate && a.bias == nullptr && a.act == 0 &&
+                         a.mask == nullptr && a.colsum == nullptr;
   int bn = bn_hint;
   if (bn == 0) {
-    // Pick the widest tile that still yields at least one wave of CTAs.
-    const int sms = device_sm_count();
     const int mt = ceil_div(a.M, kBM);
-    bn = 256;
-    while (bn > 64 && static_cast<int64_t>(mt) * ceil_div(a.N, bn) < sms) bn >>= 1;
-    if (a.N <= 64) bn = 64;
+    if (can_split && kt >= 16 && static_cast<int64_t>(mt) * ceil_div(a.N, 128) < sms) {
+      bn = a.N > 64 ? 128 : 64;  // split-K fills the GPU; keep tiles wide for operand reuse
+    } else {
+      // Pick the widest tile that still yields at least one wave of CTAs.
+      bn = 256;
+      while (bn > 64 && static_cast<int64_t>(mt) * ceil_div(a.N, bn) < sms) bn >>= 1;
+      if (a.N <= 64) bn = 64;
+    }
   }
-  if (bn == 64) launch_majors<64, 4>(a, stream);
-  else if (bn == 128) launch_majors<128, 3>(a, stream);
-  else launch_majors<256, 4>(a, stream);
+  // Split-K when the output tiles cannot fill the GPU and K is long (weight
+  // gradients: K = batch).  Partials reduce into fp32 C, which therefore must
+  // already hold the value to accumulate onto (accumulate semantics).
+  int splits = 1;
+  const int tiles = ceil_div(a.M, kBM) * ceil_div(a.N, bn);
+  if (can_split && tiles < sms && kt >= 16) {
+    splits = std::min(std::min(kt / 8, 16), std::max(1, (2 * sms + tiles - 1) / tiles));
+  }
+  if (bn == 64) launch_majors<64, 4>(a, splits, stream);
+  else if (bn == 128) launch_majors<128, 3>(a, splits, stream);
+  else launch_majors<256, 4>(a, splits, stream);
 }
 
 }  // namespace flare

@@ -157,7 +157,7 @@ class DLRM:
         """Forward only (eval): sigmoid probabilities [B, T]; no state changes besides staging."""
         cast_pad_bf16(self.dense_in, self.xd)
         bot = self.bottom.forward(self.xd)
-        pooled = self.emb.forward()
+        pooled = self.emb.forward(training=False)
         interaction_forward(bot, pooled, self.F, self.inter)
         h = self.top.forward(self.inter)
         x = h.float() @ self.head_w.float().t() + self.head_b.float()

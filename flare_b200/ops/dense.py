@@ -158,19 +158,27 @@ def cast_pad_bf16(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
     return out
 
 
-def init_uniform_(t: torch.Tensor, lo: float, hi: float, seed: int, index_offset: int = 0) -> torch.Tensor:
+def init_uniform_(t: torch.Tensor, lo: float, hi: float, seed: int, index_offset: int = 0, *,
+                  ncols: int | None = None, dim: int | None = None, col_begin: int = 0) -> torch.Tensor:
     """Fill ``t`` with uniform values from a counter-based generator.
 
-    Value i depends only on (seed, index_offset + i), so a table initialised in
-    shards equals the same table initialised whole.
+    Value i of the stream depends only on (seed, index).  For a column slice
+    (``t`` viewed as [rows, ncols] holding columns [col_begin, col_begin+ncols)
+    of a table with row length ``dim``) element (r, c) takes stream index
+    ``r*dim + col_begin + c``, so column shards reproduce the whole table.
     """
     if not t.is_contiguous():
         raise ValueError("init_uniform_ needs a contiguous tensor")
+    n = t.numel()
+    ncols = ncols or n
+    dim = dim or ncols
     if not t.is_cuda:
-        t.copy_(uniform_reference(t.numel(), lo, hi, seed, index_offset).reshape(t.shape).to(t.dtype))
+        r = torch.arange(n) // ncols
+        idx = r * dim + col_begin + (torch.arange(n) - r * ncols) + index_offset
+        t.copy_(uniform_at(idx, lo, hi, seed).reshape(t.shape).to(t.dtype))
         return t
-    native().init_uniform(t.data_ptr(), dtype_code(t.dtype), t.numel(), float(lo), float(hi), int(seed),
-                          int(index_offset))
+    native().init_uniform(t.data_ptr(), dtype_code(t.dtype), n, float(lo), float(hi), int(seed),
+                          int(index_offset), int(ncols), int(dim), int(col_begin))
     return t
 
 
@@ -187,16 +195,19 @@ def _mix64(z: torch.Tensor) -> torch.Tensor:
     return z
 
 
-def uniform_reference(n: int, lo: float, hi: float, seed: int, index_offset: int = 0) -> torch.Tensor:
+def uniform_at(idx: torch.Tensor, lo: float, hi: float, seed: int) -> torch.Tensor:
     golden = 0x9E3779B97F4A7C15
     base = (seed * golden) & _M64
     if base >= 1 << 63:
         base -= 1 << 64
-    idx = torch.arange(index_offset, index_offset + n, dtype=torch.int64)
-    z = _mix64(idx + base)
+    z = _mix64(idx.to(torch.int64) + base)
     top24 = (z >> 40) & ((1 << 24) - 1)
     u = top24.to(torch.float64) / 16777216.0
     return (lo + (hi - lo) * u).to(torch.float32)
+
+
+def uniform_reference(n: int, lo: float, hi: float, seed: int, index_offset: int = 0) -> torch.Tensor:
+    return uniform_at(torch.arange(index_offset, index_offset + n, dtype=torch.int64), lo, hi, seed)
 
 
 __all__ = [
@@ -208,5 +219,6 @@ __all__ = [
     "interaction_forward",
     "interaction_out_width",
     "interaction_pairs",
+    "uniform_at",
     "uniform_reference",
 ]

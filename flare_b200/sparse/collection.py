@@ -73,7 +73,7 @@ class ShardedEmbeddingBagCollection:
         seed: int = 0,
         out_dtype: torch.dtype = torch.bfloat16,
         grad_dtype: torch.dtype = torch.bfloat16,
-        chunk: int = 64,
+        light_max: int = 16,
         values_capacity: int | None = None,
         timeout_ns: int = DEFAULT_TIMEOUT_NS,
         init: bool = True,
@@ -96,7 +96,7 @@ class ShardedEmbeddingBagCollection:
         self.plan = plan or plan_sharding(self.tables, world_size)
         self.total_dim = self.plan.total_dim
         self.max_bag = int(max_bag_size)
-        self.chunk = int(chunk)
+        self.light_max = int(light_max)
         self.timeout_ns = int(timeout_ns)
         self.out_dtype, self.grad_dtype = out_dtype, grad_dtype
         self.step = 0
@@ -132,8 +132,9 @@ class ShardedEmbeddingBagCollection:
             for s in self.shards:
                 n = s.spec.num_embeddings * s.ncols
                 view = self.weights[s.weight_off:s.weight_off + n]
-                stream_seed = (seed * 1_000_003 + s.table * 7919 + s.col_begin) & 0x7FFFFFFF
-                init_uniform_(view, -s.spec.init_scale, s.spec.init_scale, stream_seed)
+                stream_seed = (seed * 1_000_003 + s.table * 7919) & 0x7FFFFFFF
+                init_uniform_(view, -s.spec.init_scale, s.spec.init_scale, stream_seed, ncols=s.ncols,
+                              dim=s.spec.embedding_dim, col_begin=s.col_begin)
         opt = self.optimizer
         z32 = lambda n: torch.zeros(max(n, 4), dtype=torch.float32, device=dev)  # noqa: E731
         self.state_row = z32(rbase) if opt.needs_row_state else None
@@ -155,18 +156,26 @@ class ShardedEmbeddingBagCollection:
         self.stage_bag = torch.empty(nslot * self.stage_cap, dtype=torch.int32, device=dev)
         self.stage_count = torch.zeros(nslot, dtype=torch.int32, device=dev)
         self.stage_len = torch.zeros(nslot * self.B, dtype=torch.int32, device=dev)
+        self.stage_rank = torch.empty(nslot * self.stage_cap, dtype=torch.int32, device=dev)
         self.grad_stage_ld = self.ncols_max
         self.grad_stage = torch.empty(nslot * self.B * self.ncols_max, dtype=grad_dtype, device=dev)
         self.max_occ = nslot * self.stage_cap
+        self.flags_occ = torch.empty(self.max_occ, dtype=torch.int32, device=dev)
+        self.pos = torch.empty(self.max_occ + 1, dtype=torch.int32, device=dev)
         self.uniq_row = torch.empty(self.max_occ, dtype=torch.int64, device=dev)
         self.uniq_shard = torch.empty(self.max_occ, dtype=torch.int32, device=dev)
-        self.num_unique = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.cnt_u = torch.empty(self.max_occ, dtype=torch.int32, device=dev)
+        self.first_gidx = torch.empty(self.max_occ, dtype=torch.int32, device=dev)
+        self.num_unique = torch.zeros(4, dtype=torch.int32, device=dev)
         self.seg_start = torch.empty(self.max_occ + 1, dtype=torch.int32, device=dev)
         self.block_sums = torch.empty(512, dtype=torch.int32, device=dev)
         self.occ = torch.empty(self.max_occ, dtype=torch.int32, device=dev)
-        nchunks = (self.max_occ + self.chunk - 1) // self.chunk
-        self.carry = torch.zeros(nchunks * 128 * self.vec, dtype=torch.float32, device=dev)
-        self.span_u = torch.full((nchunks,), -1, dtype=torch.int32, device=dev)
+        # rows with more than light_max occurrences take the chunked path
+        self.max_heavy = min(self.max_occ // (self.light_max + 1) + 1, 1 << 20)
+        self.heavy = torch.empty(self.max_heavy, dtype=torch.int32, device=dev)
+        self.heavy_start = torch.empty(self.max_heavy + 1, dtype=torch.int32, device=dev)
+        self.hcnt = torch.empty(self.max_heavy, dtype=torch.int32, device=dev)
+        self.heavy_acc = torch.zeros(self.max_heavy * 128 * self.vec, dtype=torch.float32, device=dev)
 
         # ---- exchange buffers (symmetric when distributed) ----
         self.values_capacity = int(values_capacity or self.F * self.B * self.max_bag)
@@ -219,7 +228,8 @@ class ShardedEmbeddingBagCollection:
         self.in_offsets.local.copy_(offsets, non_blocking=non_blocking)
         self.in_values.local[:n].copy_(values, non_blocking=non_blocking)
 
-    def forward(self) -> torch.Tensor:
+    def forward(self, training: bool = True) -> torch.Tensor:
+        """Pooled embeddings of this rank's batch; ``training`` also stages the backward."""
         d = dict(
             shards=self.shard_desc.data_ptr(), num_shards=len(self.shards), world=self.world, rank=self.rank,
             Bl=self.B, F=self.F, peer_offsets=self._peer["offsets"].data_ptr(),
@@ -262,13 +272,16 @@ class ShardedEmbeddingBagCollection:
             Bl=self.B, peer_grad=self._peer["grad"].data_ptr(), out_stride=self.total_dim,
             grad_dtype=dtype_code(self.grad_dtype), grad_stage=self.grad_stage.data_ptr(),
             grad_stage_ld=self.grad_stage_ld, stage_ids=self.stage_ids.data_ptr(),
-            stage_bag=self.stage_bag.data_ptr(), stage_count=self.stage_count.data_ptr(),
-            stage_len=self.stage_len.data_ptr(), stage_cap=self.stage_cap, weights=self.weights.data_ptr(),
-            w_dtype=dtype_code(self.value_dtype), row_count=self.row_count.data_ptr(),
-            row2u=self.row2u.data_ptr(), uniq_row=self.uniq_row.data_ptr(), uniq_shard=self.uniq_shard.data_ptr(),
+            stage_bag=self.stage_bag.data_ptr(), stage_rank=self.stage_rank.data_ptr(),
+            stage_count=self.stage_count.data_ptr(), stage_len=self.stage_len.data_ptr(),
+            stage_cap=self.stage_cap, weights=self.weights.data_ptr(), w_dtype=dtype_code(self.value_dtype),
+            row_count=self.row_count.data_ptr(), row2u=self.row2u.data_ptr(), flags=self.flags_occ.data_ptr(),
+            pos=self.pos.data_ptr(), uniq_row=self.uniq_row.data_ptr(), uniq_shard=self.uniq_shard.data_ptr(),
+            cnt_u=self.cnt_u.data_ptr(), first_gidx=self.first_gidx.data_ptr(),
             num_unique=self.num_unique.data_ptr(), seg_start=self.seg_start.data_ptr(),
-            block_sums=self.block_sums.data_ptr(), occ=self.occ.data_ptr(), carry=self.carry.data_ptr(),
-            span_u=self.span_u.data_ptr(), chunk=self.chunk, max_occ=self.max_occ, opt=op,
+            block_sums=self.block_sums.data_ptr(), occ=self.occ.data_ptr(), heavy=self.heavy.data_ptr(),
+            heavy_start=self.heavy_start.data_ptr(), hcnt=self.hcnt.data_ptr(), heavy_acc=self.heavy_acc.data_ptr(), max_heavy=self.max_heavy,
+            light_max=self.light_max, max_occ=self.max_occ, opt=op,
             flags_local=self.flags.local_ptr, peer_flags=self.flags.peer_ptrs.data_ptr(),
             flag_in=self.flags.slots(FLAG_BWD_IN), epoch_ctr=self.flags.epoch_ptr(FLAG_BWD_IN),
             block_counter=self.flags.block_counter_ptr(FLAG_BWD_IN), status=self.status.ptr,
@@ -278,6 +291,11 @@ class ShardedEmbeddingBagCollection:
 
     def check(self) -> None:
         self.status.check("sharded embedding")
+
+    def last_step_stats(self) -> dict:
+        """Unique rows, valid occurrences and heavy rows of the last backward (device sync)."""
+        u, t, h, _ = self.num_unique.tolist()
+        return {"unique_rows": u, "occurrences": t, "heavy_rows": h}
 
     # ------------------------------------------------------------ state I/O
     def shard_view(self, i: int) -> torch.Tensor:
@@ -324,8 +342,9 @@ class ShardedEmbeddingBagCollection:
 
     def memory_bytes(self) -> int:
         tensors = [self.weights, self.state_row, self.state_m, self.state_v, self.score, self.row_count,
-                   self.row2u, self.stage_ids, self.stage_bag, self.grad_stage, self.uniq_row, self.occ,
-                   self.seg_start, self.carry]
+                   self.row2u, self.stage_ids, self.stage_bag, self.stage_rank, self.grad_stage, self.uniq_row,
+                   self.occ, self.seg_start, self.flags_occ, self.pos, self.cnt_u, self.first_gidx, self.heavy,
+                   self.heavy_acc]
         return sum(t.numel() * t.element_size() for t in tensors if t is not None)
 
 

@@ -1,0 +1,106 @@
+"""Multi-GPU equivalence check for the fused DLRM path (run under torch.distributed.run).
+
+Every rank trains the world-size-W model on its own batch; rank 0 also trains a
+world-size-1 model on the concatenation of all ranks' batches.  After K steps
+the sharded tables and the dense parameters must agree (fp32 tolerance).  This
+exercises the in-kernel ids / pooled / gradient all-to-alls over NVLink peer
+memory, the table/column-wise planner and the fused ZeRO-1 dense update.
+
+    python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 \
+        -m flare_b200.testing.dist_dlrm_check
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+from flare_b200.data.synthetic import DLRMSyntheticData, SparseBatch
+from flare_b200.models.dlrm import DLRMConfig, dlrm_benchmark_tables
+from flare_b200.parallel.dist import init_distributed, shutdown
+from flare_b200.sparse.config import SparseOptimizerConfig
+from flare_b200.training.trainer import DLRMTrainer
+
+VOCABS = [300, 5000, 64, 20000, 1000, 7000, 150]
+
+
+def concat_batches(batches: list[SparseBatch], F: int) -> SparseBatch:
+    """Concatenate keyed-jagged batches along the sample axis (feature-major layout)."""
+    B = [b.dense.shape[0] for b in batches]
+    vals, offs = [], [0]
+    for f in range(F):
+        for b, n in zip(batches, B):
+            o = b.offsets.long()
+            seg = o[f * n:(f + 1) * n + 1]
+            vals.append(b.values[seg[0]:seg[-1]])
+            offs.extend((seg[1:] - seg[0] + offs[-1]).tolist())
+    return SparseBatch(torch.cat([b.dense for b in batches]), torch.cat([b.labels for b in batches]),
+                       torch.tensor(offs, dtype=torch.int32, device=batches[0].values.device), torch.cat(vals))
+
+
+def export_tables(trainer: DLRMTrainer) -> dict:
+    out = {}
+    emb = trainer.model.emb
+    for i, s in enumerate(emb.shards):
+        out[(s.table, s.col_begin)] = emb.shard_view(i).float().cpu()
+    return out
+
+
+def main(steps: int = 3, B: int = 128) -> int:
+    info = init_distributed(timeout_s=120)
+    rank, world = info.rank, info.world_size
+    dev = torch.device("cuda", torch.cuda.current_device())
+    opt = SparseOptimizerConfig(kind="rowwise_adagrad", learning_rate=0.05)
+    cfg = DLRMConfig(tables=dlrm_benchmark_tables(VOCABS, 64, opt), bottom=(128, 64), top=(128, 64),
+                     sparse_optimizer=opt)
+    gens = [DLRMSyntheticData(B, VOCABS, max_bag=10, seed=7, rank=r, device=dev, pos_rate=0.3) for r in range(world)]
+    data = [[g.next() for _ in range(steps)] for g in gens]
+    tr = DLRMTrainer(cfg, B, max_bag_size=10, rank=rank, world_size=world, device=dev, seed=11, use_graph=False)
+    losses = [tr.train_step(data[rank][k]).loss for k in range(steps)]
+    torch.cuda.synchronize()
+    tr.check()
+    tables = export_tables(tr)
+    gathered = [None] * world
+    dist.all_gather_object(gathered, tables)
+    master = tr.model.dense.gather_master()
+    ok = True
+    if rank == 0:
+        ref = DLRMTrainer(cfg, B * world, max_bag_size=10, device=dev, seed=11, use_graph=False)
+        for k in range(steps):
+            ref.train_step(concat_batches([data[r][k] for r in range(world)], len(VOCABS)))
+        torch.cuda.synchronize()
+        ref_tables = export_tables(ref)
+        full = {}
+        for part in gathered:
+            for (t, cb), w in part.items():
+                full.setdefault(t, torch.zeros(VOCABS[t], 64))[:, cb:cb + w.shape[1]] = w
+        for (t, _), w in ref_tables.items():
+            err = (full[t] - w).abs().max().item()
+            if err > 2e-4:
+                print(f"table {t}: max abs diff {err}", file=sys.stderr)
+                ok = False
+        rd = ref.model.dense
+        for name, e in tr.model.params.entries.items():
+            got = master[e.offset:e.offset + e.numel]
+            want = rd.master_view(name).reshape(-1)
+            diff = (got - want).abs()
+            # Adam normalises each element's step, so an element whose gradient
+            # is ~0 can differ by up to lr per step when summation order flips
+            # its sign; bound the maximum by steps*lr and the mean tightly.
+            if diff.max().item() > 1.2e-3 * steps or diff.mean().item() > 2e-5:
+                print(f"dense {name}: max {diff.max().item()} mean {diff.mean().item()}", file=sys.stderr)
+                ok = False
+        print(f"losses rank0 {losses}", file=sys.stderr)
+    flag = torch.tensor([1 if ok else 0], device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    tr.close()
+    shutdown()
+    if rank == 0:
+        print("DIST_OK" if flag.item() == 1 else "DIST_MISMATCH", flush=True)
+    return 0 if flag.item() == 1 else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main(int(os.environ.get("CHECK_STEPS", "3"))))

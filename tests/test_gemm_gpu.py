@@ -63,3 +63,15 @@ def test_gemm_small_k_padded_input(cuda):
     w = _rand(512, 16, device=cuda)
     out = gemm(x, w, out_dtype=torch.float32)
     torch.testing.assert_close(out, gemm_reference(x, w), rtol=2e-3, atol=2e-3)
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 480, 8192), (128, 16, 4096), (1024, 1024, 2048)])
+def test_gemm_split_k_weight_gradient(cuda, M, N, K):
+    """dW = dY^T X with K = batch: both operands MN-major, fp32 accumulate -> split-K path."""
+    torch.manual_seed(5)
+    dy = _rand(K, M, device=cuda)
+    x = _rand(K, N, device=cuda)
+    out = torch.full((M, N), 0.25, device=cuda)
+    gemm(dy, x, a_t=True, b_t=True, out=out, accumulate=True)
+    ref = 0.25 + gemm_reference(dy, x, a_t=True, b_t=True)
+    torch.testing.assert_close(out, ref, rtol=2e-3, atol=2e-2)
