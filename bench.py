@@ -54,6 +54,14 @@ def emit(obj):
     print(json.dumps(obj), flush=True)
 
 
+_T0 = time.time()
+
+
+def log(msg: str) -> None:
+    """Progress line on stderr (rank-tagged)."""
+    print(f"[bench rank{os.environ.get('RANK', '0')} +{time.time() - _T0:7.1f}s] {msg}", file=sys.stderr, flush=True)
+
+
 def reference_arm(args):
     """Run the unmodified reference through its own public API, if it can be imported."""
     ref_dir = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
@@ -96,9 +104,11 @@ def main():
     cfg = DLRMConfig(tables=dlrm_benchmark_tables(vocabs, 128, sparse_opt), sparse_optimizer=sparse_opt,
                      dense_optimizer=DenseOptimizerConfig(kind="adam", learning_rate=1e-3))
 
+    log(f"world={world} building data")
     gens = DLRMSyntheticData(B, vocabs, max_bag=args.max_bag, seed=args.seed, rank=rank, device=dev)
     batches = [gens.next() for _ in range(args.num_batches)]
-    max_nnz = max(b.values.numel() for b in batches)
+    # identical capacities on every rank (symmetric buffers)
+    max_nnz = int(max_over_ranks(max(b.values.numel() for b in batches)))
 
     if args.impl == "torch":
         run_torch_baseline(args, cfg, batches, rank, world, dev)
@@ -112,6 +122,7 @@ def main():
                           seed=args.seed, use_graph=not args.no_graph, values_capacity=max_nnz + 1024)
     model = trainer.model
     stream = torch.cuda.current_stream(dev)
+    log(f"model built: {len(model.emb.shards)} local shards, {model.emb.memory_bytes() / 1e9:.1f} GB sparse state")
 
     def device_step(i):
         b = batches[i % len(batches)]
@@ -121,7 +132,8 @@ def main():
 
     for i in range(max(args.warmup, 3)):
         device_step(i)
-    torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        log(f"warmup step {i} done")
     trainer.check()
     launches_per_step = trainer.launches_per_step
     barrier()
@@ -135,6 +147,7 @@ def main():
     torch.cuda.synchronize()
     barrier()
     clk = clocks.stop()
+    log("timed region done")
     ms = t0.elapsed_time(t1) / args.steps
     ms_max = max_over_ranks(ms)
     trainer.check()
@@ -155,6 +168,7 @@ def main():
     embed_ms = max_over_ranks(e0.elapsed_time(e1) / 3)
     emb_stats = model.emb.last_step_stats()
 
+    log("embedding-only timing done")
     # e2e through the public API: inputs in pinned host memory, loss read back every step
     e2e = None
     if not args.no_e2e:

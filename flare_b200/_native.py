@@ -96,4 +96,8 @@ def default_status(device: torch.device) -> DeviceStatus:
     return _STATUS[idx]
 
 
-DEFAULT_TIMEOUT_NS = 2_000_000_000
+DEFAULT_TIMEOUT_NS = 2_000_000_000        # waits inside one CTA (mbarrier phases)
+import os as _os
+
+# waits on another GPU's signal (absorbs host-side skew); FLARE_PEER_TIMEOUT_S overrides
+PEER_TIMEOUT_NS = int(float(_os.environ.get("FLARE_PEER_TIMEOUT_S", "30")) * 1e9)

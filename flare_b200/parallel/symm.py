@@ -58,14 +58,25 @@ class SymmetricHeap:
         self.offset = 0
 
     def alloc(self, shape, dtype: torch.dtype) -> SymBuffer:
+        """Carve a buffer at the same offset on every rank.
+
+        Every rank must call ``alloc`` in the same order; the reserved size is
+        the maximum requested over ranks, so per-rank differences in the
+        requested size (e.g. capacities derived from local data) can never
+        shift later buffers out of alignment across ranks.
+        """
         numel = 1
         for s in shape:
             numel *= int(s)
         nbytes = numel * torch.empty((), dtype=dtype).element_size()
+        reserve = nbytes
+        if self.world_size > 1:
+            sizes = all_gather_object(int(nbytes))
+            reserve = max(sizes)
         off = (self.offset + ALIGN - 1) // ALIGN * ALIGN
-        if off + nbytes > self.nbytes:
-            raise MemoryError(f"symmetric heap exhausted: need {off + nbytes} of {self.nbytes} bytes")
-        self.offset = off + nbytes
+        if off + reserve > self.nbytes:
+            raise MemoryError(f"symmetric heap exhausted: need {off + reserve} of {self.nbytes} bytes")
+        self.offset = off + reserve
         t = native().tensor_from_ptr(self.base + off, list(shape), dtype, self.device.index)
         return SymBuffer(t, off, [b + off for b in self.peer_base])
 

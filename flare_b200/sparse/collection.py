@@ -28,7 +28,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from .._native import DEFAULT_TIMEOUT_NS, DeviceStatus, dtype_code, native
+from .._native import PEER_TIMEOUT_NS, DeviceStatus, dtype_code, native
 from ..ops.dense import init_uniform_
 from ..parallel.symm import FlagRegion, SymmetricHeap
 from .config import SparseOptimizerConfig, SparseTableSpec
@@ -44,6 +44,12 @@ _SHARD_DTYPE = np.dtype([
 assert _SHARD_DTYPE.itemsize == 48
 
 FLAG_FWD_IN, FLAG_FWD_OUT, FLAG_BWD_IN, NUM_FLAG_ARRAYS = 0, 1, 2, 3
+
+
+def _with_opt(t: SparseTableSpec, opt: SparseOptimizerConfig) -> SparseTableSpec:
+    from dataclasses import replace
+
+    return replace(t, optimizer=opt)
 
 
 @dataclass
@@ -75,7 +81,7 @@ class ShardedEmbeddingBagCollection:
         grad_dtype: torch.dtype = torch.bfloat16,
         light_max: int = 16,
         values_capacity: int | None = None,
-        timeout_ns: int = DEFAULT_TIMEOUT_NS,
+        timeout_ns: int = PEER_TIMEOUT_NS,
         init: bool = True,
     ):
         if not tables:
@@ -93,7 +99,10 @@ class ShardedEmbeddingBagCollection:
         self.F = len(tables)
         self.rank, self.world = rank, world_size
         self.device = device or torch.device("cuda", torch.cuda.current_device())
-        self.plan = plan or plan_sharding(self.tables, world_size)
+        if plan is None:
+            tabs = [t if t.optimizer == self.optimizer else _with_opt(t, self.optimizer) for t in self.tables]
+            plan = plan_sharding(tabs, world_size)
+        self.plan = plan
         self.total_dim = self.plan.total_dim
         self.max_bag = int(max_bag_size)
         self.light_max = int(light_max)

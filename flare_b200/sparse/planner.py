@@ -58,7 +58,16 @@ def plan_sharding(
     expected_lookups: list[float] | None = None,
     hbm_budget_bytes: float | None = None,
     max_rounds: int = 64,
+    allow_rowwise_column_split: bool = False,
 ) -> ShardingPlan:
+    """Place tables (or column slices) on ranks.
+
+    Column splits are made only for tables whose optimizer is elementwise:
+    a row-wise optimizer (row-wise Adagrad/Adam) keeps one state value per
+    row, and splitting columns would give each slice its own state, which
+    changes the update.  ``allow_rowwise_column_split`` permits it anyway
+    (per-slice row state, as some embedding libraries do).
+    """
     if world_size < 1:
         raise ValueError("world_size must be >= 1")
     for t in tables:
@@ -103,7 +112,8 @@ def plan_sharding(
         for _ in range(max_rounds):
             hot = loads.index(max(loads))
             cand = [k for k in range(len(pieces)) if owner[k] == hot and pieces[k][2] // 2 in VALID_SHARD_WIDTHS
-                    and pieces[k][2] >= 16]
+                    and pieces[k][2] >= 32
+                    and (allow_rowwise_column_split or not tables[pieces[k][0]].optimizer.needs_row_state)]
             if not cand:
                 break
             k = max(cand, key=lambda k: (work[pieces[k][0]] * pieces[k][2], -k))

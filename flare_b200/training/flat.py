@@ -23,7 +23,7 @@ from dataclasses import dataclass, field
 
 import torch
 
-from .._native import DEFAULT_TIMEOUT_NS, DeviceStatus, native
+from .._native import PEER_TIMEOUT_NS, DeviceStatus, native
 from ..parallel.symm import FlagRegion, SymmetricHeap
 
 ALIGN = 64
@@ -104,7 +104,7 @@ class DenseState:
 
     def __init__(self, params: FlatParams, opt: DenseOptimizerConfig, *, device: torch.device,
                  rank: int = 0, world_size: int = 1, heap: SymmetricHeap | None = None, seed: int = 0,
-                 timeout_ns: int = DEFAULT_TIMEOUT_NS):
+                 timeout_ns: int = PEER_TIMEOUT_NS):
         if world_size > 1 and not opt.shardable:
             raise ValueError("sharded (ZeRO-1) dense update requires an optimizer without global-norm clipping")
         self.params, self.opt = params, opt

@@ -23,6 +23,7 @@ import torch
 from .._native import native
 from ..data.synthetic import SparseBatch
 from ..models.dlrm import DLRM, DLRMConfig
+from ..parallel.dist import barrier
 from ..parallel.symm import SymmetricHeap
 
 
@@ -63,6 +64,11 @@ class DLRMTrainer:
         self._stage_free = [torch.cuda.Event(), torch.cuda.Event()]
         self._stage_used = [False, False]
         self._pending = False
+        if world_size > 1:
+            # every rank finishes building (allocation, table init) before any
+            # rank can enter a fused kernel that waits on its peers
+            torch.cuda.synchronize(self.device)
+            barrier()
 
     # ---------------------------------------------------------------- graph
     EAGER_STEPS = 2  # steps run eagerly (module load, allocator warm-up) before capture

@@ -23,4 +23,6 @@ def test_two_gpu_matches_single_gpu_on_global_batch():
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
            "--master-addr=127.0.0.1", f"--master-port={_free_port()}", "-m", "flare_b200.testing.dist_dlrm_check"]
     res = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=400)
-    assert res.returncode == 0 and "DIST_OK" in res.stdout, res.stdout[-3000:] + res.stderr[-5000:]
+    if res.returncode != 0 or "DIST_OK" not in res.stdout:
+        lines = [ln for ln in (res.stdout + res.stderr).splitlines() if "[rank" in ln or "Error" in ln or "diff" in ln]
+        raise AssertionError("\n".join(lines[-80:]))
