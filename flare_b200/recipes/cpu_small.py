@@ -1,0 +1,125 @@
+"""The synthetic CPU ranking configuration (single process, fp32).
+
+13 dense N(0,1) features, 8 single-id categorical features (Zipf(1.1) over
+1,000 ids per table), embedding dim 16 with sum pooling, bottom MLP
+13-64-16 with ReLU, pairwise dot interaction over the 9 vectors, top MLP
+52-64-32-1, Bernoulli(sigmoid(a.x + 0.5 N(0,1))) labels; row-wise Adagrad
+(lr 0.01) for the tables and Adam (lr 1e-3) for the dense weights; batch 256,
+200 steps.  Dense training goes through ``TrainEngine`` (world size 1 or a
+gloo group) and the tables through the CPU reference collection, the same
+forward/backward contract as the fused GPU collection.
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass
+
+import torch
+import torch.nn as nn
+
+from ..data.synthetic import SmallSyntheticData
+from ..sparse.config import SparseOptimizerConfig, SparseTableSpec
+from ..sparse.reference import CpuEmbeddingBagCollection
+from ..training.contracts import TrainingExecutionPlan
+from ..training.engine import TrainEngine
+from ..training.flat import DenseOptimizerConfig
+
+
+class DotInteraction(nn.Module):
+    def __init__(self, num_vectors: int):
+        super().__init__()
+        ii, jj = torch.tril_indices(num_vectors, num_vectors, offset=-1)
+        self.register_buffer("ii", ii, persistent=False)
+        self.register_buffer("jj", jj, persistent=False)
+
+    def forward(self, bot: torch.Tensor, emb: torch.Tensor) -> torch.Tensor:
+        z = torch.cat([bot.unsqueeze(1), emb], 1)
+        zz = torch.bmm(z, z.transpose(1, 2))
+        return torch.cat([bot, zz[:, self.ii, self.jj]], 1)
+
+
+class SmallDense(nn.Module):
+    def __init__(self, num_dense: int = 13, num_sparse: int = 8, dim: int = 16):
+        super().__init__()
+        self.F, self.D = num_sparse, dim
+        self.bottom = nn.Sequential(nn.Linear(num_dense, 64), nn.ReLU(), nn.Linear(64, dim), nn.ReLU())
+        self.inter = DotInteraction(num_sparse + 1)
+        width = dim + (num_sparse + 1) * num_sparse // 2
+        self.top = nn.Sequential(nn.Linear(width, 64), nn.ReLU(), nn.Linear(64, 32), nn.ReLU(), nn.Linear(32, 1))
+
+    def forward(self, inputs):
+        dense, pooled = inputs
+        bot = self.bottom(dense)
+        x = self.inter(bot, pooled.reshape(-1, self.F, self.D))
+        return self.top(x)
+
+
+@dataclass
+class SmallRunResult:
+    losses: list[float]
+    samples_per_s: float
+    steps: int
+
+
+def small_tables(opt: SparseOptimizerConfig | None = None) -> list[SparseTableSpec]:
+    opt = opt or SparseOptimizerConfig(kind="rowwise_adagrad", learning_rate=0.01)
+    return [SparseTableSpec(f"c{i}", 1000, 16, optimizer=opt) for i in range(8)]
+
+
+def train_small_cpu(steps: int = 200, batch_size: int = 256, seed: int = 0) -> SmallRunResult:
+    torch.manual_seed(seed)
+    data = SmallSyntheticData(batch_size, seed=seed)
+    emb = CpuEmbeddingBagCollection(small_tables(), batch_size, seed=seed)
+    model = SmallDense()
+    engine = TrainEngine(model, lambda out, y: nn.functional.binary_cross_entropy_with_logits(out, y),
+                         TrainingExecutionPlan.replicated(), DenseOptimizerConfig(kind="adam", learning_rate=1e-3),
+                         device=torch.device("cpu"))
+    losses = []
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        b = data.next()
+        emb.set_input(b.offsets, b.values)
+        pooled = emb.forward().requires_grad_(True)
+        res = engine.micro_step_once((b.dense, pooled), b.labels)
+        emb.backward(pooled.grad)
+        losses.append(float(res.loss))
+    dt = time.perf_counter() - t0
+    return SmallRunResult(losses, steps * batch_size / dt, steps)
+
+
+def train_small_oracle(steps: int = 200, batch_size: int = 256, seed: int = 0) -> list[float]:
+    """Plain PyTorch oracle: nn.EmbeddingBag weights + torch.optim.Adam + explicit row-wise Adagrad."""
+    torch.manual_seed(seed)
+    data = SmallSyntheticData(batch_size, seed=seed)
+    ref = CpuEmbeddingBagCollection(small_tables(), batch_size, seed=seed)  # same initial tables
+    tables = [w.clone().requires_grad_(True) for w in ref.weights]
+    state = [torch.zeros(w.shape[0]) for w in tables]
+    model = SmallDense()
+    opt = torch.optim.Adam(model.parameters(), lr=1e-3, eps=1e-8)
+    losses = []
+    for _ in range(steps):
+        b = data.next()
+        offs = b.offsets.long()
+        pooled = []
+        for f, w in enumerate(tables):
+            seg = offs[f * batch_size:(f + 1) * batch_size + 1]
+            pooled.append(nn.functional.embedding_bag(b.values[seg[0]:seg[-1]].long(), w,
+                                                      seg[:-1] - seg[0], mode="sum"))
+        out = model((b.dense, torch.cat(pooled, 1)))
+        loss = nn.functional.binary_cross_entropy_with_logits(out, b.labels)
+        opt.zero_grad()
+        for w in tables:
+            w.grad = None
+        loss.backward()
+        opt.step()
+        with torch.no_grad():
+            for w, s in zip(tables, state):
+                g = w.grad
+                rows = torch.nonzero(g.abs().sum(1) > 0).flatten()
+                s[rows] += (g[rows] ** 2).mean(1)
+                w[rows] -= 0.01 * g[rows] / (torch.sqrt(s[rows]).unsqueeze(1) + 1e-8)
+        losses.append(float(loss.detach()))
+    return losses
+
+
+__all__ = ["SmallDense", "SmallRunResult", "small_tables", "train_small_cpu", "train_small_oracle"]

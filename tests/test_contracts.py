@@ -1,0 +1,67 @@
+import pytest
+
+from flare_b200.training.contracts import (
+    EvaluationEnvelope,
+    OptimizerUpdateWindow,
+    PayloadField,
+    PayloadSchema,
+    TrainingExecutionPlan,
+    TrainingStateBlueprint,
+    ZeroExecutionPolicy,
+    ZeroStage,
+    resolve_training_input_plan,
+    zero_partition_contract,
+)
+from flare_b200.training.precision import PrecisionPolicy
+
+
+def test_zero_contract_table():
+    c = zero_partition_contract(ZeroStage.GRADIENT)
+    assert (c.parameter_partition, c.optimizer_state_partition, c.gradient_partition) == (
+        "replicated", "sharded", "sharded")
+    assert (c.gradient_collective, c.parameter_collective) == ("reduce-scatter", "all-gather")
+    assert zero_partition_contract(ZeroStage.OPTIMIZER_STATE).gradient_collective == "all-reduce"
+    assert zero_partition_contract(ZeroStage.PARAMETER).parameter_partition == "sharded"
+    with pytest.raises(TypeError):
+        zero_partition_contract(2)
+    with pytest.raises(ValueError):
+        ZeroExecutionPolicy(ZeroStage.REPLICATED, shard_scope="node")
+
+
+def test_update_window_roundtrip_and_validation():
+    w = OptimizerUpdateWindow(2, 2, True, True, 7)
+    assert OptimizerUpdateWindow.decode(w.encode()) == w
+    with pytest.raises(ValueError):
+        OptimizerUpdateWindow(1, 2, True, False, 0)
+    with pytest.raises(ValueError):
+        OptimizerUpdateWindow(1, 2, False, True, 0)
+    with pytest.raises(ValueError):
+        OptimizerUpdateWindow.decode([1, 2, 3])
+    with pytest.raises(ValueError):
+        OptimizerUpdateWindow.decode([1, 1, 2, 0, 0])
+
+
+def test_input_plan():
+    p = resolve_training_input_plan(reader_repeat_first_batch=False, latest_checkpoint_step=None, run_steps=10,
+                                    target_step=10, checkpoint_interval_steps=5)
+    assert p.mode == "manifest" and p.checkpoint_enabled and p.checkpoint_reason == "scheduled"
+    p = resolve_training_input_plan(reader_repeat_first_batch=True, latest_checkpoint_step=None, run_steps=10,
+                                    target_step=7, checkpoint_interval_steps=50)
+    assert p.mode == "repeat_first_batch" and p.source_epochs == 7 and not p.checkpoint_enabled
+    with pytest.raises(ValueError):
+        resolve_training_input_plan(reader_repeat_first_batch=True, latest_checkpoint_step=3, run_steps=10,
+                                    target_step=7, checkpoint_interval_steps=5)
+
+
+def test_plans_schema_precision():
+    plan = TrainingExecutionPlan.sharded(ZeroStage.GRADIENT, micro_steps=4, sync_mode="micro")
+    assert plan.accumulation.micro_steps == 4 and plan.zero.stage is ZeroStage.GRADIENT
+    with pytest.raises(ValueError):
+        PayloadSchema("p", (PayloadField("a", "int32", (None,)), PayloadField("a", "int32", (None,))))
+    with pytest.raises(ValueError):
+        TrainingStateBlueprint(("g",), (("x", (1,), "float32", "param"), ("x", (1,), "float32", "param")), "d")
+    env = EvaluationEnvelope.from_metadata(payload=1, request_id="r", schema_id="s", metadata={"k": 1})
+    assert env.metadata["k"] == 1
+    assert PrecisionPolicy.BF16.gradient_transport_dtype.is_floating_point
+    assert PrecisionPolicy.BF16.sparse_storage_dtype_name == "float16"
+    assert PrecisionPolicy.FP32.sparse_gradient_transport_dtype_name == "float32"

@@ -1,0 +1,31 @@
+import numpy as np
+import torch
+
+from flare_b200.recipes.cpu_small import train_small_cpu, train_small_oracle
+from flare_b200.recipes.ranking import MultiTargetCrossEntropyLoss, RankingLossAdapter, RankingTask
+
+
+def test_cpu_small_config_matches_pytorch_oracle_and_learns():
+    res = train_small_cpu(steps=200)
+    oracle = train_small_oracle(steps=200)
+    assert max(abs(a - b) for a, b in zip(res.losses, oracle)) < 1e-4
+    assert np.mean(res.losses[-20:]) < np.mean(res.losses[:10]) - 0.1
+
+
+def test_multitarget_loss_and_adapter():
+    loss = MultiTargetCrossEntropyLoss.create(
+        {"click": {"sample_weight": {"neg": -1.0, "click": 1.0, "buy": 2.0}},
+         "buy": {"sample_weight": {"neg": -1.0, "click": -1.0, "buy": 3.0}, "class_weight": 0.5}},
+        {"neg": 0, "click": 1, "buy": 2}, target_names=("click", "buy"))
+    assert loss.target_labels.tolist() == [[0, 1, 1], [0, 0, 1]]
+    logits = torch.zeros(4, 2)
+    labels = torch.tensor([0, 1, 2, 2])
+    full = loss(logits, labels, torch.ones(4))
+    # BCE(0, y) = ln 2 for every entry; weights: click row |w|, buy row 0.5*|w|
+    w = torch.tensor([[1, 0.5], [1, 0.5], [2, 1.5], [2, 1.5]])
+    assert torch.allclose(full, w.sum() * np.log(2))
+    adapter = RankingLossAdapter(loss)
+    out = adapter({"logits": logits}, {"labels": labels, "samples_valid_count": [3], "global_row_start": 0,
+                                       "world_size": 1})
+    assert torch.allclose(out, w[:3].sum() * np.log(2) / 3)
+    RankingTask("label", "group", loss)

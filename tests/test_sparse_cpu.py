@@ -1,0 +1,107 @@
+import pytest
+import torch
+
+from flare_b200.data.synthetic import SCRAMBLE, DLRMSyntheticData, log_uniform_vocab_sizes, make_jagged, zipf_ids
+from flare_b200.ops.sparse import CpuSparseEmbeddingOperator, unique_first_occurrence, unique_first_occurrence_reference
+from flare_b200.sparse.config import SparseOptimizerConfig, SparseTableSpec
+from flare_b200.sparse.planner import plan_sharding
+from flare_b200.sparse.precision import prepare_sparse_native_gradient, require_finite_sparse_values
+from flare_b200.sparse.reference import CpuEmbeddingBagCollection, pool_reference
+
+
+def test_vocab_sizes_and_zipf():
+    v = log_uniform_vocab_sizes()
+    assert len(v) == 26 and v[0] == 1000 and v[-1] == 40_000_000 and abs(sum(v) - 2e8) / 2e8 < 0.01
+    g = torch.Generator().manual_seed(0)
+    ids = zipf_ids(100000, 1000, 1.05, g)
+    assert int(ids.min()) >= 0 and int(ids.max()) < 1000
+    # the most frequent id is the scrambled rank-0 id and is much hotter than the median
+    counts = torch.bincount(ids.long(), minlength=1000)
+    assert int(counts.argmax()) == 0 and counts.max() > 20 * counts.median()
+    assert SCRAMBLE % 1000 != 0
+
+
+def test_dlrm_generator_shapes():
+    d = DLRMSyntheticData(64, [100, 200, 300], max_bag=5)
+    b = d.next()
+    assert b.dense.shape == (64, 13) and b.labels.shape == (64, 1)
+    assert b.offsets.numel() == 3 * 64 + 1 and int(b.offsets[-1]) == b.values.numel()
+    lens = b.offsets[1:] - b.offsets[:-1]
+    assert int(lens.min()) >= 1 and int(lens.max()) <= 5
+
+
+def test_planner_balance_and_rowwise_exactness():
+    opt = SparseOptimizerConfig(kind="adam")
+    tabs = [SparseTableSpec(f"t{i}", 100 * (i + 1), 128, optimizer=opt) for i in range(26)]
+    p = plan_sharding(tabs, 8)
+    loads = p.load([1.0] * 26)
+    assert max(loads) == min(loads)
+    cols = {}
+    for pl in p.placements:
+        cols.setdefault(pl.table, []).append((pl.col_begin, pl.ncols))
+    for t, pieces in cols.items():
+        assert sum(n for _, n in pieces) == 128
+    rw = [SparseTableSpec(f"t{i}", 100, 128) for i in range(26)]  # row-wise adagrad default
+    assert all(pl.ncols == 128 for pl in plan_sharding(rw, 8).placements)
+    with pytest.raises(MemoryError):
+        plan_sharding([SparseTableSpec("big", 10**9, 128)], 2, hbm_budget_bytes=1e9)
+
+
+def test_reference_pool_matches_bruteforce():
+    tabs = [SparseTableSpec("a", 50, 8), SparseTableSpec("b", 30, 8, pooling="mean")]
+    g = torch.Generator().manual_seed(1)
+    lengths = torch.randint(0, 6, (2, 10), generator=g)
+    offs, vals = make_jagged(lengths, [50, 30], 1.1, g)
+    ws = [torch.randn(50, 8), torch.randn(30, 8)]
+    out = pool_reference(ws, tabs, offs, vals, 10)
+    for f in range(2):
+        for b in range(10):
+            s, e = int(offs[f * 10 + b]), int(offs[f * 10 + b + 1])
+            want = ws[f][vals[s:e].long()].sum(0)
+            if tabs[f].pooling == "mean" and e > s:
+                want = want / (e - s)
+            assert torch.allclose(out[b, 8 * f:8 * f + 8], want, atol=1e-6)
+
+
+def test_reference_rowwise_adagrad_update():
+    opt = SparseOptimizerConfig(kind="rowwise_adagrad", learning_rate=0.1)
+    tabs = [SparseTableSpec("a", 10, 4, optimizer=opt)]
+    coll = CpuEmbeddingBagCollection(tabs, 2, optimizer=opt, weights=[torch.zeros(10, 4)])
+    offs = torch.tensor([0, 2, 3], dtype=torch.int32)
+    vals = torch.tensor([3, 3, 5], dtype=torch.int32)
+    coll.set_input(offs, vals)
+    coll.forward()
+    g = torch.tensor([[1.0, 2.0, 3.0, 4.0], [1.0, 1.0, 1.0, 1.0]])
+    coll.backward(g, 1)
+    # row 3 appears twice in bag 0 -> gradient 2*g0; state = mean(g^2)
+    g3 = 2 * g[0]
+    s3 = (g3 ** 2).mean()
+    assert torch.allclose(coll.weights[0][3], -0.1 * g3 / (s3.sqrt() + 1e-8), atol=1e-6)
+    assert torch.allclose(coll.weights[0][5], -0.1 * g[1] / 1.0, atol=1e-6)
+
+
+def test_padded_cpu_ops_and_unique():
+    op = CpuSparseEmbeddingOperator("float32")
+    emb = torch.arange(12.0).reshape(4, 3)
+    inv = torch.tensor([0, 4, 2, 1], dtype=torch.int32)
+    out = op.gather(emb, inv, 2, 3, 4)
+    assert torch.equal(out[0, 1], torch.zeros(3)) and torch.equal(out[1, 0], emb[2])
+    pooled = op.gather_pooled(emb, inv, 2, 3, (1, 2), 4)
+    assert torch.equal(pooled[0, 0], emb[0]) and torch.equal(pooled[1, 0], emb[2] + emb[1])
+    sc = op.scatter_pooled(4, 3, inv, 4, torch.ones(2, 1, 3), (1, 2))
+    assert torch.equal(sc.sum(1), torch.tensor([3.0, 3.0, 3.0, 0.0]))
+    keys = torch.tensor([5, 3, 5, -1, 3, 9])
+    u, i, f = unique_first_occurrence(keys)
+    ru, ri, rf = unique_first_occurrence_reference(keys)
+    assert torch.equal(u, ru) and torch.equal(i, ri) and torch.equal(f, rf)
+    assert u.tolist() == [5, 3, -1, 9]
+
+
+def test_sparse_precision_rescue():
+    g = torch.randn(4, 8).to(torch.bfloat16)
+    out = prepare_sparse_native_gradient(g, transport_dtype="bfloat16", native_dtype="float32")
+    assert out.dtype == torch.float32
+    with pytest.raises(TypeError):
+        prepare_sparse_native_gradient(g.float(), transport_dtype="bfloat16", native_dtype="float32")
+    with pytest.raises(FloatingPointError):
+        require_finite_sparse_values(torch.tensor([float("nan")]), "float32", boundary="t")
