@@ -195,6 +195,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.heavy_acc = P<float>(get<uintptr_t>(d, "heavy_acc"));
     p.max_heavy = get<int>(d, "max_heavy");
     p.light_max = get_or<int>(d, "light_max", 64);
+    p.dirty = P<uint8_t>(get_or<uintptr_t>(d, "dirty", 0));
     p.max_occ = get<int64_t>(d, "max_occ");
     p.opt = parse_sparse_opt(get<py::dict>(d, "opt"));
     p.flags_local = P<uint32_t>(get_or<uintptr_t>(d, "flags_local", 0));

@@ -623,7 +623,10 @@ __global__ void __launch_bounds__(kEmbThreads, 4) emb_apply_light_kernel(EmbBwdP
       }
     }
     apply_update<TW, NV>(o, w, eoff, row, mine, act, d.ncols, acc, wv, c, G, leader);
-    if (mine && gl == 0) p.row_count[row] = 0;
+    if (mine && gl == 0) {
+      p.row_count[row] = 0;
+      if (p.dirty != nullptr) p.dirty[row] = 1;
+    }
   }
 }
 
@@ -786,7 +789,10 @@ __global__ void __launch_bounds__(kEmbThreads) emb_heavy_apply_kernel(EmbBwdPara
       wv[v] = act ? load4<TW>(wp + 4 * v) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     apply_update<TW, NV>(o, wp, eoff, row, true, act, d.ncols, acc, wv, p.cnt_u[u], 32, 0);
-    if (lane == 0) p.row_count[row] = 0;
+    if (lane == 0) {
+      p.row_count[row] = 0;
+      if (p.dirty != nullptr) p.dirty[row] = 1;
+    }
   }
 }
 

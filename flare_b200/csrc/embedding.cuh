@@ -115,6 +115,7 @@ struct EmbBwdParams {
   float* heavy_acc; // [max_heavy][32*4*NV] fp32 accumulators (kept zero between steps)
   int max_heavy;
   int light_max;
+  uint8_t* dirty;   // per-row dirty flags for incremental checkpoints (nullable)
   int64_t max_occ;  // capacity of the per-unique arrays
   SparseOptParams opt;
   uint32_t* flags_local;

@@ -156,6 +156,8 @@ class ShardedEmbeddingBagCollection:
         # ---- per-row dedup scratch (returns to zero after every backward) ----
         self.row_count = torch.zeros(max(rbase, 4), dtype=torch.int32, device=dev)
         self.row2u = torch.zeros(max(rbase, 4), dtype=torch.int32, device=dev)
+        # rows updated since the last checkpoint (incremental sparse saves)
+        self.dirty = torch.zeros(max(rbase, 4), dtype=torch.uint8, device=dev)
 
         # ---- staging ----
         ns = max(len(self.shards), 1)
@@ -290,7 +292,7 @@ class ShardedEmbeddingBagCollection:
             num_unique=self.num_unique.data_ptr(), seg_start=self.seg_start.data_ptr(),
             block_sums=self.block_sums.data_ptr(), occ=self.occ.data_ptr(), heavy=self.heavy.data_ptr(),
             heavy_start=self.heavy_start.data_ptr(), hcnt=self.hcnt.data_ptr(), heavy_acc=self.heavy_acc.data_ptr(), max_heavy=self.max_heavy,
-            light_max=self.light_max, max_occ=self.max_occ, opt=op,
+            light_max=self.light_max, max_occ=self.max_occ, opt=op, dirty=self.dirty.data_ptr(),
             flags_local=self.flags.local_ptr, peer_flags=self.flags.peer_ptrs.data_ptr(),
             flag_in=self.flags.slots(FLAG_BWD_IN), epoch_ctr=self.flags.epoch_ptr(FLAG_BWD_IN),
             block_counter=self.flags.block_counter_ptr(FLAG_BWD_IN), status=self.status.ptr,
@@ -317,6 +319,21 @@ class ShardedEmbeddingBagCollection:
             return None
         s = self.shards[i]
         return self.state_row[s.row_base:s.row_base + s.spec.num_embeddings]
+
+    def shard_fields(self, i: int) -> dict[str, torch.Tensor]:
+        """Device views of shard i: weight [rows, ncols] and optimizer state."""
+        s = self.shards[i]
+        rows, n = s.spec.num_embeddings, s.spec.num_embeddings * s.ncols
+        out = {"weight": self.shard_view(i)}
+        if self.state_row is not None:
+            out["state_row"] = self.state_row[s.row_base:s.row_base + rows]
+        if self.state_m is not None:
+            out["state_m"] = self.state_m[s.weight_off:s.weight_off + n].view(rows, s.ncols)
+        if self.state_v is not None:
+            out["state_v"] = self.state_v[s.weight_off:s.weight_off + n].view(rows, s.ncols)
+        if self.score is not None:
+            out["score"] = self.score[s.row_base:s.row_base + rows]
+        return out
 
     def local_state(self) -> dict:
         """Owned shards with optimizer state (host copies), keyed by (table, col_begin)."""
