@@ -12,6 +12,25 @@
 #include "sparse_ops.cuh"
 
 namespace flare {
+struct AucWork {
+  unsigned long long* keys_a;
+  unsigned long long* keys_b;
+  int* vals_a;
+  int* vals_b;
+  int* negs;
+  int* neg_prefix;
+  int* hist;
+  int* hist_scan;
+  int* block_sums;
+  double* credit;
+  unsigned long long* pos_cnt;
+  unsigned long long* neg_cnt;
+  double* out;
+};
+void auc_device(const float* scores, const float* labels, const int64_t* groups, int64_t n, double negative_factor,
+                const AucWork& w, cudaStream_t s);
+void radix_sort_pairs(unsigned long long* keys_a, int* vals_a, unsigned long long* keys_b, int* vals_b, int64_t n,
+                      int bits, int* hist, int* hist_scan, int* block_sums, cudaStream_t s);
 void* dev_malloc(size_t bytes);
 void dev_free(void* p);
 std::vector<char> ipc_get_handle(void* p);
@@ -334,6 +353,31 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   });
   m.def("exclusive_scan_int", [](uintptr_t in, int64_t n, uintptr_t out, uintptr_t block_sums) {
     flare::exclusive_scan_int(P<const int>(in), n, P<int>(out), P<int>(block_sums), cur_stream());
+  });
+
+  m.def("auc_device", [](uintptr_t scores, uintptr_t labels, uintptr_t groups, int64_t n, double negative_factor,
+                         const py::dict& w) {
+    flare::AucWork a{};
+    a.keys_a = P<unsigned long long>(get<uintptr_t>(w, "keys_a"));
+    a.keys_b = P<unsigned long long>(get<uintptr_t>(w, "keys_b"));
+    a.vals_a = P<int>(get<uintptr_t>(w, "vals_a"));
+    a.vals_b = P<int>(get<uintptr_t>(w, "vals_b"));
+    a.negs = P<int>(get<uintptr_t>(w, "negs"));
+    a.neg_prefix = P<int>(get<uintptr_t>(w, "neg_prefix"));
+    a.hist = P<int>(get<uintptr_t>(w, "hist"));
+    a.hist_scan = P<int>(get<uintptr_t>(w, "hist_scan"));
+    a.block_sums = P<int>(get<uintptr_t>(w, "block_sums"));
+    a.credit = P<double>(get_or<uintptr_t>(w, "credit", 0));
+    a.pos_cnt = P<unsigned long long>(get_or<uintptr_t>(w, "pos_cnt", 0));
+    a.neg_cnt = P<unsigned long long>(get_or<uintptr_t>(w, "neg_cnt", 0));
+    a.out = P<double>(get<uintptr_t>(w, "out"));
+    flare::auc_device(P<const float>(scores), P<const float>(labels), P<const int64_t>(groups), n, negative_factor, a,
+                      cur_stream());
+  });
+  m.def("radix_sort_pairs", [](uintptr_t ka, uintptr_t va, uintptr_t kb, uintptr_t vb, int64_t n, int bits,
+                               uintptr_t hist, uintptr_t hist_scan, uintptr_t block_sums) {
+    flare::radix_sort_pairs(P<unsigned long long>(ka), P<int>(va), P<unsigned long long>(kb), P<int>(vb), n, bits,
+                            P<int>(hist), P<int>(hist_scan), P<int>(block_sums), cur_stream());
   });
 
   // ---- symmetric memory plumbing ----

@@ -1,0 +1,141 @@
+"""Windowed training metrics aggregated on the device, plus sinks.
+
+``TrainMetricsWindow`` keeps the sampled predictions and labels of a window
+(default 100 steps, reference: recipes/recsys/ranking/metrics/
+train_metrics.py:127-326) in device buffers, and at the end of the window
+computes exact AUC / GAUC (on the GPU when the data is there), calibration,
+mean loss and throughput (valid samples / window wall time, reference:
+src/flare/training/components/metrics/aggregation/sliding_window.py:8-23).
+Metric names follow ``train/<metric>_<target>`` (reference:
+recipes/recsys/ranking/metrics/sink.py:7-29).
+"""
+from __future__ import annotations
+
+import json
+import math
+import time
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Protocol
+
+import torch
+
+from .ranking import auc, calibration, gauc
+
+
+@dataclass
+class MetricWindow:
+    start_time: float = field(default_factory=time.perf_counter)
+    trained_sample_count: int = 0
+    steps: int = 0
+
+    def add(self, samples: int) -> None:
+        self.trained_sample_count += int(samples)
+        self.steps += 1
+
+    def throughput_samples(self) -> float:
+        dt = time.perf_counter() - self.start_time
+        return self.trained_sample_count / dt if dt > 0 else 0.0
+
+
+class MetricSink(Protocol):
+    def write(self, step: int, metrics: dict[str, float]) -> None: ...
+
+
+class ConsoleSink:
+    def __init__(self, prefix: str = "[TrainMetrics]"):
+        self.prefix = prefix
+
+    def write(self, step: int, metrics: dict[str, float]) -> None:
+        body = " ".join(f"{k}={v:.6g}" for k, v in sorted(metrics.items()))
+        print(f"{self.prefix} step={step} {body}", flush=True)
+
+
+class JsonlSink:
+    def __init__(self, path: str | Path):
+        self.path = Path(path)
+        self.path.parent.mkdir(parents=True, exist_ok=True)
+
+    def write(self, step: int, metrics: dict[str, float]) -> None:
+        with self.path.open("a") as f:
+            f.write(json.dumps({"step": step, **metrics}) + "\n")
+
+
+class TensorBoardSink:
+    """Writes scalars with tensorboardX or torch.utils.tensorboard when installed."""
+
+    def __init__(self, logdir: str | Path):
+        try:
+            from tensorboardX import SummaryWriter  # type: ignore
+        except ImportError:
+            try:
+                from torch.utils.tensorboard import SummaryWriter  # type: ignore
+            except ImportError as exc:  # pragma: no cover - depends on the image
+                raise RuntimeError("no TensorBoard writer installed; use JsonlSink") from exc
+        self.writer = SummaryWriter(str(logdir))
+
+    def write(self, step: int, metrics: dict[str, float]) -> None:
+        for k, v in metrics.items():
+            self.writer.add_scalar(k, v, step)
+        self.writer.flush()
+
+
+class TrainMetricsWindow:
+    def __init__(self, targets: tuple[str, ...] = ("ctr",), window_steps: int = 100, capacity: int = 1 << 22,
+                 device: torch.device | None = None, sinks: list | None = None, negative_factor: float = 0.0):
+        self.targets = targets
+        self.window_steps = window_steps
+        self.device = device or torch.device("cpu")
+        T = len(targets)
+        self.scores = torch.empty(capacity, T, dtype=torch.float32, device=self.device)
+        self.labels = torch.empty(capacity, T, dtype=torch.float32, device=self.device)
+        self.groups = torch.empty(capacity, dtype=torch.int64, device=self.device)
+        self.loss_sum = torch.zeros((), dtype=torch.float64, device=self.device)
+        self.n = 0
+        self.has_groups = False
+        self.window = MetricWindow()
+        self.sinks = sinks or []
+        self.negative_factor = negative_factor
+
+    def update(self, logits: torch.Tensor, labels: torch.Tensor, *, loss_sum: torch.Tensor | float | None = None,
+               groups: torch.Tensor | None = None, valid_count: int | None = None) -> dict | None:
+        B = logits.shape[0] if valid_count is None else valid_count
+        k = min(B, self.scores.shape[0] - self.n)
+        if k > 0:
+            self.scores[self.n:self.n + k] = torch.sigmoid(logits[:k].float()).reshape(k, -1)
+            self.labels[self.n:self.n + k] = labels[:k].float().reshape(k, -1)
+            if groups is not None:
+                self.groups[self.n:self.n + k] = groups[:k].to(torch.int64)
+                self.has_groups = True
+            self.n += k
+        if loss_sum is not None:
+            self.loss_sum += loss_sum if not torch.is_tensor(loss_sum) else loss_sum.to(self.loss_sum.device).double().reshape(())
+        self.window.add(B)
+        if self.window.steps >= self.window_steps:
+            return self.flush()
+        return None
+
+    def flush(self) -> dict:
+        out: dict[str, float] = {}
+        n = self.n
+        if n:
+            for t, name in enumerate(self.targets):
+                s, y = self.scores[:n, t], self.labels[:n, t]
+                out[f"train/auc_{name}"] = auc(s, y)
+                out[f"train/calibration_{name}"] = calibration(s, y)
+                if self.has_groups:
+                    out[f"train/gauc_{name}"] = gauc(s, y, self.groups[:n], self.negative_factor)
+        samples = max(self.window.trained_sample_count, 1)
+        out["train/loss"] = float(self.loss_sum) / samples
+        out["train/throughput_samples"] = self.window.throughput_samples()
+        step = self.window.steps
+        for sink in self.sinks:
+            sink.write(step, {k: v for k, v in out.items() if not (isinstance(v, float) and math.isnan(v))})
+        self.n = 0
+        self.has_groups = False
+        self.loss_sum.zero_()
+        self.window = MetricWindow()
+        return out
+
+
+__all__ = ["ConsoleSink", "JsonlSink", "MetricSink", "MetricWindow", "TensorBoardSink", "TrainMetricsWindow"]
