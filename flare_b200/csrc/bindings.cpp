@@ -31,6 +31,7 @@ void auc_device(const float* scores, const float* labels, const int64_t* groups,
                 const AucWork& w, cudaStream_t s);
 void radix_sort_pairs(unsigned long long* keys_a, int* vals_a, unsigned long long* keys_b, int* vals_b, int64_t n,
                       int bits, int* hist, int* hist_scan, int* block_sums, cudaStream_t s);
+void wait_flag_probe(const uint32_t* flag, uint32_t target, uint64_t timeout_ns, int* status, cudaStream_t s);
 void* dev_malloc(size_t bytes);
 void dev_free(void* p);
 std::vector<char> ipc_get_handle(void* p);
@@ -381,6 +382,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   });
 
   // ---- symmetric memory plumbing ----
+  m.def("wait_flag_probe", [](uintptr_t flag, uint32_t target, uint64_t timeout_ns, uintptr_t status) {
+    flare::wait_flag_probe(P<const uint32_t>(flag), target, timeout_ns, P<int>(status), cur_stream());
+  });
   m.def("dev_malloc", [](size_t bytes) { return reinterpret_cast<uintptr_t>(flare::dev_malloc(bytes)); });
   m.def("dev_free", [](uintptr_t p) { flare::dev_free(P<void>(p)); });
   m.def("ipc_get_handle", [](uintptr_t p) {

@@ -26,6 +26,17 @@ void increment_counter(int* p, cudaStream_t s) {
   count_launch();
 }
 
+// One thread waits (bounded) for *flag >= target; used to exercise the
+// timeout path of cross-GPU waits without involving another GPU.
+__global__ void wait_flag_probe_kernel(const uint32_t* flag, uint32_t target, uint64_t timeout_ns, int* status) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) wait_flag_geq(flag, target, timeout_ns, status, 0);
+}
+void wait_flag_probe(const uint32_t* flag, uint32_t target, uint64_t timeout_ns, int* status, cudaStream_t s) {
+  wait_flag_probe_kernel<<<1, 32, 0, s>>>(flag, target, timeout_ns, status);
+  FLARE_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
 void* dev_malloc(size_t bytes) {
   void* p = nullptr;
   FLARE_CUDA_CHECK(cudaMalloc(&p, bytes));
