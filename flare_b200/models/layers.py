@@ -1,0 +1,328 @@
+"""Dense layer library (PyTorch modules).
+
+Same constructor contracts and semantics as the reference's layer library
+(src/flare/jax/layers/__init__.py:3-21): ``MLP``; ``CategoricalEmbedding``
+(side-information tables grouped by dim, sum/mean pooling with id 0 as null,
+fp32 tables); the multitask gates ``PLE`` / ``CGC`` / ``UPLE`` / ``UCGC``;
+``TokenMix``; ``BatchedExpertMoE`` (dense or top-k soft gating, SwiGLU
+experts, RMS-normalised residual); ``NamedTokens``; fp32 numerics helpers.
+
+``TcLinear`` is a linear layer whose forward and backward GEMMs run on the
+hand-written tcgen05 kernel when the input is a bf16 CUDA tensor (weight
+gradients accumulate in fp32, as ``fp32_weight_gradient_dot_general`` does in
+the reference); otherwise it is a plain fp32 ``nn.Linear``.
+"""
+from __future__ import annotations
+
+import math
+from collections.abc import Sequence
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from ..ops.gemm import gemm
+
+
+# ---------------------------------------------------------------- numerics
+def fp32_softmax(x: torch.Tensor, dim: int = -1) -> torch.Tensor:
+    return torch.softmax(x.float(), dim=dim).to(x.dtype)
+
+
+def fp32_mean(x: torch.Tensor, dim=None, keepdim: bool = False) -> torch.Tensor:
+    out = x.float().mean() if dim is None else x.float().mean(dim=dim, keepdim=keepdim)
+    return out.to(x.dtype)
+
+
+def fp32_sum(x: torch.Tensor, dim=None, keepdim: bool = False) -> torch.Tensor:
+    out = x.float().sum() if dim is None else x.float().sum(dim=dim, keepdim=keepdim)
+    return out.to(x.dtype)
+
+
+def fp32_rms_normalize(x: torch.Tensor, dim: int = -1, eps: float = 1e-5) -> torch.Tensor:
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(dim=dim, keepdim=True) + eps)).to(x.dtype)
+
+
+# ----------------------------------------------------------- tcgen05 linear
+class _TcLinearFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, b):
+        x2 = x.reshape(-1, x.shape[-1]).contiguous()
+        wb = w.to(torch.bfloat16).contiguous()
+        bb = b.to(torch.bfloat16) if b is not None else None
+        y = gemm(x2, wb, bias=bb)
+        ctx.save_for_backward(x2, wb)
+        ctx.has_bias = b is not None
+        ctx.shape = x.shape
+        return y.reshape(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, gy):
+        x2, wb = ctx.saved_tensors
+        g2 = gy.reshape(-1, gy.shape[-1]).to(torch.bfloat16).contiguous()
+        dx = gemm(g2, wb, b_t=True).reshape(ctx.shape)
+        dw = torch.zeros(wb.shape, dtype=torch.float32, device=wb.device)
+        gemm(g2, x2, a_t=True, b_t=True, out=dw, accumulate=True)
+        db = g2.float().sum(0) if ctx.has_bias else None
+        return dx, dw, db
+
+
+class TcLinear(nn.Linear):
+    """nn.Linear that uses the tcgen05 GEMM for bf16 CUDA inputs (dims multiple of 8)."""
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.is_cuda and x.dtype == torch.bfloat16 and self.in_features % 8 == 0 and self.out_features % 8 == 0:
+            return _TcLinearFn.apply(x, self.weight, self.bias)
+        return F.linear(x, self.weight.to(x.dtype), None if self.bias is None else self.bias.to(x.dtype))
+
+
+_ACTS = {"relu": F.relu, "gelu": F.gelu, "sigmoid": torch.sigmoid, "tanh": torch.tanh,
+         "softmax": lambda x: fp32_softmax(x, -1)}
+
+
+def get_activation(name: str | None):
+    if name is None or name.lower() == "none":
+        return None
+    try:
+        return _ACTS[name.lower()]
+    except KeyError as exc:
+        raise ValueError(f"unsupported activation: {name!r}") from exc
+
+
+class MLP(nn.Module):
+    def __init__(self, in_features: int, dims: Sequence[int], activate: str = "relu",
+                 last_layer_use_activate: bool = True):
+        super().__init__()
+        self.layers = nn.ModuleList()
+        for d in dims:
+            self.layers.append(TcLinear(in_features, d))
+            in_features = d
+        self.dims = list(dims)
+        self.activate = activate
+        self.last_layer_use_activate = last_layer_use_activate
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        act = get_activation(self.activate)
+        for i, layer in enumerate(self.layers):
+            x = layer(x)
+            if act is not None and (i < len(self.layers) - 1 or self.last_layer_use_activate):
+                x = act(x)
+        return x
+
+
+# ------------------------------------------------------- categorical embedding
+class CategoricalEmbedding(nn.Module):
+    """Dense side-information tables grouped by dim; id 0 is null (side-info +1 shift)."""
+
+    def __init__(self, cate_feature_metas: dict[str, tuple[int, int]], side_info_layout: dict[str, tuple[int, int]],
+                 pooling: str = "sum"):
+        super().__init__()
+        if pooling not in ("sum", "mean"):
+            raise ValueError(f"Unsupported pooling method: {pooling}")
+        self.pooling = pooling
+        totals: dict[int, int] = {}
+        self.vocab_offsets: dict[str, int] = {}
+        groups: dict[tuple[int, int], list[str]] = {}
+        for k, (vocab, dim) in cate_feature_metas.items():
+            if k not in side_info_layout:
+                raise ValueError(f"Feature {k!r} not found in side_info_layout")
+            self.vocab_offsets[k] = totals.get(dim, 0)
+            totals[dim] = totals.get(dim, 0) + vocab + 2
+            groups.setdefault((dim, side_info_layout[k][1]), []).append(k)
+        self.tables = nn.ParameterDict({str(d): nn.Parameter(torch.randn(n, d)) for d, n in totals.items()})
+        self.meta = []
+        for (dim, flen), keys in groups.items():
+            idx = torch.tensor([[side_info_layout[k][0] + i for i in range(flen)] for k in keys])
+            off = torch.tensor([self.vocab_offsets[k] for k in keys])
+            self.register_buffer(f"idx_{dim}_{flen}", idx, persistent=False)
+            self.register_buffer(f"off_{dim}_{flen}", off, persistent=False)
+            self.meta.append((dim, flen, keys))
+        self.feature_order = {d: [k for (dd, _, ks) in self.meta if dd == d for k in ks] for d in totals}
+
+    def forward(self, side_info: torch.Tensor) -> dict[int, torch.Tensor]:
+        out: dict[int, list[torch.Tensor]] = {}
+        for dim, flen, _ in self.meta:
+            idx = getattr(self, f"idx_{dim}_{flen}")
+            off = getattr(self, f"off_{dim}_{flen}")
+            ids = side_info[:, idx]                          # [B, K, flen]
+            emb = self.tables[str(dim)].float()[ids + off.view(1, -1, 1)]
+            if flen > 1:
+                mask = (ids != 0).unsqueeze(-1)
+                pooled = (emb * mask).sum(2)
+                if self.pooling == "mean":
+                    pooled = pooled / mask.sum(2).clamp_min(1)
+            else:
+                pooled = emb[:, :, 0]
+            out.setdefault(dim, []).append(pooled)
+        return {d: torch.cat(v, 1) for d, v in out.items()}
+
+
+# ------------------------------------------------------------- multitask
+class _GatedExperts(nn.Module):
+    def __init__(self, base_dim, gate_in_dim, num_experts, dims, n_tasks, activate, gate_sizes):
+        super().__init__()
+        self.num_experts, self.n_tasks, self.out_dim = num_experts, n_tasks, dims[-1]
+        self.experts = nn.ModuleList(MLP(base_dim, dims, activate) for _ in range(n_tasks * num_experts))
+        self.gate_layers = nn.ModuleList(TcLinear(gate_in_dim, g) for g in gate_sizes)
+
+    def _expert_outputs(self, base_layers):
+        outs, i = [], 0
+        for t in range(len(base_layers)):
+            outs.append([self.experts[i + e](base_layers[t]) for e in range(self.num_experts)])
+            i += self.num_experts
+        return outs
+
+    @staticmethod
+    def _mix(layers, gate_logits):
+        stacked = torch.stack(layers, -1)                     # [B, D, E]
+        gate = fp32_softmax(gate_logits, -1).unsqueeze(1)     # [B, 1, E]
+        return fp32_sum(stacked * gate, dim=-1)
+
+
+class PLE(_GatedExperts):
+    """Progressive layered extraction: N task inputs + 1 shared -> N+1 outputs."""
+
+    def __init__(self, base_dim, gate_in_dim, num_experts, dims, n_tasks, activate="relu"):
+        shared = n_tasks - 1
+        super().__init__(base_dim, gate_in_dim, num_experts, dims, n_tasks, activate,
+                         [num_experts * 2 if i != shared else num_experts * n_tasks for i in range(n_tasks)])
+
+    def forward(self, base_layers, gate_layer):
+        eo = self._expert_outputs(base_layers)
+        shared = len(base_layers) - 1
+        out = []
+        for i in range(len(base_layers)):
+            layers = eo[i] + eo[shared] if i != shared else [e for row in eo for e in row]
+            out.append(self._mix(layers, self.gate_layers[i](gate_layer)))
+        return out
+
+
+class CGC(_GatedExperts):
+    """Customized gate control: N task inputs + 1 shared -> N outputs."""
+
+    def __init__(self, base_dim, gate_in_dim, num_experts, dims, n_tasks, activate="relu"):
+        super().__init__(base_dim, gate_in_dim, num_experts, dims, n_tasks, activate,
+                         [num_experts * 2] * (n_tasks - 1))
+
+    def forward(self, base_layers, gate_layer):
+        eo = self._expert_outputs(base_layers)
+        shared = len(base_layers) - 1
+        return [self._mix(eo[i] + eo[shared], self.gate_layers[i](gate_layer)) for i in range(len(base_layers) - 1)]
+
+
+class UPLE(PLE):
+    """PLE with a separate gate input per task."""
+
+    def forward(self, base_layers, gate_layers_in):
+        eo = self._expert_outputs(base_layers)
+        shared = len(base_layers) - 1
+        out = []
+        for i in range(len(base_layers)):
+            layers = eo[i] + eo[shared] if i != shared else [e for row in eo for e in row]
+            out.append(self._mix(layers, self.gate_layers[i](gate_layers_in[i])))
+        return out
+
+
+class UCGC(CGC):
+    """CGC with a separate gate input per task."""
+
+    def forward(self, base_layers, gate_layers_in):
+        eo = self._expert_outputs(base_layers)
+        shared = len(base_layers) - 1
+        return [self._mix(eo[i] + eo[shared], self.gate_layers[i](gate_layers_in[i]))
+                for i in range(len(base_layers) - 1)]
+
+
+# -------------------------------------------------------------- token mix
+class TokenMix(nn.Module):
+    """Slice-and-concat token mixing, LayerNorm, GELU FFN, LayerNorm, mean pooling."""
+
+    def __init__(self, token_num: int, token_dim: int, layer_size: int, hidden_dims: Sequence[int] = ()):
+        super().__init__()
+        if token_dim % token_num:
+            raise ValueError("token_dim must be divisible by token_num")
+        self.token_num, self.token_dim, self.layer_size = token_num, token_dim, layer_size
+        self.slice_dim = token_dim // token_num
+        n = layer_size * token_num
+        self.mix_lns = nn.ModuleList(nn.LayerNorm(token_dim, eps=1e-3) for _ in range(n))
+        self.mix_ffns = nn.ModuleList(MLP(token_dim, list(hidden_dims) + [token_dim], activate="gelu")
+                                      for _ in range(n))
+        self.ffn_lns = nn.ModuleList(nn.LayerNorm(token_dim, eps=1e-3) for _ in range(n))
+
+    def forward(self, tokens: torch.Tensor) -> torch.Tensor:
+        out = [tokens[:, j] for j in range(self.token_num)]
+        idx = 0
+        for _ in range(self.layer_size):
+            mixed = [torch.cat([t[..., j * self.slice_dim:(j + 1) * self.slice_dim] for t in out], -1)
+                     for j in range(self.token_num)]
+            new = []
+            for j in range(self.token_num):
+                a = self.mix_lns[idx](out[j] + mixed[j])
+                new.append(self.ffn_lns[idx](a + self.mix_ffns[idx](a)))
+                idx += 1
+            out = new
+        return fp32_mean(torch.stack(out, 1), dim=1)
+
+
+class BatchedExpertMoE(nn.Module):
+    """Per-slot batched SwiGLU experts with dense or top-k softmax gating.
+
+    Input ``x`` is [slots, batch, in_dim]; every slot has its own experts.
+    """
+
+    def __init__(self, batch_dim: int, in_dim: int, scale_size: int, num_experts: int, sparse: bool, top_k: int,
+                 residual_norm: bool = True):
+        super().__init__()
+        self.batch_dim, self.in_dim, self.num_experts = batch_dim, in_dim, num_experts
+        self.sparse, self.top_k, self.residual_norm = sparse, min(top_k, num_experts), residual_norm
+        h = in_dim * scale_size
+        lecun = lambda *s: torch.randn(*s) / math.sqrt(s[-2])  # noqa: E731
+        if num_experts > 1:
+            self.w_gate = nn.Parameter(lecun(batch_dim, in_dim, num_experts))
+            self.b_gate = nn.Parameter(torch.zeros(batch_dim, num_experts))
+        self.w_up = nn.Parameter(lecun(batch_dim, num_experts, in_dim, 2 * h))
+        self.b_up = nn.Parameter(torch.zeros(batch_dim, num_experts, 2 * h))
+        self.w_down = nn.Parameter(lecun(batch_dim, num_experts, h, in_dim))
+        self.b_down = nn.Parameter(torch.zeros(batch_dim, num_experts, in_dim))
+        self.norm_scale = nn.Parameter(torch.ones(batch_dim, in_dim))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        up_gate = torch.einsum("dbi,deih->dbeh", x, self.w_up) + self.b_up.unsqueeze(1)
+        up, gate = up_gate.chunk(2, -1)
+        hidden = F.silu(gate) * up
+        outs = torch.einsum("dbeh,dehi->dbei", hidden, self.w_down) + self.b_down.unsqueeze(1)
+        if self.num_experts == 1:
+            moe = outs[:, :, 0]
+        else:
+            logits = torch.einsum("dbi,dio->dbo", x, self.w_gate) + self.b_gate.unsqueeze(1)
+            if self.sparse:
+                val, idx = logits.topk(self.top_k, -1)
+                w = fp32_softmax(val, -1)
+                picked = torch.gather(outs, 2, idx.unsqueeze(-1).expand(*idx.shape, self.in_dim))
+                moe = (picked * w.unsqueeze(-1)).sum(2)
+            else:
+                moe = (outs * fp32_softmax(logits, -1).unsqueeze(-1)).sum(2)
+        if self.residual_norm:
+            return fp32_rms_normalize(x + moe, -1) * self.norm_scale.unsqueeze(1)
+        return moe
+
+
+class NamedTokens:
+    """Ordered name -> token index registry for token-mixing models."""
+
+    def __init__(self, names: Sequence[str]):
+        if len(set(names)) != len(names):
+            raise ValueError("token names must be unique")
+        self.names = tuple(names)
+        self.index = {n: i for i, n in enumerate(self.names)}
+
+    def __len__(self) -> int:
+        return len(self.names)
+
+    def select(self, tokens: torch.Tensor, names: Sequence[str]) -> torch.Tensor:
+        return tokens[:, [self.index[n] for n in names]]
+
+
+__all__ = ["BatchedExpertMoE", "CGC", "CategoricalEmbedding", "MLP", "NamedTokens", "PLE", "TcLinear", "TokenMix",
+           "UCGC", "UPLE", "fp32_mean", "fp32_rms_normalize", "fp32_softmax", "fp32_sum", "get_activation"]
