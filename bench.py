@@ -67,15 +67,18 @@ def reference_arm(args):
     ref_dir = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
     sys.path.insert(0, ref_dir)
     missing = []
-    for mod in ("flare", "jax", "flax", "fluxway", "sparse_embedding", "ray"):
+    # the reference's training path (recipes/recsys/ranking) needs all of these
+    for mod in ("flare", "flare.kernels", "jax", "flax", "fluxway", "sparse_embedding", "ray", "cupy"):
         try:
             __import__(mod)
         except Exception:  # noqa: BLE001
             missing.append(mod)
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
     if missing:
-        if int(os.environ.get("RANK", "0")) == 0:
-            emit({"impl": "reference", "unavailable": "reference training stack not importable offline: missing "
-                  + ", ".join(missing) + " (fluxway and sparse_embedding are not vendored; jax/ray not installed)"})
+        emit({"impl": "reference", "unavailable": "reference installed offline with --no-deps into baseline/_ref "
+              "(its deps are not in the wheelhouse), but its training stack cannot import: missing "
+              + ", ".join(missing) + " (fluxway and sparse_embedding are not vendored; jax/ray/cupy not installed)"})
         return
     emit({"impl": "reference", "unavailable": "reference imports but its Ray/Fluxway cluster launch is not "
                                               "supported offline in this harness"})
@@ -176,7 +179,7 @@ def main():
         n_e2e = args.e2e_steps or args.steps
         for i in range(2):
             trainer.train_step_async(host[i % len(host)])
-        trainer.flush()
+        first = trainer.flush()
         barrier()
         torch.cuda.synchronize()
         w0 = time.perf_counter()
@@ -195,7 +198,8 @@ def main():
         e2e = {"value": B * world / (e2e_ms / 1000.0), "unit": "samples/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": bi, "d2h_bytes_per_step": 4,
                "api": "flare_b200.training.trainer.DLRMTrainer.train_step_async",
-               "last_loss": last.loss if last else None}
+               "first_loss": first.loss if first else None, "last_loss": last.loss if last else None,
+               "steps_trained_before_last_loss": trainer.steps}
     trainer.check()
 
     samples_s = B * world / (ms_max / 1000.0)
