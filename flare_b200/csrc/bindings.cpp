@@ -6,6 +6,7 @@
 #include <pybind11/stl.h>
 
 #include "common.cuh"
+#include "dcn.cuh"
 #include "dense.cuh"
 #include "embedding.cuh"
 #include "gemm.cuh"
@@ -144,6 +145,90 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       py::arg("N"), py::arg("K"), py::arg("C"), py::arg("ldc"), py::arg("c_dtype"), py::arg("accumulate"),
       py::arg("bias"), py::arg("act"), py::arg("alpha"), py::arg("mask"), py::arg("ldm"), py::arg("colsum"),
       py::arg("status"), py::arg("timeout_ns"), py::arg("bn") = 0);
+
+  m.def("gemm_dist", [](const py::dict& d) {
+    flare::DistGemmArgs a;
+    const py::dict g = get<py::dict>(d, "g");
+    a.g.A = P<const void>(get<uintptr_t>(g, "A"));
+    a.g.lda = get<int64_t>(g, "lda");
+    a.g.a_mn = get<bool>(g, "a_mn");
+    a.g.B = P<const void>(get<uintptr_t>(g, "B"));
+    a.g.ldb = get<int64_t>(g, "ldb");
+    a.g.b_mn = get<bool>(g, "b_mn");
+    a.g.M = get<int>(g, "M");
+    a.g.N = get<int>(g, "N");
+    a.g.K = get<int>(g, "K");
+    a.g.C = P<void>(get<uintptr_t>(g, "C"));
+    a.g.ldc = get<int64_t>(g, "ldc");
+    a.g.c_dtype = get<int>(g, "c_dtype");
+    a.g.accumulate = get_or<bool>(g, "accumulate", false);
+    a.g.bias = P<const __nv_bfloat16>(get_or<uintptr_t>(g, "bias", 0));
+    a.g.act = get_or<int>(g, "act", 0);
+    a.g.alpha = get_or<float>(g, "alpha", 1.f);
+    a.g.mask = P<const void>(get_or<uintptr_t>(g, "mask", 0));
+    a.g.ldm = get_or<int64_t>(g, "ldm", 0);
+    a.g.colsum = P<float>(get_or<uintptr_t>(g, "colsum", 0));
+    a.g.status = P<int>(get<uintptr_t>(g, "status"));
+    a.g.timeout_ns = get<uint64_t>(g, "timeout_ns");
+    a.tiles = P<const int>(get<uintptr_t>(d, "tiles"));
+    a.num_tiles = get<int>(d, "num_tiles");
+    a.chunks = P<const int>(get_or<uintptr_t>(d, "chunks", 0));
+    a.num_chunks = get_or<int>(d, "num_chunks", 0);
+    for (int op = 0; op < 2; ++op) {
+      const char* key = op ? "gb" : "ga";
+      if (!d.contains(key) || d[key].is_none()) continue;
+      const py::dict gd = d[key].cast<py::dict>();
+      flare::DistGather& x = op ? a.gb : a.ga;
+      x.enabled = 1;
+      x.nranks = get<int>(gd, "nranks");
+      x.my = get<int>(gd, "my");
+      const auto src = get<std::vector<uintptr_t>>(gd, "src");
+      if (static_cast<int>(src.size()) != x.nranks || x.nranks > 8) throw std::runtime_error("gather: bad src list");
+      for (int q = 0; q < x.nranks; ++q) x.src[q] = P<const void>(src[q]);
+      x.dst = P<void>(get<uintptr_t>(gd, "dst"));
+      x.ld = get<int64_t>(gd, "ld");
+      x.rows_per_rank = get<int64_t>(gd, "rows_per_rank");
+      x.row_elems = get<int64_t>(gd, "row_elems");
+      x.chunk_rows = get<int>(gd, "chunk_rows");
+      x.ready = P<uint32_t>(get<uintptr_t>(gd, "ready"));
+    }
+    if (d.contains("rs") && !d["rs"].is_none()) {
+      const py::dict rd = d["rs"].cast<py::dict>();
+      a.rs.enabled = 1;
+      a.rs.nranks = get<int>(rd, "nranks");
+      a.rs.my = get<int>(rd, "my");
+      a.rs.rows_per_rank = get<int>(rd, "rows_per_rank");
+      const auto recv = get<std::vector<uintptr_t>>(rd, "recv_peer");
+      const auto flags = get<std::vector<uintptr_t>>(rd, "flag_peer");
+      if (static_cast<int>(recv.size()) != a.rs.nranks || static_cast<int>(flags.size()) != a.rs.nranks ||
+          a.rs.nranks > 8)
+        throw std::runtime_error("reduce-scatter: bad peer lists");
+      for (int q = 0; q < a.rs.nranks; ++q) {
+        a.rs.recv_peer[q] = P<void>(recv[q]);
+        a.rs.flag_peer[q] = P<uint32_t>(flags[q]);
+      }
+      a.rs.recv_local = P<const void>(get<uintptr_t>(rd, "recv_local"));
+      a.rs.ld_recv = get<int64_t>(rd, "ld_recv");
+      a.rs.flag_local = P<const uint32_t>(get<uintptr_t>(rd, "flag_local"));
+    }
+    a.epi = get_or<int>(d, "epi", 0);
+    a.aux0 = P<const void>(get_or<uintptr_t>(d, "aux0", 0));
+    a.ld0 = get_or<int64_t>(d, "ld0", 0);
+    a.aux1 = P<const void>(get_or<uintptr_t>(d, "aux1", 0));
+    a.ld1 = get_or<int64_t>(d, "ld1", 0);
+    a.zout = P<void>(get_or<uintptr_t>(d, "zout", 0));
+    a.ldz = get_or<int64_t>(d, "ldz", 0);
+    a.world = get_or<int>(d, "world", 1);
+    a.rank = get_or<int>(d, "rank", 0);
+    a.bar_local = P<uint32_t>(get_or<uintptr_t>(d, "bar_local", 0));
+    if (d.contains("bar_peer")) {
+      const auto bp = get<std::vector<uintptr_t>>(d, "bar_peer");
+      if (static_cast<int>(bp.size()) > 8) throw std::runtime_error("barrier: too many ranks");
+      for (size_t s = 0; s < bp.size(); ++s) a.bar_peer[s] = P<uint32_t>(bp[s]);
+    }
+    a.ctl = P<uint32_t>(get<uintptr_t>(d, "ctl"));
+    flare::gemm_dist_tcgen05(a, cur_stream());
+  });
 
   m.def("emb_forward", [](const py::dict& d) {
     flare::EmbFwdParams p{};
@@ -296,6 +381,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.hi = get<int64_t>(d, "hi");
     p.peer_grad = P<float* const>(get<uintptr_t>(d, "peer_grad"));
     p.peer_param = P<void* const>(get<uintptr_t>(d, "peer_param"));
+    p.param_world = get_or<int>(d, "param_world", p.world);
     p.master_shard = P<float>(get<uintptr_t>(d, "master_shard"));
     p.m_shard = P<float>(get<uintptr_t>(d, "m_shard"));
     p.v_shard = P<float>(get<uintptr_t>(d, "v_shard"));
@@ -310,6 +396,45 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.status = P<int>(get_or<uintptr_t>(d, "status", 0));
     p.timeout_ns = get_or<uint64_t>(d, "timeout_ns", 2000000000ull);
     flare::adam_dp_fused(p, cur_stream());
+  });
+
+  m.def("dcn_concat_x0", [](uintptr_t pooled, int64_t ldp, uintptr_t dense, int nd, int64_t B, int E, uintptr_t x0,
+                            int64_t ld0) {
+    flare::dcn_concat_x0(P<const __nv_bfloat16>(pooled), ldp, P<const float>(dense), nd, B, E, P<__nv_bfloat16>(x0),
+                         ld0, cur_stream());
+  });
+  m.def("dcn_head", [](const py::dict& d) {
+    flare::DcnHeadParams p{};
+    p.h = P<const __nv_bfloat16>(get<uintptr_t>(d, "h"));
+    p.ldh = get<int64_t>(d, "ldh");
+    p.H = get<int>(d, "H");
+    p.relu_from = get<int>(d, "relu_from");
+    p.w = P<const __nv_bfloat16>(get<uintptr_t>(d, "w"));
+    p.bias = P<const __nv_bfloat16>(get<uintptr_t>(d, "bias"));
+    p.labels = P<const float>(get<uintptr_t>(d, "labels"));
+    p.B = get<int64_t>(d, "B");
+    p.valid_count = get_or<int>(d, "valid_count", -1);
+    p.grad_scale = get<float>(d, "grad_scale");
+    p.logits = P<float>(get<uintptr_t>(d, "logits"));
+    p.dl = P<float>(get<uintptr_t>(d, "dl"));
+    p.dh = P<__nv_bfloat16>(get<uintptr_t>(d, "dh"));
+    p.lddh = get<int64_t>(d, "lddh");
+    p.loss_sum = P<float>(get<uintptr_t>(d, "loss_sum"));
+    p.db = P<float>(get<uintptr_t>(d, "db"));
+    flare::dcn_head(p, cur_stream());
+  });
+  m.def("dcn_scaled_colsum", [](uintptr_t x, int64_t ldx, uintptr_t scale, int64_t rows, int cols, uintptr_t out) {
+    flare::dcn_scaled_colsum(P<const __nv_bfloat16>(x), ldx, P<const float>(scale), rows, cols, P<float>(out),
+                             cur_stream());
+  });
+  m.def("dcn_cross_bwd_elem", [](uintptr_t g, uintptr_t x0, uintptr_t z, int64_t ld, int64_t rows, int cols,
+                                 uintptr_t dz, uintptr_t acc, int64_t ld_acc, int accumulate, uintptr_t db) {
+    flare::dcn_cross_bwd_elem(P<const __nv_bfloat16>(g), P<const __nv_bfloat16>(x0), P<const __nv_bfloat16>(z), ld,
+                              rows, cols, P<__nv_bfloat16>(dz), P<float>(acc), ld_acc, accumulate, P<float>(db),
+                              cur_stream());
+  });
+  m.def("dcn_finalize_grad", [](uintptr_t acc, int64_t ld_acc, int64_t rows, int cols, uintptr_t grad, int64_t ldg) {
+    flare::dcn_finalize_grad(P<const float>(acc), ld_acc, rows, cols, P<__nv_bfloat16>(grad), ldg, cur_stream());
   });
 
   m.def("colsum_bf16", [](uintptr_t x, int64_t rows, int cols, int64_t ldx, uintptr_t out) {

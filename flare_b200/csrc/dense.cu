@@ -380,7 +380,7 @@ __global__ void adam_dp_fused_kernel(AdamDpParams p) {
     reinterpret_cast<float4*>(p.master_shard)[li] = w;
     reinterpret_cast<float4*>(p.m_shard)[li] = m;
     reinterpret_cast<float4*>(p.v_shard)[li] = v;
-    for (int s = 0; s < p.world; ++s)
+    for (int s = 0; s < p.param_world; ++s)
       store4<__nv_bfloat16>(reinterpret_cast<__nv_bfloat16*>(p.peer_param[s]) + 4 * i, w);
   }
   __threadfence_system();

@@ -68,7 +68,8 @@ struct AdamDpParams {
   int world, rank;
   int64_t lo, hi;              // owned slice of the flat buffer
   float* const* peer_grad;     // [world] fp32 flat gradient buffers
-  void* const* peer_param;     // [world] bf16 flat compute copies
+  void* const* peer_param;     // [param_world] bf16 flat compute copies the update is written to
+  int param_world;             // world: replicate (all-gather by push); 1: only the local copy (FSDP)
   float* master_shard;         // fp32 [hi-lo]
   float* m_shard;
   float* v_shard;
