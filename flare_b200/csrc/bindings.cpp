@@ -427,9 +427,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     flare::dcn_scaled_colsum(P<const __nv_bfloat16>(x), ldx, P<const float>(scale), rows, cols, P<float>(out),
                              cur_stream());
   });
-  m.def("dcn_cross_bwd_elem", [](uintptr_t g, uintptr_t x0, uintptr_t z, int64_t ld, int64_t rows, int cols,
-                                 uintptr_t dz, uintptr_t acc, int64_t ld_acc, int accumulate, uintptr_t db) {
-    flare::dcn_cross_bwd_elem(P<const __nv_bfloat16>(g), P<const __nv_bfloat16>(x0), P<const __nv_bfloat16>(z), ld,
+  m.def("dcn_cross_bwd_elem", [](uintptr_t g, int64_t ldg, uintptr_t x0, uintptr_t z, int64_t ld, int64_t rows,
+                                 int cols, uintptr_t dz, uintptr_t acc, int64_t ld_acc, int accumulate, uintptr_t db) {
+    flare::dcn_cross_bwd_elem(P<const __nv_bfloat16>(g), ldg, P<const __nv_bfloat16>(x0), P<const __nv_bfloat16>(z), ld,
                               rows, cols, P<__nv_bfloat16>(dz), P<float>(acc), ld_acc, accumulate, P<float>(db),
                               cur_stream());
   });

@@ -155,8 +155,8 @@ __global__ void __launch_bounds__(kWarps * 32) scaled_colsum_kernel(const __nv_b
 }
 
 __global__ void __launch_bounds__(kWarps * 32) cross_bwd_elem_kernel(
-    const __nv_bfloat16* __restrict__ g, const __nv_bfloat16* __restrict__ x0, const __nv_bfloat16* __restrict__ z,
-    int64_t ld, int64_t rows, int cols, __nv_bfloat16* __restrict__ dz, float* __restrict__ acc_out, int64_t ld_acc,
+    const __nv_bfloat16* __restrict__ g, int64_t ldg, const __nv_bfloat16* __restrict__ x0,
+    const __nv_bfloat16* __restrict__ z, int64_t ld, int64_t rows, int cols, __nv_bfloat16* __restrict__ dz, float* __restrict__ acc_out, int64_t ld_acc,
     int accumulate, float* __restrict__ db) {
   __shared__ float part[kWarps][kColBlock];
   const int lane = lane_id(), warp = warp_id();
@@ -168,7 +168,7 @@ __global__ void __launch_bounds__(kWarps * 32) cross_bwd_elem_kernel(
     for (int64_t r = r0 + warp; r < r1; r += kWarps) {
       float gv[8], xv[8], zv[8], d[8];
       const int64_t o = r * ld + c0;
-      bf8_to_f(*reinterpret_cast<const uint4*>(g + o), gv);
+      bf8_to_f(*reinterpret_cast<const uint4*>(g + r * ldg + c0), gv);
       bf8_to_f(*reinterpret_cast<const uint4*>(x0 + o), xv);
       bf8_to_f(*reinterpret_cast<const uint4*>(z + o), zv);
 #pragma unroll
@@ -245,12 +245,13 @@ void dcn_scaled_colsum(const __nv_bfloat16* x, int64_t ldx, const float* scale, 
   count_launch();
 }
 
-void dcn_cross_bwd_elem(const __nv_bfloat16* g, const __nv_bfloat16* x0, const __nv_bfloat16* z, int64_t ld,
+void dcn_cross_bwd_elem(const __nv_bfloat16* g, int64_t ldg, const __nv_bfloat16* x0, const __nv_bfloat16* z, int64_t ld,
                         int64_t rows, int cols, __nv_bfloat16* dz, float* acc, int64_t ld_acc, int accumulate,
                         float* db, cudaStream_t s) {
-  FLARE_CHECK(cols % 8 == 0 && ld % 8 == 0 && ld_acc % 4 == 0, "columns and pitches must be multiples of 8");
+  FLARE_CHECK(cols % 8 == 0 && ld % 8 == 0 && ldg % 8 == 0 && ld_acc % 4 == 0,
+              "columns and pitches must be multiples of 8");
   dim3 grid(ceil_div(cols, kColBlock), ceil_div(rows, kRowsPerBlock));
-  cross_bwd_elem_kernel<<<grid, kWarps * 32, 0, s>>>(g, x0, z, ld, rows, cols, dz, acc, ld_acc, accumulate, db);
+  cross_bwd_elem_kernel<<<grid, kWarps * 32, 0, s>>>(g, ldg, x0, z, ld, rows, cols, dz, acc, ld_acc, accumulate, db);
   FLARE_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

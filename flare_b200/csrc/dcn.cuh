@@ -36,7 +36,7 @@ void dcn_scaled_colsum(const __nv_bfloat16* x, int64_t ldx, const float* scale, 
 
 // Cross-layer backward elementwise part for one layer:
 //   dz = g * x0 (bf16 out), acc (=|+=) g * z (fp32), db += colsum(dz)
-void dcn_cross_bwd_elem(const __nv_bfloat16* g, const __nv_bfloat16* x0, const __nv_bfloat16* z, int64_t ld,
+void dcn_cross_bwd_elem(const __nv_bfloat16* g, int64_t ldg, const __nv_bfloat16* x0, const __nv_bfloat16* z, int64_t ld,
                         int64_t rows, int cols, __nv_bfloat16* dz, float* acc, int64_t ld_acc, int accumulate,
                         float* db, cudaStream_t s);
 

@@ -95,6 +95,39 @@ class ShardedRows:
                 "row_elems": _round_up(self.cols, 8), "chunk_rows": self.chunk_rows,
                 "ready": self.ready.data_ptr()}
 
+    def column_view(self, col_offset: int, cols: int) -> "ShardedRowsView":
+        """The columns [col_offset, col_offset+cols) as a separately gatherable operand."""
+        return ShardedRowsView(self, col_offset, cols)
+
+
+class ShardedRowsView:
+    """A column range of a ``ShardedRows`` buffer with its own ready flags."""
+
+    def __init__(self, base: ShardedRows, col_offset: int, cols: int):
+        if col_offset % 8 or col_offset + cols > base.ld:
+            raise ValueError("column views start at a multiple of 8 elements and stay inside the row")
+        self.base, self.off, self.cols = base, int(col_offset), int(cols)
+        self.R, self.my, self.S, self.ld, self.group = base.R, base.my, base.S, base.ld, base.group
+        self.chunk_rows = base.chunk_rows
+        self.ready = torch.zeros_like(base.ready)
+
+    @property
+    def full(self) -> torch.Tensor:
+        return self.base.buf.local[:, self.off:self.off + self.cols]
+
+    @property
+    def local(self) -> torch.Tensor:
+        return self.base.buf.local[self.my * self.S:(self.my + 1) * self.S, self.off:self.off + self.cols]
+
+    def gather_spec(self) -> dict | None:
+        if self.R == 1:
+            return None
+        return {"nranks": self.R, "my": self.my, "src": [p + 2 * self.off for p in
+                                                         (self.base.buf.peer_ptrs[g] for g in self.group)],
+                "dst": self.base.buf.local.data_ptr() + 2 * self.off, "ld": self.ld, "rows_per_rank": self.S,
+                "row_elems": _round_up(self.cols, 8), "chunk_rows": self.chunk_rows,
+                "ready": self.ready.data_ptr()}
+
 
 class RowReduceScatter:
     """Receive slots ``[R][S][ld]`` (bf16) and per-tile-quarter flags for a row reduce-scatter."""
@@ -184,8 +217,8 @@ class DistGemm:
     out: torch.Tensor
     a_t: bool = False
     b_t: bool = False
-    ga: ShardedRows | None = None
-    gb: ShardedRows | None = None
+    ga: "ShardedRows | ShardedRowsView | None" = None
+    gb: "ShardedRows | ShardedRowsView | None" = None
     rs: RowReduceScatter | None = None
     bias: torch.Tensor | None = None
     relu: bool = False
@@ -244,4 +277,5 @@ class DistGemm:
         return 2 * self.M * self.N * self.K
 
 
-__all__ = ["DistGemm", "DistGemmContext", "RowReduceScatter", "ShardedRows", "chunk_order", "tile_order"]
+__all__ = ["DistGemm", "DistGemmContext", "RowReduceScatter", "ShardedRows", "ShardedRowsView", "chunk_order",
+           "tile_order"]

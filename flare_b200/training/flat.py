@@ -72,6 +72,7 @@ class ParamEntry:
     init: str = "zeros"
     init_scale: float = 0.0
     zero_cols_from: int | None = None  # columns >= this start (and stay) zero: input padding
+    zero_ranges: tuple[tuple[int, int], ...] = ()  # flat [lo, hi) ranges that start at zero (padding)
 
 
 @dataclass
@@ -82,14 +83,15 @@ class FlatParams:
     size: int = 0
 
     def register(self, name: str, shape, init: str = "zeros", init_scale: float = 0.0,
-                 zero_cols_from: int | None = None) -> ParamEntry:
+                 zero_cols_from: int | None = None, zero_ranges: tuple[tuple[int, int], ...] = ()) -> ParamEntry:
         if name in self.entries:
             raise ValueError(f"duplicate parameter {name}")
         numel = 1
         for s in shape:
             numel *= int(s)
         off = (self.size + ALIGN - 1) // ALIGN * ALIGN
-        e = ParamEntry(name, tuple(int(s) for s in shape), off, numel, init, init_scale, zero_cols_from)
+        e = ParamEntry(name, tuple(int(s) for s in shape), off, numel, init, init_scale, zero_cols_from,
+                       tuple(zero_ranges))
         self.entries[name] = e
         self.size = off + numel
         return e
@@ -158,6 +160,8 @@ class DenseState:
                 vals = vals.view(e.shape).clone()
                 vals[:, e.zero_cols_from:] = 0
                 vals = vals.reshape(-1)
+            for lo, hi in e.zero_ranges:
+                vals[lo:hi] = 0
             flat[e.offset:e.offset + e.numel] = vals
         return flat
 
