@@ -190,7 +190,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       x.rows_per_rank = get<int64_t>(gd, "rows_per_rank");
       x.row_elems = get<int64_t>(gd, "row_elems");
       x.chunk_rows = get<int>(gd, "chunk_rows");
+      x.pieces = get<int>(gd, "pieces");
+      x.piece_vecs = get<int>(gd, "piece_vecs");
       x.ready = P<uint32_t>(get<uintptr_t>(gd, "ready"));
+      x.done = P<uint32_t>(get<uintptr_t>(gd, "done"));
     }
     if (d.contains("rs") && !d["rs"].is_none()) {
       const py::dict rd = d["rs"].cast<py::dict>();
@@ -208,7 +211,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         a.rs.flag_peer[q] = P<uint32_t>(flags[q]);
       }
       a.rs.recv_local = P<const void>(get<uintptr_t>(rd, "recv_local"));
-      a.rs.ld_recv = get<int64_t>(rd, "ld_recv");
+      a.rs.ld_recv = get_or<int64_t>(rd, "ld_recv", 0);
       a.rs.flag_local = P<const uint32_t>(get<uintptr_t>(rd, "flag_local"));
     }
     a.epi = get_or<int>(d, "epi", 0);

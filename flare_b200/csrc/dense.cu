@@ -343,7 +343,8 @@ __global__ void adam_flat_kernel(AdamFlatParams p) {
 // optimizer on the local fp32 master/state shard, push the new bf16 values
 // into every peer's compute copy (all-gather), zero the consumed gradient
 // slices, and finish with a barrier so every rank sees complete parameters.
-__global__ void adam_dp_fused_kernel(AdamDpParams p) {
+template <int R, bool PUSH_ALL>
+__global__ void __launch_bounds__(256, (R == 8 && PUSH_ALL) ? 3 : 4) adam_dp_fused_kernel(AdamDpParams p) {
   __shared__ int ok_sh;
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(p.epoch_ctr) + 1u;
   if (threadIdx.x == 0) {
@@ -359,29 +360,43 @@ __global__ void adam_dp_fused_kernel(AdamDpParams p) {
   if (!ok_sh) return;
   const AdamParams opt = resolve_step(p.opt);
   const int64_t lo4 = p.lo / 4, hi4 = p.hi / 4;
+  // R (group size) and PUSH_ALL (write the bf16 result into every member's copy,
+  // or only the local one) are compile-time, so the peer pointers stay in a few
+  // registers and every load of an element group is issued before its stores.
+  constexpr int PW = PUSH_ALL ? R : 1;
+  float4* gsrc[R];
+  __nv_bfloat16* pdst[PW];
+#pragma unroll
+  for (int s = 0; s < R; ++s) gsrc[s] = reinterpret_cast<float4*>(p.peer_grad[s]);
+#pragma unroll
+  for (int s = 0; s < PW; ++s) pdst[s] = reinterpret_cast<__nv_bfloat16*>(p.peer_param[s]);
+  float4* __restrict__ ws = reinterpret_cast<float4*>(p.master_shard);
+  float4* __restrict__ ms = reinterpret_cast<float4*>(p.m_shard);
+  float4* __restrict__ vs = reinterpret_cast<float4*>(p.v_shard);
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int64_t i = lo4 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < hi4;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s = 0; s < p.world; ++s) {
-      float4* gs = reinterpret_cast<float4*>(p.peer_grad[s]) + i;
-      g = f4_add(g, *gs);
-      *gs = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
     const int64_t li = i - lo4;  // index into the local shard state
-    float4 w = reinterpret_cast<float4*>(p.master_shard)[li];
-    float4 m = reinterpret_cast<float4*>(p.m_shard)[li];
-    float4 v = reinterpret_cast<float4*>(p.v_shard)[li];
+    float4 w = ws[li], m = ms[li], v = vs[li];
+    float4 gv[R];
+#pragma unroll
+    for (int s = 0; s < R; ++s) gv[s] = __ldcg(gsrc[s] + i);
+    float4 g = gv[0];
+#pragma unroll
+    for (int s = 1; s < R; ++s) g = f4_add(g, gv[s]);
+#pragma unroll
+    for (int s = 0; s < R; ++s) __stcg(gsrc[s] + i, zero);
     float* wp = reinterpret_cast<float*>(&w);
     float* gp = reinterpret_cast<float*>(&g);
     float* mp = reinterpret_cast<float*>(&m);
     float* vp = reinterpret_cast<float*>(&v);
 #pragma unroll
     for (int e = 0; e < 4; ++e) adam_elem(opt, wp[e], mp[e], vp[e], gp[e] * p.grad_scale);
-    reinterpret_cast<float4*>(p.master_shard)[li] = w;
-    reinterpret_cast<float4*>(p.m_shard)[li] = m;
-    reinterpret_cast<float4*>(p.v_shard)[li] = v;
-    for (int s = 0; s < p.param_world; ++s)
-      store4<__nv_bfloat16>(reinterpret_cast<__nv_bfloat16*>(p.peer_param[s]) + 4 * i, w);
+    ws[li] = w;
+    ms[li] = m;
+    vs[li] = v;
+#pragma unroll
+    for (int s = 0; s < PW; ++s) store4<__nv_bfloat16>(pdst[s] + 4 * i, w);
   }
   __threadfence_system();
   __syncthreads();
@@ -532,8 +547,16 @@ void adam_flat(const AdamFlatParams& p, cudaStream_t s) {
 
 void adam_dp_fused(const AdamDpParams& p, cudaStream_t s) {
   FLARE_CHECK(p.lo % 4 == 0 && p.hi % 4 == 0, "shard bounds must be multiples of 4");
+  FLARE_CHECK(p.world == 1 || p.world == 2 || p.world == 4 || p.world == 8, "group size must be 1, 2, 4 or 8");
+  FLARE_CHECK(p.param_world == 1 || p.param_world == p.world, "the update goes to the local copy or to all copies");
   const int grid = std::max(1, std::min(grid_for((p.hi - p.lo) / 4, 256), 148 * 4));
-  adam_dp_fused_kernel<<<grid, 256, 0, s>>>(p);
+  const bool all = p.param_world == p.world && p.world > 1;
+  switch (p.world) {
+    case 1: adam_dp_fused_kernel<1, false><<<grid, 256, 0, s>>>(p); break;
+    case 2: all ? adam_dp_fused_kernel<2, true><<<grid, 256, 0, s>>>(p) : adam_dp_fused_kernel<2, false><<<grid, 256, 0, s>>>(p); break;
+    case 4: all ? adam_dp_fused_kernel<4, true><<<grid, 256, 0, s>>>(p) : adam_dp_fused_kernel<4, false><<<grid, 256, 0, s>>>(p); break;
+    default: all ? adam_dp_fused_kernel<8, true><<<grid, 256, 0, s>>>(p) : adam_dp_fused_kernel<8, false><<<grid, 256, 0, s>>>(p); break;
+  }
   FLARE_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

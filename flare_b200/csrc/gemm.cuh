@@ -48,7 +48,10 @@ struct DistGather {
   int64_t rows_per_rank = 0;
   int64_t row_elems = 0;    // elements copied per row (multiple of 8, <= ld)
   int chunk_rows = 128;     // rows per ready flag
+  int pieces = 1;           // copy work items per chunk
+  int piece_vecs = 0;       // 16-byte vectors per work item
   uint32_t* ready = nullptr;  // [nranks * rows_per_rank / chunk_rows]
+  uint32_t* done = nullptr;   // [same], zero between launches
 };
 
 // Reduce-scatter of the output rows over `nranks` ranks (rank q owns output
@@ -57,10 +60,10 @@ struct DistRS {
   int enabled = 0;
   int nranks = 1, my = 0;
   int rows_per_rank = 0;
-  void* recv_peer[8] = {};        // rank q's receive buffer [nranks][rows_per_rank][ld_recv]
+  void* recv_peer[8] = {};        // rank q's receive buffer: [nranks][tiles][4][8] blocks of 32 x 32 bf16
   const void* recv_local = nullptr;
-  int64_t ld_recv = 0;
-  uint32_t* flag_peer[8] = {};    // rank q's flags [nranks][tiles_per_rank][4]
+  int64_t ld_recv = 0;            // unused (kept for the binding's field list)
+  uint32_t* flag_peer[8] = {};    // rank q's flags [nranks][tiles_per_rank][8]
   const uint32_t* flag_local = nullptr;
 };
 
@@ -68,7 +71,7 @@ struct DistGemmArgs {
   GemmArgs g;                     // C rows are LOCAL rows when rs.enabled
   const int* tiles = nullptr;     // (m_tile << 16 | n_tile) in processing order
   int num_tiles = 0;
-  const int* chunks = nullptr;    // (operand << 24 | chunk) in copy order (remote chunks only)
+  const int* chunks = nullptr;    // (operand << 31 | chunk << 12 | piece) in copy order (remote chunks only)
   int num_chunks = 0;
   DistGather ga, gb;
   DistRS rs;

@@ -21,11 +21,12 @@
 //    the peers' flags of the tile, adds their partials and runs the epilogue.
 //  * a plain persistent GEMM (R = 1), with the same epilogues.
 //
-// Structure: 256 threads.  warp 0 lane 0 = TMA producer (4-stage ring of
+// Structure: 384 threads.  warp 0 lane 0 = TMA producer (4-stage ring of
 // 128-byte-swizzled 128x64 / 256x64 bf16 tiles); warp 1 lane 0 = tcgen05.mma
 // issuer into one of two TMEM accumulators (2 x 256 columns), so the
-// epilogue of tile i overlaps the MMAs of tile i+1; warps 2-5 = epilogue
-// (warp w reads TMEM lanes 32*(w%4)..+31); warps 6-7 = copy warps.
+// epilogue of tile i overlaps the MMAs of tile i+1; warps 2-9 = epilogue
+// (warp w reads TMEM lanes 32*(w%4)..+31, columns [128*h, 128*h+128) with
+// h = (w-2)/4); warps 10-11 = copy warps.
 // The launch is cooperative (all CTAs co-resident), which the cross-CTA
 // chunk flags rely on; every wait is bounded and reports a status code.
 //
@@ -53,7 +54,9 @@ constexpr int kBM = 128;
 constexpr int kBN = 256;
 constexpr int kBK = 64;
 constexpr int kStages = 4;
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;
+constexpr int kEpiWarps = 8;   // warps 2..9: two per TMEM lane quarter, each owning half of the columns
+constexpr int kCopyWarp0 = 2 + kEpiWarps;
 constexpr int kTileA = kBM * kBK * 2;  // 16 KiB
 constexpr int kTileB = kBN * kBK * 2;  // 32 KiB
 constexpr int kOffB = kStages * kTileA;
@@ -97,7 +100,10 @@ struct GatherDev {
   int row_vecs;                         // 16-byte vectors copied per row
   int chunk_rows;
   int nranks, my;
+  int pieces;                           // copy work items per chunk
+  int piece_vecs;                       // 16-byte vectors per work item
   uint32_t* ready;                      // per chunk: epoch when its rows are local
+  uint32_t* done;                       // per chunk: pieces copied so far this launch
 };
 
 struct DistParams {
@@ -151,9 +157,10 @@ __device__ __forceinline__ bool wait_rows(const GatherDev& g, int64_t r0, int n,
   return true;
 }
 
-// One warp copies chunk `ci` of a gathered operand from its owner into the
-// local full buffer, then publishes the chunk's ready flag.
-__device__ __forceinline__ void copy_chunk(const GatherDev& g, int64_t ci, int lane, uint32_t epoch) {
+// One warp copies piece `piece` of chunk `ci` of a gathered operand from its
+// owner into the local full buffer.  The warp that completes the chunk's last
+// piece resets the chunk's counter and publishes its ready flag.
+__device__ __forceinline__ void copy_piece(const GatherDev& g, int64_t ci, int piece, int lane, uint32_t epoch) {
   const int64_t r0 = ci * g.chunk_rows;
   const int owner = static_cast<int>(r0 / g.rows_per_rank);
   const int nrows = static_cast<int>(min(static_cast<int64_t>(g.chunk_rows), g.total_rows - r0));
@@ -161,14 +168,16 @@ __device__ __forceinline__ void copy_chunk(const GatherDev& g, int64_t ci, int l
   uint4* dst = reinterpret_cast<uint4*>(g.dst + r0 * g.ld);
   const int64_t ldv = g.ld / 8;
   const int64_t total = static_cast<int64_t>(nrows) * g.row_vecs;
-  for (int64_t v0 = lane; v0 < total; v0 += 32 * kCopyUnroll) {
+  const int64_t vb = static_cast<int64_t>(piece) * g.piece_vecs;
+  const int64_t ve = min(total, vb + g.piece_vecs);
+  for (int64_t v0 = vb + lane; v0 < ve; v0 += 32 * kCopyUnroll) {
     uint4 buf[kCopyUnroll];
     int64_t off[kCopyUnroll];
 #pragma unroll
     for (int u = 0; u < kCopyUnroll; ++u) {
       const int64_t v = v0 + 32 * u;
       off[u] = -1;
-      if (v < total) {
+      if (v < ve) {
         const int64_t rr = v / g.row_vecs, cc = v - rr * g.row_vecs;
         off[u] = rr * ldv + cc;
         buf[u] = __ldcg(src + off[u]);
@@ -182,7 +191,14 @@ __device__ __forceinline__ void copy_chunk(const GatherDev& g, int64_t ci, int l
   fence_proxy_async_global();
   __threadfence();
   __syncwarp();
-  if (lane == 0) st_release_gpu(g.ready + ci, epoch);
+  if (lane == 0) {
+    const uint32_t prev = atomicAdd(g.done + ci, 1u);
+    if (prev + 1 == static_cast<uint32_t>(g.pieces)) {
+      g.done[ci] = 0u;
+      __threadfence();
+      st_release_gpu(g.ready + ci, epoch);
+    }
+  }
 }
 
 __device__ __forceinline__ uint4 pack8(const float* v) {
@@ -242,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       sm100::mbar_init(&tfull_bar[b], 1);
-      sm100::mbar_init(&tempty_bar[b], 4);
+      sm100::mbar_init(&tempty_bar[b], kEpiWarps);
     }
     *abort_flag = 0;
     sm100::fence_mbar_init();
@@ -337,9 +353,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm100::mma_commit(&tfull_bar[b]);
       }
     }
-  } else if (warp < 6) {
+  } else if (warp < kCopyWarp0) {
     // -------------------------------- epilogue --------------------------------
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;  // which 128 columns of the tile
+    const int slot = quarter * 2 + half;
     const int tiles_per_rank = p.rs ? (p.rs_rows / kBM) * p.n_tiles : 0;
     bool barrier_seen = !need_barrier;
     int local = 0;
@@ -373,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           bool ok = true;
           for (int q = 0; q < p.rs_nranks && ok; ++q) {
             if (q == p.rs_my) continue;
-            ok = wait_flag_geq(p.rs_flag_local + (static_cast<int64_t>(q) * tiles_per_rank + tile_local) * 4 + quarter,
+            ok = wait_flag_geq(p.rs_flag_local + (static_cast<int64_t>(q) * tiles_per_rank + tile_local) * 8 + slot,
                                epoch, p.timeout_ns, p.status, 600 + q);
           }
           if (!ok) {
@@ -384,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const uint32_t tbase = tmem_base + static_cast<uint32_t>(b * kBN) + (static_cast<uint32_t>(quarter * 32) << 16);
 #pragma unroll 1
-      for (int c = 0; c < kBN; c += 32) {
+      for (int c = half * (kBN / 2); c < (half + 1) * (kBN / 2); c += 32) {
         const int ncol = n0 + c;
         if (ncol >= p.N) break;  // warp-uniform
         uint32_t r[32];
@@ -395,27 +413,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
         if (send) {
-          if (row_ok) {
-            __nv_bfloat16* dst = p.rs_recv_peer[owner] + (static_cast<int64_t>(p.rs_my) * p.rs_rows + lrow) * p.ld_recv + ncol;
-            if (full_chunk) {
+          // Partial tile -> owner.  Receive layout: one 2 KiB block per (sender, tile,
+          // quarter, 32-column chunk), element (row r, col 8q+e) at q*256 + r*8 + e, so
+          // each warp-wide 16-byte store writes 512 contiguous bytes over NVLink.
+          __nv_bfloat16* blk = p.rs_recv_peer[owner] +
+                               ((((static_cast<int64_t>(p.rs_my) * tiles_per_rank + tile_local) * 4 + quarter) * 8 +
+                                 (c >> 5)) << 10);
 #pragma unroll
-              for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(dst + 8 * q) = pack8(v + 8 * q);
-            } else {
-              _Pragma("unroll") for (int j = 0; j < 32; ++j) if (ncol + j < p.N) dst[j] = __float2bfloat16_rn(v[j]);
-            }
-          }
+          for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(blk + q * 256 + lane * 8) = pack8(v + 8 * q);
           continue;
         }
-        if (p.rs && row_ok) {
+        if (p.rs) {
           for (int q = 0; q < p.rs_nranks; ++q) {
             if (q == p.rs_my) continue;
-            const __nv_bfloat16* src = p.rs_recv_local + (static_cast<int64_t>(q) * p.rs_rows + lrow) * p.ld_recv + ncol;
-            if (full_chunk) {
+            const __nv_bfloat16* blk = p.rs_recv_local +
+                                       ((((static_cast<int64_t>(q) * tiles_per_rank + tile_local) * 4 + quarter) * 8 +
+                                         (c >> 5)) << 10);
 #pragma unroll
-              for (int t = 0; t < 4; ++t) unpack8_add(__ldcg(reinterpret_cast<const uint4*>(src) + t), v + 8 * t);
-            } else {
-              _Pragma("unroll") for (int j = 0; j < 32; ++j) if (ncol + j < p.N) v[j] += __bfloat162float(src[j]);
-            }
+            for (int t = 0; t < 4; ++t)
+              unpack8_add(__ldcg(reinterpret_cast<const uint4*>(blk + t * 256 + lane * 8)), v + 8 * t);
           }
         }
         // epilogue math
@@ -523,20 +539,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) sm100::mbar_arrive(&tempty_bar[b]);
       if (send) {
         // this warp's 32 rows of the tile are in the owner's memory: publish them
-        // (one flag per tile quarter, so the four warps never wait on each other)
+        // (one flag per tile quarter and column half, so the warps never wait on each other)
         __threadfence_system();
         __syncwarp();
         if (lane == 0) {
           fence_sys();
-          st_release_sys(p.rs_flag_peer[owner] + (static_cast<int64_t>(p.rs_my) * tiles_per_rank + tile_local) * 4 +
-                             quarter, epoch);
+          st_release_sys(p.rs_flag_peer[owner] + (static_cast<int64_t>(p.rs_my) * tiles_per_rank + tile_local) * 8 + slot,
+                         epoch);
         }
       }
     }
   } else {
     // ------------------------------- copy warps -------------------------------
     const bool copier = p.gather_a || p.gather_b;
-    if (need_barrier && blockIdx.x == 0 && warp == 6 && lane == 0) {
+    if (need_barrier && blockIdx.x == 0 && warp == kCopyWarp0 && lane == 0) {
       // whole-world entry barrier: every rank finished writing what peers read
       fence_sys();
       for (int s = 0; s < p.world; ++s) st_release_sys(p.bar_peer[s] + p.rank, epoch);
@@ -547,13 +563,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (copier) {
       bool ok = !need_barrier || wait_flag_geq(p.ctl + 2, epoch, p.timeout_ns, p.status, 501);
-      const int cw = blockIdx.x * 2 + (warp - 6);
+      const int cw = blockIdx.x * 2 + (warp - kCopyWarp0);
       for (int c = cw; c < p.num_chunks && ok; c += gridDim.x * 2) {
-        const int op = p.chunks[c] >> 24;
-        const int64_t ci = p.chunks[c] & 0xFFFFFF;
+        const uint32_t item = static_cast<uint32_t>(p.chunks[c]);
+        const int op = static_cast<int>(item >> 31);
+        const int64_t ci = (item >> 12) & 0x7FFFF;
+        const int piece = static_cast<int>(item & 0xFFF);
         // two call sites keep each GatherDev in parameter space (no local copy)
-        if (op) copy_chunk(p.gb, ci, lane, epoch);
-        else copy_chunk(p.ga, ci, lane, epoch);
+        if (op) copy_piece(p.gb, ci, piece, lane, epoch);
+        else copy_piece(p.ga, ci, piece, lane, epoch);
       }
       if (!ok) *abort_flag = 1;
     }
@@ -608,7 +626,10 @@ void launch(const DistGemmArgs& a, cudaStream_t stream) {
     d.chunk_rows = s.chunk_rows;
     d.nranks = s.nranks;
     d.my = s.my;
+    d.pieces = s.pieces;
+    d.piece_vecs = s.piece_vecs;
     d.ready = s.ready;
+    d.done = s.done;
   }
   p.C = g.C;
   p.ldc = g.ldc;
@@ -683,7 +704,6 @@ void gemm_dist_tcgen05(const DistGemmArgs& a, cudaStream_t stream) {
   if (a.rs.enabled) {
     FLARE_CHECK(a.rs.rows_per_rank % kBM == 0, "reduce-scatter rows per rank must be a multiple of 128");
     FLARE_CHECK(static_cast<int64_t>(a.rs.rows_per_rank) * a.rs.nranks == g.M, "reduce-scatter rows mismatch");
-    FLARE_CHECK(a.rs.ld_recv % 8 == 0, "receive pitch must be a multiple of 8");
   }
   for (int op = 0; op < 2; ++op) {
     const DistGather& s = op ? a.gb : a.ga;
@@ -691,7 +711,10 @@ void gemm_dist_tcgen05(const DistGemmArgs& a, cudaStream_t stream) {
     FLARE_CHECK(s.nranks >= 1 && s.nranks <= kMaxRanks && s.my >= 0 && s.my < s.nranks, "bad gather group");
     FLARE_CHECK(s.row_elems % 8 == 0 && s.row_elems <= s.ld && s.ld % 8 == 0, "gather rows must be 16-byte units");
     FLARE_CHECK(s.chunk_rows > 0 && s.rows_per_rank % s.chunk_rows == 0, "chunk rows must divide rows per rank");
-    FLARE_CHECK(s.rows_per_rank * s.nranks < (int64_t(1) << 24) * s.chunk_rows, "too many chunks");
+    FLARE_CHECK(s.rows_per_rank * s.nranks <= (int64_t(1) << 19) * s.chunk_rows, "too many chunks");
+    FLARE_CHECK(s.pieces >= 1 && s.pieces <= 4096 && s.done != nullptr, "bad copy pieces");
+    FLARE_CHECK(static_cast<int64_t>(s.pieces) * s.piece_vecs >= s.chunk_rows * (s.row_elems / 8),
+                "copy pieces do not cover a chunk");
   }
   FLARE_CHECK(a.num_chunks == 0 || a.chunks != nullptr, "chunk list missing");
   if (!g.a_mn && !g.b_mn) launch<false, false>(a, stream);

@@ -252,6 +252,7 @@ class DCN:
             else:
                 self.dpre.append(torch.zeros(m, d, **bf))
         self._build_calls()
+        self._build_ops()
         if world_size > 1:
             # every rank's flags and buffers are initialised before any peer signals into them
             from ..parallel.dist import barrier
@@ -303,12 +304,12 @@ class DCN:
         # cross forward (local rows; weights FSDP-gathered inside the GEMM)
         for l in range(L):
             xl = self.xs[l][:, :W]
-            self.fwd_calls.append(DistGemm(ctx, xl, self.V[l].full, self.t[l], gb=self.V[l].w))
+            self.fwd_calls.append((f"fwd.cross{l}.V", DistGemm(ctx, xl, self.V[l].full, self.t[l], gb=self.V[l].w)))
             out = self.final_in[:, :W] if l == L - 1 else self.xs[l + 1][:, :W]
-            self.fwd_calls.append(DistGemm(ctx, self.t[l], self.U[l].full, out, gb=self.U[l].w,
-                                           bias=ds.compute_view(f"cross{l}.b"), epi="cross",
-                                           aux0=self.x0.local[:, :W], aux1=self.xs[l][:, :W],
-                                           zout=self.z[l][:, :W]))
+            self.fwd_calls.append((f"fwd.cross{l}.U", DistGemm(ctx, self.t[l], self.U[l].full, out, gb=self.U[l].w,
+                                                                bias=ds.compute_view(f"cross{l}.b"), epi="cross",
+                                                                aux0=self.x0.local[:, :W], aux1=self.xs[l][:, :W],
+                                                                zout=self.z[l][:, :W])))
         # deep forward
         a_in, a_sr = self.x0.full[:, :W], self.x0
         for i, d in enumerate(cfg.deep):
@@ -316,7 +317,8 @@ class DCN:
             bias = ds.compute_view(f"deep{i}.b")
             if self.col_parallel[i] and tp > 1:
                 bsl = bias[self.tp_idx * (d // tp):(self.tp_idx + 1) * (d // tp)]
-                self.fwd_calls.append(DistGemm(ctx, a_in, w.full, self.h[i], ga=a_sr, gb=w.w, bias=bsl, relu=True))
+                self.fwd_calls.append((f"fwd.deep{i}.ag_gemm", DistGemm(ctx, a_in, w.full, self.h[i], ga=a_sr, gb=w.w,
+                                                                        bias=bsl, relu=True)))
                 a_in, a_sr = self.h[i], None
             else:
                 if i == nd - 1:
@@ -325,8 +327,8 @@ class DCN:
                     out = self.h[i].local
                 else:
                     out = self.h[i]
-                self.fwd_calls.append(DistGemm(ctx, a_in, w.full, out, ga=a_sr if tp == 1 else None, gb=w.w,
-                                               rs=self.rs, bias=bias, relu=True))
+                self.fwd_calls.append((f"fwd.deep{i}.gemm_rs", DistGemm(ctx, a_in, w.full, out, gb=w.w, rs=self.rs,
+                                                                        bias=bias, relu=True)))
                 if i < nd - 1:
                     a_in = self.h[i].full[:, :d] if tp > 1 else self.h[i]
                     a_sr = self.h[i] if tp > 1 else None
@@ -335,15 +337,15 @@ class DCN:
             g_next = self.dfin.local[:, :ldW] if l == L - 1 else self.g[l + 1]
             calls = []
             calls.append(("elem", l, g_next))
-            calls.append(DistGemm(ctx, self.dz[:, :W], self.U[l].full, self.dt, b_t=True))       # dt = dz U
+            calls.append((f"bwd.cross{l}.dt", DistGemm(ctx, self.dz[:, :W], self.U[l].full, self.dt, b_t=True)))
             if l > 0:
-                calls.append(DistGemm(ctx, self.dt, self.V[l].full, self.g[l][:, :W], b_t=True, epi="residual",
-                                      aux1=g_next[:, :W]))                                          # g_l
+                calls.append((f"bwd.cross{l}.dx", DistGemm(ctx, self.dt, self.V[l].full, self.g[l][:, :W], b_t=True,
+                                                           epi="residual", aux1=g_next[:, :W])))
             else:
-                calls.append(DistGemm(ctx, self.dt, self.V[l].full, self.dx0[:, :W], b_t=True, epi="residual",
-                                      aux1=g_next[:, :W], accumulate=True))                         # dx0 += g_0
-            calls.append(("wgrad", self.dz[:, :W], self.t[l], self.U[l].grad))                    # dU = dz^T t
-            calls.append(("wgrad", self.dt, self.xs[l][:, :W], self.V[l].grad))                   # dV = dt^T x_l
+                calls.append((f"bwd.cross{l}.dx", DistGemm(ctx, self.dt, self.V[l].full, self.dx0[:, :W], b_t=True,
+                                                           epi="residual", aux1=g_next[:, :W], accumulate=True)))
+            calls.append(("wgrad", f"bwd.cross{l}.dU", self.dz[:, :W], self.t[l], self.U[l].grad))
+            calls.append(("wgrad", f"bwd.cross{l}.dV", self.dt, self.xs[l][:, :W], self.V[l].grad))
             self.bwd_cross.append(calls)
         # deep backward.  deep{i}.b gets colsum(dpre_i): from the head's output for
         # the last layer, otherwise from the epilogue of the GEMM producing dpre_i.
@@ -356,12 +358,13 @@ class DCN:
                 # column-parallel layer i: input rows gathered, output dpre[i] [M, d/tp]
                 a_full = self.x0.full[:, :W] if i == 0 else self.h[i - 1].full[:, :d_in]
                 if i == 0:
-                    self.bwd_deep.append(DistGemm(ctx, self.dpre[i], w.full, self.dx0[:, :W], b_t=True, rs=self.rs,
-                                                  accumulate=True))
+                    self.bwd_deep.append((f"bwd.deep{i}.dx_rs", DistGemm(ctx, self.dpre[i], w.full, self.dx0[:, :W],
+                                                                         b_t=True, rs=self.rs, accumulate=True)))
                 else:  # input came from a row-parallel layer: full-width local rows after the reduce-scatter
-                    self.bwd_deep.append(DistGemm(ctx, self.dpre[i], w.full, self.dpre[i - 1].local, b_t=True,
-                                                  rs=self.rs, mask=self.h[i - 1].local, colsum=prev_bias))
-                self.bwd_deep.append(("wgrad", self.dpre[i], a_full, w.grad))
+                    self.bwd_deep.append((f"bwd.deep{i}.dx_rs", DistGemm(ctx, self.dpre[i], w.full,
+                                                                         self.dpre[i - 1].local, b_t=True, rs=self.rs,
+                                                                         mask=self.h[i - 1].local, colsum=prev_bias)))
+                self.bwd_deep.append(("wgrad", f"bwd.deep{i}.dW", self.dpre[i], a_full, w.grad))
                 continue
             # row-parallel layer i (or any layer when tp == 1)
             last = i == nd - 1
@@ -373,19 +376,19 @@ class DCN:
                 dsr = None
                 d_full = d_local = self.dfin.local[:, ldW:] if last else self.dpre[i]
             if last:
-                self.bwd_deep.append(("colsum", d_local, ds.grad_view(f"deep{i}.b")))
+                self.bwd_deep.append(("colsum", f"bwd.deep{i}.db", d_local, ds.grad_view(f"deep{i}.b")))
             if i == 0:
-                self.bwd_deep.append(DistGemm(ctx, d_full, w.full, self.dx0[:, :W], b_t=True, ga=dsr,
-                                              accumulate=True))
-                self.bwd_deep.append(("wgrad", d_full, self.x0.full[:, :W], w.grad))
+                self.bwd_deep.append((f"bwd.deep{i}.ag_dx", DistGemm(ctx, d_full, w.full, self.dx0[:, :W], b_t=True,
+                                                                     ga=dsr, accumulate=True)))
+                self.bwd_deep.append(("wgrad", f"bwd.deep{i}.dW", d_full, self.x0.full[:, :W], w.grad))
                 continue
             h_prev = self.h[i - 1]
             if tp > 1:  # previous layer is column-parallel: this rank's slice of its bias
                 sl = dims[i] // tp
                 prev_bias = prev_bias[self.tp_idx * sl:(self.tp_idx + 1) * sl]
-            self.bwd_deep.append(DistGemm(ctx, d_full, w.full, self.dpre[i - 1], b_t=True, ga=dsr, mask=h_prev,
-                                          colsum=prev_bias))
-            self.bwd_deep.append(("wgrad", d_full, h_prev, w.grad))
+            self.bwd_deep.append((f"bwd.deep{i}.ag_dx", DistGemm(ctx, d_full, w.full, self.dpre[i - 1], b_t=True,
+                                                                 ga=dsr, mask=h_prev, colsum=prev_bias)))
+            self.bwd_deep.append(("wgrad", f"bwd.deep{i}.dW", d_full, h_prev, w.grad))
 
     # ------------------------------------------------------------------ data
     def set_batch(self, dense: torch.Tensor, labels: torch.Tensor, offsets: torch.Tensor, values: torch.Tensor,
@@ -395,65 +398,97 @@ class DCN:
         self.emb.set_input(offsets, values, non_blocking=non_blocking)
 
     # ------------------------------------------------------------------ step
+    def _build_ops(self) -> None:
+        """The training step as a flat list of (name, launch) pairs, in stream order."""
+        C = native()
+        ds = self.dense
+        ops = [("emb.forward", lambda: self.emb.forward(training=True)),
+               ("concat_x0", lambda: C.dcn_concat_x0(self.emb.pooled_output.data_ptr(), self.E, self.dense_in.data_ptr(),
+                                                     self.cfg.num_dense, self.m, self.E, self.x0.local.data_ptr(),
+                                                     self.x0.ld))]
+        ops += self.fwd_calls
+        head = dict(h=self.final_in.data_ptr(), ldh=self.H, H=self.H, relu_from=self.ldW,
+                    w=ds.compute_view("head.w").data_ptr(), bias=ds.compute_view("head.b").data_ptr(),
+                    labels=self.labels.data_ptr(), B=self.m, grad_scale=1.0 / self.global_B,
+                    logits=self.logits.data_ptr(), dl=self.dl.data_ptr(), dh=self.dfin.local.data_ptr(),
+                    lddh=self.H, loss_sum=self.loss_sum.data_ptr(), db=ds.grad_view("head.b").data_ptr())
+        ops.append(("loss.zero", self.loss_sum.zero_))
+        ops.append(("head", lambda: C.dcn_head(head)))
+        ops.append(("head.dw", lambda: C.dcn_scaled_colsum(self.final_in.data_ptr(), self.H, self.dl.data_ptr(),
+                                                           self.m, self.H, ds.grad_view("head.w").data_ptr())))
+        first = True
+        for calls in self.bwd_cross:
+            for c in calls:
+                if c[0] == "elem":
+                    _, l, g_next = c
+                    acc = 0 if first else 1
+                    first = False
+                    ops.append((f"bwd.cross{l}.elem", lambda l=l, g=g_next, acc=acc: C.dcn_cross_bwd_elem(
+                        g.data_ptr(), g.stride(0), self.x0.local.data_ptr(), self.z[l].data_ptr(), self.ldW, self.m,
+                        self.ldW, self.dz.data_ptr(), self.dx0.data_ptr(), self.ldW, acc,
+                        ds.grad_view(f"cross{l}.b").data_ptr())))
+                else:
+                    ops.append(self._op(c))
+        ops += [self._op(c) for c in self.bwd_deep]
+        ops.append(("finalize_grad", lambda: C.dcn_finalize_grad(self.dx0.data_ptr(), self.ldW, self.m, self.E,
+                                                                 self.emb.grad_input.data_ptr(),
+                                                                 self.emb.grad_input.stride(0))))
+        self.fb_ops = ops
+        upd = [("emb.backward", self.emb.backward), ("dense.apply", self.dense.apply)]
+        upd += [(f"fsdp.{w.name}", lambda w=w: w.apply(self.dense.step)) for w in self.fsdp_weights]
+        self.update_ops = upd
+
+    @staticmethod
+    def _op(c):
+        if isinstance(c[1], DistGemm):
+            return c
+        if c[0] == "wgrad":
+            _, name, dy, x, out = c
+            return name, lambda: gemm(dy, x, a_t=True, b_t=True, out=out, accumulate=True)
+        if c[0] == "colsum":
+            _, name, x, out = c
+            return name, lambda: colsum_(x, out)
+        raise ValueError(c[0])
+
+    # ------------------------------------------------------------------ step
     def forward(self, training: bool = True) -> None:
+        """Forward pass only (eval: ``training=False`` leaves the sparse staging untouched)."""
         C = native()
         pooled = self.emb.forward(training=training)
         C.dcn_concat_x0(pooled.data_ptr(), pooled.stride(0), self.dense_in.data_ptr(), self.cfg.num_dense, self.m,
                         self.E, self.x0.local.data_ptr(), self.x0.ld)
-        for call in self.fwd_calls:
+        for _, call in self.fwd_calls:
             call()
 
     def forward_backward(self) -> torch.Tensor:
-        C = native()
-        ds = self.dense
-        self.forward()
-        self.loss_sum.zero_()
-        C.dcn_head(dict(h=self.final_in.data_ptr(), ldh=self.H, H=self.H, relu_from=self.ldW,
-                        w=ds.compute_view("head.w").data_ptr(), bias=ds.compute_view("head.b").data_ptr(),
-                        labels=self.labels.data_ptr(), B=self.m, grad_scale=1.0 / self.global_B,
-                        logits=self.logits.data_ptr(), dl=self.dl.data_ptr(), dh=self.dfin.local.data_ptr(),
-                        lddh=self.H, loss_sum=self.loss_sum.data_ptr(), db=ds.grad_view("head.b").data_ptr()))
-        C.dcn_scaled_colsum(self.final_in.data_ptr(), self.H, self.dl.data_ptr(), self.m, self.H,
-                            ds.grad_view("head.w").data_ptr())
-        first = True
-        for calls in self.bwd_cross:
-            for c in calls:
-                if isinstance(c, DistGemm):
-                    c()
-                elif c[0] == "elem":
-                    _, l, g_next = c
-                    C.dcn_cross_bwd_elem(g_next.data_ptr(), g_next.stride(0), self.x0.local.data_ptr(),
-                                         self.z[l].data_ptr(), self.ldW, self.m, self.ldW, self.dz.data_ptr(),
-                                         self.dx0.data_ptr(), self.ldW, 0 if first else 1,
-                                         ds.grad_view(f"cross{l}.b").data_ptr())
-                    first = False
-                else:
-                    self._run(c)
-        for c in self.bwd_deep:
-            if isinstance(c, DistGemm):
-                c()
-            else:
-                self._run(c)
-        C.dcn_finalize_grad(self.dx0.data_ptr(), self.ldW, self.m, self.E, self.emb.grad_input.data_ptr(),
-                            self.emb.grad_input.stride(0))
+        for _, op in self.fb_ops:
+            op()
         return self.loss_sum
 
-    def _run(self, c) -> None:
-        if c[0] == "wgrad":
-            _, dy, x, out = c
-            gemm(dy, x, a_t=True, b_t=True, out=out, accumulate=True)
-        elif c[0] == "colsum":
-            colsum_(c[1], c[2])
-        else:
-            raise ValueError(c[0])
-
     def train_step(self) -> torch.Tensor:
-        loss = self.forward_backward()
-        self.emb.backward()
-        self.dense.apply()
-        for w in self.fsdp_weights:
-            w.apply(self.dense.step)
-        return loss
+        for _, op in self.fb_ops:
+            op()
+        for _, op in self.update_ops:
+            op()
+        return self.loss_sum
+
+    def profile_step(self) -> list[tuple[str, float]]:
+        """Run one eager training step with CUDA events between ops; returns (name, ms) per op."""
+        evs = []
+        ops = self.fb_ops + self.update_ops
+        for name, op in ops:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            evs.append((name, e))
+            op()
+        end = torch.cuda.Event(enable_timing=True)
+        end.record()
+        torch.cuda.synchronize()
+        out = []
+        for i, (name, e) in enumerate(evs):
+            nxt = evs[i + 1][1] if i + 1 < len(evs) else end
+            out.append((name, e.elapsed_time(nxt)))
+        return out
 
     def check(self) -> None:
         self.emb.check()
@@ -493,17 +528,19 @@ class DCN:
 class DCNTorch(nn.Module):
     """DCN-v2 in plain PyTorch autograd (EmbeddingBag sum pooling, Linear layers)."""
 
-    def __init__(self, cfg: DCNConfig, *, seed: int = 0, dtype: torch.dtype = torch.float32):
+    def __init__(self, cfg: DCNConfig, *, seed: int = 0, dtype: torch.dtype = torch.float32,
+                 device: torch.device | str | None = None, sparse_grad: bool = False):
         super().__init__()
         self.cfg = cfg
-        self.embs = nn.ModuleList(nn.EmbeddingBag(t.num_embeddings, t.embedding_dim, mode="sum")
-                                  for t in cfg.tables)
+        dk = {"device": device}
+        self.embs = nn.ModuleList(nn.EmbeddingBag(t.num_embeddings, t.embedding_dim, mode="sum", sparse=sparse_grad,
+                                                  **dk) for t in cfg.tables)
         W, r = cfg.width, cfg.cross_rank
-        self.V = nn.ModuleList(nn.Linear(W, r, bias=False) for _ in range(cfg.cross_layers))
-        self.U = nn.ModuleList(nn.Linear(r, W) for _ in range(cfg.cross_layers))
+        self.V = nn.ModuleList(nn.Linear(W, r, bias=False, **dk) for _ in range(cfg.cross_layers))
+        self.U = nn.ModuleList(nn.Linear(r, W, **dk) for _ in range(cfg.cross_layers))
         dims = [W] + list(cfg.deep)
-        self.deep = nn.ModuleList(nn.Linear(a, b) for a, b in zip(dims[:-1], dims[1:]))
-        self.head = nn.Linear(W + cfg.deep[-1], 1)
+        self.deep = nn.ModuleList(nn.Linear(a, b, **dk) for a, b in zip(dims[:-1], dims[1:]))
+        self.head = nn.Linear(W + cfg.deep[-1], 1, **dk)
         self.compute_dtype = dtype
         self.load_logical(dcn_init_weights(cfg, seed))
 

@@ -31,6 +31,16 @@ from .._native import DEFAULT_TIMEOUT_NS, PEER_TIMEOUT_NS, DeviceStatus, native
 
 BM, BN = 128, 256
 F32, BF16 = 0, 1
+PIECE_VECS = 512  # 16-byte vectors (8 KiB) per copy work item of a gathered chunk
+
+
+def _pieces(chunk_rows: int, cols: int) -> tuple[int, int]:
+    """(pieces per chunk, vectors per piece) for a chunk of ``chunk_rows`` rows of ``cols`` bf16."""
+    vecs = chunk_rows * (_round_up(cols, 8) // 8)
+    per = PIECE_VECS
+    while (vecs + per - 1) // per > 4096:
+        per *= 2
+    return (vecs + per - 1) // per, per
 
 
 def _round_up(x: int, m: int) -> int:
@@ -76,6 +86,7 @@ class ShardedRows:
         self.buf = ctx.heap.alloc((self.R * self.S, self.ld), torch.bfloat16)
         self.buf.local.zero_()
         self.ready = torch.zeros(self.R * self.S // self.chunk_rows, dtype=torch.int32, device=ctx.device)
+        self.done = torch.zeros_like(self.ready)
 
     @property
     def full(self) -> torch.Tensor:
@@ -90,10 +101,11 @@ class ShardedRows:
     def gather_spec(self) -> dict | None:
         if self.R == 1:
             return None
+        pieces, per = _pieces(self.chunk_rows, self.cols)
         return {"nranks": self.R, "my": self.my, "src": [self.buf.peer_ptrs[g] for g in self.group],
                 "dst": self.buf.local.data_ptr(), "ld": self.ld, "rows_per_rank": self.S,
                 "row_elems": _round_up(self.cols, 8), "chunk_rows": self.chunk_rows,
-                "ready": self.ready.data_ptr()}
+                "pieces": pieces, "piece_vecs": per, "ready": self.ready.data_ptr(), "done": self.done.data_ptr()}
 
     def column_view(self, col_offset: int, cols: int) -> "ShardedRowsView":
         """The columns [col_offset, col_offset+cols) as a separately gatherable operand."""
@@ -110,6 +122,7 @@ class ShardedRowsView:
         self.R, self.my, self.S, self.ld, self.group = base.R, base.my, base.S, base.ld, base.group
         self.chunk_rows = base.chunk_rows
         self.ready = torch.zeros_like(base.ready)
+        self.done = torch.zeros_like(base.ready)
 
     @property
     def full(self) -> torch.Tensor:
@@ -126,11 +139,13 @@ class ShardedRowsView:
                                                          (self.base.buf.peer_ptrs[g] for g in self.group)],
                 "dst": self.base.buf.local.data_ptr() + 2 * self.off, "ld": self.ld, "rows_per_rank": self.S,
                 "row_elems": _round_up(self.cols, 8), "chunk_rows": self.chunk_rows,
-                "ready": self.ready.data_ptr()}
+                "pieces": _pieces(self.chunk_rows, self.cols)[0], "piece_vecs": _pieces(self.chunk_rows, self.cols)[1],
+                "ready": self.ready.data_ptr(), "done": self.done.data_ptr()}
 
 
 class RowReduceScatter:
-    """Receive slots ``[R][S][ld]`` (bf16) and per-tile-quarter flags for a row reduce-scatter."""
+    """Receive blocks (bf16, one 32 x 32 block per sender/tile/quarter/column chunk) and
+    per-(tile, lane quarter, column half) flags for a row reduce-scatter."""
 
     def __init__(self, ctx: DistGemmContext, group: list[int], rows_per_rank: int, max_cols: int):
         if rows_per_rank % BM:
@@ -141,9 +156,9 @@ class RowReduceScatter:
         self.S = int(rows_per_rank)
         self.ld = _round_up(max_cols, 8)
         self.max_cols = int(max_cols)
-        self.recv = ctx.heap.alloc((self.R, self.S, self.ld), torch.bfloat16)
+        self.recv = ctx.heap.alloc((self.R, self.S, _round_up(max_cols, BN)), torch.bfloat16)
         tiles_per_rank = (self.S // BM) * ((max_cols + BN - 1) // BN)
-        self.flags = ctx.heap.alloc((self.R * tiles_per_rank * 4,), torch.int32)
+        self.flags = ctx.heap.alloc((self.R * tiles_per_rank * 8,), torch.int32)
         self.flags.local.zero_()
 
     def spec(self, n_cols: int) -> dict | None:
@@ -153,7 +168,7 @@ class RowReduceScatter:
             raise ValueError("reduce-scatter output wider than its buffers")
         return {"nranks": self.R, "my": self.my, "rows_per_rank": self.S,
                 "recv_peer": [self.recv.peer_ptrs[g] for g in self.group], "recv_local": self.recv.local.data_ptr(),
-                "ld_recv": self.ld, "flag_peer": [self.flags.peer_ptrs[g] for g in self.group],
+                "flag_peer": [self.flags.peer_ptrs[g] for g in self.group],
                 "flag_local": self.flags.local.data_ptr()}
 
 
@@ -182,7 +197,9 @@ def tile_order(M: int, N: int, *, ga: dict | None = None, gb: dict | None = None
 
 
 def chunk_order(ga: dict | None, gb: dict | None) -> list[int]:
-    """Copy order of the remote chunks: nearest owner first, operands interleaved."""
+    """Copy work items (``operand << 31 | chunk << 12 | piece``) of the remote chunks:
+    nearest owner first, operands interleaved, a chunk's pieces consecutive (so the
+    copy warps of many CTAs finish each chunk together)."""
     out = []
     rmax = max(g["nranks"] for g in (ga, gb) if g is not None) if (ga or gb) else 1
     for d in range(1, rmax):
@@ -191,7 +208,9 @@ def chunk_order(ga: dict | None, gb: dict | None) -> list[int]:
                 continue
             owner = (g["my"] + d) % g["nranks"]
             per = g["rows_per_rank"] // g["chunk_rows"]
-            out.extend((op << 24) | c for c in range(owner * per, (owner + 1) * per))
+            pieces = g.get("pieces", 1)
+            for c in range(owner * per, (owner + 1) * per):
+                out.extend(((op << 31) | (c << 12) | k) - (1 << 32 if op else 0) for k in range(pieces))
     return out
 
 

@@ -5,7 +5,10 @@ over TP pairs with the all-gather / reduce-scatter inside the GEMMs, FSDP
 weights gathered inside the GEMMs).  Every rank then rebuilds the logical
 model (gathering shards), runs ``DCNTorch`` in fp32 on the concatenation of
 all ranks' batches, and compares the loss and every gradient (relative
-Frobenius error).  Prints ``DCN_OK`` on success.
+Frobenius error).  Then one optimizer step runs (FSDP reduce-scatter + AdamW
+fused, ZeRO-1 for the replicated parameters) and every updated weight is
+compared with the fp32 AdamW update of the gathered gradients (max error in
+units of the learning rate).  Prints ``DCN_OK`` on success.
 
     python -m flare_b200.testing.dcn_check                       # 1 GPU
     python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 \\
@@ -23,6 +26,7 @@ from flare_b200.data.synthetic import DLRMSyntheticData
 from flare_b200.models.dcn import DCN, DCNConfig, DCNTorch, dcn_benchmark_tables
 from flare_b200.parallel.dist import init_distributed, shutdown
 from flare_b200.testing.dist_dlrm_check import concat_batches
+from flare_b200.training.flat import adam_reference
 
 VOCABS = [300, 5000, 64, 2000]
 
@@ -121,6 +125,20 @@ def run(m: int = 128, deep=(256, 256), rank_dim: int = 64, dim: int = 64, tol: f
     for k, g in ref_grads.items():
         errs[k] = _rel(grads[k], g)
     errs["pooled"] = _rel(dpooled[:, :cfg.emb_width], pooled.grad)
+    # ---- optimizer step: fused reduce-scatter + AdamW (FSDP and ZeRO-1 shards) vs
+    # the fp32 reference update applied to the gathered gradients
+    op = cfg.dense_optimizer.kernel_params(1)
+    model.emb.backward()
+    model.dense.apply()
+    for w in model.fsdp_weights:
+        w.apply(model.dense.step)
+    torch.cuda.synchronize()
+    model.check()
+    after = model.logical_weights()
+    for k, w0 in logical.items():
+        w = w0.clone().float()
+        adam_reference(w, grads[k].float().cpu(), torch.zeros_like(w), torch.zeros_like(w), op)
+        errs["step:" + k] = float((after[k] - w).abs().max()) / (op["lr"] + 1e-12)
     bad = {k: v for k, v in errs.items() if not v < tol}
     print(f"[rank{rank}] world={world} tp={tp} loss={loss:.6f} ref={ref_l:.6f} "
           + " ".join(f"{k}={v:.2e}" for k, v in errs.items()), flush=True)

@@ -1,4 +1,4 @@
-"""Public training API for the fused DLRM path.
+"""Public training API for the fused models (DLRM, DCN-v2).
 
 ``DLRMTrainer.train_step(batch)`` is the call a user makes: it copies the
 step's inputs from (pinned) host memory to the device, runs the fused training
@@ -33,24 +33,20 @@ class StepResult:
     step: int
 
 
-class DLRMTrainer:
-    def __init__(self, cfg: DLRMConfig, batch_size: int, *, max_bag_size: int, rank: int = 0, world_size: int = 1,
-                 device: torch.device | None = None, seed: int = 0, use_graph: bool = True,
-                 values_capacity: int | None = None, heap_bytes: int | None = None):
-        self.device = device or torch.device("cuda", torch.cuda.current_device())
+class FusedTrainer:
+    """Step driver shared by the fused models (``DLRM``, ``DCN``).
+
+    The model provides ``set_batch``, ``train_step`` (one optimizer step on
+    static buffers, returning the device loss sum), ``loss_sum``, ``dense``
+    and ``emb`` (whose host step mirrors advance once per step) and ``check``.
+    """
+
+    def __init__(self, model, batch_size: int, *, device: torch.device, rank: int = 0, world_size: int = 1,
+                 use_graph: bool = True):
+        self.device = device
         self.rank, self.world = rank, world_size
         self.B = batch_size
-        heap = None
-        if world_size > 1:
-            cap = values_capacity or len(cfg.tables) * batch_size * max_bag_size
-            total_dim = sum(t.embedding_dim for t in cfg.tables)
-            exchange = 4 * (len(cfg.tables) * batch_size + 1) + 4 * cap + 2 * 2 * batch_size * total_dim
-            dense = 6 * 16 * 1024 * 1024  # flat fp32 grads + bf16 params for up to 16M parameters
-            need = heap_bytes or (exchange + dense + 64 * 1024 * 1024)
-            heap = SymmetricHeap(need, rank=rank, world_size=world_size, device=self.device)
-        self.heap = heap
-        self.model = DLRM(cfg, batch_size, max_bag_size=max_bag_size, rank=rank, world_size=world_size,
-                          device=self.device, heap=heap, seed=seed, values_capacity=values_capacity)
+        self.model = model
         self.use_graph = use_graph
         self.graph: torch.cuda.CUDAGraph | None = None
         self.launches_per_step: int | None = None
@@ -69,6 +65,7 @@ class DLRMTrainer:
             # rank can enter a fused kernel that waits on its peers
             torch.cuda.synchronize(self.device)
             barrier()
+
 
     # ---------------------------------------------------------------- graph
     EAGER_STEPS = 2  # steps run eagerly (module load, allocator warm-up) before capture
@@ -171,4 +168,38 @@ class DLRMTrainer:
         torch.cuda.synchronize(self.device)
 
 
-__all__ = ["DLRMTrainer", "StepResult"]
+class DLRMTrainer(FusedTrainer):
+    def __init__(self, cfg: DLRMConfig, batch_size: int, *, max_bag_size: int, rank: int = 0, world_size: int = 1,
+                 device: torch.device | None = None, seed: int = 0, use_graph: bool = True,
+                 values_capacity: int | None = None, heap_bytes: int | None = None):
+        device = device or torch.device("cuda", torch.cuda.current_device())
+        heap = None
+        if world_size > 1:
+            cap = values_capacity or len(cfg.tables) * batch_size * max_bag_size
+            total_dim = sum(t.embedding_dim for t in cfg.tables)
+            exchange = 4 * (len(cfg.tables) * batch_size + 1) + 4 * cap + 2 * 2 * batch_size * total_dim
+            dense = 6 * 16 * 1024 * 1024  # flat fp32 grads + bf16 params for up to 16M parameters
+            need = heap_bytes or (exchange + dense + 64 * 1024 * 1024)
+            heap = SymmetricHeap(need, rank=rank, world_size=world_size, device=device)
+        self.heap = heap
+        model = DLRM(cfg, batch_size, max_bag_size=max_bag_size, rank=rank, world_size=world_size,
+                     device=device, heap=heap, seed=seed, values_capacity=values_capacity)
+        super().__init__(model, batch_size, device=device, rank=rank, world_size=world_size, use_graph=use_graph)
+
+
+class DCNTrainer(FusedTrainer):
+    """Public training API of the fused DCN-v2 (tensor-parallel x FSDP) model."""
+
+    def __init__(self, cfg, batch_size: int, *, max_bag_size: int, rank: int = 0, world_size: int = 1,
+                 device: torch.device | None = None, seed: int = 0, use_graph: bool = True,
+                 values_capacity: int | None = None):
+        from ..models.dcn import DCN
+
+        device = device or torch.device("cuda", torch.cuda.current_device())
+        model = DCN(cfg, batch_size, max_bag_size=max_bag_size, rank=rank, world_size=world_size, device=device,
+                    seed=seed, values_capacity=values_capacity)
+        self.heap = model.heap
+        super().__init__(model, batch_size, device=device, rank=rank, world_size=world_size, use_graph=use_graph)
+
+
+__all__ = ["DCNTrainer", "DLRMTrainer", "FusedTrainer", "StepResult"]

@@ -117,12 +117,36 @@ def test_persistent_gemm_epilogues(ctx, cuda):
 
 
 def _gather_spec(full_local, full_peer, my, S, cols, chunk_rows, ready):
+    from flare_b200.ops.dist_gemm import _pieces
+
     src = [None, None]
     src[my] = full_local.data_ptr()
     src[1 - my] = full_peer.data_ptr()
+    done = torch.zeros_like(ready)
+    _KEEP.append(done)
+    pieces, per = _pieces(chunk_rows, cols)
     return {"nranks": 2, "my": my, "src": src, "dst": full_local.data_ptr(), "ld": full_local.stride(0),
             "rows_per_rank": S, "row_elems": (cols + 7) // 8 * 8, "chunk_rows": chunk_rows,
-            "ready": ready.data_ptr()}
+            "pieces": pieces, "piece_vecs": per, "ready": ready.data_ptr(), "done": done.data_ptr()}
+
+
+_KEEP = []
+
+
+def _to_blocks(part, n_tiles):
+    """[S, N] partial -> the reduce-scatter receive layout (per tile, quarter, 32-column chunk:
+    element (r, 8q+e) of the 32 x 32 block at q*256 + r*8 + e)."""
+    S, N = part.shape
+    padded = torch.zeros(S, n_tiles * BN, dtype=part.dtype, device=part.device)
+    padded[:, :N] = part
+    x = padded.view(S // 128, 4, 32, n_tiles, 8, 4, 8)        # mt, quarter, r, nt, chunk, q, e
+    x = x.permute(0, 3, 1, 4, 5, 2, 6).contiguous()           # mt, nt, quarter, chunk, q, r, e
+    return x.view(-1)
+
+
+def _from_blocks(flat, S, N, n_tiles):
+    x = flat.view(S // 128, n_tiles, 4, 8, 4, 32, 8).permute(0, 2, 5, 1, 3, 4, 6).contiguous()
+    return x.view(S, n_tiles * BN)[:, :N]
 
 
 @pytest.mark.parametrize("my", [0, 1])
@@ -181,19 +205,19 @@ def test_reduce_scatter_rows(ctx, cuda):
     a, b = _rand(M, K, cuda), _rand(N, K, cuda)
     bias = torch.randn(N, device=cuda).to(torch.bfloat16)
     my = 1
-    ld = (N + 7) // 8 * 8
     n_tiles = (N + BN - 1) // BN
     tiles_per_rank = (S // 128) * n_tiles
-    recv_local = torch.zeros(2, S, ld, dtype=torch.bfloat16, device=cuda)
-    recv_peer = torch.zeros(2, S, ld, dtype=torch.bfloat16, device=cuda)
-    flags_local = torch.zeros(2 * tiles_per_rank * 4, dtype=torch.int32, device=cuda)
+    blk = tiles_per_rank * 4 * 8 * 1024
+    recv_local = torch.zeros(2 * blk, dtype=torch.bfloat16, device=cuda)
+    recv_peer = torch.zeros(2 * blk, dtype=torch.bfloat16, device=cuda)
+    flags_local = torch.zeros(2 * tiles_per_rank * 8, dtype=torch.int32, device=cuda)
     flags_peer = torch.zeros_like(flags_local)
     peer_partial = _rand(S, N, cuda)  # what rank 0 computed for my rows
-    recv_local[0, :, :N] = peer_partial
+    recv_local[:blk] = _to_blocks(peer_partial, n_tiles)
     epoch = int(ctx.ctl[0].item()) + 1
-    flags_local[:tiles_per_rank * 4] = epoch  # sender 0 -> all my tiles ready
+    flags_local[:tiles_per_rank * 8] = epoch  # sender 0 -> all my tiles ready
     rs = {"nranks": 2, "my": my, "rows_per_rank": S, "recv_peer": [recv_peer.data_ptr(), recv_local.data_ptr()],
-          "recv_local": recv_local.data_ptr(), "ld_recv": ld, "flag_peer": [flags_peer.data_ptr(), flags_local.data_ptr()],
+          "recv_local": recv_local.data_ptr(), "flag_peer": [flags_peer.data_ptr(), flags_local.data_ptr()],
           "flag_local": flags_local.data_ptr()}
     out = torch.empty(S, N, dtype=torch.bfloat16, device=cuda)
     _call(ctx, a, b, out, rs=rs, bias=bias, relu=True)
@@ -201,6 +225,12 @@ def test_reduce_scatter_rows(ctx, cuda):
     mine = torch.relu(full[my * S:(my + 1) * S] + peer_partial.float() + bias.float())
     torch.testing.assert_close(out.float(), mine, rtol=2e-2, atol=1e-1)
     # what was sent to rank 0: my partial of rank 0's rows, flagged
-    torch.testing.assert_close(recv_peer[my, :, :N].float(), full[:S], rtol=2e-2, atol=5e-2)
-    sent = flags_peer[my * tiles_per_rank * 4:(my + 1) * tiles_per_rank * 4]
+    sent_part = _from_blocks(recv_peer[my * blk:(my + 1) * blk], S, N, n_tiles)
+    torch.testing.assert_close(sent_part.float(), full[:S], rtol=2e-2, atol=5e-2)
+    sent = flags_peer[my * tiles_per_rank * 8:(my + 1) * tiles_per_rank * 8]
     assert bool((sent == epoch).all())
+
+
+def test_block_layout_roundtrip(cuda):
+    x = torch.randn(256, 520, device=cuda)
+    assert torch.equal(_from_blocks(_to_blocks(x, 3), 256, 520, 3), x)

@@ -30,10 +30,19 @@ def test_tile_order_reduce_scatter_sends_first():
 def test_chunk_order_only_remote_nearest_first():
     ga = _g(4, 1, 256, 64)
     gb = _g(2, 0, 512, 128)
-    chunks = chunk_order(ga, gb)
-    a = [c & 0xFFFFFF for c in chunks if c >> 24 == 0]
-    b = [c & 0xFFFFFF for c in chunks if c >> 24 == 1]
+    gb["pieces"] = 3
+    items = [c & 0xFFFFFFFF for c in chunk_order(ga, gb)]
+    a = [(c >> 12) & 0x7FFFF for c in items if c >> 31 == 0]
+    b = [((c >> 12) & 0x7FFFF, c & 0xFFF) for c in items if c >> 31 == 1]
     per_a = 256 // 64
     assert a == list(range(2 * per_a, 3 * per_a)) + list(range(3 * per_a, 4 * per_a)) + list(range(0, per_a))
-    assert b == list(range(4, 8))
+    assert b == [(c, k) for c in range(4, 8) for k in range(3)]
     assert chunk_order(None, None) == []
+
+
+def test_piece_split_covers_chunk():
+    from flare_b200.ops.dist_gemm import _pieces
+
+    for rows, cols in ((128, 6669), (64, 512), (128, 4096), (2, 8), (128, 65536)):
+        n, per = _pieces(rows, cols)
+        assert n <= 4096 and n * per >= rows * ((cols + 7) // 8) > (n - 1) * per
