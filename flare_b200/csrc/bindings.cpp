@@ -6,6 +6,7 @@
 #include <pybind11/stl.h>
 
 #include "common.cuh"
+#include "attention.cuh"
 #include "dcn.cuh"
 #include "dense.cuh"
 #include "embedding.cuh"
@@ -399,6 +400,52 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.status = P<int>(get_or<uintptr_t>(d, "status", 0));
     p.timeout_ns = get_or<uint64_t>(d, "timeout_ns", 2000000000ull);
     flare::adam_dp_fused(p, cur_stream());
+  });
+
+  m.def("attn_forward", [](const py::dict& d) {
+    flare::AttnFwdParams p{};
+    p.qkv = P<const void>(get<uintptr_t>(d, "qkv"));
+    p.ld_qkv = get<int64_t>(d, "ld_qkv");
+    p.vt = P<const void>(get<uintptr_t>(d, "vt"));
+    p.ld_vt = get<int64_t>(d, "ld_vt");
+    p.offsets = P<const int>(get<uintptr_t>(d, "offsets"));
+    p.nseq = get<int>(d, "nseq");
+    p.max_len = get<int>(d, "max_len");
+    p.T_cap = get<int64_t>(d, "T_cap");
+    p.scale = get<float>(d, "scale");
+    p.out = P<__nv_bfloat16>(get<uintptr_t>(d, "out"));
+    p.ld_out = get<int64_t>(d, "ld_out");
+    p.lse = P<float>(get<uintptr_t>(d, "lse"));
+    p.ld_lse = get<int64_t>(d, "ld_lse");
+    p.status = P<int>(get<uintptr_t>(d, "status"));
+    p.timeout_ns = get<uint64_t>(d, "timeout_ns");
+    flare::attn_forward(p, cur_stream());
+  });
+  m.def("attn_backward", [](const py::dict& d) {
+    flare::AttnBwdParams p{};
+    p.qkv = P<const void>(get<uintptr_t>(d, "qkv"));
+    p.ld_qkv = get<int64_t>(d, "ld_qkv");
+    p.dout = P<const void>(get<uintptr_t>(d, "dout"));
+    p.out = P<const void>(get<uintptr_t>(d, "out"));
+    p.ld_do = get<int64_t>(d, "ld_do");
+    p.dout_t = P<const void>(get<uintptr_t>(d, "dout_t"));
+    p.q_t = P<const void>(get<uintptr_t>(d, "q_t"));
+    p.ld_t = get<int64_t>(d, "ld_t");
+    p.offsets = P<const int>(get<uintptr_t>(d, "offsets"));
+    p.nseq = get<int>(d, "nseq");
+    p.max_len = get<int>(d, "max_len");
+    p.T_cap = get<int64_t>(d, "T_cap");
+    p.scale = get<float>(d, "scale");
+    p.lse = P<const float>(get<uintptr_t>(d, "lse"));
+    p.delta = P<float>(get<uintptr_t>(d, "delta"));
+    p.ld_stat = get<int64_t>(d, "ld_stat");
+    p.dq_acc = P<float>(get<uintptr_t>(d, "dq_acc"));
+    p.ld_dq = get<int64_t>(d, "ld_dq");
+    p.dqkv = P<__nv_bfloat16>(get<uintptr_t>(d, "dqkv"));
+    p.ld_dqkv = get<int64_t>(d, "ld_dqkv");
+    p.status = P<int>(get<uintptr_t>(d, "status"));
+    p.timeout_ns = get<uint64_t>(d, "timeout_ns");
+    flare::attn_backward(p, cur_stream());
   });
 
   m.def("dcn_concat_x0", [](uintptr_t pooled, int64_t ldp, uintptr_t dense, int nd, int64_t B, int E, uintptr_t x0,
