@@ -11,6 +11,7 @@
 #include "dense.cuh"
 #include "embedding.cuh"
 #include "gemm.cuh"
+#include "seqrec.cuh"
 #include "sparse_ops.cuh"
 
 namespace flare {
@@ -446,6 +447,50 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.status = P<int>(get<uintptr_t>(d, "status"));
     p.timeout_ns = get<uint64_t>(d, "timeout_ns");
     flare::attn_backward(p, cur_stream());
+  });
+
+  m.def("seq_embed_combine", [](uintptr_t pooled, int64_t ldp, int64_t T, uintptr_t x, int64_t ldx) {
+    flare::seq_embed_combine(P<const __nv_bfloat16>(pooled), ldp, T, P<__nv_bfloat16>(x), ldx, cur_stream());
+  });
+  m.def("seq_layernorm_fwd", [](uintptr_t x, int64_t ldx, int64_t T, uintptr_t gamma, uintptr_t beta, float eps,
+                                uintptr_t y, int64_t ldy, uintptr_t mean, uintptr_t rstd) {
+    flare::seq_layernorm_fwd(P<const __nv_bfloat16>(x), ldx, T, P<const __nv_bfloat16>(gamma),
+                             P<const __nv_bfloat16>(beta), eps,
+                             P<__nv_bfloat16>(y), ldy, P<float>(mean), P<float>(rstd), cur_stream());
+  });
+  m.def("seq_layernorm_bwd", [](uintptr_t dy, int64_t lddy, uintptr_t x, int64_t ldx, int64_t T, uintptr_t gamma,
+                                uintptr_t mean, uintptr_t rstd, uintptr_t resid, int64_t ldr, uintptr_t dx,
+                                int64_t lddx, uintptr_t dgamma, uintptr_t dbeta) {
+    flare::seq_layernorm_bwd(P<const __nv_bfloat16>(dy), lddy, P<const __nv_bfloat16>(x), ldx, T,
+                             P<const __nv_bfloat16>(gamma), P<const float>(mean), P<const float>(rstd),
+                             P<const __nv_bfloat16>(resid), ldr, P<__nv_bfloat16>(dx), lddx, P<float>(dgamma),
+                             P<float>(dbeta), cur_stream());
+  });
+  m.def("seq_sampled_softmax", [](const py::dict& d) {
+    flare::SampledSoftmaxParams p{};
+    p.y = P<const __nv_bfloat16>(get<uintptr_t>(d, "y"));
+    p.ldy = get<int64_t>(d, "ldy");
+    p.emb = P<const __nv_bfloat16>(get<uintptr_t>(d, "emb"));
+    p.ldemb = get<int64_t>(d, "ldemb");
+    p.target_row = P<const int>(get<uintptr_t>(d, "target_row"));
+    p.logits = P<const float>(get<uintptr_t>(d, "logits"));
+    p.ldlog = get<int64_t>(d, "ldlog");
+    p.T = get<int64_t>(d, "T");
+    p.N = get<int>(d, "N");
+    p.num_valid = P<const int>(get<uintptr_t>(d, "num_valid"));
+    p.dneg = P<__nv_bfloat16>(get<uintptr_t>(d, "dneg"));
+    p.lddneg = get<int64_t>(d, "lddneg");
+    p.dy = P<__nv_bfloat16>(get<uintptr_t>(d, "dy"));
+    p.lddy = get<int64_t>(d, "lddy");
+    p.dpos = P<float>(get<uintptr_t>(d, "dpos"));
+    p.loss_sum = P<float>(get<uintptr_t>(d, "loss_sum"));
+    flare::seq_sampled_softmax(p, cur_stream());
+  });
+  m.def("seq_embed_grad_split", [](uintptr_t dx, int64_t lddx, uintptr_t y, int64_t ldy, uintptr_t dpos,
+                                   uintptr_t target_row, int64_t T, uintptr_t grad, int64_t ldg) {
+    flare::seq_embed_grad_split(P<const __nv_bfloat16>(dx), lddx, P<const __nv_bfloat16>(y), ldy,
+                                P<const float>(dpos), P<const int>(target_row), T, P<__nv_bfloat16>(grad), ldg,
+                                cur_stream());
   });
 
   m.def("dcn_concat_x0", [](uintptr_t pooled, int64_t ldp, uintptr_t dense, int nd, int64_t B, int E, uintptr_t x0,

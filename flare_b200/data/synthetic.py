@@ -126,3 +126,87 @@ class SmallSyntheticData:
 
 __all__ = ["DLRMSyntheticData", "SCRAMBLE", "SmallSyntheticData", "SparseBatch", "log_uniform_vocab_sizes",
            "make_jagged", "zipf_ids"]
+
+
+@dataclass
+class SeqBatch:
+    """Packed jagged sequences for the sequential model (one rank's share).
+
+    ``seq_offsets`` [nseq+1] token offsets (each sequence padded at its end to a
+    multiple of 8); ``target_row`` [T_cap] = row of token t+1 when token t has a
+    next item in its sequence, else -1; the embedding KJT (``emb_offsets``
+    [F*(T_cap+N)+1] feature-major, ``emb_values``) has one bag per token (item,
+    4 side features; empty for padding) followed by N rows holding the shared
+    negative item ids; ``num_valid`` = tokens with a target over ALL ranks.
+    """
+
+    seq_offsets: torch.Tensor
+    target_row: torch.Tensor
+    emb_offsets: torch.Tensor
+    emb_values: torch.Tensor
+    num_valid: torch.Tensor  # int32 [1]
+    tokens: int              # packed tokens (<= T_cap) of this rank
+
+    def to(self, device, non_blocking: bool = False) -> "SeqBatch":
+        return SeqBatch(*(t.to(device, non_blocking=non_blocking) for t in
+                          (self.seq_offsets, self.target_row, self.emb_offsets, self.emb_values, self.num_valid)),
+                        self.tokens)
+
+    def pin_memory(self) -> "SeqBatch":
+        return SeqBatch(*(t.pin_memory() for t in (self.seq_offsets, self.target_row, self.emb_offsets,
+                                                     self.emb_values, self.num_valid)), self.tokens)
+
+
+class SeqSyntheticData:
+    """Jagged user histories: lengths ~ U[min_len, max_len], items Zipf(s) over ``item_rows``,
+    4 side features per token Zipf over ``side_rows``; ``negatives`` shared uniform negatives per step."""
+
+    def __init__(self, nseq: int, *, item_rows: int, side_rows: int = 100_000, num_side: int = 4,
+                 min_len: int = 32, max_len: int = 512, zipf_s: float = 1.1, negatives: int = 512,
+                 T_cap: int | None = None, seed: int = 0, rank: int = 0, world: int = 1, device="cpu"):
+        self.nseq, self.item_rows, self.side_rows, self.num_side = nseq, item_rows, side_rows, num_side
+        self.min_len, self.max_len, self.zipf_s, self.negatives = min_len, max_len, zipf_s, negatives
+        self.rank, self.world = rank, world
+        self.T_cap = T_cap or nseq * ((max_len + 7) // 8 * 8)
+        self.device = torch.device(device)
+        self.seed = seed
+        self.step = 0
+
+    def _lengths(self, r: int, step: int) -> torch.Tensor:
+        g = torch.Generator().manual_seed((self.seed * 1000 + r) * 100003 + step)
+        return torch.randint(self.min_len, self.max_len + 1, (self.nseq,), generator=g)
+
+    def next(self) -> SeqBatch:
+        step = self.step
+        self.step += 1
+        lens = self._lengths(self.rank, step)
+        # the loss mean runs over every rank's tokens: all ranks derive the same count
+        num_valid = sum(int((self._lengths(r, step) - 1).sum()) for r in range(self.world))
+        padded = (lens + 7) // 8 * 8
+        offs = torch.zeros(self.nseq + 1, dtype=torch.int64)
+        torch.cumsum(padded, 0, out=offs[1:])
+        T = int(offs[-1])
+        if T > self.T_cap:
+            raise ValueError(f"{T} packed tokens exceed the capacity {self.T_cap}")
+        g = torch.Generator(device=self.device).manual_seed((self.seed * 1000 + self.rank) * 7919 + step)
+        pos = torch.arange(self.T_cap, dtype=torch.int64)
+        seq_id = torch.searchsorted(offs[1:], pos, right=True).clamp(max=self.nseq - 1)
+        within = pos - offs[seq_id]
+        valid = (pos < T) & (within < lens[seq_id])
+        has_next = valid & (within + 1 < lens[seq_id])
+        target = torch.where(has_next, pos + 1, torch.full_like(pos, -1)).to(torch.int32)
+        n_tok = int(valid.sum())
+        B = self.T_cap + self.negatives
+        F = 1 + self.num_side
+        items = zipf_ids(n_tok, self.item_rows, self.zipf_s, g, self.device)
+        sides = [zipf_ids(n_tok, self.side_rows, self.zipf_s, g, self.device) for _ in range(self.num_side)]
+        negs = torch.randint(0, self.item_rows, (self.negatives,), generator=g, device=self.device, dtype=torch.int32)
+        tok_len = valid.to(torch.int32).to(self.device)
+        item_len = torch.cat([tok_len, torch.ones(self.negatives, dtype=torch.int32, device=self.device)])
+        side_len = torch.cat([tok_len, torch.zeros(self.negatives, dtype=torch.int32, device=self.device)])
+        lengths = torch.cat([item_len] + [side_len] * self.num_side)
+        emb_off = torch.zeros(F * B + 1, dtype=torch.int32, device=self.device)
+        torch.cumsum(lengths, 0, out=emb_off[1:])
+        values = torch.cat([items, negs] + sides)
+        return SeqBatch(offs.to(torch.int32).to(self.device), target.to(self.device), emb_off, values,
+                        torch.tensor([num_valid], dtype=torch.int32, device=self.device), T)

@@ -150,7 +150,9 @@ class DenseState:
         for e in self.params.entries.values():
             if e.init == "zeros":
                 continue
-            if e.init == "uniform":
+            if e.init == "ones":
+                vals = torch.ones(e.numel)
+            elif e.init == "uniform":
                 vals = (torch.rand(e.numel, generator=g) * 2 - 1) * e.init_scale
             elif e.init == "normal":
                 vals = torch.randn(e.numel, generator=g) * e.init_scale

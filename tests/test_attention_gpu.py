@@ -59,9 +59,3 @@ def test_backward_matches_autograd(cuda, lengths):
         err = (got[:, sl] - g[:, sl]).norm() / g[:, sl].norm()
         assert err < 3e-2, f"{name} relative error {err:.3e}"
     assert float(buf.dq_acc.abs().max()) == 0.0  # workspace left zeroed for the next call
-
-
-def test_pack_offsets_alignment():
-    o, valid = pack_offsets([3, 9, 8, 1])
-    assert o.tolist() == [0, 8, 24, 32, 40]
-    assert valid.sum().item() == 21 and valid[:3].all() and not valid[3:8].any()
