@@ -202,4 +202,85 @@ class DCNTrainer(FusedTrainer):
         super().__init__(model, batch_size, device=device, rank=rank, world_size=world_size, use_graph=use_graph)
 
 
-__all__ = ["DCNTrainer", "DLRMTrainer", "FusedTrainer", "StepResult"]
+class SeqRecTrainer(FusedTrainer):
+    """Public training API of the fused sequential-recommendation model (inputs: ``SeqBatch``)."""
+
+    def __init__(self, cfg, nseq: int, T_cap: int, *, rank: int = 0, world_size: int = 1,
+                 device: torch.device | None = None, seed: int = 0, use_graph: bool = True,
+                 values_capacity: int | None = None):
+        from ..models.seqrec import SeqRec
+
+        device = device or torch.device("cuda", torch.cuda.current_device())
+        model = SeqRec(cfg, nseq, T_cap, rank=rank, world_size=world_size, device=device, seed=seed,
+                       values_capacity=values_capacity)
+        self.heap = model.heap
+        super().__init__(model, nseq, device=device, rank=rank, world_size=world_size, use_graph=use_graph)
+        self._seq_stage = None
+        self._nv = [1, 1]  # global token count of the step whose loss sits in each loss slot
+
+    @staticmethod
+    def _loss(v: float, num_valid: int) -> float:
+        # loss_sum is this rank's sum of token losses; report it per token of the step's global count
+        return v / max(float(num_valid), 1.0)
+
+    def train_step(self, batch) -> StepResult:
+        self.model.set_batch(batch, non_blocking=True)
+        loss = self._run_step()
+        self.steps += 1
+        return StepResult(self._loss(float(loss.item()), int(batch.num_valid.reshape(-1)[0])), self.steps)
+
+    def train_step_async(self, batch) -> StepResult | None:
+        """H2D of ``batch`` on a side stream overlapping the previous step; returns the previous step's loss."""
+        m = self.model
+        cur = torch.cuda.current_stream(self.device)
+        fields = ("seq_offsets", "target_row", "emb_offsets", "emb_values", "num_valid")
+        if self._seq_stage is None:
+            cap = m.emb.values_capacity
+            self._seq_stage = [
+                {f: (torch.empty(cap, dtype=torch.int32, device=self.device) if f == "emb_values"
+                     else torch.empty_like(getattr(batch, f), device=self.device)) for f in fields}
+                for _ in range(2)]
+        idx = self._stage_idx
+        st = self._seq_stage[idx]
+        self._stage_idx ^= 1
+        with torch.cuda.stream(self.copy_stream):
+            if self._stage_used[idx]:
+                self.copy_stream.wait_event(self._stage_free[idx])
+            for f in fields:
+                src = getattr(batch, f)
+                st[f][:src.numel()].copy_(src, non_blocking=True)
+            self._copy_done.record(self.copy_stream)
+        prev = None
+        if self._pending:
+            ev = self._loss_event[self.steps % 2]
+            ev.synchronize()
+            prev = StepResult(self._loss(float(self._loss_host[self.steps % 2]), self._nv[self.steps % 2]),
+                              self.steps)
+        cur.wait_event(self._copy_done)
+        from ..data.synthetic import SeqBatch
+
+        staged = SeqBatch(st["seq_offsets"], st["target_row"], st["emb_offsets"],
+                          st["emb_values"][:batch.emb_values.numel()], st["num_valid"], batch.tokens)
+        m.set_batch(staged, non_blocking=True)
+        self._stage_free[idx].record(cur)
+        self._stage_used[idx] = True
+        loss = self._run_step()
+        self.steps += 1
+        slot = self.steps % 2
+        self._nv[slot] = int(batch.num_valid.reshape(-1)[0])
+        self._loss_host[slot:slot + 1].copy_(loss, non_blocking=True)
+        self._loss_event[slot].record(cur)
+        self._pending = True
+        return prev
+
+    def flush(self) -> StepResult | None:
+        if not self._pending:
+            return None
+        slot = self.steps % 2
+        self._loss_event[slot].synchronize()
+        self._pending = False
+        return StepResult(self._loss(float(self._loss_host[slot]), self._nv[slot]), self.steps)
+
+
+
+__all__ = ["DCNTrainer", "DLRMTrainer", "FusedTrainer", "SeqRecTrainer", "StepResult"]
