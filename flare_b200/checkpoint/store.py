@@ -110,6 +110,8 @@ def save_sparse(dirpath: Path, coll, step: int, *, mode: str = "full", base_step
     if mode == "incremental" and base_step is None:
         raise ValueError("an incremental save needs the step it builds on")
     rank, world = _rank_world()
+    if any(s.slot_map_off >= 0 for s in coll.shards):
+        raise NotImplementedError("host-tier tables are checkpointed from their host copy (HostTier.export_state)")
     dirpath.mkdir(parents=True, exist_ok=True)
     for i, s in enumerate(coll.shards):
         fields = coll.shard_fields(i)

@@ -11,6 +11,7 @@
 #include "dense.cuh"
 #include "embedding.cuh"
 #include "gemm.cuh"
+#include "host_tier.cuh"
 #include "seqrec.cuh"
 #include "sparse_ops.cuh"
 
@@ -251,6 +252,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.w_dtype = get<int>(d, "w_dtype");
     p.out_dtype = get_or<int>(d, "out_dtype", kBF16);
     p.vec = get_or<int>(d, "vec", 1);
+    p.slot_map = P<const int>(get_or<uintptr_t>(d, "slot_map", 0));
     p.stage_ids = P<int>(get<uintptr_t>(d, "stage_ids"));
     p.stage_bag = P<int>(get<uintptr_t>(d, "stage_bag"));
     p.stage_count = P<int>(get<uintptr_t>(d, "stage_count"));
@@ -492,6 +494,28 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                                 P<const float>(dpos), P<const int>(target_row), T, P<__nv_bfloat16>(grad), ldg,
                                 cur_stream());
   });
+
+  auto parse_tier = [](const py::dict& d) {
+    flare::TierCopyParams p{};
+    p.n = get<int>(d, "n");
+    p.ncols = get<int>(d, "ncols");
+    p.slots = P<const int>(get<uintptr_t>(d, "slots"));
+    p.cache_w = P<float>(get<uintptr_t>(d, "cache_w"));
+    p.cache_row = P<float>(get_or<uintptr_t>(d, "cache_row", 0));
+    p.cache_m = P<float>(get_or<uintptr_t>(d, "cache_m", 0));
+    p.cache_v = P<float>(get_or<uintptr_t>(d, "cache_v", 0));
+    p.stage_w = P<float>(get<uintptr_t>(d, "stage_w"));
+    p.stage_row = P<float>(get_or<uintptr_t>(d, "stage_row", 0));
+    p.stage_m = P<float>(get_or<uintptr_t>(d, "stage_m", 0));
+    p.stage_v = P<float>(get_or<uintptr_t>(d, "stage_v", 0));
+    p.slot_map = P<int>(get_or<uintptr_t>(d, "slot_map", 0));
+    p.new_rows = P<const int64_t>(get_or<uintptr_t>(d, "new_rows", 0));
+    p.evict_rows = P<const int64_t>(get_or<uintptr_t>(d, "evict_rows", 0));
+    p.n_evict = get_or<int>(d, "n_evict", 0);
+    return p;
+  };
+  m.def("tier_gather", [parse_tier](const py::dict& d) { flare::tier_gather(parse_tier(d), cur_stream()); });
+  m.def("tier_install", [parse_tier](const py::dict& d) { flare::tier_install(parse_tier(d), cur_stream()); });
 
   m.def("dcn_concat_x0", [](uintptr_t pooled, int64_t ldp, uintptr_t dense, int nd, int64_t B, int E, uintptr_t x0,
                             int64_t ld0) {

@@ -138,9 +138,18 @@ __global__ void __launch_bounds__(kEmbThreads) emb_fwd_kernel(EmbFwdParams p) {
         const bool has = active && j + l < len;
         if (has) {
           myid = vals[beg + j + l];
-          if (myid >= d.rows) {
+          if (myid < 0 || myid >= d.id_rows) {
             report_error(p.status, kIndexOutOfRange, d.feature);
             myid = -1;
+          } else if (d.slot_map_off >= 0) {
+            // host-tier table: the id's row must have been made resident in an HBM slot
+            const int slot = p.slot_map[d.slot_map_off + myid];
+            if (slot < 0 || slot >= d.rows) {
+              report_error(p.status, kIndexOutOfRange, 1000 + d.feature);
+              myid = -1;
+            } else {
+              myid = slot;
+            }
           }
         }
         if (has && stage_ok) {

@@ -12,11 +12,13 @@ struct ShardDesc {
   int col_begin;       // first table column held by this shard
   int ncols;           // number of columns held (multiple of 4)
   int out_col;         // column of the pooled output row receiving col_begin
-  int64_t rows;        // rows held
+  int64_t rows;        // rows held in HBM (the whole table, or the cache slots of a host-tier table)
   int64_t weight_off;  // element offset of the shard in the weight buffer
   int64_t row_base;    // offset of the shard's first row in per-row arrays
   int pooling;         // 0 = sum, 1 = mean
   int pad_;
+  int64_t id_rows;     // valid ids are [0, id_rows)
+  int64_t slot_map_off;  // >= 0: ids map to HBM rows through slot_map[slot_map_off + id]; -1: id = row
 };
 
 enum SparseOptKind : int {
@@ -63,6 +65,7 @@ struct EmbFwdParams {
   int w_dtype;
   int out_dtype;  // kBF16 or kF32
   int vec;        // float4 vectors per lane: 1 (shard width <= 128) or 2 (<= 256)
+  const int* slot_map;  // row -> HBM slot maps of host-tier shards (ShardDesc::slot_map_off), or null
   // staging for the backward pass
   int* stage_ids;    // [(sh*world+s)*stage_cap + j]
   int* stage_bag;    // same indexing: sample index of occurrence j

@@ -39,9 +39,9 @@ from .precision import TORCH_DTYPES
 _SHARD_DTYPE = np.dtype([
     ("feature", "<i4"), ("col_begin", "<i4"), ("ncols", "<i4"), ("out_col", "<i4"),
     ("rows", "<i8"), ("weight_off", "<i8"), ("row_base", "<i8"),
-    ("pooling", "<i4"), ("pad_", "<i4"),
+    ("pooling", "<i4"), ("pad_", "<i4"), ("id_rows", "<i8"), ("slot_map_off", "<i8"),
 ])
-assert _SHARD_DTYPE.itemsize == 48
+assert _SHARD_DTYPE.itemsize == 64
 
 FLAG_FWD_IN, FLAG_FWD_OUT, FLAG_BWD_IN, NUM_FLAG_ARRAYS = 0, 1, 2, 3
 
@@ -61,6 +61,8 @@ class LocalShard:
     out_col: int
     weight_off: int
     row_base: int
+    storage_rows: int = 0      # rows held in HBM (= num_embeddings, or the cache slots of a host-tier table)
+    slot_map_off: int = -1     # offset of the row -> slot map of a host-tier table, -1 if resident
 
 
 class ShardedEmbeddingBagCollection:
@@ -115,13 +117,20 @@ class ShardedEmbeddingBagCollection:
         self.shards: list[LocalShard] = []
         woff = 0
         rbase = 0
+        smoff = 0
         for p in self.plan.for_rank(rank):
             spec = self.tables[p.table]
+            cached = spec.cache_rows is not None
+            srows = int(spec.cache_rows) if cached else spec.num_embeddings
             self.shards.append(LocalShard(p.table, spec, p.col_begin, p.ncols, self.plan.out_cols[p.table] + p.col_begin,
-                                          woff, rbase))
-            woff += spec.num_embeddings * p.ncols
-            rbase += spec.num_embeddings
+                                          woff, rbase, srows, smoff if cached else -1))
+            woff += srows * p.ncols
+            rbase += srows
+            if cached:
+                smoff += spec.num_embeddings
         self.num_local_elems, self.num_local_rows = woff, rbase
+        # host-tier tables reach their HBM cache slots through a device row -> slot map (-1 = not resident)
+        self.slot_map = torch.full((max(smoff, 1),), -1, dtype=torch.int32, device=self.device) if smoff else None
         self.ncols_max = max([s.ncols for s in self.shards], default=4)
         self.vec = 2 if self.ncols_max > 128 else 1
         for s in self.shards:
@@ -132,14 +141,15 @@ class ShardedEmbeddingBagCollection:
         desc = np.zeros(max(len(self.shards), 1), dtype=_SHARD_DTYPE)
         for i, s in enumerate(self.shards):
             desc[i] = (self.features.index(s.spec.feature_name), s.col_begin, s.ncols, s.out_col,
-                       s.spec.num_embeddings, s.weight_off, s.row_base, 1 if s.spec.pooling == "mean" else 0, 0)
+                       s.storage_rows, s.weight_off, s.row_base, 1 if s.spec.pooling == "mean" else 0, 0,
+                       s.spec.num_embeddings, s.slot_map_off)
         self.shard_desc = torch.from_numpy(desc.view(np.uint8).copy()).to(dev)
 
         # ---- parameters and optimizer state (local HBM) ----
         self.weights = torch.empty(max(woff, 4), dtype=self.value_dtype, device=dev)
         if init:
             for s in self.shards:
-                n = s.spec.num_embeddings * s.ncols
+                n = s.storage_rows * s.ncols
                 view = self.weights[s.weight_off:s.weight_off + n]
                 stream_seed = (seed * 1_000_003 + s.table * 7919) & 0x7FFFFFFF
                 init_uniform_(view, -s.spec.init_scale, s.spec.init_scale, stream_seed, ncols=s.ncols,
@@ -247,6 +257,7 @@ class ShardedEmbeddingBagCollection:
             peer_values=self._peer["values"].data_ptr(), peer_out=self._peer["out"].data_ptr(),
             out_stride=self.total_dim, weights=self.weights.data_ptr(), w_dtype=dtype_code(self.value_dtype),
             out_dtype=dtype_code(self.out_dtype), vec=self.vec, stage_ids=self.stage_ids.data_ptr(),
+            slot_map=self.slot_map.data_ptr() if self.slot_map is not None else 0,
             stage_bag=self.stage_bag.data_ptr(), stage_count=self.stage_count.data_ptr(),
             stage_len=self.stage_len.data_ptr(), stage_cap=self.stage_cap,
             flags_local=self.flags.local_ptr, peer_flags=self.flags.peer_ptrs.data_ptr(),
@@ -310,20 +321,21 @@ class ShardedEmbeddingBagCollection:
 
     # ------------------------------------------------------------ state I/O
     def shard_view(self, i: int) -> torch.Tensor:
+        """HBM rows of shard i (the whole table, or the cache slots of a host-tier table)."""
         s = self.shards[i]
-        n = s.spec.num_embeddings * s.ncols
-        return self.weights[s.weight_off:s.weight_off + n].view(s.spec.num_embeddings, s.ncols)
+        n = s.storage_rows * s.ncols
+        return self.weights[s.weight_off:s.weight_off + n].view(s.storage_rows, s.ncols)
 
     def row_state_view(self, i: int) -> torch.Tensor | None:
         if self.state_row is None:
             return None
         s = self.shards[i]
-        return self.state_row[s.row_base:s.row_base + s.spec.num_embeddings]
+        return self.state_row[s.row_base:s.row_base + s.storage_rows]
 
     def shard_fields(self, i: int) -> dict[str, torch.Tensor]:
         """Device views of shard i: weight [rows, ncols] and optimizer state."""
         s = self.shards[i]
-        rows, n = s.spec.num_embeddings, s.spec.num_embeddings * s.ncols
+        rows, n = s.storage_rows, s.storage_rows * s.ncols
         out = {"weight": self.shard_view(i)}
         if self.state_row is not None:
             out["state_row"] = self.state_row[s.row_base:s.row_base + rows]
@@ -342,13 +354,13 @@ class ShardedEmbeddingBagCollection:
             entry = {"weight": self.shard_view(i).cpu(), "ncols": s.ncols}
             if self.state_row is not None:
                 entry["state_row"] = self.row_state_view(i).cpu()
-            n = s.spec.num_embeddings * s.ncols
+            n = s.storage_rows * s.ncols
             if self.state_m is not None:
                 entry["state_m"] = self.state_m[s.weight_off:s.weight_off + n].view(-1, s.ncols).cpu()
             if self.state_v is not None:
                 entry["state_v"] = self.state_v[s.weight_off:s.weight_off + n].view(-1, s.ncols).cpu()
             if self.score is not None:
-                entry["score"] = self.score[s.row_base:s.row_base + s.spec.num_embeddings].cpu()
+                entry["score"] = self.score[s.row_base:s.row_base + s.storage_rows].cpu()
             out[(s.spec.name, s.col_begin)] = entry
         return out
 
@@ -356,7 +368,7 @@ class ShardedEmbeddingBagCollection:
         for i, s in enumerate(self.shards):
             entry = state[(s.spec.name, s.col_begin)]
             self.shard_view(i).copy_(entry["weight"])
-            n = s.spec.num_embeddings * s.ncols
+            n = s.storage_rows * s.ncols
             if self.state_row is not None and "state_row" in entry:
                 self.row_state_view(i).copy_(entry["state_row"])
             if self.state_m is not None and "state_m" in entry:
@@ -364,7 +376,7 @@ class ShardedEmbeddingBagCollection:
             if self.state_v is not None and "state_v" in entry:
                 self.state_v[s.weight_off:s.weight_off + n].copy_(entry["state_v"].reshape(-1))
             if self.score is not None and "score" in entry:
-                self.score[s.row_base:s.row_base + s.spec.num_embeddings].copy_(entry["score"])
+                self.score[s.row_base:s.row_base + s.storage_rows].copy_(entry["score"])
 
     def memory_bytes(self) -> int:
         tensors = [self.weights, self.state_row, self.state_m, self.state_v, self.score, self.row_count,

@@ -108,6 +108,7 @@ class SparseTableSpec:
     init_scale: float = 0.01
     shards: int = 1
     max_staleness_steps: int = 0
+    cache_rows: int | None = None  # host-DRAM tier: rows live in pinned host memory, this many in an HBM cache
 
     def __post_init__(self) -> None:
         require_sparse_value_dtype(self.value_dtype)
@@ -118,6 +119,11 @@ class SparseTableSpec:
             raise ValueError("table shape must be positive")
         if self.embedding_dim % 4:
             raise ValueError("embedding_dim must be a multiple of 4")
+        if self.cache_rows is not None:
+            if not 0 < self.cache_rows <= self.num_embeddings:
+                raise ValueError("cache_rows must be in (0, num_embeddings]")
+            if self.value_dtype != "float32":
+                raise ValueError("host-tier tables store fp32 rows")
         if self.pooling not in ("sum", "mean"):
             raise ValueError(f"unsupported pooling {self.pooling!r}")
 
