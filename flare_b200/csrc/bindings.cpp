@@ -495,27 +495,50 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                                 cur_stream());
   });
 
-  auto parse_tier = [](const py::dict& d) {
-    flare::TierCopyParams p{};
-    p.n = get<int>(d, "n");
-    p.ncols = get<int>(d, "ncols");
-    p.slots = P<const int>(get<uintptr_t>(d, "slots"));
-    p.cache_w = P<float>(get<uintptr_t>(d, "cache_w"));
-    p.cache_row = P<float>(get_or<uintptr_t>(d, "cache_row", 0));
-    p.cache_m = P<float>(get_or<uintptr_t>(d, "cache_m", 0));
-    p.cache_v = P<float>(get_or<uintptr_t>(d, "cache_v", 0));
-    p.stage_w = P<float>(get<uintptr_t>(d, "stage_w"));
-    p.stage_row = P<float>(get_or<uintptr_t>(d, "stage_row", 0));
-    p.stage_m = P<float>(get_or<uintptr_t>(d, "stage_m", 0));
-    p.stage_v = P<float>(get_or<uintptr_t>(d, "stage_v", 0));
-    p.slot_map = P<int>(get_or<uintptr_t>(d, "slot_map", 0));
-    p.new_rows = P<const int64_t>(get_or<uintptr_t>(d, "new_rows", 0));
-    p.evict_rows = P<const int64_t>(get_or<uintptr_t>(d, "evict_rows", 0));
-    p.n_evict = get_or<int>(d, "n_evict", 0);
-    return p;
-  };
-  m.def("tier_gather", [parse_tier](const py::dict& d) { flare::tier_gather(parse_tier(d), cur_stream()); });
-  m.def("tier_install", [parse_tier](const py::dict& d) { flare::tier_install(parse_tier(d), cur_stream()); });
+  m.def("tier_prepare", [](const py::dict& d) {
+    flare::TierParams p{};
+    const auto tabs = get<py::list>(d, "tables");
+    p.num_tables = static_cast<int>(tabs.size());
+    if (p.num_tables > flare::kMaxTierTables) throw std::runtime_error("too many host-tier tables");
+    for (int k = 0; k < p.num_tables; ++k) {
+      const py::dict t = tabs[k].cast<py::dict>();
+      flare::TierTable& x = p.tables[k];
+      x.feature = get<int>(t, "feature");
+      x.ncols = get<int>(t, "ncols");
+      x.rows = get<int64_t>(t, "rows");
+      x.C = get<int>(t, "C");
+      x.slot_map = P<int>(get<uintptr_t>(t, "slot_map"));
+      x.slot2row = P<int64_t>(get<uintptr_t>(t, "slot2row"));
+      x.stamp = P<int>(get<uintptr_t>(t, "stamp"));
+      x.hand = P<unsigned>(get<uintptr_t>(t, "hand"));
+      x.cache_w = P<float>(get<uintptr_t>(t, "cache_w"));
+      x.cache_row = P<float>(get_or<uintptr_t>(t, "cache_row", 0));
+      x.cache_m = P<float>(get_or<uintptr_t>(t, "cache_m", 0));
+      x.cache_v = P<float>(get_or<uintptr_t>(t, "cache_v", 0));
+      x.host_w = P<float>(get<uintptr_t>(t, "host_w"));
+      x.host_row = P<float>(get_or<uintptr_t>(t, "host_row", 0));
+      x.host_m = P<float>(get_or<uintptr_t>(t, "host_m", 0));
+      x.host_v = P<float>(get_or<uintptr_t>(t, "host_v", 0));
+      x.miss_rows = P<int>(get<uintptr_t>(t, "miss_rows"));
+      x.num_miss = P<int>(get<uintptr_t>(t, "num_miss"));
+      x.miss_cap = get<int>(t, "miss_cap");
+    }
+    p.world = get<int>(d, "world");
+    p.rank = get<int>(d, "rank");
+    p.Bl = get<int>(d, "Bl");
+    p.peer_offsets = P<const int* const>(get<uintptr_t>(d, "peer_offsets"));
+    p.peer_values = P<const int* const>(get<uintptr_t>(d, "peer_values"));
+    p.step_ptr = P<const int>(get<uintptr_t>(d, "step_ptr"));
+    p.flags_local = P<uint32_t>(get_or<uintptr_t>(d, "flags_local", 0));
+    p.peer_flags = P<uint32_t* const>(get_or<uintptr_t>(d, "peer_flags", 0));
+    p.flag_in = get_or<int>(d, "flag_in", 0);
+    p.epoch_ctr = P<uint32_t>(get_or<uintptr_t>(d, "epoch_ctr", 0));
+    p.block_counter = P<unsigned>(get<uintptr_t>(d, "block_counter"));
+    p.block_counter2 = P<unsigned>(get<uintptr_t>(d, "block_counter2"));
+    p.status = P<int>(get_or<uintptr_t>(d, "status", 0));
+    p.timeout_ns = get_or<uint64_t>(d, "timeout_ns", 2000000000ull);
+    flare::tier_prepare(p, get<int>(d, "grid"), cur_stream());
+  });
 
   m.def("dcn_concat_x0", [](uintptr_t pooled, int64_t ldp, uintptr_t dense, int nd, int64_t B, int E, uintptr_t x0,
                             int64_t ld0) {

@@ -43,7 +43,7 @@ _SHARD_DTYPE = np.dtype([
 ])
 assert _SHARD_DTYPE.itemsize == 64
 
-FLAG_FWD_IN, FLAG_FWD_OUT, FLAG_BWD_IN, NUM_FLAG_ARRAYS = 0, 1, 2, 3
+FLAG_FWD_IN, FLAG_FWD_OUT, FLAG_BWD_IN, FLAG_TIER, NUM_FLAG_ARRAYS = 0, 1, 2, 3, 4
 
 
 def _with_opt(t: SparseTableSpec, opt: SparseOptimizerConfig) -> SparseTableSpec:
@@ -222,6 +222,13 @@ class ShardedEmbeddingBagCollection:
         self.status = DeviceStatus(dev)
         self.grid = native().device_sm_count() * 8
         self.step_dev = torch.zeros(1, dtype=torch.int32, device=dev)  # device-resident optimizer step
+        # host-DRAM tier: placement kernels run before every forward (on every rank when any table is
+        # host-tier, because the placement kernel's barrier spans all ranks)
+        self.host_tier = None
+        if any(t.cache_rows is not None for t in self.tables):
+            from .host_tier import HostTier
+
+            self.host_tier = HostTier(self, seed=seed, flag_slot=FLAG_TIER, flags=self.flags)
 
     def _heap_bytes(self) -> int:
         b = (self.F * self.B + 1) * 4 + self.F * self.B * self.max_bag * 4
@@ -265,6 +272,8 @@ class ShardedEmbeddingBagCollection:
             epoch_ctr=self.flags.epoch_ptr(FLAG_FWD_IN), block_counter=self.flags.block_counter_ptr(FLAG_FWD_IN),
             status=self.status.ptr, timeout_ns=self.timeout_ns, grid=self.grid,
         )
+        if self.host_tier is not None:
+            self.host_tier.prepare()
         native().emb_forward(d)
         return self.pooled.local
 
