@@ -9,6 +9,7 @@
 #include "attention.cuh"
 #include "dcn.cuh"
 #include "dense.cuh"
+#include "dynamic_emb.cuh"
 #include "embedding.cuh"
 #include "gemm.cuh"
 #include "host_tier.cuh"
@@ -108,7 +109,10 @@ flare::AdamParams parse_adam(const py::dict& d) {
 
 }  // namespace
 
+void register_etl(py::module_& m);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  register_etl(m);
   m.doc() = "flare_b200 native kernels (sm_100a)";
 
   m.def("device_sm_count", &flare::device_sm_count);
@@ -253,6 +257,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.out_dtype = get_or<int>(d, "out_dtype", kBF16);
     p.vec = get_or<int>(d, "vec", 1);
     p.slot_map = P<const int>(get_or<uintptr_t>(d, "slot_map", 0));
+    p.peer_remap = P<const int* const>(get_or<uintptr_t>(d, "peer_remap", 0));
     p.stage_ids = P<int>(get<uintptr_t>(d, "stage_ids"));
     p.stage_bag = P<int>(get<uintptr_t>(d, "stage_bag"));
     p.stage_count = P<int>(get<uintptr_t>(d, "stage_count"));
@@ -493,6 +498,59 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     flare::seq_embed_grad_split(P<const __nv_bfloat16>(dx), lddx, P<const __nv_bfloat16>(y), ldy,
                                 P<const float>(dpos), P<const int>(target_row), T, P<__nv_bfloat16>(grad), ldg,
                                 cur_stream());
+  });
+
+  m.def("dyn_prepare", [](const py::dict& d) {
+    flare::DynParams p{};
+    const auto tabs = get<py::list>(d, "tables");
+    p.num_tables = static_cast<int>(tabs.size());
+    if (p.num_tables > flare::kMaxDynTables) throw std::runtime_error("too many dynamic tables");
+    for (int k = 0; k < p.num_tables; ++k) {
+      const py::dict t = tabs[k].cast<py::dict>();
+      flare::DynTable& x = p.tables[k];
+      x.feature = get<int>(t, "feature");
+      x.ncols = get<int>(t, "ncols");
+      x.col_begin = get<int>(t, "col_begin");
+      x.C = get<int>(t, "C");
+      x.H = get<int>(t, "H");
+      x.init_scale = get<float>(t, "init_scale");
+      x.seed = get<uint64_t>(t, "seed");
+      x.keys = P<int>(get<uintptr_t>(t, "keys"));
+      x.slot_of = P<int>(get<uintptr_t>(t, "slot_of"));
+      x.bucket_of = P<int>(get<uintptr_t>(t, "bucket_of"));
+      x.stamp = P<int>(get<uintptr_t>(t, "stamp"));
+      x.hand = P<unsigned>(get<uintptr_t>(t, "hand"));
+      x.weights = P<float>(get<uintptr_t>(t, "weights"));
+      x.state_row = P<float>(get_or<uintptr_t>(t, "state_row", 0));
+      x.state_m = P<float>(get_or<uintptr_t>(t, "state_m", 0));
+      x.state_v = P<float>(get_or<uintptr_t>(t, "state_v", 0));
+      x.score = P<float>(get_or<uintptr_t>(t, "score", 0));
+      x.new_buckets = P<int>(get<uintptr_t>(t, "new_buckets"));
+      x.num_new = P<int>(get<uintptr_t>(t, "num_new"));
+      x.new_cap = get<int>(t, "new_cap");
+      x.num_tomb = P<int>(get<uintptr_t>(t, "num_tomb"));
+    }
+    p.world = get<int>(d, "world");
+    p.rank = get<int>(d, "rank");
+    p.Bl = get<int>(d, "Bl");
+    p.peer_offsets = P<const int* const>(get<uintptr_t>(d, "peer_offsets"));
+    p.peer_values = P<const int* const>(get<uintptr_t>(d, "peer_values"));
+    p.peer_remap = P<int* const>(get<uintptr_t>(d, "peer_remap"));
+    p.step_ptr = P<const int>(get<uintptr_t>(d, "step_ptr"));
+    p.flags_local = P<uint32_t>(get_or<uintptr_t>(d, "flags_local", 0));
+    p.peer_flags = P<uint32_t* const>(get_or<uintptr_t>(d, "peer_flags", 0));
+    p.flag_in = get_or<int>(d, "flag_in", 0);
+    p.epoch_ctr = P<uint32_t>(get_or<uintptr_t>(d, "epoch_ctr", 0));
+    p.block_counter = P<unsigned>(get<uintptr_t>(d, "block_counter"));
+    p.block_counter2 = P<unsigned>(get<uintptr_t>(d, "block_counter2"));
+    p.status = P<int>(get_or<uintptr_t>(d, "status", 0));
+    p.timeout_ns = get_or<uint64_t>(d, "timeout_ns", 2000000000ull);
+    flare::dyn_prepare(p, get<int>(d, "grid"), cur_stream());
+  });
+  m.def("dyn_rebuild", [](uintptr_t keys, uintptr_t slot_of, uintptr_t bucket_of, int H, uintptr_t live_keys,
+                          uintptr_t live_slots, int n) {
+    flare::dyn_rebuild(P<int>(keys), P<int>(slot_of), P<int>(bucket_of), H, P<const int>(live_keys),
+                       P<const int>(live_slots), n, cur_stream());
   });
 
   m.def("tier_prepare", [](const py::dict& d) {

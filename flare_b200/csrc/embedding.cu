@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(kEmbThreads) emb_fwd_kernel(EmbFwdParams p) {
       float4 acc[VEC];
 #pragma unroll
       for (int v = 0; v < VEC; ++v) acc[v] = make_float4(0.f, 0.f, 0.f, 0.f);
-      const int* vals = p.peer_values[s];
+      const int* vals = (d.flags & 1) ? p.peer_remap[s] : p.peer_values[s];
       for (int j = 0; j < maxlen; j += G) {
         int myid = -1;
         const bool has = active && j + l < len;

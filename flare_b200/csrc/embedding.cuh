@@ -16,7 +16,7 @@ struct ShardDesc {
   int64_t weight_off;  // element offset of the shard in the weight buffer
   int64_t row_base;    // offset of the shard's first row in per-row arrays
   int pooling;         // 0 = sum, 1 = mean
-  int pad_;
+  int flags;           // bit 0: ids are read from the remap buffers (dynamic tables: key -> slot)
   int64_t id_rows;     // valid ids are [0, id_rows)
   int64_t slot_map_off;  // >= 0: ids map to HBM rows through slot_map[slot_map_off + id]; -1: id = row
 };
@@ -66,6 +66,7 @@ struct EmbFwdParams {
   int out_dtype;  // kBF16 or kF32
   int vec;        // float4 vectors per lane: 1 (shard width <= 128) or 2 (<= 256)
   const int* slot_map;  // row -> HBM slot maps of host-tier shards (ShardDesc::slot_map_off), or null
+  const int* const* peer_remap;  // [world] slot buffers of dynamic tables (same layout as values), or null
   // staging for the backward pass
   int* stage_ids;    // [(sh*world+s)*stage_cap + j]
   int* stage_bag;    // same indexing: sample index of occurrence j

@@ -39,11 +39,11 @@ from .precision import TORCH_DTYPES
 _SHARD_DTYPE = np.dtype([
     ("feature", "<i4"), ("col_begin", "<i4"), ("ncols", "<i4"), ("out_col", "<i4"),
     ("rows", "<i8"), ("weight_off", "<i8"), ("row_base", "<i8"),
-    ("pooling", "<i4"), ("pad_", "<i4"), ("id_rows", "<i8"), ("slot_map_off", "<i8"),
+    ("pooling", "<i4"), ("flags", "<i4"), ("id_rows", "<i8"), ("slot_map_off", "<i8"),
 ])
 assert _SHARD_DTYPE.itemsize == 64
 
-FLAG_FWD_IN, FLAG_FWD_OUT, FLAG_BWD_IN, FLAG_TIER, NUM_FLAG_ARRAYS = 0, 1, 2, 3, 4
+FLAG_FWD_IN, FLAG_FWD_OUT, FLAG_BWD_IN, FLAG_TIER, FLAG_DYN, NUM_FLAG_ARRAYS = 0, 1, 2, 3, 4, 5
 
 
 def _with_opt(t: SparseTableSpec, opt: SparseOptimizerConfig) -> SparseTableSpec:
@@ -63,6 +63,7 @@ class LocalShard:
     row_base: int
     storage_rows: int = 0      # rows held in HBM (= num_embeddings, or the cache slots of a host-tier table)
     slot_map_off: int = -1     # offset of the row -> slot map of a host-tier table, -1 if resident
+    dynamic: bool = False      # hash-keyed table: ids reach the kernels as slots through the remap buffers
 
 
 class ShardedEmbeddingBagCollection:
@@ -123,12 +124,16 @@ class ShardedEmbeddingBagCollection:
             cached = spec.cache_rows is not None
             srows = int(spec.cache_rows) if cached else spec.num_embeddings
             self.shards.append(LocalShard(p.table, spec, p.col_begin, p.ncols, self.plan.out_cols[p.table] + p.col_begin,
-                                          woff, rbase, srows, smoff if cached else -1))
+                                          woff, rbase, srows, smoff if cached else -1, bool(spec.dynamic)))
             woff += srows * p.ncols
             rbase += srows
             if cached:
                 smoff += spec.num_embeddings
         self.num_local_elems, self.num_local_rows = woff, rbase
+        for p in self.plan.placements:
+            t = self.tables[p.table]
+            if t.dynamic and p.ncols != t.embedding_dim:
+                raise ValueError(f"dynamic table {t.name} cannot be split by columns (one hash map per table)")
         # host-tier tables reach their HBM cache slots through a device row -> slot map (-1 = not resident)
         self.slot_map = torch.full((max(smoff, 1),), -1, dtype=torch.int32, device=self.device) if smoff else None
         self.ncols_max = max([s.ncols for s in self.shards], default=4)
@@ -141,8 +146,8 @@ class ShardedEmbeddingBagCollection:
         desc = np.zeros(max(len(self.shards), 1), dtype=_SHARD_DTYPE)
         for i, s in enumerate(self.shards):
             desc[i] = (self.features.index(s.spec.feature_name), s.col_begin, s.ncols, s.out_col,
-                       s.storage_rows, s.weight_off, s.row_base, 1 if s.spec.pooling == "mean" else 0, 0,
-                       s.spec.num_embeddings, s.slot_map_off)
+                       s.storage_rows, s.weight_off, s.row_base, 1 if s.spec.pooling == "mean" else 0,
+                       1 if s.dynamic else 0, s.spec.num_embeddings, s.slot_map_off)
         self.shard_desc = torch.from_numpy(desc.view(np.uint8).copy()).to(dev)
 
         # ---- parameters and optimizer state (local HBM) ----
@@ -213,12 +218,17 @@ class ShardedEmbeddingBagCollection:
         self.pooled = heap.alloc((self.B, self.total_dim), out_dtype)
         self.grad_in = heap.alloc((self.B, self.total_dim), grad_dtype)
         self.flags = FlagRegion(heap, NUM_FLAG_ARRAYS)
+        any_dynamic = any(t.dynamic for t in self.tables)
+        # dynamic tables: owners write each occurrence's slot into the requester's remap buffer
+        self.remap = heap.alloc((self.values_capacity,), torch.int32) if any_dynamic else None
         self._peer = {
             "offsets": self.in_offsets.peer_ptr_tensor(dev),
             "values": self.in_values.peer_ptr_tensor(dev),
             "out": self.pooled.peer_ptr_tensor(dev),
             "grad": self.grad_in.peer_ptr_tensor(dev),
         }
+        if self.remap is not None:
+            self._peer["remap"] = self.remap.peer_ptr_tensor(dev)
         self.status = DeviceStatus(dev)
         self.grid = native().device_sm_count() * 8
         self.step_dev = torch.zeros(1, dtype=torch.int32, device=dev)  # device-resident optimizer step
@@ -229,9 +239,14 @@ class ShardedEmbeddingBagCollection:
             from .host_tier import HostTier
 
             self.host_tier = HostTier(self, seed=seed, flag_slot=FLAG_TIER, flags=self.flags)
+        self.dynamic = None
+        if any_dynamic:
+            from .dynamic import DynamicTables
+
+            self.dynamic = DynamicTables(self, seed=seed, flag_slot=FLAG_DYN, flags=self.flags)
 
     def _heap_bytes(self) -> int:
-        b = (self.F * self.B + 1) * 4 + self.F * self.B * self.max_bag * 4
+        b = (self.F * self.B + 1) * 4 + 2 * self.F * self.B * self.max_bag * 4
         b += 2 * self.B * self.total_dim * 4 + NUM_FLAG_ARRAYS * 64 + 8 * 256
         return b + (1 << 20)
 
@@ -274,6 +289,9 @@ class ShardedEmbeddingBagCollection:
         )
         if self.host_tier is not None:
             self.host_tier.prepare()
+        if self.dynamic is not None:
+            self.dynamic.prepare()
+            d["peer_remap"] = self._peer["remap"].data_ptr()
         native().emb_forward(d)
         return self.pooled.local
 

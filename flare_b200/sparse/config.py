@@ -109,6 +109,8 @@ class SparseTableSpec:
     shards: int = 1
     max_staleness_steps: int = 0
     cache_rows: int | None = None  # host-DRAM tier: rows live in pinned host memory, this many in an HBM cache
+    dynamic: bool = False          # hash-keyed: any int32 key >= 0, num_embeddings slots, insert on first sight
+    hash_buckets: int | None = None  # dynamic: power-of-two hash buckets (default 4 x slots rounded up)
 
     def __post_init__(self) -> None:
         require_sparse_value_dtype(self.value_dtype)
@@ -119,6 +121,8 @@ class SparseTableSpec:
             raise ValueError("table shape must be positive")
         if self.embedding_dim % 4:
             raise ValueError("embedding_dim must be a multiple of 4")
+        if self.dynamic and self.cache_rows is not None:
+            raise ValueError("a table is either dynamic or host-tier, not both")
         if self.cache_rows is not None:
             if not 0 < self.cache_rows <= self.num_embeddings:
                 raise ValueError("cache_rows must be in (0, num_embeddings]")
