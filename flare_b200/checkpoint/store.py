@@ -103,6 +103,12 @@ def load_dense(dirpath: Path, dense) -> dict:
 _FIELDS = ("weight", "state_row", "state_m", "state_v", "score")
 
 
+def _piece_name(table: str, col_begin: int, row_index: int = 0, row_shards: int = 1) -> str:
+    """File prefix of one piece: columns from ``col_begin``; a row-wise piece adds its residue."""
+    name = f"{table}.c{col_begin}"
+    return name if row_shards == 1 else f"{name}.r{row_index}of{row_shards}"
+
+
 def save_sparse(dirpath: Path, coll, step: int, *, mode: str = "full", base_step: int | None = None) -> None:
     """Each rank writes its shards; rank 0 writes the manifest."""
     if mode not in ("full", "incremental"):
@@ -115,17 +121,17 @@ def save_sparse(dirpath: Path, coll, step: int, *, mode: str = "full", base_step
     dirpath.mkdir(parents=True, exist_ok=True)
     for i, s in enumerate(coll.shards):
         fields = coll.shard_fields(i)
-        prefix = dirpath / f"{s.spec.name}.c{s.col_begin}"
+        prefix = dirpath / _piece_name(s.spec.name, s.col_begin, s.row_index, s.row_shards)
         rows = None
         if mode == "incremental":
-            rows = torch.nonzero(coll.dirty[s.row_base:s.row_base + s.spec.num_embeddings]).flatten()
+            rows = torch.nonzero(coll.dirty[s.row_base:s.row_base + s.storage_rows]).flatten()
             np.save(f"{prefix}.rows.npy", rows.cpu().numpy().astype(np.int64))
         for field, t in fields.items():
             arr = t if rows is None else t.index_select(0, rows)
             np.save(f"{prefix}.{field}.npy", arr.float().cpu().numpy())
     coll.dirty.zero_()
-    pieces = [{"table": s.spec.name, "col_begin": s.col_begin, "ncols": s.ncols, "rank": rank}
-              for s in coll.shards]
+    pieces = [{"table": s.spec.name, "col_begin": s.col_begin, "ncols": s.ncols, "rank": rank,
+               "row_index": s.row_index, "row_shards": s.row_shards} for s in coll.shards]
     gathered = [pieces]
     if world > 1:
         gathered = [None] * world
@@ -172,8 +178,9 @@ def load_sparse(root: str | os.PathLike, step: int, group: str, coll) -> dict:
                 lo, hi = max(p["col_begin"], s.col_begin), min(p["col_begin"] + p["ncols"], s.col_begin + s.ncols)
                 if lo >= hi:
                     continue
-                prefix = d / f"{s.spec.name}.c{p['col_begin']}"
-                rows = np.load(f"{prefix}.rows.npy") if man["mode"] == "incremental" else None
+                R, r = int(p.get("row_shards", 1)), int(p.get("row_index", 0))
+                prefix = d / _piece_name(s.spec.name, p["col_begin"], r, R)
+                local = np.load(f"{prefix}.rows.npy") if man["mode"] == "incremental" else None
                 for field in _FIELDS:
                     f = Path(f"{prefix}.{field}.npy")
                     if not f.exists():
@@ -183,18 +190,14 @@ def load_sparse(root: str | os.PathLike, step: int, group: str, coll) -> dict:
                         shape = (s.spec.num_embeddings, s.ncols) if arr.ndim == 2 else (s.spec.num_embeddings,)
                         entry[field] = np.zeros(shape, dtype=np.float32)
                     tgt = entry[field]
+                    # table rows of the saved rows: local row l of a row-wise piece is row l * R + r
+                    rows = (np.arange(arr.shape[0]) if local is None else local) * R + r
                     if arr.ndim == 2:
-                        src = arr[:, lo - p["col_begin"]:hi - p["col_begin"]]
-                        if rows is None:
-                            tgt[:, lo - s.col_begin:hi - s.col_begin] = src
-                        else:
-                            tgt[rows, lo - s.col_begin:hi - s.col_begin] = src
+                        tgt[rows, lo - s.col_begin:hi - s.col_begin] = arr[:, lo - p["col_begin"]:hi - p["col_begin"]]
                     else:
-                        if rows is None:
-                            tgt[:] = arr
-                        else:
-                            tgt[rows] = arr
-        state[(s.spec.name, s.col_begin)] = {k: torch.from_numpy(v) for k, v in entry.items()}
+                        tgt[rows] = arr
+        state[(s.spec.name, s.col_begin, s.row_index)] = {k: torch.from_numpy(np.ascontiguousarray(v[s.row_slice]))
+                                             for k, v in entry.items()}
     coll.load_local_state(state)
     coll.step = int(last["optimizer_step"])
     coll.step_dev.fill_(coll.step)

@@ -258,6 +258,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.vec = get_or<int>(d, "vec", 1);
     p.slot_map = P<const int>(get_or<uintptr_t>(d, "slot_map", 0));
     p.peer_remap = P<const int* const>(get_or<uintptr_t>(d, "peer_remap", 0));
+    p.peer_part = P<float* const>(get_or<uintptr_t>(d, "peer_part", 0));
+    p.part_stride = get_or<int64_t>(d, "part_stride", 0);
+    p.rw_tables = P<const flare::RwTable>(get_or<uintptr_t>(d, "rw_tables", 0));
+    p.num_rw = get_or<int>(d, "num_rw", 0);
     p.stage_ids = P<int>(get<uintptr_t>(d, "stage_ids"));
     p.stage_bag = P<int>(get<uintptr_t>(d, "stage_bag"));
     p.stage_count = P<int>(get<uintptr_t>(d, "stage_count"));
@@ -644,9 +648,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     flare::cast_pad_bf16(P<const float>(x), rows, cols, ldx, P<__nv_bfloat16>(y), ldy, cur_stream());
   });
   m.def("init_uniform", [](uintptr_t out, int dtype, int64_t n, float lo, float hi, uint64_t seed, int64_t off,
-                           int ncols, int dim, int col_begin) {
-    flare::init_uniform(P<void>(out), dtype, n, lo, hi, seed, off, ncols, dim, col_begin, cur_stream());
-  });
+                           int ncols, int dim, int col_begin, int64_t row_stride, int64_t row_first) {
+    flare::init_uniform(P<void>(out), dtype, n, lo, hi, seed, off, ncols, dim, col_begin, row_stride, row_first,
+                        cur_stream());
+  }, py::arg("out"), py::arg("dtype"), py::arg("n"), py::arg("lo"), py::arg("hi"), py::arg("seed"), py::arg("off"),
+     py::arg("ncols"), py::arg("dim"), py::arg("col_begin"), py::arg("row_stride") = 1, py::arg("row_first") = 0);
 
   m.def("sparse_gather", [](uintptr_t emb, int dtype, uintptr_t inv, int64_t slots, int dim, int pad, uintptr_t out) {
     flare::sparse_gather(P<const void>(emb), dtype, P<const int>(inv), slots, dim, pad, P<void>(out), cur_stream());

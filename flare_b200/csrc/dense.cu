@@ -459,11 +459,13 @@ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
 // a table initialised in column shards equals the table initialised whole.
 template <typename T>
 __global__ void init_uniform_kernel(T* __restrict__ out, int64_t n, float lo, float hi, uint64_t seed,
-                                    int64_t index_offset, int ncols, int dim, int col_begin) {
+                                    int64_t index_offset, int ncols, int dim, int col_begin, int64_t row_stride,
+                                    int64_t row_first) {
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t r = i / ncols;
-    const int64_t idx = r * dim + col_begin + (i - r * ncols) + index_offset;
+    // local row r is table row row_first + r * row_stride (row-wise pieces hold every row_stride-th row)
+    const int64_t idx = (row_first + r * row_stride) * dim + col_begin + (i - r * ncols) + index_offset;
     const uint64_t rnd = mix64(seed * 0x9e3779b97f4a7c15ULL + static_cast<uint64_t>(idx));
     const float u = static_cast<float>(rnd >> 40) * (1.0f / 16777216.0f);  // 24 random bits in [0,1)
     out[i] = from_f32<T>(lo + (hi - lo) * u);
@@ -578,18 +580,19 @@ void cast_pad_bf16(const float* x, int64_t rows, int cols, int64_t ldx, __nv_bfl
 }
 
 void init_uniform(void* out, int dtype, int64_t n, float lo, float hi, uint64_t seed, int64_t index_offset,
-                  int ncols, int dim, int col_begin, cudaStream_t s) {
-  FLARE_CHECK(ncols > 0 && dim >= ncols, "bad init slice");
+                  int ncols, int dim, int col_begin, int64_t row_stride, int64_t row_first, cudaStream_t s) {
+  FLARE_CHECK(ncols > 0 && dim >= ncols && row_stride >= 1, "bad init slice");
   const int grid = grid_for(n, 256);
   if (dtype == kF32)
     init_uniform_kernel<float><<<grid, 256, 0, s>>>(static_cast<float*>(out), n, lo, hi, seed, index_offset, ncols,
-                                                     dim, col_begin);
+                                                     dim, col_begin, row_stride, row_first);
   else if (dtype == kBF16)
     init_uniform_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(static_cast<__nv_bfloat16*>(out), n, lo, hi, seed,
-                                                             index_offset, ncols, dim, col_begin);
+                                                             index_offset, ncols, dim, col_begin, row_stride,
+                                                             row_first);
   else
     init_uniform_kernel<__half><<<grid, 256, 0, s>>>(static_cast<__half*>(out), n, lo, hi, seed, index_offset,
-                                                      ncols, dim, col_begin);
+                                                      ncols, dim, col_begin, row_stride, row_first);
   FLARE_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

@@ -141,6 +141,10 @@ __global__ void __launch_bounds__(kEmbThreads) emb_fwd_kernel(EmbFwdParams p) {
           if (myid < 0 || myid >= d.id_rows) {
             report_error(p.status, kIndexOutOfRange, d.feature);
             myid = -1;
+          } else if (d.rw_n > 1) {
+            // row-wise piece: only ids of this residue, at local row id / rw_n
+            const int q = myid / d.rw_n;
+            myid = (myid - q * d.rw_n == d.rw_idx) ? q : -1;
           } else if (d.slot_map_off >= 0) {
             // host-tier table: the id's row must have been made resident in an HBM slot
             const int slot = p.slot_map[d.slot_map_off + myid];
@@ -192,7 +196,13 @@ __global__ void __launch_bounds__(kEmbThreads) emb_fwd_kernel(EmbFwdParams p) {
           for (int v = 0; v < VEC; ++v) acc[v] = f4_scale(acc[v], inv);
         }
         const int64_t off = static_cast<int64_t>(b) * p.out_stride + d.out_col + col0;
-        if (p.out_dtype == kBF16) {
+        if (d.part_col >= 0) {
+          // row-wise piece: fp32 partial sum into the requester's partial rows of this residue
+          float* out = p.peer_part[s] + (static_cast<int64_t>(d.rw_idx) * p.Bl + b) * p.part_stride + d.part_col +
+                       col0;
+#pragma unroll
+          for (int v = 0; v < VEC; ++v) store4<float>(out + 4 * v, acc[v]);
+        } else if (p.out_dtype == kBF16) {
           __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.peer_out[s]) + off;
 #pragma unroll
           for (int v = 0; v < VEC; ++v) store4<__nv_bfloat16>(out + 4 * v, acc[v]);
@@ -219,6 +229,30 @@ __global__ void __launch_bounds__(kEmbThreads) emb_fwd_kernel(EmbFwdParams p) {
         barrier_signal(p.peer_flags, p.world, p.rank, p.flag_out, epoch);
         barrier_wait(p.flags_local, p.world, p.flag_out, epoch, p.timeout_ns, p.status);
       }
+    }
+  }
+}
+
+// Row-wise tables: pooled row = sum of the partial rows of the table's pieces,
+// in residue order (deterministic).  Runs on the requester after the forward,
+// whose exit barrier guarantees that every owner's partials have landed.
+template <typename TO>
+__global__ void __launch_bounds__(kEmbThreads) emb_rw_reduce_kernel(EmbFwdParams p) {
+  const float* part = p.peer_part[p.rank];
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nth = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int t = 0; t < p.num_rw; ++t) {
+    const RwTable rt = p.rw_tables[t];
+    const int q = rt.ncols / 4;
+    const int64_t total = static_cast<int64_t>(p.Bl) * q;
+    for (int64_t i = tid; i < total; i += nth) {
+      const int b = static_cast<int>(i / q);
+      const int c = static_cast<int>(i - static_cast<int64_t>(b) * q) * 4;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int r = 0; r < rt.rw_n; ++r)
+        acc = f4_add(acc, load4<float>(part + (static_cast<int64_t>(r) * p.Bl + b) * p.part_stride + rt.part_col + c));
+      TO* out = reinterpret_cast<TO*>(p.peer_out[p.rank]) + static_cast<int64_t>(b) * p.out_stride + rt.out_col + c;
+      store4<TO>(out, acc);
     }
   }
 }
@@ -847,6 +881,13 @@ void emb_forward(const EmbFwdParams& p, int grid, cudaStream_t s) {
     if (p.vec == 1) fwd_dispatch<__nv_bfloat16, 1>(p, grid, s); else fwd_dispatch<__nv_bfloat16, 2>(p, grid, s);
   }
   FLARE_CUDA_CHECK(cudaGetLastError());
+  if (p.num_rw > 0) {
+    FLARE_CHECK(p.peer_part != nullptr && p.rw_tables != nullptr, "row-wise tables need the partial buffers");
+    if (p.out_dtype == kBF16) emb_rw_reduce_kernel<__nv_bfloat16><<<grid, kEmbThreads, 0, s>>>(p);
+    else emb_rw_reduce_kernel<float><<<grid, kEmbThreads, 0, s>>>(p);
+    FLARE_CUDA_CHECK(cudaGetLastError());
+    count_launch();
+  }
 }
 
 void emb_backward(const EmbBwdParams& p, int ncols_max, int grid, cudaStream_t s) {

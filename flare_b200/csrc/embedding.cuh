@@ -5,8 +5,9 @@
 
 namespace flare {
 
-// One locally owned shard of a table: table-wise (all columns) or a
-// column-wise slice. Row ids index the shard directly (static vocabulary).
+// One locally owned shard of a table: table-wise (all columns), a column-wise
+// slice, or a row-wise (modulo) piece: rows i with i % rw_n == rw_idx, held at
+// local row i / rw_n.  Row ids index the table directly (static vocabulary).
 struct ShardDesc {
   int feature;         // index of the input feature (KJT key) feeding this table
   int col_begin;       // first table column held by this shard
@@ -19,6 +20,16 @@ struct ShardDesc {
   int flags;           // bit 0: ids are read from the remap buffers (dynamic tables: key -> slot)
   int64_t id_rows;     // valid ids are [0, id_rows)
   int64_t slot_map_off;  // >= 0: ids map to HBM rows through slot_map[slot_map_off + id]; -1: id = row
+  int rw_n;              // row shards of the table (1: the shard holds every row)
+  int rw_idx;            // this shard's residue
+  int part_col;          // row-wise: column of the fp32 partial-sum rows receiving col_begin; -1 otherwise
+  int pad_;
+};
+
+// A row-wise table as the requester sees it: partial pooled rows of its rw_n
+// pieces are summed into the pooled output.
+struct RwTable {
+  int out_col, part_col, ncols, rw_n;
 };
 
 enum SparseOptKind : int {
@@ -67,6 +78,10 @@ struct EmbFwdParams {
   int vec;        // float4 vectors per lane: 1 (shard width <= 128) or 2 (<= 256)
   const int* slot_map;  // row -> HBM slot maps of host-tier shards (ShardDesc::slot_map_off), or null
   const int* const* peer_remap;  // [world] slot buffers of dynamic tables (same layout as values), or null
+  float* const* peer_part;       // [world] fp32 partial pooled rows [rw_slots][Bl][part_stride] (row-wise tables)
+  int64_t part_stride;
+  const RwTable* rw_tables;      // row-wise tables of the collection (reduced locally after the exchange)
+  int num_rw;
   // staging for the backward pass
   int* stage_ids;    // [(sh*world+s)*stage_cap + j]
   int* stage_bag;    // same indexing: sample index of occurrence j

@@ -280,9 +280,7 @@ class DCN:
             elems += (b + 64 * world_size) * _round_up(a, 8)
         wts = 6 * elems  # bf16 compute copy + fp32 gradient
         small = 6 * (cfg.cross_layers * W + sum(cfg.deep) + H + 64 * 64) * 2
-        F = len(cfg.tables)
-        cap = values_capacity or F * batch_size * max_bag_size
-        emb = 4 * (F * batch_size + 1) + 4 * cap + 2 * 2 * batch_size * cfg.emb_width
+        emb = ShardedEmbeddingBagCollection.exchange_bytes(cfg.tables, batch_size, max_bag_size, values_capacity)
         return int(acts + rs + wts + small + emb) + 256 * ALIGN_SLACK + (64 << 20)
 
     def _load_replicated(self, name: str, value: torch.Tensor) -> None:
@@ -560,7 +558,7 @@ class DCNTorch(nn.Module):
     @torch.no_grad()
     def load_tables_from(self, fused: DCN) -> "DCNTorch":
         for i, s in enumerate(fused.emb.shards):
-            self.embs[s.table].weight[:, s.col_begin:s.col_begin + s.ncols] = fused.emb.shard_view(i).float().to(
+            self.embs[s.table].weight[s.row_slice, s.col_begin:s.col_begin + s.ncols] = fused.emb.shard_view(i).float().to(
                 self.embs[s.table].weight.device)
         return self
 

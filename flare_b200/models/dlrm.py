@@ -218,7 +218,7 @@ class DLRMTorch(nn.Module):
         self.head.weight.copy_(ds.compute_view("head.weight").float())
         self.head.bias.copy_(ds.compute_view("head.bias").float())
         for i, s in enumerate(fused.emb.shards):
-            self.embs[s.table].weight[:, s.col_begin:s.col_begin + s.ncols] = fused.emb.shard_view(i).float().to(
+            self.embs[s.table].weight[s.row_slice, s.col_begin:s.col_begin + s.ncols] = fused.emb.shard_view(i).float().to(
                 self.embs[s.table].weight.device)
         return self
 

@@ -159,13 +159,16 @@ def cast_pad_bf16(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
 
 
 def init_uniform_(t: torch.Tensor, lo: float, hi: float, seed: int, index_offset: int = 0, *,
-                  ncols: int | None = None, dim: int | None = None, col_begin: int = 0) -> torch.Tensor:
+                  ncols: int | None = None, dim: int | None = None, col_begin: int = 0, row_stride: int = 1,
+                  row_first: int = 0) -> torch.Tensor:
     """Fill ``t`` with uniform values from a counter-based generator.
 
     Value i of the stream depends only on (seed, index).  For a column slice
     (``t`` viewed as [rows, ncols] holding columns [col_begin, col_begin+ncols)
     of a table with row length ``dim``) element (r, c) takes stream index
     ``r*dim + col_begin + c``, so column shards reproduce the whole table.
+    A row-wise piece holding table rows ``row_first + r*row_stride`` passes
+    those two numbers and reproduces its rows of the whole table too.
     """
     if not t.is_contiguous():
         raise ValueError("init_uniform_ needs a contiguous tensor")
@@ -174,11 +177,11 @@ def init_uniform_(t: torch.Tensor, lo: float, hi: float, seed: int, index_offset
     dim = dim or ncols
     if not t.is_cuda:
         r = torch.arange(n) // ncols
-        idx = r * dim + col_begin + (torch.arange(n) - r * ncols) + index_offset
+        idx = (row_first + r * row_stride) * dim + col_begin + (torch.arange(n) - r * ncols) + index_offset
         t.copy_(uniform_at(idx, lo, hi, seed).reshape(t.shape).to(t.dtype))
         return t
     native().init_uniform(t.data_ptr(), dtype_code(t.dtype), n, float(lo), float(hi), int(seed),
-                          int(index_offset), int(ncols), int(dim), int(col_begin))
+                          int(index_offset), int(ncols), int(dim), int(col_begin), int(row_stride), int(row_first))
     return t
 
 

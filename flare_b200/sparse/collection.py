@@ -35,13 +35,16 @@ from .config import SparseOptimizerConfig, SparseTableSpec
 from .planner import ShardingPlan, plan_sharding
 from .precision import TORCH_DTYPES
 
-# ShardDesc layout shared with embedding.cuh (int32 x4, int64 x3, int32 x2 = 48 bytes)
+# ShardDesc layout shared with embedding.cuh (80 bytes)
 _SHARD_DTYPE = np.dtype([
     ("feature", "<i4"), ("col_begin", "<i4"), ("ncols", "<i4"), ("out_col", "<i4"),
     ("rows", "<i8"), ("weight_off", "<i8"), ("row_base", "<i8"),
     ("pooling", "<i4"), ("flags", "<i4"), ("id_rows", "<i8"), ("slot_map_off", "<i8"),
+    ("rw_n", "<i4"), ("rw_idx", "<i4"), ("part_col", "<i4"), ("pad", "<i4"),
 ])
-assert _SHARD_DTYPE.itemsize == 64
+assert _SHARD_DTYPE.itemsize == 80
+# RwTable (embedding.cuh): out_col, part_col, ncols, rw_n
+_RW_DTYPE = np.dtype([("out_col", "<i4"), ("part_col", "<i4"), ("ncols", "<i4"), ("rw_n", "<i4")])
 
 FLAG_FWD_IN, FLAG_FWD_OUT, FLAG_BWD_IN, FLAG_TIER, FLAG_DYN, NUM_FLAG_ARRAYS = 0, 1, 2, 3, 4, 5
 
@@ -64,6 +67,14 @@ class LocalShard:
     storage_rows: int = 0      # rows held in HBM (= num_embeddings, or the cache slots of a host-tier table)
     slot_map_off: int = -1     # offset of the row -> slot map of a host-tier table, -1 if resident
     dynamic: bool = False      # hash-keyed table: ids reach the kernels as slots through the remap buffers
+    row_index: int = 0         # row-wise piece: holds table rows i with i % row_shards == row_index
+    row_shards: int = 1
+    part_col: int = -1         # row-wise piece: column of its fp32 partial sums in the partial rows
+
+    @property
+    def row_slice(self) -> slice:
+        """Rows of the whole table this shard holds, in local order."""
+        return slice(self.row_index, None, self.row_shards)
 
 
 class ShardedEmbeddingBagCollection:
@@ -114,6 +125,18 @@ class ShardedEmbeddingBagCollection:
         self.step = 0
         dev = self.device
 
+        # ---- row-wise tables: fp32 partial-sum columns (every requester adds the pieces' partials) ----
+        self.rw_part_col: dict[int, int] = {}
+        pc = 0
+        for ti, t in enumerate(self.tables):
+            if self.plan.row_shards(ti) > 1:
+                if t.dynamic or t.cache_rows is not None:
+                    raise ValueError(f"table {t.name}: row-wise pieces are for resident static tables")
+                self.rw_part_col[ti] = pc
+                pc += t.embedding_dim
+        self.part_total = pc
+        self.rw_slots = max([self.plan.row_shards(ti) for ti in self.rw_part_col], default=0)
+
         # ---- local shards ----
         self.shards: list[LocalShard] = []
         woff = 0
@@ -122,9 +145,11 @@ class ShardedEmbeddingBagCollection:
         for p in self.plan.for_rank(rank):
             spec = self.tables[p.table]
             cached = spec.cache_rows is not None
-            srows = int(spec.cache_rows) if cached else spec.num_embeddings
+            srows = int(spec.cache_rows) if cached else p.num_rows(spec.num_embeddings)
+            part_col = self.rw_part_col[p.table] + p.col_begin if p.row_shards > 1 else -1
             self.shards.append(LocalShard(p.table, spec, p.col_begin, p.ncols, self.plan.out_cols[p.table] + p.col_begin,
-                                          woff, rbase, srows, smoff if cached else -1, bool(spec.dynamic)))
+                                          woff, rbase, srows, smoff if cached else -1, bool(spec.dynamic),
+                                          p.row_index, p.row_shards, part_col))
             woff += srows * p.ncols
             rbase += srows
             if cached:
@@ -147,8 +172,13 @@ class ShardedEmbeddingBagCollection:
         for i, s in enumerate(self.shards):
             desc[i] = (self.features.index(s.spec.feature_name), s.col_begin, s.ncols, s.out_col,
                        s.storage_rows, s.weight_off, s.row_base, 1 if s.spec.pooling == "mean" else 0,
-                       1 if s.dynamic else 0, s.spec.num_embeddings, s.slot_map_off)
+                       1 if s.dynamic else 0, s.spec.num_embeddings, s.slot_map_off, s.row_shards, s.row_index,
+                       s.part_col, 0)
         self.shard_desc = torch.from_numpy(desc.view(np.uint8).copy()).to(dev)
+        rw = np.zeros(max(len(self.rw_part_col), 1), dtype=_RW_DTYPE)
+        for k, (ti, pcol) in enumerate(sorted(self.rw_part_col.items())):
+            rw[k] = (self.plan.out_cols[ti], pcol, self.tables[ti].embedding_dim, self.plan.row_shards(ti))
+        self.rw_desc = torch.from_numpy(rw.view(np.uint8).copy()).to(dev)
 
         # ---- parameters and optimizer state (local HBM) ----
         self.weights = torch.empty(max(woff, 4), dtype=self.value_dtype, device=dev)
@@ -158,7 +188,8 @@ class ShardedEmbeddingBagCollection:
                 view = self.weights[s.weight_off:s.weight_off + n]
                 stream_seed = (seed * 1_000_003 + s.table * 7919) & 0x7FFFFFFF
                 init_uniform_(view, -s.spec.init_scale, s.spec.init_scale, stream_seed, ncols=s.ncols,
-                              dim=s.spec.embedding_dim, col_begin=s.col_begin)
+                              dim=s.spec.embedding_dim, col_begin=s.col_begin, row_stride=s.row_shards,
+                              row_first=s.row_index)
         opt = self.optimizer
         z32 = lambda n: torch.zeros(max(n, 4), dtype=torch.float32, device=dev)  # noqa: E731
         self.state_row = z32(rbase) if opt.needs_row_state else None
@@ -221,6 +252,9 @@ class ShardedEmbeddingBagCollection:
         any_dynamic = any(t.dynamic for t in self.tables)
         # dynamic tables: owners write each occurrence's slot into the requester's remap buffer
         self.remap = heap.alloc((self.values_capacity,), torch.int32) if any_dynamic else None
+        # row-wise tables: owners write fp32 partial pooled rows [residue][sample][part col] into the requester
+        self.partials = (heap.alloc((self.rw_slots, self.B, self.part_total), torch.float32)
+                         if self.rw_part_col else None)
         self._peer = {
             "offsets": self.in_offsets.peer_ptr_tensor(dev),
             "values": self.in_values.peer_ptr_tensor(dev),
@@ -229,6 +263,8 @@ class ShardedEmbeddingBagCollection:
         }
         if self.remap is not None:
             self._peer["remap"] = self.remap.peer_ptr_tensor(dev)
+        if self.partials is not None:
+            self._peer["part"] = self.partials.peer_ptr_tensor(dev)
         self.status = DeviceStatus(dev)
         self.grid = native().device_sm_count() * 8
         self.step_dev = torch.zeros(1, dtype=torch.int32, device=dev)  # device-resident optimizer step
@@ -245,9 +281,22 @@ class ShardedEmbeddingBagCollection:
 
             self.dynamic = DynamicTables(self, seed=seed, flag_slot=FLAG_DYN, flags=self.flags)
 
+    @staticmethod
+    def exchange_bytes(tables: list[SparseTableSpec], batch_size: int, max_bag_size: int,
+                       values_capacity: int | None = None) -> int:
+        """Symmetric memory of the exchange buffers (ids, pooled rows, pooled grads, row-wise partials)."""
+        F, B = len(tables), int(batch_size)
+        cap = values_capacity or F * B * max_bag_size
+        dim = sum(t.embedding_dim for t in tables)
+        rw = [t for t in tables if t.shards > 1]
+        part = 4 * max([t.shards for t in rw], default=0) * B * sum(t.embedding_dim for t in rw)
+        remap = 4 * cap if any(t.dynamic for t in tables) else 0
+        return 4 * (F * B + 1) + 4 * cap + remap + 2 * 4 * B * dim + part + NUM_FLAG_ARRAYS * 64 + 4096
+
     def _heap_bytes(self) -> int:
         b = (self.F * self.B + 1) * 4 + 2 * self.F * self.B * self.max_bag * 4
         b += 2 * self.B * self.total_dim * 4 + NUM_FLAG_ARRAYS * 64 + 8 * 256
+        b += self.rw_slots * self.B * self.part_total * 4 + 256
         return b + (1 << 20)
 
     # ------------------------------------------------------------------ API
@@ -292,6 +341,9 @@ class ShardedEmbeddingBagCollection:
         if self.dynamic is not None:
             self.dynamic.prepare()
             d["peer_remap"] = self._peer["remap"].data_ptr()
+        if self.partials is not None:
+            d.update(peer_part=self._peer["part"].data_ptr(), part_stride=self.part_total,
+                     rw_tables=self.rw_desc.data_ptr(), num_rw=len(self.rw_part_col))
         native().emb_forward(d)
         return self.pooled.local
 
@@ -375,7 +427,7 @@ class ShardedEmbeddingBagCollection:
         return out
 
     def local_state(self) -> dict:
-        """Owned shards with optimizer state (host copies), keyed by (table, col_begin)."""
+        """Owned shards with optimizer state (host copies), keyed by (table, col_begin, row_index)."""
         out = {}
         for i, s in enumerate(self.shards):
             entry = {"weight": self.shard_view(i).cpu(), "ncols": s.ncols}
@@ -388,12 +440,25 @@ class ShardedEmbeddingBagCollection:
                 entry["state_v"] = self.state_v[s.weight_off:s.weight_off + n].view(-1, s.ncols).cpu()
             if self.score is not None:
                 entry["score"] = self.score[s.row_base:s.row_base + s.storage_rows].cpu()
-            out[(s.spec.name, s.col_begin)] = entry
+            out[(s.spec.name, s.col_begin, s.row_index)] = entry
+        return out
+
+    def export_pieces(self) -> dict:
+        """Host fp32 copies of the owned weights keyed ``(table, col_begin, row_index, row_shards)``."""
+        return {(s.table, s.col_begin, s.row_index, s.row_shards): self.shard_view(i).float().cpu()
+                for i, s in enumerate(self.shards)}
+
+    @staticmethod
+    def assemble_tables(pieces: dict, tables: list[SparseTableSpec]) -> list[torch.Tensor]:
+        """Whole tables from the pieces of every rank (``export_pieces`` of each, merged)."""
+        out = [torch.zeros(t.num_embeddings, t.embedding_dim) for t in tables]
+        for (t, c, r, R), w in pieces.items():
+            out[t][r::R, c:c + w.shape[1]] = w
         return out
 
     def load_local_state(self, state: dict) -> None:
         for i, s in enumerate(self.shards):
-            entry = state[(s.spec.name, s.col_begin)]
+            entry = state[(s.spec.name, s.col_begin, s.row_index)]
             self.shard_view(i).copy_(entry["weight"])
             n = s.storage_rows * s.ncols
             if self.state_row is not None and "state_row" in entry:

@@ -106,7 +106,7 @@ class SparseTableSpec:
     optimizer_dtype: str = "float32"
     optimizer: SparseOptimizerConfig = field(default_factory=SparseOptimizerConfig)
     init_scale: float = 0.01
-    shards: int = 1
+    shards: int = 1                # > 1: row-wise pieces by key modulo (piece r holds rows i % shards == r)
     max_staleness_steps: int = 0
     cache_rows: int | None = None  # host-DRAM tier: rows live in pinned host memory, this many in an HBM cache
     dynamic: bool = False          # hash-keyed: any int32 key >= 0, num_embeddings slots, insert on first sight
@@ -121,6 +121,10 @@ class SparseTableSpec:
             raise ValueError("table shape must be positive")
         if self.embedding_dim % 4:
             raise ValueError("embedding_dim must be a multiple of 4")
+        if self.shards < 1:
+            raise ValueError("shards must be >= 1")
+        if self.shards > 1 and (self.dynamic or self.cache_rows is not None):
+            raise ValueError("row-wise pieces (shards > 1) are for resident static tables")
         if self.dynamic and self.cache_rows is not None:
             raise ValueError("a table is either dynamic or host-tier, not both")
         if self.cache_rows is not None:

@@ -1,17 +1,20 @@
-"""Embedding sharding planner: table-wise + column-wise placement over ranks.
+"""Embedding sharding planner: table-wise, column-wise and row-wise placement.
 
-Every rank holds whole tables (table-wise) or column slices of tables
-(column-wise), so a shard produces complete columns of the pooled output and
-no partial sums cross NVLink.  Placement balances lookup work
-(``expected lookups x columns``) with a longest-processing-time greedy pass,
-splitting the heaviest piece on the most loaded rank in half (by columns)
+A rank holds whole tables (table-wise), column slices of tables
+(column-wise), or row-wise pieces: a table with ``shards = R > 1`` is cut by
+key modulo R, piece r holding rows ``i % R == r`` (the reference's modulo
+key partitioning, src/flare/runtime/fluxway/workers/dynamic_embedding.py:
+43-66, src/flare/mesh/topology.py:20-35).  Table-wise and column-wise
+shards produce complete columns of the pooled output, so no partial sums
+cross NVLink; row-wise pieces produce fp32 partial sums that the requester
+adds in residue order.  Row-wise pieces spread a table too large for one
+GPU (or too hot for one) over several, and every row keeps its optimizer
+state in one place, so row-wise optimizers stay exact.
+
+Placement balances lookup work (``expected lookups x columns``, divided by R
+for a row-wise piece) with a longest-processing-time greedy pass, splitting
+the heaviest whole-row piece on the most loaded rank in half (by columns)
 while that lowers the maximum load, subject to an HBM budget per rank.
-
-The reference shards tables by key with a modulo PartitionSpec across
-embedding workers (src/flare/runtime/fluxway/workers/dynamic_embedding.py:
-43-66, src/flare/mesh/topology.py:20-35); key-partitioned ("row-wise")
-placement is provided for the host-tier store, while the HBM fused path uses
-this plan.
 """
 from __future__ import annotations
 
@@ -28,6 +31,11 @@ class ShardPlacement:
     col_begin: int
     ncols: int
     rank: int
+    row_index: int = 0    # row-wise piece: holds table rows i with i % row_shards == row_index
+    row_shards: int = 1
+
+    def num_rows(self, num_embeddings: int) -> int:
+        return (num_embeddings - self.row_index + self.row_shards - 1) // self.row_shards
 
 
 @dataclass(frozen=True)
@@ -43,8 +51,11 @@ class ShardingPlan:
     def load(self, work) -> list[float]:
         loads = [0.0] * self.world_size
         for p in self.placements:
-            loads[p.rank] += work[p.table] * p.ncols
+            loads[p.rank] += work[p.table] * p.ncols / p.row_shards
         return loads
+
+    def row_shards(self, table: int) -> int:
+        return max([p.row_shards for p in self.placements if p.table == table], default=1)
 
 
 def _bytes_per_elem(dtype: str) -> int:
@@ -78,17 +89,23 @@ def plan_sharding(
     for t in tables:
         out_cols.append(c)
         c += t.embedding_dim
-    # pieces: (table, col_begin, ncols)
-    pieces = [(i, 0, t.embedding_dim) for i, t in enumerate(tables)]
+    # pieces: (table, col_begin, ncols, row_index, row_shards)
+    pieces = []
+    for i, t in enumerate(tables):
+        R = max(1, int(t.shards))
+        pieces += [(i, 0, t.embedding_dim, r, R) for r in range(R)]
+
+    def pwork(pc):
+        return work[pc[0]] * pc[2] / pc[4]
 
     def assign(pcs):
-        order = sorted(range(len(pcs)), key=lambda k: (-work[pcs[k][0]] * pcs[k][2], pcs[k][0], pcs[k][1]))
+        order = sorted(range(len(pcs)), key=lambda k: (-pwork(pcs[k]), pcs[k][0], pcs[k][3], pcs[k][1]))
         loads = [0.0] * world_size
         mem = [0.0] * world_size
         owner = [0] * len(pcs)
         for k in order:
-            ti, _, nc = pcs[k]
-            nbytes = tables[ti].num_embeddings * nc * _bytes_per_elem(tables[ti].value_dtype)
+            ti, _, nc, _, R = pcs[k]
+            nbytes = tables[ti].num_embeddings / R * nc * _bytes_per_elem(tables[ti].value_dtype)
             cands = sorted(range(world_size), key=lambda r: (loads[r], mem[r], r))
             chosen = cands[0]
             if hbm_budget_bytes is not None:
@@ -97,7 +114,7 @@ def plan_sharding(
                     raise MemoryError(f"table {tables[ti].name} piece does not fit the HBM budget on any rank")
                 chosen = fits[0]
             owner[k] = chosen
-            loads[chosen] += work[ti] * nc
+            loads[chosen] += pwork(pcs[k])
             mem[chosen] += nbytes
         return owner, loads
 
@@ -112,18 +129,18 @@ def plan_sharding(
         for _ in range(max_rounds):
             hot = loads.index(max(loads))
             cand = [k for k in range(len(pieces)) if owner[k] == hot and pieces[k][2] // 2 in VALID_SHARD_WIDTHS
-                    and pieces[k][2] >= 32
+                    and pieces[k][2] >= 32 and pieces[k][4] == 1
                     and (allow_rowwise_column_split or not tables[pieces[k][0]].optimizer.needs_row_state)]
             if not cand:
                 break
-            k = max(cand, key=lambda k: (work[pieces[k][0]] * pieces[k][2], -k))
-            ti, cb, nc = pieces[k]
-            pieces = pieces[:k] + [(ti, cb, nc // 2), (ti, cb + nc // 2, nc // 2)] + pieces[k + 1:]
+            k = max(cand, key=lambda k: (pwork(pieces[k]), -k))
+            ti, cb, nc, _, _ = pieces[k]
+            pieces = pieces[:k] + [(ti, cb, nc // 2, 0, 1), (ti, cb + nc // 2, nc // 2, 0, 1)] + pieces[k + 1:]
             owner, loads = assign(pieces)
             if score(loads) < best[0]:
                 best = (score(loads), pieces, owner, loads)
         _, pieces, owner, loads = best
-    placements = tuple(ShardPlacement(ti, cb, nc, owner[k]) for k, (ti, cb, nc) in enumerate(pieces))
+    placements = tuple(ShardPlacement(ti, cb, nc, owner[k], r, R) for k, (ti, cb, nc, r, R) in enumerate(pieces))
     return ShardingPlan(world_size, placements, tuple(out_cols), c)
 
 

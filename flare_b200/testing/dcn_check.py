@@ -89,9 +89,7 @@ def run(m: int = 128, deep=(256, 256), rank_dim: int = 64, dim: int = 64, tol: f
 
     # ---- reference on the global batch
     logical = model.logical_weights()
-    tables = {}
-    for i, s in enumerate(model.emb.shards):
-        tables[(s.table, s.col_begin)] = model.emb.shard_view(i).float().cpu()
+    tables = model.emb.export_pieces()
     if world > 1:
         allt = [None] * world
         dist.all_gather_object(allt, tables)
@@ -100,8 +98,8 @@ def run(m: int = 128, deep=(256, 256), rank_dim: int = 64, dim: int = 64, tol: f
     ref = DCNTorch(cfg).to(dev)
     ref.load_logical({k: v.to(torch.bfloat16).float() if v.dim() == 2 else v for k, v in logical.items()})
     with torch.no_grad():
-        for (t, c0), w in tables.items():
-            ref.embs[t].weight[:, c0:c0 + w.shape[1]] = w.to(dev)
+        for t, w in enumerate(model.emb.assemble_tables(tables, model.emb.tables)):
+            ref.embs[t].weight.copy_(w.to(dev))
     gb = concat_batches(batches, len(VOCABS))
     pooled = ref.pooled(gb.offsets, gb.values, gb.dense.shape[0]).detach().to(torch.bfloat16).float()
     pooled.requires_grad_(True)

@@ -4,7 +4,8 @@ Every rank trains the world-size-W model on its own batch; rank 0 also trains a
 world-size-1 model on the concatenation of all ranks' batches.  After K steps
 the sharded tables and the dense parameters must agree (fp32 tolerance).  This
 exercises the in-kernel ids / pooled / gradient all-to-alls over NVLink peer
-memory, the table/column-wise planner and the fused ZeRO-1 dense update.
+memory, the table/column-wise planner and the fused ZeRO-1 dense update;
+``CHECK_ROW_SHARDS=N`` adds row-wise (modulo) pieces and their partial sums.
 
     python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 \
         -m flare_b200.testing.dist_dlrm_check
@@ -13,6 +14,7 @@ from __future__ import annotations
 
 import os
 import sys
+from dataclasses import replace
 
 import torch
 import torch.distributed as dist
@@ -41,20 +43,19 @@ def concat_batches(batches: list[SparseBatch], F: int) -> SparseBatch:
 
 
 def export_tables(trainer: DLRMTrainer) -> dict:
-    out = {}
-    emb = trainer.model.emb
-    for i, s in enumerate(emb.shards):
-        out[(s.table, s.col_begin)] = emb.shard_view(i).float().cpu()
-    return out
+    return trainer.model.emb.export_pieces()
 
 
-def main(steps: int = 3, B: int = 128) -> int:
+def main(steps: int = 3, B: int = 128, row_shards: int = 1) -> int:
+    """``row_shards > 1`` cuts tables 1 and 3 into that many row-wise (modulo) pieces."""
     info = init_distributed(timeout_s=120)
     rank, world = info.rank, info.world_size
     dev = torch.device("cuda", torch.cuda.current_device())
     opt = SparseOptimizerConfig(kind="rowwise_adagrad", learning_rate=0.05)
-    cfg = DLRMConfig(tables=dlrm_benchmark_tables(VOCABS, 64, opt), bottom=(128, 64), top=(128, 64),
-                     sparse_optimizer=opt)
+    base = dlrm_benchmark_tables(VOCABS, 64, opt)
+    tables = [replace(t, shards=row_shards) if i in (1, 3) else t for i, t in enumerate(base)]
+    cfg = DLRMConfig(tables=tables, bottom=(128, 64), top=(128, 64), sparse_optimizer=opt)
+    ref_cfg = replace(cfg, tables=base)
     gens = [DLRMSyntheticData(B, VOCABS, max_bag=10, seed=7, rank=r, device=dev, pos_rate=0.3) for r in range(world)]
     data = [[g.next() for _ in range(steps)] for g in gens]
     tr = DLRMTrainer(cfg, B, max_bag_size=10, rank=rank, world_size=world, device=dev, seed=11, use_graph=False)
@@ -67,16 +68,14 @@ def main(steps: int = 3, B: int = 128) -> int:
     master = tr.model.dense.gather_master()
     ok = True
     if rank == 0:
-        ref = DLRMTrainer(cfg, B * world, max_bag_size=10, device=dev, seed=11, use_graph=False)
+        ref = DLRMTrainer(ref_cfg, B * world, max_bag_size=10, device=dev, seed=11, use_graph=False)
         for k in range(steps):
             ref.train_step(concat_batches([data[r][k] for r in range(world)], len(VOCABS)))
         torch.cuda.synchronize()
-        ref_tables = export_tables(ref)
-        full = {}
-        for part in gathered:
-            for (t, cb), w in part.items():
-                full.setdefault(t, torch.zeros(VOCABS[t], 64))[:, cb:cb + w.shape[1]] = w
-        for (t, _), w in ref_tables.items():
+        merged = {k: v for part in gathered for k, v in part.items()}
+        full = tr.model.emb.assemble_tables(merged, cfg.tables)
+        want = ref.model.emb.assemble_tables(export_tables(ref), ref_cfg.tables)
+        for t, w in enumerate(want):
             err = (full[t] - w).abs().max().item()
             if err > 2e-4:
                 print(f"table {t}: max abs diff {err}", file=sys.stderr)
@@ -103,4 +102,4 @@ def main(steps: int = 3, B: int = 128) -> int:
 
 
 if __name__ == "__main__":
-    sys.exit(main(int(os.environ.get("CHECK_STEPS", "3"))))
+    sys.exit(main(int(os.environ.get("CHECK_STEPS", "3")), row_shards=int(os.environ.get("CHECK_ROW_SHARDS", "1"))))

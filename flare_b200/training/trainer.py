@@ -25,6 +25,7 @@ from ..data.synthetic import SparseBatch
 from ..models.dlrm import DLRM, DLRMConfig
 from ..parallel.dist import barrier
 from ..parallel.symm import SymmetricHeap
+from ..sparse.collection import ShardedEmbeddingBagCollection
 
 
 @dataclass
@@ -175,9 +176,8 @@ class DLRMTrainer(FusedTrainer):
         device = device or torch.device("cuda", torch.cuda.current_device())
         heap = None
         if world_size > 1:
-            cap = values_capacity or len(cfg.tables) * batch_size * max_bag_size
-            total_dim = sum(t.embedding_dim for t in cfg.tables)
-            exchange = 4 * (len(cfg.tables) * batch_size + 1) + 4 * cap + 2 * 2 * batch_size * total_dim
+            exchange = ShardedEmbeddingBagCollection.exchange_bytes(cfg.tables, batch_size, max_bag_size,
+                                                                    values_capacity)
             dense = 6 * 16 * 1024 * 1024  # flat fp32 grads + bf16 params for up to 16M parameters
             need = heap_bytes or (exchange + dense + 64 * 1024 * 1024)
             heap = SymmetricHeap(need, rank=rank, world_size=world_size, device=device)

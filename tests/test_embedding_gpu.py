@@ -21,7 +21,7 @@ def _export(coll, tables):
     """Full host tables assembled from the GPU shards."""
     ws = [torch.zeros(t.num_embeddings, t.embedding_dim) for t in tables]
     for i, s in enumerate(coll.shards):
-        ws[s.table][:, s.col_begin:s.col_begin + s.ncols] = coll.shard_view(i).float().cpu()
+        ws[s.table][s.row_slice, s.col_begin:s.col_begin + s.ncols] = coll.shard_view(i).float().cpu()
     return ws
 
 
@@ -90,12 +90,15 @@ def _cw_plan(tables):
 
 
 @pytest.mark.parametrize("kind", ["rowwise_adagrad", "adam", "sgd", "adagrad", "rowwise_adam"])
-@pytest.mark.parametrize("column_split", [False, True])
-def test_forward_backward_matches_reference(cuda, kind, column_split):
+@pytest.mark.parametrize("split", ["none", "column", "row"])
+def test_forward_backward_matches_reference(cuda, kind, split):
     torch.manual_seed(0)
+    column_split = split == "column"
     opt = SparseOptimizerConfig(kind=kind, learning_rate=0.05, weight_decay=0.001)
     vocabs = [50, 1000, 7]
-    tables = [SparseTableSpec(f"t{i}", v, 64, optimizer=opt, pooling="mean" if i == 1 else "sum")
+    # row: tables 0 and 1 cut into 3 modulo pieces (all owned by this rank), fp32 partials summed
+    tables = [SparseTableSpec(f"t{i}", v, 64, optimizer=opt, pooling="mean" if i == 1 else "sum",
+                              shards=3 if split == "row" and i < 2 else 1)
               for i, v in enumerate(vocabs)]
     B, max_bag = 96, 20
     plan = _cw_plan(tables) if column_split else None
@@ -165,3 +168,25 @@ def test_lr_policies(cuda):
             ref.backward(grad.float(), step)
         torch.cuda.synchronize()
         torch.testing.assert_close(_export(coll, tables)[0], ref.weights[0], rtol=1e-4, atol=1e-5, msg=pol)
+
+
+def test_row_wise_pieces_init_and_pooling(cuda):
+    """Modulo row pieces reproduce the whole table's init and its pooled rows (partials summed in fp32)."""
+    opt = SparseOptimizerConfig(kind="rowwise_adagrad", learning_rate=0.05)
+    vocabs = [1001, 37]
+    whole = [SparseTableSpec(f"t{i}", v, 128, optimizer=opt) for i, v in enumerate(vocabs)]
+    cut = [SparseTableSpec(f"t{i}", v, 128, optimizer=opt, shards=4) for i, v in enumerate(vocabs)]
+    B, max_bag = 64, 12
+    a = ShardedEmbeddingBagCollection(whole, B, max_bag_size=max_bag, device=cuda, seed=5)
+    b = ShardedEmbeddingBagCollection(cut, B, max_bag_size=max_bag, device=cuda, seed=5)
+    assert len(b.shards) == 8 and b.rw_slots == 4
+    for wa, wb in zip(_export(a, whole), _export(b, cut)):
+        assert torch.equal(wa, wb)
+    offs, vals = _batch(B, vocabs, max_bag, seed=9)
+    for c in (a, b):
+        c.set_input(offs.to(cuda), vals.to(cuda), non_blocking=False)
+    pa, pb = a.forward().float(), b.forward().float()
+    torch.cuda.synchronize()
+    a.check()
+    b.check()
+    torch.testing.assert_close(pb, pa, rtol=1e-2, atol=1e-4)

@@ -47,6 +47,22 @@ def test_planner_balance_and_rowwise_exactness():
         plan_sharding([SparseTableSpec("big", 10**9, 128)], 2, hbm_budget_bytes=1e9)
 
 
+def test_planner_row_wise_pieces():
+    """shards=R cuts a table into R modulo pieces spread over ranks; pieces are never column-split."""
+    opt = SparseOptimizerConfig(kind="adam")
+    tabs = [SparseTableSpec("huge", 10**6 + 3, 128, optimizer=opt, shards=8)] + \
+        [SparseTableSpec(f"t{i}", 1000, 64, optimizer=opt) for i in range(4)]
+    p = plan_sharding(tabs, 4, expected_lookups=[8.0, 1, 1, 1, 1])
+    pieces = [pl for pl in p.placements if pl.table == 0]
+    assert sorted(pl.row_index for pl in pieces) == list(range(8))
+    assert all(pl.row_shards == 8 and pl.ncols == 128 for pl in pieces)
+    assert sorted(pl.rank for pl in pieces) == [0, 0, 1, 1, 2, 2, 3, 3]
+    assert sum(pl.num_rows(10**6 + 3) for pl in pieces) == 10**6 + 3
+    assert p.row_shards(0) == 8 and p.row_shards(1) == 1
+    with pytest.raises(ValueError):
+        SparseTableSpec("x", 10, 8, shards=2, cache_rows=5)
+
+
 def test_reference_pool_matches_bruteforce():
     tabs = [SparseTableSpec("a", 50, 8), SparseTableSpec("b", 30, 8, pooling="mean")]
     g = torch.Generator().manual_seed(1)
