@@ -17,8 +17,8 @@
 //                optimizer state zeroed;
 //   dyn_remap  : every occurrence's bucket in the remap buffers becomes the
 //                bucket's slot; the fused forward then reads slots from there.
-// Probing skips tombstones; a rebuild (host-triggered) clears them.  Every loop
-// is bounded.  This is the lookup_or_insert behaviour of the reference's
+// Lookups probe past tombstones; inserts reuse the first tombstone of the
+// key's chain; a rebuild (host-triggered) clears them.  Every loop is bounded.  This is the lookup_or_insert behaviour of the reference's
 // external embedding store (src/flare/runtime/fluxway/workers/
 // dynamic_embedding.py:134-260: auto-insert with uniform(-0.01, 0.01) init and
 // an LFU score); eviction here is CLOCK (least-recently-used order).
@@ -92,24 +92,48 @@ __global__ void dyn_insert_kernel(DynParams p) {
         const int key = vals[i];
         int bucket = -1;
         if (key >= 0) {
-          uint32_t h = hash_key(key) & mask;
-          for (int probe = 0; probe < t.H; ++probe, h = (h + 1) & mask) {
-            int cur = t.keys[h];
-            if (cur == kEmpty) {
-              cur = atomicCAS(t.keys + h, kEmpty, key);
-              if (cur == kEmpty) {  // inserted: this thread owns the new key
-                const int q = atomicAdd(t.num_new, 1);
-                if (q < t.new_cap) t.new_buckets[q] = static_cast<int>(h);
-                else report_error(p.status, kCapacityOverflow, 4000 + k);
-                bucket = static_cast<int>(h);
-                break;
-              }
-            }
+          // Probe from the key's home bucket until the key or an empty bucket; a new key takes the
+          // first tombstone on its chain (else the empty bucket) by CAS.  Losing a CAS to another key
+          // restarts the probe; during this kernel buckets only change empty/tombstone -> key, so the
+          // restart converges.  Bounded: at most 4 passes over the table.
+          const uint32_t home = hash_key(key) & mask;
+          uint32_t h = home;
+          int probe = 0, tomb = -1;
+          for (int it = 0; it < 4 * t.H && bucket < 0; ++it) {
+            const int cur = t.keys[h];
             if (cur == key) {
               bucket = static_cast<int>(h);
               const int slot = t.slot_of[h];
               if (slot >= 0) t.stamp[slot] = step;
               break;
+            }
+            const bool end = cur == kEmpty || probe == t.H - 1;
+            if (cur == kTomb && tomb < 0) tomb = static_cast<int>(h);
+            if (!end) {
+              ++probe;
+              h = (h + 1) & mask;
+              continue;
+            }
+            // the key is not on its chain: claim the first tombstone, else this empty bucket
+            int target = tomb, expect = kTomb;
+            if (target < 0 && cur == kEmpty) {
+              target = static_cast<int>(h);
+              expect = kEmpty;
+            }
+            if (target < 0) break;  // full chain without room
+            const int got = atomicCAS(t.keys + target, expect, key);
+            if (got == expect) {  // inserted: this thread owns the new key
+              if (expect == kTomb) atomicSub(t.num_tomb, 1);
+              const int q = atomicAdd(t.num_new, 1);
+              if (q < t.new_cap) t.new_buckets[q] = target;
+              else report_error(p.status, kCapacityOverflow, 4000 + k);
+              bucket = target;
+            } else if (got == key) {  // another occurrence inserted it first
+              bucket = target;
+            } else {  // another key took the bucket: probe again from home
+              h = home;
+              probe = 0;
+              tomb = -1;
             }
           }
           if (bucket < 0) report_error(p.status, kCapacityOverflow, 4100 + k);
