@@ -41,11 +41,13 @@ def parse():
     p.add_argument("--impl", choices=["flare", "reference", "torch"], default="flare")
     p.add_argument("--batch-per-gpu", type=int, default=8192)
     p.add_argument("--total-rows", type=float, default=2e8)
+    p.add_argument("--max-rows", type=float, default=4e7, help="largest table (smaller for small profiling cases)")
     p.add_argument("--max-bag", type=int, default=64)
     p.add_argument("--num-batches", type=int, default=4, help="distinct pre-generated batches cycled through")
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--profile-ops", action="store_true", help="also print a per-op eager breakdown (stderr)")
     p.add_argument("--seed", type=int, default=0)
     return p.parse_args()
 
@@ -102,7 +104,7 @@ def main():
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
     dev = torch.device("cuda", torch.cuda.current_device())
     B = args.batch_per_gpu
-    vocabs = log_uniform_vocab_sizes(26, 1e3, 4e7, args.total_rows)
+    vocabs = log_uniform_vocab_sizes(26, 1e3, args.max_rows, args.total_rows)
     sparse_opt = SparseOptimizerConfig(kind="rowwise_adagrad", learning_rate=0.01)
     cfg = DLRMConfig(tables=dlrm_benchmark_tables(vocabs, 128, sparse_opt), sparse_optimizer=sparse_opt,
                      dense_optimizer=DenseOptimizerConfig(kind="adam", learning_rate=1e-3))
@@ -172,6 +174,13 @@ def main():
     emb_stats = model.emb.last_step_stats()
 
     log("embedding-only timing done")
+    if args.profile_ops:
+        for i in range(2):
+            b = batches[i % len(batches)]
+            model.set_batch(b.dense, b.labels, b.offsets, b.values, non_blocking=True)
+            prof = model.profile_step()
+        tot = sum(t for _, t in prof)
+        log("per-op (eager, ms): " + ", ".join(f"{n}={t:.3f}" for n, t in prof) + f", total={tot:.3f}")
     # e2e through the public API: inputs in pinned host memory, loss read back every step
     e2e = None
     if not args.no_e2e:

@@ -293,6 +293,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.stage_ids = P<const int>(get<uintptr_t>(d, "stage_ids"));
     p.stage_bag = P<const int>(get<uintptr_t>(d, "stage_bag"));
     p.stage_rank = P<int>(get<uintptr_t>(d, "stage_rank"));
+    p.slot_start = P<int>(get<uintptr_t>(d, "slot_start"));
     p.stage_count = P<const int>(get<uintptr_t>(d, "stage_count"));
     p.stage_len = P<const int>(get<uintptr_t>(d, "stage_len"));
     p.stage_cap = get<int64_t>(d, "stage_cap");

@@ -21,9 +21,9 @@
 //   6. light rows (<= light_max occurrences): one row per lane group, fp32
 //      segment sum + optimizer applied in place, per-row counter reset;
 //   7. heavy rows (Zipf head): their occurrences are cut into equal chunks
-//      across warps (balanced however skewed the counts are), partial fp32
-//      sums reduce into a per-heavy-row accumulator, then one warp per row
-//      applies the optimizer.
+//      across warps (balanced however skewed the counts are), each
+//      (row, chunk) segment stores an fp32 partial row, then one warp per row
+//      adds its partials in chunk order and applies the optimizer.
 //
 // Reference behaviour: gather/pool/scatter semantics of
 // src/flare/kernels/backends/gpu_cupy.py:52-252 and
@@ -78,6 +78,32 @@ __device__ __forceinline__ bool entry_barrier(uint32_t* flags_local, uint32_t* c
 // ============================================================================
 // Forward
 // ============================================================================
+// Validated local row of an id for shard d, or -1 (out of range: reported; other residue of a
+// row-wise piece: skipped; host-tier row not resident: reported).
+__device__ __forceinline__ int map_id(const EmbFwdParams& p, const ShardDesc& d, int id, bool report) {
+  if (id < 0 || id >= d.id_rows) {
+    if (report) report_error(p.status, kIndexOutOfRange, d.feature);
+    return -1;
+  }
+  if (d.rw_n > 1) {
+    const int q = id / d.rw_n;
+    return id - q * d.rw_n == d.rw_idx ? q : -1;
+  }
+  if (d.slot_map_off >= 0) {
+    const int slot = p.slot_map[d.slot_map_off + id];
+    if (slot < 0 || slot >= d.rows) {
+      if (report) report_error(p.status, kIndexOutOfRange, 1000 + d.feature);
+      return -1;
+    }
+    return slot;
+  }
+  return id;
+}
+
+// Forward: every (source rank, sample) bag of every owned shard; a group of G lanes per bag, each
+// lane owning 4*VEC columns, 8 rows in flight per lane.  (A variant that loaded the next bag's
+// offsets and ids while pooling this one and bulk-prefetched its rows into L2 measured 1-3% slower
+// on the DLRM benchmark: the look-ahead state cost a resident block per SM.)
 template <typename TW, int VEC>
 __global__ void __launch_bounds__(kEmbThreads) emb_fwd_kernel(EmbFwdParams p) {
   const uint32_t epoch = p.world > 1 ? *reinterpret_cast<volatile uint32_t*>(p.epoch_ctr) + 1u : 0u;
@@ -136,26 +162,7 @@ __global__ void __launch_bounds__(kEmbThreads) emb_fwd_kernel(EmbFwdParams p) {
       for (int j = 0; j < maxlen; j += G) {
         int myid = -1;
         const bool has = active && j + l < len;
-        if (has) {
-          myid = vals[beg + j + l];
-          if (myid < 0 || myid >= d.id_rows) {
-            report_error(p.status, kIndexOutOfRange, d.feature);
-            myid = -1;
-          } else if (d.rw_n > 1) {
-            // row-wise piece: only ids of this residue, at local row id / rw_n
-            const int q = myid / d.rw_n;
-            myid = (myid - q * d.rw_n == d.rw_idx) ? q : -1;
-          } else if (d.slot_map_off >= 0) {
-            // host-tier table: the id's row must have been made resident in an HBM slot
-            const int slot = p.slot_map[d.slot_map_off + myid];
-            if (slot < 0 || slot >= d.rows) {
-              report_error(p.status, kIndexOutOfRange, 1000 + d.feature);
-              myid = -1;
-            } else {
-              myid = slot;
-            }
-          }
-        }
+        if (has) myid = map_id(p, d, vals[beg + j + l], true);
         if (has && stage_ok) {
           p.stage_ids[stage_base + j + l] = myid;
           p.stage_bag[stage_base + j + l] = b;
@@ -275,18 +282,19 @@ __global__ void __launch_bounds__(kEmbThreads) emb_bwd_pull_count_kernel(EmbBwdP
     }
     if (!ok) return;
   }
-  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int tid = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int nthreads = static_cast<int>(gridDim.x) * blockDim.x;
   const int esize = p.grad_dtype == kBF16 ? 2 : 4;
   for (int sh = 0; sh < p.num_shards; ++sh) {
     const ShardDesc d = p.shards[sh];
-    const int chunks = d.ncols * esize / 16;
-    const int64_t total = static_cast<int64_t>(p.world) * p.Bl * chunks;
-    for (int64_t i = tid; i < total; i += nthreads) {
-      const int c = static_cast<int>(i % chunks);
-      const int64_t bs = i / chunks;  // bs = b * world + s
-      const int b = static_cast<int>(bs / p.world);
-      const int s = static_cast<int>(bs - static_cast<int64_t>(b) * p.world);
+    const int chunks = d.ncols * esize / 16;  // a power of two
+    const int cshift = __ffs(chunks) - 1;
+    const int total = p.world * p.Bl * chunks;
+    for (int i = tid; i < total; i += nthreads) {
+      const int c = i & (chunks - 1);
+      const int bs = i >> cshift;  // bs = b * world + s
+      const int b = bs / p.world;
+      const int s = bs - b * p.world;
       const char* src = reinterpret_cast<const char*>(p.peer_grad[s]) +
                         (static_cast<int64_t>(b) * p.out_stride + d.out_col) * esize + c * 16;
       char* dst = reinterpret_cast<char*>(p.grad_stage) +
@@ -297,38 +305,41 @@ __global__ void __launch_bounds__(kEmbThreads) emb_bwd_pull_count_kernel(EmbBwdP
   __shared__ int block_total;
   if (threadIdx.x == 0) block_total = 0;
   __syncthreads();
-  // Count occurrences per row; this occurrence's rank within its row is the
-  // counter value before the add plus its position among equal-row lanes.
+  // Count occurrences per row over the used staging positions only, slot by slot (compact index
+  // k = slot_start[slot] + j); this occurrence's rank within its row is the counter value before
+  // the add plus its position among equal-row lanes.
   const int lane = lane_id();
-  const int64_t N = static_cast<int64_t>(p.num_shards) * p.world * p.stage_cap;
-  const int64_t nwarps = nthreads >> 5;
+  const int nslot = p.num_shards * p.world;
+  const int gw = tid >> 5, nw = nthreads >> 5;
   int local = 0;
-  for (int64_t i0 = (tid >> 5) * 32; i0 < N; i0 += nwarps * 32) {
-    const int64_t i = i0 + lane;
-    int f = 0;
-    long long row = -1;
-    if (i < N) {
-      const int slot = static_cast<int>(i / p.stage_cap);
-      const int64_t j = i - static_cast<int64_t>(slot) * p.stage_cap;
-      if (j < p.stage_count[slot]) {
-        const int id = p.stage_ids[i];
-        if (id >= 0) row = p.shards[slot / p.world].row_base + id;
+  for (int slot = 0; slot < nslot; ++slot) {
+    const int cnt = static_cast<int>(min(static_cast<int64_t>(p.stage_count[slot]), p.stage_cap));
+    const int kbase = p.slot_start[slot];
+    const int64_t sbase = static_cast<int64_t>(slot) * p.stage_cap;
+    const int64_t row_base = p.shards[slot / p.world].row_base;
+    for (int j0 = gw * 32; j0 < cnt; j0 += nw * 32) {
+      const int j = j0 + lane;
+      long long row = -1;
+      if (j < cnt) {
+        const int id = p.stage_ids[sbase + j];
+        if (id >= 0) row = row_base + id;
       }
+      const bool valid = row >= 0;
+      const unsigned vmask = __ballot_sync(kFull, valid);
+      int f = 0;
+      if (valid) {
+        ++local;
+        const unsigned peers = __match_any_sync(vmask, row);
+        const int leader = __ffs(peers) - 1;
+        int old = 0;
+        if (lane == leader) old = atomicAdd(p.row_count + row, __popc(peers));
+        old = __shfl_sync(peers, old, leader);
+        const int rank = old + __popc(peers & lanemask_lt());
+        p.stage_rank[kbase + j] = rank;
+        f = rank == 0 ? 1 : 0;
+      }
+      if (j < cnt) p.flags[kbase + j] = f;
     }
-    const bool valid = row >= 0;
-    const unsigned vmask = __ballot_sync(kFull, valid);
-    if (valid) {
-      ++local;
-      const unsigned peers = __match_any_sync(vmask, row);
-      const int leader = __ffs(peers) - 1;
-      int old = 0;
-      if (lane == leader) old = atomicAdd(p.row_count + row, __popc(peers));
-      old = __shfl_sync(peers, old, leader);
-      const int rank = old + __popc(peers & lanemask_lt());
-      p.stage_rank[i] = rank;
-      f = rank == 0 ? 1 : 0;
-    }
-    if (i < N) p.flags[i] = f;
   }
   local = __reduce_add_sync(kFull, local);
   if (lane == 0 && local) atomicAdd(&block_total, local);
@@ -336,30 +347,65 @@ __global__ void __launch_bounds__(kEmbThreads) emb_bwd_pull_count_kernel(EmbBwdP
   if (threadIdx.x == 0 && block_total) atomicAdd(p.num_unique + 1, block_total);
 }
 
-// 3. per-unique metadata
+// 0. slot_start = exclusive prefix of the staged id counts per slot (one block; slots <= 1024)
+__global__ void __launch_bounds__(1024) emb_slot_prefix_kernel(EmbBwdParams p) {
+  __shared__ int wsum[32];
+  const int nslot = p.num_shards * p.world;
+  const int i = threadIdx.x, l = lane_id(), w = warp_id();
+  const int c = i < nslot ? static_cast<int>(min(static_cast<int64_t>(p.stage_count[i]), p.stage_cap)) : 0;
+  int x = c;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(kFull, x, o);
+    if (l >= o) x += y;
+  }
+  if (l == 31) wsum[w] = x;
+  __syncthreads();
+  if (w == 0) {
+    int t = l < blockDim.x / 32 ? wsum[l] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(kFull, t, o);
+      if (l >= o) t += y;
+    }
+    wsum[l] = t;
+  }
+  __syncthreads();
+  const int excl = (w > 0 ? wsum[w - 1] : 0) + x - c;
+  if (i < nslot) p.slot_start[i] = excl;
+  if (i == blockDim.x - 1) p.slot_start[nslot] = excl + c;
+}
+
+// 3. per-unique metadata (slot-major over the used staging positions)
 __global__ void __launch_bounds__(kEmbThreads) emb_emit_kernel(EmbBwdParams p) {
-  const int64_t N = static_cast<int64_t>(p.num_shards) * p.world * p.stage_cap;
-  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (tid == 0) p.num_unique[0] = p.pos[N];
-  for (int64_t i = tid; i < N; i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    if (!p.flags[i]) continue;
-    const int u = p.pos[i];
-    const int slot = static_cast<int>(i / p.stage_cap);
+  const int nslot = p.num_shards * p.world;
+  const int tid = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int nthreads = static_cast<int>(gridDim.x) * blockDim.x;
+  if (tid == 0) p.num_unique[0] = p.pos[p.slot_start[nslot]];
+  for (int slot = 0; slot < nslot; ++slot) {
+    const int kbase = p.slot_start[slot], cnt = p.slot_start[slot + 1] - kbase;
+    const int64_t sbase = static_cast<int64_t>(slot) * p.stage_cap;
     const int sh = slot / p.world;
-    const long long row = p.shards[sh].row_base + p.stage_ids[i];
-    p.uniq_row[u] = row;
-    p.uniq_shard[u] = sh;
-    p.row2u[row] = u;
-    const int c = p.row_count[row];
-    p.cnt_u[u] = c;
-    p.first_gidx[u] = slot * p.Bl + p.stage_bag[i];
-    if (c > p.light_max) {
-      const int h = atomicAdd(p.num_unique + 2, 1);
-      if (h < p.max_heavy) {
-        p.heavy[h] = u;
-        p.hcnt[h] = c;
+    const int64_t row_base = p.shards[sh].row_base;
+    for (int j = tid; j < cnt; j += nthreads) {
+      if (!p.flags[kbase + j]) continue;
+      const int u = p.pos[kbase + j];
+      const long long row = row_base + p.stage_ids[sbase + j];
+      p.uniq_row[u] = row;
+      p.uniq_shard[u] = sh;
+      p.row2u[row] = u;
+      const int c = p.row_count[row];
+      p.cnt_u[u] = c;
+      p.first_gidx[u] = slot * p.Bl + p.stage_bag[sbase + j];
+      if (c > p.light_max) {
+        const int h = atomicAdd(p.num_unique + 2, 1);
+        if (h < p.max_heavy) {
+          p.heavy[h] = u;
+          p.hcnt[h] = c;
+        } else {
+          report_error(p.status, kCapacityOverflow, -1);
+        }
       }
-      else report_error(p.status, kCapacityOverflow, -1);
     }
   }
 }
@@ -441,19 +487,74 @@ __global__ void __launch_bounds__(kScanThreads) emb_seg_final_kernel(EmbBwdParam
 
 // 5. occ[seg_start[u] + rank] = staged-grad row, for rows seen more than once
 __global__ void __launch_bounds__(kEmbThreads) emb_fill_kernel(EmbBwdParams p) {
-  const int64_t N = static_cast<int64_t>(p.num_shards) * p.world * p.stage_cap;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < N;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int slot = static_cast<int>(i / p.stage_cap);
-    const int64_t j = i - static_cast<int64_t>(slot) * p.stage_cap;
-    if (j >= p.stage_count[slot]) continue;
-    const int id = p.stage_ids[i];
-    if (id < 0) continue;
-    const int sh = slot / p.world;
-    const int u = p.row2u[p.shards[sh].row_base + id];
-    if (p.cnt_u[u] <= 1) continue;
-    p.occ[p.seg_start[u] + p.stage_rank[i]] = slot * p.Bl + p.stage_bag[i];
+  const int nslot = p.num_shards * p.world;
+  const int tid = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int nthreads = static_cast<int>(gridDim.x) * blockDim.x;
+  for (int slot = 0; slot < nslot; ++slot) {
+    const int kbase = p.slot_start[slot], cnt = p.slot_start[slot + 1] - kbase;
+    const int64_t sbase = static_cast<int64_t>(slot) * p.stage_cap;
+    const int64_t row_base = p.shards[slot / p.world].row_base;
+    for (int j = tid; j < cnt; j += nthreads) {
+      const int id = p.stage_ids[sbase + j];
+      if (id < 0) continue;
+      const int u = p.row2u[row_base + id];
+      if (p.cnt_u[u] <= 1) continue;
+      p.occ[p.seg_start[u] + p.stage_rank[kbase + j]] = slot * p.Bl + p.stage_bag[sbase + j];
+    }
   }
+}
+
+// exclusive scan of in[0..n) -> out[0..n], n = min(*n_ptr, n_max) read on the device
+__global__ void __launch_bounds__(kScanThreads) dev_scan_partial_kernel(const int* in, const int* n_ptr, int n_max,
+                                                                         int* block_sums) {
+  __shared__ int sh[32];
+  const int n = min(*n_ptr, n_max);
+  const int per = (n + kScanBlocks - 1) / kScanBlocks;
+  const int lo = min(n, static_cast<int>(blockIdx.x) * per), hi = min(n, lo + per);
+  int acc = 0;
+  for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) acc += in[i];
+  acc = block_reduce_sum(acc, sh);
+  if (threadIdx.x == 0) block_sums[blockIdx.x] = acc;
+}
+
+__global__ void __launch_bounds__(kScanThreads) dev_scan_final_kernel(const int* in, const int* n_ptr, int n_max,
+                                                                       const int* block_sums, int* out) {
+  __shared__ int sh[32];
+  __shared__ int wsum[32];
+  const int n = min(*n_ptr, n_max);
+  const int per = (n + kScanBlocks - 1) / kScanBlocks;
+  const int lo = min(n, static_cast<int>(blockIdx.x) * per), hi = min(n, lo + per);
+  int base = 0;
+  for (int i = threadIdx.x; i < blockIdx.x; i += blockDim.x) base += block_sums[i];
+  base = block_reduce_sum(base, sh);
+  const int w = warp_id(), l = lane_id();
+  for (int t0 = lo; t0 < hi; t0 += blockDim.x) {
+    const int i = t0 + threadIdx.x;
+    const int c = i < hi ? in[i] : 0;
+    int x = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(kFull, x, o);
+      if (l >= o) x += y;
+    }
+    if (l == 31) wsum[w] = x;
+    __syncthreads();
+    if (w == 0) {
+      int t = l < blockDim.x / 32 ? wsum[l] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(kFull, t, o);
+        if (l >= o) t += y;
+      }
+      wsum[l] = t;
+    }
+    __syncthreads();
+    if (i < hi) out[i] = base + (w > 0 ? wsum[w - 1] : 0) + x - c;
+    const int tile_total = wsum[blockDim.x / 32 - 1];
+    __syncthreads();
+    base += tile_total;
+  }
+  if (blockIdx.x == kScanBlocks - 1 && threadIdx.x == 0) out[n] = base;
 }
 
 __device__ __forceinline__ float lr_scale(const SparseOptParams& o, float score) {
@@ -586,7 +687,9 @@ __device__ __forceinline__ void apply_update(const SparseOptParams& o, TW* w, in
   }
 }
 
-// 6. light rows: a group of G lanes per unique row, NV float4 per lane.
+// 6. light rows: a group of G lanes per unique row, NV float4 per lane.  (A variant that loaded the
+// next row's metadata one iteration ahead and bulk-prefetched its weights / optimizer state into
+// L2 measured 0-5% slower on the DLRM benchmark.)
 template <typename TW, typename TG, int NV>
 __global__ void __launch_bounds__(kEmbThreads, 4) emb_apply_light_kernel(EmbBwdParams p, int G) {
   __shared__ ShardDesc sd[kMaxShardsSmem];
@@ -724,8 +827,8 @@ __global__ void __launch_bounds__(kScanThreads) emb_heavy_final_kernel(EmbBwdPar
   if (blockIdx.x == kScanBlocks - 1 && threadIdx.x == 0) p.heavy_start[H] = base;
 }
 
-// 7b. heavy occurrences in fixed chunks of kHeavyChunk across warps: fp32
-// partial sums per heavy row, reduced into heavy_acc with vector atomics.
+// 7b. heavy occurrences in fixed chunks of kHeavyChunk across warps: one fp32
+// partial row per (heavy row, chunk) segment, stored (no atomics).
 constexpr int kHeavyChunk = 256;
 template <typename TG, int NV>
 __global__ void __launch_bounds__(kEmbThreads) emb_heavy_accumulate_kernel(EmbBwdParams p) {
@@ -797,9 +900,11 @@ __global__ void __launch_bounds__(kEmbThreads) emb_heavy_accumulate_kernel(EmbBw
         }
       }
       if (act) {
-        float* dst = p.heavy_acc + static_cast<int64_t>(h) * acc_ld + col;
+        // segment (row h, chunk c) has its own partial slot h + c (injective: rows occupy disjoint,
+        // increasing position ranges), so the apply sums the partials in chunk order: deterministic
+        float* dst = p.heavy_acc + (static_cast<int64_t>(h) + c) * acc_ld + col;
 #pragma unroll
-        for (int v = 0; v < NV; ++v) atomicAdd(reinterpret_cast<float4*>(dst + 4 * v), acc[v]);
+        for (int v = 0; v < NV; ++v) reinterpret_cast<float4*>(dst)[v] = acc[v];
       }
     }
   }
@@ -821,15 +926,20 @@ __global__ void __launch_bounds__(kEmbThreads) emb_heavy_apply_kernel(EmbBwdPara
     const long long row = p.uniq_row[u];
     const ShardDesc d = p.shards[p.uniq_shard[u]];
     const bool act = col < d.ncols;
-    float* src = p.heavy_acc + h * acc_ld + col;
     float4 acc[NV], wv[NV];
     const int64_t eoff = d.weight_off + (row - d.row_base) * d.ncols + col;
     TW* wp = reinterpret_cast<TW*>(p.weights) + eoff;
 #pragma unroll
     for (int v = 0; v < NV; ++v) {
-      acc[v] = act ? reinterpret_cast<float4*>(src)[v] : make_float4(0.f, 0.f, 0.f, 0.f);
-      if (act) reinterpret_cast<float4*>(src)[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+      acc[v] = make_float4(0.f, 0.f, 0.f, 0.f);
       wv[v] = act ? load4<TW>(wp + 4 * v) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    // partials of the row's chunks, in chunk order (slot h + c)
+    const int c0 = p.heavy_start[h] / kHeavyChunk, c1 = (p.heavy_start[h + 1] - 1) / kHeavyChunk;
+    for (int c = c0; act && c <= c1; ++c) {
+      const float4* src = reinterpret_cast<const float4*>(p.heavy_acc + (h + c) * acc_ld + col);
+#pragma unroll
+      for (int v = 0; v < NV; ++v) acc[v] = f4_add(acc[v], src[v]);
     }
     apply_update<TW, NV>(o, wp, eoff, row, true, act, d.ncols, acc, wv, p.cnt_u[u], 32, 0);
     if (lane == 0) {
@@ -872,6 +982,8 @@ void bwd_apply_g(const EmbBwdParams& p, int ncols_max, int grid, cudaStream_t s)
 
 void emb_forward(const EmbFwdParams& p, int grid, cudaStream_t s) {
   FLARE_CHECK(grid > 0, "grid must be positive");
+  FLARE_CHECK(static_cast<int64_t>(p.world) * p.Bl + 2ll * grid * (kEmbThreads / 32) * 32 < (1ll << 31),
+              "too many (source, sample) bags for 32-bit work indices");
   FLARE_CHECK(p.vec == 1 || p.vec == 2, "vec must be 1 or 2");
   if (p.w_dtype == kF32) {
     if (p.vec == 1) fwd_dispatch<float, 1>(p, grid, s); else fwd_dispatch<float, 2>(p, grid, s);
@@ -896,10 +1008,17 @@ void emb_backward(const EmbBwdParams& p, int ncols_max, int grid, cudaStream_t s
   FLARE_CHECK(p.num_shards <= kMaxShardsSmem, "too many local shards");
   const int64_t N = static_cast<int64_t>(p.num_shards) * p.world * p.stage_cap;
   FLARE_CHECK(N < (1ll << 31) - 1, "staging space exceeds 2^31 occurrences");
+  FLARE_CHECK(p.num_shards * p.world <= 1024, "at most 1024 (shard, source) slots");
+  FLARE_CHECK(static_cast<int64_t>(p.world) * p.Bl * 64 < (1ll << 31), "too many pooled-gradient chunks");
   FLARE_CUDA_CHECK(cudaMemsetAsync(p.num_unique, 0, 4 * sizeof(int), s));
+  emb_slot_prefix_kernel<<<1, 1024, 0, s>>>(p);
   emb_bwd_pull_count_kernel<<<grid, kEmbThreads, 0, s>>>(p);
-  count_launch();
-  exclusive_scan_int(p.flags, N, p.pos, p.block_sums, s);
+  const int nslot = p.num_shards * p.world;
+  dev_scan_partial_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(p.flags, p.slot_start + nslot,
+                                                               static_cast<int>(N), p.block_sums);
+  dev_scan_final_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(p.flags, p.slot_start + nslot, static_cast<int>(N),
+                                                             p.block_sums, p.pos);
+  count_launch(4);
   emb_emit_kernel<<<grid, kEmbThreads, 0, s>>>(p);
   emb_seg_partial_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(p);
   emb_seg_final_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(p);

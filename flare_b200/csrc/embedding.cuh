@@ -109,7 +109,8 @@ struct EmbBwdParams {
   int64_t grad_stage_ld;
   const int* stage_ids;
   const int* stage_bag;
-  int* stage_rank;   // written by the counting pass
+  int* stage_rank;   // written by the counting pass (compact index: slot_start[slot] + j)
+  int* slot_start;   // [nslot + 1] exclusive prefix of the staged ids per (shard, source) slot
   const int* stage_count;
   const int* stage_len;
   int64_t stage_cap;
@@ -118,8 +119,8 @@ struct EmbBwdParams {
   // dedup / segment scratch
   int* row_count;   // per-row occurrence counter (reset to zero by the apply kernels)
   int* row2u;       // per-row unique index
-  int* flags;       // [nslot*stage_cap] 1 at each row's first occurrence
-  int* pos;         // [nslot*stage_cap + 1] exclusive scan of flags
+  int* flags;       // [T] 1 at each row's first occurrence (compact index)
+  int* pos;         // [T + 1] exclusive scan of flags
   int64_t* uniq_row;
   int* uniq_shard;
   int* cnt_u;       // occurrences of unique row u
@@ -131,7 +132,7 @@ struct EmbBwdParams {
   int* heavy;       // unique rows with more than light_max occurrences
   int* hcnt;        // [H] occurrence count of each heavy row
   int* heavy_start; // [H+1] exclusive prefix of heavy-row counts
-  float* heavy_acc; // [max_heavy][32*4*NV] fp32 accumulators (kept zero between steps)
+  float* heavy_acc; // [max_heavy + max_occ / 256 + 2][32*4*NV] fp32 partial sums per (heavy row, chunk)
   int max_heavy;
   int light_max;
   uint8_t* dirty;   // per-row dirty flags for incremental checkpoints (nullable)

@@ -146,6 +146,46 @@ class DLRM:
         self.bottom.backward(self.dbot, need_input_grad=False)
         return self.loss_sum
 
+    def profile_step(self) -> list[tuple[str, float]]:
+        """One eager training step with CUDA events between its ops; returns (op, ms) in order."""
+        st: dict = {}
+
+        def inter_fwd():
+            interaction_forward(st["bot"], st["pooled"], self.F, self.inter)
+
+        def head():
+            self.loss_sum.zero_()
+            head_bce(st["h"], self.head_w, self.head_b, self.labels, grad_scale=1.0 / self.global_B,
+                     logits=self.logits, loss_sum=self.loss_sum, dh=self.dh, dw=self.head_dw, db=self.head_db)
+
+        def inter_bwd():
+            interaction_backward(st["dinter"], st["bot"], st["pooled"], self.F, self.dbot, self.emb.grad_input,
+                                 relu_mask_bot=True)
+
+        ops = [
+            ("cast_dense", lambda: cast_pad_bf16(self.dense_in, self.xd)),
+            ("bottom_fwd", lambda: st.__setitem__("bot", self.bottom.forward(self.xd))),
+            ("emb_fwd", lambda: st.__setitem__("pooled", self.emb.forward())),
+            ("interaction_fwd", inter_fwd),
+            ("top_fwd", lambda: st.__setitem__("h", self.top.forward(self.inter))),
+            ("head_bce", head),
+            ("top_bwd", lambda: st.__setitem__("dinter", self.top.backward(self.dh, need_input_grad=True))),
+            ("interaction_bwd", inter_bwd),
+            ("bottom_bwd", lambda: self.bottom.backward(self.dbot, need_input_grad=False)),
+            ("emb_bwd", lambda: self.emb.backward()),
+            ("dense_apply", lambda: self.dense.apply()),
+        ]
+        evs = []
+        for name, op in ops:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            evs.append((name, e))
+            op()
+        end = torch.cuda.Event(enable_timing=True)
+        end.record()
+        torch.cuda.synchronize(self.device)
+        return [(name, e.elapsed_time(evs[i + 1][1] if i + 1 < len(evs) else end)) for i, (name, e) in enumerate(evs)]
+
     def train_step(self) -> torch.Tensor:
         """One full optimizer step; returns the device scalar sum of per-sample losses."""
         loss = self.forward_backward()

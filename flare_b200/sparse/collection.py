@@ -214,6 +214,7 @@ class ShardedEmbeddingBagCollection:
         self.stage_count = torch.zeros(nslot, dtype=torch.int32, device=dev)
         self.stage_len = torch.zeros(nslot * self.B, dtype=torch.int32, device=dev)
         self.stage_rank = torch.empty(nslot * self.stage_cap, dtype=torch.int32, device=dev)
+        self.slot_start = torch.zeros(nslot + 1, dtype=torch.int32, device=dev)
         self.grad_stage_ld = self.ncols_max
         self.grad_stage = torch.empty(nslot * self.B * self.ncols_max, dtype=grad_dtype, device=dev)
         self.max_occ = nslot * self.stage_cap
@@ -232,7 +233,9 @@ class ShardedEmbeddingBagCollection:
         self.heavy = torch.empty(self.max_heavy, dtype=torch.int32, device=dev)
         self.heavy_start = torch.empty(self.max_heavy + 1, dtype=torch.int32, device=dev)
         self.hcnt = torch.empty(self.max_heavy, dtype=torch.int32, device=dev)
-        self.heavy_acc = torch.zeros(self.max_heavy * 128 * self.vec, dtype=torch.float32, device=dev)
+        # one fp32 partial row per (heavy row, 256-occurrence chunk) segment
+        self.heavy_acc = torch.zeros((self.max_heavy + self.max_occ // 256 + 2) * 128 * self.vec,
+                                     dtype=torch.float32, device=dev)
 
         # ---- exchange buffers (symmetric when distributed) ----
         self.values_capacity = int(values_capacity or self.F * self.B * self.max_bag)
@@ -374,6 +377,7 @@ class ShardedEmbeddingBagCollection:
             grad_dtype=dtype_code(self.grad_dtype), grad_stage=self.grad_stage.data_ptr(),
             grad_stage_ld=self.grad_stage_ld, stage_ids=self.stage_ids.data_ptr(),
             stage_bag=self.stage_bag.data_ptr(), stage_rank=self.stage_rank.data_ptr(),
+            slot_start=self.slot_start.data_ptr(),
             stage_count=self.stage_count.data_ptr(), stage_len=self.stage_len.data_ptr(),
             stage_cap=self.stage_cap, weights=self.weights.data_ptr(), w_dtype=dtype_code(self.value_dtype),
             row_count=self.row_count.data_ptr(), row2u=self.row2u.data_ptr(), flags=self.flags_occ.data_ptr(),
