@@ -256,6 +256,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.w_dtype = get<int>(d, "w_dtype");
     p.out_dtype = get_or<int>(d, "out_dtype", kBF16);
     p.vec = get_or<int>(d, "vec", 1);
+    p.bulk = get_or<int>(d, "bulk", 0);
     p.slot_map = P<const int>(get_or<uintptr_t>(d, "slot_map", 0));
     p.peer_remap = P<const int* const>(get_or<uintptr_t>(d, "peer_remap", 0));
     p.peer_part = P<float* const>(get_or<uintptr_t>(d, "peer_part", 0));

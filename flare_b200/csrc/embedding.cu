@@ -32,6 +32,7 @@
 // (src/flare/runtime/fluxway/workers/dynamic_embedding.py:362-438, 551-681)
 // and updates rows in its external native store.
 #include "embedding.cuh"
+#include "sm100.cuh"
 #include "sparse_ops.cuh"
 
 #include <algorithm>
@@ -104,8 +105,8 @@ __device__ __forceinline__ int map_id(const EmbFwdParams& p, const ShardDesc& d,
 // lane owning 4*VEC columns, 8 rows in flight per lane.  (A variant that loaded the next bag's
 // offsets and ids while pooling this one and bulk-prefetched its rows into L2 measured 1-3% slower
 // on the DLRM benchmark: the look-ahead state cost a resident block per SM.)
-template <typename TW, int VEC>
-__global__ void __launch_bounds__(kEmbThreads) emb_fwd_kernel(EmbFwdParams p) {
+template <typename TW, int VEC, int MINB>
+__global__ void __launch_bounds__(kEmbThreads, MINB) emb_fwd_kernel(EmbFwdParams p) {
   const uint32_t epoch = p.world > 1 ? *reinterpret_cast<volatile uint32_t*>(p.epoch_ctr) + 1u : 0u;
   if (p.world > 1) {
     if (!entry_barrier(p.flags_local, p.peer_flags, p.world, p.rank, p.flag_in, epoch, p.timeout_ns, p.status))
@@ -226,6 +227,285 @@ __global__ void __launch_bounds__(kEmbThreads) emb_fwd_kernel(EmbFwdParams p) {
     // Exit barrier: the last block to finish tells every peer that this
     // rank's writes into their pooled buffers are complete, then waits until
     // all owners have finished writing into ours.
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned prev = atomicAdd(p.block_counter, 1u);
+      if (prev == gridDim.x - 1) {
+        *p.block_counter = 0u;
+        *p.epoch_ctr = epoch;
+        barrier_signal(p.peer_flags, p.world, p.rank, p.flag_out, epoch);
+        barrier_wait(p.flags_local, p.world, p.flag_out, epoch, p.timeout_ns, p.status);
+      }
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Forward, TMA bulk-gather variant (used when every shard's rows are 16-byte
+// aligned).  A persistent CTA per SM; each warp runs its own pipeline over
+// "jobs" (up to R ids of one bag): the ids of the next job are loaded one job
+// ahead, each id's row is copied HBM -> shared memory by one cp.async.bulk
+// issued by the lane holding the id (completion counted on the stage's
+// mbarrier, no registers held while the copy is in flight), and a job is
+// pooled from shared memory kBulkStages - 1 jobs after it was issued.  The
+// rows of up to kBulkStages jobs per warp are in flight at once, so the
+// gather runs at the memory system's rate instead of the registers' reach.
+// ----------------------------------------------------------------------------
+constexpr int kBulkWarps = 8;
+constexpr int kBulkStages = 4;
+constexpr int kBulkStageBytes = 6144;
+constexpr int kBulkThreads = kBulkWarps * 32;
+constexpr int kBulkMeta = 6;  // item, shard, nvalid, flags (1 first, 2 last), len, pad
+constexpr size_t kBulkSmem = static_cast<size_t>(kBulkWarps) * kBulkStages * kBulkStageBytes +
+                             kBulkWarps * kBulkStages * (8 + kBulkMeta * 4) + kMaxShardsSmem * sizeof(ShardDesc) + 256;
+
+struct BulkCursor {
+  int sh, item, c;       // shard, work item (source-fastest bag index), chunk within the bag
+  int beg, len, fbase;   // bag (broadcast to every lane)
+  bool valid;
+};
+
+template <typename TW, int VEC>
+__global__ void __launch_bounds__(kBulkThreads, 1) emb_fwd_bulk_kernel(EmbFwdParams p) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint8_t* stages = smem_raw;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(stages + static_cast<size_t>(kBulkWarps) * kBulkStages *
+                                                             kBulkStageBytes);
+  int* meta_all = reinterpret_cast<int*>(bars + kBulkWarps * kBulkStages);
+  ShardDesc* sd = reinterpret_cast<ShardDesc*>(meta_all + kBulkWarps * kBulkStages * kBulkMeta);
+
+  const uint32_t epoch = p.world > 1 ? *reinterpret_cast<volatile uint32_t*>(p.epoch_ctr) + 1u : 0u;
+  for (int i = threadIdx.x; i < p.num_shards; i += blockDim.x) sd[i] = p.shards[i];
+  const int warp = warp_id(), lane = lane_id();
+  uint64_t* wbars = bars + warp * kBulkStages;
+  int* wmeta = meta_all + warp * kBulkStages * kBulkMeta;
+  uint8_t* wst = stages + static_cast<size_t>(warp) * kBulkStages * kBulkStageBytes;
+  if (lane == 0) {
+    for (int i = 0; i < kBulkStages; ++i) sm100::mbar_init(wbars + i, 1);
+    sm100::fence_mbar_init();
+  }
+  __syncthreads();
+  if (p.world > 1) {
+    if (!entry_barrier(p.flags_local, p.peer_flags, p.world, p.rank, p.flag_in, epoch, p.timeout_ns, p.status))
+      return;
+  }
+  const int nitems = p.world * p.Bl;
+  const int nwt = static_cast<int>(gridDim.x) * kBulkWarps;  // warps in the grid: item stride
+  const int gw = static_cast<int>(blockIdx.x) * kBulkWarps + warp;
+  const char* W = reinterpret_cast<const char*>(p.weights);
+  constexpr int kSegVals = 16 / static_cast<int>(sizeof(TW));  // values per 16-byte segment
+
+  auto rows_per_job = [&](const ShardDesc& d) {
+    const int rb = d.ncols * static_cast<int>(sizeof(TW));
+    return min(32, kBulkStageBytes / rb);
+  };
+  // raw bag info of (sh, item), read by lane 0 (which also records the staging metadata)
+  auto load_bag_raw = [&](int sh, int item, int& beg, int& len, int& fbase) {
+    beg = len = fbase = 0;
+    if (lane == 0 && sh < p.num_shards && item < nitems) {
+      const ShardDesc& d = sd[sh];
+      const int b = item / p.world, s = item - b * p.world;
+      const int* offs = p.peer_offsets[s];
+      fbase = offs[d.feature * p.Bl];
+      beg = offs[d.feature * p.Bl + b];
+      len = offs[d.feature * p.Bl + b + 1] - beg;
+      const int slot = sh * p.world + s;
+      p.stage_len[static_cast<int64_t>(slot) * p.Bl + b] = len;
+      if (b == 0) p.stage_count[slot] = offs[d.feature * p.Bl + p.Bl] - fbase;
+    }
+  };
+  auto next_bag = [&](int& sh, int& item) {
+    item += nwt;
+    if (item >= nitems) {
+      item = gw;
+      ++sh;
+    }
+  };
+  // first bag
+  BulkCursor A;
+  A.sh = 0;
+  A.item = gw;
+  A.c = 0;
+  if (gw >= nitems) A.sh = p.num_shards;  // more warps than bags: nothing to do
+  A.valid = A.sh < p.num_shards;
+  load_bag_raw(A.sh, A.item, A.beg, A.len, A.fbase);
+  A.beg = __shfl_sync(kFull, A.beg, 0);
+  A.len = __shfl_sync(kFull, A.len, 0);
+  A.fbase = __shfl_sync(kFull, A.fbase, 0);
+  int nb_sh = A.sh, nb_item = A.item;
+  next_bag(nb_sh, nb_item);
+  int nb_beg, nb_len, nb_fbase;  // raw in lane 0
+  load_bag_raw(nb_sh, nb_item, nb_beg, nb_len, nb_fbase);
+
+  auto load_ids = [&](const BulkCursor& X) -> int {
+    if (!X.valid) return -1;
+    const ShardDesc& d = sd[X.sh];
+    const int R = rows_per_job(d);
+    const int j = X.c * R + lane;
+    if (lane >= R || j >= X.len) return -1;
+    const int s = X.item % p.world;
+    const int* vals = (d.flags & 1) ? p.peer_remap[s] : p.peer_values[s];
+    return vals[X.beg + j];
+  };
+  int ids_A = load_ids(A);
+
+  uint32_t parity = 0;  // bit i: parity of the next completion of stage i
+  int head = 0, tail = 0;
+  bool abort = false;
+  float acc[VEC][kSegVals];
+#pragma unroll
+  for (int v = 0; v < VEC; ++v)
+#pragma unroll
+    for (int e = 0; e < kSegVals; ++e) acc[v][e] = 0.f;
+
+  while (A.valid || head > tail) {
+    if (A.valid && head - tail < kBulkStages) {
+      // ---- advance the cursor to job B and start loading its ids
+      const ShardDesc& d = sd[A.sh];
+      const int R = rows_per_job(d);
+      const int njobs = max(1, (A.len + R - 1) / R);
+      BulkCursor B = A;
+      if (A.c + 1 < njobs) {
+        B.c = A.c + 1;
+      } else {
+        B.sh = nb_sh;
+        B.item = nb_item;
+        B.c = 0;
+        B.valid = nb_sh < p.num_shards;
+        B.beg = __shfl_sync(kFull, nb_beg, 0);
+        B.len = __shfl_sync(kFull, nb_len, 0);
+        B.fbase = __shfl_sync(kFull, nb_fbase, 0);
+        next_bag(nb_sh, nb_item);
+        load_bag_raw(nb_sh, nb_item, nb_beg, nb_len, nb_fbase);
+      }
+      const int ids_B = load_ids(B);
+
+      // ---- produce job A: map ids, stage them for the backward, issue the row copies
+      const int b = A.item / p.world, s = A.item - b * p.world;
+      const int slot = A.sh * p.world + s;
+      const int cnt = min(R, max(0, A.len - A.c * R));
+      const int64_t spos = A.beg - A.fbase;
+      const bool stage_ok = spos + A.len <= p.stage_cap;
+      if (A.c == 0 && lane == 0 && !stage_ok) report_error(p.status, kCapacityOverflow, slot);
+      int row = -1;
+      if (lane < cnt) {
+        row = map_id(p, d, ids_A, true);
+        if (stage_ok) {
+          const int64_t at = static_cast<int64_t>(slot) * p.stage_cap + spos + A.c * R + lane;
+          p.stage_ids[at] = row;
+          p.stage_bag[at] = b;
+        }
+      }
+      const unsigned vmask = __ballot_sync(kFull, row >= 0);
+      const int nvalid = __popc(vmask);
+      const int st = head % kBulkStages;
+      const int rb = d.ncols * static_cast<int>(sizeof(TW));
+      if (lane == 0) {
+        int* m = wmeta + st * kBulkMeta;
+        m[0] = A.item;
+        m[1] = A.sh;
+        m[2] = nvalid;
+        m[3] = (A.c == 0 ? 1 : 0) | (A.c + 1 >= njobs ? 2 : 0);
+        m[4] = A.len;
+        sm100::mbar_arrive_expect_tx(wbars + st, static_cast<uint32_t>(nvalid * rb));
+      }
+      __syncwarp();
+      if (row >= 0) {
+        const int pos = __popc(vmask & lanemask_lt());
+        sm100::bulk_load(wst + st * kBulkStageBytes + pos * rb,
+                         W + (d.weight_off + static_cast<int64_t>(row) * d.ncols) * static_cast<int64_t>(sizeof(TW)),
+                         static_cast<uint32_t>(rb), wbars + st);
+      }
+      ++head;
+      A = B;
+      ids_A = ids_B;
+      if (A.valid && head - tail < kBulkStages) continue;  // keep the ring full
+    }
+    // ---- consume the oldest job
+    const int st = tail % kBulkStages;
+    const uint64_t limit = abort ? 1000000ull : p.timeout_ns;
+    if (!sm100::mbar_wait(wbars + st, (parity >> st) & 1u, limit, p.status, 5000 + st)) {
+      abort = true;    // stop issuing; drain the jobs in flight with short waits, then return
+      A.valid = false;
+    }
+    parity ^= 1u << st;
+    const int* m = wmeta + st * kBulkMeta;
+    const int item = m[0], sh = m[1], nvalid = m[2], fl = m[3], len = m[4];
+    const ShardDesc& d = sd[sh];
+    const int rb = d.ncols * static_cast<int>(sizeof(TW));
+    const int segs = rb / 16;
+    const int G = segs >= 32 ? 32 : segs;  // lanes per row
+    const int P = 32 / G;                   // rows per pass
+    const int g = lane / G, l = lane - g * G;
+    if (fl & 1) {
+#pragma unroll
+      for (int v = 0; v < VEC; ++v)
+#pragma unroll
+        for (int e = 0; e < kSegVals; ++e) acc[v][e] = 0.f;
+    }
+    if (!abort) {
+      const uint8_t* base = wst + st * kBulkStageBytes;
+      for (int r = g; r < nvalid; r += P) {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+          const int seg = l + 32 * v;
+          if (seg < segs) {
+            const uint4 q = *reinterpret_cast<const uint4*>(base + r * rb + seg * 16);
+            const TW* t = reinterpret_cast<const TW*>(&q);
+#pragma unroll
+            for (int e = 0; e < kSegVals; ++e) acc[v][e] += to_f32(t[e]);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    sm100::fence_proxy_async_smem();  // these generic reads precede the stage's next async writes
+    ++tail;
+    if (fl & 2) {
+      // pooled row complete: add the P row groups, scale (mean), store
+      for (int o = G; o < 32; o <<= 1)
+#pragma unroll
+        for (int v = 0; v < VEC; ++v)
+#pragma unroll
+          for (int e = 0; e < kSegVals; ++e) acc[v][e] += __shfl_xor_sync(kFull, acc[v][e], o);
+      const int b = item / p.world, s = item - b * p.world;
+      if (d.pooling == 1 && len > 0) {
+        const float inv = 1.f / static_cast<float>(len);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v)
+#pragma unroll
+          for (int e = 0; e < kSegVals; ++e) acc[v][e] *= inv;
+      }
+      if (g == 0) {
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+          const int seg = l + 32 * v;
+          if (seg >= segs) continue;
+          const int col = seg * kSegVals;
+#pragma unroll
+          for (int e = 0; e < kSegVals; e += 4) {
+            const float4 q = make_float4(acc[v][e], acc[v][e + 1], acc[v][e + 2], acc[v][e + 3]);
+            if (d.part_col >= 0) {
+              float* out = p.peer_part[s] + (static_cast<int64_t>(d.rw_idx) * p.Bl + b) * p.part_stride +
+                           d.part_col + col + e;
+              store4<float>(out, q);
+            } else if (p.out_dtype == kBF16) {
+              store4<__nv_bfloat16>(reinterpret_cast<__nv_bfloat16*>(p.peer_out[s]) +
+                                        static_cast<int64_t>(b) * p.out_stride + d.out_col + col + e,
+                                    q);
+            } else {
+              store4<float>(reinterpret_cast<float*>(p.peer_out[s]) + static_cast<int64_t>(b) * p.out_stride +
+                                d.out_col + col + e,
+                            q);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  if (p.world > 1) {
     __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -690,8 +970,8 @@ __device__ __forceinline__ void apply_update(const SparseOptParams& o, TW* w, in
 // 6. light rows: a group of G lanes per unique row, NV float4 per lane.  (A variant that loaded the
 // next row's metadata one iteration ahead and bulk-prefetched its weights / optimizer state into
 // L2 measured 0-5% slower on the DLRM benchmark.)
-template <typename TW, typename TG, int NV>
-__global__ void __launch_bounds__(kEmbThreads, 4) emb_apply_light_kernel(EmbBwdParams p, int G) {
+template <typename TW, typename TG, int NV, int MINB>
+__global__ void __launch_bounds__(kEmbThreads, MINB) emb_apply_light_kernel(EmbBwdParams p, int G) {
   __shared__ ShardDesc sd[kMaxShardsSmem];
   for (int i = threadIdx.x; i < p.num_shards; i += blockDim.x) sd[i] = p.shards[i];
   __syncthreads();
@@ -949,9 +1229,10 @@ __global__ void __launch_bounds__(kEmbThreads) emb_heavy_apply_kernel(EmbBwdPara
   }
 }
 
+// 4 resident blocks per SM (64 registers, a few spilled) measured ~1% faster than 3 (80 registers).
 template <typename TW, int VEC>
 void fwd_dispatch(const EmbFwdParams& p, int grid, cudaStream_t s) {
-  emb_fwd_kernel<TW, VEC><<<grid, kEmbThreads, 0, s>>>(p);
+  emb_fwd_kernel<TW, VEC, 4><<<grid, kEmbThreads, 0, s>>>(p);
   count_launch();
 }
 
@@ -959,7 +1240,8 @@ template <typename TW, typename TG>
 void bwd_apply(const EmbBwdParams& p, int ncols_max, int grid, cudaStream_t s) {
   // light rows: 2 float4 (8 columns) per lane -> ncols_max / 8 lanes per row
   const int G = std::max(1, ncols_max / 8);
-  emb_apply_light_kernel<TW, TG, 2><<<grid, kEmbThreads, 0, s>>>(p, G);
+  // 4 blocks per SM: ~10% faster than 3 on the DLRM benchmark despite a few spilled registers
+  emb_apply_light_kernel<TW, TG, 2, 4><<<grid, kEmbThreads, 0, s>>>(p, G);
   emb_heavy_partial_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(p);
   emb_heavy_final_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(p);
   if (ncols_max > 128) {
@@ -978,14 +1260,33 @@ void bwd_apply_g(const EmbBwdParams& p, int ncols_max, int grid, cudaStream_t s)
   else bwd_apply<TW, float>(p, ncols_max, grid, s);
 }
 
+template <typename TW>
+void fwd_bulk_launch(const EmbFwdParams& p, cudaStream_t s) {
+  int dev = 0, sms = 0;
+  FLARE_CUDA_CHECK(cudaGetDevice(&dev));
+  FLARE_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  auto k1 = emb_fwd_bulk_kernel<TW, 1>;
+  auto k2 = emb_fwd_bulk_kernel<TW, 2>;
+  auto k = p.vec == 2 ? k2 : k1;
+  FLARE_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kBulkSmem)));
+  k<<<sms, kBulkThreads, kBulkSmem, s>>>(p);
+  count_launch();
+}
+
 }  // namespace
 
 void emb_forward(const EmbFwdParams& p, int grid, cudaStream_t s) {
   FLARE_CHECK(grid > 0, "grid must be positive");
+  FLARE_CHECK(p.num_shards <= kMaxShardsSmem, "too many local shards");
   FLARE_CHECK(static_cast<int64_t>(p.world) * p.Bl + 2ll * grid * (kEmbThreads / 32) * 32 < (1ll << 31),
               "too many (source, sample) bags for 32-bit work indices");
   FLARE_CHECK(p.vec == 1 || p.vec == 2, "vec must be 1 or 2");
-  if (p.w_dtype == kF32) {
+  if (p.bulk) {
+    // every shard's rows are 16-byte aligned (checked by the caller): TMA bulk-gather forward
+    if (p.w_dtype == kF32) fwd_bulk_launch<float>(p, s);
+    else if (p.w_dtype == kF16) fwd_bulk_launch<__half>(p, s);
+    else fwd_bulk_launch<__nv_bfloat16>(p, s);
+  } else if (p.w_dtype == kF32) {
     if (p.vec == 1) fwd_dispatch<float, 1>(p, grid, s); else fwd_dispatch<float, 2>(p, grid, s);
   } else if (p.w_dtype == kF16) {
     if (p.vec == 1) fwd_dispatch<__half, 1>(p, grid, s); else fwd_dispatch<__half, 2>(p, grid, s);

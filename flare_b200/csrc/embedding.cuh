@@ -75,7 +75,9 @@ struct EmbFwdParams {
   const void* weights;
   int w_dtype;
   int out_dtype;  // kBF16 or kF32
-  int vec;        // float4 vectors per lane: 1 (shard width <= 128) or 2 (<= 256)
+  int vec;        // float4 vectors per lane: 1 (shard width <= 128) or 2 (<= 256); bulk: 16-byte segments
+                  // per lane: 1 (rows <= 512 bytes) or 2 (<= 1024)
+  int bulk;       // 1: TMA bulk-gather forward (every shard's rows 16-byte aligned, <= 1024 bytes)
   const int* slot_map;  // row -> HBM slot maps of host-tier shards (ShardDesc::slot_map_off), or null
   const int* const* peer_remap;  // [world] slot buffers of dynamic tables (same layout as values), or null
   float* const* peer_part;       // [world] fp32 partial pooled rows [rw_slots][Bl][part_stride] (row-wise tables)
