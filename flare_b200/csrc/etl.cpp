@@ -17,8 +17,12 @@
 //   bucketize      : index of the first bound >= value (sorted bounds);
 //   fixed_width    : trunc(value / width);
 //   pack_fids      : slot in the top 16 bits, the value's low 48 bits below;
-//   intersect_lists: per row, how many items of list A occur in list B.
-// The reference implements these with Cython (processing/native/_scan.pyx:73)
+//   intersect_lists: per row, how many items of list A occur in list B;
+//   parse_rows     : the record format read from an Arrow string column's
+//                    buffers, with category vocabularies, variable-length
+//                    lists, direct and metadata columns (details below).
+// The reference implements these with Cython (processing/native/_scan.pyx:73,
+// builder/_fast_parse.pyx:87-350)
 // and Numba (builder/encoding/sparse_id.py:206,253,269, encoding/dense.py:30,40,
 // cross/fea_ops.py:63-94); this is a separate implementation of the same
 // record format and encodings.
@@ -286,11 +290,226 @@ py::array_t<int32_t> intersect_lists(py::array_t<int64_t, py::array::c_style> a,
   return out;
 }
 
+// ---------------------------------------------------------------------------
+// parse_rows: the same record format read straight from an Arrow string
+// column (its data buffer + int64 offsets, no per-row Python objects), with
+// four kinds of outputs:
+//   fixed    : code -> [rows, length] int64 / float64 (as scan_records);
+//   list     : code -> variable-length int64 / float64 values + [rows + 1]
+//              offsets (caller-sized value capacity);
+//   category : code -> int32 [rows]: the value token looked up in that code's
+//              vocabulary (token bytes -> index), unknown tokens -> the code's
+//              default index, missing -> -3;
+//   direct   : TAB column -> int64 [rows] (the column parsed as an integer);
+//   metadata : TAB column -> int32 [rows] through a string -> id table
+//              (unknown -> the table's default).
+// Validity bytes are set per output row where a value was seen.
+// ---------------------------------------------------------------------------
+struct Out {
+  int kind;  // 0 fixed, 1 list, 2 category
+  int length;
+  bool is_float;
+  char* data;
+  int64_t cap;  // rows (fixed/category) or value capacity (list)
+  int64_t* offs;
+  uint8_t* valid;
+  const std::unordered_map<std::string, int32_t>* vocab;
+  int32_t dflt;
+};
+
+template <typename T>
+T* arr_ptr(py::handle h, int64_t& n) {
+  py::array a = py::reinterpret_borrow<py::array>(h);
+  if (!(a.flags() & py::array::c_style)) throw std::invalid_argument("arrays must be C-contiguous");
+  if (a.itemsize() != sizeof(T)) throw std::invalid_argument("array has the wrong element size");
+  n = a.shape(0);
+  return static_cast<T*>(a.mutable_data());
+}
+
+py::tuple parse_rows(py::array_t<uint8_t, py::array::c_style> data, py::array_t<int64_t, py::array::c_style> offsets,
+                     int64_t n_rows, int feature_column, py::dict plan, py::dict categories, py::list direct,
+                     py::list metadata) {
+  if (offsets.size() < n_rows + 1) throw std::invalid_argument("offsets shorter than n_rows + 1");
+  const uint8_t* base = data.data();
+  const int64_t* ro = offsets.data();
+  if (n_rows > 0 && (ro[0] < 0 || ro[n_rows] > data.size())) throw std::out_of_range("offsets outside the data");
+  // category vocabularies
+  std::unordered_map<int64_t, std::unordered_map<std::string, int32_t>> vocabs;
+  std::unordered_map<int64_t, int32_t> dflts;
+  for (auto item : categories) {
+    const int64_t code = item.first.cast<int64_t>();
+    const auto t = item.second.cast<py::tuple>();
+    auto& v = vocabs[code];
+    for (auto kv : t[0].cast<py::dict>()) v[kv.first.cast<std::string>()] = kv.second.cast<int32_t>();
+    dflts[code] = t[1].cast<int32_t>();
+  }
+  // plan: code -> (kind, length, is_float, buffer, offsets or None, validity or None)
+  std::unordered_map<int64_t, Out> outs;
+  for (auto item : plan) {
+    const int64_t code = item.first.cast<int64_t>();
+    const auto t = item.second.cast<py::tuple>();
+    Out o{};
+    o.kind = t[0].cast<int>();
+    o.length = t[1].cast<int>();
+    o.is_float = t[2].cast<bool>();
+    int64_t n = 0;
+    o.data = o.kind == 2 ? reinterpret_cast<char*>(arr_ptr<int32_t>(t[3], n))
+                         : (o.is_float ? reinterpret_cast<char*>(arr_ptr<double>(t[3], n))
+                                       : reinterpret_cast<char*>(arr_ptr<int64_t>(t[3], n)));
+    o.cap = n;
+    if (o.kind == 1) {
+      int64_t no = 0;
+      o.offs = arr_ptr<int64_t>(t[4], no);
+      if (no < n_rows + 1) throw std::invalid_argument("list offsets shorter than n_rows + 1");
+      o.offs[0] = 0;
+    }
+    if (!t[5].is_none()) {
+      int64_t nv = 0;
+      o.valid = arr_ptr<uint8_t>(t[5], nv);
+      if (nv < n_rows) throw std::invalid_argument("validity shorter than n_rows");
+    }
+    if (o.kind == 2) {
+      const auto it = vocabs.find(code);
+      if (it == vocabs.end()) throw std::invalid_argument("category output without a vocabulary");
+      o.vocab = &it->second;
+      o.dflt = dflts[code];
+    }
+    if (o.kind != 1 && o.cap < n_rows) throw std::invalid_argument("output has fewer rows than n_rows");
+    outs[code] = o;
+  }
+  struct Direct {
+    int col;
+    int64_t* out;
+    uint8_t* valid;
+  };
+  std::vector<Direct> dcols;
+  for (auto h : direct) {
+    const auto t = h.cast<py::tuple>();
+    int64_t n = 0, nv = 0;
+    Direct d{t[0].cast<int>(), arr_ptr<int64_t>(t[1], n), t[2].is_none() ? nullptr : arr_ptr<uint8_t>(t[2], nv)};
+    if (n < n_rows) throw std::invalid_argument("direct output shorter than n_rows");
+    dcols.push_back(d);
+  }
+  struct Meta {
+    int col;
+    std::unordered_map<std::string, int32_t> table;
+    int32_t dflt;
+    int32_t* out;
+  };
+  std::vector<Meta> mcols;
+  for (auto h : metadata) {
+    const auto t = h.cast<py::tuple>();
+    Meta m;
+    m.col = t[0].cast<int>();
+    for (auto kv : t[1].cast<py::dict>()) m.table[kv.first.cast<std::string>()] = kv.second.cast<int32_t>();
+    m.dflt = t[2].cast<int32_t>();
+    int64_t n = 0;
+    m.out = arr_ptr<int32_t>(t[3], n);
+    if (n < n_rows) throw std::invalid_argument("metadata output shorter than n_rows");
+    mcols.push_back(std::move(m));
+  }
+  // outputs start as null / empty
+  for (auto& kv : outs) {
+    Out& o = kv.second;
+    if (o.kind == 0) {
+      for (int64_t i = 0; i < n_rows * o.length; ++i) {
+        if (o.is_float) reinterpret_cast<double*>(o.data)[i] = static_cast<double>(kNull);
+        else reinterpret_cast<int64_t*>(o.data)[i] = kNull;
+      }
+    } else if (o.kind == 2) {
+      for (int64_t i = 0; i < n_rows; ++i) reinterpret_cast<int32_t*>(o.data)[i] = static_cast<int32_t>(kNull);
+    }
+    if (o.valid) std::memset(o.valid, 0, static_cast<size_t>(n_rows));
+  }
+  for (auto& d : dcols) {
+    for (int64_t i = 0; i < n_rows; ++i) d.out[i] = kNull;
+    if (d.valid) std::memset(d.valid, 0, static_cast<size_t>(n_rows));
+  }
+  for (auto& m : mcols)
+    for (int64_t i = 0; i < n_rows; ++i) m.out[i] = m.dflt;
+  std::unordered_map<int64_t, int64_t> fill;  // list outputs: values written so far
+  for (auto& kv : outs)
+    if (kv.second.kind == 1) fill[kv.first] = 0;
+
+  for (int64_t row = 0; row < n_rows; ++row) {
+    const char* p = reinterpret_cast<const char*>(base + ro[row]);
+    const char* le = reinterpret_cast<const char*>(base + ro[row + 1]);
+    if (le > p && le[-1] == '\n') --le;
+    const char* col = p;
+    for (int c = 0; col <= le; ++c) {
+      const char* tab = static_cast<const char*>(std::memchr(col, '\t', le - col));
+      const char* ce = tab ? tab : le;
+      for (auto& d : dcols)
+        if (d.col == c && ce > col) {
+          d.out[row] = parse_int(col, ce);
+          if (d.valid) d.valid[row] = 1;
+        }
+      for (auto& m : mcols)
+        if (m.col == c) {
+          const auto it = m.table.find(std::string(col, ce));
+          m.out[row] = it == m.table.end() ? m.dflt : it->second;
+        }
+      if (c == feature_column) {
+        const char* kvp = col;
+        while (kvp < ce) {
+          const char* sep = static_cast<const char*>(std::memchr(kvp, '\x02', ce - kvp));
+          const char* kve = sep ? sep : ce;
+          const char* eq = static_cast<const char*>(std::memchr(kvp, '\x03', kve - kvp));
+          if (eq) {
+            const int64_t code = parse_int(kvp, eq);
+            const auto it = outs.find(code);
+            if (it != outs.end()) {
+              Out& o = it->second;
+              const char* v = eq + 1;
+              if (o.kind == 2) {
+                const auto f = o.vocab->find(std::string(v, kve));
+                reinterpret_cast<int32_t*>(o.data)[row] = f == o.vocab->end() ? o.dflt : f->second;
+              } else if (o.kind == 0) {
+                for (int k = 0; k < o.length && v <= kve; ++k) {
+                  const char* comma = static_cast<const char*>(std::memchr(v, ',', kve - v));
+                  const char* vend = (o.length > 1 && comma) ? comma : kve;
+                  const int64_t off = row * o.length + k;
+                  if (o.is_float) reinterpret_cast<double*>(o.data)[off] = parse_float(v, vend);
+                  else reinterpret_cast<int64_t*>(o.data)[off] = parse_int(v, vend);
+                  if (vend == kve) break;
+                  v = vend + 1;
+                }
+              } else {
+                int64_t& n = fill[code];
+                while (v < kve) {
+                  const char* comma = static_cast<const char*>(std::memchr(v, ',', kve - v));
+                  const char* vend = comma ? comma : kve;
+                  if (n >= o.cap) throw std::out_of_range("list values exceed the output capacity");
+                  if (o.is_float) reinterpret_cast<double*>(o.data)[n] = parse_float(v, vend);
+                  else reinterpret_cast<int64_t*>(o.data)[n] = parse_int(v, vend);
+                  ++n;
+                  v = comma ? comma + 1 : kve;
+                }
+              }
+              if (o.valid) o.valid[row] = 1;
+            }
+          }
+          if (!sep) break;
+          kvp = sep + 1;
+        }
+      }
+      if (!tab) break;
+      col = tab + 1;
+    }
+    for (auto& kv : outs)
+      if (kv.second.kind == 1) kv.second.offs[row + 1] = fill[kv.first];
+  }
+  py::dict counts;
+  for (auto& kv : fill) counts[py::int_(kv.first)] = kv.second;
+  return py::make_tuple(n_rows, counts);
+}
+
 }  // namespace flare_etl
 
 void register_etl(py::module_& m) {
   auto e = m.def_submodule("etl", "native feature-ETL kernels (host)");
   e.def("scan_records", &flare_etl::scan_records);
+  e.def("parse_rows", &flare_etl::parse_rows);
   e.def("fnv1a_lists", &flare_etl::fnv1a_lists, py::arg("values"), py::arg("offsets"), py::arg("buckets") = 0);
   e.def("fnv1a_seeded", &flare_etl::fnv1a_seeded);
   e.def("hash_bucket", &flare_etl::hash_bucket);

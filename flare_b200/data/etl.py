@@ -88,6 +88,130 @@ class RecordScanner:
         return ({c: b[:rows] for c, b in bufs.items()}, {c: v[:rows] for c, v in valid.items()}, rows)
 
 
+class ArrowRowParser:
+    """Parse an Arrow string column of records (one record per row) without per-row Python objects.
+
+    ``fixed``: code -> (length, is_float) fixed-width outputs [rows, length];
+    ``lists``: code -> is_float variable-length outputs (values, int64 offsets [rows+1]);
+    ``categories``: code -> (vocabulary {token: index}, default index) -> int32 [rows];
+    ``direct``: name -> TAB column parsed as int64; ``metadata``: name -> (TAB column,
+    {string: id}, default id) -> int32.  Missing values are -3 (``NULL``).
+    Reference behaviour: src/flare/data/pipeline/production/builder/_fast_parse.pyx:87-350.
+    """
+
+    def __init__(self, *, feature_column: int, fixed=None, lists=None, categories=None, direct=None,
+                 metadata=None):
+        self.feature_column = feature_column
+        self.fixed = dict(fixed or {})
+        self.lists = dict(lists or {})
+        self.categories = {c: (dict(v), int(d)) for c, (v, d) in (categories or {}).items()}
+        self.direct = dict(direct or {})
+        self.metadata = {n: (c, dict(t), int(d)) for n, (c, t, d) in (metadata or {}).items()}
+        both = set(self.fixed) & set(self.lists) | set(self.fixed) & set(self.categories) | \
+            set(self.lists) & set(self.categories)
+        if both:
+            raise ValueError(f"feature codes with two output kinds: {sorted(both)}")
+
+    @staticmethod
+    def _buffers(column):
+        import pyarrow as pa
+
+        if isinstance(column, pa.ChunkedArray):
+            column = column.combine_chunks()
+        if pa.types.is_large_string(column.type) or pa.types.is_large_binary(column.type):
+            odt = np.int64
+        elif pa.types.is_string(column.type) or pa.types.is_binary(column.type):
+            odt = np.int32
+        else:
+            raise TypeError(f"expected a string column, got {column.type}")
+        _, obuf, dbuf = column.buffers()
+        n = len(column)
+        offs = np.frombuffer(obuf, dtype=odt, count=column.offset + n + 1)[column.offset:].astype(np.int64)
+        data = np.frombuffer(dbuf, dtype=np.uint8) if dbuf is not None else np.zeros(1, np.uint8)
+        return data, offs, n
+
+    def parse(self, column, *, list_capacity: int | None = None) -> dict:
+        data, offs, n = self._buffers(column)
+        cap = list_capacity or max(16, int(offs[-1] - offs[0]) // 2 + 16)
+        plan, out = {}, {"fixed": {}, "lists": {}, "categories": {}, "direct": {}, "metadata": {}, "valid": {}}
+        for code, (length, is_float) in self.fixed.items():
+            buf = np.empty((n, length), dtype=np.float64 if is_float else np.int64)
+            val = np.empty(n, dtype=np.uint8)
+            plan[code] = (0, length, bool(is_float), buf, None, val)
+            out["fixed"][code], out["valid"][code] = buf, val
+        for code, is_float in self.lists.items():
+            vals = np.empty(cap, dtype=np.float64 if is_float else np.int64)
+            lo = np.empty(n + 1, dtype=np.int64)
+            val = np.empty(n, dtype=np.uint8)
+            plan[code] = (1, 0, bool(is_float), vals, lo, val)
+            out["lists"][code], out["valid"][code] = (vals, lo), val
+        cats = {}
+        for code, (vocab, dflt) in self.categories.items():
+            buf = np.empty(n, dtype=np.int32)
+            val = np.empty(n, dtype=np.uint8)
+            plan[code] = (2, 1, False, buf, None, val)
+            cats[code] = ({k.encode() if isinstance(k, str) else k: v for k, v in vocab.items()}, dflt)
+            out["categories"][code], out["valid"][code] = buf, val
+        direct = []
+        for name, col in self.direct.items():
+            buf = np.empty(n, dtype=np.int64)
+            direct.append((col, buf, None))
+            out["direct"][name] = buf
+        meta = []
+        for name, (col, table, dflt) in self.metadata.items():
+            buf = np.empty(n, dtype=np.int32)
+            meta.append((col, {k.encode() if isinstance(k, str) else k: v for k, v in table.items()}, dflt, buf))
+            out["metadata"][name] = buf
+        _, counts = _etl().parse_rows(data, offs, n, self.feature_column, plan, cats, direct, meta)
+        for code, used in counts.items():
+            vals, lo = out["lists"][code]
+            out["lists"][code] = (vals[:used], lo)
+        return out
+
+    def parse_reference(self, lines: list[str]) -> dict:
+        """Pure-Python restatement (the oracle of the tests)."""
+        n = len(lines)
+        res = {"fixed": {c: np.full((n, ln), NULL, dtype=np.float64 if f else np.int64)
+                         for c, (ln, f) in self.fixed.items()},
+               "lists": {c: [[] for _ in range(n)] for c in self.lists},
+               "categories": {c: np.full(n, NULL, dtype=np.int32) for c in self.categories},
+               "direct": {k: np.full(n, NULL, dtype=np.int64) for k in self.direct},
+               "metadata": {k: np.full(n, d, dtype=np.int32) for k, (_, _, d) in self.metadata.items()}}
+
+        def num(tok, is_float):
+            try:
+                return float(tok) if is_float else int(float(tok))
+            except ValueError:
+                return NULL
+
+        for r, line in enumerate(lines):
+            cols = line.rstrip("\n").split("\t")
+            for k, col in self.direct.items():
+                if col < len(cols) and cols[col]:
+                    res["direct"][k][r] = num(cols[col], False)
+            for k, (col, table, d) in self.metadata.items():
+                if col < len(cols):
+                    res["metadata"][k][r] = table.get(cols[col], d)
+            if self.feature_column >= len(cols):
+                continue
+            for item in cols[self.feature_column].split("\x02"):
+                if "\x03" not in item:
+                    continue
+                code_s, val = item.split("\x03", 1)
+                code = num(code_s, False)
+                if code in self.fixed:
+                    ln, f = self.fixed[code]
+                    parts = val.split(",") if ln > 1 else [val]
+                    for j, tok in enumerate(parts[:ln]):
+                        res["fixed"][code][r, j] = num(tok, f)
+                elif code in self.lists:
+                    res["lists"][code][r] = [num(t, self.lists[code]) for t in val.split(",") if t != ""]
+                elif code in self.categories:
+                    vocab, d = self.categories[code]
+                    res["categories"][code][r] = vocab.get(val, d)
+        return res
+
+
 # ---------------------------------------------------------------- encoders
 def hash_bucket(values: np.ndarray, buckets: int, default_value: int = NULL) -> np.ndarray:
     return _etl().hash_bucket(np.ascontiguousarray(values, dtype=np.int64), int(buckets), int(default_value))
@@ -171,5 +295,5 @@ def intersect_lists_reference(a, oa, b, ob):
     return np.array(out, dtype=np.int32)
 
 
-__all__ = ["FieldSpec", "NULL", "RecordScanner", "bucketize", "fixed_width", "fnv1a_lists", "fnv1a_seeded",
+__all__ = ["ArrowRowParser", "FieldSpec", "NULL", "RecordScanner", "bucketize", "fixed_width", "fnv1a_lists", "fnv1a_seeded",
            "hash_bucket", "intersect_lists", "pack_fids"]

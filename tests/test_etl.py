@@ -62,3 +62,34 @@ def test_encoders_match_reference():
     b = rng.integers(0, 50, ob[-1])
     a = rng.integers(0, 50, off[-1])
     np.testing.assert_array_equal(etl.intersect_lists(a, off, b, ob), etl.intersect_lists_reference(a, off, b, ob))
+
+
+def test_arrow_row_parser_matches_reference():
+    pa = pytest.importorskip("pyarrow")
+    rng = np.random.default_rng(2)
+    vocab = {"red": 1, "green": 2, "blue": 3}
+    lines = []
+    for i in range(300):
+        items = []
+        if rng.random() < 0.8:
+            items.append(f"5\x03{rng.integers(-3, 10**9)}")
+        if rng.random() < 0.8:
+            items.append("8\x03" + ",".join(str(x) for x in rng.integers(0, 100, rng.integers(0, 6))))
+        if rng.random() < 0.8:
+            items.append(f"9\x03{rng.choice(['red', 'green', 'blue', 'mauve'])}")
+        if rng.random() < 0.5:
+            items.append(f"11\x03{rng.random():.5f},{rng.random():.5f}")
+        lines.append(f"{rng.integers(0, 10**6)}\t{rng.choice(['ios', 'android', 'web'])}\t" + "\x02".join(items))
+    parser = etl.ArrowRowParser(feature_column=2, fixed={5: (1, False), 11: (2, True)}, lists={8: False},
+                                categories={9: (vocab, 0)}, direct={"uid": 0},
+                                metadata={"os": (1, {"ios": 1, "android": 2}, 0)})
+    col = pa.array(lines, type=pa.string()).slice(7)   # a slice exercises the offset handling
+    got = parser.parse(col)
+    want = parser.parse_reference(lines[7:])
+    for c in (5, 11):
+        np.testing.assert_array_equal(got["fixed"][c], want["fixed"][c])
+    vals, offs = got["lists"][8]
+    assert [list(vals[offs[i]:offs[i + 1]]) for i in range(len(offs) - 1)] == want["lists"][8]
+    np.testing.assert_array_equal(got["categories"][9], want["categories"][9])
+    np.testing.assert_array_equal(got["direct"]["uid"], want["direct"]["uid"])
+    np.testing.assert_array_equal(got["metadata"]["os"], want["metadata"]["os"])
