@@ -1,0 +1,168 @@
+// CPU sparse embedding ops (host C++, at::parallel_for): the CPU backend of the
+// padded gather / pool / scatter contract and the first-occurrence dedup.
+//
+//   cpu_gather         out[slot] = inv == pad ? 0 : emb[inv]              (value dtype kept)
+//   cpu_gather_pooled  out[bag] = sum_e emb[inv[bag, e]] over non-pad e  (fp32 accumulation)
+//   cpu_scatter        out[row] += grad[slot] for slots with inv == row  (fp32)
+//   cpu_scatter_pooled out[row] += grad[bag] for every non-pad id of the bag
+//   cpu_unique_first   unique keys in first-occurrence order, inverse, first index
+//
+// The scatters are deterministic: slots are deduplicated first, grouped per
+// unique row by a counting sort (slot order kept) and each unique row sums its
+// slots in order, rows in parallel; no atomics, no private copies of the table.
+// fp16 / bf16 values are decoded to fp32 with the library conversions.
+// Reference behaviour: src/flare/ops/sparse_gather.py:16-148,
+// sparse_scatter.py:15-144 and sparse_unique.py:17-49 (Numba kernels).
+#include <torch/extension.h>
+#include <ATen/Parallel.h>
+
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+namespace py = pybind11;
+
+namespace flare_cpu {
+
+enum : int { kF32 = 0, kBF16 = 1, kF16 = 2 };
+
+inline float load_val(const void* base, int dtype, int64_t i) {
+  if (dtype == kF32) return static_cast<const float*>(base)[i];
+  if (dtype == kBF16) return static_cast<float>(static_cast<const c10::BFloat16*>(base)[i]);
+  return static_cast<float>(static_cast<const c10::Half*>(base)[i]);
+}
+
+inline void store_val(void* base, int dtype, int64_t i, float v) {
+  if (dtype == kF32) static_cast<float*>(base)[i] = v;
+  else if (dtype == kBF16) static_cast<c10::BFloat16*>(base)[i] = c10::BFloat16(v);
+  else static_cast<c10::Half*>(base)[i] = c10::Half(v);
+}
+
+inline int64_t esize(int dtype) { return dtype == kF32 ? 4 : 2; }
+
+void cpu_gather(uintptr_t emb, int dtype, uintptr_t inv, int64_t slots, int dim, int pad, uintptr_t out) {
+  const int32_t* iv = reinterpret_cast<const int32_t*>(inv);
+  const char* e = reinterpret_cast<const char*>(emb);
+  char* o = reinterpret_cast<char*>(out);
+  const int64_t rb = dim * esize(dtype);
+  at::parallel_for(0, slots, 1024, [&](int64_t lo, int64_t hi) {
+    for (int64_t s = lo; s < hi; ++s) {
+      if (iv[s] == pad) std::memset(o + s * rb, 0, rb);
+      else std::memcpy(o + s * rb, e + static_cast<int64_t>(iv[s]) * rb, rb);
+    }
+  });
+}
+
+void cpu_gather_pooled(uintptr_t emb, int dtype, uintptr_t inv, int64_t bags, int E, int dim, int pad,
+                       uintptr_t out) {
+  const int32_t* iv = reinterpret_cast<const int32_t*>(inv);
+  const void* e = reinterpret_cast<const void*>(emb);
+  void* o = reinterpret_cast<void*>(out);
+  at::parallel_for(0, bags, 256, [&](int64_t lo, int64_t hi) {
+    std::vector<float> acc(dim);
+    for (int64_t b = lo; b < hi; ++b) {
+      std::fill(acc.begin(), acc.end(), 0.f);
+      for (int k = 0; k < E; ++k) {
+        const int32_t r = iv[b * E + k];
+        if (r == pad) continue;
+        const int64_t base = static_cast<int64_t>(r) * dim;
+        for (int d = 0; d < dim; ++d) acc[d] += load_val(e, dtype, base + d);
+      }
+      for (int d = 0; d < dim; ++d) store_val(o, dtype, b * dim + d, acc[d]);
+    }
+  });
+}
+
+// first-occurrence dedup with an open-addressing table (Fibonacci hashing)
+struct Dedup {
+  std::vector<int64_t> unique, first;
+  std::vector<int32_t> inverse;
+};
+
+Dedup dedup(const int64_t* keys, int64_t n, bool skip, int64_t skip_key) {
+  Dedup r;
+  r.inverse.assign(n, -1);
+  int64_t cap = 16;
+  while (cap < 2 * n) cap <<= 1;
+  std::vector<int64_t> tk(cap);
+  std::vector<int32_t> tu(cap, -1);
+  const int shift = 64 - __builtin_ctzll(static_cast<uint64_t>(cap));
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t k = keys[i];
+    if (skip && k == skip_key) continue;
+    uint64_t h = (static_cast<uint64_t>(k) * 11400714819323198485ull) >> shift;
+    while (true) {
+      if (tu[h] < 0) {
+        tu[h] = static_cast<int32_t>(r.unique.size());
+        tk[h] = k;
+        r.unique.push_back(k);
+        r.first.push_back(i);
+        break;
+      }
+      if (tk[h] == k) break;
+      h = (h + 1) & static_cast<uint64_t>(cap - 1);
+    }
+    r.inverse[i] = tu[h];
+  }
+  return r;
+}
+
+py::tuple cpu_unique_first(torch::Tensor keys) {
+  TORCH_CHECK(!keys.is_cuda() && (keys.scalar_type() == torch::kInt64 || keys.scalar_type() == torch::kInt32),
+              "cpu_unique_first: int32/int64 CPU keys");
+  auto k64 = keys.reshape(-1).to(torch::kInt64).contiguous();
+  const int64_t n = k64.numel();
+  Dedup d = dedup(k64.data_ptr<int64_t>(), n, false, 0);
+  const int64_t u = static_cast<int64_t>(d.unique.size());
+  auto uniq = torch::from_blob(d.unique.data(), {u}, torch::kInt64).clone().to(keys.scalar_type());
+  auto inv = torch::from_blob(d.inverse.data(), {n}, torch::kInt32).clone();
+  auto first = torch::from_blob(d.first.data(), {u}, torch::kInt64).clone();
+  return py::make_tuple(uniq, inv, first);
+}
+
+// rows of `inv` (pad skipped) -> per unique row its source indices in order; then out[row] = sum
+void scatter_grouped(const int32_t* iv, int64_t n, int pad, int dim, const void* g, int gdtype, int64_t g_div,
+                     float* out) {
+  std::vector<int64_t> k(n);
+  for (int64_t i = 0; i < n; ++i) k[i] = iv[i];
+  Dedup d = dedup(k.data(), n, true, pad);
+  const int64_t U = static_cast<int64_t>(d.unique.size());
+  std::vector<int64_t> start(U + 1, 0);
+  for (int64_t i = 0; i < n; ++i)
+    if (d.inverse[i] >= 0) ++start[d.inverse[i] + 1];
+  for (int64_t u = 0; u < U; ++u) start[u + 1] += start[u];
+  std::vector<int64_t> pos(start.begin(), start.end() - 1), order(start[U]);
+  for (int64_t i = 0; i < n; ++i)
+    if (d.inverse[i] >= 0) order[pos[d.inverse[i]]++] = i;
+  at::parallel_for(0, U, 64, [&](int64_t lo, int64_t hi) {
+    for (int64_t u = lo; u < hi; ++u) {
+      float* o = out + d.unique[u] * dim;
+      for (int64_t q = start[u]; q < start[u + 1]; ++q) {
+        const int64_t src = (order[q] / g_div) * dim;  // g_div = E for pooled gradients (one per bag)
+        for (int c = 0; c < dim; ++c) o[c] += load_val(g, gdtype, src + c);
+      }
+    }
+  });
+}
+
+void cpu_scatter(uintptr_t grad, int gdtype, uintptr_t inv, int64_t slots, int dim, int pad, uintptr_t out) {
+  scatter_grouped(reinterpret_cast<const int32_t*>(inv), slots, pad, dim, reinterpret_cast<const void*>(grad),
+                  gdtype, 1, reinterpret_cast<float*>(out));
+}
+
+void cpu_scatter_pooled(uintptr_t grad, int gdtype, uintptr_t inv, int64_t bags, int E, int dim, int pad,
+                        uintptr_t out) {
+  scatter_grouped(reinterpret_cast<const int32_t*>(inv), bags * E, pad, dim, reinterpret_cast<const void*>(grad),
+                  gdtype, E, reinterpret_cast<float*>(out));
+}
+
+}  // namespace flare_cpu
+
+void register_sparse_cpu(py::module_& m) {
+  auto c = m.def_submodule("cpu", "CPU sparse embedding ops (host)");
+  c.def("gather", &flare_cpu::cpu_gather);
+  c.def("gather_pooled", &flare_cpu::cpu_gather_pooled);
+  c.def("scatter", &flare_cpu::cpu_scatter);
+  c.def("scatter_pooled", &flare_cpu::cpu_scatter_pooled);
+  c.def("unique_first", &flare_cpu::cpu_unique_first);
+}

@@ -5,7 +5,8 @@ contracts.py:16-96) and factory (src/flare/ops/factory.py:14): ``gather``,
 ``gather_pooled``, ``scatter`` and ``scatter_pooled`` over a padded inverse
 index with a pad sentinel, plus ``unique_first_occurrence``
 (src/flare/ops/sparse_unique.py:52).  Two backends exist: ``cuda`` (the
-hand-written sm_100a kernels) and ``cpu`` (PyTorch reference code).  The
+hand-written sm_100a kernels) and ``cpu`` (native C++ kernels, with PyTorch
+reference code as the fallback and test oracle).  The
 product training path does not use these padded ops: it uses the fused
 sharded embedding kernels in ``flare_b200.sparse.collection``.
 """
@@ -62,10 +63,30 @@ class SparseEmbeddingOperator(ABC):
         return None
 
 
+def _cpu_native():
+    """The native CPU kernels (``csrc/sparse_cpu.cpp``), or None when the extension is not built."""
+    try:
+        return native().cpu
+    except Exception:  # pragma: no cover - extension not built
+        return None
+
+
 class CpuSparseEmbeddingOperator(SparseEmbeddingOperator):
-    """PyTorch CPU implementation; fp16 tables are pooled in fp32."""
+    """CPU backend: native C++ kernels (fp32 accumulation, deterministic scatters); PyTorch
+    reference code when the extension is not built (and as the oracle in the tests)."""
+
+    def __init__(self, value_dtype: str, gradient_dtype: str = "float32", *, use_native: bool = True):
+        super().__init__(value_dtype, gradient_dtype)
+        self.nat = _cpu_native() if use_native else None
 
     def gather(self, emb_flat, inverse, batch_size, emb_dim, pad_index):
+        if self.nat is not None:
+            inv = _check_inverse(inverse)
+            emb = emb_flat.contiguous()
+            out = torch.empty((inv.numel(), emb_dim), dtype=emb.dtype)
+            self.nat.gather(emb.data_ptr(), dtype_code(emb.dtype), inv.data_ptr(), inv.numel(), emb_dim, pad_index,
+                            out.data_ptr())
+            return out.reshape(batch_size, -1, emb_dim)
         inv = _check_inverse(inverse).long()
         emb = emb_flat.reshape(-1, emb_dim)
         mask = inv != pad_index
@@ -75,6 +96,13 @@ class CpuSparseEmbeddingOperator(SparseEmbeddingOperator):
 
     def gather_pooled(self, emb_flat, inverse, batch_size, emb_dim, target_widths, pad_index):
         F, E = pooled_sparse_widths(target_widths)
+        if self.nat is not None:
+            inv = _check_inverse(inverse)
+            emb = emb_flat.contiguous()
+            out = torch.empty((batch_size, F, emb_dim), dtype=emb.dtype)
+            self.nat.gather_pooled(emb.data_ptr(), dtype_code(emb.dtype), inv.data_ptr(), batch_size * F, E,
+                                   emb_dim, pad_index, out.data_ptr())
+            return out
         inv = _check_inverse(inverse).long().reshape(batch_size, F, E)
         emb = emb_flat.reshape(-1, emb_dim).float()
         mask = (inv != pad_index).unsqueeze(-1)
@@ -82,6 +110,13 @@ class CpuSparseEmbeddingOperator(SparseEmbeddingOperator):
         return (rows * mask).sum(2).to(emb_flat.dtype)
 
     def scatter(self, emb_rows, emb_dim, inverse, pad_index, gradient):
+        if self.nat is not None:
+            inv = _check_inverse(inverse)
+            g = gradient.contiguous()
+            out = torch.zeros((emb_rows, emb_dim), dtype=torch.float32)
+            self.nat.scatter(g.data_ptr(), dtype_code(g.dtype), inv.data_ptr(), inv.numel(), emb_dim, pad_index,
+                             out.data_ptr())
+            return out
         inv = _check_inverse(inverse).long().reshape(-1)
         g = gradient.reshape(-1, emb_dim).float()
         out = torch.zeros((emb_rows, emb_dim), dtype=torch.float32)
@@ -91,6 +126,16 @@ class CpuSparseEmbeddingOperator(SparseEmbeddingOperator):
 
     def scatter_pooled(self, emb_rows, emb_dim, inverse, pad_index, gradient, target_widths):
         F, E = pooled_sparse_widths(target_widths)
+        if self.nat is not None:
+            inv = _check_inverse(inverse)
+            g = gradient.contiguous()
+            bags = g.numel() // emb_dim
+            if bags * E != inv.numel() or bags % F:
+                raise ValueError("inverse and gradient shapes disagree")
+            out = torch.zeros((emb_rows, emb_dim), dtype=torch.float32)
+            self.nat.scatter_pooled(g.data_ptr(), dtype_code(g.dtype), inv.data_ptr(), bags, E, emb_dim, pad_index,
+                                    out.data_ptr())
+            return out
         inv = _check_inverse(inverse).long().reshape(-1, F, E)
         g = gradient.reshape(-1, F, 1, emb_dim).float().expand(-1, F, E, emb_dim).reshape(-1, emb_dim)
         flat = inv.reshape(-1)
@@ -186,6 +231,9 @@ def unique_first_occurrence(values: torch.Tensor):
     if not on_cuda(values):
         if values.numel() == 0:
             return values.reshape(-1).clone(), torch.empty(0, dtype=torch.int32), torch.empty(0, dtype=torch.int64)
+        nat = _cpu_native()
+        if nat is not None:  # open-addressing hash, one pass in occurrence order
+            return nat.unique_first(values)
         # Vectorised CPU path: torch.unique + first index per group.
         flat = values.reshape(-1)
         uniq, inv = torch.unique(flat, sorted=True, return_inverse=True)

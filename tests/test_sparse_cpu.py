@@ -121,3 +121,29 @@ def test_sparse_precision_rescue():
         prepare_sparse_native_gradient(g.float(), transport_dtype="bfloat16", native_dtype="float32")
     with pytest.raises(FloatingPointError):
         require_finite_sparse_values(torch.tensor([float("nan")]), "float32", boundary="t")
+
+
+@pytest.mark.parametrize("dtype,vd", [(torch.float32, "float32"), (torch.float16, "float16")])
+def test_native_cpu_ops_match_torch_reference(dtype, vd):
+    from flare_b200.ops.sparse import _cpu_native
+
+    if _cpu_native() is None:
+        pytest.skip("native extension not built")
+    g = torch.Generator().manual_seed(3)
+    nat = CpuSparseEmbeddingOperator(vd, use_native=True)
+    ref = CpuSparseEmbeddingOperator(vd, use_native=False)
+    rows, dim, B, F, E = 300, 32, 16, 4, 6
+    emb = torch.randn(rows * dim, generator=g).to(dtype)
+    inv = torch.randint(-1, rows, (B * F * E,), generator=g, dtype=torch.int32)
+    torch.testing.assert_close(nat.gather(emb, inv, B, dim, -1), ref.gather(emb, inv, B, dim, -1))
+    torch.testing.assert_close(nat.gather_pooled(emb, inv, B, dim, (F, E), -1).float(),
+                               ref.gather_pooled(emb, inv, B, dim, (F, E), -1).float(), rtol=1e-3, atol=1e-3)
+    gp = torch.randn(B * F * dim, generator=g).to(dtype)
+    torch.testing.assert_close(nat.scatter_pooled(rows, dim, inv, -1, gp, (F, E)),
+                               ref.scatter_pooled(rows, dim, inv, -1, gp, (F, E)), rtol=1e-5, atol=1e-5)
+    gs = torch.randn(inv.numel() * dim, generator=g).to(dtype)
+    torch.testing.assert_close(nat.scatter(rows, dim, inv, -1, gs), ref.scatter(rows, dim, inv, -1, gs),
+                               rtol=1e-5, atol=1e-5)
+    keys = torch.randint(0, 97, (2000,), generator=g)
+    for a, b in zip(unique_first_occurrence(keys), unique_first_occurrence_reference(keys)):
+        assert torch.equal(a, b)
