@@ -48,6 +48,7 @@ def parse():
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--profile-ops", action="store_true", help="also print a per-op eager breakdown (stderr)")
+    p.add_argument("--uniform-plan", action="store_true", help="place tables by columns only (no cost model)")
     p.add_argument("--seed", type=int, default=0)
     return p.parse_args()
 
@@ -123,8 +124,18 @@ def main():
     from flare_b200._native import native
     from flare_b200.training.trainer import DLRMTrainer
 
+    costs = None
+    if world > 1 and not args.uniform_plan:
+        # per-table work of the global batch (lookups + the unique rows the backward updates), identical on
+        # every rank (same seed): the planner balances it, splitting heavy tables into row-wise pieces
+        from flare_b200.sparse.planner import estimate_table_costs
+
+        costs = estimate_table_costs(vocabs, int(B * world * (args.max_bag + 1) / 2), 1.05, device=dev)
     trainer = DLRMTrainer(cfg, B, max_bag_size=args.max_bag, rank=rank, world_size=world, device=dev,
-                          seed=args.seed, use_graph=not args.no_graph, values_capacity=max_nnz + 1024)
+                          seed=args.seed, use_graph=not args.no_graph, values_capacity=max_nnz + 1024,
+                          table_costs=costs)
+    plan = trainer.model.emb.plan
+    n_rw = len({p.table for p in plan.placements if p.row_shards > 1})
     model = trainer.model
     stream = torch.cuda.current_stream(dev)
     log(f"model built: {len(model.emb.shards)} local shards, {model.emb.memory_bytes() / 1e9:.1f} GB sparse state")
@@ -219,7 +230,9 @@ def main():
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded Zipf ids, random-init weights)",
             "impl": "flare",
             "config": {"model": MODEL, "global_batch": B * world, "batch_per_gpu": B, "seq_len": None,
-                       "parallelism": f"dp{world} dense (fused ZeRO-1) + table/column-wise sharded embeddings",
+                       "parallelism": f"dp{world} dense (fused ZeRO-1) + table/column/row-wise sharded embeddings",
+                       "sharding_plan": ("uniform" if costs is None else "cost-weighted (lookups + 2 x unique rows)")
+                       + f", {n_rw} tables in row-wise pieces",
                        "tables": 26, "total_rows": sum(vocabs), "embedding_dim": 128,
                        "embedding_storage": "fp32", "sparse_optimizer": "rowwise_adagrad",
                        "dense_optimizer": "adam", "l2": "inputs larger than L2 (tables > 100 GB, "

@@ -23,7 +23,7 @@ dynamic_embedding.py:69-106).
 """
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+from dataclasses import dataclass, field, replace
 
 import torch
 import torch.nn as nn
@@ -32,6 +32,7 @@ from ..ops.dense import cast_pad_bf16, head_bce, interaction_backward, interacti
 from ..parallel.symm import SymmetricHeap
 from ..sparse.collection import ShardedEmbeddingBagCollection
 from ..sparse.config import SparseOptimizerConfig, SparseTableSpec
+from ..sparse.planner import ShardingPlan, plan_sharding
 from ..training.flat import DenseOptimizerConfig, DenseState, FlatParams
 from .mlp import MLPTower, pad_to
 
@@ -77,12 +78,22 @@ def dlrm_benchmark_tables(vocab_sizes: list[int], dim: int = 128, optimizer: Spa
             for i, v in enumerate(vocab_sizes)]
 
 
+def dlrm_plan(cfg: DLRMConfig, world_size: int, table_costs: list[float] | None = None) -> ShardingPlan | None:
+    """Sharding plan weighted by per-table work (None: the collection's default plan)."""
+    if table_costs is None:
+        return None
+    tabs = [t if t.optimizer == cfg.sparse_optimizer else replace(t, optimizer=cfg.sparse_optimizer)
+            for t in cfg.tables]
+    return plan_sharding(tabs, world_size, expected_lookups=table_costs)
+
+
 class DLRM:
     """Fused B200 DLRM for one rank's local batch."""
 
     def __init__(self, cfg: DLRMConfig, batch_size: int, *, max_bag_size: int, rank: int = 0, world_size: int = 1,
                  device: torch.device | None = None, heap: SymmetricHeap | None = None, seed: int = 0,
-                 global_batch_size: int | None = None, values_capacity: int | None = None):
+                 global_batch_size: int | None = None, values_capacity: int | None = None,
+                 table_costs: list[float] | None = None, plan: ShardingPlan | None = None):
         self.cfg = cfg
         self.B = int(batch_size)
         self.global_B = int(global_batch_size or batch_size * world_size)
@@ -111,7 +122,8 @@ class DLRM:
 
         self.emb = ShardedEmbeddingBagCollection(
             cfg.tables, self.B, max_bag_size=max_bag_size, rank=rank, world_size=world_size, device=dev, heap=heap,
-            optimizer=cfg.sparse_optimizer, seed=seed, values_capacity=values_capacity)
+            optimizer=cfg.sparse_optimizer, seed=seed, values_capacity=values_capacity,
+            plan=plan if plan is not None else dlrm_plan(cfg, world_size, table_costs))
 
         bf = dict(dtype=torch.bfloat16, device=dev)
         self.dense_in = torch.zeros(self.B, cfg.num_dense, dtype=torch.float32, device=dev)

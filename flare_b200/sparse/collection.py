@@ -297,13 +297,14 @@ class ShardedEmbeddingBagCollection:
 
     @staticmethod
     def exchange_bytes(tables: list[SparseTableSpec], batch_size: int, max_bag_size: int,
-                       values_capacity: int | None = None) -> int:
+                       values_capacity: int | None = None, plan: ShardingPlan | None = None) -> int:
         """Symmetric memory of the exchange buffers (ids, pooled rows, pooled grads, row-wise partials)."""
         F, B = len(tables), int(batch_size)
         cap = values_capacity or F * B * max_bag_size
         dim = sum(t.embedding_dim for t in tables)
-        rw = [t for t in tables if t.shards > 1]
-        part = 4 * max([t.shards for t in rw], default=0) * B * sum(t.embedding_dim for t in rw)
+        shards = [plan.row_shards(i) if plan is not None else t.shards for i, t in enumerate(tables)]
+        rw = [i for i, r in enumerate(shards) if r > 1]
+        part = 4 * max([shards[i] for i in rw], default=0) * B * sum(tables[i].embedding_dim for i in rw)
         remap = 4 * cap if any(t.dynamic for t in tables) else 0
         return 4 * (F * B + 1) + 4 * cap + remap + 2 * 4 * B * dim + part + NUM_FLAG_ARRAYS * 64 + 4096
 

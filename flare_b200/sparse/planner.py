@@ -70,14 +70,22 @@ def plan_sharding(
     hbm_budget_bytes: float | None = None,
     max_rounds: int = 64,
     allow_rowwise_column_split: bool = False,
+    row_split: bool = True,
+    rw_overhead: float = 0.06,
 ) -> ShardingPlan:
-    """Place tables (or column slices) on ranks.
+    """Place tables (or column slices, or row-wise pieces) on ranks.
 
     Column splits are made only for tables whose optimizer is elementwise:
     a row-wise optimizer (row-wise Adagrad/Adam) keeps one state value per
     row, and splitting columns would give each slice its own state, which
     changes the update.  ``allow_rowwise_column_split`` permits it anyway
-    (per-slice row state, as some embedding libraries do).
+    (per-slice row state, as some embedding libraries do).  Where a column
+    split is not allowed, ``row_split`` lets the balancing rounds double a
+    table's row-wise pieces instead (exact for every optimizer); each piece
+    is charged ``rw_overhead`` of the table's work for its partial-sum rows
+    and its pull of the pooled gradients.  ``expected_lookups`` is the
+    relative work per column of each table (lookups, plus the unique rows the
+    backward updates: ``estimate_table_costs``).
     """
     if world_size < 1:
         raise ValueError("world_size must be >= 1")
@@ -96,7 +104,7 @@ def plan_sharding(
         pieces += [(i, 0, t.embedding_dim, r, R) for r in range(R)]
 
     def pwork(pc):
-        return work[pc[0]] * pc[2] / pc[4]
+        return work[pc[0]] * pc[2] * (1.0 / pc[4] + (rw_overhead if pc[4] > 1 else 0.0))
 
     def assign(pcs):
         order = sorted(range(len(pcs)), key=lambda k: (-pwork(pcs[k]), pcs[k][0], pcs[k][3], pcs[k][1]))
@@ -131,11 +139,23 @@ def plan_sharding(
             cand = [k for k in range(len(pieces)) if owner[k] == hot and pieces[k][2] // 2 in VALID_SHARD_WIDTHS
                     and pieces[k][2] >= 32 and pieces[k][4] == 1
                     and (allow_rowwise_column_split or not tables[pieces[k][0]].optimizer.needs_row_state)]
-            if not cand:
-                break
-            k = max(cand, key=lambda k: (pwork(pieces[k]), -k))
-            ti, cb, nc, _, _ = pieces[k]
-            pieces = pieces[:k] + [(ti, cb, nc // 2, 0, 1), (ti, cb + nc // 2, nc // 2, 0, 1)] + pieces[k + 1:]
+            if cand:
+                k = max(cand, key=lambda k: (pwork(pieces[k]), -k))
+                ti, cb, nc, _, _ = pieces[k]
+                pieces = pieces[:k] + [(ti, cb, nc // 2, 0, 1), (ti, cb + nc // 2, nc // 2, 0, 1)] + pieces[k + 1:]
+            else:
+                # double the row-wise pieces of the heaviest full-width table on the hot rank
+                rcand = [k for k in range(len(pieces)) if owner[k] == hot and row_split
+                         and pieces[k][2] == tables[pieces[k][0]].embedding_dim
+                         and pieces[k][4] * 2 <= world_size and not tables[pieces[k][0]].dynamic
+                         and tables[pieces[k][0]].cache_rows is None
+                         and tables[pieces[k][0]].num_embeddings >= 2 * pieces[k][4]]
+                if not rcand:
+                    break
+                ti = pieces[max(rcand, key=lambda k: (pwork(pieces[k]), -k))][0]
+                R = next(pc[4] for pc in pieces if pc[0] == ti) * 2
+                dim = tables[ti].embedding_dim
+                pieces = [pc for pc in pieces if pc[0] != ti] + [(ti, 0, dim, r, R) for r in range(R)]
             owner, loads = assign(pieces)
             if score(loads) < best[0]:
                 best = (score(loads), pieces, owner, loads)
@@ -144,4 +164,24 @@ def plan_sharding(
     return ShardingPlan(world_size, placements, tuple(out_cols), c)
 
 
-__all__ = ["ShardPlacement", "ShardingPlan", "VALID_SHARD_WIDTHS", "plan_sharding"]
+def estimate_table_costs(vocab_sizes: list[int], lookups: int, zipf_s: float = 1.05, *, unique_weight: float = 2.0,
+                         seed: int = 0, device="cpu") -> list[float]:
+    """Relative per-column work of each table for ``lookups`` Zipf(``zipf_s``) ids per step.
+
+    Work = lookups (forward gather, backward gradient gather) + ``unique_weight`` x the
+    distinct rows a step touches (the backward reads and writes each once), counted on a
+    sample of the id distribution, normalised by ``lookups``.
+    """
+    import torch
+
+    from ..data.synthetic import zipf_ids
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    out = []
+    for v in vocab_sizes:
+        u = torch.unique(zipf_ids(int(lookups), int(v), zipf_s, g, device=device)).numel()
+        out.append(1.0 + unique_weight * u / float(lookups))
+    return out
+
+
+__all__ = ["ShardPlacement", "ShardingPlan", "VALID_SHARD_WIDTHS", "estimate_table_costs", "plan_sharding"]

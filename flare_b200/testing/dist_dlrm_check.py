@@ -75,9 +75,13 @@ def main(steps: int = 3, B: int = 128, row_shards: int = 1) -> int:
         merged = {k: v for part in gathered for k, v in part.items()}
         full = tr.model.emb.assemble_tables(merged, cfg.tables)
         want = ref.model.emb.assemble_tables(export_tables(ref), ref_cfg.tables)
+        # After the first step the dense weights differ by fp32 summation order (per-rank partial sums
+        # vs one batch), so the bf16 pooled gradients can differ by one bf16 ulp (2^-8 relative) and
+        # each row-wise Adagrad step (about lr in size) by lr * 2^-8: bound the table error by that.
+        tol = 2e-4 + 2.0 * opt.learning_rate * 2.0 ** -8 * (steps - 1)
         for t, w in enumerate(want):
             err = (full[t] - w).abs().max().item()
-            if err > 2e-4:
+            if err > tol:
                 print(f"table {t}: max abs diff {err}", file=sys.stderr)
                 ok = False
         rd = ref.model.dense

@@ -22,7 +22,7 @@ import torch
 
 from .._native import native
 from ..data.synthetic import SparseBatch
-from ..models.dlrm import DLRM, DLRMConfig
+from ..models.dlrm import DLRM, DLRMConfig, dlrm_plan
 from ..parallel.dist import barrier
 from ..parallel.symm import SymmetricHeap
 from ..sparse.collection import ShardedEmbeddingBagCollection
@@ -172,18 +172,20 @@ class FusedTrainer:
 class DLRMTrainer(FusedTrainer):
     def __init__(self, cfg: DLRMConfig, batch_size: int, *, max_bag_size: int, rank: int = 0, world_size: int = 1,
                  device: torch.device | None = None, seed: int = 0, use_graph: bool = True,
-                 values_capacity: int | None = None, heap_bytes: int | None = None):
+                 values_capacity: int | None = None, heap_bytes: int | None = None,
+                 table_costs: list[float] | None = None):
         device = device or torch.device("cuda", torch.cuda.current_device())
         heap = None
+        plan = dlrm_plan(cfg, world_size, table_costs)
         if world_size > 1:
             exchange = ShardedEmbeddingBagCollection.exchange_bytes(cfg.tables, batch_size, max_bag_size,
-                                                                    values_capacity)
+                                                                    values_capacity, plan=plan)
             dense = 6 * 16 * 1024 * 1024  # flat fp32 grads + bf16 params for up to 16M parameters
             need = heap_bytes or (exchange + dense + 64 * 1024 * 1024)
             heap = SymmetricHeap(need, rank=rank, world_size=world_size, device=device)
         self.heap = heap
         model = DLRM(cfg, batch_size, max_bag_size=max_bag_size, rank=rank, world_size=world_size,
-                     device=device, heap=heap, seed=seed, values_capacity=values_capacity)
+                     device=device, heap=heap, seed=seed, values_capacity=values_capacity, plan=plan)
         super().__init__(model, batch_size, device=device, rank=rank, world_size=world_size, use_graph=use_graph)
 
 
