@@ -77,12 +77,16 @@ def main(steps: int = 3, B: int = 128, row_shards: int = 1) -> int:
         want = ref.model.emb.assemble_tables(export_tables(ref), ref_cfg.tables)
         # After the first step the dense weights differ by fp32 summation order (per-rank partial sums
         # vs one batch), so the bf16 pooled gradients can differ by one bf16 ulp (2^-8 relative) and
-        # each row-wise Adagrad step (about lr in size) by lr * 2^-8: bound the table error by that.
+        # each row-wise Adagrad step (about lr in size) by lr * 2^-8.  A row whose first gradient is
+        # ~0 is the exception: Adagrad normalises it to a step of +-lr whatever its size, so a sign
+        # flip moves it by 2 lr.  Bound the typical error tightly and allow such rows to be rare.
         tol = 2e-4 + 2.0 * opt.learning_rate * 2.0 ** -8 * (steps - 1)
         for t, w in enumerate(want):
-            err = (full[t] - w).abs().max().item()
-            if err > tol:
-                print(f"table {t}: max abs diff {err}", file=sys.stderr)
+            diff = (full[t] - w).abs()
+            err = diff.max().item()
+            frac = (diff > tol).float().mean().item()
+            if (steps == 1 and err > tol) or frac > 2e-3 or err > 2.0 * opt.learning_rate * steps + 1e-6:
+                print(f"table {t}: max abs diff {err}, fraction above {tol:.2e}: {frac:.2e}", file=sys.stderr)
                 ok = False
         rd = ref.model.dense
         for name, e in tr.model.params.entries.items():
