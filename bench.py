@@ -48,7 +48,9 @@ def parse():
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--profile-ops", action="store_true", help="also print a per-op eager breakdown (stderr)")
-    p.add_argument("--uniform-plan", action="store_true", help="place tables by columns only (no cost model)")
+    p.add_argument("--plan", choices=["uniform", "cost", "cost-rw"], default="uniform",
+                   help="table placement: by columns only; weighted by sampled per-table work; and also "
+                        "splitting heavy tables into row-wise pieces")
     p.add_argument("--seed", type=int, default=0)
     return p.parse_args()
 
@@ -125,7 +127,7 @@ def main():
     from flare_b200.training.trainer import DLRMTrainer
 
     costs = None
-    if world > 1 and not args.uniform_plan:
+    if world > 1 and args.plan != "uniform":
         # per-table work of the global batch (lookups + the unique rows the backward updates), identical on
         # every rank (same seed): the planner balances it, splitting heavy tables into row-wise pieces
         from flare_b200.sparse.planner import estimate_table_costs
@@ -133,7 +135,7 @@ def main():
         costs = estimate_table_costs(vocabs, int(B * world * (args.max_bag + 1) / 2), 1.05, device=dev)
     trainer = DLRMTrainer(cfg, B, max_bag_size=args.max_bag, rank=rank, world_size=world, device=dev,
                           seed=args.seed, use_graph=not args.no_graph, values_capacity=max_nnz + 1024,
-                          table_costs=costs)
+                          table_costs=costs, row_split=args.plan == "cost-rw")
     plan = trainer.model.emb.plan
     n_rw = len({p.table for p in plan.placements if p.row_shards > 1})
     model = trainer.model
@@ -191,7 +193,7 @@ def main():
             model.set_batch(b.dense, b.labels, b.offsets, b.values, non_blocking=True)
             prof = model.profile_step()
         tot = sum(t for _, t in prof)
-        log("per-op (eager, ms): " + ", ".join(f"{n}={t:.3f}" for n, t in prof) + f", total={tot:.3f}")
+        log(f"{len(model.emb.shards)} shards; per-op (eager, ms): " + ", ".join(f"{n}={t:.3f}" for n, t in prof) + f", total={tot:.3f}")
     # e2e through the public API: inputs in pinned host memory, loss read back every step
     e2e = None
     if not args.no_e2e:
@@ -233,6 +235,7 @@ def main():
                        "parallelism": f"dp{world} dense (fused ZeRO-1) + table/column/row-wise sharded embeddings",
                        "sharding_plan": ("uniform" if costs is None else "cost-weighted (lookups + 2 x unique rows)")
                        + f", {n_rw} tables in row-wise pieces",
+                       "embed_shards_rank0": len(model.emb.shards),
                        "tables": 26, "total_rows": sum(vocabs), "embedding_dim": 128,
                        "embedding_storage": "fp32", "sparse_optimizer": "rowwise_adagrad",
                        "dense_optimizer": "adam", "l2": "inputs larger than L2 (tables > 100 GB, "

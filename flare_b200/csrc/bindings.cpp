@@ -261,6 +261,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.bulk = get_or<int>(d, "bulk", 0);
     p.slot_map = P<const int>(get_or<uintptr_t>(d, "slot_map", 0));
     p.peer_remap = P<const int* const>(get_or<uintptr_t>(d, "peer_remap", 0));
+    p.fetch_offs = P<int>(get_or<uintptr_t>(d, "fetch_offs", 0));
     p.peer_part = P<float* const>(get_or<uintptr_t>(d, "peer_part", 0));
     p.part_stride = get_or<int64_t>(d, "part_stride", 0);
     p.rw_tables = P<const flare::RwTable>(get_or<uintptr_t>(d, "rw_tables", 0));

@@ -101,6 +101,35 @@ __device__ __forceinline__ int map_id(const EmbFwdParams& p, const ShardDesc& d,
   return id;
 }
 
+// Multi-GPU forward prologue: after the entry barrier, copy every (owned shard, source rank) run of
+// bag offsets and ids from the source's memory into local buffers (the ids land in the staging rows,
+// where the forward maps them in place).  Bandwidth-bound bulk reads over NVLink replace the
+// forward's two dependent remote round trips per bag (offsets, then ids).
+__global__ void __launch_bounds__(kEmbThreads) emb_fetch_kernel(EmbFwdParams p) {
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(p.epoch_ctr) + 1u;
+  if (!entry_barrier(p.flags_local, p.peer_flags, p.world, p.rank, p.flag_in, epoch, p.timeout_ns, p.status))
+    return;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t nth = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int nslot = p.num_shards * p.world;
+  for (int slot = 0; slot < nslot; ++slot) {
+    const int sh = slot / p.world, s = slot - sh * p.world;
+    const ShardDesc& d = p.shards[sh];
+    const int* offs = p.peer_offsets[s] + d.feature * p.Bl;
+    int* lo = p.fetch_offs + static_cast<int64_t>(slot) * (p.Bl + 1);
+    for (int64_t i = tid; i <= p.Bl; i += nth) lo[i] = offs[i];
+    const int fbase = offs[0];
+    int64_t cnt = offs[p.Bl] - fbase;
+    if (cnt > p.stage_cap) {
+      if (tid == 0) report_error(p.status, kCapacityOverflow, slot);
+      cnt = p.stage_cap;
+    }
+    const int* src = ((d.flags & 1) ? p.peer_remap[s] : p.peer_values[s]) + fbase;
+    int* dst = p.stage_ids + static_cast<int64_t>(slot) * p.stage_cap;
+    for (int64_t i = tid; i < cnt; i += nth) dst[i] = src[i];
+  }
+}
+
 // Forward: every (source rank, sample) bag of every owned shard; a group of G lanes per bag, each
 // lane owning 4*VEC columns, 8 rows in flight per lane.  (A variant that loaded the next bag's
 // offsets and ids while pooling this one and bulk-prefetched its rows into L2 measured 1-3% slower
@@ -108,7 +137,8 @@ __device__ __forceinline__ int map_id(const EmbFwdParams& p, const ShardDesc& d,
 template <typename TW, int VEC, int MINB>
 __global__ void __launch_bounds__(kEmbThreads, MINB) emb_fwd_kernel(EmbFwdParams p) {
   const uint32_t epoch = p.world > 1 ? *reinterpret_cast<volatile uint32_t*>(p.epoch_ctr) + 1u : 0u;
-  if (p.world > 1) {
+  const bool fetched = p.fetch_offs != nullptr;  // offsets and ids already copied here (emb_fetch_kernel)
+  if (p.world > 1 && !fetched) {
     if (!entry_barrier(p.flags_local, p.peer_flags, p.world, p.rank, p.flag_in, epoch, p.timeout_ns, p.status))
       return;
   }
@@ -135,14 +165,14 @@ __global__ void __launch_bounds__(kEmbThreads, MINB) emb_fwd_kernel(EmbFwdParams
       const int s = active ? static_cast<int>(item - static_cast<int64_t>(b) * p.world) : 0;
       int beg = 0, len = 0, fbase = 0;
       if (active && l == 0) {
-        const int* offs = p.peer_offsets[s];
-        const int o = d.feature * p.Bl + b;
-        fbase = offs[d.feature * p.Bl];
-        beg = offs[o];
-        len = offs[o + 1] - beg;
         const int slot = sh * p.world + s;
+        const int* offs = fetched ? p.fetch_offs + static_cast<int64_t>(slot) * (p.Bl + 1)
+                                  : p.peer_offsets[s] + d.feature * p.Bl;
+        fbase = offs[0];
+        beg = offs[b];
+        len = offs[b + 1] - beg;
         p.stage_len[static_cast<int64_t>(slot) * p.Bl + b] = len;
-        if (b == 0) p.stage_count[slot] = offs[d.feature * p.Bl + p.Bl] - fbase;
+        if (b == 0) p.stage_count[slot] = offs[p.Bl] - fbase;
       }
       beg = __shfl_sync(kFull, beg, g * G);
       len = __shfl_sync(kFull, len, g * G);
@@ -163,7 +193,7 @@ __global__ void __launch_bounds__(kEmbThreads, MINB) emb_fwd_kernel(EmbFwdParams
       for (int j = 0; j < maxlen; j += G) {
         int myid = -1;
         const bool has = active && j + l < len;
-        if (has) myid = map_id(p, d, vals[beg + j + l], true);
+        if (has) myid = map_id(p, d, fetched ? (stage_ok ? p.stage_ids[stage_base + j + l] : -1) : vals[beg + j + l], true);
         if (has && stage_ok) {
           p.stage_ids[stage_base + j + l] = myid;
           p.stage_bag[stage_base + j + l] = b;
@@ -1281,6 +1311,12 @@ void emb_forward(const EmbFwdParams& p, int grid, cudaStream_t s) {
   FLARE_CHECK(static_cast<int64_t>(p.world) * p.Bl + 2ll * grid * (kEmbThreads / 32) * 32 < (1ll << 31),
               "too many (source, sample) bags for 32-bit work indices");
   FLARE_CHECK(p.vec == 1 || p.vec == 2, "vec must be 1 or 2");
+  if (p.fetch_offs != nullptr) {
+    FLARE_CHECK(p.world > 1 && !p.bulk, "the id prefetch is for the multi-GPU register-gather forward");
+    emb_fetch_kernel<<<grid, kEmbThreads, 0, s>>>(p);
+    FLARE_CUDA_CHECK(cudaGetLastError());
+    count_launch();
+  }
   if (p.bulk) {
     // every shard's rows are 16-byte aligned (checked by the caller): TMA bulk-gather forward
     if (p.w_dtype == kF32) fwd_bulk_launch<float>(p, s);

@@ -80,6 +80,8 @@ struct EmbFwdParams {
   int bulk;       // 1: TMA bulk-gather forward (every shard's rows 16-byte aligned, <= 1024 bytes)
   const int* slot_map;  // row -> HBM slot maps of host-tier shards (ShardDesc::slot_map_off), or null
   const int* const* peer_remap;  // [world] slot buffers of dynamic tables (same layout as values), or null
+  int* fetch_offs;               // multi-GPU: local copy of every (shard, source) bag-offset run [nslot][Bl + 1];
+                                 // the ids are copied into the staging rows (emb_fetch_kernel), or null
   float* const* peer_part;       // [world] fp32 partial pooled rows [rw_slots][Bl][part_stride] (row-wise tables)
   int64_t part_stride;
   const RwTable* rw_tables;      // row-wise tables of the collection (reduced locally after the exchange)

@@ -78,13 +78,14 @@ def dlrm_benchmark_tables(vocab_sizes: list[int], dim: int = 128, optimizer: Spa
             for i, v in enumerate(vocab_sizes)]
 
 
-def dlrm_plan(cfg: DLRMConfig, world_size: int, table_costs: list[float] | None = None) -> ShardingPlan | None:
+def dlrm_plan(cfg: DLRMConfig, world_size: int, table_costs: list[float] | None = None, *,
+              row_split: bool = False) -> ShardingPlan | None:
     """Sharding plan weighted by per-table work (None: the collection's default plan)."""
     if table_costs is None:
         return None
     tabs = [t if t.optimizer == cfg.sparse_optimizer else replace(t, optimizer=cfg.sparse_optimizer)
             for t in cfg.tables]
-    return plan_sharding(tabs, world_size, expected_lookups=table_costs)
+    return plan_sharding(tabs, world_size, expected_lookups=table_costs, row_split=row_split)
 
 
 class DLRM:

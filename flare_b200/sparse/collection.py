@@ -224,6 +224,11 @@ class ShardedEmbeddingBagCollection:
         self.stage_bag = torch.empty(nslot * self.stage_cap, dtype=torch.int32, device=dev)
         self.stage_count = torch.zeros(nslot, dtype=torch.int32, device=dev)
         self.stage_len = torch.zeros(nslot * self.B, dtype=torch.int32, device=dev)
+        # multi-GPU: local copies of every (shard, source) offset run (ids go to stage_ids) fetched in bulk
+        # before the forward (FLARE_EMB_FETCH=0 reads them from the peers inside the forward instead)
+        self.fetch = world_size > 1 and os.environ.get("FLARE_EMB_FETCH", "1") != "0"
+        self.fetch_offs = (torch.zeros(nslot * (self.B + 1), dtype=torch.int32, device=dev)
+                           if self.fetch else None)
         self.stage_rank = torch.empty(nslot * self.stage_cap, dtype=torch.int32, device=dev)
         self.slot_start = torch.zeros(nslot + 1, dtype=torch.int32, device=dev)
         self.grad_stage_ld = self.ncols_max
@@ -357,6 +362,8 @@ class ShardedEmbeddingBagCollection:
         if self.dynamic is not None:
             self.dynamic.prepare()
             d["peer_remap"] = self._peer["remap"].data_ptr()
+        if self.fetch and not self.bulk and training:
+            d["fetch_offs"] = self.fetch_offs.data_ptr()
         if self.partials is not None:
             d.update(peer_part=self._peer["part"].data_ptr(), part_stride=self.part_total,
                      rw_tables=self.rw_desc.data_ptr(), num_rw=len(self.rw_part_col))

@@ -173,10 +173,10 @@ class DLRMTrainer(FusedTrainer):
     def __init__(self, cfg: DLRMConfig, batch_size: int, *, max_bag_size: int, rank: int = 0, world_size: int = 1,
                  device: torch.device | None = None, seed: int = 0, use_graph: bool = True,
                  values_capacity: int | None = None, heap_bytes: int | None = None,
-                 table_costs: list[float] | None = None):
+                 table_costs: list[float] | None = None, row_split: bool = False):
         device = device or torch.device("cuda", torch.cuda.current_device())
         heap = None
-        plan = dlrm_plan(cfg, world_size, table_costs)
+        plan = dlrm_plan(cfg, world_size, table_costs, row_split=row_split)
         if world_size > 1:
             exchange = ShardedEmbeddingBagCollection.exchange_bytes(cfg.tables, batch_size, max_bag_size,
                                                                     values_capacity, plan=plan)
