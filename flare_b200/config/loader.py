@@ -88,7 +88,7 @@ def _convert(tp, raw):
             return None
         return _convert(non_none[0], raw)
     if origin in (list, tuple, Sequence):
-        items = raw if isinstance(raw, list) else [raw]
+        items = list(raw) if isinstance(raw, (list, tuple)) else [raw]
         inner = args[0] if args else str
         vals = [_convert(inner, x) for x in items]
         return tuple(vals) if origin is tuple else vals

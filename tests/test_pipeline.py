@@ -1,0 +1,99 @@
+"""Feature-production pipeline (CPU): parse + encode + windowed Parquet publication, resume, leases, reconcile."""
+import json
+
+import numpy as np
+import pytest
+
+pa = pytest.importorskip("pyarrow")
+pq = pytest.importorskip("pyarrow.parquet")
+try:
+    from flare_b200._native import native
+
+    native().etl
+except Exception:  # pragma: no cover
+    pytest.skip("native extension not built", allow_module_level=True)
+
+
+from flare_b200.data.pipeline import DataPipeline, Lease, PipelineConfig  # noqa: E402
+from flare_b200.data.run import main as run_main  # noqa: E402
+
+
+def _write_logs(path, n, seed):
+    rng = np.random.default_rng(seed)
+    with open(path, "w") as f:
+        for i in range(n):
+            items = [f"1\x03{int(rng.random() < 0.3)}", f"10\x03{rng.exponential(5):.3f}",
+                     f"20\x03{rng.integers(0, 10**9)}", f"21\x03{rng.integers(0, 50)}",
+                     "30\x03" + ",".join(str(x) for x in rng.integers(0, 100, rng.integers(1, 5)))]
+            if rng.random() < 0.2:
+                items.pop(2)
+            f.write(f"u{i}\tctx\t" + "\x02".join(items) + "\n")
+
+
+def _cfg(tmp_path, **kw):
+    base = dict(inputs=(str(tmp_path / "logs"),), output=str(tmp_path / "out"), feature_column=2, label_code=1,
+                dense=({"code": 10, "transform": "log1p"},),
+                sparse=({"kind": "hash", "codes": (20,), "buckets": 1000},
+                        {"kind": "cross", "codes": (20, 21), "buckets": 500},
+                        {"kind": "fnv_list", "codes": (30,), "buckets": 777}),
+                rows_per_file=100, files_per_window=2)
+    base.update(kw)
+    from flare_b200.config.loader import build_dataclass
+
+    return build_dataclass(PipelineConfig, base)
+
+
+def test_publish_resume_and_training_layout(tmp_path):
+    (tmp_path / "logs").mkdir()
+    _write_logs(tmp_path / "logs" / "a.txt", 350, 0)
+    pipe = DataPipeline(_cfg(tmp_path))
+    (tmp_path / "out").mkdir()
+    (tmp_path / "out" / ".window-crashed").mkdir()      # left by a crashed run
+    man = pipe.run()
+    assert not list((tmp_path / "out").glob(".window-*"))
+    assert [w["rows"] for w in man["windows"]] == [200, 150]
+    files = pipe.published_files()
+    t = pq.read_table(files[0])
+    assert set(t.column_names) == {"label", "d0", "s0", "s1", "s2"}
+    s0 = t.column("s0").combine_chunks()
+    assert np.asarray(s0.values).max() < 1000 and len(s0) == 100
+    # hash column = value mod buckets of the parsed feature
+    lines = open(tmp_path / "logs" / "a.txt").read().splitlines()[:100]
+    want = []
+    for ln in lines:
+        kv = dict(item.split("\x03") for item in ln.split("\t")[2].split("\x02"))
+        want.append([int(kv["20"]) % 1000] if "20" in kv else [])
+    assert s0.to_pylist() == want
+    # resume: a second run publishes only the new input
+    _write_logs(tmp_path / "logs" / "b.txt", 120, 1)
+    man2 = DataPipeline(_cfg(tmp_path)).run()
+    assert len(man2["windows"]) == 3 and man2["windows"][-1]["rows"] == 120
+    # the training source reads the published files
+    from flare_b200.data.sources import ParquetSourceFactory, stream_batches
+
+    batches = list(stream_batches(ParquetSourceFactory(DataPipeline(_cfg(tmp_path)).published_files()), 64,
+                                  policy="drop"))
+    assert sum(b.validity.valid_count for b in batches) == 64 * (470 // 64)
+
+
+def test_lease_blocks_second_publisher(tmp_path):
+    out = tmp_path / "o"
+    out.mkdir()
+    a, b = Lease(out, 60), Lease(out, 60)
+    a.acquire()
+    with pytest.raises(RuntimeError):
+        b.acquire()
+    a.release()
+    b.acquire()
+    b.release()
+
+
+def test_cli(tmp_path, capsys):
+    (tmp_path / "logs").mkdir()
+    _write_logs(tmp_path / "logs" / "a.txt", 50, 2)
+    cfg = {"inputs": [str(tmp_path / "logs")], "output": str(tmp_path / "out"), "label_code": 1,
+           "sparse": [{"kind": "hash", "codes": [20], "buckets": 10}]}
+    (tmp_path / "p.json").write_text(json.dumps(cfg))
+    assert run_main(["--config", str(tmp_path / "p.json")]) == 0
+    assert json.loads(capsys.readouterr().out)["rows"] == 50
+
