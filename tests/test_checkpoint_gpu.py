@@ -95,6 +95,13 @@ def test_row_wise_pieces_reshard(cuda, tmp_path, src, dst):
     losses_a = [_step(a, b) for b in batches[2:]]
     b_model = DLRM(_cfg("rowwise_adagrad", dst), 128, max_bag_size=8, device=cuda, seed=77)
     assert mgr.restore(b_model) == 2
+    # the restored state, saved again from the other split, audits to the same digests
+    from flare_b200.checkpoint.audit import audit_step
+
+    CheckpointManager(str(tmp_path / "again")).save(2, b_model)
+    ra, rb = audit_step(tmp_path, 2), audit_step(tmp_path / "again", 2)
+    assert ra["ok"] and rb["ok"] and ra["sparse"]["chain"] == [1, 2]
+    assert ra["sparse"]["digest"] == rb["sparse"]["digest"] and ra["dense"]["digest"] == rb["dense"]["digest"]
     losses_b = [_step(b_model, b) for b in batches[2:]]
     torch.cuda.synchronize()
     for x, y in zip(losses_a, losses_b):
