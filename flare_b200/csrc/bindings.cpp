@@ -282,6 +282,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     flare::emb_forward(p, get<int>(d, "grid"), cur_stream());
   });
 
+  m.def("emb_det_temp_bytes", [](int64_t max_occ) { return flare::emb_det_temp_bytes(max_occ); });
   m.def("emb_backward", [](const py::dict& d) {
     flare::EmbBwdParams p{};
     p.shards = P<const flare::ShardDesc>(get<uintptr_t>(d, "shards"));
@@ -323,6 +324,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.light_max = get_or<int>(d, "light_max", 64);
     p.dirty = P<uint8_t>(get_or<uintptr_t>(d, "dirty", 0));
     p.max_occ = get<int64_t>(d, "max_occ");
+    p.deterministic = get_or<int>(d, "deterministic", 0);
+    p.det_keys = P<int>(get_or<uintptr_t>(d, "det_keys", 0));
+    p.det_vals = P<int>(get_or<uintptr_t>(d, "det_vals", 0));
+    p.det_temp = P<void>(get_or<uintptr_t>(d, "det_temp", 0));
+    p.det_temp_bytes = get_or<size_t>(d, "det_temp_bytes", 0);
     p.opt = parse_sparse_opt(get<py::dict>(d, "opt"));
     p.flags_local = P<uint32_t>(get_or<uintptr_t>(d, "flags_local", 0));
     p.peer_flags = P<uint32_t* const>(get_or<uintptr_t>(d, "peer_flags", 0));

@@ -33,6 +33,8 @@
 // and updates rows in its external native store.
 #include "embedding.cuh"
 #include "sm100.cuh"
+
+#include <cub/device/device_radix_sort.cuh>
 #include "sparse_ops.cuh"
 
 #include <algorithm>
@@ -867,6 +869,49 @@ __global__ void __launch_bounds__(kScanThreads) dev_scan_final_kernel(const int*
   if (blockIdx.x == kScanBlocks - 1 && threadIdx.x == 0) out[n] = base;
 }
 
+// ---- deterministic-reduction mode -------------------------------------------
+// heavy rows listed in unique-row order (the emit kernel lists them in atomic order)
+__global__ void __launch_bounds__(kEmbThreads) emb_det_heavy_flags_kernel(EmbBwdParams p) {
+  const int U = p.num_unique[0];
+  for (int u = blockIdx.x * blockDim.x + threadIdx.x; u < U; u += gridDim.x * blockDim.x)
+    p.flags[u] = p.cnt_u[u] > p.light_max ? 1 : 0;
+}
+
+__global__ void __launch_bounds__(kEmbThreads) emb_det_heavy_place_kernel(EmbBwdParams p) {
+  const int U = p.num_unique[0];
+  for (int u = blockIdx.x * blockDim.x + threadIdx.x; u < U; u += gridDim.x * blockDim.x) {
+    if (!p.flags[u]) continue;
+    const int h = p.pos[u];
+    if (h < p.max_heavy) {
+      p.heavy[h] = u;
+      p.hcnt[h] = p.cnt_u[u];
+    }
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) p.num_unique[2] = p.pos[U];
+}
+
+// sort keys: the occurrence's unique row (invalid / unused positions sort last), value: its staged-grad row
+__global__ void __launch_bounds__(kEmbThreads) emb_det_keys_kernel(EmbBwdParams p, int n) {
+  const int nslot = p.num_shards * p.world;
+  const int tid = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int nthreads = static_cast<int>(gridDim.x) * blockDim.x;
+  const int T = p.slot_start[nslot];
+  for (int k = T + tid; k < n; k += nthreads) {
+    p.det_keys[k] = 0x7fffffff;
+    p.det_vals[k] = 0;
+  }
+  for (int slot = 0; slot < nslot; ++slot) {
+    const int kbase = p.slot_start[slot], cnt = p.slot_start[slot + 1] - kbase;
+    const int64_t sbase = static_cast<int64_t>(slot) * p.stage_cap;
+    const int64_t row_base = p.shards[slot / p.world].row_base;
+    for (int j = tid; j < cnt; j += nthreads) {
+      const int id = p.stage_ids[sbase + j];
+      p.det_keys[kbase + j] = id < 0 ? 0x7fffffff : p.row2u[row_base + id];
+      p.det_vals[kbase + j] = slot * p.Bl + p.stage_bag[sbase + j];
+    }
+  }
+}
+
 __device__ __forceinline__ float lr_scale(const SparseOptParams& o, float score) {
   switch (o.lr_policy) {
     case kLrSqrtDecay:
@@ -1339,6 +1384,14 @@ void emb_forward(const EmbFwdParams& p, int grid, cudaStream_t s) {
   }
 }
 
+size_t emb_det_temp_bytes(int64_t max_occ) {
+  size_t bytes = 0;
+  FLARE_CUDA_CHECK(cub::DeviceRadixSort::SortPairs(nullptr, bytes, static_cast<const int*>(nullptr),
+                                                   static_cast<int*>(nullptr), static_cast<const int*>(nullptr),
+                                                   static_cast<int*>(nullptr), static_cast<int>(max_occ), 0, 31));
+  return bytes;
+}
+
 void emb_backward(const EmbBwdParams& p, int ncols_max, int grid, cudaStream_t s) {
   FLARE_CHECK(ncols_max >= 16 && ncols_max <= 256 && (ncols_max & (ncols_max - 1)) == 0,
               "the backward needs a power-of-two widest shard in [16, 256] columns");
@@ -1359,8 +1412,25 @@ void emb_backward(const EmbBwdParams& p, int ncols_max, int grid, cudaStream_t s
   emb_emit_kernel<<<grid, kEmbThreads, 0, s>>>(p);
   emb_seg_partial_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(p);
   emb_seg_final_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(p);
-  emb_fill_kernel<<<grid, kEmbThreads, 0, s>>>(p);
-  count_launch(4);
+  count_launch(3);
+  if (!p.deterministic) {
+    emb_fill_kernel<<<grid, kEmbThreads, 0, s>>>(p);
+    count_launch();
+  } else {
+    // heavy rows in unique-row order; occurrences grouped per unique row by a stable radix sort, so
+    // each row adds its gradients in staging order whatever order the counting atomics ran in
+    FLARE_CHECK(p.det_keys && p.det_vals && p.det_temp, "deterministic mode needs its sort buffers");
+    const int n = static_cast<int>(N);
+    emb_det_heavy_flags_kernel<<<grid, kEmbThreads, 0, s>>>(p);
+    dev_scan_partial_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(p.flags, p.num_unique, n, p.block_sums);
+    dev_scan_final_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(p.flags, p.num_unique, n, p.block_sums, p.pos);
+    emb_det_heavy_place_kernel<<<grid, kEmbThreads, 0, s>>>(p);
+    emb_det_keys_kernel<<<grid, kEmbThreads, 0, s>>>(p, n);
+    size_t bytes = p.det_temp_bytes;
+    FLARE_CUDA_CHECK(cub::DeviceRadixSort::SortPairs(p.det_temp, bytes, p.det_keys, p.det_keys + n, p.det_vals,
+                                                     p.occ, n, 0, 31, s));
+    count_launch(5);
+  }
   if (p.w_dtype == kF32) bwd_apply_g<float>(p, ncols_max, grid, s);
   else if (p.w_dtype == kF16) bwd_apply_g<__half>(p, ncols_max, grid, s);
   else bwd_apply_g<__nv_bfloat16>(p, ncols_max, grid, s);

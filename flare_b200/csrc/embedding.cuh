@@ -141,6 +141,14 @@ struct EmbBwdParams {
   int light_max;
   uint8_t* dirty;   // per-row dirty flags for incremental checkpoints (nullable)
   int64_t max_occ;  // capacity of the per-unique arrays
+  // deterministic-reduction mode: every row adds its occurrences in staging order (run-to-run
+  // bitwise identical results); needs det_keys [2 * max_occ], det_vals [max_occ] and the sort's
+  // temporary storage (emb_det_temp_bytes)
+  int deterministic;
+  int* det_keys;
+  int* det_vals;
+  void* det_temp;
+  size_t det_temp_bytes;
   SparseOptParams opt;
   uint32_t* flags_local;
   uint32_t* const* peer_flags;
@@ -153,5 +161,6 @@ struct EmbBwdParams {
 
 void emb_forward(const EmbFwdParams& p, int grid, cudaStream_t s);
 void emb_backward(const EmbBwdParams& p, int ncols_max, int grid, cudaStream_t s);
+size_t emb_det_temp_bytes(int64_t max_occ);
 
 }  // namespace flare

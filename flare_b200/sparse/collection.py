@@ -98,6 +98,7 @@ class ShardedEmbeddingBagCollection:
         values_capacity: int | None = None,
         timeout_ns: int = PEER_TIMEOUT_NS,
         init: bool = True,
+        deterministic: bool | None = None,
     ):
         if not tables:
             raise ValueError("at least one table is required")
@@ -252,6 +253,17 @@ class ShardedEmbeddingBagCollection:
         # one fp32 partial row per (heavy row, 256-occurrence chunk) segment
         self.heavy_acc = torch.zeros((self.max_heavy + self.max_occ // 256 + 2) * 128 * self.vec,
                                      dtype=torch.float32, device=dev)
+        # deterministic-reduction mode (FLARE_DETERMINISTIC=1): rows add their occurrences in staging
+        # order, so repeated runs are bitwise identical (a race detector for the sparse backward)
+        if deterministic is None:
+            deterministic = os.environ.get("FLARE_DETERMINISTIC", "0") == "1"
+        self.deterministic = bool(deterministic)
+        self.det = None
+        if self.deterministic:
+            nbytes = int(native().emb_det_temp_bytes(self.max_occ))
+            self.det = dict(keys=torch.empty(2 * self.max_occ, dtype=torch.int32, device=dev),
+                            vals=torch.empty(self.max_occ, dtype=torch.int32, device=dev),
+                            temp=torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev), bytes=nbytes)
 
         # ---- exchange buffers (symmetric when distributed) ----
         self.values_capacity = int(values_capacity or self.F * self.B * self.max_bag)
@@ -412,6 +424,9 @@ class ShardedEmbeddingBagCollection:
             block_counter=self.flags.block_counter_ptr(FLAG_BWD_IN), status=self.status.ptr,
             timeout_ns=self.timeout_ns, ncols_max=self.ncols_max, grid=self.grid,
         )
+        if self.det is not None:
+            d.update(deterministic=1, det_keys=self.det["keys"].data_ptr(), det_vals=self.det["vals"].data_ptr(),
+                     det_temp=self.det["temp"].data_ptr(), det_temp_bytes=self.det["bytes"])
         native().emb_backward(d)
 
     def check(self) -> None:

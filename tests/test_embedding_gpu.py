@@ -190,3 +190,28 @@ def test_row_wise_pieces_init_and_pooling(cuda):
     a.check()
     b.check()
     torch.testing.assert_close(pb, pa, rtol=1e-2, atol=1e-4)
+
+
+def test_deterministic_mode_is_bitwise_repeatable(cuda):
+    """FLARE_DETERMINISTIC: heavy-hitter batches give bitwise-identical tables on repeated runs."""
+    opt = SparseOptimizerConfig(kind="adam", learning_rate=0.01)
+    vocabs = [40, 5000]
+    tables = [SparseTableSpec(f"t{i}", v, 128, optimizer=opt) for i, v in enumerate(vocabs)]
+    B, max_bag = 512, 32
+    runs = []
+    for _ in range(2):
+        coll = ShardedEmbeddingBagCollection(tables, B, max_bag_size=max_bag, device=cuda, optimizer=opt, seed=1,
+                                             deterministic=True)
+        for step in range(1, 4):
+            offs, vals = _batch(B, vocabs, max_bag, seed=100 + step, zipf=1.3)
+            coll.set_input(offs.to(cuda), vals.to(cuda), non_blocking=False)
+            coll.forward()
+            g = torch.Generator().manual_seed(step)
+            coll.grad_input.copy_((torch.randn(B, coll.total_dim, generator=g) * 0.1).to(torch.bfloat16).to(cuda))
+            coll.backward(step)
+        torch.cuda.synchronize()
+        coll.check()
+        assert coll.last_step_stats()["heavy_rows"] > 0
+        runs.append(_export(coll, tables))
+    for a, b in zip(*runs):
+        assert torch.equal(a, b)
