@@ -325,6 +325,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.dirty = P<uint8_t>(get_or<uintptr_t>(d, "dirty", 0));
     p.max_occ = get<int64_t>(d, "max_occ");
     p.deterministic = get_or<int>(d, "deterministic", 0);
+    p.det_first = P<int>(get_or<uintptr_t>(d, "det_first", 0));
     p.det_keys = P<int>(get_or<uintptr_t>(d, "det_keys", 0));
     p.det_vals = P<int>(get_or<uintptr_t>(d, "det_vals", 0));
     p.det_temp = P<void>(get_or<uintptr_t>(d, "det_temp", 0));

@@ -649,6 +649,7 @@ __global__ void __launch_bounds__(kEmbThreads) emb_bwd_pull_count_kernel(EmbBwdP
         const int rank = old + __popc(peers & lanemask_lt());
         p.stage_rank[kbase + j] = rank;
         f = rank == 0 ? 1 : 0;
+        if (p.deterministic) atomicMin(p.det_first + row, kbase + j);  // first occurrence by position
       }
       if (j < cnt) p.flags[kbase + j] = f;
     }
@@ -706,6 +707,7 @@ __global__ void __launch_bounds__(kEmbThreads) emb_emit_kernel(EmbBwdParams p) {
       p.uniq_row[u] = row;
       p.uniq_shard[u] = sh;
       p.row2u[row] = u;
+      if (p.deterministic) p.det_first[row] = 0x7fffffff;
       const int c = p.row_count[row];
       p.cnt_u[u] = c;
       p.first_gidx[u] = slot * p.Bl + p.stage_bag[sbase + j];
@@ -870,6 +872,22 @@ __global__ void __launch_bounds__(kScanThreads) dev_scan_final_kernel(const int*
 }
 
 // ---- deterministic-reduction mode -------------------------------------------
+// first-occurrence flags by staging position (the counting pass flags the first by atomic order)
+__global__ void __launch_bounds__(kEmbThreads) emb_det_first_kernel(EmbBwdParams p) {
+  const int nslot = p.num_shards * p.world;
+  const int tid = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int nthreads = static_cast<int>(gridDim.x) * blockDim.x;
+  for (int slot = 0; slot < nslot; ++slot) {
+    const int kbase = p.slot_start[slot], cnt = p.slot_start[slot + 1] - kbase;
+    const int64_t sbase = static_cast<int64_t>(slot) * p.stage_cap;
+    const int64_t row_base = p.shards[slot / p.world].row_base;
+    for (int j = tid; j < cnt; j += nthreads) {
+      const int id = p.stage_ids[sbase + j];
+      p.flags[kbase + j] = (id >= 0 && p.det_first[row_base + id] == kbase + j) ? 1 : 0;
+    }
+  }
+}
+
 // heavy rows listed in unique-row order (the emit kernel lists them in atomic order)
 __global__ void __launch_bounds__(kEmbThreads) emb_det_heavy_flags_kernel(EmbBwdParams p) {
   const int U = p.num_unique[0];
@@ -1403,6 +1421,11 @@ void emb_backward(const EmbBwdParams& p, int ncols_max, int grid, cudaStream_t s
   FLARE_CUDA_CHECK(cudaMemsetAsync(p.num_unique, 0, 4 * sizeof(int), s));
   emb_slot_prefix_kernel<<<1, 1024, 0, s>>>(p);
   emb_bwd_pull_count_kernel<<<grid, kEmbThreads, 0, s>>>(p);
+  if (p.deterministic) {
+    FLARE_CHECK(p.det_first != nullptr, "deterministic mode needs the per-row first-position array");
+    emb_det_first_kernel<<<grid, kEmbThreads, 0, s>>>(p);
+    count_launch();
+  }
   const int nslot = p.num_shards * p.world;
   dev_scan_partial_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(p.flags, p.slot_start + nslot,
                                                                static_cast<int>(N), p.block_sums);

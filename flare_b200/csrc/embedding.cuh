@@ -145,6 +145,7 @@ struct EmbBwdParams {
   // bitwise identical results); needs det_keys [2 * max_occ], det_vals [max_occ] and the sort's
   // temporary storage (emb_det_temp_bytes)
   int deterministic;
+  int* det_first;    // per-row first staging position (INT_MAX when idle; reset by the emit kernel)
   int* det_keys;
   int* det_vals;
   void* det_temp;

@@ -261,7 +261,8 @@ class ShardedEmbeddingBagCollection:
         self.det = None
         if self.deterministic:
             nbytes = int(native().emb_det_temp_bytes(self.max_occ))
-            self.det = dict(keys=torch.empty(2 * self.max_occ, dtype=torch.int32, device=dev),
+            self.det = dict(first=torch.full((max(rbase, 4),), 2**31 - 1, dtype=torch.int32, device=dev),
+                            keys=torch.empty(2 * self.max_occ, dtype=torch.int32, device=dev),
                             vals=torch.empty(self.max_occ, dtype=torch.int32, device=dev),
                             temp=torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev), bytes=nbytes)
 
@@ -425,7 +426,8 @@ class ShardedEmbeddingBagCollection:
             timeout_ns=self.timeout_ns, ncols_max=self.ncols_max, grid=self.grid,
         )
         if self.det is not None:
-            d.update(deterministic=1, det_keys=self.det["keys"].data_ptr(), det_vals=self.det["vals"].data_ptr(),
+            d.update(deterministic=1, det_first=self.det["first"].data_ptr(), det_keys=self.det["keys"].data_ptr(),
+                     det_vals=self.det["vals"].data_ptr(),
                      det_temp=self.det["temp"].data_ptr(), det_temp_bytes=self.det["bytes"])
         native().emb_backward(d)
 
