@@ -18,9 +18,10 @@
 //   pass 2: recompute S, P = exp2(S' - lse) (final, no rescaling of O), write
 //           P as bf16 into shared memory in the 128-byte-swizzled K-major
 //           layout and issue O += P V^T-tile (A = P from smem, B = V^T tile).
-//   K / V^T tiles and P are double-buffered: the next key step's tiles load
-//   by TMA during this step's softmax, and a step's P.V MMAs are not waited
-//   for until the next S MMA's commit.
+//   S is computed one head at a time into a 128-column accumulator (256 TMEM
+//   columns and 82 KB of shared memory per CTA), so two CTAs share an SM and
+//   one CTA's softmax overlaps the other's TMA / MMA waits; fully visible key
+//   tiles skip the causal / length mask.
 // Backward (CTA = sequence x head pair x 128-row key tile, thread i = key row
 // i): for each causal query tile and head, S^T = K Q^T and dP^T = V dO^T into
 // TMEM; P^T, dS^T = P^T (dP^T - Delta) go to shared memory; then
@@ -85,20 +86,20 @@ __device__ __forceinline__ uint64_t desc_mn(uint32_t base, int lbo, int k) {
 
 struct AttnSmemF {
   static constexpr int Q = 0;            // [128 x 64] 16 KB
-  static constexpr int K = 16384;        // 2 buffers of [128 x 64] 16 KB
-  static constexpr int VT = 49152;       // 2 buffers of 2 atoms of [64 rows x 64 kv] = 16 KB
-  static constexpr int P = 81920;        // 2 buffers of 2 heads x 2 atoms x 16 KB = 64 KB
-  static constexpr int BAR = 212992;
-  static constexpr int BYTES = BAR + 128 + 1024;
+  static constexpr int K = 16384;        // [128 x 64] 16 KB
+  static constexpr int VT = 32768;       // 2 atoms of [64 rows x 64 kv] = 16 KB
+  static constexpr int P = 49152;        // one head: 2 atoms x 16 KB = 32 KB
+  static constexpr int BAR = 81920;
+  static constexpr int BYTES = BAR + 128 + 1024;  // two CTAs fit in one SM's shared memory
 };
 
-__global__ void __launch_bounds__(kThreadsA, 1)
+__global__ void __launch_bounds__(kThreadsA, 2)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_vt,
                     AttnFwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + AttnSmemF::BAR);  // 0 q, 1/3 kv buffers, 2 mma
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + AttnSmemF::BAR);  // 0 q, 1 kv, 2 mma
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 4);
   const int tid = threadIdx.x, warp = warp_id(), lane = lane_id();
   const int qt = blockIdx.x, seq = blockIdx.y, hp = blockIdx.z;
@@ -114,18 +115,18 @@ __global__ void __launch_bounds__(kThreadsA, 1)
   if (tid == 0) {
     sm100::tma_prefetch_desc(&tm_qkv);
     sm100::tma_prefetch_desc(&tm_vt);
-    for (int i = 0; i < 4; ++i) sm100::mbar_init(&bar[i], 1);
+    for (int i = 0; i < 3; ++i) sm100::mbar_init(&bar[i], 1);
     sm100::fence_mbar_init();
   }
   if (warp == 0) {
-    sm100::tmem_alloc(tslot, 512);
+    sm100::tmem_alloc(tslot, 256);
     sm100::tmem_relinquish();
   }
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *tslot;
-  const uint32_t tS = tmem, tO = tmem + 256;  // S: heads at +0 / +128; O: heads at +256 / +288
+  const uint32_t tS = tmem, tO = tmem + 128;  // S: one head at a time; O: heads at +128 / +160
   const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
   constexpr uint32_t idesc_s = sm100::make_idesc_bf16(128, 128, false, false);
   constexpr uint32_t idesc_o = sm100::make_idesc_bf16(128, 32, false, false);
@@ -134,111 +135,107 @@ __global__ void __launch_bounds__(kThreadsA, 1)
   uint32_t ph_mma = 0;
   bool ok = true;
 
-  // Pipeline: the K (and, in pass 2, V^T) tile of the next key step is loaded by TMA while this
-  // step's softmax runs (two buffers, barriers bar[1] / bar[3]); P is double-buffered so the P.V
-  // MMAs of a step are not waited for until the next S MMA's commit.  Steps are numbered across
-  // both passes (it = pass * (qt + 1) + kt), buffer = it & 1.
-  const int nkt = qt + 1, nit = 2 * nkt;
-  auto issue_kv = [&](int it) {  // thread 0 only
-    const int ps = it / nkt, kt = it - ps * nkt, b = it & 1;
-    const int k0 = s0 + kt * kT;
-    uint64_t* kb = &bar[b ? 3 : 1];
-    sm100::mbar_arrive_expect_tx(kb, kT * 64 * 2 + (ps ? 2 * 64 * 64 * 2 : 0));
-    sm100::tma_load_2d(sm + AttnSmemF::K + b * 16384, &tm_qkv, kb, 256 + hp * 64, k0);
-    if (ps) {
-      sm100::tma_load_2d(sm + AttnSmemF::VT + b * 16384, &tm_vt, kb, k0, hp * 64);
-      sm100::tma_load_2d(sm + AttnSmemF::VT + b * 16384 + 8192, &tm_vt, kb, k0 + 64, hp * 64);
-    }
-  };
-  uint32_t ph_kv2[2] = {0, 0};
+  // Per key step: TMA K (+ V^T in pass 2); for each head: S_h = Q_h K_h^T into the one 128-column S
+  // accumulator, softmax on it (pass 1: running max / sum; pass 2: P_h to shared memory and
+  // O_h += P_h V_h^T).  256 TMEM columns and 82 KB of shared memory per CTA let two CTAs share an
+  // SM, so one CTA's softmax overlaps the other's TMA and MMA waits.
   if (tid == 0) {
     sm100::mbar_arrive_expect_tx(&bar[0], kT * 64 * 2);
     sm100::tma_load_2d(sm + AttnSmemF::Q, &tm_qkv, &bar[0], hp * 64, q0);
-    issue_kv(0);
     ok = sm100::mbar_wait(&bar[0], 0, p.timeout_ns, p.status, 10);
   }
+  uint32_t ph_kv = 0;
   float m2[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-  for (int it = 0; it < nit; ++it) {
-    const int pass = it / nkt, kt = it - pass * nkt, b = it & 1;
-    if (tid == 0 && ok) {
-      ok = sm100::mbar_wait(&bar[b ? 3 : 1], ph_kv2[b], p.timeout_ns, p.status, 11);
-      sm100::tc_fence_after();
-      if (ok) {
-        const uint32_t qa = smem_u32(sm + AttnSmemF::Q), ka = smem_u32(sm + AttnSmemF::K + b * 16384);
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
+  for (int pass = 0; pass < 2; ++pass) {
+    for (int kt = 0; kt <= qt; ++kt) {
+      const int k0 = s0 + kt * kT;
+      if (tid == 0 && ok) {
+        sm100::mbar_arrive_expect_tx(&bar[1], kT * 64 * 2 + (pass ? 2 * 64 * 64 * 2 : 0));
+        sm100::tma_load_2d(sm + AttnSmemF::K, &tm_qkv, &bar[1], 256 + hp * 64, k0);
+        if (pass) {
+          sm100::tma_load_2d(sm + AttnSmemF::VT, &tm_vt, &bar[1], k0, hp * 64);
+          sm100::tma_load_2d(sm + AttnSmemF::VT + 8192, &tm_vt, &bar[1], k0 + 64, hp * 64);
+        }
+        ok = sm100::mbar_wait(&bar[1], ph_kv, p.timeout_ns, p.status, 11);
+      }
+      ph_kv ^= 1;
+      // a fully visible key tile (below the diagonal, inside the sequence) needs no mask
+      const bool full = kt < qt && (kt + 1) * kT <= L && qi < L;
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        if (tid == 0 && ok) {
+          sm100::tc_fence_after();
+          const uint32_t qa = smem_u32(sm + AttnSmemF::Q), ka = smem_u32(sm + AttnSmemF::K);
 #pragma unroll
           for (int k = 0; k < 2; ++k)
-            sm100::mma_f16_ss(tS + h * 128, desc_k(qa, 16384, 2 * h + k), desc_k(ka, 16384, 2 * h + k), idesc_s,
+            sm100::mma_f16_ss(tS, desc_k(qa, 16384, 2 * h + k), desc_k(ka, 16384, 2 * h + k), idesc_s,
                               k > 0 ? 1u : 0u);
-        sm100::mma_commit(&bar[2]);  // also covers the previous step's P.V MMAs
-      }
-    }
-    ph_kv2[b] ^= 1;
-    // everyone waits for S (and for the previous P.V, which read the other K/V^T/P buffers)
-    if (!sm100::mbar_wait(&bar[2], ph_mma, p.timeout_ns, p.status, 12)) ok = false;
-    ph_mma ^= 1;
-    sm100::tc_fence_after();
-    // the other buffers are free now: load the next step's tiles behind this step's softmax
-    if (tid == 0 && ok && it + 1 < nit) issue_kv(it + 1);
+          sm100::mma_commit(&bar[2]);  // also covers the previous step's P.V MMAs
+        }
+        if (!sm100::mbar_wait(&bar[2], ph_mma, p.timeout_ns, p.status, 12)) ok = false;
+        ph_mma ^= 1;
+        sm100::tc_fence_after();
+        float pv[128];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      float pv[128];
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          sm100::tmem_ld_32x32b_x32(tS + lane_off + c * 32, r);
+          sm100::tmem_ld_wait();
+          if (full) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        sm100::tmem_ld_32x32b_x32(tS + h * 128 + lane_off + c * 32, r);
-        sm100::tmem_ld_wait();
+            for (int j = 0; j < 32; ++j) pv[c * 32 + j] = __uint_as_float(r[j]) * c2;
+          } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int kj = kt * kT + c * 32 + j;
-          const bool valid = kj <= qi && kj < L && qi < L;
-          pv[c * 32 + j] = valid ? __uint_as_float(r[j]) * c2 : -INFINITY;
+            for (int j = 0; j < 32; ++j) {
+              const int kj = kt * kT + c * 32 + j;
+              const bool valid = kj <= qi && kj < L && qi < L;
+              pv[c * 32 + j] = valid ? __uint_as_float(r[j]) * c2 : -INFINITY;
+            }
+          }
+        }
+        if (pass == 0) {
+          float mx = m2[h];
+#pragma unroll
+          for (int j = 0; j < 128; ++j) mx = fmaxf(mx, pv[j]);
+          if (mx != -INFINITY) {
+            float sum = 0.f;
+#pragma unroll
+            for (int j = 0; j < 128; ++j) sum += exp2f(pv[j] - mx);
+            l[h] = l[h] * exp2f(m2[h] - mx) + sum;
+            m2[h] = mx;
+          }
+        } else {
+          const float lse = (l[h] > 0.f) ? m2[h] + log2f(l[h]) : 0.f;
+          uint8_t* pt = sm + AttnSmemF::P;  // the previous head's P.V MMAs finished (S commit above)
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            float e[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t) e[t] = exp2f(pv[c * 8 + t] - lse);
+            st_swizzled(pt, 16384, tid, c, pack_bf16x8(e));
+          }
+        }
+        if (pass == 1) fence_proxy_async_smem_();
+        sm100::tc_fence_before();
+        __syncthreads();  // S read by every thread before the next S MMA overwrites it; P written
+        if (pass == 1 && tid == 0 && ok) {
+          // O_h += P_h V_h^T; the next S MMA's commit (or the one below) covers these MMAs
+          sm100::tc_fence_after();
+          const uint32_t va = smem_u32(sm + AttnSmemF::VT), pa = smem_u32(sm + AttnSmemF::P);
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            sm100::mma_f16_ss(tO + h * 32, desc_k(pa, 16384, k), desc_k(va + h * 4096, 8192, k), idesc_o,
+                              (kt > 0 || k > 0) ? 1u : 0u);
+          if (h == 1) sm100::mma_commit(&bar[2]);
         }
       }
-      if (pass == 0) {
-        float mx = m2[h];
-#pragma unroll
-        for (int j = 0; j < 128; ++j) mx = fmaxf(mx, pv[j]);
-        if (mx != -INFINITY) {
-          float sum = 0.f;
-#pragma unroll
-          for (int j = 0; j < 128; ++j) sum += exp2f(pv[j] - mx);
-          l[h] = l[h] * exp2f(m2[h] - mx) + sum;
-          m2[h] = mx;
-        }
-      } else {
-        const float lse = (l[h] > 0.f) ? m2[h] + log2f(l[h]) : 0.f;
-        uint8_t* pt = sm + AttnSmemF::P + b * 65536 + h * 32768;
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          float e[8];
-#pragma unroll
-          for (int t = 0; t < 8; ++t) e[t] = exp2f(pv[c * 8 + t] - lse);
-          st_swizzled(pt, 16384, tid, c, pack_bf16x8(e));
-        }
-      }
-    }
-    if (pass == 1) fence_proxy_async_smem_();
-    sm100::tc_fence_before();
-    __syncthreads();  // S fully read (the next S MMA may overwrite it); P written
-    if (pass == 1 && tid == 0 && ok) {
-      sm100::tc_fence_after();
-      const uint32_t va = smem_u32(sm + AttnSmemF::VT + b * 16384);
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t pa = smem_u32(sm + AttnSmemF::P + b * 65536 + h * 32768);
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          sm100::mma_f16_ss(tO + h * 32, desc_k(pa, 16384, k), desc_k(va + h * 4096, 8192, k), idesc_o,
-                            (kt > 0 || k > 0) ? 1u : 0u);
+      if (pass == 1) {
+        // P and the V^T tile are overwritten next step: wait for the P.V MMAs
+        if (!sm100::mbar_wait(&bar[2], ph_mma, p.timeout_ns, p.status, 13)) ok = false;
+        ph_mma ^= 1;
       }
     }
   }
-  // the last P.V MMAs
-  if (tid == 0 && ok) sm100::mma_commit(&bar[2]);
-  if (!sm100::mbar_wait(&bar[2], ph_mma, p.timeout_ns, p.status, 13)) ok = false;
-  ph_mma ^= 1;
   // ---- epilogue: O and LSE
   sm100::tc_fence_after();
 #pragma unroll
@@ -261,7 +258,7 @@ __global__ void __launch_bounds__(kThreadsA, 1)
   }
   sm100::tc_fence_before();
   __syncthreads();
-  if (warp == 0) sm100::tmem_dealloc(tmem, 512);
+  if (warp == 0) sm100::tmem_dealloc(tmem, 256);
 }
 
 // ------------------------------------------------------------------ backward
