@@ -373,6 +373,8 @@ __global__ void __launch_bounds__(kThreadsA, 1)
       sm100::tc_fence_after();
       const float* lse_h = st_lse + h * kT;
       const float* del_h = st_delta + h * kT;
+      // a query tile entirely after this key tile and inside the sequence needs no mask
+      const bool full = qt > kt && (qt + 1) * kT <= L && ki < L;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t rs[32], rd[32];
@@ -380,14 +382,24 @@ __global__ void __launch_bounds__(kThreadsA, 1)
         sm100::tmem_ld_32x32b_x32(tdP + lane_off + c * 32, rd);
         sm100::tmem_ld_wait();
         float pt[32], ds[32];
+        if (full) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int qc = c * 32 + j;
-          const int qidx = qt * kT + qc;
-          const bool valid = qidx >= ki && qidx < L && ki < L;
-          const float pp = valid ? exp2f(__uint_as_float(rs[j]) * c2 - lse_h[qc]) : 0.f;
-          pt[j] = pp;
-          ds[j] = pp * (__uint_as_float(rd[j]) - del_h[qc]);
+          for (int j = 0; j < 32; ++j) {
+            const int qc = c * 32 + j;
+            const float pp = exp2f(__uint_as_float(rs[j]) * c2 - lse_h[qc]);
+            pt[j] = pp;
+            ds[j] = pp * (__uint_as_float(rd[j]) - del_h[qc]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int qc = c * 32 + j;
+            const int qidx = qt * kT + qc;
+            const bool valid = qidx >= ki && qidx < L && ki < L;
+            const float pp = valid ? exp2f(__uint_as_float(rs[j]) * c2 - lse_h[qc]) : 0.f;
+            pt[j] = pp;
+            ds[j] = pp * (__uint_as_float(rd[j]) - del_h[qc]);
+          }
         }
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
