@@ -21,6 +21,12 @@ Stages (host CPU; the hot loops are the native parser and encoders of
    place, then recorded in the publication manifest (atomic JSON), so a
    reader never sees a half-published window.
 
+With ``run(workers=N)`` the inputs are split into N groups balanced by size
+(largest first onto the least-loaded group) and encoded in parallel worker
+processes; the coordinator renames and records their windows in input
+order, and every input's written row count is checked against its decoded
+records.
+
 Operational state: a lease file (exclusive create, owner + expiry) keeps two
 publishers off the same output; the manifest is the resume state (inputs
 already published are skipped); on start, temporary windows left by a
@@ -29,7 +35,9 @@ crashed run are removed (crash reconciliation).
 Reference behaviour: src/flare/data/pipeline/production/pipeline.py:46
 (DataPipeline), publish/runner.py:291-334 (manifest), publication/
 session.py:25 (leases), builder/resume_state_manager.py:45, stages/parse.py:89
-and stages/feature_transform_split.py:24 (parse / encode).  Iceberg commits
+and stages/feature_transform_split.py:24 (parse / encode),
+recipes/recsys/data/heap_stream.py:44-64 (worker planning, size-balanced
+groups) and category_values.py (vocabulary files).  Iceberg commits
 are replaced by the window manifest (no Iceberg client in this build).
 """
 from __future__ import annotations
@@ -181,6 +189,95 @@ class FeatureProcessor:
         return pa.table(cols)
 
 
+# ------------------------------------------------------------------ encode workers
+def encode_input(cfg: PipelineConfig, path: str, out: str, proc: FeatureProcessor | None = None) -> list[dict]:
+    """Encode one input into temporary window directories under ``out`` (renamed on commit).
+
+    Checks that every decoded record is in the written Parquet files.
+    """
+    import pyarrow.parquet as pq
+
+    proc = proc or FeatureProcessor(cfg)
+    windows, cur, decoded = [], None, 0
+    for lines in read_chunks(path, cfg.rows_per_file):
+        if cur is None:
+            cur = {"tmp": f"{TMP_PREFIX}{uuid.uuid4().hex[:12]}", "parts": 0, "rows": 0}
+            (Path(out) / cur["tmp"]).mkdir()
+        table = proc.encode(lines)
+        pq.write_table(table, Path(out) / cur["tmp"] / f"part-{cur['parts']:05d}.parquet")
+        cur["parts"] += 1
+        cur["rows"] += table.num_rows
+        decoded += len(lines)
+        if cur["parts"] == cfg.files_per_window:
+            windows.append(cur)
+            cur = None
+    if cur is not None:
+        windows.append(cur)
+    if sum(w["rows"] for w in windows) != decoded:
+        raise RuntimeError(f"{path}: written rows differ from decoded records")
+    return windows
+
+
+def encode_group(cfg: PipelineConfig, paths: list[str], out: str) -> list[tuple[str, list[dict]]]:
+    """Worker process: encode a group of inputs (one feature processor for all)."""
+    proc = FeatureProcessor(cfg)
+    return [(p, encode_input(cfg, p, out, proc)) for p in paths]
+
+
+def plan_groups(paths: list[str], workers: int) -> list[list[str]]:
+    """Inputs into at most ``workers`` groups balanced by size: the largest remaining input goes to the
+    least-loaded group (a heap of group loads); inputs keep their order inside a group."""
+    import heapq
+
+    heap = [(0, g) for g in range(min(workers, len(paths)))]
+    groups: list[list[int]] = [[] for _ in heap]
+    for i in sorted(range(len(paths)), key=lambda i: (-os.path.getsize(paths[i]), i)):
+        load, g = heapq.heappop(heap)
+        groups[g].append(i)
+        heapq.heappush(heap, (load + os.path.getsize(paths[i]), g))
+    return [[paths[i] for i in sorted(g)] for g in groups if g]
+
+
+def plan_workers(*, cpus: int, memory_bytes: int, cpus_per_worker: int, memory_per_worker: int,
+                 requested: int | None = None) -> int:
+    """Encode workers that fit: leave ~3.5 % of the CPUs (at least one) to the driver and reserve at
+    most 90 % of the memory; a request above that raises."""
+    import math
+
+    if cpus_per_worker <= 0 or memory_per_worker <= 0:
+        raise ValueError("worker CPU and memory reservations must be positive")
+    cpu_slots = (cpus - max(1, math.ceil(cpus * 0.035))) // cpus_per_worker
+    avail = min(cpu_slots, int(memory_bytes * 0.9) // memory_per_worker)
+    if avail < 1:
+        raise ValueError("no encode worker fits the machine")
+    if requested is not None and requested > avail:
+        raise ValueError(f"requested {requested} workers, at most {avail} fit")
+    return requested or avail
+
+
+def load_category_values(category_files: dict[str, str], category_dir: str | Path
+                         ) -> tuple[dict[str, dict[str, int]], frozenset[str]]:
+    """Feature -> {value: index} from vocabulary files (one value per line, index = line order);
+    features declared "auto" get no fixed vocabulary.  Empty or duplicate vocabularies raise."""
+    cache: dict[str, dict[str, int]] = {}
+    values, auto = {}, set()
+    for feature, fname in category_files.items():
+        if fname == "auto":
+            auto.add(feature)
+            continue
+        if fname not in cache:
+            vals = [v.strip() for v in (Path(category_dir) / fname).read_text(encoding="utf-8").splitlines()
+                    if v.strip()]
+            if not vals:
+                raise ValueError(f"category vocabulary {fname} is empty")
+            m = {v: i for i, v in enumerate(vals)}
+            if len(m) != len(vals):
+                raise ValueError(f"category vocabulary {fname} has duplicate values")
+            cache[fname] = m
+        values[feature] = cache[fname]
+    return values, frozenset(auto)
+
+
 # ------------------------------------------------------------------ publication state
 class Lease:
     """Exclusive publisher lease on an output directory (owner + expiry; a stale lease is taken over)."""
@@ -227,7 +324,8 @@ class DataPipeline:
             gone.append(d.name)
         return gone
 
-    def run(self) -> dict:
+    def run(self, workers: int = 1) -> dict:
+        """Publish every input not yet in the manifest; ``workers > 1`` encodes in parallel processes."""
         self.out.mkdir(parents=True, exist_ok=True)
         lease = Lease(self.out, self.cfg.lease_seconds)
         lease.acquire()
@@ -236,38 +334,32 @@ class DataPipeline:
             man = self.manifest()
             done = set(man["inputs_done"])
             todo = [f for f in _input_files(self.cfg.inputs) if f not in done]
-            for path in todo:
-                self._publish_input(path, man)
+            if workers <= 1 or len(todo) <= 1:
+                for path in todo:
+                    self._commit(man, path, encode_input(self.cfg, path, str(self.out)))
+                return man
+            import concurrent.futures as cf
+            import multiprocessing as mp
+
+            groups = plan_groups(todo, workers)
+            with cf.ProcessPoolExecutor(max_workers=len(groups), mp_context=mp.get_context("spawn")) as ex:
+                futs = [ex.submit(encode_group, self.cfg, g, str(self.out)) for g in groups]
+                for fut in futs:  # commit in group order; each group's inputs in order
+                    for path, windows in fut.result():
+                        self._commit(man, path, windows)
             return man
         finally:
             lease.release()
 
-    def _publish_input(self, path: str, man: dict) -> None:
-        import pyarrow.parquet as pq
-
-        window, parts, rows = None, 0, 0
-        wid = len(man["windows"])
-
-        def commit():
-            nonlocal window, parts, rows, wid
+    def _commit(self, man: dict, path: str, windows: list[dict]) -> None:
+        """Rename an input's encoded windows into place and record them (the input is done)."""
+        for w in windows:
+            wid = len(man["windows"])
             final = self.out / f"window-{wid:06d}"
-            os.replace(window, final)
-            man["windows"].append({"id": wid, "dir": final.name, "parts": parts, "rows": rows, "input": path})
+            os.replace(self.out / w["tmp"], final)
+            man["windows"].append({"id": wid, "dir": final.name, "parts": w["parts"], "rows": w["rows"],
+                                   "input": path})
             write_json(self.out / MANIFEST, man)
-            window, parts, rows, wid = None, 0, 0, wid + 1
-
-        for lines in read_chunks(path, self.cfg.rows_per_file):
-            if window is None:
-                window = self.out / f"{TMP_PREFIX}{uuid.uuid4().hex[:12]}"
-                window.mkdir()
-            table = self.proc.encode(lines)
-            pq.write_table(table, window / f"part-{parts:05d}.parquet")
-            parts += 1
-            rows += table.num_rows
-            if parts == self.cfg.files_per_window:
-                commit()
-        if window is not None:
-            commit()
         man["inputs_done"].append(path)
         write_json(self.out / MANIFEST, man)
 
@@ -276,4 +368,5 @@ class DataPipeline:
         return [str(self.out / w["dir"] / f"part-{i:05d}.parquet") for w in man["windows"] for i in range(w["parts"])]
 
 
-__all__ = ["DataPipeline", "DenseSpec", "FeatureProcessor", "Lease", "PipelineConfig", "SparseSpec", "read_chunks"]
+__all__ = ["DataPipeline", "DenseSpec", "FeatureProcessor", "Lease", "PipelineConfig", "SparseSpec", "encode_group",
+           "encode_input", "load_category_values", "plan_groups", "plan_workers", "read_chunks"]

@@ -22,8 +22,14 @@ from .pipeline import DataPipeline, PipelineConfig
 
 
 def main(argv=None) -> int:
-    cfg = LayeredConfigLoader().load(PipelineConfig, list(sys.argv[1:] if argv is None else argv))
-    man = DataPipeline(cfg).run()
+    argv = list(sys.argv[1:] if argv is None else argv)
+    workers = 1
+    if "--workers" in argv:
+        i = argv.index("--workers")
+        workers = int(argv[i + 1])
+        del argv[i:i + 2]
+    cfg = LayeredConfigLoader().load(PipelineConfig, argv)
+    man = DataPipeline(cfg).run(workers=workers)
     print(json.dumps({"windows": len(man["windows"]), "rows": sum(w["rows"] for w in man["windows"]),
                       "inputs": len(man["inputs_done"])}))
     return 0

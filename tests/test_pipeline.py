@@ -97,3 +97,22 @@ def test_cli(tmp_path, capsys):
     assert run_main(["--config", str(tmp_path / "p.json")]) == 0
     assert json.loads(capsys.readouterr().out)["rows"] == 50
 
+
+
+def test_parallel_workers_and_planning(tmp_path):
+    from flare_b200.data.pipeline import load_category_values, plan_groups, plan_workers
+
+    (tmp_path / "logs").mkdir()
+    for i, n in enumerate([300, 50, 120, 80]):
+        _write_logs(tmp_path / "logs" / f"f{i}.txt", n, 10 + i)
+    files = sorted(str(p) for p in (tmp_path / "logs").iterdir())
+    groups = plan_groups(files, 2)
+    assert sorted(f for g in groups for f in g) == files and len(groups) == 2
+    man = DataPipeline(_cfg(tmp_path)).run(workers=2)
+    assert sum(w["rows"] for w in man["windows"]) == 550 and len(man["inputs_done"]) == 4
+    assert plan_workers(cpus=64, memory_bytes=256 << 30, cpus_per_worker=4, memory_per_worker=8 << 30) == 15
+    with pytest.raises(ValueError):
+        plan_workers(cpus=4, memory_bytes=1 << 30, cpus_per_worker=8, memory_per_worker=1 << 20)
+    (tmp_path / "colors.txt").write_text("red\ngreen\n\nblue\n")
+    vals, auto = load_category_values({"c": "colors.txt", "d": "auto"}, tmp_path)
+    assert vals["c"] == {"red": 0, "green": 1, "blue": 2} and auto == {"d"}
