@@ -580,6 +580,31 @@ __global__ void __launch_bounds__(kEmbThreads) emb_rw_reduce_kernel(EmbFwdParams
 // Backward
 // ============================================================================
 
+// Slot table of a backward pass in shared memory: compact staging index k belongs to the slot
+// (shard, source) with slot_start[slot] <= k < slot_start[slot + 1].  Loops run over k with a grid
+// stride (balanced however the slots differ in size) and find the slot by binary search here.
+struct SlotSmem {
+  int start[1025];
+  long long row_base[kMaxShardsSmem];
+};
+
+__device__ __forceinline__ void load_slot_smem(const EmbBwdParams& p, SlotSmem& t) {
+  const int nslot = p.num_shards * p.world;
+  for (int i = threadIdx.x; i <= nslot; i += blockDim.x) t.start[i] = p.slot_start[i];
+  for (int i = threadIdx.x; i < p.num_shards; i += blockDim.x) t.row_base[i] = p.shards[i].row_base;
+  __syncthreads();
+}
+
+__device__ __forceinline__ int find_slot(const SlotSmem& t, int nslot, int k) {
+  int lo = 0, hi = nslot;  // the largest slot with start <= k (empty slots share a start)
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (t.start[mid] <= k) lo = mid;
+    else hi = mid;
+  }
+  return lo;
+}
+
 // 1. pooled-gradient all-to-all (pull) + occurrence counting, ranks, first-occurrence flags
 __global__ void __launch_bounds__(kEmbThreads) emb_bwd_pull_count_kernel(EmbBwdParams p) {
   if (p.world > 1) {
@@ -617,42 +642,40 @@ __global__ void __launch_bounds__(kEmbThreads) emb_bwd_pull_count_kernel(EmbBwdP
   __shared__ int block_total;
   if (threadIdx.x == 0) block_total = 0;
   __syncthreads();
-  // Count occurrences per row over the used staging positions only, slot by slot (compact index
-  // k = slot_start[slot] + j); this occurrence's rank within its row is the counter value before
-  // the add plus its position among equal-row lanes.
+  // Count occurrences per row over the used staging positions only (compact index k); this
+  // occurrence's rank within its row is the counter value before the add plus its position among
+  // equal-row lanes.
+  __shared__ SlotSmem st;
+  load_slot_smem(p, st);
   const int lane = lane_id();
   const int nslot = p.num_shards * p.world;
+  const int T = st.start[nslot];
   const int gw = tid >> 5, nw = nthreads >> 5;
   int local = 0;
-  for (int slot = 0; slot < nslot; ++slot) {
-    const int cnt = static_cast<int>(min(static_cast<int64_t>(p.stage_count[slot]), p.stage_cap));
-    const int kbase = p.slot_start[slot];
-    const int64_t sbase = static_cast<int64_t>(slot) * p.stage_cap;
-    const int64_t row_base = p.shards[slot / p.world].row_base;
-    for (int j0 = gw * 32; j0 < cnt; j0 += nw * 32) {
-      const int j = j0 + lane;
-      long long row = -1;
-      if (j < cnt) {
-        const int id = p.stage_ids[sbase + j];
-        if (id >= 0) row = row_base + id;
-      }
-      const bool valid = row >= 0;
-      const unsigned vmask = __ballot_sync(kFull, valid);
-      int f = 0;
-      if (valid) {
-        ++local;
-        const unsigned peers = __match_any_sync(vmask, row);
-        const int leader = __ffs(peers) - 1;
-        int old = 0;
-        if (lane == leader) old = atomicAdd(p.row_count + row, __popc(peers));
-        old = __shfl_sync(peers, old, leader);
-        const int rank = old + __popc(peers & lanemask_lt());
-        p.stage_rank[kbase + j] = rank;
-        f = rank == 0 ? 1 : 0;
-        if (p.deterministic) atomicMin(p.det_first + row, kbase + j);  // first occurrence by position
-      }
-      if (j < cnt) p.flags[kbase + j] = f;
+  for (int k0 = gw * 32; k0 < T; k0 += nw * 32) {
+    const int k = k0 + lane;
+    long long row = -1;
+    if (k < T) {
+      const int slot = find_slot(st, nslot, k);
+      const int id = p.stage_ids[static_cast<int64_t>(slot) * p.stage_cap + (k - st.start[slot])];
+      if (id >= 0) row = st.row_base[slot / p.world] + id;
     }
+    const bool valid = row >= 0;
+    const unsigned vmask = __ballot_sync(kFull, valid);
+    int f = 0;
+    if (valid) {
+      ++local;
+      const unsigned peers = __match_any_sync(vmask, row);
+      const int leader = __ffs(peers) - 1;
+      int old = 0;
+      if (lane == leader) old = atomicAdd(p.row_count + row, __popc(peers));
+      old = __shfl_sync(peers, old, leader);
+      const int rank = old + __popc(peers & lanemask_lt());
+      p.stage_rank[k] = rank;
+      f = rank == 0 ? 1 : 0;
+      if (p.deterministic) atomicMin(p.det_first + row, k);  // first occurrence by position
+    }
+    if (k < T) p.flags[k] = f;
   }
   local = __reduce_add_sync(kFull, local);
   if (lane == 0 && local) atomicAdd(&block_total, local);
@@ -691,34 +714,34 @@ __global__ void __launch_bounds__(1024) emb_slot_prefix_kernel(EmbBwdParams p) {
 
 // 3. per-unique metadata (slot-major over the used staging positions)
 __global__ void __launch_bounds__(kEmbThreads) emb_emit_kernel(EmbBwdParams p) {
+  __shared__ SlotSmem st;
+  load_slot_smem(p, st);
   const int nslot = p.num_shards * p.world;
   const int tid = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int nthreads = static_cast<int>(gridDim.x) * blockDim.x;
-  if (tid == 0) p.num_unique[0] = p.pos[p.slot_start[nslot]];
-  for (int slot = 0; slot < nslot; ++slot) {
-    const int kbase = p.slot_start[slot], cnt = p.slot_start[slot + 1] - kbase;
-    const int64_t sbase = static_cast<int64_t>(slot) * p.stage_cap;
+  const int T = st.start[nslot];
+  if (tid == 0) p.num_unique[0] = p.pos[T];
+  for (int k = tid; k < T; k += nthreads) {
+    if (!p.flags[k]) continue;
+    const int slot = find_slot(st, nslot, k);
+    const int64_t at = static_cast<int64_t>(slot) * p.stage_cap + (k - st.start[slot]);
     const int sh = slot / p.world;
-    const int64_t row_base = p.shards[sh].row_base;
-    for (int j = tid; j < cnt; j += nthreads) {
-      if (!p.flags[kbase + j]) continue;
-      const int u = p.pos[kbase + j];
-      const long long row = row_base + p.stage_ids[sbase + j];
-      p.uniq_row[u] = row;
-      p.uniq_shard[u] = sh;
-      p.row2u[row] = u;
-      if (p.deterministic) p.det_first[row] = 0x7fffffff;
-      const int c = p.row_count[row];
-      p.cnt_u[u] = c;
-      p.first_gidx[u] = slot * p.Bl + p.stage_bag[sbase + j];
-      if (c > p.light_max) {
-        const int h = atomicAdd(p.num_unique + 2, 1);
-        if (h < p.max_heavy) {
-          p.heavy[h] = u;
-          p.hcnt[h] = c;
-        } else {
-          report_error(p.status, kCapacityOverflow, -1);
-        }
+    const int u = p.pos[k];
+    const long long row = st.row_base[sh] + p.stage_ids[at];
+    p.uniq_row[u] = row;
+    p.uniq_shard[u] = sh;
+    p.row2u[row] = u;
+    if (p.deterministic) p.det_first[row] = 0x7fffffff;
+    const int c = p.row_count[row];
+    p.cnt_u[u] = c;
+    p.first_gidx[u] = slot * p.Bl + p.stage_bag[at];
+    if (c > p.light_max) {
+      const int h = atomicAdd(p.num_unique + 2, 1);
+      if (h < p.max_heavy) {
+        p.heavy[h] = u;
+        p.hcnt[h] = c;
+      } else {
+        report_error(p.status, kCapacityOverflow, -1);
       }
     }
   }
@@ -801,20 +824,20 @@ __global__ void __launch_bounds__(kScanThreads) emb_seg_final_kernel(EmbBwdParam
 
 // 5. occ[seg_start[u] + rank] = staged-grad row, for rows seen more than once
 __global__ void __launch_bounds__(kEmbThreads) emb_fill_kernel(EmbBwdParams p) {
+  __shared__ SlotSmem st;
+  load_slot_smem(p, st);
   const int nslot = p.num_shards * p.world;
   const int tid = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int nthreads = static_cast<int>(gridDim.x) * blockDim.x;
-  for (int slot = 0; slot < nslot; ++slot) {
-    const int kbase = p.slot_start[slot], cnt = p.slot_start[slot + 1] - kbase;
-    const int64_t sbase = static_cast<int64_t>(slot) * p.stage_cap;
-    const int64_t row_base = p.shards[slot / p.world].row_base;
-    for (int j = tid; j < cnt; j += nthreads) {
-      const int id = p.stage_ids[sbase + j];
-      if (id < 0) continue;
-      const int u = p.row2u[row_base + id];
-      if (p.cnt_u[u] <= 1) continue;
-      p.occ[p.seg_start[u] + p.stage_rank[kbase + j]] = slot * p.Bl + p.stage_bag[sbase + j];
-    }
+  const int T = st.start[nslot];
+  for (int k = tid; k < T; k += nthreads) {
+    const int slot = find_slot(st, nslot, k);
+    const int64_t at = static_cast<int64_t>(slot) * p.stage_cap + (k - st.start[slot]);
+    const int id = p.stage_ids[at];
+    if (id < 0) continue;
+    const int u = p.row2u[st.row_base[slot / p.world] + id];
+    if (p.cnt_u[u] <= 1) continue;
+    p.occ[p.seg_start[u] + p.stage_rank[k]] = slot * p.Bl + p.stage_bag[at];
   }
 }
 
@@ -874,17 +897,16 @@ __global__ void __launch_bounds__(kScanThreads) dev_scan_final_kernel(const int*
 // ---- deterministic-reduction mode -------------------------------------------
 // first-occurrence flags by staging position (the counting pass flags the first by atomic order)
 __global__ void __launch_bounds__(kEmbThreads) emb_det_first_kernel(EmbBwdParams p) {
+  __shared__ SlotSmem st;
+  load_slot_smem(p, st);
   const int nslot = p.num_shards * p.world;
   const int tid = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int nthreads = static_cast<int>(gridDim.x) * blockDim.x;
-  for (int slot = 0; slot < nslot; ++slot) {
-    const int kbase = p.slot_start[slot], cnt = p.slot_start[slot + 1] - kbase;
-    const int64_t sbase = static_cast<int64_t>(slot) * p.stage_cap;
-    const int64_t row_base = p.shards[slot / p.world].row_base;
-    for (int j = tid; j < cnt; j += nthreads) {
-      const int id = p.stage_ids[sbase + j];
-      p.flags[kbase + j] = (id >= 0 && p.det_first[row_base + id] == kbase + j) ? 1 : 0;
-    }
+  const int T = st.start[nslot];
+  for (int k = tid; k < T; k += nthreads) {
+    const int slot = find_slot(st, nslot, k);
+    const int id = p.stage_ids[static_cast<int64_t>(slot) * p.stage_cap + (k - st.start[slot])];
+    p.flags[k] = (id >= 0 && p.det_first[st.row_base[slot / p.world] + id] == k) ? 1 : 0;
   }
 }
 
@@ -910,23 +932,23 @@ __global__ void __launch_bounds__(kEmbThreads) emb_det_heavy_place_kernel(EmbBwd
 
 // sort keys: the occurrence's unique row (invalid / unused positions sort last), value: its staged-grad row
 __global__ void __launch_bounds__(kEmbThreads) emb_det_keys_kernel(EmbBwdParams p, int n) {
+  __shared__ SlotSmem st;
+  load_slot_smem(p, st);
   const int nslot = p.num_shards * p.world;
   const int tid = static_cast<int>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int nthreads = static_cast<int>(gridDim.x) * blockDim.x;
-  const int T = p.slot_start[nslot];
-  for (int k = T + tid; k < n; k += nthreads) {
-    p.det_keys[k] = 0x7fffffff;
-    p.det_vals[k] = 0;
-  }
-  for (int slot = 0; slot < nslot; ++slot) {
-    const int kbase = p.slot_start[slot], cnt = p.slot_start[slot + 1] - kbase;
-    const int64_t sbase = static_cast<int64_t>(slot) * p.stage_cap;
-    const int64_t row_base = p.shards[slot / p.world].row_base;
-    for (int j = tid; j < cnt; j += nthreads) {
-      const int id = p.stage_ids[sbase + j];
-      p.det_keys[kbase + j] = id < 0 ? 0x7fffffff : p.row2u[row_base + id];
-      p.det_vals[kbase + j] = slot * p.Bl + p.stage_bag[sbase + j];
+  const int T = st.start[nslot];
+  for (int k = tid; k < n; k += nthreads) {
+    if (k >= T) {
+      p.det_keys[k] = 0x7fffffff;
+      p.det_vals[k] = 0;
+      continue;
     }
+    const int slot = find_slot(st, nslot, k);
+    const int64_t at = static_cast<int64_t>(slot) * p.stage_cap + (k - st.start[slot]);
+    const int id = p.stage_ids[at];
+    p.det_keys[k] = id < 0 ? 0x7fffffff : p.row2u[st.row_base[slot / p.world] + id];
+    p.det_vals[k] = slot * p.Bl + p.stage_bag[at];
   }
 }
 
