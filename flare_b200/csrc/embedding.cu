@@ -1356,6 +1356,8 @@ void bwd_apply(const EmbBwdParams& p, int ncols_max, int grid, cudaStream_t s) {
   // light rows: 2 float4 (8 columns) per lane -> ncols_max / 8 lanes per row
   const int G = std::max(1, ncols_max / 8);
   // 4 blocks per SM: ~10% faster than 3 on the DLRM benchmark despite a few spilled registers
+  // (loading the row-wise state together with the weights, at 3 or 4 blocks per SM, measured 2-3 %
+  // slower on the DLRM benchmark)
   emb_apply_light_kernel<TW, TG, 2, 4><<<grid, kEmbThreads, 0, s>>>(p, G);
   emb_heavy_partial_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(p);
   emb_heavy_final_kernel<<<kScanBlocks, kScanThreads, 0, s>>>(p);
