@@ -1,0 +1,149 @@
+"""Per-rank batch reader: assigned work items, resumable cut position, audit, global valid count.
+
+``BatchReader`` reads the work items of a ``SourceFactory`` assigned to this
+rank (item k goes to rank ``k % world``), cuts them into fixed-size batches
+under a completion policy and yields ``(batch, validity)``.  Its checkpoint
+state is the cut position only: the global ids of the items fully consumed
+and the row offset inside the current one.  ``restore_state`` accepts a
+state saved at any world size (global reshard): the union of every rank's
+saved states marks the consumed items, and the remaining items are dealt to
+the new ranks.  ``repeat_first_batch`` replays the first batch forever (the
+simulation mode used to measure the training path without input cost).
+``close`` writes an audit JSON (items, rows, batches, padded rows, errors,
+seconds).  ``global_valid_count`` sums the valid samples of a step over the
+ranks and checks it against the scheduled work.
+
+Reference behaviour: src/flare/runtime/fluxway/workers/reader.py:77-516
+(BatchReaderSPMD: assigned reads, repeat-first-batch, capture / restore of
+the cut position, audit at shutdown) and recipes/recsys/ranking/workers/
+reader.py:148-166 (global valid-prefix count).
+"""
+from __future__ import annotations
+
+import time
+from collections.abc import Callable, Iterator
+from pathlib import Path
+from typing import Any
+
+from ..io.artifacts import write_json
+from .sources import BatchAssembler, SourceFactory, WorkItem
+
+
+class BatchReader:
+    def __init__(self, factory: SourceFactory, batch_size: int, *, rank: int = 0, world: int = 1,
+                 policy: str = "pad", repeat_first_batch: bool = False, audit_path: str | Path | None = None,
+                 transform: Callable[[Any], Any] | None = None):
+        if not 0 <= rank < world:
+            raise ValueError("rank must be in [0, world)")
+        self.factory, self.B, self.rank, self.world = factory, int(batch_size), rank, world
+        self.policy, self.repeat = policy, bool(repeat_first_batch)
+        self.audit_path = Path(audit_path) if audit_path else None
+        self.transform = transform or (lambda x: x)
+        self.items: list[WorkItem] = [it for it in factory.plan() if it.item_id % world == rank]
+        self.done: set[int] = set()        # global ids of fully consumed items
+        self.cur_item: int | None = None   # global id of the item being read
+        self.cur_row = 0                   # rows of it already handed out
+        self.stats = {"items": 0, "rows": 0, "batches": 0, "padded_rows": 0, "errors": 0}
+        self._t0 = time.time()
+
+    # ------------------------------------------------------------------ state
+    def capture_state(self) -> dict:
+        return {"rank": self.rank, "world": self.world, "done": sorted(self.done),
+                "current": None if self.cur_item is None else [self.cur_item, self.cur_row]}
+
+    def restore_state(self, states: list[dict]) -> None:
+        """Resume from the saved states of every rank of the previous run (any world size)."""
+        done: set[int] = set()
+        partial: dict[int, int] = {}
+        for st in states:
+            done.update(st["done"])
+            if st.get("current"):
+                item, row = st["current"]
+                partial[item] = max(partial.get(item, 0), row)
+        self.done = done
+        all_items = [it for it in self.factory.plan() if it.item_id not in done]
+        self.items = [it for k, it in enumerate(all_items) if k % self.world == self.rank]
+        self._partial = {k: v for k, v in partial.items() if k not in done}
+
+    # ------------------------------------------------------------------ reading
+    def _chunks(self) -> Iterator[tuple[int, Any, int, int]]:
+        session = self.factory.create_session()
+        partial = getattr(self, "_partial", {})
+        try:
+            for it in self.items:
+                if it.item_id in self.done:
+                    continue
+                table = session.read(it)
+                skip = partial.get(it.item_id, 0)
+                rows = table.num_rows if hasattr(table, "num_rows") else len(next(iter(table.values())))
+                if skip:
+                    table = table.slice(skip) if hasattr(table, "slice") else {k: v[skip:] for k, v in table.items()}
+                yield it.item_id, table, rows - skip, skip
+        finally:
+            session.close()
+
+    def _advance(self, valid: int) -> None:
+        """Account ``valid`` more rows handed out: items whose rows are all out are done."""
+        self._emitted += valid
+        while self._pushed and self._pushed[0][2] <= self._emitted:
+            self.done.add(self._pushed.pop(0)[0])
+            self.stats["items"] += 1
+        if self._pushed and self._pushed[0][1] < self._emitted:
+            item, start, _, skip = self._pushed[0]
+            self.cur_item, self.cur_row = item, skip + self._emitted - start
+        else:
+            self.cur_item, self.cur_row = None, 0
+
+    def __iter__(self):
+        asm = BatchAssembler(self.B, self.policy)
+        self._pushed: list[tuple[int, int, int, int]] = []  # (item, first row, end row, skipped rows)
+        self._emitted, pushed_rows, first = 0, 0, None
+        for item, table, n, skip in self._chunks():
+            self._pushed.append((item, pushed_rows, pushed_rows + n, skip))
+            pushed_rows += n
+            self.stats["rows"] += n
+            if n == 0:
+                self._advance(0)
+            for ab in asm.push(table):
+                if self.repeat:
+                    first = first or ab
+                    while True:
+                        self.stats["batches"] += 1
+                        yield self.transform(first.data), first.validity
+                self.stats["batches"] += 1
+                self._advance(ab.validity.valid_count)
+                yield self.transform(ab.data), ab.validity
+        for ab in asm.finish():
+            self.stats["batches"] += 1
+            self.stats["padded_rows"] += ab.validity.batch_size - ab.validity.valid_count
+            self._advance(ab.validity.valid_count)
+            yield self.transform(ab.data), ab.validity
+        # rows the completion policy dropped at the end of the stream are consumed too
+        self._advance(pushed_rows - self._emitted)
+
+    # ------------------------------------------------------------------ accounting
+    def close(self) -> dict:
+        audit = {**self.stats, "rank": self.rank, "world": self.world, "seconds": time.time() - self._t0,
+                 "assigned_items": [it.item_id for it in self.items], "done": sorted(self.done)}
+        if self.audit_path is not None:
+            write_json(self.audit_path, audit)
+        return audit
+
+
+def global_valid_count(valid: int, *, expected: int | None = None) -> int:
+    """Valid samples of this step summed over the ranks (int32 all-reduce); checked against ``expected``."""
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([int(valid)], dtype=torch.int32)
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        if dist.get_backend() == "nccl":
+            t = t.cuda()
+        dist.all_reduce(t)
+    total = int(t.item())
+    if expected is not None and total != expected:
+        raise RuntimeError(f"global valid samples {total} differ from the scheduled {expected}")
+    return total
+
+
+__all__ = ["BatchReader", "global_valid_count"]

@@ -1,0 +1,75 @@
+"""Per-rank batch reader: assignment, cut-position resume across world sizes, repeat mode, audit (CPU)."""
+import json
+
+import pytest
+
+pa = pytest.importorskip("pyarrow")
+pq = pytest.importorskip("pyarrow.parquet")
+
+from flare_b200.data.reader import BatchReader, global_valid_count  # noqa: E402
+from flare_b200.data.sources import ParquetSourceFactory  # noqa: E402
+
+
+def _files(tmp_path, n_files=3, rows=100):
+    paths = []
+    for f in range(n_files):
+        p = tmp_path / f"f{f}.parquet"
+        pq.write_table(pa.table({"x": list(range(f * 1000, f * 1000 + rows))}), p, row_group_size=25)
+        paths.append(str(p))
+    return paths
+
+
+def _ids(batches):
+    return [v for b, val in batches for v in b.column("x").to_pylist()[:val.valid_count]]
+
+
+def test_ranks_partition_the_items_and_audit(tmp_path):
+    fac = ParquetSourceFactory(_files(tmp_path))  # 12 items of 25 rows
+    seen = []
+    for r in range(2):
+        rd = BatchReader(fac, 16, rank=r, world=2, audit_path=tmp_path / f"audit{r}.json")
+        seen += _ids(list(rd))
+        rd.close()
+    assert sorted(seen) == sorted(x for f in range(3) for x in range(f * 1000, f * 1000 + 100))
+    a = json.loads((tmp_path / "audit0.json").read_text())
+    assert a["items"] == 6 and a["rows"] == 150 and a["padded_rows"] == 10
+
+
+def test_resume_with_a_different_world(tmp_path):
+    fac = ParquetSourceFactory(_files(tmp_path))
+    readers = [BatchReader(fac, 25, rank=r, world=2, policy="drop") for r in range(2)]
+    got = []
+    for rd in readers:  # each rank consumes 3 batches (3 whole items) and stops
+        it = iter(rd)
+        got += _ids([next(it) for _ in range(3)])
+    states = [rd.capture_state() for rd in readers]
+    rest = []
+    for r in range(3):  # resume on 3 ranks
+        rd = BatchReader(fac, 25, rank=r, world=3, policy="drop")
+        rd.restore_state(states)
+        rest += _ids(list(rd))
+    assert sorted(got + rest) == sorted(x for f in range(3) for x in range(f * 1000, f * 1000 + 100))
+    assert not set(got) & set(rest)
+
+
+def test_repeat_first_batch_and_global_count(tmp_path):
+    rd = BatchReader(ParquetSourceFactory(_files(tmp_path, 1)), 10, repeat_first_batch=True)
+    it = iter(rd)
+    a, b = next(it), next(it)
+    assert a[0].column("x").to_pylist() == b[0].column("x").to_pylist()
+    assert global_valid_count(10, expected=10) == 10
+    with pytest.raises(RuntimeError):
+        global_valid_count(9, expected=10)
+
+
+def test_cut_position_inside_an_item(tmp_path):
+    fac = ParquetSourceFactory(_files(tmp_path, 2))  # 8 items of 25 rows
+    rd = BatchReader(fac, 10, rank=0, world=1, policy="pad")
+    it = iter(rd)
+    got = _ids([next(it) for _ in range(4)])  # 40 rows: items 0 (25) done, item 1 cut at 15
+    st = rd.capture_state()
+    assert st["done"] == [0] and st["current"] == [1, 15]
+    rd2 = BatchReader(fac, 10, rank=0, world=1, policy="pad")
+    rd2.restore_state([st])
+    rest = _ids(list(rd2))
+    assert sorted(got + rest) == sorted(x for f in range(2) for x in range(f * 1000, f * 1000 + 100))
