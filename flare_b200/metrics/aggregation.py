@@ -33,8 +33,11 @@ class MetricWindow:
         self.trained_sample_count += int(samples)
         self.steps += 1
 
+    def elapsed(self) -> float:
+        return time.perf_counter() - self.start_time
+
     def throughput_samples(self) -> float:
-        dt = time.perf_counter() - self.start_time
+        dt = self.elapsed()
         return self.trained_sample_count / dt if dt > 0 else 0.0
 
 
@@ -82,8 +85,14 @@ class TensorBoardSink:
 
 class TrainMetricsWindow:
     def __init__(self, targets: tuple[str, ...] = ("ctr",), window_steps: int = 100, capacity: int = 1 << 22,
-                 device: torch.device | None = None, sinks: list | None = None, negative_factor: float = 0.0):
+                 device: torch.device | None = None, sinks: list | None = None, negative_factor: float = 0.0,
+                 distributed: bool | None = None, group=None):
+        """``distributed``: merge every rank's window into one exact AUC / GAUC / calibration / loss /
+        throughput (default: when a process group of more than one rank is up).  Every rank must then
+        call ``update`` for the same steps, since the flush is a collective."""
         self.targets = targets
+        self.group = group
+        self.distributed = distributed
         self.window_steps = window_steps
         self.device = device or torch.device("cpu")
         T = len(targets)
@@ -115,19 +124,43 @@ class TrainMetricsWindow:
             return self.flush()
         return None
 
+    def _is_distributed(self) -> bool:
+        if self.distributed is not None:
+            return self.distributed
+        import torch.distributed as dist
+
+        return dist.is_available() and dist.is_initialized() and dist.get_world_size(self.group) > 1
+
     def flush(self) -> dict:
         out: dict[str, float] = {}
         n = self.n
-        if n:
+        if self._is_distributed():
+            from .distributed import _max_scalar, _sum_scalars, distributed_metrics
+
+            grouped = self.has_groups
             for t, name in enumerate(self.targets):
-                s, y = self.scores[:n, t], self.labels[:n, t]
-                out[f"train/auc_{name}"] = auc(s, y)
-                out[f"train/calibration_{name}"] = calibration(s, y)
-                if self.has_groups:
-                    out[f"train/gauc_{name}"] = gauc(s, y, self.groups[:n], self.negative_factor)
-        samples = max(self.window.trained_sample_count, 1)
-        out["train/loss"] = float(self.loss_sum) / samples
-        out["train/throughput_samples"] = self.window.throughput_samples()
+                m = distributed_metrics(self.scores[:n, t], self.labels[:n, t], self.groups[:n] if grouped else None,
+                                        negative_factor=self.negative_factor, group=self.group)
+                for k, v in m.items():
+                    out[f"train/{k}_{name}"] = v
+            elapsed = self.window.elapsed()
+            # loss and samples summed over the ranks, wall time of the slowest rank
+            loss, samples = _sum_scalars([float(self.loss_sum), float(self.window.trained_sample_count)],
+                                         self.group, self.loss_sum.device)
+            slowest = _max_scalar(elapsed, self.group, self.loss_sum.device)
+            out["train/loss"] = loss / max(samples, 1.0)
+            out["train/throughput_samples"] = samples / max(slowest, 1e-9)
+        else:
+            if n:
+                for t, name in enumerate(self.targets):
+                    s, y = self.scores[:n, t], self.labels[:n, t]
+                    out[f"train/auc_{name}"] = auc(s, y)
+                    out[f"train/calibration_{name}"] = calibration(s, y)
+                    if self.has_groups:
+                        out[f"train/gauc_{name}"] = gauc(s, y, self.groups[:n], self.negative_factor)
+            samples = max(self.window.trained_sample_count, 1)
+            out["train/loss"] = float(self.loss_sum) / samples
+            out["train/throughput_samples"] = self.window.throughput_samples()
         step = self.window.steps
         for sink in self.sinks:
             sink.write(step, {k: v for k, v in out.items() if not (isinstance(v, float) and math.isnan(v))})

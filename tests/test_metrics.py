@@ -1,3 +1,5 @@
+import math
+
 import numpy as np
 import pytest
 import torch
@@ -46,3 +48,66 @@ def test_train_metrics_window(tmp_path):
         out = w.update(logits, y, loss_sum=torch.tensor(64 * 0.5))
     assert out is not None and out["train/auc_ctr"] > 0.75 and abs(out["train/loss"] - 0.5) < 1e-9
     assert (tmp_path / "m.jsonl").read_text().count("\n") == 1
+
+
+def _samples(seed, n=3000, groups=17):
+    g = torch.Generator().manual_seed(seed)
+    y = (torch.rand(n, generator=g) < 0.35).float()
+    # coarse scores so that many samples tie, inside a rank and across ranks
+    s = torch.round(torch.sigmoid(y + torch.randn(n, generator=g)) * 64) / 64
+    grp = torch.randint(0, groups, (n,), generator=g)
+    return s, y, grp
+
+
+def test_summary_merge_is_exact_for_any_split():
+    from flare_b200.metrics.distributed import auc_from_summary, gauc_from_summary, merge_summaries, score_summary
+
+    s, y, grp = _samples(3)
+    ref_auc = auc_reference(s.numpy(), y.numpy())
+    ref_gauc = gauc_reference(s.numpy(), y.numpy(), grp.numpy(), 0.5)
+    for cuts in ([1000, 2000], [1, 2999], [1500]):
+        bounds = [0, *cuts, s.numel()]
+        parts = [score_summary(s[a:b], y[a:b], grp[a:b]) for a, b in zip(bounds[:-1], bounds[1:])]
+        merged = merge_summaries(parts)
+        assert merged.shape[0] < s.numel()  # ties collapsed into one key
+        assert abs(auc_from_summary(merged) - ref_auc) < 1e-12
+        assert abs(gauc_from_summary(merged, 0.5) - ref_gauc) < 1e-12
+    one_class = score_summary(s[y > 0.5], y[y > 0.5])
+    assert math.isnan(auc_from_summary(one_class))
+
+
+def _dist_metrics(rank, world):
+    from flare_b200.metrics.aggregation import TrainMetricsWindow
+    from flare_b200.metrics.distributed import distributed_metrics
+
+    s, y, grp = _samples(7, n=2400)
+    n = s.numel() // world
+    sl = slice(rank * n, (rank + 1) * n)
+    m = distributed_metrics(s[sl], y[sl], grp[sl], negative_factor=0.25)
+    # the window: 3 steps of this rank's share, logits whose sigmoid is the score
+    w = TrainMetricsWindow(window_steps=3, capacity=n)
+    logits = torch.logit(s[sl].clamp(1e-6, 1 - 1e-6)).reshape(-1, 1)
+    k = n // 3
+    out = None
+    for i in range(3):
+        part = slice(i * k, (i + 1) * k)
+        out = w.update(logits[part], y[sl][part].reshape(-1, 1), loss_sum=float(rank + 1) * k)
+    return m, out
+
+
+def test_distributed_metrics_over_gloo_ranks():
+    from flare_b200.testing.gloo import run_ranks
+
+    s, y, grp = _samples(7, n=2400)
+    ref_auc = auc_reference(s.numpy(), y.numpy())
+    ref_gauc = gauc_reference(s.numpy(), y.numpy(), grp.numpy(), 0.25)
+    ref_cal = float(s.double().sum() / y.double().sum())
+    sc = torch.sigmoid(torch.logit(s.clamp(1e-6, 1 - 1e-6)))
+    ref_window_auc = auc_reference(sc.numpy(), y.numpy())
+    outs = run_ranks(_dist_metrics, 2)
+    for m, out in outs:
+        assert abs(m["auc"] - ref_auc) < 1e-12 and abs(m["gauc"] - ref_gauc) < 1e-12
+        assert abs(m["calibration"] - ref_cal) < 1e-9
+        assert abs(out["train/auc_ctr"] - ref_window_auc) < 1e-5  # sigmoid of a slice may differ by an ulp
+        assert abs(out["train/loss"] - 1.5) < 1e-12  # (1 * 1200 + 2 * 1200) / 2400
+    assert outs[0][1]["train/auc_ctr"] == outs[1][1]["train/auc_ctr"]
