@@ -51,6 +51,9 @@ def parse():
     p.add_argument("--plan", choices=["uniform", "cost", "cost-rw"], default="uniform",
                    help="table placement: by columns only; weighted by sampled per-table work; and also "
                         "splitting heavy tables into row-wise pieces")
+    p.add_argument("--sparse-policy", choices=["sync", "pipelined"], default="sync",
+                   help="pipelined: the sparse update of step t-1 overlaps step t's dense work (lookups one "
+                        "step stale)")
     p.add_argument("--seed", type=int, default=0)
     return p.parse_args()
 
@@ -135,7 +138,7 @@ def main():
         costs = estimate_table_costs(vocabs, int(B * world * (args.max_bag + 1) / 2), 1.05, device=dev)
     trainer = DLRMTrainer(cfg, B, max_bag_size=args.max_bag, rank=rank, world_size=world, device=dev,
                           seed=args.seed, use_graph=not args.no_graph, values_capacity=max_nnz + 1024,
-                          table_costs=costs, row_split=args.plan == "cost-rw")
+                          table_costs=costs, row_split=args.plan == "cost-rw", sparse_policy=args.sparse_policy)
     plan = trainer.model.emb.plan
     n_rw = len({p.table for p in plan.placements if p.row_shards > 1})
     model = trainer.model
@@ -171,6 +174,7 @@ def main():
     trainer.check()
 
     # embedding-only time (fused fwd + bwd kernels) on this rank, for "embed ms/step"
+    trainer.flush_pending_updates()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
@@ -236,6 +240,8 @@ def main():
                        "sharding_plan": ("uniform" if costs is None else "cost-weighted (lookups + 2 x unique rows)")
                        + f", {n_rw} tables in row-wise pieces",
                        "embed_shards_rank0": len(model.emb.shards),
+                       "sparse_policy": args.sparse_policy if args.sparse_policy == "sync" else
+                       "pipelined (sparse update of step t-1 beside step t's dense work; lookups one step stale)",
                        "tables": 26, "total_rows": sum(vocabs), "embedding_dim": 128,
                        "embedding_storage": "fp32", "sparse_optimizer": "rowwise_adagrad",
                        "dense_optimizer": "adam", "l2": "inputs larger than L2 (tables > 100 GB, "

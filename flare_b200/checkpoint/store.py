@@ -213,6 +213,11 @@ class CheckpointManager:
     root: str
 
     def save(self, step: int, model, *, group: str = "tables", incremental: bool | None = None) -> Path:
+        """Write ``steps/<step>`` for every rank's part of ``model``.  A sparse update the model still
+        holds back (pipelined policy) is applied first, so the saved tables include every step."""
+        flush = getattr(model, "flush_pending_updates", None)
+        if flush is not None:
+            flush()
         rank, _ = _rank_world()
         final = step_dir(self.root, step)
         tmp = final.with_name(f"{final.name}.partial")
@@ -237,6 +242,9 @@ class CheckpointManager:
         step = latest_step(self.root) if step is None else step
         if step is None:
             raise FileNotFoundError(f"no checkpoint under {self.root}")
+        flush = getattr(model, "flush_pending_updates", None)
+        if flush is not None:
+            flush()  # a pending update belongs to the state being replaced
         load_dense(step_dir(self.root, step) / "model", model.dense)
         load_sparse(self.root, step, group, model.emb)
         return step

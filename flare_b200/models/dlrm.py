@@ -11,6 +11,18 @@ captured in a CUDA graph:
     bottom MLP backward -> sharded embedding backward (grad all-to-all + dedup + row-wise optimizer)
     dense optimizer (fused reduce-scatter + Adam + all-gather when data parallel)
 
+With ``sparse_policy="pipelined"`` the sparse update of step t-1 runs in the
+shadow of step t's dense work: a side stream carries every kernel that waits
+on the other ranks (embedding forward of step t, embedding backward of step
+t-1, the dense update) in the same order on every rank, while the main stream
+runs the dense kernels, which wait on nothing.  Step t therefore looks up
+tables that lack the update of step t-1 (staleness one step, the reference's
+``AsyncPolicy.pipelined``: src/flare/runtime/fluxway/workers/sparse_input.py:
+473-476 and the bounded-stale lookups of .../dynamic_embedding.py:109-130);
+``flush_pending_updates`` applies the last pending update (before a
+checkpoint, an evaluation or the end of training, as the reference's
+``flush_pending_updates``, .../dynamic_embedding.py:683).
+
 ``DLRMTorch`` is the same model in plain PyTorch autograd (nn.EmbeddingBag,
 nn.Linear, torch optimizers): the CPU configuration, the numerics oracle and
 the library baseline arm (cuBLAS + NCCL through DDP) of the benchmark.
@@ -94,8 +106,13 @@ class DLRM:
     def __init__(self, cfg: DLRMConfig, batch_size: int, *, max_bag_size: int, rank: int = 0, world_size: int = 1,
                  device: torch.device | None = None, heap: SymmetricHeap | None = None, seed: int = 0,
                  global_batch_size: int | None = None, values_capacity: int | None = None,
-                 table_costs: list[float] | None = None, plan: ShardingPlan | None = None):
+                 table_costs: list[float] | None = None, plan: ShardingPlan | None = None,
+                 sparse_policy: str = "sync"):
+        if sparse_policy not in ("sync", "pipelined"):
+            raise ValueError(f"sparse_policy must be 'sync' or 'pipelined', not {sparse_policy!r}")
         self.cfg = cfg
+        self.sparse_policy = sparse_policy
+        self.pipelined = sparse_policy == "pipelined"
         self.B = int(batch_size)
         self.global_B = int(global_batch_size or batch_size * world_size)
         self.rank, self.world = rank, world_size
@@ -124,7 +141,16 @@ class DLRM:
         self.emb = ShardedEmbeddingBagCollection(
             cfg.tables, self.B, max_bag_size=max_bag_size, rank=rank, world_size=world_size, device=dev, heap=heap,
             optimizer=cfg.sparse_optimizer, seed=seed, values_capacity=values_capacity,
-            plan=plan if plan is not None else dlrm_plan(cfg, world_size, table_costs))
+            plan=plan if plan is not None else dlrm_plan(cfg, world_size, table_costs), pipelined=self.pipelined)
+        # pipelined policy: staging slot of the next forward, slot whose sparse update is pending
+        self._next_slot = 0
+        self.pending_slot: int | None = None
+        if self.pipelined:
+            # high priority: the side stream carries the step's critical path (embedding forward and
+            # backward); the dense kernels beside it fill the SMs it leaves
+            self.comm_stream = torch.cuda.Stream(device=dev, priority=-1)
+            self._ev_fwd = torch.cuda.Event()
+            self._ev_bwd = torch.cuda.Event()
 
         bf = dict(dtype=torch.bfloat16, device=dev)
         self.dense_in = torch.zeros(self.B, cfg.num_dense, dtype=torch.float32, device=dev)
@@ -201,13 +227,79 @@ class DLRM:
 
     def train_step(self) -> torch.Tensor:
         """One full optimizer step; returns the device scalar sum of per-sample losses."""
+        if self.pipelined:
+            return self._pipelined_step()
         loss = self.forward_backward()
         self.emb.backward()
         self.dense.apply()
         return loss
 
+    def _pipelined_step(self) -> torch.Tensor:
+        main = torch.cuda.current_stream(self.device)
+        comm = self.comm_stream
+        slot, pend = self._next_slot, self.pending_slot
+        comm.wait_stream(main)  # this step's inputs and the previous step's dense reads are ordered before
+        cast_pad_bf16(self.dense_in, self.xd)
+        bot = self.bottom.forward(self.xd)
+        with torch.cuda.stream(comm):
+            pooled = self.emb.forward(slot=slot)
+            self._ev_fwd.record(comm)
+            if pend is not None:
+                self.emb.backward(slot=pend)  # the previous step's sparse update, beside this step's dense work
+        main.wait_event(self._ev_fwd)
+        interaction_forward(bot, pooled, self.F, self.inter)
+        h = self.top.forward(self.inter)
+        self.loss_sum.zero_()
+        head_bce(h, self.head_w, self.head_b, self.labels, grad_scale=1.0 / self.global_B, logits=self.logits,
+                 loss_sum=self.loss_sum, dh=self.dh, dw=self.head_dw, db=self.head_db)
+        dinter = self.top.backward(self.dh, need_input_grad=True)
+        interaction_backward(dinter, bot, pooled, self.F, self.dbot, self.emb.grad_ins[slot].local,
+                             relu_mask_bot=True)
+        self.bottom.backward(self.dbot, need_input_grad=False)
+        self._ev_bwd.record(main)
+        with torch.cuda.stream(comm):
+            comm.wait_event(self._ev_bwd)
+            self.dense.apply()
+        main.wait_stream(comm)
+        self._next_slot, self.pending_slot = slot ^ 1, slot
+        return self.loss_sum
+
+    def flush_pending_updates(self) -> bool:
+        """Apply the pending sparse update of the pipelined policy; True if there was one."""
+        if self.pending_slot is None:
+            return False
+        self.emb.backward(slot=self.pending_slot)
+        self.pending_slot = None
+        return True
+
+    # host-side state of a step, for CUDA-graph capture (undone) and replay (advanced)
+    def graph_key(self):
+        """Steps with equal keys launch the same kernels on the same buffers (None: do not capture)."""
+        if not self.pipelined:
+            return 0
+        return None if self.pending_slot is None else (self._next_slot, self.pending_slot)
+
+    def host_state(self) -> tuple:
+        return (self.dense.step, self.emb.step, self._next_slot, self.pending_slot, self.emb._slot)
+
+    def restore_host_state(self, st: tuple) -> None:
+        self.dense.step, self.emb.step, self._next_slot, self.pending_slot, self.emb._slot = st
+
+    def advance_host_state(self) -> None:
+        """The host-side effect of one replayed step (a captured step runs exactly one sparse backward:
+        its own under the sync policy, the pending one under the pipelined policy)."""
+        self.dense.step += 1
+        self.emb.step += 1
+        if self.pipelined:
+            self.emb._slot = self._next_slot
+            self._next_slot, self.pending_slot = self._next_slot ^ 1, self._next_slot
+
     def predict(self) -> torch.Tensor:
-        """Forward only (eval): sigmoid probabilities [B, T]; no state changes besides staging."""
+        """Forward only (eval): sigmoid probabilities [B, T]; no state changes besides staging.
+
+        Under the pipelined policy the pending sparse update is applied first, so the
+        prediction sees every trained step."""
+        self.flush_pending_updates()
         cast_pad_bf16(self.dense_in, self.xd)
         bot = self.bottom.forward(self.xd)
         pooled = self.emb.forward(training=False)

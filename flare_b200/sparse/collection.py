@@ -99,6 +99,7 @@ class ShardedEmbeddingBagCollection:
         timeout_ns: int = PEER_TIMEOUT_NS,
         init: bool = True,
         deterministic: bool | None = None,
+        pipelined: bool = False,
     ):
         if not tables:
             raise ValueError("at least one table is required")
@@ -126,6 +127,15 @@ class ShardedEmbeddingBagCollection:
         self.out_dtype, self.grad_dtype = out_dtype, grad_dtype
         self.step = 0
         dev = self.device
+        # pipelined sparse policy: the backward of step t-1 runs after the forward of step t, so the
+        # buffers a forward fills for its backward (staged ids / bags / lengths, pooled gradients) are
+        # double-buffered and every call names its staging slot
+        self.pipelined = bool(pipelined)
+        self.nbuf = 2 if self.pipelined else 1
+        self._slot = 0
+        if self.pipelined and any(t.dynamic or t.cache_rows is not None for t in self.tables):
+            raise ValueError("the pipelined sparse policy needs resident static tables: the next forward's "
+                             "placement (host tier, dynamic insert) could move a row the pending update writes")
 
         # ---- row-wise tables: fp32 partial-sum columns (every requester adds the pieces' partials) ----
         self.rw_part_col: dict[int, int] = {}
@@ -221,10 +231,13 @@ class ShardedEmbeddingBagCollection:
         ns = max(len(self.shards), 1)
         self.stage_cap = self.B * self.max_bag
         nslot = ns * world_size
-        self.stage_ids = torch.empty(nslot * self.stage_cap, dtype=torch.int32, device=dev)
-        self.stage_bag = torch.empty(nslot * self.stage_cap, dtype=torch.int32, device=dev)
-        self.stage_count = torch.zeros(nslot, dtype=torch.int32, device=dev)
-        self.stage_len = torch.zeros(nslot * self.B, dtype=torch.int32, device=dev)
+        self._stages = [dict(ids=torch.empty(nslot * self.stage_cap, dtype=torch.int32, device=dev),
+                             bag=torch.empty(nslot * self.stage_cap, dtype=torch.int32, device=dev),
+                             count=torch.zeros(nslot, dtype=torch.int32, device=dev),
+                             len=torch.zeros(nslot * self.B, dtype=torch.int32, device=dev))
+                        for _ in range(self.nbuf)]
+        st0 = self._stages[0]
+        self.stage_ids, self.stage_bag, self.stage_count, self.stage_len = st0["ids"], st0["bag"], st0["count"], st0["len"]
         # multi-GPU: local copies of every (shard, source) offset run (ids go to stage_ids) fetched in bulk
         # before the forward (FLARE_EMB_FETCH=0 reads them from the peers inside the forward instead)
         self.fetch = world_size > 1 and os.environ.get("FLARE_EMB_FETCH", "1") != "0"
@@ -279,7 +292,8 @@ class ShardedEmbeddingBagCollection:
         self.in_offsets = heap.alloc((self.F * self.B + 1,), torch.int32)
         self.in_values = heap.alloc((self.values_capacity,), torch.int32)
         self.pooled = heap.alloc((self.B, self.total_dim), out_dtype)
-        self.grad_in = heap.alloc((self.B, self.total_dim), grad_dtype)
+        self.grad_ins = [heap.alloc((self.B, self.total_dim), grad_dtype) for _ in range(self.nbuf)]
+        self.grad_in = self.grad_ins[0]
         self.flags = FlagRegion(heap, NUM_FLAG_ARRAYS)
         any_dynamic = any(t.dynamic for t in self.tables)
         # dynamic tables: owners write each occurrence's slot into the requester's remap buffer
@@ -291,8 +305,8 @@ class ShardedEmbeddingBagCollection:
             "offsets": self.in_offsets.peer_ptr_tensor(dev),
             "values": self.in_values.peer_ptr_tensor(dev),
             "out": self.pooled.peer_ptr_tensor(dev),
-            "grad": self.grad_in.peer_ptr_tensor(dev),
         }
+        self._peer_grad = [g.peer_ptr_tensor(dev) for g in self.grad_ins]
         if self.remap is not None:
             self._peer["remap"] = self.remap.peer_ptr_tensor(dev)
         if self.partials is not None:
@@ -315,7 +329,8 @@ class ShardedEmbeddingBagCollection:
 
     @staticmethod
     def exchange_bytes(tables: list[SparseTableSpec], batch_size: int, max_bag_size: int,
-                       values_capacity: int | None = None, plan: ShardingPlan | None = None) -> int:
+                       values_capacity: int | None = None, plan: ShardingPlan | None = None,
+                       pipelined: bool = False) -> int:
         """Symmetric memory of the exchange buffers (ids, pooled rows, pooled grads, row-wise partials)."""
         F, B = len(tables), int(batch_size)
         cap = values_capacity or F * B * max_bag_size
@@ -324,11 +339,12 @@ class ShardedEmbeddingBagCollection:
         rw = [i for i, r in enumerate(shards) if r > 1]
         part = 4 * max([shards[i] for i in rw], default=0) * B * sum(tables[i].embedding_dim for i in rw)
         remap = 4 * cap if any(t.dynamic for t in tables) else 0
-        return 4 * (F * B + 1) + 4 * cap + remap + 2 * 4 * B * dim + part + NUM_FLAG_ARRAYS * 64 + 4096
+        grads = 2 if pipelined else 1
+        return 4 * (F * B + 1) + 4 * cap + remap + (1 + grads) * 4 * B * dim + part + NUM_FLAG_ARRAYS * 64 + 4096
 
     def _heap_bytes(self) -> int:
         b = (self.F * self.B + 1) * 4 + 2 * self.F * self.B * self.max_bag * 4
-        b += 2 * self.B * self.total_dim * 4 + NUM_FLAG_ARRAYS * 64 + 8 * 256
+        b += (1 + self.nbuf) * self.B * self.total_dim * 4 + NUM_FLAG_ARRAYS * 64 + 8 * 256
         b += self.rw_slots * self.B * self.part_total * 4 + 256
         return b + (1 << 20)
 
@@ -340,8 +356,14 @@ class ShardedEmbeddingBagCollection:
 
     @property
     def grad_input(self) -> torch.Tensor:
-        """[B, total_dim] buffer the dense backward writes the pooled gradients into."""
-        return self.grad_in.local
+        """[B, total_dim] buffer the dense backward writes the pooled gradients into (slot of the last forward)."""
+        return self.grad_ins[self._slot].local
+
+    def _slot_of(self, slot: int | None) -> int:
+        s = self._slot if slot is None else int(slot)
+        if not 0 <= s < self.nbuf:
+            raise ValueError(f"staging slot {s} out of range (the collection has {self.nbuf})")
+        return s
 
     def set_input(self, offsets: torch.Tensor, values: torch.Tensor, non_blocking: bool = True) -> None:
         """Copy this rank's keyed-jagged batch into the exchange buffers."""
@@ -353,18 +375,22 @@ class ShardedEmbeddingBagCollection:
         self.in_offsets.local.copy_(offsets, non_blocking=non_blocking)
         self.in_values.local[:n].copy_(values, non_blocking=non_blocking)
 
-    def forward(self, training: bool = True) -> torch.Tensor:
-        """Pooled embeddings of this rank's batch; ``training`` also stages the backward."""
+    def forward(self, training: bool = True, slot: int | None = None) -> torch.Tensor:
+        """Pooled embeddings of this rank's batch; ``training`` also stages the backward (into ``slot``)."""
+        sl = self._slot_of(slot)
+        if training:
+            self._slot = sl
+        st = self._stages[sl]
         d = dict(
             shards=self.shard_desc.data_ptr(), num_shards=len(self.shards), world=self.world, rank=self.rank,
             Bl=self.B, F=self.F, peer_offsets=self._peer["offsets"].data_ptr(),
             peer_values=self._peer["values"].data_ptr(), peer_out=self._peer["out"].data_ptr(),
             out_stride=self.total_dim, weights=self.weights.data_ptr(), w_dtype=dtype_code(self.value_dtype),
             out_dtype=dtype_code(self.out_dtype), vec=self.bulk_vec if self.bulk else self.vec,
-            bulk=1 if self.bulk else 0, stage_ids=self.stage_ids.data_ptr(),
+            bulk=1 if self.bulk else 0, stage_ids=st["ids"].data_ptr(),
             slot_map=self.slot_map.data_ptr() if self.slot_map is not None else 0,
-            stage_bag=self.stage_bag.data_ptr(), stage_count=self.stage_count.data_ptr(),
-            stage_len=self.stage_len.data_ptr(), stage_cap=self.stage_cap,
+            stage_bag=st["bag"].data_ptr(), stage_count=st["count"].data_ptr(),
+            stage_len=st["len"].data_ptr(), stage_cap=self.stage_cap,
             flags_local=self.flags.local_ptr, peer_flags=self.flags.peer_ptrs.data_ptr(),
             flag_in=self.flags.slots(FLAG_FWD_IN), flag_out=self.flags.slots(FLAG_FWD_OUT),
             epoch_ctr=self.flags.epoch_ptr(FLAG_FWD_IN), block_counter=self.flags.block_counter_ptr(FLAG_FWD_IN),
@@ -383,12 +409,14 @@ class ShardedEmbeddingBagCollection:
         native().emb_forward(d)
         return self.pooled.local
 
-    def backward(self, step: int | None = None) -> None:
-        """Consume ``grad_input`` (pooled gradients) and update the owned shards.
+    def backward(self, step: int | None = None, slot: int | None = None) -> None:
+        """Consume the pooled gradients of staging ``slot`` (default: the last forward's) and update the owned shards.
 
         The optimizer step used for bias corrections is the device counter,
         advanced by one per call (``step`` sets it explicitly first).
         """
+        sl = self._slot_of(slot)
+        st = self._stages[sl]
         if step is not None:
             self.step = int(step) - 1
             self.step_dev.fill_(self.step)
@@ -406,12 +434,12 @@ class ShardedEmbeddingBagCollection:
         )
         d = dict(
             shards=self.shard_desc.data_ptr(), num_shards=len(self.shards), world=self.world, rank=self.rank,
-            Bl=self.B, peer_grad=self._peer["grad"].data_ptr(), out_stride=self.total_dim,
+            Bl=self.B, peer_grad=self._peer_grad[sl].data_ptr(), out_stride=self.total_dim,
             grad_dtype=dtype_code(self.grad_dtype), grad_stage=self.grad_stage.data_ptr(),
-            grad_stage_ld=self.grad_stage_ld, stage_ids=self.stage_ids.data_ptr(),
-            stage_bag=self.stage_bag.data_ptr(), stage_rank=self.stage_rank.data_ptr(),
+            grad_stage_ld=self.grad_stage_ld, stage_ids=st["ids"].data_ptr(),
+            stage_bag=st["bag"].data_ptr(), stage_rank=self.stage_rank.data_ptr(),
             slot_start=self.slot_start.data_ptr(),
-            stage_count=self.stage_count.data_ptr(), stage_len=self.stage_len.data_ptr(),
+            stage_count=st["count"].data_ptr(), stage_len=st["len"].data_ptr(),
             stage_cap=self.stage_cap, weights=self.weights.data_ptr(), w_dtype=dtype_code(self.value_dtype),
             row_count=self.row_count.data_ptr(), row2u=self.row2u.data_ptr(), flags=self.flags_occ.data_ptr(),
             pos=self.pos.data_ptr(), uniq_row=self.uniq_row.data_ptr(), uniq_shard=self.uniq_shard.data_ptr(),

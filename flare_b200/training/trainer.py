@@ -50,6 +50,7 @@ class FusedTrainer:
         self.model = model
         self.use_graph = use_graph
         self.graph: torch.cuda.CUDAGraph | None = None
+        self.graphs: dict = {}  # graph key of the model's host state -> captured step
         self.launches_per_step: int | None = None
         self.steps = 0
         self.copy_stream = torch.cuda.Stream(device=self.device)
@@ -71,33 +72,59 @@ class FusedTrainer:
     # ---------------------------------------------------------------- graph
     EAGER_STEPS = 2  # steps run eagerly (module load, allocator warm-up) before capture
 
-    def prepare_execution(self) -> None:
-        """Capture the training step as a CUDA graph.
+    def _graph_key(self):
+        f = getattr(self.model, "graph_key", None)
+        return 0 if f is None else f()
 
-        Capture records kernels without running them, so it changes no state;
-        the first replay performs the step.  Step counters used by the
-        optimizers are device-resident and advance inside the graph.
+    def _host_state(self):
+        f = getattr(self.model, "host_state", None)
+        return f() if f is not None else (self.model.dense.step, self.model.emb.step)
+
+    def _restore_host_state(self, st) -> None:
+        f = getattr(self.model, "restore_host_state", None)
+        if f is not None:
+            f(st)
+        else:
+            self.model.dense.step, self.model.emb.step = st
+
+    def _advance_host_state(self) -> None:
+        f = getattr(self.model, "advance_host_state", None)
+        if f is not None:
+            f()
+        else:
+            self.model.dense.step += 1
+            self.model.emb.step += 1
+
+    def prepare_execution(self) -> None:
+        """Capture the training step of the model's current host state as a CUDA graph.
+
+        Capture records kernels without running them, so it changes no state
+        (the host-side mirrors the recording advanced are put back); the first
+        replay performs the step.  Step counters used by the optimizers are
+        device-resident and advance inside the graph.  A model whose steps
+        alternate buffers (the pipelined sparse policy) gets one graph per key.
         """
-        if not self.use_graph or self.graph is not None:
+        key = self._graph_key()
+        if not self.use_graph or key is None or key in self.graphs:
             return
         torch.cuda.synchronize(self.device)
+        st = self._host_state()
         before = native().launch_count()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             self.model.train_step()
         self.launches_per_step = native().launch_count() - before
-        # train_step advanced the host mirrors while recording; undo that
-        self.model.dense.step -= 1
-        self.model.emb.step -= 1
+        self._restore_host_state(st)
+        self.graphs[key] = g
         self.graph = g
 
     def _run_step(self) -> torch.Tensor:
-        if self.use_graph and self.graph is None and self.steps >= self.EAGER_STEPS:
+        if self.use_graph and self.steps >= self.EAGER_STEPS:
             self.prepare_execution()
-        if self.graph is not None:
-            self.graph.replay()
-            self.model.dense.step += 1
-            self.model.emb.step += 1
+        g = self.graphs.get(self._graph_key()) if self.use_graph else None
+        if g is not None:
+            g.replay()
+            self._advance_host_state()
             return self.model.loss_sum
         before = native().launch_count()
         loss = self.model.train_step()
@@ -164,8 +191,15 @@ class FusedTrainer:
     def check(self) -> None:
         self.model.check()
 
+    def flush_pending_updates(self) -> bool:
+        """Apply a sparse update the model still holds back (pipelined policy); True if there was one."""
+        f = getattr(self.model, "flush_pending_updates", None)
+        return bool(f()) if f is not None else False
+
     def close(self) -> None:
+        self.flush_pending_updates()
         self.graph = None
+        self.graphs.clear()
         torch.cuda.synchronize(self.device)
 
 
@@ -173,19 +207,21 @@ class DLRMTrainer(FusedTrainer):
     def __init__(self, cfg: DLRMConfig, batch_size: int, *, max_bag_size: int, rank: int = 0, world_size: int = 1,
                  device: torch.device | None = None, seed: int = 0, use_graph: bool = True,
                  values_capacity: int | None = None, heap_bytes: int | None = None,
-                 table_costs: list[float] | None = None, row_split: bool = False):
+                 table_costs: list[float] | None = None, row_split: bool = False, sparse_policy: str = "sync"):
         device = device or torch.device("cuda", torch.cuda.current_device())
         heap = None
         plan = dlrm_plan(cfg, world_size, table_costs, row_split=row_split)
         if world_size > 1:
             exchange = ShardedEmbeddingBagCollection.exchange_bytes(cfg.tables, batch_size, max_bag_size,
-                                                                    values_capacity, plan=plan)
+                                                                    values_capacity, plan=plan,
+                                                                    pipelined=sparse_policy == "pipelined")
             dense = 6 * 16 * 1024 * 1024  # flat fp32 grads + bf16 params for up to 16M parameters
             need = heap_bytes or (exchange + dense + 64 * 1024 * 1024)
             heap = SymmetricHeap(need, rank=rank, world_size=world_size, device=device)
         self.heap = heap
         model = DLRM(cfg, batch_size, max_bag_size=max_bag_size, rank=rank, world_size=world_size,
-                     device=device, heap=heap, seed=seed, values_capacity=values_capacity, plan=plan)
+                     device=device, heap=heap, seed=seed, values_capacity=values_capacity, plan=plan,
+                     sparse_policy=sparse_policy)
         super().__init__(model, batch_size, device=device, rank=rank, world_size=world_size, use_graph=use_graph)
 
 

@@ -49,3 +49,36 @@ def test_training_reduces_loss_and_graph_matches_eager(cuda):
     assert sum(eager[-8:]) / 8 < sum(eager[:4]) / 4
     for a, b in zip(eager, graph):
         assert abs(a - b) <= 1e-3 * max(1.0, abs(a)), (a, b)
+
+
+def test_pipelined_policy_matches_stale_emulation(cuda):
+    """Pipelined steps equal sync steps whose lookups read the tables one sparse update behind."""
+    cfg = _cfg(lr_sparse=0.05)
+    B = 256
+    data = DLRMSyntheticData(B, VOCABS, max_bag=8, device=cuda, seed=11, pos_rate=0.3)
+    batches = [data.next() for _ in range(7)]
+    tr = DLRMTrainer(cfg, B, max_bag_size=8, device=cuda, seed=4, use_graph=True, sparse_policy="pipelined")
+    piped = [tr.train_step(b).loss for b in batches]
+    assert tr.model.pending_slot is not None and len(tr.graphs) == 2  # slots alternate: one graph per parity
+    assert tr.flush_pending_updates() and not tr.flush_pending_updates()
+    tr.check()
+
+    ref = DLRM(cfg, B, max_bag_size=8, device=cuda, seed=4)
+    prev, emulated = None, []
+    for b in batches:
+        ref.set_batch(b.dense, b.labels, b.offsets, b.values, non_blocking=False)
+        cur = ref.emb.weights.clone()  # tables with the updates of every earlier step
+        if prev is not None:
+            ref.emb.weights.copy_(prev)  # lookups see the tables before the previous step's update
+        loss = ref.forward_backward()
+        ref.emb.weights.copy_(cur)
+        ref.emb.backward()
+        ref.dense.apply()
+        emulated.append(float(loss.item()) / B)
+        prev = cur
+    ref.check()
+    for a, b in zip(piped, emulated):
+        assert abs(a - b) <= 1e-3 * max(1.0, abs(a)), (piped, emulated)
+    torch.testing.assert_close(tr.model.emb.weights, ref.emb.weights, rtol=1e-3, atol=1e-4)
+    torch.testing.assert_close(tr.model.dense.master, ref.dense.master, rtol=1e-3, atol=1e-4)
+    tr.close()
