@@ -358,6 +358,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.demb = P<__nv_bfloat16>(get_or<uintptr_t>(d, "demb", 0));
     p.demb_ld = get_or<int64_t>(d, "demb_ld", 0);
     p.relu_mask_bot = get_or<int>(d, "relu_mask_bot", 1);
+    p.status = P<int>(get_or<uintptr_t>(d, "status", 0));
     return p;
   };
   m.def("interaction_forward", [parse_inter](const py::dict& d) { flare::interaction_forward(parse_inter(d), cur_stream()); });

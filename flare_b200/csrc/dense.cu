@@ -1,5 +1,7 @@
 // Dense-tower kernels other than the GEMM (sm_100a):
-//   * DLRM pairwise dot interaction, forward and backward (one warp/sample)
+//   * DLRM pairwise dot interaction, forward and backward: tcgen05 MMAs over
+//     four samples per 128-row tile (up to 32 vectors a sample), and the
+//     CUDA-core kernels (one warp per sample) for 33 vectors
 //   * fused prediction head + multi-target weighted sigmoid BCE, forward and
 //     backward in one pass (replaces optax sigmoid_binary_cross_entropy used by
 //     recipes/recsys/ranking/losses.py:69-95 of the reference)
@@ -9,6 +11,8 @@
 //     memory (ZeRO-1 semantics of src/flare/training/zero/contracts.py:40-48)
 //   * small helpers: fp32 -> bf16 cast with padding, counter-based uniform init
 #include "dense.cuh"
+#include "gemm.cuh"
+#include "sm100.cuh"
 
 #include <algorithm>
 
@@ -212,6 +216,275 @@ __global__ void __launch_bounds__(kInterWarps * 32) interaction_bwd_kernel(Inter
     }
     __syncwarp();
   }
+}
+
+// ----------------------- interaction on tcgen05 ---------------------------
+// Four samples share one 128-row tile: row 32*s + i holds vector i of sample
+// s (bot, then the F pooled embeddings; rows T..31 zero), stored K-major with
+// the 128-byte swizzle in D/64 atoms of 16 KB.
+//   forward:  one 128 x 128 x D MMA (A = B = the tile) gives every dot product
+//             inside the group; warp s reads its sample's diagonal 32 x 32
+//             block from TMEM with one tcgen05.ld and keeps the strict lower
+//             triangle (the other 12 blocks are the price of a full tile).
+//   backward: dZ = S Z per sample, with S the symmetric dDot matrix (zero
+//             diagonal).  The four S's sit on the diagonal of a 128 x 128 bf16
+//             tile (off-diagonal blocks zero), and the same Z tile read as an
+//             MN-major operand (K = vector index, N = column) is B: one
+//             128 x D x 128 MMA.  dDot is bf16 already, so S loses nothing.
+// One CTA of 4 warps (one per sample of the group) loops over groups; a
+// thread owns tile row 32*warp + lane in both epilogues.
+constexpr int kItThreads = 128;
+constexpr int kItAtom = 16384;  // one 64-column atom of a 128-row tile
+constexpr uint64_t kItTimeoutNs = 2000000000ull;
+
+__device__ __forceinline__ void st_sw128(uint8_t* tile, int r, int c, uint4 v) {
+  const int atom = c >> 3, ch = c & 7;
+  *reinterpret_cast<uint4*>(tile + atom * kItAtom + r * 128 + ((ch ^ (r & 7)) << 4)) = v;
+}
+// K-major operand, k-step k (16 columns): atom k / 4, 32 bytes per step inside the 128-byte row
+__device__ __forceinline__ uint64_t it_desc_k(uint32_t base, int k) {
+  return sm100::make_smem_desc(base + (k >> 2) * kItAtom + (k & 3) * 32, 16, 1024);
+}
+// MN-major operand, k-step k (16 tile rows of 128 bytes); 64-column atoms kItAtom apart
+__device__ __forceinline__ uint64_t it_desc_mn(uint32_t base, int k) {
+  return sm100::make_smem_desc(base + k * 2048, kItAtom, 1024);
+}
+
+// rows [32*w, 32*w + 32) of the Z tile from sample b (zeros past T, or for a sample past the batch);
+// every global load of a lane is issued before its shared-memory stores
+__device__ __forceinline__ void stage_group_z(uint8_t* tile, int w, const InteractionParams& p, int b, bool valid,
+                                              int T) {
+  const int lane = lane_id();
+  const int qpr = p.D / 8;  // 16-byte chunks per row
+  const int total = 32 * qpr;
+  const __nv_bfloat16* bot = p.bot + static_cast<int64_t>(b) * p.bot_ld;
+  const __nv_bfloat16* emb = p.emb + static_cast<int64_t>(b) * p.emb_ld;
+  constexpr int kBatch = 16;  // D = 128: the whole sample in one round trip
+  for (int q0 = 0; q0 < total; q0 += 32 * kBatch) {
+    uint4 buf[kBatch];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int q = q0 + lane + 32 * k;
+      const int r = q / qpr, c = q - r * qpr;
+      buf[k] = make_uint4(0u, 0u, 0u, 0u);
+      if (valid && q < total && r < T)
+        buf[k] = *reinterpret_cast<const uint4*>(r == 0 ? bot + 8 * c : emb + static_cast<int64_t>(r - 1) * p.D + 8 * c);
+    }
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int q = q0 + lane + 32 * k;
+      if (q < total) {
+        const int r = q / qpr, c = q - r * qpr;
+        st_sw128(tile, 32 * w + r, c, buf[k]);
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kItThreads) interaction_fwd_tc_kernel(InteractionParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  const int natoms = p.D / 64;
+  const int opitch = static_cast<int>(p.out_ld) + 8;  // bf16 per output staging row (16-byte multiple)
+  uint8_t* ztile = sm;
+  const int tid = threadIdx.x, w = warp_id(), lane = lane_id();
+  __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(sm + natoms * kItAtom) + w * opitch;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + natoms * kItAtom + 4 * opitch * 2);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
+  const int T = p.F + 1, npairs = T * (T - 1) / 2;
+  if (tid == 0) {
+    sm100::mbar_init(bar, 1);
+    sm100::fence_mbar_init();
+  }
+  if (w == 0) {
+    sm100::tmem_alloc(tslot, 128);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t zaddr = smem_u32(ztile);
+  constexpr uint32_t idesc = sm100::make_idesc_bf16(128, 128, false, false);
+  const int ngroups = (p.B + 3) / 4;
+  uint32_t phase = 0;
+  for (int g = blockIdx.x; g < ngroups; g += gridDim.x) {
+    const int b = 4 * g + w;
+    const bool valid = b < p.B;
+    stage_group_z(ztile, w, p, b, valid, T);
+    if (valid) {  // the output row: bot, (dots later), zero tail
+      const uint4* bot = reinterpret_cast<const uint4*>(p.bot + static_cast<int64_t>(b) * p.bot_ld);
+      for (int c = lane; c < p.D / 8; c += 32) reinterpret_cast<uint4*>(orow)[c] = bot[c];
+      for (int c = p.D + npairs + lane; c < p.out_ld; c += 32) orow[c] = __float2bfloat16_rn(0.f);
+    }
+    sm100::fence_proxy_async_smem();  // the tile's generic-proxy stores, visible to the tensor core
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    if (tid == 0) {
+      for (int k = 0; k < p.D / 16; ++k)
+        sm100::mma_f16_ss(tmem, it_desc_k(zaddr, k), it_desc_k(zaddr, k), idesc, k > 0 ? 1u : 0u);
+      sm100::mma_commit(bar);
+    }
+    const bool done = sm100::mbar_wait(bar, phase, kItTimeoutNs, p.status, g);
+    phase ^= 1u;
+    if (!__syncthreads_and(done ? 1 : 0)) break;  // the status word holds the timeout
+    sm100::tc_fence_after();
+    uint32_t r[32];
+    sm100::tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(32 * w) << 16) + static_cast<uint32_t>(32 * w), r);
+    sm100::tmem_ld_wait();
+    if (valid) {
+      const int i = lane;
+      if (i >= 1 && i < T) {
+        __nv_bfloat16* dst = orow + p.D + i * (i - 1) / 2;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < i) dst[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+      }
+      __syncwarp();
+      uint4* out = reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(b) * p.out_ld);
+      for (int q = lane; q < p.out_ld / 8; q += 32) out[q] = reinterpret_cast<const uint4*>(orow)[q];
+    }
+    sm100::tc_fence_before();
+    __syncthreads();  // TMEM read and tile / staging row consumed before the next group
+  }
+  sm100::tc_fence_after();
+  if (w == 0) sm100::tmem_dealloc(tmem, 128);
+}
+
+__global__ void __launch_bounds__(kItThreads) interaction_bwd_tc_kernel(InteractionParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  const int natoms = p.D / 64;
+  const int T = p.F + 1, npairs = T * (T - 1) / 2;
+  const int dlen = p.D + (npairs + 7) / 8 * 8;  // staged dOut prefix: d(bot) part + dDot (16-byte chunks)
+  const int dpitch = dlen + 8;                  // bf16 per staging row
+  uint8_t* ztile = sm;
+  uint8_t* stile = sm + natoms * kItAtom;  // 128 x 128 bf16: two atoms
+  const int tid = threadIdx.x, w = warp_id(), lane = lane_id();
+  __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(stile + 2 * kItAtom) + w * dpitch;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(stile + 2 * kItAtom + 4 * dpitch * 2);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
+  // the off-diagonal blocks of S stay zero; the diagonal blocks are rewritten for every group
+  for (int q = tid; q < 2 * kItAtom / 16; q += kItThreads)
+    reinterpret_cast<uint4*>(stile)[q] = make_uint4(0u, 0u, 0u, 0u);
+  if (tid == 0) {
+    sm100::mbar_init(bar, 1);
+    sm100::fence_mbar_init();
+  }
+  if (w == 0) {
+    sm100::tmem_alloc(tslot, static_cast<uint32_t>(p.D));
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t zaddr = smem_u32(ztile), saddr = smem_u32(stile);
+  const uint32_t idesc = sm100::make_idesc_bf16(128, p.D, false, true);
+  const int ngroups = (p.B + 3) / 4;
+  uint32_t phase = 0;
+  for (int g = blockIdx.x; g < ngroups; g += gridDim.x) {
+    const int b = 4 * g + w;
+    const bool valid = b < p.B;
+    // this sample's dOut row up to the last dDot (out_ld covers the rounded tail): loads first, so
+    // they overlap the tile staging
+    uint4 dq[4];
+    const uint4* dsrc = reinterpret_cast<const uint4*>(p.dout + static_cast<int64_t>(b) * p.out_ld);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int q = lane + 32 * k;
+      dq[k] = (valid && q < dlen / 8) ? dsrc[q] : make_uint4(0u, 0u, 0u, 0u);
+    }
+    stage_group_z(ztile, w, p, b, valid, T);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int q = lane + 32 * k;
+      if (q < dlen / 8) reinterpret_cast<uint4*>(drow)[q] = dq[k];
+    }
+    __syncwarp();
+    // row i = lane of S_b: S[i][j] = dDot(max, min) for i != j < T, else 0 (columns 32*w + j)
+#pragma unroll
+    for (int c4 = 0; c4 < 4; ++c4) {
+      uint32_t wd[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        uint32_t h[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int j = c4 * 8 + t * 2 + e;
+          h[e] = 0u;
+          if (valid && lane < T && j < T && j != lane) {
+            const int hi = max(lane, j), lo = min(lane, j);
+            h[e] = __bfloat16_as_ushort(drow[p.D + hi * (hi - 1) / 2 + lo]);
+          }
+        }
+        wd[t] = h[0] | (h[1] << 16);
+      }
+      st_sw128(stile, 32 * w + lane, 4 * w + c4, make_uint4(wd[0], wd[1], wd[2], wd[3]));
+    }
+    sm100::fence_proxy_async_smem();
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    if (tid == 0) {
+      for (int k = 0; k < 8; ++k)  // K = 128 tile rows
+        sm100::mma_f16_ss(tmem, it_desc_k(saddr, k), it_desc_mn(zaddr, k), idesc, k > 0 ? 1u : 0u);
+      sm100::mma_commit(bar);
+    }
+    const bool done = sm100::mbar_wait(bar, phase, kItTimeoutNs, p.status, g);
+    phase ^= 1u;
+    if (!__syncthreads_and(done ? 1 : 0)) break;
+    sm100::tc_fence_after();
+    const int i = lane;
+    const bool act = valid && i < T;
+    __nv_bfloat16* dst = i == 0 ? p.dbot + static_cast<int64_t>(b) * p.dbot_ld
+                                : p.demb + static_cast<int64_t>(b) * p.demb_ld + static_cast<int64_t>(i - 1) * p.D;
+    for (int cc = 0; cc < p.D / 32; ++cc) {
+      __syncwarp();  // tcgen05.ld is warp-collective: reconverge after the previous chunk's stores
+      uint32_t r[32];
+      sm100::tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(32 * w) << 16) + static_cast<uint32_t>(32 * cc), r);
+      sm100::tmem_ld_wait();
+      if (!act) continue;
+      float v[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]);
+      if (i == 0) {  // d(bot) = dZ_0 + dOut[:, :D], masked by the bottom MLP's ReLU (bot = tile row 32*w)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int c = 4 * cc + q;  // 16-byte chunk of the row
+          const uint4 zb = *reinterpret_cast<const uint4*>(ztile + (c >> 3) * kItAtom + (32 * w) * 128 +
+                                                           (((c & 7) ^ 0) << 4));
+          const uint4 gd = reinterpret_cast<const uint4*>(drow)[c];
+          const __nv_bfloat16* zbh = reinterpret_cast<const __nv_bfloat16*>(&zb);
+          const __nv_bfloat16* gdh = reinterpret_cast<const __nv_bfloat16*>(&gd);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            float x = v[8 * q + e] + __bfloat162float(gdh[e]);
+            if (p.relu_mask_bot && __bfloat162float(zbh[e]) <= 0.f) x = 0.f;
+            v[8 * q + e] = x;
+          }
+        }
+      }
+      uint4* o = reinterpret_cast<uint4*>(dst + 32 * cc);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t wd[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          __nv_bfloat162 hv = __floats2bfloat162_rn(v[8 * q + 2 * t], v[8 * q + 2 * t + 1]);
+          wd[t] = *reinterpret_cast<uint32_t*>(&hv);
+        }
+        o[q] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+      }
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+  }
+  sm100::tc_fence_after();
+  if (w == 0) sm100::tmem_dealloc(tmem, static_cast<uint32_t>(p.D));
 }
 
 // --------------------------- fused head + BCE ------------------------------
@@ -480,12 +753,43 @@ int grid_for(int64_t n, int threads) {
   return static_cast<int>(want < 1 ? 1 : (want > cap ? cap : want));
 }
 
+// CTAs of an interaction kernel that share an SM: shared memory (with the per-block reservation),
+// capped by the TMEM columns (`tmem_cap` CTAs); the grid is this many per SM, so every CTA is resident
+int it_ctas_per_sm(size_t smem, int tmem_cap) {
+  static int sm_bytes = -1, reserved = 0;
+  if (sm_bytes < 0) {
+    int dev = 0;
+    FLARE_CUDA_CHECK(cudaGetDevice(&dev));
+    FLARE_CUDA_CHECK(cudaDeviceGetAttribute(&sm_bytes, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev));
+    FLARE_CUDA_CHECK(cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev));
+  }
+  const int by_smem = static_cast<int>(static_cast<size_t>(sm_bytes) / (smem + static_cast<size_t>(reserved)));
+  return std::max(1, std::min(by_smem, tmem_cap));
+}
+
 void interaction_forward(const InteractionParams& p, cudaStream_t s) {
   FLARE_CHECK(p.D % 64 == 0 && p.D <= 256, "interaction width must be a multiple of 64 and <= 256");
   const int T = p.F + 1;
   FLARE_CHECK(p.out_ld >= p.D + T * (T - 1) / 2, "interaction output too narrow");
   const int TP = (T + 2) / 3 * 3;
   FLARE_CHECK(p.out_ld % 8 == 0 && T <= 33, "interaction: out_ld must be a multiple of 8 and F <= 32");
+  if (p.B <= 0) return;
+  if (T <= 32) {
+    // at least 56 KB per CTA: at most 4 CTAs (4 x 128 TMEM columns) share an SM
+    const size_t tc_smem = std::max<size_t>(
+        1024 + static_cast<size_t>(p.D / 64) * kItAtom + 4 * static_cast<size_t>(p.out_ld + 8) * 2 + 64, 57344);
+    FLARE_CUDA_CHECK(cudaFuncSetAttribute(interaction_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(tc_smem)));
+    // shared memory is what limits residency: ask for the full carveout, or the occupancy query (and
+    // the launch) assume the default L1 / shared split and allow one CTA per SM
+    FLARE_CUDA_CHECK(cudaFuncSetAttribute(interaction_fwd_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                          cudaSharedmemCarveoutMaxShared));
+    const int grid = std::min(ceil_div(p.B, 4), device_sm_count() * it_ctas_per_sm(tc_smem, 4));
+    interaction_fwd_tc_kernel<<<grid, kItThreads, tc_smem, s>>>(p);
+    FLARE_CUDA_CHECK(cudaGetLastError());
+    count_launch();
+    return;
+  }
   const size_t smem = static_cast<size_t>(kInterWarps) * (TP * (p.D / 2 + 1) + (p.out_ld + 1) / 2 + 4) * 4;
   FLARE_CUDA_CHECK(cudaFuncSetAttribute(interaction_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(smem)));
@@ -510,6 +814,25 @@ void interaction_bwd_launch(const InteractionParams& p, cudaStream_t s) {
 void interaction_backward(const InteractionParams& p, cudaStream_t s) {
   FLARE_CHECK(p.D % 64 == 0 && p.D <= 256, "interaction width must be a multiple of 64 and <= 256");
   FLARE_CHECK(p.F + 1 <= 33, "interaction supports up to 32 embedded features");
+  const int T = p.F + 1;
+  FLARE_CHECK(p.out_ld % 8 == 0 && p.out_ld >= p.D + T * (T - 1) / 2, "interaction gradient too narrow");
+  if (p.B <= 0) return;
+  if (T <= 32) {
+    // Z + S + dDot rows: 2 (D = 256) to 4 (D = 64) CTAs per SM, each with D TMEM columns (<= 512 in all)
+    const size_t dpitch = static_cast<size_t>(p.D + (T * (T - 1) / 2 + 7) / 8 * 8 + 8);
+    FLARE_CHECK(p.D + (T * (T - 1) / 2 + 7) / 8 * 8 <= 4 * 32 * 8, "interaction: dOut row staging too long");
+    const size_t tc_smem =
+        1024 + static_cast<size_t>(p.D / 64 + 2) * kItAtom + 4 * dpitch * 2 + 64;
+    FLARE_CUDA_CHECK(cudaFuncSetAttribute(interaction_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(tc_smem)));
+    FLARE_CUDA_CHECK(cudaFuncSetAttribute(interaction_bwd_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                          cudaSharedmemCarveoutMaxShared));
+    const int grid = std::min(ceil_div(p.B, 4), device_sm_count() * it_ctas_per_sm(tc_smem, 512 / p.D));
+    interaction_bwd_tc_kernel<<<grid, kItThreads, tc_smem, s>>>(p);
+    FLARE_CUDA_CHECK(cudaGetLastError());
+    count_launch();
+    return;
+  }
   if (p.D == 64) interaction_bwd_launch<2>(p, s);
   else if (p.D == 128) interaction_bwd_launch<4>(p, s);
   else interaction_bwd_launch<8>(p, s);

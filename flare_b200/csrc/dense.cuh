@@ -19,6 +19,7 @@ struct InteractionParams {
   __nv_bfloat16* demb;
   int64_t demb_ld;
   int relu_mask_bot;  // apply ReLU-backward using bot > 0
+  int* status;        // device status word for the bounded tcgen05 waits (may be null)
 };
 
 struct HeadBceParams {

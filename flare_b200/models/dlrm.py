@@ -40,6 +40,7 @@ from dataclasses import dataclass, field, replace
 import torch
 import torch.nn as nn
 
+from .._native import DeviceStatus
 from ..ops.dense import cast_pad_bf16, head_bce, interaction_backward, interaction_forward, interaction_out_width
 from ..parallel.symm import SymmetricHeap
 from ..sparse.collection import ShardedEmbeddingBagCollection
@@ -161,6 +162,7 @@ class DLRM:
         self.dh = torch.empty(self.B, H, **bf)
         self.logits = torch.zeros(self.B, cfg.num_targets, dtype=torch.float32, device=dev)
         self.loss_sum = torch.zeros(1, dtype=torch.float32, device=dev)
+        self.inter_status = DeviceStatus(dev)  # bounded tensor-core waits of the interaction kernels
 
     # ------------------------------------------------------------------ data
     def set_batch(self, dense: torch.Tensor, labels: torch.Tensor, offsets: torch.Tensor, values: torch.Tensor,
@@ -175,13 +177,14 @@ class DLRM:
         cast_pad_bf16(self.dense_in, self.xd)
         bot = self.bottom.forward(self.xd)
         pooled = self.emb.forward()
-        interaction_forward(bot, pooled, self.F, self.inter)
+        interaction_forward(bot, pooled, self.F, self.inter, self.inter_status)
         h = self.top.forward(self.inter)
         self.loss_sum.zero_()
         head_bce(h, self.head_w, self.head_b, self.labels, grad_scale=1.0 / self.global_B, logits=self.logits,
                  loss_sum=self.loss_sum, dh=self.dh, dw=self.head_dw, db=self.head_db)
         dinter = self.top.backward(self.dh, need_input_grad=True)
-        interaction_backward(dinter, bot, pooled, self.F, self.dbot, self.emb.grad_input, relu_mask_bot=True)
+        interaction_backward(dinter, bot, pooled, self.F, self.dbot, self.emb.grad_input, relu_mask_bot=True,
+                             status=self.inter_status)
         self.bottom.backward(self.dbot, need_input_grad=False)
         return self.loss_sum
 
@@ -190,7 +193,7 @@ class DLRM:
         st: dict = {}
 
         def inter_fwd():
-            interaction_forward(st["bot"], st["pooled"], self.F, self.inter)
+            interaction_forward(st["bot"], st["pooled"], self.F, self.inter, self.inter_status)
 
         def head():
             self.loss_sum.zero_()
@@ -199,7 +202,7 @@ class DLRM:
 
         def inter_bwd():
             interaction_backward(st["dinter"], st["bot"], st["pooled"], self.F, self.dbot, self.emb.grad_input,
-                                 relu_mask_bot=True)
+                                 relu_mask_bot=True, status=self.inter_status)
 
         ops = [
             ("cast_dense", lambda: cast_pad_bf16(self.dense_in, self.xd)),
@@ -247,14 +250,14 @@ class DLRM:
             if pend is not None:
                 self.emb.backward(slot=pend)  # the previous step's sparse update, beside this step's dense work
         main.wait_event(self._ev_fwd)
-        interaction_forward(bot, pooled, self.F, self.inter)
+        interaction_forward(bot, pooled, self.F, self.inter, self.inter_status)
         h = self.top.forward(self.inter)
         self.loss_sum.zero_()
         head_bce(h, self.head_w, self.head_b, self.labels, grad_scale=1.0 / self.global_B, logits=self.logits,
                  loss_sum=self.loss_sum, dh=self.dh, dw=self.head_dw, db=self.head_db)
         dinter = self.top.backward(self.dh, need_input_grad=True)
         interaction_backward(dinter, bot, pooled, self.F, self.dbot, self.emb.grad_ins[slot].local,
-                             relu_mask_bot=True)
+                             relu_mask_bot=True, status=self.inter_status)
         self.bottom.backward(self.dbot, need_input_grad=False)
         self._ev_bwd.record(main)
         with torch.cuda.stream(comm):
@@ -303,13 +306,14 @@ class DLRM:
         cast_pad_bf16(self.dense_in, self.xd)
         bot = self.bottom.forward(self.xd)
         pooled = self.emb.forward(training=False)
-        interaction_forward(bot, pooled, self.F, self.inter)
+        interaction_forward(bot, pooled, self.F, self.inter, self.inter_status)
         h = self.top.forward(self.inter)
         x = h.float() @ self.head_w.float().t() + self.head_b.float()
         return torch.sigmoid(x)
 
     def check(self) -> None:
         self.emb.check()
+        self.inter_status.check("dot interaction")
         if self.dense.status is not None:
             self.dense.status.check("dense optimizer")
 

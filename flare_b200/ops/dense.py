@@ -27,8 +27,12 @@ def interaction_out_width(num_features: int, dim: int, pad_to: int = 16) -> int:
     return (w + pad_to - 1) // pad_to * pad_to
 
 
-def interaction_forward(bot: torch.Tensor, emb: torch.Tensor, num_features: int, out: torch.Tensor) -> torch.Tensor:
-    """out[b] = [bot[b], <z_i, z_j> for i > j, zeros]  with z = [bot, emb_0..emb_{F-1}]."""
+def interaction_forward(bot: torch.Tensor, emb: torch.Tensor, num_features: int, out: torch.Tensor,
+                        status=None) -> torch.Tensor:
+    """out[b] = [bot[b], <z_i, z_j> for i > j, zeros]  with z = [bot, emb_0..emb_{F-1}].
+
+    On the GPU (up to 31 embedded features) four samples share one 128-row tcgen05 tile; ``status``
+    (a ``DeviceStatus``) receives a timed-out tensor-core wait."""
     B, D = bot.shape
     if not on_cuda(bot, emb, out):
         z = torch.cat([bot.float().unsqueeze(1), emb.float().reshape(B, num_features, D)], dim=1)
@@ -42,7 +46,8 @@ def interaction_forward(bot: torch.Tensor, emb: torch.Tensor, num_features: int,
         return out
     native().interaction_forward(
         dict(B=B, F=num_features, D=D, bot=bot.data_ptr(), bot_ld=bot.stride(0), emb=emb.data_ptr(),
-             emb_ld=emb.stride(0), out=out.data_ptr(), out_ld=out.stride(0))
+             emb_ld=emb.stride(0), out=out.data_ptr(), out_ld=out.stride(0),
+             status=status.ptr if status is not None else 0)
     )
     return out
 
@@ -55,6 +60,7 @@ def interaction_backward(
     dbot: torch.Tensor,
     demb: torch.Tensor,
     relu_mask_bot: bool = True,
+    status=None,
 ) -> None:
     B, D = bot.shape
     if not on_cuda(dout, bot, emb, dbot, demb):
@@ -76,7 +82,7 @@ def interaction_backward(
         dict(B=B, F=num_features, D=D, bot=bot.data_ptr(), bot_ld=bot.stride(0), emb=emb.data_ptr(),
              emb_ld=emb.stride(0), dout=dout.data_ptr(), out_ld=dout.stride(0), dbot=dbot.data_ptr(),
              dbot_ld=dbot.stride(0), demb=demb.data_ptr(), demb_ld=demb.stride(0),
-             relu_mask_bot=1 if relu_mask_bot else 0)
+             relu_mask_bot=1 if relu_mask_bot else 0, status=status.ptr if status is not None else 0)
     )
 
 

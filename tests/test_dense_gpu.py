@@ -8,7 +8,7 @@ from flare_b200.training.flat import adam_reference
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("B,F,dim", [(64, 26, 128), (37, 4, 64), (16, 8, 256)])
+@pytest.mark.parametrize("B,F,dim", [(64, 26, 128), (37, 4, 64), (16, 8, 256), (1001, 31, 128), (9, 32, 64)])
 def test_interaction_fwd_bwd(cuda, B, F, dim):
     torch.manual_seed(0)
     W = D.interaction_out_width(F, dim)
