@@ -5,7 +5,9 @@ Same constructor contracts and semantics as the reference's layer library
 (side-information tables grouped by dim, sum/mean pooling with id 0 as null,
 fp32 tables); the multitask gates ``PLE`` / ``CGC`` / ``UPLE`` / ``UCGC``;
 ``TokenMix``; ``BatchedExpertMoE`` (dense or top-k soft gating, SwiGLU
-experts, RMS-normalised residual); ``NamedTokens``; fp32 numerics helpers.
+experts, RMS-normalised residual); the multi-head MoE token mixers
+``TokenMixLargeMoe`` / ``TokenMixLargePreGateNoPool``; ``NamedTokens``; fp32
+numerics helpers.
 
 ``TcLinear`` is a linear layer whose forward and backward GEMMs run on the
 hand-written tcgen05 kernel when the input is a bf16 CUDA tensor (weight
@@ -308,6 +310,110 @@ class BatchedExpertMoE(nn.Module):
         return moe
 
 
+class RMSNorm(nn.Module):
+    """RMS normalisation over the last dim in fp32 with a learnable scale (eps 1e-6)."""
+
+    def __init__(self, dim: int, eps: float = 1e-6):
+        super().__init__()
+        self.eps = eps
+        self.scale = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return (fp32_rms_normalize(x, -1, self.eps) * self.scale.float()).to(x.dtype)
+
+
+def _head_major(x: torch.Tensor, heads: int) -> torch.Tensor:
+    """[B, T, D] -> [heads, B, T * D / heads]: every head sees its slice of every token."""
+    B, T, D = x.shape
+    return x.reshape(B, T, heads, D // heads).permute(2, 0, 1, 3).reshape(heads, B, T * (D // heads))
+
+
+def _token_major(y: torch.Tensor, tokens: int) -> torch.Tensor:
+    """[heads, B, T * hd] -> [T, B, heads * hd]: back to one row per token (heads concatenated)."""
+    H, B, _ = y.shape
+    return y.reshape(H, B, tokens, -1).permute(2, 1, 0, 3).reshape(tokens, B, -1)
+
+
+class TokenMixLargeMoe(nn.Module):
+    """Multi-head token mixing with MoE feed-forwards, mean-pooled over tokens.
+
+    Each of ``layer_num`` layers runs a ``BatchedExpertMoE`` over heads (one expert bank per head,
+    input = that head's slice of all tokens) and then one over tokens (one bank per token, input =
+    the token's heads concatenated).  Input [B, token_num, token_dim]; output [B, token_dim].
+    Reference behaviour: src/flare/jax/layers/token_mix.py:147-223.
+    """
+
+    def __init__(self, layer_num: int, token_num: int, token_dim: int, head_num: int = 12, scale_size: int = 4,
+                 num_experts: int = 1, sparse: bool = False, top_k: int = 2):
+        super().__init__()
+        if token_dim % head_num:
+            raise ValueError(f"token_dim {token_dim} must be divisible by head_num {head_num}")
+        self.layer_num, self.token_num, self.token_dim, self.head_num = layer_num, token_num, token_dim, head_num
+        self.head_dim = token_dim // head_num
+        k = min(top_k, num_experts)
+        self.head_moe = nn.ModuleList(BatchedExpertMoE(head_num, token_num * self.head_dim, scale_size, num_experts,
+                                                       sparse, k) for _ in range(layer_num))
+        self.token_moe = nn.ModuleList(BatchedExpertMoE(token_num, token_dim, scale_size, num_experts, sparse, k)
+                                       for _ in range(layer_num))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        for i in range(self.layer_num):
+            y = self.head_moe[i](_head_major(x, self.head_num))
+            x = self.token_moe[i](_token_major(y, self.token_num)).transpose(0, 1)
+        return fp32_mean(x, dim=1)
+
+
+class TokenMixLargePreGateNoPool(nn.Module):
+    """``TokenMixLargeMoe`` with per-layer input gates, pre-norm residual MoE blocks and no pooling.
+
+    ``forward(x, pre_layer_gates)``: before layer i the tokens are scaled by
+    ``pre_layer_gates[:, i*D:(i+1)*D]`` (one gate vector per sample, shared by the tokens); each MoE
+    block is ``y = y + MoE(RMSNorm(y))``; layers listed in ``residual_layers`` (with
+    ``residual_enabled``) also normalise their input and add it back after the layer.  Output
+    [B, token_num, token_dim].  Reference behaviour: src/flare/jax/layers/token_mix.py:226-335.
+    """
+
+    def __init__(self, layer_num: int, token_num: int, token_dim: int, head_num: int = 12, scale_size: int = 4,
+                 num_experts: int = 1, sparse: bool = False, top_k: int = 2, residual_enabled: bool = False,
+                 residual_layers: Sequence[int] = ()):
+        super().__init__()
+        if token_dim % head_num:
+            raise ValueError(f"token_dim {token_dim} must be divisible by head_num {head_num}")
+        for li in residual_layers:
+            if not 0 <= li < layer_num:
+                raise ValueError(f"residual layer index {li} is outside [0, {layer_num})")
+        self.layer_num, self.token_num, self.token_dim, self.head_num = layer_num, token_num, token_dim, head_num
+        self.head_dim = token_dim // head_num
+        self.residual_enabled, self.residual_layers = residual_enabled, frozenset(residual_layers)
+        k = min(top_k, num_experts)
+        hw = token_num * self.head_dim
+        self.head_moe = nn.ModuleList(BatchedExpertMoE(head_num, hw, scale_size, num_experts, sparse, k,
+                                                       residual_norm=False) for _ in range(layer_num))
+        self.token_moe = nn.ModuleList(BatchedExpertMoE(token_num, token_dim, scale_size, num_experts, sparse, k,
+                                                        residual_norm=False) for _ in range(layer_num))
+        self.head_norms = nn.ModuleList(RMSNorm(hw) for _ in range(layer_num))
+        self.token_norms = nn.ModuleList(RMSNorm(token_dim) for _ in range(layer_num))
+        self.block_norms = nn.ModuleDict({str(i): RMSNorm(token_dim) for i in sorted(self.residual_layers)})
+
+    def forward(self, x: torch.Tensor, pre_layer_gates: torch.Tensor | None = None) -> torch.Tensor:
+        D = self.token_dim
+        for i in range(self.layer_num):
+            if pre_layer_gates is not None:
+                x = x * pre_layer_gates[:, i * D:(i + 1) * D].unsqueeze(1)
+            block_in = x
+            res = self.residual_enabled and i in self.residual_layers
+            if res:
+                x = self.block_norms[str(i)](x)
+            y = _head_major(x, self.head_num)
+            y = y + self.head_moe[i](self.head_norms[i](y))
+            t = _token_major(y, self.token_num)
+            t = t + self.token_moe[i](self.token_norms[i](t))
+            x = t.transpose(0, 1)
+            if res:
+                x = x + block_in
+        return x
+
+
 class NamedTokens:
     """Ordered name -> token index registry for token-mixing models."""
 
@@ -324,5 +430,6 @@ class NamedTokens:
         return tokens[:, [self.index[n] for n in names]]
 
 
-__all__ = ["BatchedExpertMoE", "CGC", "CategoricalEmbedding", "MLP", "NamedTokens", "PLE", "TcLinear", "TokenMix",
-           "UCGC", "UPLE", "fp32_mean", "fp32_rms_normalize", "fp32_softmax", "fp32_sum", "get_activation"]
+__all__ = ["BatchedExpertMoE", "CGC", "CategoricalEmbedding", "MLP", "NamedTokens", "PLE", "RMSNorm", "TcLinear",
+           "TokenMix", "TokenMixLargeMoe", "TokenMixLargePreGateNoPool", "UCGC", "UPLE", "fp32_mean",
+           "fp32_rms_normalize", "fp32_softmax", "fp32_sum", "get_activation"]
