@@ -16,6 +16,12 @@ collectives (src/flare/jax/training/zero/collectives.py:14-95):
   steps and all-gathers it before each micro-step;
 * gradients travel in the precision policy's transport dtype (bf16 under
   mixed precision) and are averaged over the world size;
+* ``shard_scope="node"`` shards the optimizer state (and, for ZeRO-2/3, the
+  gradients and parameters) over the ranks of one node only: gradients are
+  all-reduced over every rank and each rank keeps its node-local slice, and
+  parameter shards are all-gathered inside the node (the node scope of
+  src/flare/jax/training/zero/collectives.py:33-36), so the inter-node
+  traffic is one all-reduce and the shards replicate across nodes;
 * sharded optimizers must be elementwise (no global-norm clipping), the
   shard-update capability rule of
   src/flare/jax/training/optimizers/base.py:70-150;
@@ -29,6 +35,7 @@ This engine serves generic models, the CPU configuration and tests.
 from __future__ import annotations
 
 import hashlib
+import os
 from collections.abc import Callable, Mapping
 from dataclasses import dataclass
 from typing import Any
@@ -55,7 +62,7 @@ class TrainEngine:
     def __init__(self, model: nn.Module, loss_fn: Callable[[Any, Any], torch.Tensor], plan: TrainingExecutionPlan,
                  optimizer: DenseOptimizerConfig, *, precision: PrecisionPolicy = PrecisionPolicy.FP32,
                  process_group: dist.ProcessGroup | None = None, device: torch.device | None = None,
-                 forward: Callable[[nn.Module, Any], Any] | None = None):
+                 forward: Callable[[nn.Module, Any], Any] | None = None, node_size: int | None = None):
         self.model = model
         self.loss_fn = loss_fn
         self.plan = plan
@@ -69,6 +76,20 @@ class TrainEngine:
         self.stage = plan.zero.stage
         if self.world > 1 and self.stage is not ZeroStage.REPLICATED and not optimizer.shardable:
             raise ValueError("sharded optimizer updates require an elementwise optimizer without global-norm clip")
+        # shard group: every rank (global scope) or the ranks of this node (node scope)
+        self.node_scope = plan.zero.shard_scope == "node" and self.world > 1
+        self.shard_pg, q, shard_rank = self.pg, max(self.world, 1), self.rank
+        if self.node_scope:
+            ns = int(node_size or os.environ.get("LOCAL_WORLD_SIZE", self.world))
+            if ns < 1 or self.world % ns:
+                raise ValueError(f"node size {ns} does not divide the world size {self.world}")
+            base = dist.get_process_group_ranks(process_group) if process_group is not None else list(range(self.world))
+            for n in range(self.world // ns):  # every rank creates every node group, in the same order
+                g = dist.new_group(base[n * ns:(n + 1) * ns])
+                if n == self.rank // ns:
+                    self.shard_pg = g
+            q, shard_rank = ns, self.rank % ns
+        self.shards = q
         self.micro_steps = plan.accumulation.micro_steps
         self.micro_step = 0
         self.step = 0
@@ -79,10 +100,9 @@ class TrainEngine:
             self.offsets.append(off)
             off += p.numel()
         self.numel = off
-        q = max(self.world, 1)
         self.padded = (off + q - 1) // q * q
         self.shard = self.padded // q
-        self.lo, self.hi = self.rank * self.shard, (self.rank + 1) * self.shard
+        self.lo, self.hi = shard_rank * self.shard, (shard_rank + 1) * self.shard
         flat = torch.zeros(self.padded, dtype=torch.float32, device=self.device)
         with torch.no_grad():
             for p, o in zip(self.params, self.offsets):
@@ -120,6 +140,9 @@ class TrainEngine:
         if self.stage in (ZeroStage.REPLICATED, ZeroStage.OPTIMIZER_STATE):
             dist.all_reduce(wire, group=self.pg)
             return wire.float() / self.world
+        if self.node_scope:  # global sum, then this rank's node-local slice
+            dist.all_reduce(wire, group=self.pg)
+            return wire[self.lo:self.hi].float() / self.world
         out = torch.empty(self.shard, dtype=wire.dtype, device=self.device)
         dist.reduce_scatter_tensor(out, wire, group=self.pg)
         return out.float() / self.world
@@ -128,7 +151,7 @@ class TrainEngine:
         """ZeRO-3: all-gather the parameter shards before a micro-step."""
         if self.world > 1 and self.stage is ZeroStage.PARAMETER:
             full = torch.empty(self.padded, dtype=torch.float32, device=self.device)
-            dist.all_gather_into_tensor(full, self.master, group=self.pg)
+            dist.all_gather_into_tensor(full, self.master, group=self.shard_pg)
             self._scatter_params(full)
 
     # --------------------------------------------------------------- step
@@ -174,7 +197,7 @@ class TrainEngine:
         adam_reference(self.master, g, self.m, self.v, op)
         if self.world > 1 and self.stage is not ZeroStage.REPLICATED:
             full = torch.empty(self.padded, dtype=torch.float32, device=self.device)
-            dist.all_gather_into_tensor(full, self.master, group=self.pg)
+            dist.all_gather_into_tensor(full, self.master, group=self.shard_pg)
             self._scatter_params(full)
         else:
             self._scatter_params(self.master)
@@ -194,14 +217,14 @@ class TrainEngine:
         if self.world == 1 or self.stage is ZeroStage.REPLICATED:
             return self.master
         full = torch.empty(self.padded, dtype=torch.float32, device=self.device)
-        dist.all_gather_into_tensor(full, self.master, group=self.pg)
+        dist.all_gather_into_tensor(full, self.master, group=self.shard_pg)
         return full
 
     def _full(self, t: torch.Tensor) -> torch.Tensor:
         if self.world == 1 or self.stage is ZeroStage.REPLICATED:
             return t
         full = torch.empty(self.padded, dtype=torch.float32, device=self.device)
-        dist.all_gather_into_tensor(full, t, group=self.pg)
+        dist.all_gather_into_tensor(full, t, group=self.shard_pg)
         return full
 
     def _unflatten(self, flat: torch.Tensor) -> dict[str, torch.Tensor]:
@@ -210,7 +233,8 @@ class TrainEngine:
 
     def checkpoint_layout(self) -> Mapping[str, Any]:
         return {"leaves": [(n, tuple(p.shape), "float32") for n, p in zip(self.names, self.params)],
-                "schema_digest": self.schema_digest(), "zero_stage": int(self.stage), "world_size": self.world}
+                "schema_digest": self.schema_digest(), "zero_stage": int(self.stage), "world_size": self.world,
+                "shard_scope": "node" if self.node_scope else "global", "shards": self.shards}
 
     def schema_digest(self) -> str:
         h = hashlib.sha256()

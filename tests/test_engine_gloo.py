@@ -66,3 +66,27 @@ def _ckpt_roundtrip(rank, world):
 def test_checkpoint_roundtrip_sharded():
     diffs = run_ranks(_ckpt_roundtrip, 2)
     assert max(diffs) == 0.0
+
+
+def _train_node(rank, world, stage, sync_mode, steps=3, micro=2):
+    plan = TrainingExecutionPlan.sharded(ZeroStage(stage), micro_steps=micro, sync_mode=sync_mode, shard_scope="node")
+    eng = TrainEngine(_model(), lambda o, y: nn.functional.binary_cross_entropy_with_logits(o, y), plan,
+                      DenseOptimizerConfig(kind="adam", learning_rate=0.01), device=torch.device("cpu"), node_size=2)
+    assert eng.shards == 2 and eng.master.numel() == (eng.padded if stage == 0 else eng.padded // 2)
+    for s in range(steps):
+        for m in range(micro):
+            x, y = _data(s, m)
+            n = x.shape[0] // world
+            eng.micro_step_once(x[rank * n:(rank + 1) * n], y[rank * n:(rank + 1) * n])
+    st = eng.capture_checkpoint_state()
+    return {k: v.clone() for k, v in st["model_state"].items()}, st["step"], eng.checkpoint_layout()["shard_scope"]
+
+
+@pytest.mark.parametrize("stage", [1, 2, 3])
+def test_node_scope_zero_matches_single_rank(stage):
+    """4 ranks as 2 nodes x 2: shards live inside a node, gradients are summed over all 4 ranks."""
+    ref, ref_step = _train(0, 1, stage, "boundary")
+    for params, step, scope in run_ranks(_train_node, 4, stage, "boundary"):
+        assert step == ref_step == 3 and scope == "node"
+        for k in ref:
+            torch.testing.assert_close(params[k], ref[k], rtol=1e-5, atol=1e-6)
