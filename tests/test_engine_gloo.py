@@ -90,3 +90,19 @@ def test_node_scope_zero_matches_single_rank(stage):
         assert step == ref_step == 3 and scope == "node"
         for k in ref:
             torch.testing.assert_close(params[k], ref[k], rtol=1e-5, atol=1e-6)
+
+
+def _topology(rank, world, stage):
+    from flare_b200.benchmarks.zero_topology import run
+
+    return run(rank, world, stage=stage, node_size=2, steps=3, width=32, depth=2, batch=8)
+
+
+@pytest.mark.parametrize("stage", [2, 3])
+def test_zero_topology_benchmark_node_equals_global(stage):
+    out = run_ranks(_topology, 4, stage)[0]
+    assert out["max_param_diff_global_vs_node"] < 1e-6
+    g, n = out["scopes"]["global"], out["scopes"]["node"]
+    assert g["shards"] == 4 and n["shards"] == 2
+    assert n["intra_node_bytes"] > 0 and g["intra_node_bytes"] == 0
+    assert n["cross_node_bytes"] > 0 and g["ms_per_step"] > 0 and n["ms_per_step"] > 0
