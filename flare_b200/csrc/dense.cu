@@ -19,8 +19,6 @@
 namespace flare {
 namespace {
 
-constexpr unsigned kFull = 0xffffffffu;
-
 // ------------------------------- interaction -------------------------------
 // Vector index pairs (i > j) enumerated row by row: p = i*(i-1)/2 + j.
 __device__ __forceinline__ void pair_of(int p, int& i, int& j) {

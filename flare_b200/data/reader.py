@@ -130,6 +130,38 @@ class BatchReader:
         return audit
 
 
+def reconcile_reader_audits(audits: list[dict], planned_items: list[int] | None = None,
+                            planned_rows: int | None = None) -> dict:
+    """Check the readers' audits of one run against each other and against the plan.
+
+    Every planned item must be consumed by exactly one rank (``done`` of its
+    audit), no rank may report an item outside the plan, and the rows the
+    ranks read must add up to ``planned_rows`` when given.  Returns a report
+    with ``ok`` and the offending item ids.  Reference behaviour: the reader
+    audit reconciliation tool of tools/validation (reader execution audits
+    written at shutdown, src/flare/runtime/fluxway/workers/reader.py:455-477).
+    """
+    owner: dict[int, list[int]] = {}
+    for a in audits:
+        for item in a.get("done", []):
+            owner.setdefault(int(item), []).append(int(a.get("rank", -1)))
+    duplicated = sorted(i for i, rs in owner.items() if len(rs) > 1)
+    planned = set(planned_items) if planned_items is not None else None
+    missing = sorted(planned - owner.keys()) if planned is not None else []
+    unexpected = sorted(owner.keys() - planned) if planned is not None else []
+    rows = sum(int(a.get("rows", 0)) for a in audits)
+    errors = sum(int(a.get("errors", 0)) for a in audits)
+    rows_ok = planned_rows is None or rows == planned_rows
+    ranks = sorted(int(a.get("rank", -1)) for a in audits)
+    worlds = {int(a.get("world", len(audits))) for a in audits}
+    ranks_ok = len(worlds) == 1 and ranks == list(range(worlds.pop()))
+    return {"ok": not duplicated and not missing and not unexpected and rows_ok and ranks_ok and errors == 0,
+            "items_consumed": len(owner), "duplicated": duplicated, "missing": missing, "unexpected": unexpected,
+            "rows": rows, "planned_rows": planned_rows, "errors": errors, "ranks": ranks, "ranks_complete": ranks_ok,
+            "padded_rows": sum(int(a.get("padded_rows", 0)) for a in audits),
+            "seconds_max": max((float(a.get("seconds", 0.0)) for a in audits), default=0.0)}
+
+
 def global_valid_count(valid: int, *, expected: int | None = None) -> int:
     """Valid samples of this step summed over the ranks (int32 all-reduce); checked against ``expected``."""
     import torch
@@ -146,4 +178,24 @@ def global_valid_count(valid: int, *, expected: int | None = None) -> int:
     return total
 
 
-__all__ = ["BatchReader", "global_valid_count"]
+def main(argv=None) -> int:
+    """``python -m flare_b200.data.reader AUDIT.json... [--items N] [--rows R]``: reconcile audits (exit 1 if not ok)."""
+    import argparse
+    import json
+
+    p = argparse.ArgumentParser(prog="flare_b200.data.reader")
+    p.add_argument("audits", nargs="+")
+    p.add_argument("--items", type=int, default=None, help="planned item count (ids 0..N-1)")
+    p.add_argument("--rows", type=int, default=None, help="planned row count")
+    args = p.parse_args(argv)
+    audits = [json.loads(Path(f).read_text()) for f in args.audits]
+    rep = reconcile_reader_audits(audits, list(range(args.items)) if args.items is not None else None, args.rows)
+    print(json.dumps(rep, indent=1))
+    return 0 if rep["ok"] else 1
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
+
+
+__all__ = ["BatchReader", "global_valid_count", "reconcile_reader_audits"]

@@ -73,3 +73,23 @@ def test_cut_position_inside_an_item(tmp_path):
     rd2.restore_state([st])
     rest = _ids(list(rd2))
     assert sorted(got + rest) == sorted(x for f in range(2) for x in range(f * 1000, f * 1000 + 100))
+
+
+def test_reconcile_reader_audits(tmp_path):
+    from flare_b200.data.reader import main, reconcile_reader_audits
+
+    fac = ParquetSourceFactory(_files(tmp_path))
+    audits = []
+    for r in range(3):
+        rd = BatchReader(fac, 16, rank=r, world=3, audit_path=tmp_path / f"a{r}.json")
+        list(rd)
+        audits.append(rd.close())
+    items = [it.item_id for it in fac.plan()]
+    rep = reconcile_reader_audits(audits, items, planned_rows=300)
+    assert rep["ok"] and rep["items_consumed"] == 12 and rep["rows"] == 300
+    bad = [dict(audits[0]), audits[1]]  # rank 2's audit lost, rank 0 also claims one of rank 1's items
+    bad[0]["done"] = bad[0]["done"] + [audits[1]["done"][0]]
+    rep = reconcile_reader_audits(bad, items, planned_rows=300)
+    assert not rep["ok"] and rep["duplicated"] == [audits[1]["done"][0]]
+    assert rep["missing"] == sorted(audits[2]["done"]) and not rep["ranks_complete"]
+    assert main([str(tmp_path / f"a{r}.json") for r in range(3)] + ["--items", "12", "--rows", "300"]) == 0
