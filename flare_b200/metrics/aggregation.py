@@ -11,6 +11,7 @@ recipes/recsys/ranking/metrics/sink.py:7-29).
 """
 from __future__ import annotations
 
+import collections
 import json
 import math
 import time
@@ -86,10 +87,17 @@ class TensorBoardSink:
 class TrainMetricsWindow:
     def __init__(self, targets: tuple[str, ...] = ("ctr",), window_steps: int = 100, capacity: int = 1 << 22,
                  device: torch.device | None = None, sinks: list | None = None, negative_factor: float = 0.0,
-                 distributed: bool | None = None, group=None):
+                 distributed: bool | None = None, group=None, background: bool = False, max_pending: int = 2):
         """``distributed``: merge every rank's window into one exact AUC / GAUC / calibration / loss /
         throughput (default: when a process group of more than one rank is up).  Every rank must then
-        call ``update`` for the same steps, since the flush is a collective."""
+        call ``update`` for the same steps, since the flush is a collective.
+
+        ``background`` (rank-local windows): a finished window is copied on the device and its metrics
+        are computed by one worker thread while training goes on; at most ``max_pending`` windows wait
+        (the next flush blocks on the oldest, so a slow metric slows training instead of queueing
+        without bound).  Results reach the sinks in window order and ``completed``; ``drain()`` waits
+        for all of them.  Reference behaviour: bounded background pending windows of the train
+        metrics aggregator (recipes/recsys/ranking/metrics/train_metrics.py:127-326)."""
         self.targets = targets
         self.group = group
         self.distributed = distributed
@@ -105,6 +113,11 @@ class TrainMetricsWindow:
         self.window = MetricWindow()
         self.sinks = sinks or []
         self.negative_factor = negative_factor
+        self.total_steps = 0
+        self.background, self.max_pending = bool(background), max(1, int(max_pending))
+        self._pool = None
+        self._pending: collections.deque = collections.deque()
+        self.completed: list[dict] = []
 
     def update(self, logits: torch.Tensor, labels: torch.Tensor, *, loss_sum: torch.Tensor | float | None = None,
                groups: torch.Tensor | None = None, valid_count: int | None = None) -> dict | None:
@@ -120,6 +133,7 @@ class TrainMetricsWindow:
         if loss_sum is not None:
             self.loss_sum += loss_sum if not torch.is_tensor(loss_sum) else loss_sum.to(self.loss_sum.device).double().reshape(())
         self.window.add(B)
+        self.total_steps += 1
         if self.window.steps >= self.window_steps:
             return self.flush()
         return None
@@ -131,7 +145,8 @@ class TrainMetricsWindow:
 
         return dist.is_available() and dist.is_initialized() and dist.get_world_size(self.group) > 1
 
-    def flush(self) -> dict:
+    def flush(self) -> dict | None:
+        """End the window: its metrics (None when a background worker computes them)."""
         out: dict[str, float] = {}
         n = self.n
         if self._is_distributed():
@@ -150,25 +165,74 @@ class TrainMetricsWindow:
             slowest = _max_scalar(elapsed, self.group, self.loss_sum.device)
             out["train/loss"] = loss / max(samples, 1.0)
             out["train/throughput_samples"] = samples / max(slowest, 1e-9)
+        elif self.background:
+            snap = (self.scores[:n].clone(), self.labels[:n].clone(),
+                    self.groups[:n].clone() if self.has_groups else None, self.loss_sum.clone(),
+                    self.window.trained_sample_count, self.window.throughput_samples(), self.total_steps)
+            ev = None
+            if self.device.type == "cuda":
+                ev = torch.cuda.Event()
+                ev.record()
+            while len(self._pending) >= self.max_pending:
+                self._pending.popleft().result()
+            if self._pool is None:
+                from concurrent.futures import ThreadPoolExecutor
+
+                self._pool = ThreadPoolExecutor(max_workers=1, thread_name_prefix="metrics-window")
+            self._pending.append(self._pool.submit(self._background_window, snap, ev))
+            self._reset()
+            return None
         else:
-            if n:
-                for t, name in enumerate(self.targets):
-                    s, y = self.scores[:n, t], self.labels[:n, t]
-                    out[f"train/auc_{name}"] = auc(s, y)
-                    out[f"train/calibration_{name}"] = calibration(s, y)
-                    if self.has_groups:
-                        out[f"train/gauc_{name}"] = gauc(s, y, self.groups[:n], self.negative_factor)
-            samples = max(self.window.trained_sample_count, 1)
-            out["train/loss"] = float(self.loss_sum) / samples
-            out["train/throughput_samples"] = self.window.throughput_samples()
-        step = self.window.steps
+            out = self._local_metrics(self.scores[:n], self.labels[:n], self.groups[:n] if self.has_groups else None,
+                                      float(self.loss_sum), self.window.trained_sample_count,
+                                      self.window.throughput_samples())
+        self._emit(self.total_steps, out)
+        self._reset()
+        return out
+
+    def _local_metrics(self, scores, labels, groups, loss_sum: float, samples: int, throughput: float) -> dict:
+        out: dict[str, float] = {}
+        if scores.shape[0]:
+            for t, name in enumerate(self.targets):
+                s, y = scores[:, t], labels[:, t]
+                out[f"train/auc_{name}"] = auc(s, y)
+                out[f"train/calibration_{name}"] = calibration(s, y)
+                if groups is not None:
+                    out[f"train/gauc_{name}"] = gauc(s, y, groups, self.negative_factor)
+        out["train/loss"] = loss_sum / max(samples, 1)
+        out["train/throughput_samples"] = throughput
+        return out
+
+    def _background_window(self, snap, ev) -> dict:
+        scores, labels, groups, loss, samples, throughput, step = snap
+        if ev is not None:
+            ev.synchronize()  # the copies were queued on the training stream
+        out = self._local_metrics(scores, labels, groups, float(loss), samples, throughput)
+        self._emit(step, out)
+        self.completed.append(out)
+        return out
+
+    def _emit(self, step: int, out: dict) -> None:
         for sink in self.sinks:
             sink.write(step, {k: v for k, v in out.items() if not (isinstance(v, float) and math.isnan(v))})
+
+    def _reset(self) -> None:
         self.n = 0
         self.has_groups = False
         self.loss_sum.zero_()
         self.window = MetricWindow()
-        return out
+
+    def drain(self) -> list[dict]:
+        """Wait for every background window; returns all completed window results (in order)."""
+        while self._pending:
+            self._pending.popleft().result()
+        return list(self.completed)
+
+    def close(self) -> None:
+        self.drain()
+        if self._pool is not None:
+            self._pool.shutdown(wait=True)
+            self._pool = None
 
 
 __all__ = ["ConsoleSink", "JsonlSink", "MetricSink", "MetricWindow", "TensorBoardSink", "TrainMetricsWindow"]

@@ -111,3 +111,35 @@ def test_distributed_metrics_over_gloo_ranks():
         assert abs(out["train/auc_ctr"] - ref_window_auc) < 1e-5  # sigmoid of a slice may differ by an ulp
         assert abs(out["train/loss"] - 1.5) < 1e-12  # (1 * 1200 + 2 * 1200) / 2400
     assert outs[0][1]["train/auc_ctr"] == outs[1][1]["train/auc_ctr"]
+
+
+class _ListSink:
+    def __init__(self):
+        self.rows = []
+
+    def write(self, step, metrics):
+        self.rows.append((step, metrics))
+
+
+def test_background_windows_match_synchronous_and_stay_bounded():
+    from flare_b200.metrics.aggregation import TrainMetricsWindow
+
+    g = torch.Generator().manual_seed(5)
+    steps = [((torch.rand(64, 1, generator=g) < 0.3).float(), torch.randn(64, 1, generator=g)) for _ in range(9)]
+    sync_sink, bg_sink = _ListSink(), _ListSink()
+    sync = TrainMetricsWindow(window_steps=3, capacity=256, sinks=[sync_sink])
+    bg = TrainMetricsWindow(window_steps=3, capacity=256, sinks=[bg_sink], background=True, max_pending=1)
+    sync_out = []
+    for y, noise in steps:
+        logits = (y * 2 - 1) + noise
+        r = sync.update(logits, y, loss_sum=64 * 0.25)
+        if r is not None:
+            sync_out.append(r)
+        assert bg.update(logits, y, loss_sum=64 * 0.25) is None
+        assert len(bg._pending) <= 1
+    got = bg.drain()
+    bg.close()
+    assert len(got) == len(sync_out) == 3
+    for a, b in zip(got, sync_out):
+        assert a["train/auc_ctr"] == b["train/auc_ctr"] and a["train/loss"] == b["train/loss"]
+    assert [s for s, _ in bg_sink.rows] == [s for s, _ in sync_sink.rows] == [3, 6, 9]
