@@ -228,6 +228,52 @@ class DLRM:
         torch.cuda.synchronize(self.device)
         return [(name, e.elapsed_time(evs[i + 1][1] if i + 1 < len(evs) else end)) for i, (name, e) in enumerate(evs)]
 
+    def traced_step(self, tracer, step: int) -> torch.Tensor:
+        """One eager training step that records the semantic execution trace (opt-in diagnostics).
+
+        Emits one event per stage with the reference's stage names (input_unique, sparse_lookup,
+        module_gather, module_gradient, sparse_update, module_update, sparse_commit; reference:
+        recipes/recsys/ranking/metrics/execution_trace.py:75-380) carrying tensor summaries
+        (finite / NaN / Inf counts, range, mean) and counters, inside NVTX ranges of the same names.
+        Reading the summaries synchronises the device, so this is a diagnostics path, not the hot
+        one; ``flare_b200.utils.trace_audit`` replays the trace."""
+        nvtx = torch.cuda.nvtx
+        self.flush_pending_updates()
+        with nvtx.range("input_unique"):
+            offs = self.emb.in_offsets.local
+            nnz = int(offs[-1])
+            tracer.emit("input_unique", "step", step=step, ids=nnz, bags=int(offs.numel() - 1),
+                        values=self.emb.in_values.local[:nnz])
+        with nvtx.range("sparse_lookup"):
+            cast_pad_bf16(self.dense_in, self.xd)
+            bot = self.bottom.forward(self.xd)
+            pooled = self.emb.forward()
+            tracer.emit("sparse_lookup", "step", step=step, pooled=pooled)
+        with nvtx.range("module_gather"):
+            interaction_forward(bot, pooled, self.F, self.inter, self.inter_status)
+            tracer.emit("module_gather", "step", step=step, bottom=bot, interaction=self.inter)
+        with nvtx.range("module_gradient"):
+            h = self.top.forward(self.inter)
+            self.loss_sum.zero_()
+            head_bce(h, self.head_w, self.head_b, self.labels, grad_scale=1.0 / self.global_B, logits=self.logits,
+                     loss_sum=self.loss_sum, dh=self.dh, dw=self.head_dw, db=self.head_db)
+            dinter = self.top.backward(self.dh, need_input_grad=True)
+            interaction_backward(dinter, bot, pooled, self.F, self.dbot, self.emb.grad_input, relu_mask_bot=True,
+                                 status=self.inter_status)
+            self.bottom.backward(self.dbot, need_input_grad=False)
+            tracer.emit("module_gradient", "step", step=step, loss_sum=float(self.loss_sum), logits=self.logits,
+                        dense_grad=self.dense.grad, sparse_input_grad=self.emb.grad_input)
+        with nvtx.range("sparse_update"):
+            self.emb.backward()
+            tracer.emit("sparse_update", "step", step=step, **self.emb.last_step_stats())
+        with nvtx.range("module_update"):
+            self.dense.apply()
+            tracer.emit("module_update", "step", step=step, master=self.dense.master)
+        with nvtx.range("sparse_commit"):
+            tracer.emit("sparse_commit", "step", step=step, sparse_optimizer_step=self.emb.step,
+                        dense_optimizer_step=self.dense.step)
+        return self.loss_sum
+
     def train_step(self) -> torch.Tensor:
         """One full optimizer step; returns the device scalar sum of per-sample losses."""
         if self.pipelined:
