@@ -100,6 +100,7 @@ class ShardedEmbeddingBagCollection:
         init: bool = True,
         deterministic: bool | None = None,
         pipelined: bool = False,
+        validate_inputs: bool | None = None,
     ):
         if not tables:
             raise ValueError("at least one table is required")
@@ -131,6 +132,9 @@ class ShardedEmbeddingBagCollection:
         # buffers a forward fills for its backward (staged ids / bags / lengths, pooled gradients) are
         # double-buffered and every call names its staging slot
         self.pipelined = bool(pipelined)
+        # debug mode (FLARE_VALIDATE_INPUTS=1): every batch's offsets and ids are checked before the copy
+        self.validate_inputs = (os.environ.get("FLARE_VALIDATE_INPUTS", "0") == "1" if validate_inputs is None
+                                else bool(validate_inputs))
         self.nbuf = 2 if self.pipelined else 1
         self._slot = 0
         if self.pipelined and any(t.dynamic or t.cache_rows is not None for t in self.tables):
@@ -372,6 +376,8 @@ class ShardedEmbeddingBagCollection:
         n = values.numel()
         if n > self.values_capacity:
             raise ValueError(f"{n} ids exceed the values capacity {self.values_capacity}")
+        if self.validate_inputs:
+            validate_keyed_jagged(offsets, values, self.tables, self.B, self.max_bag)
         self.in_offsets.local.copy_(offsets, non_blocking=non_blocking)
         self.in_values.local[:n].copy_(values, non_blocking=non_blocking)
 
@@ -547,9 +553,43 @@ class ShardedEmbeddingBagCollection:
         return sum(t.numel() * t.element_size() for t in tensors if t is not None)
 
 
+def validate_keyed_jagged(offsets: torch.Tensor, values: torch.Tensor, tables: list[SparseTableSpec], batch: int,
+                          max_bag: int) -> None:
+    """Check a keyed-jagged batch before the kernels see it (debug mode; reads the data on the host).
+
+    ``offsets`` [F*B+1] int32 starts at 0, never decreases and ends at the id count; no bag is longer
+    than ``max_bag`` (the staging capacity); every id of table f is in [0, rows_f) (dynamic tables:
+    any id >= 0).  Raises ``ValueError`` naming the first offending feature / sample.  The same
+    contract as the reference's ragged-input validation before native writes
+    (src/flare/data/schema/input.py:90-123)."""
+    F = len(tables)
+    if offsets.dtype != torch.int32 or values.dtype != torch.int32:
+        raise ValueError("offsets and ids must be int32")
+    off = offsets.detach().to("cpu", torch.int64)
+    if off.numel() != F * batch + 1 or int(off[0]) != 0:
+        raise ValueError("offsets must have F*B+1 entries and start at 0")
+    lens = off[1:] - off[:-1]
+    if bool((lens < 0).any()):
+        k = int(torch.nonzero(lens < 0)[0])
+        raise ValueError(f"offsets decrease at feature {k // batch}, sample {k % batch}")
+    if int(off[-1]) != values.numel():
+        raise ValueError(f"offsets end at {int(off[-1])}, but {values.numel()} ids were given")
+    if bool((lens > max_bag).any()):
+        k = int(torch.nonzero(lens > max_bag)[0])
+        raise ValueError(f"feature {k // batch}, sample {k % batch}: bag of {int(lens[k])} ids > max_bag {max_bag}")
+    ids = values.detach().to("cpu", torch.int64)
+    for f, t in enumerate(tables):
+        seg = ids[int(off[f * batch]):int(off[(f + 1) * batch])]
+        if seg.numel() == 0:
+            continue
+        lo, hi = int(seg.min()), int(seg.max())
+        if lo < 0 or (not t.dynamic and hi >= t.num_embeddings):
+            raise ValueError(f"feature {f} (table {t.name}): ids span [{lo}, {hi}], rows [0, {t.num_embeddings})")
+
+
 def expected_math_bytes(num_ids: int, dim: int, value_bytes: int = 4) -> float:
     """Bytes a forward gather-pool must read at minimum (for roofline reports)."""
     return float(num_ids) * dim * value_bytes
 
 
-__all__ = ["LocalShard", "ShardedEmbeddingBagCollection", "expected_math_bytes"]
+__all__ = ["LocalShard", "ShardedEmbeddingBagCollection", "expected_math_bytes", "validate_keyed_jagged"]

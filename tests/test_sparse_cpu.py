@@ -147,3 +147,27 @@ def test_native_cpu_ops_match_torch_reference(dtype, vd):
     keys = torch.randint(0, 97, (2000,), generator=g)
     for a, b in zip(unique_first_occurrence(keys), unique_first_occurrence_reference(keys)):
         assert torch.equal(a, b)
+
+
+def test_validate_keyed_jagged_catches_bad_batches():
+    import pytest
+    import torch
+
+    from flare_b200.sparse.collection import validate_keyed_jagged
+    from flare_b200.sparse.config import SparseTableSpec
+
+    tables = [SparseTableSpec("a", 10, 8), SparseTableSpec("b", 5, 8, dynamic=True)]
+    B = 3
+    off = torch.tensor([0, 1, 3, 3, 4, 6, 7], dtype=torch.int32)
+    ids = torch.tensor([1, 2, 9, 100, 0, 4, 7], dtype=torch.int32)
+    validate_keyed_jagged(off, ids, tables, B, max_bag=4)  # dynamic table b takes any id >= 0
+    with pytest.raises(ValueError, match="feature 0"):
+        validate_keyed_jagged(off, torch.tensor([1, 2, 10, 100, 0, 4, 7], dtype=torch.int32), tables, B, 4)
+    with pytest.raises(ValueError, match="decrease at feature 0, sample 2"):
+        validate_keyed_jagged(torch.tensor([0, 1, 3, 2, 4, 6, 7], dtype=torch.int32), ids, tables, B, 4)
+    with pytest.raises(ValueError, match="max_bag"):
+        validate_keyed_jagged(off, ids, tables, B, max_bag=1)
+    with pytest.raises(ValueError, match="end at"):
+        validate_keyed_jagged(off, ids[:6], tables, B, 4)
+    with pytest.raises(ValueError, match="int32"):
+        validate_keyed_jagged(off.long(), ids, tables, B, 4)
