@@ -43,6 +43,9 @@ def _parser() -> argparse.ArgumentParser:
     t.add_argument("--metrics-jsonl", default=None)
     t.add_argument("--seed", type=int, default=0)
     t.add_argument("--no-graph", action="store_true")
+    t.add_argument("--table-shards", default="",
+                   help='row-wise pieces per table: "4" (every table) or "t0:4,t3:2" (the rest keep their config)')
+    t.add_argument("--sparse-policy", choices=["sync", "pipelined"], default="sync")
     e = sub.add_parser("eval")
     e.add_argument("--model-config", required=True)
     e.add_argument("--checkpoint-dir", required=True)
@@ -55,12 +58,17 @@ def _parser() -> argparse.ArgumentParser:
     return p
 
 
-def _dlrm_cfg(path):
-    from .config.loader import load_model_config
+def _dlrm_cfg(path, table_shards: str = ""):
+    from dataclasses import replace
+
+    from .config.loader import load_model_config, parse_group_counts
 
     name, cfg = load_model_config(path)
     if name != "dlrm":
         raise SystemExit(f"the cli trains the dlrm model family; {name!r} has its own benchmark entry point")
+    if table_shards:
+        counts = parse_group_counts(table_shards, [t.name for t in cfg.tables], what="table shards")
+        cfg.tables = [replace(t, shards=counts.get(t.name, t.shards)) for t in cfg.tables]
     return cfg
 
 
@@ -108,10 +116,10 @@ def train(args) -> int:
     info = init_distributed(timeout_s=300)
     rank, world = info.rank, max(info.world_size, 1)
     dev = torch.device("cuda", torch.cuda.current_device())
-    cfg = _dlrm_cfg(args.model_config)
+    cfg = _dlrm_cfg(args.model_config, args.table_shards)
     B = args.batch_per_gpu
     trainer = DLRMTrainer(cfg, B, max_bag_size=args.max_bag, rank=rank, world_size=world, device=dev,
-                          seed=args.seed, use_graph=not args.no_graph)
+                          seed=args.seed, use_graph=not args.no_graph, sparse_policy=args.sparse_policy)
     mgr = CheckpointManager(args.checkpoint_dir) if args.checkpoint_dir else None
     start = 0
     if args.resume and mgr is not None and latest_step(args.checkpoint_dir) is not None:

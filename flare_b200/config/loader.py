@@ -203,6 +203,43 @@ class LayeredConfigLoader:
         return build_dataclass(cls, tree)
 
 
+def parse_group_counts(arg: str, groups: Sequence[str], *, default: int | None = None,
+                       what: str = "count") -> dict[str, int]:
+    """``"8"`` (every group) or ``"users:2,items:1"`` (per group, the rest ``default``) -> {group: count}.
+
+    Counts are positive integers; unknown or repeated groups are errors.  The same knob grammar as
+    the reference's sparse worker counts (recipes/recsys/ranking/schema/sparse_features.py:14-43)."""
+    def positive(v: str, label: str) -> int:
+        try:
+            n = int(v)
+        except ValueError:
+            raise ValueError(f"{label} must be a positive integer, got {v!r}") from None
+        if n < 1:
+            raise ValueError(f"{label} must be a positive integer, got {v!r}")
+        return n
+
+    names = list(dict.fromkeys(groups))
+    out = {} if default is None else dict.fromkeys(names, default)
+    arg = arg.strip()
+    if not arg:
+        return out
+    if ":" not in arg:
+        return dict.fromkeys(names, positive(arg, what))
+    seen: set[str] = set()
+    for item in arg.split(","):
+        parts = [x.strip() for x in item.split(":")]
+        if len(parts) != 2:
+            raise ValueError(f"{what} overrides are name:count, got {item!r}")
+        name, v = parts
+        if name not in names:
+            raise ValueError(f"unknown group {name!r} (known: {names})")
+        if name in seen:
+            raise ValueError(f"group {name!r} given twice")
+        out[name] = positive(v, f"{what} of {name!r}")
+        seen.add(name)
+    return out
+
+
 def load_model_config(source: str | Path | Mapping[str, Any]):
     """Model-structure file -> (model name, config dataclass) for ``dlrm``, ``dcn`` or ``seqrec``."""
     raw = dict(source) if isinstance(source, Mapping) else _read_file(Path(source))
@@ -218,5 +255,5 @@ def load_model_config(source: str | Path | Mapping[str, Any]):
     return name, build_dataclass(C, raw)
 
 
-__all__ = ["LayeredConfigLoader", "build_dataclass", "dict_to_cli_args", "load_model_config",
+__all__ = ["LayeredConfigLoader", "build_dataclass", "dict_to_cli_args", "load_model_config", "parse_group_counts",
            "resolve_environment"]

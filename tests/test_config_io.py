@@ -73,3 +73,18 @@ def test_http_session_per_process():
     s = get_process_http_session()
     assert s is get_process_http_session()
     assert s.get_adapter("https://example.invalid").max_retries.total == 5
+
+
+def test_parse_group_counts():
+    import pytest
+
+    from flare_b200.config.loader import parse_group_counts
+
+    g = ["users", "items", "ctx"]
+    assert parse_group_counts("8", g) == {"users": 8, "items": 8, "ctx": 8}
+    assert parse_group_counts("users:2,items:1", g, default=4) == {"users": 2, "items": 1, "ctx": 4}
+    assert parse_group_counts("", g) == {}
+    for bad, msg in [("0", "positive"), ("users:2,users:3", "twice"), ("nope:1", "unknown"), ("users:2:3", "name:count"),
+                     ("users:x", "positive")]:
+        with pytest.raises(ValueError, match=msg):
+            parse_group_counts(bad, g)
