@@ -173,7 +173,11 @@ class DLRM:
 
     # ------------------------------------------------------------------ step
     def forward_backward(self) -> torch.Tensor:
-        """Forward + backward of the local batch; gradients land in the flat/sparse buffers."""
+        """Forward + backward of the local batch; gradients land in the flat/sparse buffers.
+
+        Synchronous semantics: a sparse update still pending under the pipelined policy is applied
+        first (its staging slot is the one this forward would reuse)."""
+        self.flush_pending_updates()
         cast_pad_bf16(self.dense_in, self.xd)
         bot = self.bottom.forward(self.xd)
         pooled = self.emb.forward()
@@ -189,7 +193,8 @@ class DLRM:
         return self.loss_sum
 
     def profile_step(self) -> list[tuple[str, float]]:
-        """One eager training step with CUDA events between its ops; returns (op, ms) in order."""
+        """One eager (synchronous) training step with CUDA events between its ops; returns (op, ms) in order."""
+        self.flush_pending_updates()
         st: dict = {}
 
         def inter_fwd():
