@@ -128,14 +128,27 @@ def apply_rows_reference(opt: SparseOptimizerConfig, step: int, w: torch.Tensor,
 
 
 class CpuEmbeddingBagCollection:
-    """Whole tables on the host; same forward/backward contract as the GPU collection."""
+    """Whole tables on the host; same forward/backward contract as the GPU collection.
+
+    With ``storage`` (``SparseStorageOptions``) every table lives in a native paged store instead
+    of a tensor: one record per row holds the weights and the optimizer state, pages beyond the
+    memory limit spill to disk, and a step reads and writes only the rows of its batch (the
+    reference's external store with an AutoStorage memory limit and spill directory).
+    """
 
     def __init__(self, tables: list[SparseTableSpec], batch_size: int, *, optimizer: SparseOptimizerConfig | None = None,
-                 seed: int = 0, weights: list[torch.Tensor] | None = None):
+                 seed: int = 0, weights: list[torch.Tensor] | None = None, storage=None):
         self.tables = list(tables)
         self.B = int(batch_size)
         self.optimizer = optimizer or tables[0].optimizer
         self.total_dim = sum(t.embedding_dim for t in tables)
+        self.step = 0
+        self._offsets = None
+        self._values = None
+        self.stores = None
+        if storage is not None:
+            self._init_paged(storage, seed, weights)
+            return
         g = torch.Generator().manual_seed(seed)
         if weights is None:
             weights = [((torch.rand(t.num_embeddings, t.embedding_dim, generator=g) * 2 - 1) * t.init_scale)
@@ -154,21 +167,107 @@ class CpuEmbeddingBagCollection:
             if opt.needs_score:
                 st["score"] = torch.zeros(t.num_embeddings)
             self.state.append(st)
-        self.step = 0
-        self._offsets = None
-        self._values = None
 
     def set_input(self, offsets: torch.Tensor, values: torch.Tensor, non_blocking: bool = False) -> None:
         self._offsets, self._values = offsets.cpu(), values.cpu()
 
     def forward(self) -> torch.Tensor:
+        if self.stores is not None:
+            return self._forward_paged()
         return pool_reference(self.weights, self.tables, self._offsets, self._values, self.B)
 
     def backward(self, grad_pooled: torch.Tensor, step: int | None = None) -> None:
         self.step = self.step + 1 if step is None else int(step)
         for f, (rows, g, cnt) in enumerate(row_gradients(self.tables, self._offsets, self._values, grad_pooled,
                                                          self.B)):
-            apply_rows_reference(self.optimizer, self.step, self.weights[f], rows, g, cnt, self.state[f])
+            if self.stores is not None:
+                self._apply_paged(f, rows, g, cnt)
+            else:
+                apply_rows_reference(self.optimizer, self.step, self.weights[f], rows, g, cnt, self.state[f])
+
+    # ------------------------------------------------------------ paged storage
+    def _layout(self, t: SparseTableSpec) -> list[tuple[str, int]]:
+        """Record fields (name, width): weights, then the optimizer state the optimizer keeps."""
+        opt, d = self.optimizer, t.embedding_dim
+        fields = [("weight", d)]
+        if opt.needs_m:
+            fields.append(("m", d))
+        if opt.needs_v:
+            fields.append(("v", d))
+        if opt.needs_row_state:
+            fields.append(("row", 1))
+        if opt.needs_score:
+            fields.append(("score", 1))
+        return fields
+
+    def _init_paged(self, storage, seed: int, weights) -> None:
+        self.layouts = [self._layout(t) for t in self.tables]
+        specs = [(t.name, t.num_embeddings, sum(w for _, w in lay), t.embedding_dim, t.init_scale)
+                 for t, lay in zip(self.tables, self.layouts)]
+        self.stores = storage.build_stores(specs, seed)
+        if weights is not None:  # start from given tables (every row is written once)
+            for f, w in enumerate(weights):
+                ids = torch.arange(w.shape[0])
+                rec = self.stores[f].gather(ids)
+                rec[:, :w.shape[1]] = w.float()
+                self.stores[f].scatter(ids, rec)
+
+    def _split(self, f: int, rec: torch.Tensor) -> dict[str, torch.Tensor]:
+        out, c = {}, 0
+        for name, w in self.layouts[f]:
+            out[name] = rec[:, c:c + w] if w > 1 else rec[:, c]
+            c += w
+        return out
+
+    def _ids_of(self, f: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        B = self.B
+        offs, vals = self._offsets.long(), self._values.long()
+        beg, end = offs[f * B:(f + 1) * B], offs[f * B + 1:(f + 1) * B + 1]
+        lens = end - beg
+        ids = vals[beg[0]:end[-1]] if B else vals[:0]
+        return ids, torch.repeat_interleave(torch.arange(B), lens), lens
+
+    def _forward_paged(self) -> torch.Tensor:
+        out = torch.zeros(self.B, self.total_dim, dtype=torch.float32)
+        col = 0
+        for f, t in enumerate(self.tables):
+            d = t.embedding_dim
+            ids, bag, lens = self._ids_of(f)
+            keep = ids >= 0
+            uniq, inv = torch.unique(ids.clamp_min(0), return_inverse=True)
+            w = self._split(f, self.stores[f].gather(uniq))["weight"].to(TORCH_DTYPES[t.value_dtype]).float()
+            pooled = torch.zeros(self.B, d)
+            pooled.index_add_(0, bag, w[inv] * keep.unsqueeze(1))
+            if t.pooling == "mean":
+                pooled = pooled / lens.clamp_min(1).unsqueeze(1).float()
+            out[:, col:col + d] = pooled
+            col += d
+        return out
+
+    def _apply_paged(self, f: int, rows: torch.Tensor, g: torch.Tensor, cnt: torch.Tensor) -> None:
+        if rows.numel() == 0:
+            return
+        rec = self.stores[f].gather(rows)
+        parts = self._split(f, rec)
+        w = parts["weight"].to(TORCH_DTYPES[self.tables[f].value_dtype])
+        state = {k: v.clone() for k, v in parts.items() if k != "weight"}
+        apply_rows_reference(self.optimizer, self.step, w, torch.arange(rows.numel()), g, cnt, state)
+        c = 0
+        for name, width in self.layouts[f]:
+            v = w.float() if name == "weight" else state[name]
+            rec[:, c:c + width] = v if width > 1 else v.unsqueeze(1)
+            c += width
+        self.stores[f].scatter(rows, rec)
+
+    def table_weights(self, f: int) -> torch.Tensor:
+        """Table f's weights (every row; reads the whole paged table when stored)."""
+        if self.stores is None:
+            return self.weights[f]
+        t = self.tables[f]
+        return self._split(f, self.stores[f].gather(torch.arange(t.num_embeddings)))["weight"].clone()
+
+    def storage_stats(self) -> list[dict]:
+        return [s.stats() for s in self.stores] if self.stores is not None else []
 
 
 __all__ = ["CpuEmbeddingBagCollection", "apply_rows_reference", "lr_scale_reference", "pool_reference",
