@@ -66,10 +66,14 @@ def small_tables(opt: SparseOptimizerConfig | None = None) -> list[SparseTableSp
     return [SparseTableSpec(f"c{i}", 1000, 16, optimizer=opt) for i in range(8)]
 
 
-def train_small_cpu(steps: int = 200, batch_size: int = 256, seed: int = 0) -> SmallRunResult:
+def train_small_cpu(steps: int = 200, batch_size: int = 256, seed: int = 0, storage=None) -> SmallRunResult:
+    """``storage`` (``SparseStorageOptions``): keep the tables in the paged store (memory limit, disk
+    spill), starting from the same initial rows as the in-memory run."""
     torch.manual_seed(seed)
     data = SmallSyntheticData(batch_size, seed=seed)
     emb = CpuEmbeddingBagCollection(small_tables(), batch_size, seed=seed)
+    if storage is not None:
+        emb = CpuEmbeddingBagCollection(small_tables(), batch_size, seed=seed, storage=storage, weights=emb.weights)
     model = SmallDense()
     engine = TrainEngine(model, lambda out, y: nn.functional.binary_cross_entropy_with_logits(out, y),
                          TrainingExecutionPlan.replicated(), DenseOptimizerConfig(kind="adam", learning_rate=1e-3),
