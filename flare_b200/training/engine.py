@@ -26,7 +26,13 @@ collectives (src/flare/jax/training/zero/collectives.py:14-95):
   shard-update capability rule of
   src/flare/jax/training/optimizers/base.py:70-150;
 * checkpoint capture is allowed only at a window boundary and stores logical
-  (unpadded) shapes; ``finalize_checkpoint_window`` applies a partial window.
+  (unpadded) shapes; ``finalize_checkpoint_window`` applies a partial window;
+* non-parameter state (module buffers) follows the reference's rules
+  (src/flare/jax/training/engines/distributed.py:663-701): float buffers
+  (e.g. normalisation statistics) are averaged over the ranks after every
+  micro-step, integer / bool buffers must stay replicated (checked against
+  every rank's copy when ``check_replication``), the reported loss is the
+  mean over the ranks, and the buffers are part of the checkpoint.
 
 The B200 product paths (fused DLRM) do not use this engine's NCCL
 collectives; they use the fused kernels of ``flare_b200.training.flat``.
@@ -62,7 +68,8 @@ class TrainEngine:
     def __init__(self, model: nn.Module, loss_fn: Callable[[Any, Any], torch.Tensor], plan: TrainingExecutionPlan,
                  optimizer: DenseOptimizerConfig, *, precision: PrecisionPolicy = PrecisionPolicy.FP32,
                  process_group: dist.ProcessGroup | None = None, device: torch.device | None = None,
-                 forward: Callable[[nn.Module, Any], Any] | None = None, node_size: int | None = None):
+                 forward: Callable[[nn.Module, Any], Any] | None = None, node_size: int | None = None,
+                 sync_buffers: bool = True, check_replication: bool = False):
         self.model = model
         self.loss_fn = loss_fn
         self.plan = plan
@@ -95,6 +102,7 @@ class TrainEngine:
         self.step = 0
         self.params = [p for p in model.parameters() if p.requires_grad]
         self.names = [n for n, p in model.named_parameters() if p.requires_grad]
+        self.sync_buffers, self.check_replication = sync_buffers, check_replication
         self.offsets, off = [], 0
         for p in self.params:
             self.offsets.append(off)
@@ -165,6 +173,7 @@ class TrainEngine:
             outputs = self.forward_fn(self.model, inputs)
             loss = self.loss_fn(outputs, targets)
         loss.backward()
+        self._sync_buffer_state()
         g = self._gather_flat_grad()
         self.micro_step += 1
         if self.plan.accumulation.sync_mode == "micro":
@@ -177,9 +186,29 @@ class TrainEngine:
         if at_boundary and self.plan.update.apply_optimizer_at_boundary:
             self.apply_accumulated_update()
             applied = True
-        self.last_loss = float(loss.detach())
-        return TrainStepResult(loss.detach(), self.micro_step if not applied else self.micro_steps, self.step,
+        mean_loss = loss.detach()
+        if self.world > 1:  # the reported loss is the mean over the ranks
+            mean_loss = mean_loss.float().clone()
+            dist.all_reduce(mean_loss, group=self.pg)
+            mean_loss = mean_loss / self.world
+        self.last_loss = float(mean_loss)
+        return TrainStepResult(mean_loss, self.micro_step if not applied else self.micro_steps, self.step,
                                at_boundary, outputs)
+
+    def _sync_buffer_state(self) -> None:
+        """Average float buffers over the ranks; check that the others are replicated (when asked)."""
+        if self.world == 1 or not self.sync_buffers:
+            return
+        for name, b in self.model.named_buffers():
+            if b.is_floating_point():
+                t = b.detach().float().clone()
+                dist.all_reduce(t, group=self.pg)
+                b.copy_((t / self.world).to(b.dtype))
+            elif self.check_replication:
+                parts = [torch.empty_like(b) for _ in range(self.world)]
+                dist.all_gather(parts, b.detach().contiguous(), group=self.pg)
+                if any(not torch.equal(parts[0], x) for x in parts[1:]):
+                    raise RuntimeError(f"non-float buffer {name} differs across ranks")
 
     def apply_accumulated_update(self, micro_steps: int | None = None) -> None:
         n = micro_steps or self.micro_steps
@@ -247,7 +276,8 @@ class TrainEngine:
             raise RuntimeError("checkpoint capture requires an optimizer-window boundary")
         return {"step": self.step, "schema_digest": self.schema_digest(),
                 "model_state": self._unflatten(self._full_master()),
-                "optimizer_state": {"m": self._unflatten(self._full(self.m)), "v": self._unflatten(self._full(self.v))}}
+                "optimizer_state": {"m": self._unflatten(self._full(self.m)), "v": self._unflatten(self._full(self.v))},
+                "buffers": {n: b.detach().cpu().clone() for n, b in self.model.named_buffers()}}
 
     def restore_checkpoint_state(self, state: Mapping[str, Any]) -> None:
         if state.get("schema_digest") not in (None, self.schema_digest()):
@@ -273,6 +303,11 @@ class TrainEngine:
         self.acc_grad.zero_()
         self.reduced.zero_()
         self._scatter_params(full)
+        bufs = dict(self.model.named_buffers())
+        for n, t in state.get("buffers", {}).items():
+            if n not in bufs:
+                raise ValueError(f"checkpoint buffer {n} is not in the model")
+            bufs[n].copy_(t.to(bufs[n].device, bufs[n].dtype))
 
 
 class DistributedTrainStepExecutor:

@@ -106,3 +106,30 @@ def test_zero_topology_benchmark_node_equals_global(stage):
     assert g["shards"] == 4 and n["shards"] == 2
     assert n["intra_node_bytes"] > 0 and g["intra_node_bytes"] == 0
     assert n["cross_node_bytes"] > 0 and g["ms_per_step"] > 0 and n["ms_per_step"] > 0
+
+
+def _bn_model():
+    torch.manual_seed(0)
+    return nn.Sequential(nn.Linear(7, 16), nn.BatchNorm1d(16), nn.ReLU(), nn.Linear(16, 1))
+
+
+def _train_bn(rank, world, check):
+    plan = TrainingExecutionPlan.sharded(ZeroStage(1), micro_steps=1)
+    eng = TrainEngine(_bn_model(), lambda o, y: nn.functional.binary_cross_entropy_with_logits(o, y), plan,
+                      DenseOptimizerConfig(learning_rate=0.01), device=torch.device("cpu"), check_replication=check)
+    losses = []
+    for s in range(3):
+        x, y = _data(s, 0)
+        n = x.shape[0] // world
+        losses.append(float(eng.micro_step_once(x[rank * n:(rank + 1) * n], y[rank * n:(rank + 1) * n]).loss))
+    st = eng.capture_checkpoint_state()
+    bn = eng.model[1]
+    return bn.running_mean.clone(), int(bn.num_batches_tracked), losses, st["buffers"]["1.running_mean"]
+
+
+def test_buffers_are_averaged_and_replicated_and_loss_is_global():
+    outs = run_ranks(_train_bn, 2, True)
+    (m0, n0, l0, ck0), (m1, n1, l1, ck1) = outs
+    torch.testing.assert_close(m0, m1)  # averaged running statistics, identical on both ranks
+    assert n0 == n1 == 3 and l0 == l1  # replicated integer buffer (checked), loss reported as the global mean
+    torch.testing.assert_close(ck0, m0)  # buffers are checkpoint state
