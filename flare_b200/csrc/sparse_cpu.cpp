@@ -16,6 +16,7 @@
 #include <torch/extension.h>
 #include <ATen/Parallel.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstring>
 #include <vector>
@@ -156,6 +157,124 @@ void cpu_scatter_pooled(uintptr_t grad, int gdtype, uintptr_t inv, int64_t bags,
                   gdtype, E, reinterpret_cast<float*>(out));
 }
 
+// ---- keyed-jagged collection ops (the CPU configuration's sparse step) ----
+// offsets [F*B+1] (int32) cut `values` (int32 ids) into bags, feature-major;
+// table f is `weights[f]` [rows_f, dims_f] (fp32 / bf16 / fp16).
+
+inline int dtype_code(const torch::Tensor& t) {
+  if (t.scalar_type() == torch::kFloat32) return kF32;
+  if (t.scalar_type() == torch::kBFloat16) return kBF16;
+  TORCH_CHECK(t.scalar_type() == torch::kFloat16, "tables must be float32, bfloat16 or float16");
+  return kF16;
+}
+
+void check_bags(const torch::Tensor& offsets, const torch::Tensor& values, int64_t F, int64_t B) {
+  TORCH_CHECK(!offsets.is_cuda() && !values.is_cuda() && offsets.scalar_type() == torch::kInt32 &&
+                  values.scalar_type() == torch::kInt32 && offsets.is_contiguous() && values.is_contiguous(),
+              "offsets / values: contiguous int32 CPU tensors");
+  TORCH_CHECK(offsets.numel() == F * B + 1, "offsets must have F*B+1 entries");
+  const int32_t* off = offsets.data_ptr<int32_t>();
+  TORCH_CHECK(off[0] >= 0 && off[F * B] <= values.numel(), "offsets outside the id array");
+  for (int64_t k = 0; k < F * B; ++k) TORCH_CHECK(off[k + 1] >= off[k], "offsets must not decrease");
+}
+
+// out[b, col_f:col_f+d_f] = sum (mean) of table f's rows over bag (f, b); ids < 0 are skipped
+torch::Tensor cpu_bag_pool(std::vector<torch::Tensor> weights, torch::Tensor offsets, torch::Tensor values,
+                           int64_t B, std::vector<int64_t> mean) {
+  const int64_t F = static_cast<int64_t>(weights.size());
+  TORCH_CHECK(static_cast<int64_t>(mean.size()) == F, "one pooling flag per table");
+  check_bags(offsets, values, F, B);
+  std::vector<int64_t> cols(F + 1, 0);
+  for (int64_t f = 0; f < F; ++f) {
+    TORCH_CHECK(!weights[f].is_cuda() && weights[f].dim() == 2 && weights[f].is_contiguous(), "tables: 2-D CPU");
+    cols[f + 1] = cols[f] + weights[f].size(1);
+  }
+  const int32_t* off = offsets.data_ptr<int32_t>();
+  const int32_t* ids = values.data_ptr<int32_t>();
+  for (int64_t f = 0; f < F; ++f)  // id range, before any parallel work
+    for (int64_t e = off[f * B]; e < off[(f + 1) * B]; ++e)
+      TORCH_CHECK(ids[e] < weights[f].size(0), "id ", ids[e], " of table ", f, " >= ", weights[f].size(0));
+  auto out = torch::zeros({B, cols[F]}, torch::kFloat32);
+  float* o = out.data_ptr<float>();
+  at::parallel_for(0, F * B, 64, [&](int64_t lo, int64_t hi) {
+    for (int64_t k = lo; k < hi; ++k) {
+      const int64_t f = k / B, b = k - f * B, d = weights[f].size(1);
+      const void* w = weights[f].data_ptr();
+      const int dt = dtype_code(weights[f]);
+      float* acc = o + b * cols[F] + cols[f];
+      for (int64_t e = off[k]; e < off[k + 1]; ++e) {
+        if (ids[e] < 0) continue;
+        const int64_t base = static_cast<int64_t>(ids[e]) * d;
+        for (int64_t c = 0; c < d; ++c) acc[c] += load_val(w, dt, base + c);
+      }
+      if (mean[f]) {
+        const float inv = 1.f / static_cast<float>(std::max<int64_t>(1, off[k + 1] - off[k]));
+        for (int64_t c = 0; c < d; ++c) acc[c] *= inv;
+      }
+    }
+  });
+  return out;
+}
+
+// Per table: (unique ids ascending [U] int64, summed fp32 gradient rows [U, d], occurrence counts [U] fp32).
+// Each unique id adds its occurrences' pooled gradients in occurrence order (deterministic; no atomics).
+std::vector<py::tuple> cpu_bag_row_grads(torch::Tensor grad, torch::Tensor offsets, torch::Tensor values,
+                                         int64_t B, std::vector<int64_t> dims, std::vector<int64_t> mean) {
+  const int64_t F = static_cast<int64_t>(dims.size());
+  check_bags(offsets, values, F, B);
+  TORCH_CHECK(!grad.is_cuda() && grad.scalar_type() == torch::kFloat32 && grad.is_contiguous() && grad.dim() == 2 &&
+                  grad.size(0) == B, "grad: contiguous float32 [B, total_dim] CPU tensor");
+  const int64_t total = grad.size(1);
+  const int32_t* off = offsets.data_ptr<int32_t>();
+  const int32_t* ids = values.data_ptr<int32_t>();
+  const float* g = grad.data_ptr<float>();
+  std::vector<int64_t> cols(F + 1, 0);
+  for (int64_t f = 0; f < F; ++f) cols[f + 1] = cols[f] + dims[f];
+  TORCH_CHECK(cols[F] == total, "table widths must add up to the gradient width");
+  std::vector<torch::Tensor> uq(F), acc(F), cnt(F);
+  at::parallel_for(0, F, 1, [&](int64_t lo, int64_t hi) {
+    for (int64_t f = lo; f < hi; ++f) {
+      const int64_t e0 = off[f * B], e1 = off[(f + 1) * B], d = dims[f];
+      // occurrences (id, bag) in order, stably sorted by id
+      std::vector<int64_t> occ;
+      occ.reserve(static_cast<size_t>(e1 - e0));
+      std::vector<int64_t> bag_of(static_cast<size_t>(e1 - e0));
+      for (int64_t b = 0; b < B; ++b)
+        for (int64_t e = off[f * B + b]; e < off[f * B + b + 1]; ++e) bag_of[e - e0] = b;
+      for (int64_t e = e0; e < e1; ++e)
+        if (ids[e] >= 0) occ.push_back(e);
+      std::stable_sort(occ.begin(), occ.end(), [&](int64_t a, int64_t c) { return ids[a] < ids[c]; });
+      int64_t U = 0;
+      for (size_t i = 0; i < occ.size(); ++i)
+        if (i == 0 || ids[occ[i]] != ids[occ[i - 1]]) ++U;
+      auto u = torch::empty({U}, torch::kInt64);
+      auto a = torch::zeros({U, d}, torch::kFloat32);
+      auto n = torch::zeros({U}, torch::kFloat32);
+      int64_t* up = u.data_ptr<int64_t>();
+      float* ap = a.data_ptr<float>();
+      float* np = n.data_ptr<float>();
+      int64_t j = -1;
+      for (size_t i = 0; i < occ.size(); ++i) {
+        const int64_t e = occ[i];
+        if (i == 0 || ids[e] != ids[occ[i - 1]]) up[++j] = ids[e];
+        const int64_t b = bag_of[e - e0];
+        float scale = 1.f;
+        if (mean[f]) scale = 1.f / static_cast<float>(std::max<int64_t>(1, off[f * B + b + 1] - off[f * B + b]));
+        const float* src = g + b * total + cols[f];
+        float* dst = ap + j * d;
+        for (int64_t c = 0; c < d; ++c) dst[c] += src[c] * scale;
+        np[j] += 1.f;
+      }
+      uq[f] = u;
+      acc[f] = a;
+      cnt[f] = n;
+    }
+  });
+  std::vector<py::tuple> res;
+  for (int64_t f = 0; f < F; ++f) res.push_back(py::make_tuple(uq[f], acc[f], cnt[f]));
+  return res;
+}
+
 }  // namespace flare_cpu
 
 void register_sparse_cpu(py::module_& m) {
@@ -165,4 +284,6 @@ void register_sparse_cpu(py::module_& m) {
   c.def("scatter", &flare_cpu::cpu_scatter);
   c.def("scatter_pooled", &flare_cpu::cpu_scatter_pooled);
   c.def("unique_first", &flare_cpu::cpu_unique_first);
+  c.def("bag_pool", &flare_cpu::cpu_bag_pool);
+  c.def("bag_row_grads", &flare_cpu::cpu_bag_row_grads);
 }

@@ -66,12 +66,14 @@ def small_tables(opt: SparseOptimizerConfig | None = None) -> list[SparseTableSp
     return [SparseTableSpec(f"c{i}", 1000, 16, optimizer=opt) for i in range(8)]
 
 
-def train_small_cpu(steps: int = 200, batch_size: int = 256, seed: int = 0, storage=None) -> SmallRunResult:
+def train_small_cpu(steps: int = 200, batch_size: int = 256, seed: int = 0, storage=None,
+                    native: bool = True) -> SmallRunResult:
     """``storage`` (``SparseStorageOptions``): keep the tables in the paged store (memory limit, disk
-    spill), starting from the same initial rows as the in-memory run."""
+    spill), starting from the same initial rows as the in-memory run.  ``native``: pool and reduce
+    the sparse gradients with the host C++ ops (the tensor-op path otherwise)."""
     torch.manual_seed(seed)
     data = SmallSyntheticData(batch_size, seed=seed)
-    emb = CpuEmbeddingBagCollection(small_tables(), batch_size, seed=seed)
+    emb = CpuEmbeddingBagCollection(small_tables(), batch_size, seed=seed, native=native)
     if storage is not None:
         emb = CpuEmbeddingBagCollection(small_tables(), batch_size, seed=seed, storage=storage, weights=emb.weights)
     model = SmallDense()

@@ -137,7 +137,7 @@ class CpuEmbeddingBagCollection:
     """
 
     def __init__(self, tables: list[SparseTableSpec], batch_size: int, *, optimizer: SparseOptimizerConfig | None = None,
-                 seed: int = 0, weights: list[torch.Tensor] | None = None, storage=None):
+                 seed: int = 0, weights: list[torch.Tensor] | None = None, storage=None, native: bool = False):
         self.tables = list(tables)
         self.B = int(batch_size)
         self.optimizer = optimizer or tables[0].optimizer
@@ -146,6 +146,10 @@ class CpuEmbeddingBagCollection:
         self._offsets = None
         self._values = None
         self.stores = None
+        # native: pooling and per-row gradient sums in the host C++ ops (parallel over bags / tables,
+        # fp32, each row adds its occurrences in order) instead of tensor ops; the tensor-op path stays
+        # the plain-PyTorch oracle of the GPU kernels
+        self.native = bool(native)
         if storage is not None:
             self._init_paged(storage, seed, weights)
             return
@@ -171,15 +175,31 @@ class CpuEmbeddingBagCollection:
     def set_input(self, offsets: torch.Tensor, values: torch.Tensor, non_blocking: bool = False) -> None:
         self._offsets, self._values = offsets.cpu(), values.cpu()
 
+    def _mean_flags(self) -> list[int]:
+        return [1 if t.pooling == "mean" else 0 for t in self.tables]
+
     def forward(self) -> torch.Tensor:
         if self.stores is not None:
             return self._forward_paged()
+        if self.native:
+            from .._native import native
+
+            return native().cpu.bag_pool([w.contiguous() for w in self.weights], self._offsets.int().contiguous(),
+                                         self._values.int().contiguous(), self.B, self._mean_flags())
         return pool_reference(self.weights, self.tables, self._offsets, self._values, self.B)
+
+    def _row_gradients(self, grad_pooled: torch.Tensor):
+        if self.native:
+            from .._native import native
+
+            return native().cpu.bag_row_grads(grad_pooled.detach().float().contiguous(),
+                                              self._offsets.int().contiguous(), self._values.int().contiguous(),
+                                              self.B, [t.embedding_dim for t in self.tables], self._mean_flags())
+        return row_gradients(self.tables, self._offsets, self._values, grad_pooled, self.B)
 
     def backward(self, grad_pooled: torch.Tensor, step: int | None = None) -> None:
         self.step = self.step + 1 if step is None else int(step)
-        for f, (rows, g, cnt) in enumerate(row_gradients(self.tables, self._offsets, self._values, grad_pooled,
-                                                         self.B)):
+        for f, (rows, g, cnt) in enumerate(self._row_gradients(grad_pooled)):
             if self.stores is not None:
                 self._apply_paged(f, rows, g, cnt)
             else:

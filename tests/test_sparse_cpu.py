@@ -171,3 +171,33 @@ def test_validate_keyed_jagged_catches_bad_batches():
         validate_keyed_jagged(off, ids[:6], tables, B, 4)
     with pytest.raises(ValueError, match="int32"):
         validate_keyed_jagged(off.long(), ids, tables, B, 4)
+
+
+def test_native_collection_ops_match_the_tensor_oracle():
+    import torch
+
+    from flare_b200.sparse.config import SparseOptimizerConfig, SparseTableSpec
+    from flare_b200.sparse.reference import CpuEmbeddingBagCollection
+
+    opt = SparseOptimizerConfig(kind="rowwise_adagrad", learning_rate=0.05)
+    tables = [SparseTableSpec("a", 500, 8, optimizer=opt), SparseTableSpec("b", 80, 16, pooling="mean", optimizer=opt),
+              SparseTableSpec("c", 300, 4, value_dtype="float16", optimizer=opt)]
+    B = 48
+    plain = CpuEmbeddingBagCollection(tables, B, optimizer=opt, seed=3)
+    fast = CpuEmbeddingBagCollection(tables, B, optimizer=opt, weights=[w.clone() for w in plain.weights],
+                                     native=True)
+    g = torch.Generator().manual_seed(1)
+    for _ in range(3):
+        lens = torch.randint(0, 7, (3 * B,), generator=g)
+        offs = torch.cat([torch.zeros(1, dtype=torch.long), lens.cumsum(0)]).int()
+        vals = torch.cat([torch.randint(-1, n, (int(lens[f * B:(f + 1) * B].sum()),), generator=g)
+                          for f, n in enumerate((500, 80, 300))]).int()  # -1: skipped ids
+        ys = []
+        for c in (plain, fast):
+            c.set_input(offs, vals)
+            y = c.forward()
+            c.backward(torch.sin(y) + 0.1)
+            ys.append(y)
+        torch.testing.assert_close(ys[1], ys[0], rtol=1e-6, atol=1e-6)
+    for a, b in zip(plain.weights, fast.weights):
+        torch.testing.assert_close(b.float(), a.float(), rtol=1e-5, atol=1e-6)
