@@ -5,7 +5,7 @@
 Stages (host CPU; the hot loops are the native parser and encoders of
 ``csrc/etl.cpp``):
 
-1. read: record files (plain or gzip), one record per line (TAB columns; the
+1. read: record files (plain, gzip or zstd), one record per line (TAB columns; the
    feature column holds ``code\\x03value`` items separated by ``\\x02``), in
    chunks of ``rows_per_file`` lines;
 2. parse: ``ArrowRowParser`` on the chunk's Arrow string column (fixed,
@@ -104,9 +104,22 @@ def _input_files(paths) -> list[str]:
     return out
 
 
+def _open_text(path: str):
+    """Text stream of a record file: plain, gzip (``.gz``) or zstd (``.zst`` / ``.zstd``, Arrow's codec)."""
+    if path.endswith(".gz"):
+        return gzip.open(path, "rt", encoding="utf-8", newline="\n")
+    if path.endswith((".zst", ".zstd")):
+        import io
+
+        import pyarrow as pa
+
+        raw = pa.CompressedInputStream(pa.OSFile(path, "rb"), "zstd")
+        return io.TextIOWrapper(io.BufferedReader(raw), encoding="utf-8", newline="\n")
+    return open(path, "rt", encoding="utf-8", newline="\n")
+
+
 def read_chunks(path: str, rows: int) -> Iterator[list[str]]:
-    opener = gzip.open if path.endswith(".gz") else open
-    with opener(path, "rt", encoding="utf-8", newline="\n") as f:
+    with _open_text(path) as f:
         chunk = []
         for line in f:
             if line.strip("\n"):

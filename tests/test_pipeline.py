@@ -116,3 +116,18 @@ def test_parallel_workers_and_planning(tmp_path):
     (tmp_path / "colors.txt").write_text("red\ngreen\n\nblue\n")
     vals, auto = load_category_values({"c": "colors.txt", "d": "auto"}, tmp_path)
     assert vals["c"] == {"red": 0, "green": 1, "blue": 2} and auto == {"d"}
+
+
+def test_zstd_inputs_encode_like_plain_ones(tmp_path):
+    plain, packed = tmp_path / "p", tmp_path / "z"
+    (plain / "logs").mkdir(parents=True)
+    (packed / "logs").mkdir(parents=True)
+    _write_logs(plain / "logs" / "a.txt", 230, 4)
+    with pa.CompressedOutputStream(str(packed / "logs" / "a.txt.zst"), "zstd") as out:
+        out.write((plain / "logs" / "a.txt").read_bytes())
+    tabs = []
+    for root in (plain, packed):
+        DataPipeline(_cfg(root)).run()
+        files = sorted((root / "out").rglob("*.parquet"))
+        tabs.append(pa.concat_tables([pq.read_table(f) for f in files]))
+    assert tabs[0].num_rows == tabs[1].num_rows == 230 and tabs[0].equals(tabs[1])
