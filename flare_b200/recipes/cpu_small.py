@@ -87,7 +87,7 @@ def train_small_cpu(steps: int = 200, batch_size: int = 256, seed: int = 0, stor
         emb.set_input(b.offsets, b.values)
         pooled = emb.forward().requires_grad_(True)
         res = engine.micro_step_once((b.dense, pooled), b.labels)
-        emb.backward(pooled.grad)
+        emb.backward(engine.input_gradients({"pooled": pooled})["pooled"])
         losses.append(float(res.loss))
     dt = time.perf_counter() - t0
     return SmallRunResult(losses, steps * batch_size / dt, steps)

@@ -210,6 +210,14 @@ class TrainEngine:
                 if any(not torch.equal(parts[0], x) for x in parts[1:]):
                     raise RuntimeError(f"non-float buffer {name} differs across ranks")
 
+    def input_gradients(self, inputs: Mapping[str, torch.Tensor]) -> dict[str, torch.Tensor]:
+        """Gradients of the named inputs of the last micro-step (the pooled embeddings, for the sparse
+        tables), normalised by world size x micro-steps: the sample-mean contract of
+        ``training.gradients.normalize_input_gradients``."""
+        from .gradients import input_gradients
+
+        return input_gradients(inputs, world_size=self.world, micro_steps=self.micro_steps)
+
     def apply_accumulated_update(self, micro_steps: int | None = None) -> None:
         n = micro_steps or self.micro_steps
         if self.plan.accumulation.sync_mode == "boundary":

@@ -133,3 +133,24 @@ def test_buffers_are_averaged_and_replicated_and_loss_is_global():
     torch.testing.assert_close(m0, m1)  # averaged running statistics, identical on both ranks
     assert n0 == n1 == 3 and l0 == l1  # replicated integer buffer (checked), loss reported as the global mean
     torch.testing.assert_close(ck0, m0)  # buffers are checkpoint state
+
+
+def _sparse_contract(rank, world):
+    """Two ranks, each with half the batch: summed normalised input gradients = the global-batch gradient."""
+    torch.manual_seed(0)
+    model = nn.Linear(4, 1)
+    plan = TrainingExecutionPlan.sharded(ZeroStage(0), micro_steps=1)
+    eng = TrainEngine(model, lambda o, y: nn.functional.mse_loss(o, y), plan, DenseOptimizerConfig(learning_rate=0.0),
+                      device=torch.device("cpu"))
+    g = torch.Generator().manual_seed(3)
+    x, y = torch.randn(8, 4, generator=g), torch.randn(8, 1, generator=g)
+    n = 8 // world
+    pooled = x[rank * n:(rank + 1) * n].clone().requires_grad_(True)
+    eng.micro_step_once(pooled, y[rank * n:(rank + 1) * n])
+    return eng.input_gradients({"pooled": pooled})["pooled"]
+
+
+def test_input_gradients_follow_the_sample_mean_contract():
+    one = _sparse_contract(0, 1)
+    parts = run_ranks(_sparse_contract, 2)
+    torch.testing.assert_close(torch.cat(parts), one, rtol=1e-6, atol=1e-7)
