@@ -69,7 +69,7 @@ class TrainEngine:
                  optimizer: DenseOptimizerConfig, *, precision: PrecisionPolicy = PrecisionPolicy.FP32,
                  process_group: dist.ProcessGroup | None = None, device: torch.device | None = None,
                  forward: Callable[[nn.Module, Any], Any] | None = None, node_size: int | None = None,
-                 sync_buffers: bool = True, check_replication: bool = False):
+                 sync_buffers: bool = True, check_replication: bool = False, validate_constants: bool = False):
         self.model = model
         self.loss_fn = loss_fn
         self.plan = plan
@@ -103,6 +103,10 @@ class TrainEngine:
         self.params = [p for p in model.parameters() if p.requires_grad]
         self.names = [n for n, p in model.named_parameters() if p.requires_grad]
         self.sync_buffers, self.check_replication = sync_buffers, check_replication
+        from .precision import constant_buffers
+
+        self.constants = constant_buffers(model)  # immutable buffers: never averaged; checked on request
+        self.validate_constants = validate_constants
         self.offsets, off = [], 0
         for p in self.params:
             self.offsets.append(off)
@@ -169,10 +173,15 @@ class TrainEngine:
         for p in self.params:
             p.grad = None
         dt = self.precision.compute_dtype
+        before = {n: c.detach().clone() for n, c in self.constants.items()} if self.validate_constants else None
         with torch.autocast(device_type=self.device.type, dtype=dt, enabled=dt != torch.float32):
             outputs = self.forward_fn(self.model, inputs)
             loss = self.loss_fn(outputs, targets)
         loss.backward()
+        if before is not None:
+            for n, c in self.constants.items():
+                if not torch.equal(before[n], c):
+                    raise RuntimeError(f"constant buffer {n} changed during the forward / backward")
         self._sync_buffer_state()
         g = self._gather_flat_grad()
         self.micro_step += 1
@@ -200,6 +209,8 @@ class TrainEngine:
         if self.world == 1 or not self.sync_buffers:
             return
         for name, b in self.model.named_buffers():
+            if name in self.constants:
+                continue
             if b.is_floating_point():
                 t = b.detach().float().clone()
                 dist.all_reduce(t, group=self.pg)

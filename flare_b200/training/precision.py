@@ -70,4 +70,39 @@ class PrecisionPolicy(str, Enum):
         return "float32" if self is PrecisionPolicy.FP32 else "bfloat16"
 
 
-__all__ = ["PrecisionPolicy"]
+# ------------------------------------------------------------ fp32 islands and constants
+class Fp32Island(torch.nn.Module):
+    """Runs the wrapped module in fp32 whatever the surrounding autocast: floating inputs are cast
+    to fp32 and autocast is off inside (the compute view of the reference's ``Fp32Param``, whose
+    parameters keep their fp32 view under mixed precision; src/flare/jax/roles.py:11)."""
+
+    def __init__(self, inner: torch.nn.Module):
+        super().__init__()
+        self.inner = inner
+
+    def forward(self, *args, **kwargs):
+        cast = lambda x: x.float() if torch.is_tensor(x) and x.is_floating_point() else x  # noqa: E731
+        dev = next((a.device.type for a in args if torch.is_tensor(a)), "cpu")
+        with torch.autocast(device_type=dev, enabled=False):
+            return self.inner(*[cast(a) for a in args], **{k: cast(v) for k, v in kwargs.items()})
+
+
+def register_constant(module: torch.nn.Module, name: str, value: torch.Tensor) -> None:
+    """An immutable, non-trainable tensor carried as module state (the reference's
+    ``ConstantBuffer``, src/flare/jax/roles.py:15): a persistent buffer, checkpointed, never averaged
+    across ranks, and checked for mutation when the engine runs with ``validate_constants``."""
+    module.register_buffer(name, value, persistent=True)
+    names = module.__dict__.setdefault("_flare_constants", set())
+    names.add(name)
+
+
+def constant_buffers(model: torch.nn.Module) -> dict[str, torch.Tensor]:
+    """Every registered constant of ``model`` by its dotted buffer name."""
+    out = {}
+    for prefix, m in model.named_modules():
+        for n in m.__dict__.get("_flare_constants", ()):
+            out[f"{prefix}.{n}" if prefix else n] = getattr(m, n)
+    return out
+
+
+__all__ = ["Fp32Island", "PrecisionPolicy", "constant_buffers", "register_constant"]

@@ -154,3 +154,41 @@ def test_input_gradients_follow_the_sample_mean_contract():
     one = _sparse_contract(0, 1)
     parts = run_ranks(_sparse_contract, 2)
     torch.testing.assert_close(torch.cat(parts), one, rtol=1e-6, atol=1e-7)
+
+
+class _WithConstant(nn.Module):
+    def __init__(self, mutate: bool):
+        super().__init__()
+        from flare_b200.training.precision import register_constant
+
+        self.lin = nn.Linear(7, 1)
+        self.mutate = mutate
+        register_constant(self, "table", torch.arange(7, dtype=torch.float32))
+
+    def forward(self, x):
+        if self.mutate:
+            self.table.add_(1.0)
+        return self.lin(x * self.table)
+
+
+def test_constant_buffers_are_checked_and_fp32_islands_stay_fp32():
+    from flare_b200.training.precision import Fp32Island, PrecisionPolicy, constant_buffers
+
+    plan = TrainingExecutionPlan.replicated()
+    x, y = _data(0, 0)
+    for mutate in (False, True):
+        m = _WithConstant(mutate)
+        assert list(constant_buffers(m)) == ["table"]
+        eng = TrainEngine(m, lambda o, t: nn.functional.binary_cross_entropy_with_logits(o, t), plan,
+                          DenseOptimizerConfig(learning_rate=0.01), device=torch.device("cpu"), validate_constants=True)
+        if mutate:
+            with pytest.raises(RuntimeError, match="constant buffer table changed"):
+                eng.micro_step_once(x, y)
+        else:
+            eng.micro_step_once(x, y)
+            assert "table" in eng.capture_checkpoint_state()["buffers"]
+    lin = nn.Linear(7, 3)
+    island = Fp32Island(lin)
+    with torch.autocast("cpu", dtype=PrecisionPolicy.bf16().compute_dtype):
+        assert lin(x).dtype == torch.bfloat16 and island(x.bfloat16()).dtype == torch.float32
+    torch.testing.assert_close(island(x), lin(x))
