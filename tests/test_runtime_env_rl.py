@@ -53,3 +53,44 @@ def test_gae_and_returns_match_loops():
         run = r[t, 1] + 0.9 * run
         want[t] = run
     np.testing.assert_allclose(rets, want, rtol=1e-5, atol=1e-6)
+
+
+def _exp(r, v=0.0, d=0.0):
+    from flare_b200.training.rl import Experience
+
+    return Experience({"x": r}, 0, r, {"x": r}, d, values=v)
+
+
+def test_replay_buffer_ring_and_prioritized_sampling():
+    import numpy as np
+
+    from flare_b200.training.rl import ReplayBuffer, ReplayBufferSpec
+
+    buf = ReplayBuffer(ReplayBufferSpec(capacity=4, batch_size=2))
+    for i in range(6):
+        buf.push(_exp(float(i)))
+    assert buf.size() == 4 and sorted(e.rewards for e in buf.items) == [2.0, 3.0, 4.0, 5.0]  # oldest overwritten
+    pb = ReplayBuffer(ReplayBufferSpec(capacity=8, batch_size=4000, prioritized=True, alpha=1.0, beta=1.0), seed=1)
+    for i in range(4):
+        pb.push(_exp(float(i)))
+    pb.update_priorities([0, 1, 2, 3], [1.0, 1.0, 1.0, 7.0])
+    ex, idx, w = pb.sample()
+    assert abs(np.mean(idx == 3) - 0.7) < 0.03  # P(3) = 7 / 10
+    assert abs(w[idx == 3][0] - 1.0 / 7.0) < 1e-6 and w.max() == 1.0  # (N P)^-beta / max (priorities + eps)
+
+
+def test_rollout_buffer_gae_matches_compute_gae():
+    import torch
+
+    from flare_b200.training.rl import RolloutBuffer, RolloutBufferSpec, compute_gae
+
+    rb = RolloutBuffer(RolloutBufferSpec(buffer_size=5, gamma=0.9, gae_lambda=0.8))
+    rs, vs, ds = [1.0, 0.0, 2.0, -1.0, 0.5], [0.2, 0.1, 0.4, 0.0, 0.3], [0.0, 0.0, 1.0, 0.0, 0.0]
+    for r, v, d in zip(rs, vs, ds):
+        rb.push(_exp(r, v, d))
+    adv, ret = rb.finish(next_value=0.25)
+    a2, r2 = compute_gae(torch.tensor(rs), torch.tensor(vs), torch.tensor(ds), 0.25, 0.9, 0.8)
+    torch.testing.assert_close(adv, a2)
+    torch.testing.assert_close(ret, r2)
+    ex, a, r = rb.sample(3)
+    assert len(ex) == 3 and a.shape == (3,)
