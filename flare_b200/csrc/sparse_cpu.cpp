@@ -17,6 +17,7 @@
 #include <ATen/Parallel.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdint>
 #include <cstring>
 #include <vector>
@@ -275,6 +276,137 @@ std::vector<py::tuple> cpu_bag_row_grads(torch::Tensor grad, torch::Tensor offse
   return res;
 }
 
+// ---- row-wise sparse optimizer on the touched rows (host) ----
+// w[rows[u]] updated from the summed gradient g[u] (fp32 math, the weights' dtype on store); the
+// optimizer state lives in full-table fp32 tensors (row: [rows], m / v: [rows, d], score: [rows]).
+enum OptKind : int { kSgd = 0, kRowAdagrad = 1, kAdam = 2, kRowAdam = 3, kAdagrad = 4 };  // sparse/config.py codes
+enum LrPolicy : int { kConst = 0, kSqrt = 1, kLog = 2, kInverse = 3, kCosine = 4, kLut = 5 };
+
+struct OptArgs {
+  int kind, policy;
+  float lr, b1, b2, eps, wd, cos_min, cos_max;
+  int64_t step;
+  std::vector<float> lut;
+};
+
+inline float lr_scale(const OptArgs& o, float score) {
+  switch (o.policy) {
+    case kSqrt: return 1.f / std::sqrt(std::max(score, 1.f));
+    case kLog: return 1.f / (1.f + std::log1p(std::max(score, 0.f)));
+    case kInverse: return 1.f / std::max(score, 1.f);
+    case kCosine: {
+      const float S = std::max(o.cos_max, 1e-12f);
+      const float x = std::min(std::max(score, 0.f), o.cos_max) / S;
+      return o.cos_min + (1.f - o.cos_min) * 0.5f * (1.f + std::cos(3.14159265358979323846f * x));
+    }
+    case kLut: {
+      const int64_t i = std::min<int64_t>(static_cast<int64_t>(std::floor(std::max(score, 0.f))),
+                                          static_cast<int64_t>(o.lut.size()) - 1);
+      return o.lut[static_cast<size_t>(i)];
+    }
+    default: return 1.f;
+  }
+}
+
+void cpu_apply_rows(int kind, int policy, std::vector<double> hp, std::vector<double> lut, int64_t step,
+                    torch::Tensor w, torch::Tensor rows, torch::Tensor g, torch::Tensor cnt, torch::Tensor row_state,
+                    torch::Tensor m, torch::Tensor v, torch::Tensor score) {
+  TORCH_CHECK(hp.size() == 7, "hyper-parameters: lr, beta1, beta2, eps, weight_decay, cos_min, cos_max");
+  OptArgs o{kind, policy, static_cast<float>(hp[0]), static_cast<float>(hp[1]), static_cast<float>(hp[2]),
+            static_cast<float>(hp[3]), static_cast<float>(hp[4]), static_cast<float>(hp[5]),
+            static_cast<float>(hp[6]), std::max<int64_t>(step, 1), {}};
+  for (double x : lut) o.lut.push_back(static_cast<float>(x));
+  TORCH_CHECK(policy != kLut || !o.lut.empty(), "custom LUT policy needs a LUT");
+  TORCH_CHECK(w.dim() == 2 && w.is_contiguous() && !w.is_cuda(), "w: contiguous 2-D CPU table");
+  TORCH_CHECK(rows.scalar_type() == torch::kInt64 && rows.is_contiguous(), "rows: contiguous int64");
+  TORCH_CHECK(g.scalar_type() == torch::kFloat32 && g.is_contiguous() && g.dim() == 2 && g.size(0) == rows.numel() &&
+                  g.size(1) == w.size(1), "g: contiguous float32 [U, d]");
+  TORCH_CHECK(cnt.scalar_type() == torch::kFloat32 && cnt.numel() == rows.numel(), "cnt: float32 [U]");
+  const bool need_row = kind == kRowAdagrad || kind == kRowAdam, need_m = kind == kAdagrad || kind == kAdam ||
+                                                                          kind == kRowAdam,
+             need_v = kind == kAdam, need_score = policy != kConst;
+  auto ok = [&](const torch::Tensor& t, bool need, bool two_d) {
+    if (!need) return;
+    TORCH_CHECK(t.defined() && t.numel() > 0 && t.scalar_type() == torch::kFloat32 && t.is_contiguous() &&
+                    t.size(0) == w.size(0) && (two_d ? t.dim() == 2 && t.size(1) == w.size(1) : t.dim() == 1),
+                "optimizer state tensor has the wrong shape / dtype");
+  };
+  ok(row_state, need_row, false);
+  ok(m, need_m, true);
+  ok(v, need_v, true);
+  ok(score, need_score, false);
+  const int64_t U = rows.numel(), d = w.size(1), R = w.size(0);
+  const int64_t* rp = rows.data_ptr<int64_t>();
+  for (int64_t u = 0; u < U; ++u) TORCH_CHECK(rp[u] >= 0 && rp[u] < R, "row ", rp[u], " outside the table");
+  const float* gp = g.data_ptr<float>();
+  const float* cp = cnt.data_ptr<float>();
+  float* rs = need_row ? row_state.data_ptr<float>() : nullptr;
+  float* mp = need_m ? m.data_ptr<float>() : nullptr;
+  float* vp = need_v ? v.data_ptr<float>() : nullptr;
+  float* sp = need_score ? score.data_ptr<float>() : nullptr;
+  void* wp = w.data_ptr();
+  const int wdt = dtype_code(w);
+  const float bc1 = 1.f - std::pow(o.b1, static_cast<float>(o.step));
+  const float bc2 = 1.f - std::pow(o.b2, static_cast<float>(o.step));
+  at::parallel_for(0, U, 64, [&](int64_t lo, int64_t hi) {
+    std::vector<float> wr(static_cast<size_t>(d)), gr(static_cast<size_t>(d));
+    for (int64_t u = lo; u < hi; ++u) {
+      const int64_t r = rp[u];
+      float g2 = 0.f;
+      for (int64_t c = 0; c < d; ++c) {
+        wr[c] = load_val(wp, wdt, r * d + c);
+        gr[c] = gp[u * d + c] + o.wd * wr[c];
+        g2 += gr[c] * gr[c];
+      }
+      g2 /= static_cast<float>(d);
+      float lr = o.lr;
+      if (sp) {
+        sp[r] += cp[u];
+        lr *= lr_scale(o, sp[r]);
+      }
+      switch (kind) {
+        case kSgd:
+          for (int64_t c = 0; c < d; ++c) wr[c] -= lr * gr[c];
+          break;
+        case kRowAdagrad: {
+          rs[r] += g2;
+          const float den = std::sqrt(rs[r]) + o.eps;
+          for (int64_t c = 0; c < d; ++c) wr[c] -= lr * gr[c] / den;
+          break;
+        }
+        case kAdagrad:
+          for (int64_t c = 0; c < d; ++c) {
+            float& acc = mp[r * d + c];
+            acc += gr[c] * gr[c];
+            wr[c] -= lr * gr[c] / (std::sqrt(acc) + o.eps);
+          }
+          break;
+        case kAdam:
+          for (int64_t c = 0; c < d; ++c) {
+            float& mm = mp[r * d + c];
+            float& vv = vp[r * d + c];
+            mm = o.b1 * mm + (1.f - o.b1) * gr[c];
+            vv = o.b2 * vv + (1.f - o.b2) * gr[c] * gr[c];
+            wr[c] -= lr * (mm / bc1) / (std::sqrt(vv / bc2) + o.eps);
+          }
+          break;
+        case kRowAdam: {
+          rs[r] = o.b2 * rs[r] + (1.f - o.b2) * g2;
+          const float den = std::sqrt(rs[r] / bc2) + o.eps;
+          for (int64_t c = 0; c < d; ++c) {
+            float& mm = mp[r * d + c];
+            mm = o.b1 * mm + (1.f - o.b1) * gr[c];
+            wr[c] -= lr * (mm / bc1) / den;
+          }
+          break;
+        }
+        default: break;
+      }
+      for (int64_t c = 0; c < d; ++c) store_val(wp, wdt, r * d + c, wr[c]);
+    }
+  });
+}
+
 }  // namespace flare_cpu
 
 void register_sparse_cpu(py::module_& m) {
@@ -286,4 +418,5 @@ void register_sparse_cpu(py::module_& m) {
   c.def("unique_first", &flare_cpu::cpu_unique_first);
   c.def("bag_pool", &flare_cpu::cpu_bag_pool);
   c.def("bag_row_grads", &flare_cpu::cpu_bag_row_grads);
+  c.def("apply_rows", &flare_cpu::cpu_apply_rows);
 }

@@ -146,9 +146,9 @@ class CpuEmbeddingBagCollection:
         self._offsets = None
         self._values = None
         self.stores = None
-        # native: pooling and per-row gradient sums in the host C++ ops (parallel over bags / tables,
-        # fp32, each row adds its occurrences in order) instead of tensor ops; the tensor-op path stays
-        # the plain-PyTorch oracle of the GPU kernels
+        # native: pooling, per-row gradient sums and the row-wise optimizer in the host C++ ops
+        # (parallel over bags / tables / rows, fp32, each row adds its occurrences in order) instead of
+        # tensor ops; the tensor-op path stays the plain-PyTorch oracle of the GPU kernels
         self.native = bool(native)
         if storage is not None:
             self._init_paged(storage, seed, weights)
@@ -202,8 +202,22 @@ class CpuEmbeddingBagCollection:
         for f, (rows, g, cnt) in enumerate(self._row_gradients(grad_pooled)):
             if self.stores is not None:
                 self._apply_paged(f, rows, g, cnt)
+            elif self.native:
+                self._apply_native(f, rows, g, cnt)
             else:
                 apply_rows_reference(self.optimizer, self.step, self.weights[f], rows, g, cnt, self.state[f])
+
+    def _apply_native(self, f: int, rows: torch.Tensor, g: torch.Tensor, cnt: torch.Tensor) -> None:
+        from .._native import native
+        from .config import LR_POLICIES, OPTIMIZER_KINDS
+
+        opt, st, none = self.optimizer, self.state[f], torch.empty(0)
+        native().cpu.apply_rows(OPTIMIZER_KINDS[opt.kind], LR_POLICIES[opt.dynamic_lr_policy],
+                                [opt.learning_rate, opt.beta1, opt.beta2, opt.eps, opt.weight_decay,
+                                 opt.cosine_min_lr_ratio, opt.cosine_max_score], list(opt.custom_lut), self.step,
+                                self.weights[f], rows.long().contiguous(), g.float().contiguous(),
+                                cnt.float().contiguous(), st.get("row", none), st.get("m", none), st.get("v", none),
+                                st.get("score", none))
 
     # ------------------------------------------------------------ paged storage
     def _layout(self, t: SparseTableSpec) -> list[tuple[str, int]]:

@@ -35,6 +35,6 @@ def test_cpu_recipe_with_paged_tables_trains_identically(tmp_path):
     from flare_b200.sparse.storage import SparseStorageOptions
 
     opts = SparseStorageOptions(memory_limit_bytes=64 * 1024, spill_directory=str(tmp_path), entries_per_page=4096)
-    a = train_small_cpu(steps=20, batch_size=64)
+    a = train_small_cpu(steps=20, batch_size=64, native=False)  # the paged tables use the tensor-op optimizer
     b = train_small_cpu(steps=20, batch_size=64, storage=opts)
     assert a.losses == b.losses

@@ -201,3 +201,46 @@ def test_native_collection_ops_match_the_tensor_oracle():
         torch.testing.assert_close(ys[1], ys[0], rtol=1e-6, atol=1e-6)
     for a, b in zip(plain.weights, fast.weights):
         torch.testing.assert_close(b.float(), a.float(), rtol=1e-5, atol=1e-6)
+
+
+def test_native_row_optimizer_matches_reference_for_every_kind_and_policy():
+    import itertools
+
+    import torch
+
+    from flare_b200._native import native
+    from flare_b200.sparse.config import LR_POLICIES, OPTIMIZER_KINDS, SparseOptimizerConfig
+    from flare_b200.sparse.reference import apply_rows_reference
+
+    g0 = torch.Generator().manual_seed(0)
+    for kind, policy in itertools.product(OPTIMIZER_KINDS, LR_POLICIES):
+        opt = SparseOptimizerConfig(kind=kind, learning_rate=0.05, weight_decay=0.01, dynamic_lr_policy=policy,
+                                    cosine_max_score=6.0, cosine_min_lr_ratio=0.2,
+                                    custom_lut=(1.0, 0.5, 0.25) if policy == "custom_lut" else ())
+        R, d = 20, 8
+        w0 = torch.randn(R, d, generator=g0)
+        st0 = {}
+        if opt.needs_row_state:
+            st0["row"] = torch.rand(R, generator=g0)
+        if opt.needs_m:
+            st0["m"] = torch.rand(R, d, generator=g0)
+        if opt.needs_v:
+            st0["v"] = torch.rand(R, d, generator=g0)
+        if opt.needs_score:
+            st0["score"] = torch.rand(R, generator=g0) * 3
+        rows = torch.tensor([0, 3, 7, 19])
+        g = torch.randn(4, d, generator=g0)
+        cnt = torch.tensor([1.0, 3.0, 2.0, 5.0])
+        for step in (1, 4):
+            wa, sa = w0.clone(), {k: v.clone() for k, v in st0.items()}
+            wb, sb = w0.clone(), {k: v.clone() for k, v in st0.items()}
+            apply_rows_reference(opt, step, wa, rows, g, cnt, sa)
+            e = torch.empty(0)
+            native().cpu.apply_rows(OPTIMIZER_KINDS[kind], LR_POLICIES[policy],
+                                    [opt.learning_rate, opt.beta1, opt.beta2, opt.eps, opt.weight_decay,
+                                     opt.cosine_min_lr_ratio, opt.cosine_max_score], list(opt.custom_lut), step,
+                                    wb, rows, g, cnt, sb.get("row", e), sb.get("m", e), sb.get("v", e),
+                                    sb.get("score", e))
+            torch.testing.assert_close(wb, wa, rtol=1e-5, atol=1e-6, msg=f"{kind}/{policy}/step {step}")
+            for k in sa:
+                torch.testing.assert_close(sb[k], sa[k], rtol=1e-5, atol=1e-6, msg=f"{kind}/{policy} {k}")
