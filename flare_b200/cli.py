@@ -55,6 +55,8 @@ def _parser() -> argparse.ArgumentParser:
     e.add_argument("--max-bag", type=int, default=64)
     e.add_argument("--data", default=None)
     e.add_argument("--seed", type=int, default=12345)
+    e.add_argument("--gauc-feature", type=int, default=None,
+                   help="also report GAUC, grouping samples by the first id of this sparse feature (e.g. a user id)")
     return p
 
 
@@ -153,7 +155,7 @@ def train(args) -> int:
 def evaluate(args) -> int:
     from .checkpoint.inference import bind_inference_weights
     from .checkpoint.store import latest_step
-    from .metrics.ranking import auc, calibration
+    from .metrics.ranking import auc, calibration, gauc
     from .models.dlrm import DLRM
 
     dev = torch.device("cuda", torch.cuda.current_device())
@@ -166,18 +168,36 @@ def evaluate(args) -> int:
     w.load_model(model.dense)
     w.load_sparse(model.emb)
     data = _batches(args, cfg, args.batch, 0, 1, dev)
-    scores, labels = [], []
+    scores, labels, groups = [], [], []
     for _ in range(args.batches):
         b = next(data)
         model.set_batch(b.dense.to(dev), b.labels.to(dev), b.offsets.to(dev), b.values.to(dev), non_blocking=False)
         scores.append(model.predict()[:, 0].clone())
         labels.append(model.labels[:, 0].clone())
+        if args.gauc_feature is not None:
+            groups.append(group_ids(b.offsets, b.values, args.gauc_feature, args.batch).to(dev))
     model.check()
     s, y = torch.cat(scores), torch.cat(labels)
     w.verify()
-    print(json.dumps({"step": step, "samples": int(s.numel()), "auc": auc(s, y), "calibration": calibration(s, y)}),
-          flush=True)
+    out = {"step": step, "samples": int(s.numel()), "auc": auc(s, y), "calibration": calibration(s, y)}
+    if groups:
+        g = torch.cat(groups)
+        keep = g >= 0
+        out["gauc"] = gauc(s[keep], y[keep], g[keep])
+    print("[MetricsAggregator] " + " ".join(f"{k}={v:.6g}" if isinstance(v, float) else f"{k}={v}"
+                                             for k, v in out.items()), flush=True)
+    print(json.dumps(out), flush=True)
     return 0
+
+
+def group_ids(offsets: torch.Tensor, values: torch.Tensor, feature: int, batch: int) -> torch.Tensor:
+    """Per sample: the first id of its bag of sparse ``feature`` (-1 for an empty bag)."""
+    offs = offsets.long().cpu()
+    vals = values.long().cpu()
+    start = offs[feature * batch:(feature + 1) * batch]
+    lens = offs[feature * batch + 1:(feature + 1) * batch + 1] - start
+    first = vals[start.clamp(max=max(vals.numel() - 1, 0))] if vals.numel() else torch.zeros_like(start)
+    return torch.where(lens > 0, first, torch.full_like(first, -1))
 
 
 def main(argv=None) -> int:

@@ -29,6 +29,8 @@ def test_train_resume_eval(tmp_path, capsys):
     lines = (tmp_path / "m.jsonl").read_text().strip().splitlines()
     assert len(lines) >= 3 and "train/auc_ctr" in lines[0]
     assert cli.main(["eval", "--model-config", m, "--checkpoint-dir", ck, "--batch", "512", "--batches", "4",
-                     "--max-bag", "8"]) == 0
-    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+                     "--max-bag", "8", "--gauc-feature", "0"]) == 0
+    out = capsys.readouterr().out.strip().splitlines()
+    res = json.loads(out[-1])
     assert res["step"] == 15 and res["samples"] == 2048 and 0.0 <= res["auc"] <= 1.0
+    assert out[-2].startswith("[MetricsAggregator] ") and isinstance(res["gauc"], float)

@@ -88,3 +88,15 @@ def test_parse_group_counts():
                      ("users:x", "positive")]:
         with pytest.raises(ValueError, match=msg):
             parse_group_counts(bad, g)
+
+
+def test_cli_group_ids_first_id_of_a_feature():
+    import torch
+
+    from flare_b200.cli import group_ids
+
+    # 2 features x 3 samples: feature 1 bags = [7, 8], [], [9]
+    offs = torch.tensor([0, 1, 2, 3, 5, 5, 6], dtype=torch.int32)
+    vals = torch.tensor([1, 2, 3, 7, 8, 9], dtype=torch.int32)
+    assert group_ids(offs, vals, 1, 3).tolist() == [7, -1, 9]
+    assert group_ids(offs, vals, 0, 3).tolist() == [1, 2, 3]
