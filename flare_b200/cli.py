@@ -45,7 +45,8 @@ def _parser() -> argparse.ArgumentParser:
     t.add_argument("--no-graph", action="store_true")
     t.add_argument("--table-shards", default="",
                    help='row-wise pieces per table: "4" (every table) or "t0:4,t3:2" (the rest keep their config)')
-    t.add_argument("--sparse-policy", choices=["sync", "pipelined"], default="sync")
+    t.add_argument("--sparse-policy", choices=["sync", "pipelined"], default=None,
+                   help="default: pipelined when every table allows max_staleness_steps >= 1, else sync")
     e = sub.add_parser("eval")
     e.add_argument("--model-config", required=True)
     e.add_argument("--checkpoint-dir", required=True)

@@ -11,7 +11,8 @@ captured in a CUDA graph:
     bottom MLP backward -> sharded embedding backward (grad all-to-all + dedup + row-wise optimizer)
     dense optimizer (fused reduce-scatter + Adam + all-gather when data parallel)
 
-With ``sparse_policy="pipelined"`` the sparse update of step t-1 runs in the
+With ``sparse_policy="pipelined"`` (the default when every table's
+``max_staleness_steps`` is at least 1) the sparse update of step t-1 runs in the
 shadow of step t's dense work: a side stream carries every kernel that waits
 on the other ranks (embedding forward of step t, embedding backward of step
 t-1, the dense update) in the same order on every rank, while the main stream
@@ -108,7 +109,10 @@ class DLRM:
                  device: torch.device | None = None, heap: SymmetricHeap | None = None, seed: int = 0,
                  global_batch_size: int | None = None, values_capacity: int | None = None,
                  table_costs: list[float] | None = None, plan: ShardingPlan | None = None,
-                 sparse_policy: str = "sync"):
+                 sparse_policy: str | None = None):
+        if sparse_policy is None:  # from the tables: a staleness bound of >= 1 step everywhere allows the overlap
+            stale = [t.max_staleness_steps for t in cfg.tables]
+            sparse_policy = "pipelined" if stale and min(stale) >= 1 else "sync"
         if sparse_policy not in ("sync", "pipelined"):
             raise ValueError(f"sparse_policy must be 'sync' or 'pipelined', not {sparse_policy!r}")
         self.cfg = cfg

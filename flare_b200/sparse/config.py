@@ -107,7 +107,7 @@ class SparseTableSpec:
     optimizer: SparseOptimizerConfig = field(default_factory=SparseOptimizerConfig)
     init_scale: float = 0.01
     shards: int = 1                # > 1: row-wise pieces by key modulo (piece r holds rows i % shards == r)
-    max_staleness_steps: int = 0
+    max_staleness_steps: int = 0   # lookups may miss this many recent updates (>= 1 everywhere: pipelined step)
     cache_rows: int | None = None  # host-DRAM tier: rows live in pinned host memory, this many in an HBM cache
     dynamic: bool = False          # hash-keyed: any int32 key >= 0, num_embeddings slots, insert on first sight
     hash_buckets: int | None = None  # dynamic: power-of-two hash buckets (default 4 x slots rounded up)
@@ -134,6 +134,8 @@ class SparseTableSpec:
                 raise ValueError("host-tier tables store fp32 rows")
         if self.pooling not in ("sum", "mean"):
             raise ValueError(f"unsupported pooling {self.pooling!r}")
+        if isinstance(self.max_staleness_steps, bool) or self.max_staleness_steps < 0:
+            raise ValueError(f"max_staleness_steps must be non-negative, got {self.max_staleness_steps}")
 
     @property
     def feature_name(self) -> str:

@@ -203,18 +203,25 @@ class FusedTrainer:
         torch.cuda.synchronize(self.device)
 
 
+def _pipelined(cfg: DLRMConfig, sparse_policy: str | None) -> bool:
+    if sparse_policy is not None:
+        return sparse_policy == "pipelined"
+    stale = [t.max_staleness_steps for t in cfg.tables]
+    return bool(stale) and min(stale) >= 1
+
+
 class DLRMTrainer(FusedTrainer):
     def __init__(self, cfg: DLRMConfig, batch_size: int, *, max_bag_size: int, rank: int = 0, world_size: int = 1,
                  device: torch.device | None = None, seed: int = 0, use_graph: bool = True,
                  values_capacity: int | None = None, heap_bytes: int | None = None,
-                 table_costs: list[float] | None = None, row_split: bool = False, sparse_policy: str = "sync"):
+                 table_costs: list[float] | None = None, row_split: bool = False, sparse_policy: str | None = None):
         device = device or torch.device("cuda", torch.cuda.current_device())
         heap = None
         plan = dlrm_plan(cfg, world_size, table_costs, row_split=row_split)
         if world_size > 1:
             exchange = ShardedEmbeddingBagCollection.exchange_bytes(cfg.tables, batch_size, max_bag_size,
                                                                     values_capacity, plan=plan,
-                                                                    pipelined=sparse_policy == "pipelined")
+                                                                    pipelined=_pipelined(cfg, sparse_policy))
             dense = 6 * 16 * 1024 * 1024  # flat fp32 grads + bf16 params for up to 16M parameters
             need = heap_bytes or (exchange + dense + 64 * 1024 * 1024)
             heap = SymmetricHeap(need, rank=rank, world_size=world_size, device=device)

@@ -244,3 +244,13 @@ def test_native_row_optimizer_matches_reference_for_every_kind_and_policy():
             torch.testing.assert_close(wb, wa, rtol=1e-5, atol=1e-6, msg=f"{kind}/{policy}/step {step}")
             for k in sa:
                 torch.testing.assert_close(sb[k], sa[k], rtol=1e-5, atol=1e-6, msg=f"{kind}/{policy} {k}")
+
+
+def test_staleness_bound_validation():
+    import pytest
+
+    from flare_b200.sparse.config import SparseTableSpec
+
+    with pytest.raises(ValueError, match="max_staleness_steps"):
+        SparseTableSpec("a", 10, 8, max_staleness_steps=-1)
+    assert SparseTableSpec("a", 10, 8, max_staleness_steps=2).max_staleness_steps == 2
