@@ -112,11 +112,13 @@ flare::AdamParams parse_adam(const py::dict& d) {
 void register_etl(py::module_& m);
 void register_sparse_cpu(py::module_& m);
 void register_paged_store(py::module_& m);
+void register_dyn_map(py::module_& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_etl(m);
   register_sparse_cpu(m);
   register_paged_store(m);
+  register_dyn_map(m);
   m.doc() = "flare_b200 native kernels (sm_100a)";
 
   m.def("device_sm_count", &flare::device_sm_count);

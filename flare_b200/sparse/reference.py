@@ -150,6 +150,14 @@ class CpuEmbeddingBagCollection:
         # (parallel over bags / tables / rows, fp32, each row adds its occurrences in order) instead of
         # tensor ops; the tensor-op path stays the plain-PyTorch oracle of the GPU kernels
         self.native = bool(native)
+        # hash-keyed tables: any int64 key; a native key -> slot map inserts on first sight (LFU eviction
+        # when full) and the table's rows are indexed by slot
+        self.maps = {}
+        self._init_gen = torch.Generator().manual_seed(seed * 1_000_003 + 17)
+        if any(t.dynamic for t in self.tables):
+            from .._native import native as _nat
+
+            self.maps = {f: _nat().DynamicKeyMap(t.num_embeddings) for f, t in enumerate(self.tables) if t.dynamic}
         if storage is not None:
             self._init_paged(storage, seed, weights)
             return
@@ -174,11 +182,43 @@ class CpuEmbeddingBagCollection:
 
     def set_input(self, offsets: torch.Tensor, values: torch.Tensor, non_blocking: bool = False) -> None:
         self._offsets, self._values = offsets.cpu(), values.cpu()
+        self._keys = self._values  # the batch's ids as given (dynamic tables: keys, translated in forward)
+
+    def _translate(self, training: bool) -> None:
+        """Dynamic tables: keys -> slots (training lookups insert and re-initialise the new slots' rows)."""
+        if not self.maps:
+            return
+        vals = self._keys.to(torch.int64).clone()
+        offs, B = self._offsets.long(), self.B
+        for f, m in self.maps.items():
+            lo, hi = int(offs[f * B]), int(offs[(f + 1) * B])
+            slots, new, _evicted = m.lookup(vals[lo:hi].contiguous(), training)
+            vals[lo:hi] = slots
+            if new.numel():
+                self._init_rows(f, new)
+        self._values = vals.to(torch.int32)
+
+    def _init_rows(self, f: int, rows: torch.Tensor) -> None:
+        t = self.tables[f]
+        w = (torch.rand(rows.numel(), t.embedding_dim, generator=self._init_gen) * 2 - 1) * t.init_scale
+        if self.stores is not None:
+            rec = torch.zeros(rows.numel(), sum(wd for _, wd in self.layouts[f]))
+            rec[:, :t.embedding_dim] = w
+            self.stores[f].scatter(rows, rec)
+            return
+        self.weights[f][rows] = w.to(self.weights[f].dtype)
+        for v in self.state[f].values():
+            v[rows] = 0
+
+    def dynamic_items(self, f: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """(keys, slots, use counts) of dynamic table f's occupied slots."""
+        return self.maps[f].items()
 
     def _mean_flags(self) -> list[int]:
         return [1 if t.pooling == "mean" else 0 for t in self.tables]
 
-    def forward(self) -> torch.Tensor:
+    def forward(self, training: bool = True) -> torch.Tensor:
+        self._translate(training)
         if self.stores is not None:
             return self._forward_paged()
         if self.native:
