@@ -122,28 +122,30 @@ class DynamicKeyMap {
   int64_t size() const { return static_cast<int64_t>(map_.size()); }
   int64_t capacity() const { return cap_; }
 
-  // (keys, slots, uses) of every occupied slot, by slot
+  // (keys, slots, uses, last-use batch) of every occupied slot, by slot
   py::tuple items() const {
-    std::vector<int64_t> ks, ss, us;
+    std::vector<int64_t> ks, ss, us, ls;
     for (int64_t s = 0; s < cap_; ++s)
       if (slot_key_[s] >= 0) {
         ks.push_back(slot_key_[s]);
         ss.push_back(s);
         us.push_back(static_cast<int64_t>(uses_[s]));
+        ls.push_back(static_cast<int64_t>(last_[s]));
       }
     auto vec = [](const std::vector<int64_t>& v) {
       auto t = torch::empty({static_cast<int64_t>(v.size())}, torch::kInt64);
       std::copy(v.begin(), v.end(), t.data_ptr<int64_t>());
       return t;
     };
-    return py::make_tuple(vec(ks), vec(ss), vec(us));
+    return py::make_tuple(vec(ks), vec(ss), vec(us), vec(ls));
   }
 
-  // rebuild from items() output (restore)
-  void load(torch::Tensor keys, torch::Tensor slots, torch::Tensor uses) {
-    TORCH_CHECK(keys.numel() == slots.numel() && keys.numel() == uses.numel(), "items must align");
+  // rebuild from items() output (restore); the batch counter resumes after the latest last-use
+  void load(torch::Tensor keys, torch::Tensor slots, torch::Tensor uses, torch::Tensor last) {
+    TORCH_CHECK(keys.numel() == slots.numel() && keys.numel() == uses.numel() && keys.numel() == last.numel(),
+                "items must align");
     auto k = keys.to(torch::kInt64).contiguous(), s = slots.to(torch::kInt64).contiguous(),
-         u = uses.to(torch::kInt64).contiguous();
+         u = uses.to(torch::kInt64).contiguous(), l = last.to(torch::kInt64).contiguous();
     std::fill(slot_key_.begin(), slot_key_.end(), -1);
     std::fill(uses_.begin(), uses_.end(), 0);
     std::fill(last_.begin(), last_.end(), 0);
@@ -153,6 +155,8 @@ class DynamicKeyMap {
       TORCH_CHECK(sl >= 0 && sl < cap_ && slot_key_[sl] < 0, "bad or repeated slot ", sl);
       slot_key_[sl] = k.data_ptr<int64_t>()[i];
       uses_[sl] = static_cast<uint64_t>(u.data_ptr<int64_t>()[i]);
+      last_[sl] = static_cast<uint64_t>(l.data_ptr<int64_t>()[i]);
+      batch_ = std::max(batch_, last_[sl]);
       map_[slot_key_[sl]] = sl;
     }
     free_.clear();

@@ -212,7 +212,7 @@ class CpuEmbeddingBagCollection:
 
     def dynamic_items(self, f: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
         """(keys, slots, use counts) of dynamic table f's occupied slots."""
-        return self.maps[f].items()
+        return self.maps[f].items()[:3]
 
     def _mean_flags(self) -> list[int]:
         return [1 if t.pooling == "mean" else 0 for t in self.tables]
@@ -339,6 +339,40 @@ class CpuEmbeddingBagCollection:
             return self.weights[f]
         t = self.tables[f]
         return self._split(f, self.stores[f].gather(torch.arange(t.num_embeddings)))["weight"].clone()
+
+    # ------------------------------------------------------------ checkpoint state
+    def state_dict(self) -> dict:
+        """Step, every table's weights and optimizer state (by table name), dynamic tables' key maps."""
+        tables = {}
+        for f, t in enumerate(self.tables):
+            if self.stores is not None:
+                parts = self._split(f, self.stores[f].gather(torch.arange(t.num_embeddings)))
+                tables[t.name] = {k: v.clone() for k, v in parts.items()}
+            else:
+                tables[t.name] = {"weight": self.weights[f].clone(), **{k: v.clone() for k, v in self.state[f].items()}}
+        dynamic = {self.tables[f].name: tuple(x.clone() for x in m.items()) for f, m in self.maps.items()}
+        return {"step": self.step, "optimizer": self.optimizer.kind, "tables": tables, "dynamic": dynamic,
+                "init_rng": self._init_gen.get_state()}  # rows of keys inserted later draw from it
+
+    def load_state_dict(self, state: dict) -> None:
+        if state.get("optimizer", self.optimizer.kind) != self.optimizer.kind:
+            raise ValueError(f"checkpoint optimizer {state['optimizer']!r} is not {self.optimizer.kind!r}")
+        for f, t in enumerate(self.tables):
+            if t.name not in state["tables"]:
+                raise ValueError(f"table {t.name} is not in the checkpoint")
+            st = state["tables"][t.name]
+            if self.stores is not None:
+                rec = torch.cat([st[n].float().reshape(t.num_embeddings, -1) for n, _ in self.layouts[f]], 1)
+                self.stores[f].scatter(torch.arange(t.num_embeddings), rec)
+            else:
+                self.weights[f].copy_(st["weight"].to(self.weights[f].dtype))
+                for k, v in self.state[f].items():
+                    v.copy_(st[k])
+        for f, m in self.maps.items():
+            m.load(*state["dynamic"][self.tables[f].name])
+        if "init_rng" in state:
+            self._init_gen.set_state(state["init_rng"])
+        self.step = int(state["step"])
 
     def storage_stats(self) -> list[dict]:
         return [s.stats() for s in self.stores] if self.stores is not None else []

@@ -69,3 +69,41 @@ def test_dynamic_table_on_paged_storage(tmp_path):
     keys, slots, uses = c.dynamic_items(0)
     assert sorted(keys.tolist()) == [5, 123456789] and sorted(uses.tolist()) == [1, 2]
     assert y.abs().max() <= 2 * t.init_scale + 1e-6
+
+
+@pytest.mark.parametrize("paged", [False, True])
+def test_cpu_collection_state_round_trip_resumes_identically(tmp_path, paged):
+    from flare_b200.sparse.storage import SparseStorageOptions
+
+    opt = SparseOptimizerConfig(kind="adam", learning_rate=0.05)
+    # 8 slots for 12 distinct keys: the resumed run must evict exactly as the original
+    tables = [SparseTableSpec("d", 8, 8, dynamic=True, optimizer=opt), SparseTableSpec("s", 50, 4, optimizer=opt)]
+    B = 4
+    mk = lambda: CpuEmbeddingBagCollection(  # noqa: E731
+        tables, B, optimizer=opt, seed=2,
+        storage=SparseStorageOptions(memory_limit_bytes=4096 * 64, spill_directory=str(tmp_path)) if paged else None)
+    g = torch.Generator().manual_seed(0)
+
+    def batch():
+        lens = torch.randint(1, 3, (2 * B,), generator=g)
+        offs = torch.cat([torch.zeros(1, dtype=torch.long), lens.cumsum(0)]).int()
+        vals = torch.cat([torch.randint(0, 10**9, (int(lens[:B].sum()),), generator=g) % 12 * 7919,
+                          torch.randint(0, 50, (int(lens[B:].sum()),), generator=g)]).int()
+        return offs, vals
+
+    def step(c, b):
+        c.set_input(*b)
+        y = c.forward()
+        c.backward(torch.cos(y))
+        return y
+
+    a = mk()
+    for _ in range(3):
+        step(a, batch())
+    state = a.state_dict()
+    b = mk()
+    b.load_state_dict(state)
+    for _ in range(3):
+        nb = batch()
+        torch.testing.assert_close(step(b, nb), step(a, nb), rtol=0, atol=0)
+    assert b.state_dict()["step"] == a.state_dict()["step"] == 6
