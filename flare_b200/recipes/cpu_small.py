@@ -67,10 +67,14 @@ def small_tables(opt: SparseOptimizerConfig | None = None) -> list[SparseTableSp
 
 
 def train_small_cpu(steps: int = 200, batch_size: int = 256, seed: int = 0, storage=None,
-                    native: bool = True) -> SmallRunResult:
+                    native: bool = True, checkpoint_dir: str | None = None, save_every: int = 0,
+                    resume: bool = False) -> SmallRunResult:
     """``storage`` (``SparseStorageOptions``): keep the tables in the paged store (memory limit, disk
     spill), starting from the same initial rows as the in-memory run.  ``native``: pool and reduce
-    the sparse gradients with the host C++ ops (the tensor-op path otherwise)."""
+    the sparse gradients with the host C++ ops (the tensor-op path otherwise).  ``checkpoint_dir``:
+    save every ``save_every`` steps (``checkpoint.cpu``); ``resume`` continues from the latest
+    complete step (the synthetic stream skips the batches already trained on), so ``steps`` counts
+    the steps of this call."""
     torch.manual_seed(seed)
     data = SmallSyntheticData(batch_size, seed=seed)
     emb = CpuEmbeddingBagCollection(small_tables(), batch_size, seed=seed, native=native)
@@ -80,15 +84,28 @@ def train_small_cpu(steps: int = 200, batch_size: int = 256, seed: int = 0, stor
     engine = TrainEngine(model, lambda out, y: nn.functional.binary_cross_entropy_with_logits(out, y),
                          TrainingExecutionPlan.replicated(), DenseOptimizerConfig(kind="adam", learning_rate=1e-3),
                          device=torch.device("cpu"))
+    start = 0
+    if resume and checkpoint_dir is not None:
+        from ..checkpoint.cpu import restore_cpu
+        from ..checkpoint.store import latest_step
+
+        if latest_step(checkpoint_dir) is not None:
+            start = restore_cpu(checkpoint_dir, engine, emb)
+            for _ in range(start):
+                data.next()
     losses = []
     t0 = time.perf_counter()
-    for _ in range(steps):
+    for step in range(start + 1, start + steps + 1):
         b = data.next()
         emb.set_input(b.offsets, b.values)
         pooled = emb.forward().requires_grad_(True)
         res = engine.micro_step_once((b.dense, pooled), b.labels)
         emb.backward(engine.input_gradients({"pooled": pooled})["pooled"])
         losses.append(float(res.loss))
+        if checkpoint_dir is not None and save_every and step % save_every == 0:
+            from ..checkpoint.cpu import save_cpu
+
+            save_cpu(checkpoint_dir, step, engine, emb)
     dt = time.perf_counter() - t0
     return SmallRunResult(losses, steps * batch_size / dt, steps)
 

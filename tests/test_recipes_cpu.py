@@ -38,3 +38,13 @@ def test_cpu_recipe_with_paged_tables_trains_identically(tmp_path):
     a = train_small_cpu(steps=20, batch_size=64, native=False)  # the paged tables use the tensor-op optimizer
     b = train_small_cpu(steps=20, batch_size=64, storage=opts)
     assert a.losses == b.losses
+
+
+def test_cpu_recipe_checkpoint_resume_matches_an_uninterrupted_run(tmp_path):
+    from flare_b200.checkpoint.store import list_steps
+
+    full = train_small_cpu(steps=12, batch_size=32)
+    first = train_small_cpu(steps=6, batch_size=32, checkpoint_dir=str(tmp_path), save_every=3)
+    assert list_steps(tmp_path) == [3, 6] and first.losses == full.losses[:6]
+    second = train_small_cpu(steps=6, batch_size=32, checkpoint_dir=str(tmp_path), resume=True)
+    assert second.losses == full.losses[6:]
