@@ -145,4 +145,40 @@ def train_small_oracle(steps: int = 200, batch_size: int = 256, seed: int = 0) -
     return losses
 
 
-__all__ = ["SmallDense", "SmallRunResult", "small_tables", "train_small_cpu", "train_small_oracle"]
+def main(argv=None) -> int:
+    """``python -m flare_b200.recipes.cpu_small [--steps N] [--batch B] [--checkpoint-dir D --save-every K]
+    [--resume] [--memory-limit BYTES --spill-dir DIR] [--tensor-ops]``: one JSON line (samples/s, losses)."""
+    import argparse
+    import json
+
+    p = argparse.ArgumentParser(prog="flare_b200.recipes.cpu_small")
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--batch", type=int, default=256)
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--checkpoint-dir", default=None)
+    p.add_argument("--save-every", type=int, default=0)
+    p.add_argument("--resume", action="store_true")
+    p.add_argument("--memory-limit", type=int, default=None, help="sparse storage memory limit (bytes)")
+    p.add_argument("--spill-dir", default=None)
+    p.add_argument("--tensor-ops", action="store_true", help="tensor-op sparse step instead of the native one")
+    a = p.parse_args(argv)
+    storage = None
+    if a.memory_limit is not None or a.spill_dir is not None:
+        from ..sparse.storage import SparseStorageOptions
+
+        storage = SparseStorageOptions(memory_limit_bytes=a.memory_limit, spill_directory=a.spill_dir)
+    r = train_small_cpu(a.steps, a.batch, a.seed, storage=storage, native=not a.tensor_ops,
+                        checkpoint_dir=a.checkpoint_dir, save_every=a.save_every, resume=a.resume)
+    print(json.dumps({"metric": "train samples/s", "value": r.samples_per_s, "steps": r.steps,
+                      "first_loss": r.losses[0] if r.losses else None, "last_loss": r.losses[-1] if r.losses else None,
+                      "config": {"batch": a.batch, "tables": 8, "rows_per_table": 1000, "dim": 16,
+                                 "sparse_step": "tensor ops" if a.tensor_ops else "native C++",
+                                 "storage": "paged" if storage else "in memory"}}), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
+
+
+__all__ = ["SmallDense", "SmallRunResult", "main", "small_tables", "train_small_cpu", "train_small_oracle"]
