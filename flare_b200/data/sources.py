@@ -310,8 +310,64 @@ def stream_batches(factory: SourceFactory, batch_size: int, *, policy: str = "ca
         session.close()
 
 
+class ParquetRangeBatchLoader:
+    """Standalone loader: static Parquet ranges of one shard -> fixed-size batches -> a caller's transform.
+
+    ``dataset_path`` is a file or a directory of ``*.parquet`` files; ``projection`` the columns to
+    read; work items (row-group ranges) are dealt to shards (item k to shard k % shard_count); every
+    epoch reads this shard's items in order and yields ``batch_transformer(table)`` for each batch of
+    ``batch_size`` rows, the last one padded with a validity prefix (``policy="pad"``; ``"drop"`` drops
+    it, ``"carry"`` carries rows into the next epoch's first batch).  Reference behaviour:
+    src/flare/data/pipeline/consumption/dataloader/parquet.py:11-90 (same arguments).
+    """
+
+    def __init__(self, *, dataset_path: str, projection: Sequence[str], batch_size: int,
+                 batch_transformer: Callable[[Any], Any], shard_index: int = 0, shard_count: int = 1,
+                 num_epochs: int = 1, policy: str = "pad", rows_per_item: int | None = None):
+        if not isinstance(dataset_path, str) or not dataset_path:
+            raise ValueError("dataset_path must be a non-empty string")
+        if not projection:
+            raise ValueError("projection must not be empty")
+        if isinstance(batch_size, bool) or not isinstance(batch_size, int) or batch_size <= 0:
+            raise ValueError("batch_size must be a positive integer")
+        if not callable(batch_transformer):
+            raise TypeError("batch_transformer must be callable")
+        for v, n in ((shard_index, "shard_index"), (shard_count, "shard_count"), (num_epochs, "num_epochs")):
+            if isinstance(v, bool) or not isinstance(v, int) or v < 0:
+                raise ValueError(f"{n} must be a non-negative integer")
+        if shard_count < 1 or shard_index >= shard_count:
+            raise ValueError("shard_index must be in [0, shard_count)")
+        if os.path.isdir(dataset_path):
+            paths = sorted(os.path.join(dataset_path, f) for f in os.listdir(dataset_path) if f.endswith(".parquet"))
+        else:
+            paths = [dataset_path]
+        if not paths:
+            raise ValueError(f"no Parquet files under {dataset_path}")
+        self.factory = ParquetSourceFactory(paths, columns=list(projection), rows_per_item=rows_per_item)
+        self.items = [it for k, it in enumerate(self.factory.plan()) if k % shard_count == shard_index]
+        self.batch_size, self.transform, self.num_epochs, self.policy = batch_size, batch_transformer, num_epochs, policy
+        self.last_validity: BatchValidity | None = None
+
+    def __iter__(self) -> Iterator[Any]:
+        session = self.factory.create_session()
+        asm = BatchAssembler(self.batch_size, self.policy)
+        try:
+            for epoch in range(self.num_epochs):
+                for item in self.items:
+                    for ab in asm.push(session.read(item)):
+                        self.last_validity = ab.validity
+                        yield self.transform(ab.data)
+                if self.policy != "carry" or epoch == self.num_epochs - 1:
+                    for ab in asm.finish():
+                        self.last_validity = ab.validity  # a padded batch's valid prefix
+                        yield self.transform(ab.data)
+        finally:
+            session.close()
+
+
 __all__ = [
-    "AssembledBatch", "BatchAssembler", "BatchValidity", "CompletionPolicy", "ParquetSourceFactory", "RecordRange",
+    "AssembledBatch", "BatchAssembler", "BatchValidity", "CompletionPolicy", "ParquetRangeBatchLoader",
+    "ParquetSourceFactory", "RecordRange",
     "RecordRangeReadSession", "SourceFactory", "SourceReadSession", "StandardSourceFactory", "WorkItem",
     "coalesce_source_ranges", "stream_batches",
 ]

@@ -93,3 +93,26 @@ def test_reconcile_reader_audits(tmp_path):
     assert not rep["ok"] and rep["duplicated"] == [audits[1]["done"][0]]
     assert rep["missing"] == sorted(audits[2]["done"]) and not rep["ranks_complete"]
     assert main([str(tmp_path / f"a{r}.json") for r in range(3)] + ["--items", "12", "--rows", "300"]) == 0
+
+
+def test_parquet_range_batch_loader_shards_epochs_and_tail(tmp_path):
+    from flare_b200.data.sources import ParquetRangeBatchLoader
+
+    d = tmp_path / "ds"
+    d.mkdir()
+    for f in range(2):
+        pq.write_table(pa.table({"x": list(range(f * 100, f * 100 + 100)), "y": [0] * 100}), d / f"p{f}.parquet",
+                       row_group_size=25)
+    seen, valid = [], 0
+    for shard in range(2):
+        ld = ParquetRangeBatchLoader(dataset_path=str(d), projection=["x"], batch_size=32,
+                                     batch_transformer=lambda t: t, shard_index=shard, shard_count=2, num_epochs=2)
+        for t in ld:
+            assert t.column_names == ["x"] and t.num_rows == 32
+            n = ld.last_validity.valid_count
+            seen += t.column("x").to_pylist()[:n]
+            valid += n
+    assert valid == 400 and sorted(seen) == sorted(list(range(200)) * 2)
+    with pytest.raises(ValueError, match="shard_index"):
+        ParquetRangeBatchLoader(dataset_path=str(d), projection=["x"], batch_size=8, batch_transformer=len,
+                                shard_index=2, shard_count=2)
