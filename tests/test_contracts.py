@@ -1,3 +1,4 @@
+"""Training contracts: ZeRO table, execution / input plans, update windows, task and payload schemas (CPU)."""
 import pytest
 
 from flare_b200.training.contracts import (

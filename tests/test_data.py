@@ -1,3 +1,4 @@
+"""Schema, ragged batches, completion policies, range reads, synthetic generators and the prefetch loader (CPU)."""
 import numpy as np
 import pyarrow as pa
 import pyarrow.parquet as pq

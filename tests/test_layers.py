@@ -1,3 +1,4 @@
+"""Dense layer library vs explicit references (CPU); the tcgen05 linear layer on the GPU."""
 import pytest
 import torch
 

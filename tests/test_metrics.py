@@ -1,3 +1,4 @@
+"""Exact AUC / GAUC / calibration: references vs sklearn, device kernels, distributed merge, metric windows."""
 import math
 
 import numpy as np

@@ -1,3 +1,4 @@
+"""CPU configuration: training vs the plain PyTorch oracle, paged tables, checkpoint / resume (CPU)."""
 import numpy as np
 import torch
 

@@ -1,3 +1,4 @@
+"""CPU sparse ops, planner, collection oracles, native CPU steps and input validation (CPU)."""
 import pytest
 import torch
 
