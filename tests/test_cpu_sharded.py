@@ -1,0 +1,68 @@
+"""Table-wise sharded CPU collection over gloo ranks equals one collection on the global batch (CPU)."""
+import pytest
+import torch
+
+from flare_b200.sparse.config import SparseOptimizerConfig, SparseTableSpec
+from flare_b200.testing.gloo import run_ranks
+
+OPT = SparseOptimizerConfig(kind="rowwise_adagrad", learning_rate=0.1)
+TABLES = [SparseTableSpec(f"t{i}", n, d, optimizer=OPT, pooling="mean" if i == 1 else "sum")
+          for i, (n, d) in enumerate([(50, 8), (30, 4), (70, 8), (20, 12), (40, 4)])]
+B = 6
+
+
+def _global_batch(step, world):
+    g = torch.Generator().manual_seed(100 + step)
+    GB = B * world
+    lens = torch.randint(0, 4, (len(TABLES), GB), generator=g)
+    ids = [torch.randint(0, t.num_embeddings, (int(lens[f].sum()),), generator=g) for f, t in enumerate(TABLES)]
+    return lens, ids
+
+
+def _local(lens, ids, rank, bsz):
+    """Rank's KJT: its ``bsz`` samples of every feature."""
+    vals, ls = [], []
+    for f in range(len(TABLES)):
+        cum = torch.cat([torch.zeros(1, dtype=torch.long), lens[f].cumsum(0)])
+        lo, hi = int(cum[rank * bsz]), int(cum[(rank + 1) * bsz])
+        vals.append(ids[f][lo:hi])
+        ls.append(lens[f][rank * bsz:(rank + 1) * bsz])
+    ls = torch.cat(ls)
+    offs = torch.cat([torch.zeros(1, dtype=torch.long), ls.cumsum(0)]).int()
+    return offs, torch.cat(vals).int()
+
+
+def _run(rank, world, native, steps=3):
+    from flare_b200.sparse.cpu_sharded import ShardedCpuEmbeddingBagCollection
+
+    c = ShardedCpuEmbeddingBagCollection(TABLES, B, optimizer=OPT, seed=7, native=native)
+    outs = []
+    for s in range(steps):
+        lens, ids = _global_batch(s, world)
+        c.set_input(*_local(lens, ids, rank, B))
+        y = c.forward()
+        outs.append(y)
+        c.backward(torch.tanh(y) * 0.5)  # per-sample gradients: rows of the global batch's gradient
+    return outs, {f: c.table_weights(f) for f in range(len(TABLES)) if c.table_weights(f) is not None}
+
+
+@pytest.mark.parametrize("native", [False, True])
+def test_two_ranks_equal_one_collection_on_the_global_batch(native):
+    from flare_b200.sparse.cpu_sharded import ShardedCpuEmbeddingBagCollection
+
+    ref = ShardedCpuEmbeddingBagCollection(TABLES, 2 * B, optimizer=OPT, seed=7, native=native)  # world 1
+    ref_outs = []
+    for s in range(3):
+        lens, ids = _global_batch(s, 2)
+        ref.set_input(*_local(lens, ids, 0, 2 * B))
+        y = ref.forward()
+        ref_outs.append(y)
+        ref.backward(torch.tanh(y) * 0.5)
+    results = run_ranks(_run, 2, native)
+    for r, (outs, tabs) in enumerate(results):
+        for s in range(3):
+            torch.testing.assert_close(outs[s], ref_outs[s][r * B:(r + 1) * B], rtol=0, atol=0)
+        for f, w in tabs.items():
+            assert f % 2 == r  # table-wise placement
+            torch.testing.assert_close(w, ref.table_weights(f), rtol=0, atol=0)
+    assert sorted(f for _, tabs in results for f in tabs) == list(range(len(TABLES)))
