@@ -76,6 +76,12 @@ def train_small_cpu(steps: int = 200, batch_size: int = 256, seed: int = 0, stor
     complete step (the synthetic stream skips the batches already trained on), so ``steps`` counts
     the steps of this call."""
     torch.manual_seed(seed)
+    import torch.distributed as dist
+
+    world = dist.get_world_size() if dist.is_initialized() else 1
+    rank = dist.get_rank() if dist.is_initialized() else 0
+    if world > 1:  # global batch batch_size * world; tables dealt to the ranks (gloo all-to-all)
+        return _train_small_sharded(steps, batch_size, seed, native, rank, world)
     data = SmallSyntheticData(batch_size, seed=seed)
     emb = CpuEmbeddingBagCollection(small_tables(), batch_size, seed=seed, native=native)
     if storage is not None:
@@ -108,6 +114,33 @@ def train_small_cpu(steps: int = 200, batch_size: int = 256, seed: int = 0, stor
             save_cpu(checkpoint_dir, step, engine, emb)
     dt = time.perf_counter() - t0
     return SmallRunResult(losses, steps * batch_size / dt, steps)
+
+
+def _train_small_sharded(steps: int, batch_size: int, seed: int, native: bool, rank: int, world: int) -> SmallRunResult:
+    """The same model over ``world`` gloo ranks: each rank trains ``batch_size`` samples of a global batch;
+    dense gradients are all-reduced (ZeRO-0), the tables are sharded table-wise; the tables start
+    from the single-process run's rows, so the trajectory matches it on the global batch."""
+    from ..sparse.cpu_sharded import ShardedCpuEmbeddingBagCollection, slice_samples
+
+    data = SmallSyntheticData(batch_size * world, seed=seed)
+    init = CpuEmbeddingBagCollection(small_tables(), batch_size * world, seed=seed).weights
+    emb = ShardedCpuEmbeddingBagCollection(small_tables(), batch_size, seed=seed, native=native, weights=init)
+    model = SmallDense()
+    engine = TrainEngine(model, lambda out, y: nn.functional.binary_cross_entropy_with_logits(out, y),
+                         TrainingExecutionPlan.replicated(), DenseOptimizerConfig(kind="adam", learning_rate=1e-3),
+                         device=torch.device("cpu"))
+    lo, hi = rank * batch_size, (rank + 1) * batch_size
+    losses = []
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        b = data.next()
+        emb.set_input(*slice_samples(b.offsets, b.values, data.F, batch_size * world, lo, hi))
+        pooled = emb.forward().requires_grad_(True)
+        res = engine.micro_step_once((b.dense[lo:hi], pooled), b.labels[lo:hi])
+        emb.backward(engine.input_gradients({"pooled": pooled})["pooled"])
+        losses.append(float(res.loss))
+    dt = time.perf_counter() - t0
+    return SmallRunResult(losses, steps * batch_size * world / dt, steps)
 
 
 def train_small_oracle(steps: int = 200, batch_size: int = 256, seed: int = 0) -> list[float]:

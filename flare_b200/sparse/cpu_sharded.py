@@ -52,7 +52,6 @@ class ShardedCpuEmbeddingBagCollection:
                  for f in self.owned]
             self.local = CpuEmbeddingBagCollection([tables[f] for f in self.owned], self.world * self.B, optimizer=opt,
                                                    weights=w, native=native)
-        self._recv_dims = None
 
     def _a2a(self, send: list[torch.Tensor], recv_sizes: list[int], dtype) -> list[torch.Tensor]:
         out = torch.empty(sum(recv_sizes), dtype=dtype)
@@ -128,4 +127,17 @@ class ShardedCpuEmbeddingBagCollection:
         return self.local.table_weights(self.owned.index(f)) if f in self.owned else None
 
 
-__all__ = ["ShardedCpuEmbeddingBagCollection"]
+def slice_samples(offsets: torch.Tensor, values: torch.Tensor, num_features: int, batch: int, lo: int,
+                  hi: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Samples [lo, hi) of a feature-major keyed-jagged batch of ``batch`` samples (a rank's share)."""
+    offs = offsets.long()
+    lens, vals = [], []
+    for f in range(num_features):
+        a, b = f * batch + lo, f * batch + hi
+        lens.append(offs[a + 1:b + 1] - offs[a:b])
+        vals.append(values[int(offs[a]):int(offs[b])])
+    ls = torch.cat(lens)
+    return torch.cat([torch.zeros(1, dtype=torch.long), ls.cumsum(0)]).to(offsets.dtype), torch.cat(vals)
+
+
+__all__ = ["ShardedCpuEmbeddingBagCollection", "slice_samples"]

@@ -66,3 +66,19 @@ def test_two_ranks_equal_one_collection_on_the_global_batch(native):
             assert f % 2 == r  # table-wise placement
             torch.testing.assert_close(w, ref.table_weights(f), rtol=0, atol=0)
     assert sorted(f for _, tabs in results for f in tabs) == list(range(len(TABLES)))
+
+
+def _recipe(rank, world):
+    from flare_b200.recipes.cpu_small import train_small_cpu
+
+    return train_small_cpu(steps=8, batch_size=16).losses
+
+
+def test_cpu_recipe_over_two_gloo_ranks_tracks_one_rank():
+    from flare_b200.recipes.cpu_small import train_small_cpu
+
+    one = train_small_cpu(steps=8, batch_size=32).losses
+    two = run_ranks(_recipe, 2)
+    assert two[0] == two[1]  # the global-mean loss is the same on every rank
+    for a, b in zip(one, two[0]):
+        assert abs(a - b) <= 1e-5 * max(1.0, abs(a)), (one, two[0])
