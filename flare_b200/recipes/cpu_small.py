@@ -200,11 +200,26 @@ def main(argv=None) -> int:
         from ..sparse.storage import SparseStorageOptions
 
         storage = SparseStorageOptions(memory_limit_bytes=a.memory_limit, spill_directory=a.spill_dir)
+    import os
+
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1 and not dist.is_initialized():  # launched by torch.distributed.run: gloo ranks
+        from ..parallel.dist import init_distributed
+
+        init_distributed(backend="gloo")
     r = train_small_cpu(a.steps, a.batch, a.seed, storage=storage, native=not a.tensor_ops,
                         checkpoint_dir=a.checkpoint_dir, save_every=a.save_every, resume=a.resume)
+    rank = dist.get_rank() if dist.is_initialized() else 0
+    if dist.is_initialized():
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
     print(json.dumps({"metric": "train samples/s", "value": r.samples_per_s, "steps": r.steps,
                       "first_loss": r.losses[0] if r.losses else None, "last_loss": r.losses[-1] if r.losses else None,
-                      "config": {"batch": a.batch, "tables": 8, "rows_per_table": 1000, "dim": 16,
+                      "config": {"batch_per_rank": a.batch, "ranks": world, "tables": 8, "rows_per_table": 1000,
+                                 "dim": 16,
                                  "sparse_step": "tensor ops" if a.tensor_ops else "native C++",
                                  "storage": "paged" if storage else "in memory"}}), flush=True)
     return 0
