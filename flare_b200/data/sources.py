@@ -310,6 +310,88 @@ def stream_batches(factory: SourceFactory, batch_size: int, *, policy: str = "ca
         session.close()
 
 
+class StreamingBatchReader:
+    """Keeps one batch assembler alive while source loaders come and go; resumable without payload.
+
+    ``append_fragment(table, source_range)`` returns the full batches the fragment completes;
+    ``finish_loader()`` ends one loader without flushing (rows carry into the next loader's
+    fragments); ``finalize()`` applies the completion policy to the tail.  ``checkpoint_state()``
+    holds no rows: it names the source ranges whose rows are still pending and how many leading
+    rows of the first one were already emitted, so a restored reader re-reads exactly those rows
+    (``replay_ranges``) before continuing.  Reference behaviour:
+    src/flare/data/pipeline/consumption/source/batching/stream_reader.py:25-117.
+    """
+
+    def __init__(self, *, batch_size: int, completion_policy: str = "carry", validity_field: str | None = None):
+        if validity_field is not None and (not validity_field or validity_field.strip() != validity_field):
+            raise ValueError("validity_field must be a non-empty canonical string")
+        self._asm = BatchAssembler(batch_size, completion_policy)
+        self._validity_field = validity_field
+        self._frags: list[list] = []  # [source_range, rows] of fragments with rows still pending
+        self._replay: list[tuple[Any, int]] = []
+
+    @property
+    def pending_rows(self) -> int:
+        return self._asm._pending_rows
+
+    @property
+    def replay_ranges(self) -> tuple[tuple[Any, int], ...]:
+        """(source range, rows of it to skip) to re-read after a restore."""
+        return tuple(self._replay)
+
+    def _with_validity(self, ab: AssembledBatch):
+        if self._validity_field is None:
+            return ab.data
+        if pa is not None and isinstance(ab.data, pa.Table):
+            meta = dict(ab.data.schema.metadata or {})
+            meta[self._validity_field.encode()] = str(ab.validity.valid_count).encode()
+            return ab.data.replace_schema_metadata(meta)
+        return {**ab.data, self._validity_field: ab.validity.valid_count}
+
+    def _trim(self) -> None:
+        """Keep only the fragments that still hold pending rows (the newest ones)."""
+        left, keep = self.pending_rows, []
+        for rng, rows in reversed(self._frags):
+            if left <= 0:
+                break
+            keep.append([rng, rows])
+            left -= rows
+        self._frags = list(reversed(keep))
+
+    def append_fragment(self, fragment, source_range=None) -> tuple:
+        rows = fragment.num_rows if hasattr(fragment, "num_rows") else len(next(iter(fragment.values())))
+        self._frags.append([source_range, rows])
+        out = tuple(self._with_validity(ab) for ab in self._asm.push(fragment))
+        self._trim()
+        return out
+
+    def append_loader(self, loader) -> Iterator:
+        for item in loader:
+            frag, rng = item if isinstance(item, tuple) else (item, None)
+            yield from self.append_fragment(frag, rng)
+
+    def finish_loader(self) -> tuple:
+        return ()
+
+    def finalize(self) -> tuple:
+        out = tuple(self._with_validity(ab) for ab in self._asm.finish())
+        self._frags = []
+        return out
+
+    def checkpoint_state(self) -> dict:
+        pending, spans = self.pending_rows, []
+        total = sum(r for _, r in self._frags)
+        skip = total - pending  # rows of the first kept fragment already emitted
+        for i, (rng, rows) in enumerate(self._frags):
+            spans.append([rng, skip if i == 0 else 0])
+        return {"pending_rows": pending, "replay": spans}
+
+    def restore_state(self, state: Mapping[str, Any]) -> None:
+        if self.pending_rows:
+            raise RuntimeError("restore into a fresh reader")
+        self._replay = [(rng, int(skip)) for rng, skip in state.get("replay", [])]
+
+
 class ParquetRangeBatchLoader:
     """Standalone loader: static Parquet ranges of one shard -> fixed-size batches -> a caller's transform.
 
@@ -367,7 +449,7 @@ class ParquetRangeBatchLoader:
 
 __all__ = [
     "AssembledBatch", "BatchAssembler", "BatchValidity", "CompletionPolicy", "ParquetRangeBatchLoader",
-    "ParquetSourceFactory", "RecordRange",
+    "ParquetSourceFactory", "RecordRange", "StreamingBatchReader",
     "RecordRangeReadSession", "SourceFactory", "SourceReadSession", "StandardSourceFactory", "WorkItem",
     "coalesce_source_ranges", "stream_batches",
 ]

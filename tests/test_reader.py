@@ -116,3 +116,31 @@ def test_parquet_range_batch_loader_shards_epochs_and_tail(tmp_path):
     with pytest.raises(ValueError, match="shard_index"):
         ParquetRangeBatchLoader(dataset_path=str(d), projection=["x"], batch_size=8, batch_transformer=len,
                                 shard_index=2, shard_count=2)
+
+
+def test_streaming_batch_reader_resumes_from_replay_ranges():
+    from flare_b200.data.sources import StreamingBatchReader
+
+    frags = {f"r{i}": pa.table({"x": list(range(i * 10, i * 10 + 10))}) for i in range(5)}
+
+    def run(reader, names, first_skip=0):
+        out = []
+        for j, n in enumerate(names):
+            t = frags[n].slice(first_skip) if j == 0 and first_skip else frags[n]
+            out += [b.column("x").to_pylist() for b in reader.append_fragment(t, n)]
+        return out
+
+    whole = run(StreamingBatchReader(batch_size=16), list(frags))
+    a = StreamingBatchReader(batch_size=16, validity_field="valid")
+    head = run(a, ["r0", "r1"])
+    state = a.checkpoint_state()
+    assert state == {"pending_rows": 4, "replay": [["r1", 6]]}
+    b = StreamingBatchReader(batch_size=16)
+    b.restore_state(state)
+    (rng, skip), = b.replay_ranges
+    tail = run(b, [rng, "r2", "r3", "r4"], first_skip=skip)
+    assert head + tail == whole and len(whole) == 3
+    last = StreamingBatchReader(batch_size=16, completion_policy="pad", validity_field="valid")
+    run(last, ["r0"])
+    (t,) = last.finalize()
+    assert t.num_rows == 16 and t.schema.metadata[b"valid"] == b"10"
