@@ -23,6 +23,7 @@ from __future__ import annotations
 import json
 import os
 import shutil
+import time
 from dataclasses import dataclass
 from pathlib import Path
 
@@ -45,6 +46,25 @@ def _barrier() -> None:
         from ..parallel.dist import barrier
 
         barrier()
+
+
+READ_ATTEMPTS = 3
+
+
+def _read_array(path) -> np.ndarray:
+    """``np.load`` with up to ``READ_ATTEMPTS`` tries on transient I/O errors (network file systems);
+    a missing file fails at once.  The reference retries transient read errors of its sparse
+    checkpoints three times (src/flare/runtime/fluxway/checkpoint/sparse.py:20-47)."""
+    for attempt in range(READ_ATTEMPTS):
+        try:
+            return np.load(path)
+        except FileNotFoundError:
+            raise
+        except OSError:
+            if attempt == READ_ATTEMPTS - 1:
+                raise
+            time.sleep(0.05 * (attempt + 1))
+    raise AssertionError("unreachable")
 
 
 def step_dir(root: str | os.PathLike, step: int) -> Path:
@@ -94,7 +114,7 @@ def load_dense(dirpath: Path, dense) -> dict:
             raise ValueError(f"parameter {name}: checkpoint shape differs from the model")
         for field in ("master", "m", "v"):
             full[field][e.offset:e.offset + e.numel] = torch.from_numpy(
-                np.load(dirpath / f"{name}.{field}.npy")).reshape(-1)
+                _read_array(dirpath / f"{name}.{field}.npy")).reshape(-1)
     dense.load_state_dict({"step": manifest["optimizer_step"], **full})
     return manifest
 
@@ -180,12 +200,12 @@ def load_sparse(root: str | os.PathLike, step: int, group: str, coll) -> dict:
                     continue
                 R, r = int(p.get("row_shards", 1)), int(p.get("row_index", 0))
                 prefix = d / _piece_name(s.spec.name, p["col_begin"], r, R)
-                local = np.load(f"{prefix}.rows.npy") if man["mode"] == "incremental" else None
+                local = _read_array(f"{prefix}.rows.npy") if man["mode"] == "incremental" else None
                 for field in _FIELDS:
                     f = Path(f"{prefix}.{field}.npy")
                     if not f.exists():
                         continue
-                    arr = np.load(f)
+                    arr = _read_array(f)
                     if field not in entry:
                         shape = (s.spec.num_embeddings, s.ncols) if arr.ndim == 2 else (s.spec.num_embeddings,)
                         entry[field] = np.zeros(shape, dtype=np.float32)

@@ -56,3 +56,26 @@ def test_audit_reports_problems(tmp_path):
     _write(tmp_path / "d", 1, split_rows=True, drop_piece=True)
     rep = audit_step(tmp_path / "d")
     assert not rep["ok"] and any("cover" in p for p in rep["sparse"]["problems"])
+
+
+def test_checkpoint_reads_retry_transient_errors(tmp_path, monkeypatch):
+    import numpy as np
+    import pytest
+
+    from flare_b200.checkpoint import store
+
+    np.save(tmp_path / "a.npy", np.arange(3))
+    real, calls = np.load, []
+
+    def flaky(path, *a, **k):
+        calls.append(path)
+        if len(calls) < 3:
+            raise OSError("transient")
+        return real(path, *a, **k)
+
+    monkeypatch.setattr(store.np, "load", flaky)
+    assert store._read_array(tmp_path / "a.npy").tolist() == [0, 1, 2] and len(calls) == 3
+    calls.clear()
+    monkeypatch.setattr(store.np, "load", lambda *a, **k: (_ for _ in ()).throw(OSError("down")))
+    with pytest.raises(OSError):
+        store._read_array(tmp_path / "a.npy")
