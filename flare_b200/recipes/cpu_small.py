@@ -12,7 +12,7 @@ forward/backward contract as the fused GPU collection.
 from __future__ import annotations
 
 import time
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 
 import torch
 import torch.nn as nn
@@ -59,6 +59,7 @@ class SmallRunResult:
     losses: list[float]
     samples_per_s: float
     steps: int
+    windows: list = field(default_factory=list)  # flushed metric windows (train/auc_ctr, loss, throughput)
 
 
 def small_tables(opt: SparseOptimizerConfig | None = None) -> list[SparseTableSpec]:
@@ -68,7 +69,7 @@ def small_tables(opt: SparseOptimizerConfig | None = None) -> list[SparseTableSp
 
 def train_small_cpu(steps: int = 200, batch_size: int = 256, seed: int = 0, storage=None,
                     native: bool = True, checkpoint_dir: str | None = None, save_every: int = 0,
-                    resume: bool = False) -> SmallRunResult:
+                    resume: bool = False, metrics_every: int = 50) -> SmallRunResult:
     """``storage`` (``SparseStorageOptions``): keep the tables in the paged store (memory limit, disk
     spill), starting from the same initial rows as the in-memory run.  ``native``: pool and reduce
     the sparse gradients with the host C++ ops (the tensor-op path otherwise).  ``checkpoint_dir``:
@@ -81,7 +82,7 @@ def train_small_cpu(steps: int = 200, batch_size: int = 256, seed: int = 0, stor
     world = dist.get_world_size() if dist.is_initialized() else 1
     rank = dist.get_rank() if dist.is_initialized() else 0
     if world > 1:  # global batch batch_size * world; tables dealt to the ranks (gloo all-to-all)
-        return _train_small_sharded(steps, batch_size, seed, native, rank, world)
+        return _train_small_sharded(steps, batch_size, seed, native, rank, world, metrics_every)
     data = SmallSyntheticData(batch_size, seed=seed)
     emb = CpuEmbeddingBagCollection(small_tables(), batch_size, seed=seed, native=native)
     if storage is not None:
@@ -99,6 +100,10 @@ def train_small_cpu(steps: int = 200, batch_size: int = 256, seed: int = 0, stor
             start = restore_cpu(checkpoint_dir, engine, emb)
             for _ in range(start):
                 data.next()
+    from ..metrics.aggregation import TrainMetricsWindow
+
+    window = TrainMetricsWindow(window_steps=metrics_every, capacity=metrics_every * batch_size)
+    windows = []
     losses = []
     t0 = time.perf_counter()
     for step in range(start + 1, start + steps + 1):
@@ -108,15 +113,19 @@ def train_small_cpu(steps: int = 200, batch_size: int = 256, seed: int = 0, stor
         res = engine.micro_step_once((b.dense, pooled), b.labels)
         emb.backward(engine.input_gradients({"pooled": pooled})["pooled"])
         losses.append(float(res.loss))
+        w = window.update(res.outputs.detach(), b.labels, loss_sum=float(res.loss) * batch_size)
+        if w is not None:
+            windows.append(w)
         if checkpoint_dir is not None and save_every and step % save_every == 0:
             from ..checkpoint.cpu import save_cpu
 
             save_cpu(checkpoint_dir, step, engine, emb)
     dt = time.perf_counter() - t0
-    return SmallRunResult(losses, steps * batch_size / dt, steps)
+    return SmallRunResult(losses, steps * batch_size / dt, steps, windows)
 
 
-def _train_small_sharded(steps: int, batch_size: int, seed: int, native: bool, rank: int, world: int) -> SmallRunResult:
+def _train_small_sharded(steps: int, batch_size: int, seed: int, native: bool, rank: int, world: int,
+                         metrics_every: int = 50) -> SmallRunResult:
     """The same model over ``world`` gloo ranks: each rank trains ``batch_size`` samples of a global batch;
     dense gradients are all-reduced (ZeRO-0), the tables are sharded table-wise; the tables start
     from the single-process run's rows, so the trajectory matches it on the global batch."""
@@ -129,8 +138,11 @@ def _train_small_sharded(steps: int, batch_size: int, seed: int, native: bool, r
     engine = TrainEngine(model, lambda out, y: nn.functional.binary_cross_entropy_with_logits(out, y),
                          TrainingExecutionPlan.replicated(), DenseOptimizerConfig(kind="adam", learning_rate=1e-3),
                          device=torch.device("cpu"))
+    from ..metrics.aggregation import TrainMetricsWindow
+
+    window = TrainMetricsWindow(window_steps=metrics_every, capacity=metrics_every * batch_size)  # merged over ranks
     lo, hi = rank * batch_size, (rank + 1) * batch_size
-    losses = []
+    losses, windows = [], []
     t0 = time.perf_counter()
     for _ in range(steps):
         b = data.next()
@@ -139,8 +151,11 @@ def _train_small_sharded(steps: int, batch_size: int, seed: int, native: bool, r
         res = engine.micro_step_once((b.dense[lo:hi], pooled), b.labels[lo:hi])
         emb.backward(engine.input_gradients({"pooled": pooled})["pooled"])
         losses.append(float(res.loss))
+        w = window.update(res.outputs.detach(), b.labels[lo:hi], loss_sum=float(res.loss) * batch_size)
+        if w is not None:
+            windows.append(w)
     dt = time.perf_counter() - t0
-    return SmallRunResult(losses, steps * batch_size * world / dt, steps)
+    return SmallRunResult(losses, steps * batch_size * world / dt, steps, windows)
 
 
 def train_small_oracle(steps: int = 200, batch_size: int = 256, seed: int = 0) -> list[float]:
@@ -218,6 +233,7 @@ def main(argv=None) -> int:
         return 0
     print(json.dumps({"metric": "train samples/s", "value": r.samples_per_s, "steps": r.steps,
                       "first_loss": r.losses[0] if r.losses else None, "last_loss": r.losses[-1] if r.losses else None,
+                      "last_window": r.windows[-1] if r.windows else None,
                       "config": {"batch_per_rank": a.batch, "ranks": world, "tables": 8, "rows_per_table": 1000,
                                  "dim": 16,
                                  "sparse_step": "tensor ops" if a.tensor_ops else "native C++",
