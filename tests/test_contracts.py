@@ -66,3 +66,34 @@ def test_plans_schema_precision():
     assert PrecisionPolicy.BF16.gradient_transport_dtype.is_floating_point
     assert PrecisionPolicy.BF16.sparse_storage_dtype_name == "float16"
     assert PrecisionPolicy.FP32.sparse_gradient_transport_dtype_name == "float32"
+
+
+def test_pipelined_host_state_machine_without_cuda():
+    """Graph keys, capture snapshot / restore and replay advance of the fused DLRM's host state."""
+    from types import SimpleNamespace
+
+    from flare_b200.models.dlrm import DLRM
+
+    def model(pipelined):
+        m = object.__new__(DLRM)  # no CUDA: only the host-side bookkeeping is exercised
+        m.pipelined, m._next_slot, m.pending_slot = pipelined, 0, None
+        m.dense, m.emb = SimpleNamespace(step=0), SimpleNamespace(step=0, _slot=0)
+        return m
+
+    s = model(False)
+    assert s.graph_key() == 0
+    s.advance_host_state()
+    assert (s.dense.step, s.emb.step) == (1, 1)
+
+    p = model(True)
+    assert p.graph_key() is None  # the first step has no pending update: eager, never captured
+    p._next_slot, p.pending_slot, p.emb._slot = 1, 0, 0  # after one eager step on slot 0
+    keys = []
+    for _ in range(4):
+        keys.append(p.graph_key())
+        snap = p.host_state()
+        p._next_slot, p.pending_slot, p.dense.step = 9, 9, 99  # what a capture may leave behind
+        p.restore_host_state(snap)
+        p.advance_host_state()
+    assert keys == [(1, 0), (0, 1), (1, 0), (0, 1)]  # two graphs, alternating
+    assert (p.dense.step, p.emb.step, p.emb._slot, p._next_slot, p.pending_slot) == (4, 4, 0, 1, 0)
