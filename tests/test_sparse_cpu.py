@@ -255,3 +255,13 @@ def test_staleness_bound_validation():
     with pytest.raises(ValueError, match="max_staleness_steps"):
         SparseTableSpec("a", 10, 8, max_staleness_steps=-1)
     assert SparseTableSpec("a", 10, 8, max_staleness_steps=2).max_staleness_steps == 2
+
+
+def test_exchange_bytes_account_for_the_pipelined_gradient_buffer():
+    from flare_b200.sparse.collection import ShardedEmbeddingBagCollection
+    from flare_b200.sparse.config import SparseTableSpec
+
+    tabs = [SparseTableSpec("a", 100, 16), SparseTableSpec("b", 50, 8)]
+    sync = ShardedEmbeddingBagCollection.exchange_bytes(tabs, 32, 4)
+    piped = ShardedEmbeddingBagCollection.exchange_bytes(tabs, 32, 4, pipelined=True)
+    assert piped - sync == 4 * 32 * (16 + 8)  # one more [B, total_dim] pooled-gradient buffer
