@@ -122,6 +122,25 @@ class ShardedCpuEmbeddingBagCollection:
         if self.owned:
             self.local.backward(torch.cat([x.reshape(B, own_dim) for x in recv]), step)
 
+    def state_dict(self) -> dict:
+        """This rank's owned tables (whole, by name), their optimizer state and dynamic key maps."""
+        st = self.local.state_dict() if self.local is not None else {"tables": {}, "dynamic": {}, "step": 0}
+        return {**st, "world": self.world, "rank": self.rank}
+
+    def load_state_dict(self, states) -> None:
+        """Restore from one state or from every rank's states of a run at any world size (tables are
+        whole per owner, so the union of the states holds every table)."""
+        states = [states] if isinstance(states, dict) else list(states)
+        if self.local is None:
+            return
+        merged = {"tables": {}, "dynamic": {}, "step": max(int(s.get("step", 0)) for s in states)}
+        for s in states:
+            merged["tables"].update(s["tables"])
+            merged["dynamic"].update(s.get("dynamic", {}))
+            if "optimizer" in s:
+                merged["optimizer"] = s["optimizer"]
+        self.local.load_state_dict(merged)
+
     def table_weights(self, f: int) -> torch.Tensor | None:
         """Table f's weights on its owner (None elsewhere)."""
         return self.local.table_weights(self.owned.index(f)) if f in self.owned else None

@@ -82,3 +82,33 @@ def test_cpu_recipe_over_two_gloo_ranks_tracks_one_rank():
     assert two[0] == two[1]  # the global-mean loss is the same on every rank
     for a, b in zip(one, two[0]):
         assert abs(a - b) <= 1e-5 * max(1.0, abs(a)), (one, two[0])
+
+
+def _train_and_save(rank, world):
+    from flare_b200.sparse.cpu_sharded import ShardedCpuEmbeddingBagCollection
+
+    c = ShardedCpuEmbeddingBagCollection(TABLES, B, optimizer=OPT, seed=7)
+    for s in range(2):
+        lens, ids = _global_batch(s, world)
+        c.set_input(*_local(lens, ids, rank, B))
+        y = c.forward()
+        c.backward(torch.tanh(y) * 0.5)
+    return c.state_dict()
+
+
+def test_sharded_state_restores_at_another_world_size():
+    from flare_b200.sparse.cpu_sharded import ShardedCpuEmbeddingBagCollection
+
+    states = run_ranks(_train_and_save, 2)  # 2 ranks, each with its own tables
+    assert sorted(n for st in states for n in st["tables"]) == sorted(t.name for t in TABLES)
+    ref = ShardedCpuEmbeddingBagCollection(TABLES, 2 * B, optimizer=OPT, seed=7)  # one rank, straight through
+    resumed = ShardedCpuEmbeddingBagCollection(TABLES, 2 * B, optimizer=OPT, seed=0)
+    resumed.load_state_dict(states)  # one rank restored from the two ranks' states
+    for s in range(4):
+        lens, ids = _global_batch(s, 2)
+        for c in ([ref] if s < 2 else [ref, resumed]):
+            c.set_input(*_local(lens, ids, 0, 2 * B))
+            y = c.forward()
+            c.backward(torch.tanh(y) * 0.5)
+    for f in range(len(TABLES)):
+        torch.testing.assert_close(resumed.table_weights(f), ref.table_weights(f), rtol=0, atol=0)
