@@ -30,15 +30,17 @@ def test_tracer_and_fingerprint(tmp_path):
 def _heartbeat_world(rank, world):
     store = dist.distributed_c10d._get_default_store()
     hb = Heartbeat(store, rank, interval_s=0.1)
-    dog = PeerWatchdog(store, world, rank, timeout_s=0.6)
+    # margins well above a loaded host's scheduling delays: beats every 0.1 s, silence after 2 s
+    dog = PeerWatchdog(store, world, rank, timeout_s=2.0)
     dist.barrier()
     time.sleep(0.3)
     dog.check()  # everyone alive
+    dist.barrier()  # both ranks passed the first check before rank 1 goes silent
     if rank == 1:
         hb.stop()  # this rank goes silent (a hang, from the peers' point of view)
-        time.sleep(1.5)
+        time.sleep(4.0)
         return "silent"
-    time.sleep(1.2)
+    time.sleep(3.0)
     try:
         dog.check()
     except PeerFailure as e:
