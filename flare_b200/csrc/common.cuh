@@ -164,6 +164,18 @@ __device__ __forceinline__ float4 f4_scale(float4 a, float s) {
   return make_float4(a.x * s, a.y * s, a.z * s, a.w * s);
 }
 
+// 64-bit finaliser of MurmurHash3 (Austin Appleby, public domain): every output bit depends on
+// every input bit, so masking its low bits to a power-of-two table spreads keys that differ only
+// in their high bits (ids with a table tag packed above bit 32, multiples of 2^20, ...).
+__device__ __forceinline__ unsigned long long hash_mix64(unsigned long long k) {
+  k ^= k >> 33;
+  k *= 0xff51afd7ed558ccdull;
+  k ^= k >> 33;
+  k *= 0xc4ceb9fe1a85ec53ull;
+  k ^= k >> 33;
+  return k;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -78,7 +78,6 @@ __global__ void scatter_pool_kernel(const T* __restrict__ grad, const int* __res
 
 // ---------------------------- first-occurrence unique -----------------------
 constexpr unsigned long long kEmptyKey = 0xFFFFFFFFFFFFFFFFull;
-constexpr unsigned long long kFibMul = 11400714819323198485ull;  // 2^64 / golden ratio
 
 __global__ void unique_insert_kernel(const int64_t* __restrict__ keys, int64_t n, unsigned long long* tab_keys,
                                      int* tab_first, int64_t cap_mask, int64_t* slot_of) {
@@ -87,7 +86,7 @@ __global__ void unique_insert_kernel(const int64_t* __restrict__ keys, int64_t n
     // Flip the sign bit so the empty sentinel (all ones) corresponds to the
     // key INT64_MAX, which is reserved; -1 and every other key are usable.
     const unsigned long long k = static_cast<unsigned long long>(keys[i]) ^ 0x8000000000000000ull;
-    int64_t slot = static_cast<int64_t>((k * kFibMul) & static_cast<unsigned long long>(cap_mask));
+    int64_t slot = static_cast<int64_t>(hash_mix64(k) & static_cast<unsigned long long>(cap_mask));
     while (true) {
       const unsigned long long cur = tab_keys[slot];
       if (cur == k) break;

@@ -35,8 +35,17 @@
 // GPU (different streams, or different host threads without ordering) race on
 // the array and must be serialised by the caller.
 //
+// The cached address belongs to the device's primary context: after
+// cudaDeviceReset (or anything else that destroys and recreates the primary
+// context) the module is loaded again at a possibly different address, so a
+// caller that resets a device must call flare_unique_noalloc_forget_device()
+// for it before the next call on that device.
+//
 // Return codes: 0 ok, -1 n out of range, -2 the scratch address could not be
-// obtained, -3 a kernel launch failed.  The function performs no cudaMalloc,
+// obtained, -3 a kernel launch failed.  Launch errors are read with
+// cudaPeekAtLastError, which leaves the error state as it is: an error that
+// was already pending before the call (left by other code) is also reported
+// as -3, and stays pending for its owner to see.  The function performs no cudaMalloc,
 // cudaFree or other allocating call; work is enqueued on `stream` and the
 // function does not wait for it.
 #include "unique_noalloc.h"
@@ -54,7 +63,6 @@ constexpr int kNaScanBlocks = 256;
 constexpr int kNaThreads = 256;
 constexpr int kNaMaxDevices = 64;
 constexpr unsigned long long kNaEmpty = 0xFFFFFFFFFFFFFFFFull;
-constexpr unsigned long long kNaFibMul = 11400714819323198485ull;  // 2^64 / golden ratio
 
 struct NaScratch {
   unsigned long long tab_keys[kNaTableSlots];  // 4 MiB
@@ -81,7 +89,7 @@ __global__ void na_insert_kernel(NaScratch* s, const int64_t* __restrict__ keys,
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     // sign bit flipped so the empty pattern stands for the reserved INT64_MAX
     const unsigned long long k = static_cast<unsigned long long>(keys[i]) ^ 0x8000000000000000ull;
-    int64_t slot = static_cast<int64_t>((k * kNaFibMul) & static_cast<unsigned long long>(cap_mask));
+    int64_t slot = static_cast<int64_t>(hash_mix64(k) & static_cast<unsigned long long>(cap_mask));
     while (true) {
       const unsigned long long cur = s->tab_keys[slot];
       if (cur == k) break;
@@ -181,9 +189,12 @@ __global__ void na_emit_kernel(NaScratch* s, const int64_t* __restrict__ keys, i
 
 __global__ void na_zero_count_kernel(int32_t* num_unique) { *num_unique = 0; }
 
+std::mutex g_na_mu;
+NaScratch* g_na_cache[kNaMaxDevices] = {};
+
 NaScratch* na_scratch_for_current_device() {
-  static std::mutex mu;
-  static NaScratch* cache[kNaMaxDevices] = {};
+  std::mutex& mu = g_na_mu;
+  NaScratch** cache = g_na_cache;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNaMaxDevices) return nullptr;
   std::lock_guard<std::mutex> lock(mu);
@@ -224,7 +235,7 @@ extern "C" __attribute__((visibility("default"))) int flare_unique_first_occurre
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (n == 0) {
     na_zero_count_kernel<<<1, 1, 0, st>>>(num_unique);
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    return cudaPeekAtLastError() == cudaSuccess ? 0 : -3;
   }
   int64_t cap = 1;
   while (cap < 2 * n) cap <<= 1;
@@ -235,5 +246,15 @@ extern "C" __attribute__((visibility("default"))) int flare_unique_first_occurre
   na_scan_partial_kernel<<<kNaScanBlocks, kNaThreads, 0, st>>>(s, n);
   na_scan_final_kernel<<<kNaScanBlocks, kNaThreads, 0, st>>>(s, n);
   na_emit_kernel<<<g, kNaThreads, 0, st>>>(s, keys, n, unique, inverse, first_index, num_unique);
-  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+  return cudaPeekAtLastError() == cudaSuccess ? 0 : -3;
+}
+
+// Drop the cached scratch address of `device` (after cudaDeviceReset on it); the next call on that
+// device looks the address up again.  Returns 0, or -1 for a device number out of range.
+extern "C" __attribute__((visibility("default"))) int flare_unique_noalloc_forget_device(int device) {
+  using namespace flare;
+  if (device < 0 || device >= kNaMaxDevices) return -1;
+  std::lock_guard<std::mutex> lock(g_na_mu);
+  g_na_cache[device] = nullptr;
+  return 0;
 }

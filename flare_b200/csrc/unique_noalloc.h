@@ -22,6 +22,10 @@ extern "C" {
 int flare_unique_first_occurrence_noalloc(const int64_t* keys, int64_t n, int64_t* unique, int32_t* inverse,
                                           int64_t* first_index, int32_t* num_unique, void* stream);
 
+// Forget the cached scratch address of `device`; call it after cudaDeviceReset on that device
+// (the reset reloads the module, possibly at another address).  Returns 0, or -1 if out of range.
+int flare_unique_noalloc_forget_device(int device);
+
 #ifdef __cplusplus
 }
 #endif

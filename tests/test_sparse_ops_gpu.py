@@ -41,3 +41,17 @@ def test_unique_first_occurrence(cuda, n):
     u, inv, first = unique_first_occurrence(keys.to(cuda))
     ru, rinv, rfirst = unique_first_occurrence_reference(keys)
     assert torch.equal(u.cpu(), ru) and torch.equal(inv.cpu(), rinv) and torch.equal(first.cpu(), rfirst)
+
+
+def test_unique_first_occurrence_high_bit_keys(cuda):
+    """Keys that differ only above bit 32 (a table tag packed into the high bits) hash apart."""
+    import time
+
+    keys = (torch.arange(4096, dtype=torch.int64) % 1024) << 32
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    u, inv, first = unique_first_occurrence(keys.to(cuda))
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 1.0
+    ru, rinv, rfirst = unique_first_occurrence_reference(keys)
+    assert torch.equal(u.cpu(), ru) and torch.equal(inv.cpu(), rinv) and torch.equal(first.cpu(), rfirst)

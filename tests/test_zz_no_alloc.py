@@ -64,3 +64,32 @@ def test_noalloc_dedup_rejects_too_many_keys():
     rc = fn(out.data_ptr(), MAX_KEYS + 1, out.data_ptr(), out.data_ptr(), out.data_ptr(), out.data_ptr(),
             torch.cuda.current_stream(dev).cuda_stream)
     assert rc == -1
+
+
+def test_noalloc_dedup_keys_differing_only_in_high_bits():
+    """Keys i << 32 (a table tag packed above bit 32) must spread over the hash table: the
+    call finishes quickly and returns what the allocating entry point returns."""
+    import time
+
+    from flare_b200.ops.sparse import unique_first_occurrence
+
+    fn = _entry_point()
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev)
+    n = 4096
+    keys = (torch.arange(n, device=dev, dtype=torch.int64) % 1024) << 32
+    unique = torch.empty(n, dtype=torch.int64, device=dev)
+    inverse = torch.empty(n, dtype=torch.int32, device=dev)
+    first = torch.empty(n, dtype=torch.int64, device=dev)
+    count = torch.empty(1, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    rc = fn(keys.data_ptr(), n, unique.data_ptr(), inverse.data_ptr(), first.data_ptr(), count.data_ptr(),
+            stream.cuda_stream)
+    torch.cuda.synchronize(dev)
+    assert rc == 0
+    assert time.perf_counter() - t0 < 1.0
+    ref_u, ref_inv, ref_first = unique_first_occurrence(keys)
+    k = int(count.item())
+    assert k == 1024 == ref_u.numel()
+    assert torch.equal(unique[:k], ref_u) and torch.equal(inverse, ref_inv) and torch.equal(first[:k], ref_first)
