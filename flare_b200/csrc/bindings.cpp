@@ -287,6 +287,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   });
 
   m.def("emb_det_temp_bytes", [](int64_t max_occ) { return flare::emb_det_temp_bytes(max_occ); });
+  m.def("emb_hash_sizes", [](int64_t max_occ, int light_max) {
+    return py::make_tuple(flare::emb_hash_tile_count(max_occ), flare::emb_hash_max_chunks(max_occ, light_max),
+                          flare::emb_hash_max_parts(max_occ), flare::emb_hash_scan_vals());
+  });
   m.def("emb_backward", [](const py::dict& d) {
     flare::EmbBwdParams p{};
     p.shards = P<const flare::ShardDesc>(get<uintptr_t>(d, "shards"));
@@ -308,23 +312,23 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.stage_cap = get<int64_t>(d, "stage_cap");
     p.weights = P<void>(get<uintptr_t>(d, "weights"));
     p.w_dtype = get<int>(d, "w_dtype");
-    p.row_count = P<int>(get<uintptr_t>(d, "row_count"));
-    p.row2u = P<int>(get<uintptr_t>(d, "row2u"));
+    p.row_count = P<int>(get_or<uintptr_t>(d, "row_count", 0));
+    p.row2u = P<int>(get_or<uintptr_t>(d, "row2u", 0));
     p.flags = P<int>(get<uintptr_t>(d, "flags"));
-    p.pos = P<int>(get<uintptr_t>(d, "pos"));
-    p.uniq_row = P<int64_t>(get<uintptr_t>(d, "uniq_row"));
-    p.uniq_shard = P<int>(get<uintptr_t>(d, "uniq_shard"));
-    p.cnt_u = P<int>(get<uintptr_t>(d, "cnt_u"));
-    p.first_gidx = P<int>(get<uintptr_t>(d, "first_gidx"));
+    p.pos = P<int>(get_or<uintptr_t>(d, "pos", 0));
+    p.uniq_row = P<int64_t>(get_or<uintptr_t>(d, "uniq_row", 0));
+    p.uniq_shard = P<int>(get_or<uintptr_t>(d, "uniq_shard", 0));
+    p.cnt_u = P<int>(get_or<uintptr_t>(d, "cnt_u", 0));
+    p.first_gidx = P<int>(get_or<uintptr_t>(d, "first_gidx", 0));
     p.num_unique = P<int>(get<uintptr_t>(d, "num_unique"));
     p.seg_start = P<int>(get<uintptr_t>(d, "seg_start"));
-    p.block_sums = P<int>(get<uintptr_t>(d, "block_sums"));
+    p.block_sums = P<int>(get_or<uintptr_t>(d, "block_sums", 0));
     p.occ = P<int>(get<uintptr_t>(d, "occ"));
-    p.heavy = P<int>(get<uintptr_t>(d, "heavy"));
-    p.heavy_start = P<int>(get<uintptr_t>(d, "heavy_start"));
-    p.hcnt = P<int>(get<uintptr_t>(d, "hcnt"));
-    p.heavy_acc = P<float>(get<uintptr_t>(d, "heavy_acc"));
-    p.max_heavy = get<int>(d, "max_heavy");
+    p.heavy = P<int>(get_or<uintptr_t>(d, "heavy", 0));
+    p.heavy_start = P<int>(get_or<uintptr_t>(d, "heavy_start", 0));
+    p.hcnt = P<int>(get_or<uintptr_t>(d, "hcnt", 0));
+    p.heavy_acc = P<float>(get_or<uintptr_t>(d, "heavy_acc", 0));
+    p.max_heavy = get_or<int>(d, "max_heavy", 0);
     p.light_max = get_or<int>(d, "light_max", 64);
     p.dirty = P<uint8_t>(get_or<uintptr_t>(d, "dirty", 0));
     p.max_occ = get<int64_t>(d, "max_occ");
@@ -334,6 +338,26 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.det_vals = P<int>(get_or<uintptr_t>(d, "det_vals", 0));
     p.det_temp = P<void>(get_or<uintptr_t>(d, "det_temp", 0));
     p.det_temp_bytes = get_or<size_t>(d, "det_temp_bytes", 0);
+    p.hash_mode = get_or<int>(d, "hash_mode", 0);
+    if (p.hash_mode) {
+      p.htab = P<unsigned long long>(get<uintptr_t>(d, "htab"));
+      p.hseg = P<int>(get<uintptr_t>(d, "hseg"));
+      p.ovf_list = P<int>(get<uintptr_t>(d, "ovf_list"));
+      p.hcap = get<int64_t>(d, "hcap");
+      p.hregion = get_or<int64_t>(d, "hregion", 0);
+      p.grad_direct = get_or<int>(d, "grad_direct", 0);
+      p.occ_h = P<int>(get<uintptr_t>(d, "occ_h"));
+      p.occ_rank = P<int>(get<uintptr_t>(d, "occ_rank"));
+      p.occ_bag = P<int>(get<uintptr_t>(d, "occ_bag"));
+      p.lrec = P<int4>(get<uintptr_t>(d, "lrec"));
+      p.crec = P<int4>(get<uintptr_t>(d, "crec"));
+      p.max_chunks = get<int64_t>(d, "max_chunks");
+      p.hpart = P<float>(get<uintptr_t>(d, "hpart"));
+      p.max_parts = get<int64_t>(d, "max_parts");
+      p.occ_scale = P<float>(get_or<uintptr_t>(d, "occ_scale", 0));
+      p.scan_val = P<int>(get<uintptr_t>(d, "scan_val"));
+      p.max_tiles = get<int64_t>(d, "max_tiles");
+    }
     p.opt = parse_sparse_opt(get<py::dict>(d, "opt"));
     p.flags_local = P<uint32_t>(get_or<uintptr_t>(d, "flags_local", 0));
     p.peer_flags = P<uint32_t* const>(get_or<uintptr_t>(d, "peer_flags", 0));

@@ -33,6 +33,7 @@
 // and updates rows in its external native store.
 #include "embedding.cuh"
 #include "sm100.cuh"
+#include "sparse_update.cuh"
 
 #include <cub/device/device_radix_sort.cuh>
 #include "sparse_ops.cuh"
@@ -952,136 +953,6 @@ __global__ void __launch_bounds__(kEmbThreads) emb_det_keys_kernel(EmbBwdParams 
   }
 }
 
-__device__ __forceinline__ float lr_scale(const SparseOptParams& o, float score) {
-  switch (o.lr_policy) {
-    case kLrSqrtDecay:
-      return rsqrtf(fmaxf(score, 1.f));
-    case kLrLogDecay:
-      return 1.f / (1.f + log1pf(fmaxf(score, 0.f)));
-    case kLrInverseDecay:
-      return 1.f / fmaxf(score, 1.f);
-    case kLrCosineFrequency: {
-      const float x = fminf(fmaxf(score, 0.f), o.policy_b) / fmaxf(o.policy_b, 1e-12f);
-      return o.policy_a + (1.f - o.policy_a) * 0.5f * (1.f + cospif(x));
-    }
-    case kLrCustomLut: {
-      if (o.lut == nullptr || o.lut_len <= 0) return 1.f;
-      const int i = min(static_cast<int>(fmaxf(score, 0.f)), o.lut_len - 1);
-      return o.lut[i];
-    }
-    default:
-      return 1.f;
-  }
-}
-
-__device__ __forceinline__ void resolve_sparse_step(SparseOptParams& o) {
-  if (o.step_ptr != nullptr) {
-    const float t = static_cast<float>(*o.step_ptr);
-    o.bias_corr1 = 1.f - powf(o.beta1, t);
-    o.bias_corr2 = 1.f - powf(o.beta2, t);
-  }
-}
-
-// Sum over the G lanes of an aligned lane group (G a power of two).
-__device__ __forceinline__ float group_sum(float v, int G) {
-  for (int o = G >> 1; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
-  return v;
-}
-
-// Apply the sparse optimizer to one row.  Called by every lane of the warp in
-// lockstep; a group of G lanes owns the row and lane `leader` is its first
-// lane; a lane covers columns [col, col + 4*NV) of the row when `act`.
-template <typename TW, int NV>
-__device__ __forceinline__ void apply_update(const SparseOptParams& o, TW* w, int64_t eoff, long long row,
-                                             bool row_ok, bool act, int ncols, float4 (&gv4)[NV],
-                                             float4 (&wv4)[NV], int count, int G, int leader) {
-  float* g = reinterpret_cast<float*>(gv4);
-  float* wv = reinterpret_cast<float*>(wv4);
-  float lr = o.lr;
-  if (o.score != nullptr) {
-    float sc = 0.f;
-    if (row_ok && lane_id() == leader) {
-      sc = o.score[row] + static_cast<float>(count);
-      o.score[row] = sc;
-    }
-    sc = __shfl_sync(kFull, sc, leader);
-    lr *= lr_scale(o, sc);
-  }
-#pragma unroll
-  for (int e = 0; e < 4 * NV; ++e) g[e] += o.weight_decay * wv[e];
-  if (o.kind == kOptRowwiseAdagrad || o.kind == kOptRowwiseAdam) {
-    float sq = 0.f;
-    if (act) {
-#pragma unroll
-      for (int e = 0; e < 4 * NV; ++e) sq += g[e] * g[e];
-    }
-    sq = group_sum(sq, G) / static_cast<float>(ncols);
-    float st = 0.f;
-    if (row_ok && lane_id() == leader) {
-      const float old = o.state_row[row];
-      st = o.kind == kOptRowwiseAdagrad ? old + sq : o.beta2 * old + (1.f - o.beta2) * sq;
-      o.state_row[row] = st;
-    }
-    st = __shfl_sync(kFull, st, leader);
-    if (o.kind == kOptRowwiseAdagrad) {
-      const float scale = lr / (sqrtf(st) + o.eps);
-#pragma unroll
-      for (int e = 0; e < 4 * NV; ++e) wv[e] -= scale * g[e];
-    } else if (act) {
-      const float denom = sqrtf(st / o.bias_corr2) + o.eps;
-#pragma unroll
-      for (int v = 0; v < NV; ++v) {
-        float4 m = *reinterpret_cast<float4*>(o.state_m + eoff + 4 * v);
-        float* mm = reinterpret_cast<float*>(&m);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          mm[e] = o.beta1 * mm[e] + (1.f - o.beta1) * g[4 * v + e];
-          wv[4 * v + e] -= lr * (mm[e] / o.bias_corr1) / denom;
-        }
-        *reinterpret_cast<float4*>(o.state_m + eoff + 4 * v) = m;
-      }
-    }
-  } else if (act) {
-    if (o.kind == kOptSgd) {
-#pragma unroll
-      for (int e = 0; e < 4 * NV; ++e) wv[e] -= lr * g[e];
-    } else if (o.kind == kOptAdagrad) {
-#pragma unroll
-      for (int v = 0; v < NV; ++v) {
-        float4 m = *reinterpret_cast<float4*>(o.state_m + eoff + 4 * v);
-        float* mm = reinterpret_cast<float*>(&m);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          mm[e] += g[4 * v + e] * g[4 * v + e];
-          wv[4 * v + e] -= lr * g[4 * v + e] / (sqrtf(mm[e]) + o.eps);
-        }
-        *reinterpret_cast<float4*>(o.state_m + eoff + 4 * v) = m;
-      }
-    } else if (o.kind == kOptAdam) {
-#pragma unroll
-      for (int v = 0; v < NV; ++v) {
-        float4 m = *reinterpret_cast<float4*>(o.state_m + eoff + 4 * v);
-        float4 s2 = *reinterpret_cast<float4*>(o.state_v + eoff + 4 * v);
-        float* mm = reinterpret_cast<float*>(&m);
-        float* vv = reinterpret_cast<float*>(&s2);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float ge = g[4 * v + e];
-          mm[e] = o.beta1 * mm[e] + (1.f - o.beta1) * ge;
-          vv[e] = o.beta2 * vv[e] + (1.f - o.beta2) * ge * ge;
-          wv[4 * v + e] -= lr * (mm[e] / o.bias_corr1) / (sqrtf(vv[e] / o.bias_corr2) + o.eps);
-        }
-        *reinterpret_cast<float4*>(o.state_m + eoff + 4 * v) = m;
-        *reinterpret_cast<float4*>(o.state_v + eoff + 4 * v) = s2;
-      }
-    }
-  }
-  if (act) {
-#pragma unroll
-    for (int v = 0; v < NV; ++v) store4<TW>(w + 4 * v, wv4[v]);
-  }
-}
-
 // 6. light rows: a group of G lanes per unique row, NV float4 per lane.  (A variant that loaded the
 // next row's metadata one iteration ahead and bulk-prefetched its weights / optimizer state into
 // L2 measured 0-5% slower on the DLRM benchmark.)
@@ -1442,7 +1313,13 @@ void emb_backward(const EmbBwdParams& p, int ncols_max, int grid, cudaStream_t s
   FLARE_CHECK(N < (1ll << 31) - 1, "staging space exceeds 2^31 occurrences");
   FLARE_CHECK(p.num_shards * p.world <= 1024, "at most 1024 (shard, source) slots");
   FLARE_CHECK(static_cast<int64_t>(p.world) * p.Bl * 64 < (1ll << 31), "too many pooled-gradient chunks");
-  FLARE_CUDA_CHECK(cudaMemsetAsync(p.num_unique, 0, 4 * sizeof(int), s));
+  FLARE_CUDA_CHECK(cudaMemsetAsync(p.num_unique, 0, (p.hash_mode ? 8 : 4) * sizeof(int), s));
+  if (p.hash_mode && !p.deterministic) {
+    emb_backward_hash(p, ncols_max, grid, s);
+    return;
+  }
+  FLARE_CHECK(p.row_count && p.row2u && p.pos && p.uniq_row && p.cnt_u && p.heavy && p.heavy_acc,
+              "the sorted backward needs its per-row scratch buffers");
   emb_slot_prefix_kernel<<<1, 1024, 0, s>>>(p);
   emb_bwd_pull_count_kernel<<<grid, kEmbThreads, 0, s>>>(p);
   if (p.deterministic) {

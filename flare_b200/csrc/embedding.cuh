@@ -129,7 +129,8 @@ struct EmbBwdParams {
   int* uniq_shard;
   int* cnt_u;       // occurrences of unique row u
   int* first_gidx;  // staged-grad row of u's first occurrence
-  int* num_unique;  // [0] U, [1] T (valid occurrences), [2] heavy rows
+  int* num_unique;  // [0] U, [1] T (valid occurrences), [2] heavy rows; hash path: [3] work chunks,
+                    // [4] single-occurrence rows, [5] other light rows, [6] overflow slots in use
   int* seg_start;   // [U+1]
   int* block_sums;
   int* occ;         // staged-grad row index per occurrence, grouped by unique row
@@ -150,6 +151,28 @@ struct EmbBwdParams {
   int* det_vals;
   void* det_temp;
   size_t det_temp_bytes;
+  // hash-dedup path (the default when not deterministic): an open-addressing table of the step's
+  // touched rows replaces the per-row count / index arrays, so the dedup stays in L2
+  int hash_mode;
+  int grad_direct;           // 1 (one GPU): read the pooled gradients in place, no pull into grad_stage
+  unsigned long long* htab;  // [hregion + hcap] slot word: key (local row, low 32 bits) | count (high 32); empty = 0xFFFFFFFF
+  int* hseg;                 // [hregion + hcap] segment start of an occupied slot's occurrences in occ, or
+                             // -1 - record index of a single-occurrence row
+  int* ovf_list;             // [max_occ] overflow-table slots in use this step
+  int64_t hcap;              // overflow table slots (power of two >= max_occ), after the region
+  int64_t hregion;           // region slots (power of two, or 0): the first probes of every key
+  int* occ_h;                // [max_occ] hash slot of compact occurrence k (-1: invalid id)
+  int* occ_rank;             // [max_occ] rank of k among its row's occurrences
+  int* occ_bag;              // [max_occ] bag index of k: slot * Bl + sample
+  int4* lrec;                // [max_occ] light-row records {row, slot, seg, count}: single-occurrence rows from
+                             // the front, the other light rows from the back
+  int4* crec;                // [max_chunks][2] work-chunk records {row, slot, first, len}, {part, chunk, chunks, count}
+  int64_t max_chunks;
+  float* hpart;              // [max_parts][ncols_max] fp32 partial sums of multi-chunk rows
+  int64_t max_parts;
+  float* occ_scale;          // [max_occ] 1 / bag length per grouped occurrence (mean pooling), or null
+  int* scan_val;             // [max_tiles][6] per-block totals of the slot scan
+  int64_t max_tiles;         // scan blocks at most
   SparseOptParams opt;
   uint32_t* flags_local;
   uint32_t* const* peer_flags;
@@ -162,6 +185,12 @@ struct EmbBwdParams {
 
 void emb_forward(const EmbFwdParams& p, int grid, cudaStream_t s);
 void emb_backward(const EmbBwdParams& p, int ncols_max, int grid, cudaStream_t s);
+void emb_backward_hash(const EmbBwdParams& p, int ncols_max, int grid, cudaStream_t s);
 size_t emb_det_temp_bytes(int64_t max_occ);
+// scratch sizes of the hash-dedup backward
+int64_t emb_hash_tile_count(int64_t max_occ);
+int64_t emb_hash_max_chunks(int64_t max_occ, int light_max);
+int64_t emb_hash_max_parts(int64_t max_occ);
+int emb_hash_scan_vals();
 
 }  // namespace flare

@@ -179,7 +179,10 @@ class ShardedEmbeddingBagCollection:
         self.slot_map = torch.full((max(smoff, 1),), -1, dtype=torch.int32, device=self.device) if smoff else None
         self.ncols_max = max([s.ncols for s in self.shards], default=4)
         self.vec = 2 if self.ncols_max > 128 else 1
+        gsize = torch.empty(0, dtype=grad_dtype).element_size()
         for s in self.shards:
+            if (s.ncols * gsize) % 16:
+                raise ValueError(f"shard width {s.ncols}: pooled-gradient rows must be a multiple of 16 bytes")
             g = s.ncols // (4 * self.vec)
             if g < 1 or g > 32 or (g & (g - 1)):
                 raise ValueError(f"shard width {s.ncols} unsupported with vec={self.vec}")
@@ -225,9 +228,6 @@ class ShardedEmbeddingBagCollection:
         self.lut = (torch.tensor(opt.custom_lut, dtype=torch.float32, device=dev)
                     if opt.dynamic_lr_policy == "custom_lut" else None)
 
-        # ---- per-row dedup scratch (returns to zero after every backward) ----
-        self.row_count = torch.zeros(max(rbase, 4), dtype=torch.int32, device=dev)
-        self.row2u = torch.zeros(max(rbase, 4), dtype=torch.int32, device=dev)
         # rows updated since the last checkpoint (incremental sparse saves)
         self.dirty = torch.zeros(max(rbase, 4), dtype=torch.uint8, device=dev)
 
@@ -250,31 +250,66 @@ class ShardedEmbeddingBagCollection:
         self.stage_rank = torch.empty(nslot * self.stage_cap, dtype=torch.int32, device=dev)
         self.slot_start = torch.zeros(nslot + 1, dtype=torch.int32, device=dev)
         self.grad_stage_ld = self.ncols_max
-        self.grad_stage = torch.empty(nslot * self.B * self.ncols_max, dtype=grad_dtype, device=dev)
         self.max_occ = nslot * self.stage_cap
         self.flags_occ = torch.empty(self.max_occ, dtype=torch.int32, device=dev)
-        self.pos = torch.empty(self.max_occ + 1, dtype=torch.int32, device=dev)
-        self.uniq_row = torch.empty(self.max_occ, dtype=torch.int64, device=dev)
-        self.uniq_shard = torch.empty(self.max_occ, dtype=torch.int32, device=dev)
-        self.cnt_u = torch.empty(self.max_occ, dtype=torch.int32, device=dev)
-        self.first_gidx = torch.empty(self.max_occ, dtype=torch.int32, device=dev)
-        self.num_unique = torch.zeros(4, dtype=torch.int32, device=dev)
+        self.num_unique = torch.zeros(8, dtype=torch.int32, device=dev)
         self.seg_start = torch.empty(self.max_occ + 1, dtype=torch.int32, device=dev)
-        self.block_sums = torch.empty(512, dtype=torch.int32, device=dev)
         self.occ = torch.empty(self.max_occ, dtype=torch.int32, device=dev)
-        # rows with more than light_max occurrences take the chunked path
-        self.max_heavy = min(self.max_occ // (self.light_max + 1) + 1, 1 << 20)
-        self.heavy = torch.empty(self.max_heavy, dtype=torch.int32, device=dev)
-        self.heavy_start = torch.empty(self.max_heavy + 1, dtype=torch.int32, device=dev)
-        self.hcnt = torch.empty(self.max_heavy, dtype=torch.int32, device=dev)
-        # one fp32 partial row per (heavy row, 256-occurrence chunk) segment
-        self.heavy_acc = torch.zeros((self.max_heavy + self.max_occ // 256 + 2) * 128 * self.vec,
-                                     dtype=torch.float32, device=dev)
         # deterministic-reduction mode (FLARE_DETERMINISTIC=1): rows add their occurrences in staging
         # order, so repeated runs are bitwise identical (a race detector for the sparse backward)
         if deterministic is None:
             deterministic = os.environ.get("FLARE_DETERMINISTIC", "0") == "1"
         self.deterministic = bool(deterministic)
+        # hash-dedup backward (default): the step's touched rows go into an open-addressing table that
+        # stays in L2; the sorted per-row path serves the deterministic mode (and FLARE_EMB_LEGACY_BWD=1)
+        # (its lanes cover 16 columns: every shard width a multiple of 16)
+        self.hash_bwd = (not self.deterministic and os.environ.get("FLARE_EMB_LEGACY_BWD", "0") != "1"
+                         and rbase < 2**32 - 1 and all(sh.ncols % 16 == 0 for sh in self.shards))
+        i32 = lambda n: torch.empty(max(int(n), 4), dtype=torch.int32, device=dev)  # noqa: E731
+        # pooled gradients pulled from every rank (at one GPU the hash path reads them where the dense
+        # backward wrote them)
+        # (16-byte gradient loads need 8-element-aligned rows for bf16 gradients)
+        aligned = grad_dtype == torch.float32 or (self.total_dim % 8 == 0 and all(sh.out_col % 8 == 0
+                                                                                 for sh in self.shards))
+        self.grad_direct = (self.hash_bwd and world_size == 1 and aligned
+                            and os.environ.get("FLARE_EMB_GRAD_STAGE", "0") != "1")
+        staged = not self.grad_direct
+        self.grad_stage = torch.empty(nslot * self.B * self.ncols_max if staged else 8, dtype=grad_dtype, device=dev)
+        if self.hash_bwd:
+            # touched-row table: a region sized for the step's unique rows (its slots are prefetched into L2
+            # and take every key's first probes) and an overflow table with room for every possible key
+            hcap = 1 << max(4, (self.max_occ - 1).bit_length())
+            self.hash_region_cap = min(hcap, 1 << 22)
+            tiles, max_chunks, max_parts, scan_vals = native().emb_hash_sizes(self.max_occ, self.light_max)
+            # slot word: key (low 32 bits) = 0xFFFFFFFF and count 0 when empty; every backward leaves it empty
+            self.htab = torch.full((self.hash_region_cap + hcap,), 0xFFFFFFFF, dtype=torch.int64, device=dev)
+            self.hash = dict(hcap=hcap, hregion=self.hash_region_cap, max_tiles=tiles, max_chunks=max_chunks,
+                             max_parts=max_parts, hseg=i32(self.hash_region_cap + hcap),
+                             ovf_list=i32(self.max_occ), occ_bag=i32(self.max_occ),
+                             lrec=i32(4 * self.max_occ), crec=i32(8 * max_chunks),
+                             hpart=torch.empty(max_parts * self.ncols_max, dtype=torch.float32, device=dev),
+                             occ_scale=(torch.empty(self.max_occ, dtype=torch.float32, device=dev)
+                                        if any(s.spec.pooling == "mean" for s in self.shards) else None),
+                             scan_val=torch.zeros(tiles * scan_vals, dtype=torch.int32, device=dev))
+        else:
+            self.htab, self.hash = None, None
+            # per-row dedup scratch (returns to zero after every backward)
+            self.row_count = torch.zeros(max(rbase, 4), dtype=torch.int32, device=dev)
+            self.row2u = torch.zeros(max(rbase, 4), dtype=torch.int32, device=dev)
+            self.pos = i32(self.max_occ + 1)
+            self.uniq_row = torch.empty(self.max_occ, dtype=torch.int64, device=dev)
+            self.uniq_shard = i32(self.max_occ)
+            self.cnt_u = i32(self.max_occ)
+            self.first_gidx = i32(self.max_occ)
+            self.block_sums = i32(512)
+            # rows with more than light_max occurrences take the chunked path
+            self.max_heavy = min(self.max_occ // (self.light_max + 1) + 1, 1 << 20)
+            self.heavy = i32(self.max_heavy)
+            self.heavy_start = i32(self.max_heavy + 1)
+            self.hcnt = i32(self.max_heavy)
+            # one fp32 partial row per (heavy row, 256-occurrence chunk) segment
+            self.heavy_acc = torch.zeros((self.max_heavy + self.max_occ // 256 + 2) * 128 * self.vec,
+                                         dtype=torch.float32, device=dev)
         self.det = None
         if self.deterministic:
             nbytes = int(native().emb_det_temp_bytes(self.max_occ))
@@ -447,30 +482,73 @@ class ShardedEmbeddingBagCollection:
             slot_start=self.slot_start.data_ptr(),
             stage_count=st["count"].data_ptr(), stage_len=st["len"].data_ptr(),
             stage_cap=self.stage_cap, weights=self.weights.data_ptr(), w_dtype=dtype_code(self.value_dtype),
-            row_count=self.row_count.data_ptr(), row2u=self.row2u.data_ptr(), flags=self.flags_occ.data_ptr(),
-            pos=self.pos.data_ptr(), uniq_row=self.uniq_row.data_ptr(), uniq_shard=self.uniq_shard.data_ptr(),
-            cnt_u=self.cnt_u.data_ptr(), first_gidx=self.first_gidx.data_ptr(),
-            num_unique=self.num_unique.data_ptr(), seg_start=self.seg_start.data_ptr(),
-            block_sums=self.block_sums.data_ptr(), occ=self.occ.data_ptr(), heavy=self.heavy.data_ptr(),
-            heavy_start=self.heavy_start.data_ptr(), hcnt=self.hcnt.data_ptr(), heavy_acc=self.heavy_acc.data_ptr(), max_heavy=self.max_heavy,
+            flags=self.flags_occ.data_ptr(), num_unique=self.num_unique.data_ptr(),
+            seg_start=self.seg_start.data_ptr(), occ=self.occ.data_ptr(),
             light_max=self.light_max, max_occ=self.max_occ, opt=op, dirty=self.dirty.data_ptr(),
             flags_local=self.flags.local_ptr, peer_flags=self.flags.peer_ptrs.data_ptr(),
             flag_in=self.flags.slots(FLAG_BWD_IN), epoch_ctr=self.flags.epoch_ptr(FLAG_BWD_IN),
             block_counter=self.flags.block_counter_ptr(FLAG_BWD_IN), status=self.status.ptr,
             timeout_ns=self.timeout_ns, ncols_max=self.ncols_max, grid=self.grid,
         )
+        if self.hash is not None:
+            h = self.hash
+            self._tune_hash_region()
+            d.update(hash_mode=1, grad_direct=int(self.grad_direct), htab=self.htab.data_ptr(), hcap=h["hcap"],
+                     hregion=h["hregion"],
+                     occ_h=self.flags_occ.data_ptr(),
+                     occ_rank=self.stage_rank.data_ptr(), max_tiles=h["max_tiles"], max_chunks=h["max_chunks"],
+                     max_parts=h["max_parts"],
+                     occ_scale=h["occ_scale"].data_ptr() if h["occ_scale"] is not None else 0,
+                     **{k: h[k].data_ptr() for k in ("hseg", "ovf_list", "occ_bag", "lrec", "crec", "hpart",
+                                                     "scan_val")})
+        else:
+            d.update(row_count=self.row_count.data_ptr(), row2u=self.row2u.data_ptr(), pos=self.pos.data_ptr(),
+                     uniq_row=self.uniq_row.data_ptr(), uniq_shard=self.uniq_shard.data_ptr(),
+                     cnt_u=self.cnt_u.data_ptr(), first_gidx=self.first_gidx.data_ptr(),
+                     block_sums=self.block_sums.data_ptr(), heavy=self.heavy.data_ptr(),
+                     heavy_start=self.heavy_start.data_ptr(), hcnt=self.hcnt.data_ptr(),
+                     heavy_acc=self.heavy_acc.data_ptr(), max_heavy=self.max_heavy)
         if self.det is not None:
             d.update(deterministic=1, det_first=self.det["first"].data_ptr(), det_keys=self.det["keys"].data_ptr(),
                      det_vals=self.det["vals"].data_ptr(),
                      det_temp=self.det["temp"].data_ptr(), det_temp_bytes=self.det["bytes"])
         native().emb_backward(d)
 
+    def _tune_hash_region(self) -> None:
+        """Size the L2 region of the touched-row table from the first backward's unique-row count.
+
+        The first backward runs with the largest region and copies its count to pinned host memory
+        behind an event; a later call outside stream capture reads it (once the event completed) and
+        keeps the region at 1.6x that count, rounded up to a power of two.  Keys beyond the region's
+        probes go to the overflow table, so the choice affects speed only."""
+        h = self.hash
+        if h.get("tuned"):
+            return
+        if torch.cuda.is_current_stream_capturing():
+            return
+        if "probe" not in h:
+            h["probe"] = torch.empty(1, dtype=torch.int32, pin_memory=True)
+            h["probe_ev"] = None
+            return
+        if h["probe_ev"] is None:
+            h["probe"].copy_(self.num_unique[:1], non_blocking=True)
+            h["probe_ev"] = torch.cuda.Event()
+            h["probe_ev"].record()
+            return
+        if not h["probe_ev"].query():
+            return
+        u = int(h["probe"][0])
+        if u > 0:
+            want = 1 << max(12, int(u * 1.6 - 1).bit_length())
+            h["hregion"] = min(self.hash_region_cap, want)
+        h["tuned"] = True
+
     def check(self) -> None:
         self.status.check("sharded embedding")
 
     def last_step_stats(self) -> dict:
         """Unique rows, valid occurrences and heavy rows of the last backward (device sync)."""
-        u, t, h, _ = self.num_unique.tolist()
+        u, t, h = self.num_unique.tolist()[:3]
         return {"unique_rows": u, "occurrences": t, "heavy_rows": h}
 
     # ------------------------------------------------------------ state I/O
@@ -546,10 +624,13 @@ class ShardedEmbeddingBagCollection:
                 self.score[s.row_base:s.row_base + s.storage_rows].copy_(entry["score"])
 
     def memory_bytes(self) -> int:
-        tensors = [self.weights, self.state_row, self.state_m, self.state_v, self.score, self.row_count,
-                   self.row2u, self.stage_ids, self.stage_bag, self.stage_rank, self.grad_stage, self.uniq_row,
-                   self.occ, self.seg_start, self.flags_occ, self.pos, self.cnt_u, self.first_gidx, self.heavy,
-                   self.heavy_acc]
+        tensors = [self.weights, self.state_row, self.state_m, self.state_v, self.score, self.stage_ids,
+                   self.stage_bag, self.stage_rank, self.grad_stage, self.occ, self.seg_start, self.flags_occ]
+        if self.hash is not None:
+            tensors += [self.htab] + [v for v in self.hash.values() if isinstance(v, torch.Tensor)]
+        else:
+            tensors += [self.row_count, self.row2u, self.uniq_row, self.pos, self.cnt_u, self.first_gidx,
+                        self.heavy, self.heavy_acc]
         return sum(t.numel() * t.element_size() for t in tensors if t is not None)
 
 

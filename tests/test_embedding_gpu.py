@@ -89,9 +89,28 @@ def _cw_plan(tables):
     return ShardingPlan(1, tuple(pl), tuple(out), c)
 
 
+def _assert_scratch_clean(coll):
+    """Every backward leaves its dedup scratch as it found it (hash table empty / row counters zero)."""
+    if coll.hash_bwd:
+        assert bool((coll.htab == 0xFFFFFFFF).all())
+    else:
+        assert int(coll.row_count.abs().max()) == 0
+
+
+@pytest.fixture(params=["hash", "sorted", "hash_staged"])
+def bwd_path(request, monkeypatch):
+    """The hash-dedup backward (gradients read in place, or pulled into the staging buffer as on several
+    GPUs) and the sorted per-row backward."""
+    if request.param == "sorted":
+        monkeypatch.setenv("FLARE_EMB_LEGACY_BWD", "1")
+    if request.param == "hash_staged":
+        monkeypatch.setenv("FLARE_EMB_GRAD_STAGE", "1")
+    return request.param
+
+
 @pytest.mark.parametrize("kind", ["rowwise_adagrad", "adam", "sgd", "adagrad", "rowwise_adam"])
 @pytest.mark.parametrize("split", ["none", "column", "row"])
-def test_forward_backward_matches_reference(cuda, kind, split):
+def test_forward_backward_matches_reference(cuda, kind, split, bwd_path):
     torch.manual_seed(0)
     column_split = split == "column"
     opt = SparseOptimizerConfig(kind=kind, learning_rate=0.05, weight_decay=0.001)
@@ -104,6 +123,8 @@ def test_forward_backward_matches_reference(cuda, kind, split):
     plan = _cw_plan(tables) if column_split else None
     coll = ShardedEmbeddingBagCollection(tables, B, max_bag_size=max_bag, device=cuda, plan=plan, optimizer=opt,
                                          seed=3, light_max=3)
+    assert coll.hash_bwd == (bwd_path != "sorted")
+    assert coll.grad_direct == (bwd_path == "hash")
     ref = CpuEmbeddingBagCollection(tables, B, optimizer=opt, weights=_export(coll, tables))
     split_ref = column_split and opt.needs_row_state
     if split_ref:
@@ -125,11 +146,11 @@ def test_forward_backward_matches_reference(cuda, kind, split):
         coll.check()
         for w_gpu, w_ref in zip(_export(coll, tables), ref.weights):
             torch.testing.assert_close(w_gpu, w_ref, rtol=1e-4, atol=1e-5)
-    assert int(coll.row_count.abs().max()) == 0  # per-row counters returned to zero
+    _assert_scratch_clean(coll)
 
 
-def test_hot_rows_heavy_path(cuda):
-    """A few rows hit thousands of times (Zipf head) take the block-per-row path."""
+def test_hot_rows_heavy_path(cuda, bwd_path):
+    """A few rows hit thousands of times (Zipf head): chunked across warps, partials added in order."""
     opt = SparseOptimizerConfig(kind="rowwise_adagrad", learning_rate=0.1)
     tables = [SparseTableSpec("hot", 4, 128, optimizer=opt)]
     B, max_bag = 512, 32
@@ -147,7 +168,9 @@ def test_hot_rows_heavy_path(cuda):
     coll.check()
     torch.testing.assert_close(_export(coll, tables)[0], ref.weights[0], rtol=1e-4, atol=1e-5)
     assert int(coll.num_unique[2]) > 0  # the heavy path ran
-    assert int(coll.row_count.abs().max()) == 0
+    if coll.hash_bwd:
+        assert int(coll.num_unique[3]) > 4  # rows of more than 256 occurrences were cut into several chunks
+    _assert_scratch_clean(coll)
 
 
 def test_lr_policies(cuda):
@@ -215,3 +238,31 @@ def test_deterministic_mode_is_bitwise_repeatable(cuda):
         runs.append(_export(coll, tables))
     for a, b in zip(*runs):
         assert torch.equal(a, b)
+
+
+def test_many_unique_rows_across_tiles(cuda, bwd_path):
+    """Tens of thousands of distinct rows: many counting tiles, many scan tiles chained by look-back,
+    light, single-chunk and multi-chunk rows in one step; two steps so the emptied table is reused."""
+    opt = SparseOptimizerConfig(kind="rowwise_adagrad", learning_rate=0.05)
+    vocabs = [200_000, 3_000]
+    tables = [SparseTableSpec(f"t{i}", v, 128, optimizer=opt) for i, v in enumerate(vocabs)]
+    B, max_bag = 2048, 32
+    coll = ShardedEmbeddingBagCollection(tables, B, max_bag_size=max_bag, device=cuda, optimizer=opt, seed=2)
+    ref = CpuEmbeddingBagCollection(tables, B, optimizer=opt, weights=_export(coll, tables))
+    for step in (1, 2):
+        offs, vals = _batch(B, vocabs, max_bag, seed=40 + step, zipf=1.05)
+        coll.set_input(offs.to(cuda), vals.to(cuda), non_blocking=False)
+        ref.set_input(offs, vals)
+        coll.forward()
+        ref.forward()
+        grad = (torch.randn(B, coll.total_dim) * 0.1).to(torch.bfloat16)
+        coll.grad_input.copy_(grad.to(cuda))
+        coll.backward(step)
+        ref.backward(grad.float(), step)
+        torch.cuda.synchronize()
+        coll.check()
+        stats = coll.last_step_stats()
+        assert stats["unique_rows"] > 5000 and stats["heavy_rows"] > 0
+        for w_gpu, w_ref in zip(_export(coll, tables), ref.weights):
+            torch.testing.assert_close(w_gpu, w_ref, rtol=1e-4, atol=1e-5)
+    _assert_scratch_clean(coll)
