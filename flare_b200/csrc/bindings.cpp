@@ -345,6 +345,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       p.ovf_list = P<int>(get<uintptr_t>(d, "ovf_list"));
       p.hcap = get<int64_t>(d, "hcap");
       p.hregion = get_or<int64_t>(d, "hregion", 0);
+      p.hprefetch = get_or<int>(d, "hprefetch", 1);
       p.grad_direct = get_or<int>(d, "grad_direct", 0);
       p.occ_h = P<int>(get<uintptr_t>(d, "occ_h"));
       p.occ_rank = P<int>(get<uintptr_t>(d, "occ_rank"));

@@ -161,6 +161,7 @@ struct EmbBwdParams {
   int* ovf_list;             // [max_occ] overflow-table slots in use this step
   int64_t hcap;              // overflow table slots (power of two >= max_occ), after the region
   int64_t hregion;           // region slots (power of two, or 0): the first probes of every key
+  int hprefetch;             // 1: the counting pass prefetches the region into L2
   int* occ_h;                // [max_occ] hash slot of compact occurrence k (-1: invalid id)
   int* occ_rank;             // [max_occ] rank of k among its row's occurrences
   int* occ_bag;              // [max_occ] bag index of k: slot * Bl + sample

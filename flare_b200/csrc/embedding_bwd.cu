@@ -95,7 +95,7 @@ __global__ void __launch_bounds__(kHThreads) emb_hash_count_kernel(EmbBwdParams 
   __shared__ long long slot_rb[1024];   // row base of each slot's shard
   __shared__ int s_valid;
   // the region of the touched-row table into L2 first (its slots take this step's atomics)
-  {
+  if (p.hprefetch) {
     const int64_t rbytes = p.hregion * 8;
     for (int64_t off = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4096; off < rbytes;
          off += static_cast<int64_t>(gridDim.x) * blockDim.x * 4096)

@@ -494,7 +494,7 @@ class ShardedEmbeddingBagCollection:
             h = self.hash
             self._tune_hash_region()
             d.update(hash_mode=1, grad_direct=int(self.grad_direct), htab=self.htab.data_ptr(), hcap=h["hcap"],
-                     hregion=h["hregion"],
+                     hregion=h["hregion"], hprefetch=0 if os.environ.get("FLARE_EMB_HASH_PREFETCH") == "0" else 1,
                      occ_h=self.flags_occ.data_ptr(),
                      occ_rank=self.stage_rank.data_ptr(), max_tiles=h["max_tiles"], max_chunks=h["max_chunks"],
                      max_parts=h["max_parts"],
@@ -517,30 +517,20 @@ class ShardedEmbeddingBagCollection:
     def _tune_hash_region(self) -> None:
         """Size the L2 region of the touched-row table from the first backward's unique-row count.
 
-        The first backward runs with the largest region and copies its count to pinned host memory
-        behind an event; a later call outside stream capture reads it (once the event completed) and
-        keeps the region at 1.6x that count, rounded up to a power of two.  Keys beyond the region's
-        probes go to the overflow table, so the choice affects speed only."""
+        The first backward runs with the largest region; the next call made outside stream capture
+        reads its count (one device sync, during warm-up) and keeps the region at 1.6x that count,
+        rounded up to a power of two, for every later step, so a CUDA graph captured after the
+        warm-up steps records the tuned region.  Keys beyond the region's probes go to the overflow
+        table, so the choice affects speed only."""
         h = self.hash
-        if h.get("tuned"):
+        if h.get("tuned") or torch.cuda.is_current_stream_capturing():
             return
-        if torch.cuda.is_current_stream_capturing():
+        if not h.get("ran"):
+            h["ran"] = True
             return
-        if "probe" not in h:
-            h["probe"] = torch.empty(1, dtype=torch.int32, pin_memory=True)
-            h["probe_ev"] = None
-            return
-        if h["probe_ev"] is None:
-            h["probe"].copy_(self.num_unique[:1], non_blocking=True)
-            h["probe_ev"] = torch.cuda.Event()
-            h["probe_ev"].record()
-            return
-        if not h["probe_ev"].query():
-            return
-        u = int(h["probe"][0])
+        u = int(self.num_unique[0].item())
         if u > 0:
-            want = 1 << max(12, int(u * 1.6 - 1).bit_length())
-            h["hregion"] = min(self.hash_region_cap, want)
+            h["hregion"] = min(self.hash_region_cap, 1 << max(12, int(u * 1.6 - 1).bit_length()))
         h["tuned"] = True
 
     def check(self) -> None:

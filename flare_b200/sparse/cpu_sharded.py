@@ -51,7 +51,7 @@ class ShardedCpuEmbeddingBagCollection:
                  CpuEmbeddingBagCollection([tables[f]], 1, optimizer=opt, seed=seed * 1_000_003 + f).weights[0]
                  for f in self.owned]
             self.local = CpuEmbeddingBagCollection([tables[f] for f in self.owned], self.world * self.B, optimizer=opt,
-                                                   weights=w, native=native)
+                                                   weights=w, native=native, seed=seed)
 
     def _a2a(self, send: list[torch.Tensor], recv_sizes: list[int], dtype) -> list[torch.Tensor]:
         out = torch.empty(sum(recv_sizes), dtype=dtype)
@@ -133,6 +133,7 @@ class ShardedCpuEmbeddingBagCollection:
         states = [states] if isinstance(states, dict) else list(states)
         if self.local is None:
             return
+        # every table's entry carries its own row-init stream, so the union restores each table exactly
         merged = {"tables": {}, "dynamic": {}, "step": max(int(s.get("step", 0)) for s in states)}
         for s in states:
             merged["tables"].update(s["tables"])

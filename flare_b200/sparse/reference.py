@@ -127,6 +127,13 @@ def apply_rows_reference(opt: SparseOptimizerConfig, step: int, w: torch.Tensor,
     w[rows] = wr.to(w.dtype)
 
 
+def _table_stream_seed(seed: int, name: str) -> int:
+    """Seed of a table's row-init stream: a function of the run seed and the table's name only."""
+    import zlib
+
+    return (int(seed) * 1_000_003 + 17 + zlib.crc32(name.encode())) & 0x7FFFFFFFFFFFFFFF
+
+
 class CpuEmbeddingBagCollection:
     """Whole tables on the host; same forward/backward contract as the GPU collection.
 
@@ -153,7 +160,9 @@ class CpuEmbeddingBagCollection:
         # hash-keyed tables: any int64 key; a native key -> slot map inserts on first sight (LFU eviction
         # when full) and the table's rows are indexed by slot
         self.maps = {}
-        self._init_gen = torch.Generator().manual_seed(seed * 1_000_003 + 17)
+        # one row-init generator per table, seeded from (seed, table name): rows of keys inserted later
+        # draw from their own table's stream, whichever rank owns the table and whatever else it owns
+        self._init_gens = [torch.Generator().manual_seed(_table_stream_seed(seed, t.name)) for t in self.tables]
         if any(t.dynamic for t in self.tables):
             from .._native import native as _nat
 
@@ -200,7 +209,7 @@ class CpuEmbeddingBagCollection:
 
     def _init_rows(self, f: int, rows: torch.Tensor) -> None:
         t = self.tables[f]
-        w = (torch.rand(rows.numel(), t.embedding_dim, generator=self._init_gen) * 2 - 1) * t.init_scale
+        w = (torch.rand(rows.numel(), t.embedding_dim, generator=self._init_gens[f]) * 2 - 1) * t.init_scale
         if self.stores is not None:
             rec = torch.zeros(rows.numel(), sum(wd for _, wd in self.layouts[f]))
             rec[:, :t.embedding_dim] = w
@@ -350,9 +359,10 @@ class CpuEmbeddingBagCollection:
                 tables[t.name] = {k: v.clone() for k, v in parts.items()}
             else:
                 tables[t.name] = {"weight": self.weights[f].clone(), **{k: v.clone() for k, v in self.state[f].items()}}
+            # the table's row-init stream travels with the table (rows of keys inserted later draw from it)
+            tables[t.name]["init_rng"] = self._init_gens[f].get_state()
         dynamic = {self.tables[f].name: tuple(x.clone() for x in m.items()) for f, m in self.maps.items()}
-        return {"step": self.step, "optimizer": self.optimizer.kind, "tables": tables, "dynamic": dynamic,
-                "init_rng": self._init_gen.get_state()}  # rows of keys inserted later draw from it
+        return {"step": self.step, "optimizer": self.optimizer.kind, "tables": tables, "dynamic": dynamic}
 
     def load_state_dict(self, state: dict) -> None:
         if state.get("optimizer", self.optimizer.kind) != self.optimizer.kind:
@@ -361,6 +371,8 @@ class CpuEmbeddingBagCollection:
             if t.name not in state["tables"]:
                 raise ValueError(f"table {t.name} is not in the checkpoint")
             st = state["tables"][t.name]
+            if "init_rng" in st:
+                self._init_gens[f].set_state(st["init_rng"])
             if self.stores is not None:
                 rec = torch.cat([st[n].float().reshape(t.num_embeddings, -1) for n, _ in self.layouts[f]], 1)
                 self.stores[f].scatter(torch.arange(t.num_embeddings), rec)
@@ -370,8 +382,6 @@ class CpuEmbeddingBagCollection:
                     v.copy_(st[k])
         for f, m in self.maps.items():
             m.load(*state["dynamic"][self.tables[f].name])
-        if "init_rng" in state:
-            self._init_gen.set_state(state["init_rng"])
         self.step = int(state["step"])
 
     def storage_stats(self) -> list[dict]:

@@ -112,3 +112,76 @@ def test_sharded_state_restores_at_another_world_size():
             c.backward(torch.tanh(y) * 0.5)
     for f in range(len(TABLES)):
         torch.testing.assert_close(resumed.table_weights(f), ref.table_weights(f), rtol=0, atol=0)
+
+
+DYN_TABLES = [SparseTableSpec("d0", 64, 8, optimizer=OPT, dynamic=True),
+              SparseTableSpec("s1", 30, 4, optimizer=OPT),
+              SparseTableSpec("d2", 48, 4, optimizer=OPT, dynamic=True)]
+
+
+def _dyn_batch(step, world):
+    """Keys of the dynamic tables widen with the step: later steps insert keys never seen before."""
+    g = torch.Generator().manual_seed(300 + step)
+    GB = B * world
+    lens = torch.randint(1, 4, (len(DYN_TABLES), GB), generator=g)
+    ids = []
+    for f, t in enumerate(DYN_TABLES):
+        hi = 1000 * (f + 1) + 5 * (step + 1) if t.dynamic else t.num_embeddings
+        lo = 1000 * (f + 1) if t.dynamic else 0
+        ids.append(torch.randint(lo, hi, (int(lens[f].sum()),), generator=g))
+    return lens, ids
+
+
+def _dyn_local(lens, ids, rank, bsz):
+    vals, ls = [], []
+    for f in range(len(DYN_TABLES)):
+        cum = torch.cat([torch.zeros(1, dtype=torch.long), lens[f].cumsum(0)])
+        lo, hi = int(cum[rank * bsz]), int(cum[(rank + 1) * bsz])
+        vals.append(ids[f][lo:hi])
+        ls.append(lens[f][rank * bsz:(rank + 1) * bsz])
+    ls = torch.cat(ls)
+    return torch.cat([torch.zeros(1, dtype=torch.long), ls.cumsum(0)]).int(), torch.cat(vals).int()
+
+
+def _dyn_steps(c, rank, world, bsz, steps):
+    for s in steps:
+        lens, ids = _dyn_batch(s, world)
+        c.set_input(*_dyn_local(lens, ids, rank, bsz))
+        y = c.forward()
+        c.backward(torch.tanh(y) * 0.5)
+
+
+def _dyn_train_save(rank, world):
+    from flare_b200.sparse.cpu_sharded import ShardedCpuEmbeddingBagCollection
+
+    c = ShardedCpuEmbeddingBagCollection(DYN_TABLES, B, optimizer=OPT, seed=7)
+    _dyn_steps(c, rank, world, B, range(2))
+    return c.state_dict()
+
+
+def _dyn_resume_two(rank, world, states):
+    from flare_b200.sparse.cpu_sharded import ShardedCpuEmbeddingBagCollection
+
+    c = ShardedCpuEmbeddingBagCollection(DYN_TABLES, B, optimizer=OPT, seed=123)  # the state brings the streams
+    c.load_state_dict(states)
+    _dyn_steps(c, rank, world, B, range(2, 5))
+    return {f: c.table_weights(f) for f in range(len(DYN_TABLES)) if c.table_weights(f) is not None}
+
+
+def test_dynamic_tables_resume_bitwise_with_new_keys_after_the_restore():
+    """Hash-keyed tables keep inserting keys after a restore; their new rows come from each table's
+    own init stream, carried in the checkpoint, so a resumed run matches the straight-through run
+    bitwise at the same world size and at another one."""
+    from flare_b200.sparse.cpu_sharded import ShardedCpuEmbeddingBagCollection
+
+    states = run_ranks(_dyn_train_save, 2)
+    ref = ShardedCpuEmbeddingBagCollection(DYN_TABLES, 2 * B, optimizer=OPT, seed=7)
+    _dyn_steps(ref, 0, 2, 2 * B, range(5))
+    one = ShardedCpuEmbeddingBagCollection(DYN_TABLES, 2 * B, optimizer=OPT, seed=0)
+    one.load_state_dict(states)
+    _dyn_steps(one, 0, 2, 2 * B, range(2, 5))
+    two = run_ranks(_dyn_resume_two, 2, states)
+    merged = {f: w for part in two for f, w in part.items()}
+    for f in range(len(DYN_TABLES)):
+        torch.testing.assert_close(one.table_weights(f), ref.table_weights(f), rtol=0, atol=0)
+        torch.testing.assert_close(merged[f], ref.table_weights(f), rtol=0, atol=0)
