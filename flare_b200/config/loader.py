@@ -42,22 +42,41 @@ def resolve_environment(value: Any) -> Any:
     return value
 
 
+def _flatten(config: Mapping[str, Any], prefix: str = "") -> list[tuple[str, Any]]:
+    """Leaves of a nested mapping as (dotted path, value), in the mapping's order; None leaves dropped."""
+    out: list[tuple[str, Any]] = []
+    pending: list[tuple[str, Any]] = [(prefix, config)]
+    while pending:
+        path, node = pending.pop()
+        if isinstance(node, Mapping):
+            # pushed in reverse so the mapping's own order comes out first
+            pending.extend((f"{path}{k}." if isinstance(v, Mapping) else f"{path}{k}", v)
+                           for k, v in reversed(list(node.items())))
+        elif node is not None:
+            out.append((path, node))
+    return out
+
+
+def _cli_tokens(flag: str, value: Any) -> list[str]:
+    """One leaf in the command-line grammar of the configs."""
+    if isinstance(value, bool):
+        return [f"--{flag}" if value else f"--no-{flag}"]
+    if isinstance(value, (list, tuple)):
+        tokens: list[str] = []
+        for item in value:  # the flag repeats once per item; structured items travel as JSON
+            tokens += [f"--{flag}", json.dumps(item) if isinstance(item, (Mapping, list)) else str(item)]
+        return tokens
+    return [f"--{flag}", str(value)]
+
+
 def dict_to_cli_args(config: Mapping[str, Any], prefix: str = "") -> list[str]:
-    """Nested mapping -> ``--a.b-c value`` arguments (bools: ``--x`` / ``--no-x``; lists repeat the flag)."""
+    """Nested mapping -> ``--a.b-c value`` arguments (bools: ``--x`` / ``--no-x``; lists repeat the flag).
+
+    The grammar is the configs' command-line interface: dotted paths for nesting, ``-`` for ``_``
+    in names, ``None`` values left out."""
     args: list[str] = []
-    for key, value in config.items():
-        if value is None:
-            continue
-        name = f"{prefix}{key}".replace("_", "-")
-        if isinstance(value, Mapping):
-            args += dict_to_cli_args(value, f"{prefix}{key}.")
-        elif isinstance(value, bool):
-            args.append(f"--{name}" if value else f"--no-{name}")
-        elif isinstance(value, (list, tuple)):
-            for item in value:
-                args += [f"--{name}", json.dumps(item) if isinstance(item, (dict, list)) else str(item)]
-        else:
-            args += [f"--{name}", str(value)]
+    for path, value in _flatten(config, prefix):
+        args += _cli_tokens(path.replace("_", "-"), value)
     return args
 
 

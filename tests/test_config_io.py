@@ -100,3 +100,32 @@ def test_cli_group_ids_first_id_of_a_feature():
     vals = torch.tensor([1, 2, 3, 7, 8, 9], dtype=torch.int32)
     assert group_ids(offs, vals, 1, 3).tolist() == [7, -1, 9]
     assert group_ids(offs, vals, 0, 3).tolist() == [1, 2, 3]
+
+
+def test_publish_bytes_create_mode_first_writer_wins(tmp_path):
+    from flare_b200.io.artifacts import companion_file, publish_bytes
+
+    p = tmp_path / "lease.json"
+    publish_bytes(p, b"one", mode="create")
+    try:
+        publish_bytes(p, b"two", mode="create")
+        raise AssertionError("a second create must fail")
+    except FileExistsError:
+        pass
+    assert p.read_bytes() == b"one"
+    publish_bytes(p, b"three")  # replace supersedes
+    assert p.read_bytes() == b"three"
+    assert not [q for q in tmp_path.iterdir() if q.name.endswith(".partial")]  # no scratch left behind
+    assert companion_file(p, ".sha").name == "lease.json.sha"
+
+
+def test_process_sessions_are_cached_per_settings():
+    from flare_b200.io.http import HttpSettings, process_session
+
+    a, b = process_session(), process_session()
+    c = process_session(HttpSettings(retries=2))
+    assert a is b and a is not c
+    opts = HttpSettings().socket_options()
+    import socket
+
+    assert (socket.SOL_SOCKET, socket.SO_KEEPALIVE, 1) in opts
