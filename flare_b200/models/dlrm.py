@@ -376,6 +376,61 @@ class DLRM:
 # ---------------------------------------------------------------------------
 # Plain PyTorch reference / baseline
 # ---------------------------------------------------------------------------
+class RowwiseAdagradTorch:
+    """Row-wise Adagrad for ``nn.EmbeddingBag(sparse=True)`` tables in plain PyTorch.
+
+    Per touched row r with summed gradient g_r (plus weight decay): state_r += mean(g_r^2) over the
+    row's columns; w_r -= lr * g_r / (sqrt(state_r) + eps) -- the update of the fused kernels and of
+    the reference's row-wise optimizer (src/flare/runtime/fluxway/workers/dynamic_embedding.py:481-549).
+    ``all_gather_grads``: with replicated tables on several ranks, every rank applies the union of all
+    ranks' sparse gradients, each divided by the world size (the global-mean gradient)."""
+
+    def __init__(self, params, lr: float = 0.01, eps: float = 1e-8, weight_decay: float = 0.0,
+                 all_gather_grads: bool = False):
+        self.params = list(params)
+        self.lr, self.eps, self.wd = float(lr), float(eps), float(weight_decay)
+        self.state = [torch.zeros(p.shape[0], device=p.device) for p in self.params]
+        self.gather = all_gather_grads
+
+    def zero_grad(self) -> None:
+        for p in self.params:
+            p.grad = None
+
+    @torch.no_grad()
+    def step(self) -> None:
+        import torch.distributed as dist
+
+        for p, st in zip(self.params, self.state):
+            if p.grad is None:
+                continue
+            g = p.grad.coalesce()
+            idx, val = g.indices()[0], g.values().float()
+            if self.gather and dist.is_initialized() and dist.get_world_size() > 1:
+                w = dist.get_world_size()
+                n = torch.tensor([idx.numel()], device=idx.device)
+                ns = [torch.zeros_like(n) for _ in range(w)]
+                dist.all_gather(ns, n)
+                m = int(max(int(x) for x in ns))
+                pad_i = torch.full((m,), -1, dtype=idx.dtype, device=idx.device)
+                pad_v = torch.zeros((m, val.shape[1]), device=val.device)
+                pad_i[:idx.numel()], pad_v[:idx.numel()] = idx, val
+                gi = [torch.empty_like(pad_i) for _ in range(w)]
+                gv = [torch.empty_like(pad_v) for _ in range(w)]
+                dist.all_gather(gi, pad_i)
+                dist.all_gather(gv, pad_v)
+                allv = torch.cat(gv) / w
+                alli = torch.cat(gi)
+                keep = alli >= 0
+                g = torch.sparse_coo_tensor(alli[keep].unsqueeze(0), allv[keep], p.shape).coalesce()
+                idx, val = g.indices()[0], g.values()
+            rows = p.data[idx].float()
+            if self.wd:
+                val = val + self.wd * rows
+            st.index_add_(0, idx, (val * val).mean(1))
+            scale = self.lr / (st[idx].sqrt() + self.eps)
+            p.data[idx] = (rows - scale.unsqueeze(1) * val).to(p.dtype)
+
+
 class DLRMTorch(nn.Module):
     """DLRM in plain PyTorch: nn.EmbeddingBag (sum), nn.Linear towers, dot interaction."""
 
@@ -449,4 +504,4 @@ class DLRMTorch(nn.Module):
             return self.head(h).float()
 
 
-__all__ = ["DLRM", "DLRMConfig", "DLRMTorch", "dlrm_benchmark_tables"]
+__all__ = ["RowwiseAdagradTorch", "DLRM", "DLRMConfig", "DLRMTorch", "dlrm_benchmark_tables"]
