@@ -23,6 +23,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from ..ops.dense import colsum_
 from ..ops.gemm import gemm
 
 
@@ -48,6 +49,11 @@ def fp32_rms_normalize(x: torch.Tensor, dim: int = -1, eps: float = 1e-5) -> tor
 
 # ----------------------------------------------------------- tcgen05 linear
 class _TcLinearFn(torch.autograd.Function):
+    """y = x W^T + b on the tcgen05 GEMM.  A weight bound to a flat fused optimizer (it carries
+    ``_flare_grad``, an fp32 view of the flat gradient buffer) receives ``dW`` straight from the GEMM
+    epilogue (accumulated in fp32) and its bias ``db`` from a column-sum kernel; autograd then gets no
+    gradient for them.  An unbound weight gets an ordinary fp32 gradient."""
+
     @staticmethod
     def forward(ctx, x, w, b):
         x2 = x.reshape(-1, x.shape[-1]).contiguous()
@@ -57,16 +63,26 @@ class _TcLinearFn(torch.autograd.Function):
         ctx.save_for_backward(x2, wb)
         ctx.has_bias = b is not None
         ctx.shape = x.shape
+        ctx.flat_w = getattr(w, "_flare_grad", None)
+        ctx.flat_b = getattr(b, "_flare_grad", None) if b is not None else None
         return y.reshape(*x.shape[:-1], w.shape[0])
 
     @staticmethod
     def backward(ctx, gy):
         x2, wb = ctx.saved_tensors
         g2 = gy.reshape(-1, gy.shape[-1]).to(torch.bfloat16).contiguous()
-        dx = gemm(g2, wb, b_t=True).reshape(ctx.shape)
-        dw = torch.zeros(wb.shape, dtype=torch.float32, device=wb.device)
-        gemm(g2, x2, a_t=True, b_t=True, out=dw, accumulate=True)
-        db = g2.float().sum(0) if ctx.has_bias else None
+        dx = gemm(g2, wb, b_t=True).reshape(ctx.shape) if ctx.needs_input_grad[0] else None
+        dw = db = None
+        if ctx.flat_w is not None:
+            gemm(g2, x2, a_t=True, b_t=True, out=ctx.flat_w, accumulate=True)
+        elif ctx.needs_input_grad[1]:
+            dw = torch.zeros(wb.shape, dtype=torch.float32, device=wb.device)
+            gemm(g2, x2, a_t=True, b_t=True, out=dw, accumulate=True)
+        if ctx.has_bias:
+            if ctx.flat_b is not None:
+                colsum_(g2, ctx.flat_b)
+            elif ctx.needs_input_grad[2]:
+                db = g2.float().sum(0)
         return dx, dw, db
 
 

@@ -64,12 +64,21 @@ class MultiTargetCrossEntropyLoss:
                 weights[ti, label_map[lab]] = abs(float(w))
         return cls(labels, weights, cw, targets)
 
+    def _tables(self, dev: torch.device) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """The label / weight tables on ``dev``, copied there once (later calls make no host transfer,
+        so a step that uses the loss can be captured in a CUDA graph after one eager call)."""
+        cache = self.__dict__.setdefault("_device_tables", {})
+        key = str(dev)
+        if key not in cache:
+            cache[key] = tuple(torch.as_tensor(a, device=dev)
+                               for a in (self.target_labels, self.target_weights, self.class_weights))
+        return cache[key]
+
     def per_target(self, label_ids: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         """(labels [B,T], weights [B,T]) for integer label ids [B]."""
-        dev = label_ids.device
-        lab = torch.as_tensor(self.target_labels, device=dev)[:, label_ids.long()].t()
-        w = torch.as_tensor(self.target_weights, device=dev)[:, label_ids.long()].t()
-        return lab, w * torch.as_tensor(self.class_weights, device=dev)
+        lab_t, w_t, cw = self._tables(label_ids.device)
+        idx = label_ids.long()
+        return lab_t[:, idx].t(), w_t[:, idx].t() * cw
 
     def __call__(self, logits: torch.Tensor, label_ids: torch.Tensor, row_weights: torch.Tensor,
                  valid_mask: torch.Tensor | None = None) -> torch.Tensor:
@@ -149,7 +158,17 @@ class BaseRankingRecipe(ABC):
     def ranking_task(self) -> RankingTask: ...
 
     def model(self) -> Any:
-        return self.model_builder()()
+        """The dense module of the application (``model_builder().create_module()``)."""
+        return self.model_builder().create_module()
+
+    def trainer(self, *, rank: int = 0, world_size: int = 1, device=None, use_graph: bool = True, seed: int = 0,
+                **kwargs) -> Any:
+        """A ``RankingModelTrainer`` for this recipe: the builder's sparse tables on the fused sharded
+        collection, its module on the flat fused optimizer, the task's objective as the loss."""
+        from ..training.ranking_trainer import RankingModelTrainer
+
+        return RankingModelTrainer(self.model_builder(), self.ranking_task().objective, self.batch_size, rank=rank,
+                                   world_size=world_size, device=device, use_graph=use_graph, seed=seed, **kwargs)
 
 
 __all__ = ["BaseRankingRecipe", "MultiTargetCrossEntropyLoss", "RankingLossAdapter", "RankingTask"]

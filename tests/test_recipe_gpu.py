@@ -1,0 +1,110 @@
+"""A user model (multitask PLE recipe) on the fused path: trainer, graph assembly, 2-GPU equivalence."""
+import os
+import socket
+import subprocess
+import sys
+
+import pytest
+import torch
+import torch.nn as nn
+
+from flare_b200.models.dlrm import RowwiseAdagradTorch
+from flare_b200.recipes.multitask import MultitaskModelBuilder, MultitaskRankingRecipe, synthetic_multitask_batch
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _torch_replica(builder, tr, seed):
+    """The same model in plain PyTorch fp32: nn.EmbeddingBag tables copied from the fused collection."""
+    torch.manual_seed(seed)
+    module = builder.create_module().to(tr.device)
+    embs = nn.ModuleList()
+    for i, s in enumerate(tr.coll.shards):
+        e = nn.EmbeddingBag(s.spec.num_embeddings, s.spec.embedding_dim, mode="sum", sparse=True).to(tr.device)
+        with torch.no_grad():
+            e.weight.copy_(tr.coll.shard_view(i).float())
+        embs.append(e)
+    return module, embs
+
+
+def _pooled_ref(embs, offsets, values, B):
+    offs = offsets.long()
+    outs = []
+    for f, e in enumerate(embs):
+        seg = offs[f * B:(f + 1) * B + 1]
+        outs.append(e(values[seg[0]:seg[-1]].long(), seg[:-1] - seg[0]))
+    return torch.cat(outs, 1)
+
+
+def test_multitask_recipe_trains_on_fused_path_and_tracks_pytorch(cuda):
+    builder = MultitaskModelBuilder()
+    recipe = MultitaskRankingRecipe(name="mt", task_name="ranking", batch_size=512, builder=builder)
+    tr = recipe.trainer(device=cuda, use_graph=True, seed=4)
+    ref_mod, ref_embs = _torch_replica(builder, tr, 4)
+    objective = recipe.ranking_task().objective
+    opt_d = torch.optim.Adam(ref_mod.parameters(), lr=1e-3, betas=(0.9, 0.999), eps=1e-8)
+    opt_s = RowwiseAdagradTorch([e.weight for e in ref_embs], lr=0.05)
+    B = recipe.batch_size
+    fused, plain = [], []
+    for step in range(30):
+        dense, labels, offs, vals = synthetic_multitask_batch(B, builder.vocabs, builder.num_dense,
+                                                             builder.max_bag_size, seed=100 + step, device=cuda)
+        fused.append(tr.train_step(dense, labels, offs, vals).loss)
+        if step < 8:
+            pooled = _pooled_ref(ref_embs, offs, vals, B)
+            logits = ref_mod(dense, pooled, {})
+            loss = objective(logits, labels, torch.full((B,), 1.0 / B, device=cuda))
+            opt_d.zero_grad(set_to_none=True)
+            opt_s.zero_grad()
+            loss.backward()
+            opt_d.step()
+            opt_s.step()
+            plain.append(float(loss))
+    tr.check()
+    assert tr.graph is not None  # steps after the warm-up replay one CUDA graph
+    for i, (a, p) in enumerate(zip(fused, plain)):
+        assert abs(a - p) <= 0.03 * abs(p) + 3e-3, (i, fused[:8], plain)
+    assert sum(fused[-5:]) < sum(fused[:5])
+
+
+def test_assembled_training_and_evaluation_graphs(cuda):
+    from flare_b200.recipes.graph import (RANKING_PHASE_ORDER, assemble_ranking_evaluation_graph,
+                                          assemble_ranking_training_graph, build_pipeline_nodes)
+
+    builder = MultitaskModelBuilder()
+    recipe = MultitaskRankingRecipe(name="mt", task_name="ranking", batch_size=512, builder=builder)
+
+    def source(seed0):
+        s = seed0
+        while True:
+            yield synthetic_multitask_batch(512, builder.vocabs, builder.num_dense, builder.max_bag_size, seed=s,
+                                            device=cuda)
+            s += 1
+
+    inputs = build_pipeline_nodes(recipe, source=source(0), device=cuda, seed=1)
+    g = assemble_ranking_training_graph(inputs, metrics_static_args=dict(targets=("click", "like"), window_steps=10))
+    losses = g["task_graph"].run(40)
+    assert set(g["task_graph"].phase_seconds) == set(RANKING_PHASE_ORDER)
+    assert losses[-1] < losses[0]
+    assert g["metrics"].window.completed or g["metrics"].window.total_steps == 40
+    ev_inputs = build_pipeline_nodes(recipe, source=source(10_000), device=cuda, seed=1)
+    ev_inputs.trainer = inputs.trainer  # evaluate the trained model
+    out = assemble_ranking_evaluation_graph(ev_inputs)["task_graph"].run(4)
+    assert out["auc/click"] > 0.6 and out["auc/like"] > 0.6, out
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_multitask_recipe_two_gpus_match_one_gpu_on_global_batch():
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=ROOT)
+    cmd = ["timeout", "-k", "30", "400", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
+           "-m", "flare_b200.recipes.multitask_dist_check"]
+    res = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=450)
+    assert res.returncode == 0 and "RECIPE_DIST_OK" in res.stdout, (res.stdout + res.stderr)[-5000:]

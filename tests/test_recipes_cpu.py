@@ -49,3 +49,22 @@ def test_cpu_recipe_checkpoint_resume_matches_an_uninterrupted_run(tmp_path):
     assert list_steps(tmp_path) == [3, 6] and first.losses == full.losses[:6]
     second = train_small_cpu(steps=6, batch_size=32, checkpoint_dir=str(tmp_path), resume=True)
     assert second.losses == full.losses[6:]
+
+
+def test_ranking_phase_schedule_contract():
+    """The step's phases in dependency order; the cross-step edge (update -> next train_core) has
+    distance 1; a same-step cycle is rejected."""
+    import pytest
+
+    from flare_b200.recipes.graph import (RANKING_PHASE_DEPENDENCIES, RANKING_PHASE_ORDER, RANKING_PHASES,
+                                          schedule_order)
+
+    order = schedule_order()
+    assert set(order) == set(RANKING_PHASE_ORDER)
+    pos = {n: i for i, n in enumerate(order)}
+    for a, b, d in RANKING_PHASE_DEPENDENCIES:
+        if d == 0:
+            assert pos[a] < pos[b]
+    assert ("update", "train_core", 1) in RANKING_PHASE_DEPENDENCIES
+    with pytest.raises(ValueError):
+        schedule_order(RANKING_PHASES, RANKING_PHASE_DEPENDENCIES + (("update", "train_core", 0),))
