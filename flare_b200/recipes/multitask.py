@@ -118,7 +118,6 @@ __all__ = ["LogitHeads", "MultitaskModelBuilder", "MultitaskRankingModel", "Mult
 def main(argv=None) -> int:
     """Train the multitask recipe on synthetic data (one rank per GPU under torch.distributed.run)."""
     import argparse
-    import os
 
     from ..parallel.dist import init_distributed
 
@@ -142,7 +141,11 @@ def main(argv=None) -> int:
             print(f"step {res.step} loss {res.loss:.5f}", flush=True)
     tr.check()
     tr.close()
-    return 0 if os.environ.get("RANK", "0") is not None else 1
+    if info.world_size > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
 
 
 if __name__ == "__main__":
