@@ -32,7 +32,7 @@ from .sources import BatchAssembler, SourceFactory, WorkItem
 class BatchReader:
     def __init__(self, factory: SourceFactory, batch_size: int, *, rank: int = 0, world: int = 1,
                  policy: str = "pad", repeat_first_batch: bool = False, audit_path: str | Path | None = None,
-                 transform: Callable[[Any], Any] | None = None):
+                 transform: Callable[[Any], Any] | None = None, position_audit_path: str | Path | None = None):
         if not 0 <= rank < world:
             raise ValueError("rank must be in [0, world)")
         self.factory, self.B, self.rank, self.world = factory, int(batch_size), rank, world
@@ -45,11 +45,18 @@ class BatchReader:
         self.cur_row = 0                   # rows of it already handed out
         self.stats = {"items": 0, "rows": 0, "batches": 0, "padded_rows": 0, "errors": 0}
         self._t0 = time.time()
+        # global step positions: the readers interleave (position p is read by rank p % world), so
+        # this rank's k-th batch since the last restore is the k-th position at or after the base
+        # that is congruent to its rank (one JSON line each in the position audit)
+        self.position_base = 0
+        self.position_audit_path = Path(position_audit_path) if position_audit_path else None
+        self.positions: list[dict] = []
 
     # ------------------------------------------------------------------ state
     def capture_state(self) -> dict:
         return {"rank": self.rank, "world": self.world, "done": sorted(self.done),
-                "current": None if self.cur_item is None else [self.cur_item, self.cur_row]}
+                "current": None if self.cur_item is None else [self.cur_item, self.cur_row],
+                "position_base": self.position_base, "batches": len(self.positions)}
 
     def restore_state(self, states: list[dict]) -> None:
         """Resume from the saved states of every rank of the previous run (any world size)."""
@@ -61,6 +68,10 @@ class BatchReader:
                 item, row = st["current"]
                 partial[item] = max(partial.get(item, 0), row)
         self.done = done
+        # positions consumed by the saved run: its base plus every rank's batches since then
+        self.position_base = max((int(st.get("position_base", 0)) for st in states), default=0) + \
+            sum(int(st.get("batches", 0)) for st in states)
+        self.positions = []
         all_items = [it for it in self.factory.plan() if it.item_id not in done]
         self.items = [it for k, it in enumerate(all_items) if k % self.world == self.rank]
         self._partial = {k: v for k, v in partial.items() if k not in done}
@@ -109,17 +120,26 @@ class BatchReader:
                     first = first or ab
                     while True:
                         self.stats["batches"] += 1
+                        self._note_position()
                         yield self.transform(first.data), first.validity
                 self.stats["batches"] += 1
                 self._advance(ab.validity.valid_count)
+                self._note_position()
                 yield self.transform(ab.data), ab.validity
         for ab in asm.finish():
             self.stats["batches"] += 1
             self.stats["padded_rows"] += ab.validity.batch_size - ab.validity.valid_count
             self._advance(ab.validity.valid_count)
+            self._note_position()
             yield self.transform(ab.data), ab.validity
         # rows the completion policy dropped at the end of the stream are consumed too
         self._advance(pushed_rows - self._emitted)
+
+    def _note_position(self) -> None:
+        k = len(self.positions)
+        first = self.position_base + (self.rank - self.position_base) % self.world
+        self.positions.append({"position": first + k * self.world, "rank": self.rank,
+                               "world_size": self.world})
 
     # ------------------------------------------------------------------ accounting
     def close(self) -> dict:
@@ -127,6 +147,10 @@ class BatchReader:
                  "assigned_items": [it.item_id for it in self.items], "done": sorted(self.done)}
         if self.audit_path is not None:
             write_json(self.audit_path, audit)
+        if self.position_audit_path is not None:
+            import json
+
+            self.position_audit_path.write_text("".join(json.dumps(p) + "\n" for p in self.positions))
         return audit
 
 

@@ -126,29 +126,56 @@ class RankingTaskGraph:
     steps_run: int = 0
     losses: list[float] = field(default_factory=list)
 
-    def run(self, steps: int, *, read_loss_every: int = 1) -> list[float]:
-        """Run ``steps`` training steps; returns the losses read back (every ``read_loss_every`` steps)."""
+    def run(self, steps: int, *, read_loss_every: int = 1, trace=None) -> list[float]:
+        """Run ``steps`` training steps; returns the losses read back (every ``read_loss_every`` steps;
+        0: never, so the host runs ahead of the GPU).  ``trace`` (a ``validation.perfetto.PerfettoWriter``)
+        receives one slice per phase and step on ``rank:<r>/<lane>`` tracks: host phases as measured on
+        the host, ``train_core`` as its device interval (CUDA events around the step's graph)."""
         tr = self.inputs.trainer
+        lane = {p.name: p.lane for p in RANKING_PHASES}
+        rank_track = f"rank:{tr.rank}"
+        dev_marks = []
+        if trace is not None:
+            torch.cuda.synchronize(tr.device)
+            host0 = time.perf_counter_ns()
+            base = torch.cuda.Event(enable_timing=True)
+            base.record()
         for _ in range(steps):
+            step = self.steps_run
             batch = None
             loss = None
             for phase in self.order:
-                t0 = time.perf_counter()
+                t0 = time.perf_counter_ns()
                 if phase == "prepare_sparse_materialize":
                     batch = next(self.inputs.reader)
                 elif phase == "prepare_bind":
                     self.inputs.input_node.step(batch)
                 elif phase == "train_core":
+                    if trace is not None:
+                        ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        ea.record()
                     loss = tr._run()  # forward, backward (fused sparse update inside), fused dense update
                     tr.steps += 1
+                    if trace is not None:
+                        eb.record()
+                        dev_marks.append((step, ea, eb))
                 elif phase == "materialize_train_metrics" and self.metrics is not None:
                     logits = self.metrics.logits_fn()
                     self.metrics.window.update(logits, self.metrics.labels_fn(), loss_sum=loss * tr.global_B)
                 # scatter_sparse_grads and update ran inside train_core's graph
-                self.phase_seconds[phase] = self.phase_seconds.get(phase, 0.0) + time.perf_counter() - t0
+                t1 = time.perf_counter_ns()
+                self.phase_seconds[phase] = self.phase_seconds.get(phase, 0.0) + (t1 - t0) / 1e9
+                if trace is not None and phase != "train_core":
+                    trace.slice((rank_track, lane[phase]), phase, t0, t1, step=step, lane=lane[phase])
             self.steps_run += 1
             if read_loss_every and self.steps_run % read_loss_every == 0:
                 self.losses.append(float(loss.item()))
+        if trace is not None:
+            torch.cuda.synchronize(tr.device)
+            for step, ea, eb in dev_marks:
+                a = host0 + int(base.elapsed_time(ea) * 1e6)
+                b = host0 + int(base.elapsed_time(eb) * 1e6)
+                trace.slice((rank_track, "compute"), "train_core", a, b, step=step, lane="compute")
         return self.losses
 
 

@@ -68,7 +68,7 @@ def test_multitask_recipe_trains_on_fused_path_and_tracks_pytorch(cuda):
     assert sum(fused[-5:]) < sum(fused[:5])
 
 
-def test_assembled_training_and_evaluation_graphs(cuda):
+def test_assembled_training_and_evaluation_graphs(cuda, tmp_path):
     from flare_b200.recipes.graph import (RANKING_PHASE_ORDER, assemble_ranking_evaluation_graph,
                                           assemble_ranking_training_graph, build_pipeline_nodes)
 
@@ -88,6 +88,18 @@ def test_assembled_training_and_evaluation_graphs(cuda):
     assert set(g["task_graph"].phase_seconds) == set(RANKING_PHASE_ORDER)
     assert losses[-1] < losses[0]
     assert g["metrics"].window.completed or g["metrics"].window.total_steps == 40
+    # a timeline of 12 more steps without per-step loss reads: the host materialises the next step's
+    # batch while the GPU trains this one
+    from flare_b200.validation.overlap import effective_overlap, phase_overlap
+    from flare_b200.validation.perfetto import PerfettoWriter, parse_trace
+
+    w = PerfettoWriter()
+    g["task_graph"].run(12, read_loss_every=0, trace=w)
+    path = w.save(tmp_path / "ranking.pftrace")
+    rep = phase_overlap(parse_trace(path), set(range(42, 51)))
+    assert all(r["overlaps"]["materialize_next"]["present"] for r in rep["rows"])
+    assert effective_overlap(rep, relations=("materialize_next",))["relations"]["materialize_next"][
+        "positive_hidden_count"] > 0
     ev_inputs = build_pipeline_nodes(recipe, source=source(10_000), device=cuda, seed=1)
     ev_inputs.trainer = inputs.trainer  # evaluate the trained model
     out = assemble_ranking_evaluation_graph(ev_inputs)["task_graph"].run(4)
