@@ -88,6 +88,7 @@ flare::SparseOptParams parse_sparse_opt(const py::dict& d) {
   o.state_v = P<float>(get_or<uintptr_t>(d, "state_v", 0));
   o.score = P<float>(get_or<uintptr_t>(d, "score", 0));
   o.step_ptr = P<const int>(get_or<uintptr_t>(d, "step_ptr", 0));
+  o.grad_scale = get_or<float>(d, "grad_scale", 1.f);
   return o;
 }
 
@@ -286,6 +287,23 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     flare::emb_forward(p, get<int>(d, "grid"), cur_stream());
   });
 
+  m.def("emb_window_append", [](const py::dict& d) {
+    flare::EmbWindowParams p{};
+    p.ids = P<const int>(get<uintptr_t>(d, "ids"));
+    p.bag = P<const int>(get<uintptr_t>(d, "bag"));
+    p.count = P<const int>(get<uintptr_t>(d, "count"));
+    p.len = P<const int>(get<uintptr_t>(d, "len"));
+    p.wids = P<int>(get<uintptr_t>(d, "wids"));
+    p.wbag = P<int>(get<uintptr_t>(d, "wbag"));
+    p.wprefix = P<int>(get<uintptr_t>(d, "wprefix"));
+    p.wlen = P<int>(get<uintptr_t>(d, "wlen"));
+    p.nslot = get<int>(d, "nslot");
+    p.Bl = get<int>(d, "Bl");
+    p.micro = get<int>(d, "micro");
+    p.micro_steps = get<int>(d, "micro_steps");
+    p.stage_cap = get<int64_t>(d, "stage_cap");
+    flare::emb_window_append(p, cur_stream());
+  });
   m.def("emb_det_temp_bytes", [](int64_t max_occ) { return flare::emb_det_temp_bytes(max_occ); });
   m.def("emb_hash_sizes", [](int64_t max_occ, int light_max) {
     return py::make_tuple(flare::emb_hash_tile_count(max_occ), flare::emb_hash_max_chunks(max_occ, light_max),

@@ -1297,6 +1297,45 @@ void emb_forward(const EmbFwdParams& p, int grid, cudaStream_t s) {
   }
 }
 
+// One block row per staging slot; blocks of a row stride over its occurrences.  Row `micro` of the
+// prefix is read, row `micro + 1` written (by block 0), so no block reads what another writes.
+__global__ void emb_window_append_kernel(EmbWindowParams p) {
+  const int slot = blockIdx.y;
+  const int c = static_cast<int>(min(static_cast<int64_t>(max(p.count[slot], 0)), p.stage_cap));
+  const int base = p.micro == 0 ? 0 : p.wprefix[static_cast<int64_t>(p.micro) * p.nslot + slot];
+  const int64_t wcap = p.stage_cap * p.micro_steps;
+  const int* src_ids = p.ids + static_cast<int64_t>(slot) * p.stage_cap;
+  const int* src_bag = p.bag + static_cast<int64_t>(slot) * p.stage_cap;
+  int* dst_ids = p.wids + static_cast<int64_t>(slot) * wcap + base;
+  int* dst_bag = p.wbag + static_cast<int64_t>(slot) * wcap + base;
+  const int shift = p.micro * p.Bl;
+  const int stride = gridDim.x * blockDim.x;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < c; i += stride) {
+    dst_ids[i] = __ldcs(src_ids + i);
+    dst_bag[i] = __ldcs(src_bag + i) + shift;
+  }
+  const int* src_len = p.len + static_cast<int64_t>(slot) * p.Bl;
+  int* dst_len = p.wlen + static_cast<int64_t>(slot) * p.micro_steps * p.Bl + shift;
+  for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < p.Bl; b += stride) dst_len[b] = src_len[b];
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    if (p.micro == 0) p.wprefix[slot] = 0;
+    p.wprefix[static_cast<int64_t>(p.micro + 1) * p.nslot + slot] = base + c;
+  }
+}
+
+void emb_window_append(const EmbWindowParams& p, cudaStream_t s) {
+  FLARE_CHECK(p.nslot > 0 && p.nslot < 65536, "window append: slot count out of range");
+  FLARE_CHECK(p.micro >= 0 && p.micro < p.micro_steps, "window append: micro-step outside the window");
+  FLARE_CHECK(p.stage_cap * p.micro_steps < (1ll << 31), "window staging exceeds 32-bit positions");
+  FLARE_CHECK(static_cast<int64_t>(p.micro_steps) * p.Bl < (1ll << 31), "window samples exceed 32 bits");
+  constexpr int kThreads = 256;
+  const int64_t per_slot = std::max<int64_t>(p.stage_cap, p.Bl);
+  const int bx = static_cast<int>(std::min<int64_t>((per_slot + kThreads * 4 - 1) / (kThreads * 4), 32));
+  emb_window_append_kernel<<<dim3(std::max(bx, 1), p.nslot), kThreads, 0, s>>>(p);
+  FLARE_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
 size_t emb_det_temp_bytes(int64_t max_occ) {
   size_t bytes = 0;
   FLARE_CUDA_CHECK(cub::DeviceRadixSort::SortPairs(nullptr, bytes, static_cast<const int*>(nullptr),

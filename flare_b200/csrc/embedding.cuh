@@ -62,6 +62,7 @@ struct SparseOptParams {
   float* state_m;    // per-element first moment (adam) / accumulator (adagrad)
   float* state_v;    // per-element second moment (adam)
   float* score;      // per-row access score for frequency-based LR policies (nullable)
+  float grad_scale;  // multiplies every row's gradient sum (1 / micro-steps of an accumulation window)
 };
 
 struct EmbFwdParams {
@@ -184,7 +185,23 @@ struct EmbBwdParams {
   uint64_t timeout_ns;
 };
 
+// Gradient-accumulation window: the staging of micro-step `micro` appended to the window's staging,
+// which the backward then reads as one batch of micro_steps * Bl samples (bags shifted by micro * Bl).
+struct EmbWindowParams {
+  const int* ids;    // the step's staging: [nslot][stage_cap] ids / bags, [nslot] counts, [nslot][Bl] lengths
+  const int* bag;
+  const int* count;
+  const int* len;
+  int* wids;         // the window's staging: [nslot][micro_steps * stage_cap] ids / bags
+  int* wbag;
+  int* wprefix;      // [micro_steps + 1][nslot]: occurrences of each slot before micro-step k (row k)
+  int* wlen;         // [nslot][micro_steps * Bl]
+  int nslot, Bl, micro, micro_steps;
+  int64_t stage_cap;
+};
+
 void emb_forward(const EmbFwdParams& p, int grid, cudaStream_t s);
+void emb_window_append(const EmbWindowParams& p, cudaStream_t s);
 void emb_backward(const EmbBwdParams& p, int ncols_max, int grid, cudaStream_t s);
 void emb_backward_hash(const EmbBwdParams& p, int ncols_max, int grid, cudaStream_t s);
 size_t emb_det_temp_bytes(int64_t max_occ);

@@ -71,7 +71,7 @@ __device__ __forceinline__ void apply_update(const SparseOptParams& o, TW* w, in
     lr *= lr_scale(o, sc);
   }
 #pragma unroll
-  for (int e = 0; e < 4 * NV; ++e) g[e] += o.weight_decay * wv[e];
+  for (int e = 0; e < 4 * NV; ++e) g[e] = g[e] * o.grad_scale + o.weight_decay * wv[e];
   if (o.kind == kOptRowwiseAdagrad || o.kind == kOptRowwiseAdam) {
     float sq = 0.f;
     if (act) {

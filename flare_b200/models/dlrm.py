@@ -109,12 +109,17 @@ class DLRM:
                  device: torch.device | None = None, heap: SymmetricHeap | None = None, seed: int = 0,
                  global_batch_size: int | None = None, values_capacity: int | None = None,
                  table_costs: list[float] | None = None, plan: ShardingPlan | None = None,
-                 sparse_policy: str | None = None):
+                 sparse_policy: str | None = None, accumulation_steps: int = 1):
+        self.accum = int(accumulation_steps)
+        if self.accum < 1:
+            raise ValueError("accumulation_steps must be >= 1")
         if sparse_policy is None:  # from the tables: a staleness bound of >= 1 step everywhere allows the overlap
             stale = [t.max_staleness_steps for t in cfg.tables]
-            sparse_policy = "pipelined" if stale and min(stale) >= 1 else "sync"
+            sparse_policy = "pipelined" if stale and min(stale) >= 1 and self.accum == 1 else "sync"
         if sparse_policy not in ("sync", "pipelined"):
             raise ValueError(f"sparse_policy must be 'sync' or 'pipelined', not {sparse_policy!r}")
+        if sparse_policy == "pipelined" and self.accum > 1:
+            raise ValueError("accumulation windows run under the sync sparse policy")
         self.cfg = cfg
         self.sparse_policy = sparse_policy
         self.pipelined = sparse_policy == "pipelined"
@@ -146,7 +151,8 @@ class DLRM:
         self.emb = ShardedEmbeddingBagCollection(
             cfg.tables, self.B, max_bag_size=max_bag_size, rank=rank, world_size=world_size, device=dev, heap=heap,
             optimizer=cfg.sparse_optimizer, seed=seed, values_capacity=values_capacity,
-            plan=plan if plan is not None else dlrm_plan(cfg, world_size, table_costs), pipelined=self.pipelined)
+            plan=plan if plan is not None else dlrm_plan(cfg, world_size, table_costs), pipelined=self.pipelined,
+            accumulation_steps=self.accum)
         # pipelined policy: staging slot of the next forward, slot whose sparse update is pending
         self._next_slot = 0
         self.pending_slot: int | None = None
@@ -180,8 +186,10 @@ class DLRM:
         """Forward + backward of the local batch; gradients land in the flat/sparse buffers.
 
         Synchronous semantics: a sparse update still pending under the pipelined policy is applied
-        first (its staging slot is the one this forward would reuse)."""
-        self.flush_pending_updates()
+        first (its staging slot is the one this forward would reuse).  In an accumulation window the
+        dense gradients add up in the flat buffer and the pooled gradients in the window's micro-step
+        slot."""
+        self._flush_pipelined()
         cast_pad_bf16(self.dense_in, self.xd)
         bot = self.bottom.forward(self.xd)
         pooled = self.emb.forward()
@@ -284,13 +292,25 @@ class DLRM:
         return self.loss_sum
 
     def train_step(self) -> torch.Tensor:
-        """One full optimizer step; returns the device scalar sum of per-sample losses."""
+        """One step; returns the device scalar sum of per-sample losses.
+
+        With ``accumulation_steps`` n > 1 a call is one micro-step: the n-th call of a window applies
+        the sparse and dense optimizers once to the window's summed gradients divided by n (the
+        reference's micro-step windows with the update at the boundary:
+        src/flare/jax/training/engines/distributed.py:1017-1180 and the sparse fp32 accumulation
+        before ``optimizer_step(n_micro)``, src/flare/runtime/fluxway/workers/dynamic_embedding.py:
+        481-549)."""
         if self.pipelined:
             return self._pipelined_step()
         loss = self.forward_backward()
-        self.emb.backward()
-        self.dense.apply()
+        if self.accum == 1 or self.emb.micro_filled == self.accum:
+            self._close_window()
         return loss
+
+    def _close_window(self) -> None:
+        micro = self.emb.micro_filled if self.accum > 1 else 1
+        self.emb.backward()
+        self.dense.apply(grad_scale=1.0 / micro)
 
     def _pipelined_step(self) -> torch.Tensor:
         main = torch.cuda.current_stream(self.device)
@@ -323,7 +343,15 @@ class DLRM:
         return self.loss_sum
 
     def flush_pending_updates(self) -> bool:
-        """Apply the pending sparse update of the pipelined policy; True if there was one."""
+        """Apply what the model holds back: the pending sparse update of the pipelined policy, or the
+        open accumulation window (a tail window, normalised by its own micro-step count); True if
+        there was something."""
+        if self.accum > 1 and self.emb.micro_filled > 0:
+            self._close_window()
+            return True
+        return self._flush_pipelined()
+
+    def _flush_pipelined(self) -> bool:
         if self.pending_slot is None:
             return False
         self.emb.backward(slot=self.pending_slot)
@@ -333,19 +361,31 @@ class DLRM:
     # host-side state of a step, for CUDA-graph capture (undone) and replay (advanced)
     def graph_key(self):
         """Steps with equal keys launch the same kernels on the same buffers (None: do not capture)."""
+        if self.accum > 1:
+            return ("micro", self.emb.micro_filled)
         if not self.pipelined:
             return 0
         return None if self.pending_slot is None else (self._next_slot, self.pending_slot)
 
     def host_state(self) -> tuple:
-        return (self.dense.step, self.emb.step, self._next_slot, self.pending_slot, self.emb._slot)
+        return (self.dense.step, self.emb.step, self._next_slot, self.pending_slot, self.emb._slot,
+                self.emb.micro_filled, self.emb._micro)
 
     def restore_host_state(self, st: tuple) -> None:
-        self.dense.step, self.emb.step, self._next_slot, self.pending_slot, self.emb._slot = st
+        (self.dense.step, self.emb.step, self._next_slot, self.pending_slot, self.emb._slot,
+         self.emb.micro_filled, self.emb._micro) = st
 
     def advance_host_state(self) -> None:
         """The host-side effect of one replayed step (a captured step runs exactly one sparse backward:
-        its own under the sync policy, the pending one under the pipelined policy)."""
+        its own under the sync policy, the pending one under the pipelined policy; a micro-step of an
+        accumulation window runs one only when it closes the window)."""
+        if self.accum > 1:
+            k = self.emb.micro_filled
+            self.emb._micro = k
+            if k + 1 < self.accum:
+                self.emb.micro_filled = k + 1
+                return
+            self.emb.micro_filled = 0
         self.dense.step += 1
         self.emb.step += 1
         if self.pipelined:

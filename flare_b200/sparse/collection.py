@@ -101,6 +101,7 @@ class ShardedEmbeddingBagCollection:
         deterministic: bool | None = None,
         pipelined: bool = False,
         validate_inputs: bool | None = None,
+        accumulation_steps: int = 1,
     ):
         if not tables:
             raise ValueError("at least one table is required")
@@ -140,6 +141,18 @@ class ShardedEmbeddingBagCollection:
         if self.pipelined and any(t.dynamic or t.cache_rows is not None for t in self.tables):
             raise ValueError("the pipelined sparse policy needs resident static tables: the next forward's "
                              "placement (host tier, dynamic insert) could move a row the pending update writes")
+        # gradient-accumulation window: every training forward appends its staging to the window's, and
+        # one backward per window reduces all micro-steps' gradients per row in fp32 and applies the
+        # optimizer once with the sum scaled by 1 / micro-steps (lookups inside a window see the weights
+        # of the window's start)
+        self.accum = int(accumulation_steps)
+        if self.accum < 1:
+            raise ValueError("accumulation_steps must be >= 1")
+        if self.accum > 1 and (self.pipelined or any(t.dynamic or t.cache_rows is not None for t in self.tables)):
+            raise ValueError("accumulation windows need resident static tables and the synchronous policy: a "
+                             "placement inside the window could move a row that an earlier micro-step staged")
+        self.micro_filled = 0   # micro-steps staged in the open window
+        self._micro = 0         # micro-step of the last training forward
 
         # ---- row-wise tables: fp32 partial-sum columns (every requester adds the pieces' partials) ----
         self.rw_part_col: dict[int, int] = {}
@@ -247,10 +260,19 @@ class ShardedEmbeddingBagCollection:
         self.fetch = world_size > 1 and os.environ.get("FLARE_EMB_FETCH", "1") != "0"
         self.fetch_offs = (torch.zeros(nslot * (self.B + 1), dtype=torch.int32, device=dev)
                            if self.fetch else None)
-        self.stage_rank = torch.empty(nslot * self.stage_cap, dtype=torch.int32, device=dev)
+        # the backward's batch: one step, or every micro-step of an accumulation window
+        self.Bb = self.B * self.accum
+        self.bwd_cap = self.stage_cap * self.accum
+        self.nslot = nslot
+        self._win = None
+        if self.accum > 1:
+            i32z = lambda n: torch.zeros(n, dtype=torch.int32, device=dev)  # noqa: E731
+            self._win = dict(ids=i32z(nslot * self.bwd_cap), bag=i32z(nslot * self.bwd_cap),
+                             prefix=i32z((self.accum + 1) * nslot), len=i32z(nslot * self.Bb))
+        self.stage_rank = torch.empty(nslot * self.bwd_cap, dtype=torch.int32, device=dev)
         self.slot_start = torch.zeros(nslot + 1, dtype=torch.int32, device=dev)
         self.grad_stage_ld = self.ncols_max
-        self.max_occ = nslot * self.stage_cap
+        self.max_occ = nslot * self.bwd_cap
         self.flags_occ = torch.empty(self.max_occ, dtype=torch.int32, device=dev)
         self.num_unique = torch.zeros(8, dtype=torch.int32, device=dev)
         self.seg_start = torch.empty(self.max_occ + 1, dtype=torch.int32, device=dev)
@@ -274,7 +296,7 @@ class ShardedEmbeddingBagCollection:
         self.grad_direct = (self.hash_bwd and world_size == 1 and aligned
                             and os.environ.get("FLARE_EMB_GRAD_STAGE", "0") != "1")
         staged = not self.grad_direct
-        self.grad_stage = torch.empty(nslot * self.B * self.ncols_max if staged else 8, dtype=grad_dtype, device=dev)
+        self.grad_stage = torch.empty(nslot * self.Bb * self.ncols_max if staged else 8, dtype=grad_dtype, device=dev)
         if self.hash_bwd:
             # touched-row table: a region sized for the step's unique rows (its slots are prefetched into L2
             # and take every key's first probes) and an overflow table with room for every possible key
@@ -331,7 +353,7 @@ class ShardedEmbeddingBagCollection:
         self.in_offsets = heap.alloc((self.F * self.B + 1,), torch.int32)
         self.in_values = heap.alloc((self.values_capacity,), torch.int32)
         self.pooled = heap.alloc((self.B, self.total_dim), out_dtype)
-        self.grad_ins = [heap.alloc((self.B, self.total_dim), grad_dtype) for _ in range(self.nbuf)]
+        self.grad_ins = [heap.alloc((self.Bb, self.total_dim), grad_dtype) for _ in range(self.nbuf)]
         self.grad_in = self.grad_ins[0]
         self.flags = FlagRegion(heap, NUM_FLAG_ARRAYS)
         any_dynamic = any(t.dynamic for t in self.tables)
@@ -369,7 +391,7 @@ class ShardedEmbeddingBagCollection:
     @staticmethod
     def exchange_bytes(tables: list[SparseTableSpec], batch_size: int, max_bag_size: int,
                        values_capacity: int | None = None, plan: ShardingPlan | None = None,
-                       pipelined: bool = False) -> int:
+                       pipelined: bool = False, accumulation_steps: int = 1) -> int:
         """Symmetric memory of the exchange buffers (ids, pooled rows, pooled grads, row-wise partials)."""
         F, B = len(tables), int(batch_size)
         cap = values_capacity or F * B * max_bag_size
@@ -378,12 +400,12 @@ class ShardedEmbeddingBagCollection:
         rw = [i for i, r in enumerate(shards) if r > 1]
         part = 4 * max([shards[i] for i in rw], default=0) * B * sum(tables[i].embedding_dim for i in rw)
         remap = 4 * cap if any(t.dynamic for t in tables) else 0
-        grads = 2 if pipelined else 1
+        grads = (2 if pipelined else 1) * max(1, int(accumulation_steps))
         return 4 * (F * B + 1) + 4 * cap + remap + (1 + grads) * 4 * B * dim + part + NUM_FLAG_ARRAYS * 64 + 4096
 
     def _heap_bytes(self) -> int:
         b = (self.F * self.B + 1) * 4 + 2 * self.F * self.B * self.max_bag * 4
-        b += (1 + self.nbuf) * self.B * self.total_dim * 4 + NUM_FLAG_ARRAYS * 64 + 8 * 256
+        b += (self.B + self.nbuf * self.Bb) * self.total_dim * 4 + NUM_FLAG_ARRAYS * 64 + 8 * 256
         b += self.rw_slots * self.B * self.part_total * 4 + 256
         return b + (1 << 20)
 
@@ -395,8 +417,10 @@ class ShardedEmbeddingBagCollection:
 
     @property
     def grad_input(self) -> torch.Tensor:
-        """[B, total_dim] buffer the dense backward writes the pooled gradients into (slot of the last forward)."""
-        return self.grad_ins[self._slot].local
+        """[B, total_dim] buffer the dense backward writes the pooled gradients into (slot / micro-step of the
+        last training forward)."""
+        g = self.grad_ins[self._slot].local
+        return g if self.accum == 1 else g[self._micro * self.B:(self._micro + 1) * self.B]
 
     def _slot_of(self, slot: int | None) -> int:
         s = self._slot if slot is None else int(slot)
@@ -448,16 +472,40 @@ class ShardedEmbeddingBagCollection:
             d.update(peer_part=self._peer["part"].data_ptr(), part_stride=self.part_total,
                      rw_tables=self.rw_desc.data_ptr(), num_rw=len(self.rw_part_col))
         native().emb_forward(d)
+        if training and self.accum > 1:
+            k = self.micro_filled
+            if k >= self.accum:
+                raise RuntimeError(f"the accumulation window holds {self.accum} micro-steps: run backward() first")
+            w = self._win
+            native().emb_window_append(dict(
+                ids=st["ids"].data_ptr(), bag=st["bag"].data_ptr(), count=st["count"].data_ptr(),
+                len=st["len"].data_ptr(), wids=w["ids"].data_ptr(), wbag=w["bag"].data_ptr(),
+                wprefix=w["prefix"].data_ptr(), wlen=w["len"].data_ptr(), nslot=self.nslot, Bl=self.B,
+                micro=k, micro_steps=self.accum, stage_cap=self.stage_cap))
+            self._micro, self.micro_filled = k, k + 1
         return self.pooled.local
 
     def backward(self, step: int | None = None, slot: int | None = None) -> None:
         """Consume the pooled gradients of staging ``slot`` (default: the last forward's) and update the owned shards.
 
         The optimizer step used for bias corrections is the device counter,
-        advanced by one per call (``step`` sets it explicitly first).
+        advanced by one per call (``step`` sets it explicitly first).  With an
+        accumulation window the call closes the window: every staged
+        micro-step's gradients are summed per row and the optimizer applies
+        the sum divided by the number of micro-steps (a shorter tail window
+        divides by its own count).
         """
         sl = self._slot_of(slot)
         st = self._stages[sl]
+        micro = 1
+        if self.accum > 1:
+            micro = self.micro_filled
+            if micro == 0:
+                raise RuntimeError("backward() with no micro-step staged in the accumulation window")
+            w = self._win
+            st = dict(ids=w["ids"], bag=w["bag"], len=w["len"],
+                      count=w["prefix"][micro * self.nslot:(micro + 1) * self.nslot])
+            self.micro_filled = 0
         if step is not None:
             self.step = int(step) - 1
             self.step_dev.fill_(self.step)
@@ -465,6 +513,7 @@ class ShardedEmbeddingBagCollection:
         native().increment_counter(self.step_dev.data_ptr())
         op = self.optimizer.kernel_params(self.step)
         op.update(
+            grad_scale=1.0 / micro,
             step_ptr=self.step_dev.data_ptr(),
             state_row=self.state_row.data_ptr() if self.state_row is not None else 0,
             state_m=self.state_m.data_ptr() if self.state_m is not None else 0,
@@ -475,13 +524,13 @@ class ShardedEmbeddingBagCollection:
         )
         d = dict(
             shards=self.shard_desc.data_ptr(), num_shards=len(self.shards), world=self.world, rank=self.rank,
-            Bl=self.B, peer_grad=self._peer_grad[sl].data_ptr(), out_stride=self.total_dim,
+            Bl=self.Bb, peer_grad=self._peer_grad[sl].data_ptr(), out_stride=self.total_dim,
             grad_dtype=dtype_code(self.grad_dtype), grad_stage=self.grad_stage.data_ptr(),
             grad_stage_ld=self.grad_stage_ld, stage_ids=st["ids"].data_ptr(),
             stage_bag=st["bag"].data_ptr(), stage_rank=self.stage_rank.data_ptr(),
             slot_start=self.slot_start.data_ptr(),
             stage_count=st["count"].data_ptr(), stage_len=st["len"].data_ptr(),
-            stage_cap=self.stage_cap, weights=self.weights.data_ptr(), w_dtype=dtype_code(self.value_dtype),
+            stage_cap=self.bwd_cap, weights=self.weights.data_ptr(), w_dtype=dtype_code(self.value_dtype),
             flags=self.flags_occ.data_ptr(), num_unique=self.num_unique.data_ptr(),
             seg_start=self.seg_start.data_ptr(), occ=self.occ.data_ptr(),
             light_max=self.light_max, max_occ=self.max_occ, opt=op, dirty=self.dirty.data_ptr(),

@@ -1,10 +1,12 @@
 """Run a function on N CPU ranks over gloo (multi-process tests without a GPU)."""
 from __future__ import annotations
 
+import io
 import os
 import socket
 import traceback
 
+import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
@@ -21,7 +23,11 @@ def _entry(rank, world, port, fn, args, queue):
     try:
         dist.init_process_group("gloo", rank=rank, world_size=world)
         out = fn(rank, world, *args)
-        queue.put((rank, "ok", out))
+        # results travel as bytes: a tensor put on the queue as is would be shared through a file
+        # descriptor that the parent can no longer fetch once this process has exited
+        buf = io.BytesIO()
+        torch.save(out, buf)
+        queue.put((rank, "ok", buf.getvalue()))
     except BaseException:  # noqa: BLE001 - report any failure to the parent
         queue.put((rank, "err", traceback.format_exc()))
     finally:
@@ -43,7 +49,7 @@ def run_ranks(fn, world: int, *args, timeout: float = 120.0):
             rank, status, out = q.get(timeout=timeout)
             if status != "ok":
                 raise RuntimeError(f"rank {rank} failed:\n{out}")
-            results[rank] = out
+            results[rank] = torch.load(io.BytesIO(out), weights_only=False)
     finally:
         for p in procs:
             p.join(timeout=10)

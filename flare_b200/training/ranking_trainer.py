@@ -23,6 +23,13 @@ global_batch`` make every rank's gradient its share of the global sample
 mean, so the fused reduce-scatter (a sum over ranks) yields the global mean
 (the sample-mean contract of src/flare/jax/training/steppers.py:32-90 and the
 ranking loss adapter).
+
+``accumulation_steps`` n > 1 makes a step one micro-step of a window: dense
+gradients add up in the flat buffer, pooled gradients in the collection's
+window, and the n-th micro-step applies both optimizers once to the sums
+divided by n (``finish_window`` closes a shorter tail window); one CUDA
+graph per micro-step position (the reference's micro-step windows,
+src/flare/jax/training/engines/distributed.py:1017-1180).
 """
 from __future__ import annotations
 
@@ -51,7 +58,7 @@ class RankingModelTrainer:
     def __init__(self, builder: Any, objective, batch_size: int, *, rank: int = 0, world_size: int = 1,
                  device: torch.device | None = None, dense_optimizer: DenseOptimizerConfig | None = None,
                  sparse_optimizer: SparseOptimizerConfig | None = None, use_graph: bool = True, seed: int = 0,
-                 values_capacity: int | None = None):
+                 values_capacity: int | None = None, accumulation_steps: int = 1):
         from ..parallel.symm import SymmetricHeap
 
         self.device = device or torch.device("cuda", torch.cuda.current_device())
@@ -59,6 +66,7 @@ class RankingModelTrainer:
         self.global_B = self.B * world_size
         self.objective = objective
         self.use_graph = use_graph
+        self.accum = int(accumulation_steps)
         tables = list(builder.sparse_tables())
         self.num_dense = int(builder.num_dense)
         max_bag = int(builder.max_bag_size)
@@ -67,7 +75,8 @@ class RankingModelTrainer:
         module.to(self.device)
         heap = None
         if world_size > 1:
-            exchange = ShardedEmbeddingBagCollection.exchange_bytes(tables, self.B, max_bag, values_capacity)
+            exchange = ShardedEmbeddingBagCollection.exchange_bytes(tables, self.B, max_bag, values_capacity,
+                                                                    accumulation_steps=self.accum)
             nparam = sum(p.numel() for p in module.parameters() if p.requires_grad)
             heap = SymmetricHeap(exchange + 6 * (nparam + 4096 * world_size) + (64 << 20), rank=rank,
                                  world_size=world_size, device=self.device)
@@ -75,8 +84,8 @@ class RankingModelTrainer:
         self.coll = ShardedEmbeddingBagCollection(tables, self.B, max_bag_size=max_bag, rank=rank,
                                                   world_size=world_size, device=self.device, heap=heap,
                                                   optimizer=sparse_optimizer, seed=seed,
-                                                  values_capacity=values_capacity)
-        self.emb = FusedEmbeddingBag(self.coll)
+                                                  values_capacity=values_capacity, accumulation_steps=self.accum)
+        self.emb = FusedEmbeddingBag(self.coll, update="deferred" if self.accum > 1 else "immediate")
         self.module = module
         self.dense = FusedDenseParameters(module, dense_optimizer or DenseOptimizerConfig(), device=self.device,
                                           rank=rank, world_size=world_size, heap=heap)
@@ -86,7 +95,7 @@ class RankingModelTrainer:
         self.row_weights = torch.full((self.B,), 1.0 / self.global_B, device=self.device)
         self.loss = torch.zeros((), device=self.device)
         self.steps = 0
-        self.graph: torch.cuda.CUDAGraph | None = None
+        self.graphs: dict[int, tuple[torch.cuda.CUDAGraph, torch.Tensor]] = {}  # micro-step position -> graph
 
     # ------------------------------------------------------------------ step
     def set_batch(self, dense: torch.Tensor, label_ids: torch.Tensor, offsets: torch.Tensor,
@@ -100,27 +109,65 @@ class RankingModelTrainer:
         logits = self.module(self.x_dense, pooled, self.emb.split(pooled))
         loss = self.objective(logits, self.label_ids, self.row_weights)
         loss.backward()
-        self.dense.step()
+        if self.accum == 1:
+            self.dense.step()
+        elif self.coll.micro_filled == self.accum:
+            self._close_window()
         return loss.detach()
+
+    def _close_window(self) -> None:
+        micro = self.coll.micro_filled
+        self.emb.apply_pending()
+        self.dense.step(grad_scale=1.0 / micro)
+
+    def finish_window(self) -> bool:
+        """Apply the optimizers to an open (tail) window, normalised by its micro-step count."""
+        if self.accum > 1 and self.coll.micro_filled > 0:
+            self._close_window()
+            return True
+        return False
+
+    @property
+    def graph(self) -> torch.cuda.CUDAGraph | None:
+        """The first captured step (None before capture)."""
+        return next(iter(self.graphs.values()))[0] if self.graphs else None
+
+    # host-side mirrors of the device state: capture records kernels without running them, so the
+    # mirrors it advanced are put back; a replay advances them as the eager step would
+    def _host_state(self) -> tuple:
+        return self.dense.state.step, self.coll.step, self.coll.micro_filled, self.coll._micro, self.emb.pending
+
+    def _restore_host_state(self, st: tuple) -> None:
+        self.dense.state.step, self.coll.step, self.coll.micro_filled, self.coll._micro, self.emb.pending = st
+
+    def _advance_host_state(self) -> None:
+        if self.accum > 1:
+            k = self.coll.micro_filled
+            self.coll._micro = k
+            if k + 1 < self.accum:
+                self.coll.micro_filled, self.emb.pending = k + 1, True
+                return
+            self.coll.micro_filled, self.emb.pending = 0, False
+        self.dense.state.step += 1
+        self.coll.step += 1
 
     def _run(self) -> torch.Tensor:
         self.module.train()
         self.emb.train()
         if self.use_graph and self.steps >= self.EAGER_STEPS:
-            if self.graph is None:
+            key = self.coll.micro_filled
+            if key not in self.graphs:
                 torch.cuda.synchronize(self.device)
                 g = torch.cuda.CUDAGraph()
-                # capture records the kernels without running them: the optimizer step counters are
-                # device-resident, the host mirrors advance on replay
-                dstep, cstep = self.dense.state.step, self.coll.step
+                st = self._host_state()
                 with torch.cuda.graph(g):
                     out = self._body()
-                self.dense.state.step, self.coll.step = dstep, cstep
-                self.graph, self._graph_loss = g, out
-            self.graph.replay()
-            self.dense.state.step += 1
-            self.coll.step += 1
-            self.loss.copy_(self._graph_loss)
+                self._restore_host_state(st)
+                self.graphs[key] = (g, out)
+            g, out = self.graphs[key]
+            g.replay()
+            self._advance_host_state()
+            self.loss.copy_(out)
             return self.loss
         out = self._body()
         self.loss.copy_(out)
@@ -136,6 +183,8 @@ class RankingModelTrainer:
 
     @torch.no_grad()
     def predict(self, dense: torch.Tensor, offsets: torch.Tensor, values: torch.Tensor) -> torch.Tensor:
+        """Probabilities of a batch; an open accumulation window is applied first."""
+        self.finish_window()
         self.module.eval()
         self.emb.eval()
         self.x_dense.copy_(dense)
@@ -148,7 +197,8 @@ class RankingModelTrainer:
         self.coll.check()
 
     def close(self) -> None:
-        self.graph = None
+        self.finish_window()
+        self.graphs.clear()
 
 
 __all__ = ["RankingModelTrainer", "RankingStepResult"]

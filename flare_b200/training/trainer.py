@@ -214,21 +214,23 @@ class DLRMTrainer(FusedTrainer):
     def __init__(self, cfg: DLRMConfig, batch_size: int, *, max_bag_size: int, rank: int = 0, world_size: int = 1,
                  device: torch.device | None = None, seed: int = 0, use_graph: bool = True,
                  values_capacity: int | None = None, heap_bytes: int | None = None,
-                 table_costs: list[float] | None = None, row_split: bool = False, sparse_policy: str | None = None):
+                 table_costs: list[float] | None = None, row_split: bool = False, sparse_policy: str | None = None,
+                 accumulation_steps: int = 1):
         device = device or torch.device("cuda", torch.cuda.current_device())
         heap = None
         plan = dlrm_plan(cfg, world_size, table_costs, row_split=row_split)
         if world_size > 1:
-            exchange = ShardedEmbeddingBagCollection.exchange_bytes(cfg.tables, batch_size, max_bag_size,
-                                                                    values_capacity, plan=plan,
-                                                                    pipelined=_pipelined(cfg, sparse_policy))
+            exchange = ShardedEmbeddingBagCollection.exchange_bytes(
+                cfg.tables, batch_size, max_bag_size, values_capacity, plan=plan,
+                pipelined=accumulation_steps == 1 and _pipelined(cfg, sparse_policy),
+                accumulation_steps=accumulation_steps)
             dense = 6 * 16 * 1024 * 1024  # flat fp32 grads + bf16 params for up to 16M parameters
             need = heap_bytes or (exchange + dense + 64 * 1024 * 1024)
             heap = SymmetricHeap(need, rank=rank, world_size=world_size, device=device)
         self.heap = heap
         model = DLRM(cfg, batch_size, max_bag_size=max_bag_size, rank=rank, world_size=world_size,
                      device=device, heap=heap, seed=seed, values_capacity=values_capacity, plan=plan,
-                     sparse_policy=sparse_policy)
+                     sparse_policy=sparse_policy, accumulation_steps=accumulation_steps)
         super().__init__(model, batch_size, device=device, rank=rank, world_size=world_size, use_graph=use_graph)
 
 

@@ -76,8 +76,8 @@ def test_pipelined_host_state_machine_without_cuda():
 
     def model(pipelined):
         m = object.__new__(DLRM)  # no CUDA: only the host-side bookkeeping is exercised
-        m.pipelined, m._next_slot, m.pending_slot = pipelined, 0, None
-        m.dense, m.emb = SimpleNamespace(step=0), SimpleNamespace(step=0, _slot=0)
+        m.pipelined, m._next_slot, m.pending_slot, m.accum = pipelined, 0, None, 1
+        m.dense, m.emb = SimpleNamespace(step=0), SimpleNamespace(step=0, _slot=0, micro_filled=0, _micro=0)
         return m
 
     s = model(False)
@@ -97,3 +97,25 @@ def test_pipelined_host_state_machine_without_cuda():
         p.advance_host_state()
     assert keys == [(1, 0), (0, 1), (1, 0), (0, 1)]  # two graphs, alternating
     assert (p.dense.step, p.emb.step, p.emb._slot, p._next_slot, p.pending_slot) == (4, 4, 0, 1, 0)
+
+
+def test_accumulation_window_host_state_machine_without_cuda():
+    """A window of 3 micro-steps: one graph per position, optimizer steps only when the window closes."""
+    from types import SimpleNamespace
+
+    from flare_b200.models.dlrm import DLRM
+
+    m = object.__new__(DLRM)
+    m.pipelined, m._next_slot, m.pending_slot, m.accum = False, 0, None, 3
+    m.dense, m.emb = SimpleNamespace(step=0), SimpleNamespace(step=0, _slot=0, micro_filled=0, _micro=0)
+    keys, steps = [], []
+    for _ in range(7):
+        keys.append(m.graph_key())
+        snap = m.host_state()
+        m.emb.micro_filled, m.dense.step = 2, 50  # what a capture may leave behind
+        m.restore_host_state(snap)
+        m.advance_host_state()
+        steps.append((m.dense.step, m.emb.step, m.emb.micro_filled, m.emb._micro))
+    assert keys == [("micro", 0), ("micro", 1), ("micro", 2)] * 2 + [("micro", 0)]
+    assert steps == [(0, 0, 1, 0), (0, 0, 2, 1), (1, 1, 0, 2), (1, 1, 1, 0), (1, 1, 2, 1), (2, 2, 0, 2),
+                     (2, 2, 1, 0)]
