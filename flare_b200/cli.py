@@ -47,6 +47,11 @@ def _parser() -> argparse.ArgumentParser:
                    help='row-wise pieces per table: "4" (every table) or "t0:4,t3:2" (the rest keep their config)')
     t.add_argument("--sparse-policy", choices=["sync", "pipelined"], default=None,
                    help="default: pipelined when every table allows max_staleness_steps >= 1, else sync")
+    t.add_argument("--staleness", type=int, default=None,
+                   help="pipelined policy: sparse updates in flight (lookups miss that many steps; default: the "
+                        "smallest max_staleness_steps of the tables, at least 1)")
+    t.add_argument("--accumulation-steps", type=int, default=1,
+                   help="micro-steps per optimizer step (sync policy): sparse and dense updates once per window")
     e = sub.add_parser("eval")
     e.add_argument("--model-config", required=True)
     e.add_argument("--checkpoint-dir", required=True)
@@ -122,7 +127,8 @@ def train(args) -> int:
     cfg = _dlrm_cfg(args.model_config, args.table_shards)
     B = args.batch_per_gpu
     trainer = DLRMTrainer(cfg, B, max_bag_size=args.max_bag, rank=rank, world_size=world, device=dev,
-                          seed=args.seed, use_graph=not args.no_graph, sparse_policy=args.sparse_policy)
+                          seed=args.seed, use_graph=not args.no_graph, sparse_policy=args.sparse_policy,
+                          staleness=args.staleness, accumulation_steps=args.accumulation_steps)
     mgr = CheckpointManager(args.checkpoint_dir) if args.checkpoint_dir else None
     start = 0
     if args.resume and mgr is not None and latest_step(args.checkpoint_dir) is not None:

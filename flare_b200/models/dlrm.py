@@ -12,17 +12,20 @@ captured in a CUDA graph:
     dense optimizer (fused reduce-scatter + Adam + all-gather when data parallel)
 
 With ``sparse_policy="pipelined"`` (the default when every table's
-``max_staleness_steps`` is at least 1) the sparse update of step t-1 runs in the
-shadow of step t's dense work: a side stream carries every kernel that waits
-on the other ranks (embedding forward of step t, embedding backward of step
-t-1, the dense update) in the same order on every rank, while the main stream
-runs the dense kernels, which wait on nothing.  Step t therefore looks up
-tables that lack the update of step t-1 (staleness one step, the reference's
-``AsyncPolicy.pipelined``: src/flare/runtime/fluxway/workers/sparse_input.py:
-473-476 and the bounded-stale lookups of .../dynamic_embedding.py:109-130);
-``flush_pending_updates`` applies the last pending update (before a
-checkpoint, an evaluation or the end of training, as the reference's
-``flush_pending_updates``, .../dynamic_embedding.py:683).
+``max_staleness_steps`` is at least 1) the sparse update of step t-d runs in
+the shadow of step t's dense work, d being the smallest
+``max_staleness_steps`` of the tables (or ``staleness``): a side stream
+carries every kernel that waits on the other ranks (embedding forward of
+step t, embedding backward of step t-d, the dense update) in the same order
+on every rank, while the main stream runs the dense kernels, which wait on
+nothing.  Step t therefore looks up tables that lack the updates of steps
+t-d .. t-1 (the reference's bounded-stale lookups with pipeline depth d + 1:
+``sparse_lookup_async_policy``, src/flare/runtime/fluxway/workers/
+dynamic_embedding.py:109-130, and ``AsyncPolicy.pipelined``, .../
+sparse_input.py:473-476); staging and pooled-gradient buffers rotate over
+d + 1 slots.  ``flush_pending_updates`` applies the pending updates in step
+order (before a checkpoint, an evaluation or the end of training, as the
+reference's ``flush_pending_updates``, .../dynamic_embedding.py:683).
 
 ``DLRMTorch`` is the same model in plain PyTorch autograd (nn.EmbeddingBag,
 nn.Linear, torch optimizers): the CPU configuration, the numerics oracle and
@@ -92,6 +95,29 @@ def dlrm_benchmark_tables(vocab_sizes: list[int], dim: int = 128, optimizer: Spa
             for i, v in enumerate(vocab_sizes)]
 
 
+MAX_PIPELINE_STALENESS = 4  # staging and pooled-gradient buffers per slot: d + 1 of each
+
+
+def sparse_staleness(cfg: DLRMConfig, sparse_policy: str | None = None, staleness: int | None = None,
+                     accumulation_steps: int = 1) -> int:
+    """Steps of update lag the sparse policy runs with: 0 (sync) or d >= 1 (pipelined)."""
+    stale = [t.max_staleness_steps for t in cfg.tables]
+    if sparse_policy is None:  # from the tables: a staleness bound of >= 1 step everywhere allows the overlap
+        sparse_policy = "pipelined" if stale and min(stale) >= 1 and accumulation_steps == 1 else "sync"
+    if sparse_policy not in ("sync", "pipelined"):
+        raise ValueError(f"sparse_policy must be 'sync' or 'pipelined', not {sparse_policy!r}")
+    if sparse_policy == "sync":
+        return 0
+    if accumulation_steps > 1:
+        raise ValueError("accumulation windows run under the sync sparse policy")
+    d = int(staleness) if staleness is not None else max(1, min(stale, default=1))
+    if not 1 <= d <= MAX_PIPELINE_STALENESS:
+        raise ValueError(f"pipelined staleness must be in [1, {MAX_PIPELINE_STALENESS}], got {d}")
+    if stale and d > min(stale) and min(stale) >= 1:
+        raise ValueError(f"staleness {d} exceeds a table's max_staleness_steps ({min(stale)})")
+    return d
+
+
 def dlrm_plan(cfg: DLRMConfig, world_size: int, table_costs: list[float] | None = None, *,
               row_split: bool = False) -> ShardingPlan | None:
     """Sharding plan weighted by per-table work (None: the collection's default plan)."""
@@ -109,20 +135,14 @@ class DLRM:
                  device: torch.device | None = None, heap: SymmetricHeap | None = None, seed: int = 0,
                  global_batch_size: int | None = None, values_capacity: int | None = None,
                  table_costs: list[float] | None = None, plan: ShardingPlan | None = None,
-                 sparse_policy: str | None = None, accumulation_steps: int = 1):
+                 sparse_policy: str | None = None, accumulation_steps: int = 1, staleness: int | None = None):
         self.accum = int(accumulation_steps)
         if self.accum < 1:
             raise ValueError("accumulation_steps must be >= 1")
-        if sparse_policy is None:  # from the tables: a staleness bound of >= 1 step everywhere allows the overlap
-            stale = [t.max_staleness_steps for t in cfg.tables]
-            sparse_policy = "pipelined" if stale and min(stale) >= 1 and self.accum == 1 else "sync"
-        if sparse_policy not in ("sync", "pipelined"):
-            raise ValueError(f"sparse_policy must be 'sync' or 'pipelined', not {sparse_policy!r}")
-        if sparse_policy == "pipelined" and self.accum > 1:
-            raise ValueError("accumulation windows run under the sync sparse policy")
+        self.staleness = sparse_staleness(cfg, sparse_policy, staleness, self.accum)
         self.cfg = cfg
-        self.sparse_policy = sparse_policy
-        self.pipelined = sparse_policy == "pipelined"
+        self.pipelined = self.staleness > 0
+        self.sparse_policy = "pipelined" if self.pipelined else "sync"
         self.B = int(batch_size)
         self.global_B = int(global_batch_size or batch_size * world_size)
         self.rank, self.world = rank, world_size
@@ -152,10 +172,10 @@ class DLRM:
             cfg.tables, self.B, max_bag_size=max_bag_size, rank=rank, world_size=world_size, device=dev, heap=heap,
             optimizer=cfg.sparse_optimizer, seed=seed, values_capacity=values_capacity,
             plan=plan if plan is not None else dlrm_plan(cfg, world_size, table_costs), pipelined=self.pipelined,
-            accumulation_steps=self.accum)
-        # pipelined policy: staging slot of the next forward, slot whose sparse update is pending
+            pipeline_depth=max(self.staleness, 1), accumulation_steps=self.accum)
+        # pipelined policy: staging slot of the next forward; slots whose sparse updates are pending, oldest first
         self._next_slot = 0
-        self.pending_slot: int | None = None
+        self.pending: list[int] = []
         if self.pipelined:
             # high priority: the side stream carries the step's critical path (embedding forward and
             # backward); the dense kernels beside it fill the SMs it leaves
@@ -312,10 +332,16 @@ class DLRM:
         self.emb.backward()
         self.dense.apply(grad_scale=1.0 / micro)
 
+    @property
+    def pending_slot(self) -> int | None:
+        """Slot of the newest pending sparse update (None when nothing is pending)."""
+        return self.pending[-1] if self.pending else None
+
     def _pipelined_step(self) -> torch.Tensor:
         main = torch.cuda.current_stream(self.device)
         comm = self.comm_stream
-        slot, pend = self._next_slot, self.pending_slot
+        slot = self._next_slot
+        pend = self.pending[0] if len(self.pending) == self.staleness else None
         comm.wait_stream(main)  # this step's inputs and the previous step's dense reads are ordered before
         cast_pad_bf16(self.dense_in, self.xd)
         bot = self.bottom.forward(self.xd)
@@ -323,7 +349,7 @@ class DLRM:
             pooled = self.emb.forward(slot=slot)
             self._ev_fwd.record(comm)
             if pend is not None:
-                self.emb.backward(slot=pend)  # the previous step's sparse update, beside this step's dense work
+                self.emb.backward(slot=pend)  # step t-d's sparse update, beside this step's dense work
         main.wait_event(self._ev_fwd)
         interaction_forward(bot, pooled, self.F, self.inter, self.inter_status)
         h = self.top.forward(self.inter)
@@ -339,7 +365,8 @@ class DLRM:
             comm.wait_event(self._ev_bwd)
             self.dense.apply()
         main.wait_stream(comm)
-        self._next_slot, self.pending_slot = slot ^ 1, slot
+        self.pending = (self.pending[1:] if pend is not None else self.pending) + [slot]
+        self._next_slot = (slot + 1) % (self.staleness + 1)
         return self.loss_sum
 
     def flush_pending_updates(self) -> bool:
@@ -352,10 +379,11 @@ class DLRM:
         return self._flush_pipelined()
 
     def _flush_pipelined(self) -> bool:
-        if self.pending_slot is None:
+        if not self.pending:
             return False
-        self.emb.backward(slot=self.pending_slot)
-        self.pending_slot = None
+        for sl in self.pending:
+            self.emb.backward(slot=sl)
+        self.pending = []
         return True
 
     # host-side state of a step, for CUDA-graph capture (undone) and replay (advanced)
@@ -365,15 +393,17 @@ class DLRM:
             return ("micro", self.emb.micro_filled)
         if not self.pipelined:
             return 0
-        return None if self.pending_slot is None else (self._next_slot, self.pending_slot)
+        # steps that fill the pipeline run eagerly; a full pipeline cycles through d + 1 states
+        return None if len(self.pending) < self.staleness else (self._next_slot, tuple(self.pending))
 
     def host_state(self) -> tuple:
-        return (self.dense.step, self.emb.step, self._next_slot, self.pending_slot, self.emb._slot,
+        return (self.dense.step, self.emb.step, self._next_slot, tuple(self.pending), self.emb._slot,
                 self.emb.micro_filled, self.emb._micro)
 
     def restore_host_state(self, st: tuple) -> None:
-        (self.dense.step, self.emb.step, self._next_slot, self.pending_slot, self.emb._slot,
+        (self.dense.step, self.emb.step, self._next_slot, pending, self.emb._slot,
          self.emb.micro_filled, self.emb._micro) = st
+        self.pending = list(pending)
 
     def advance_host_state(self) -> None:
         """The host-side effect of one replayed step (a captured step runs exactly one sparse backward:
@@ -389,8 +419,10 @@ class DLRM:
         self.dense.step += 1
         self.emb.step += 1
         if self.pipelined:
-            self.emb._slot = self._next_slot
-            self._next_slot, self.pending_slot = self._next_slot ^ 1, self._next_slot
+            slot = self._next_slot
+            self.emb._slot = slot
+            self.pending = self.pending[1:] + [slot]
+            self._next_slot = (slot + 1) % (self.staleness + 1)
 
     def predict(self) -> torch.Tensor:
         """Forward only (eval): sigmoid probabilities [B, T]; no state changes besides staging.

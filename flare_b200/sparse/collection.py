@@ -102,6 +102,7 @@ class ShardedEmbeddingBagCollection:
         pipelined: bool = False,
         validate_inputs: bool | None = None,
         accumulation_steps: int = 1,
+        pipeline_depth: int = 1,
     ):
         if not tables:
             raise ValueError("at least one table is required")
@@ -129,14 +130,16 @@ class ShardedEmbeddingBagCollection:
         self.out_dtype, self.grad_dtype = out_dtype, grad_dtype
         self.step = 0
         dev = self.device
-        # pipelined sparse policy: the backward of step t-1 runs after the forward of step t, so the
-        # buffers a forward fills for its backward (staged ids / bags / lengths, pooled gradients) are
-        # double-buffered and every call names its staging slot
+        # pipelined sparse policy: the backward of step t-d runs after the forward of step t, so the
+        # buffers a forward fills for its backward (staged ids / bags / lengths, pooled gradients) rotate
+        # over d + 1 slots and every call names its staging slot
         self.pipelined = bool(pipelined)
+        if int(pipeline_depth) < 1:
+            raise ValueError("pipeline_depth must be >= 1")
         # debug mode (FLARE_VALIDATE_INPUTS=1): every batch's offsets and ids are checked before the copy
         self.validate_inputs = (os.environ.get("FLARE_VALIDATE_INPUTS", "0") == "1" if validate_inputs is None
                                 else bool(validate_inputs))
-        self.nbuf = 2 if self.pipelined else 1
+        self.nbuf = int(pipeline_depth) + 1 if self.pipelined else 1
         self._slot = 0
         if self.pipelined and any(t.dynamic or t.cache_rows is not None for t in self.tables):
             raise ValueError("the pipelined sparse policy needs resident static tables: the next forward's "
@@ -391,7 +394,7 @@ class ShardedEmbeddingBagCollection:
     @staticmethod
     def exchange_bytes(tables: list[SparseTableSpec], batch_size: int, max_bag_size: int,
                        values_capacity: int | None = None, plan: ShardingPlan | None = None,
-                       pipelined: bool = False, accumulation_steps: int = 1) -> int:
+                       pipelined: bool = False, accumulation_steps: int = 1, pipeline_depth: int = 1) -> int:
         """Symmetric memory of the exchange buffers (ids, pooled rows, pooled grads, row-wise partials)."""
         F, B = len(tables), int(batch_size)
         cap = values_capacity or F * B * max_bag_size
@@ -400,7 +403,7 @@ class ShardedEmbeddingBagCollection:
         rw = [i for i, r in enumerate(shards) if r > 1]
         part = 4 * max([shards[i] for i in rw], default=0) * B * sum(tables[i].embedding_dim for i in rw)
         remap = 4 * cap if any(t.dynamic for t in tables) else 0
-        grads = (2 if pipelined else 1) * max(1, int(accumulation_steps))
+        grads = (int(pipeline_depth) + 1 if pipelined else 1) * max(1, int(accumulation_steps))
         return 4 * (F * B + 1) + 4 * cap + remap + (1 + grads) * 4 * B * dim + part + NUM_FLAG_ARRAYS * 64 + 4096
 
     def _heap_bytes(self) -> int:

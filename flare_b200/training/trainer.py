@@ -22,7 +22,7 @@ import torch
 
 from .._native import native
 from ..data.synthetic import SparseBatch
-from ..models.dlrm import DLRM, DLRMConfig, dlrm_plan
+from ..models.dlrm import DLRM, DLRMConfig, dlrm_plan, sparse_staleness
 from ..parallel.dist import barrier
 from ..parallel.symm import SymmetricHeap
 from ..sparse.collection import ShardedEmbeddingBagCollection
@@ -203,34 +203,27 @@ class FusedTrainer:
         torch.cuda.synchronize(self.device)
 
 
-def _pipelined(cfg: DLRMConfig, sparse_policy: str | None) -> bool:
-    if sparse_policy is not None:
-        return sparse_policy == "pipelined"
-    stale = [t.max_staleness_steps for t in cfg.tables]
-    return bool(stale) and min(stale) >= 1
-
-
 class DLRMTrainer(FusedTrainer):
     def __init__(self, cfg: DLRMConfig, batch_size: int, *, max_bag_size: int, rank: int = 0, world_size: int = 1,
                  device: torch.device | None = None, seed: int = 0, use_graph: bool = True,
                  values_capacity: int | None = None, heap_bytes: int | None = None,
                  table_costs: list[float] | None = None, row_split: bool = False, sparse_policy: str | None = None,
-                 accumulation_steps: int = 1):
+                 accumulation_steps: int = 1, staleness: int | None = None):
         device = device or torch.device("cuda", torch.cuda.current_device())
         heap = None
         plan = dlrm_plan(cfg, world_size, table_costs, row_split=row_split)
+        depth = sparse_staleness(cfg, sparse_policy, staleness, accumulation_steps)
         if world_size > 1:
             exchange = ShardedEmbeddingBagCollection.exchange_bytes(
-                cfg.tables, batch_size, max_bag_size, values_capacity, plan=plan,
-                pipelined=accumulation_steps == 1 and _pipelined(cfg, sparse_policy),
-                accumulation_steps=accumulation_steps)
+                cfg.tables, batch_size, max_bag_size, values_capacity, plan=plan, pipelined=depth > 0,
+                pipeline_depth=max(depth, 1), accumulation_steps=accumulation_steps)
             dense = 6 * 16 * 1024 * 1024  # flat fp32 grads + bf16 params for up to 16M parameters
             need = heap_bytes or (exchange + dense + 64 * 1024 * 1024)
             heap = SymmetricHeap(need, rank=rank, world_size=world_size, device=device)
         self.heap = heap
         model = DLRM(cfg, batch_size, max_bag_size=max_bag_size, rank=rank, world_size=world_size,
                      device=device, heap=heap, seed=seed, values_capacity=values_capacity, plan=plan,
-                     sparse_policy=sparse_policy, accumulation_steps=accumulation_steps)
+                     sparse_policy=sparse_policy, accumulation_steps=accumulation_steps, staleness=staleness)
         super().__init__(model, batch_size, device=device, rank=rank, world_size=world_size, use_graph=use_graph)
 
 

@@ -68,46 +68,55 @@ def test_plans_schema_precision():
     assert PrecisionPolicy.FP32.sparse_gradient_transport_dtype_name == "float32"
 
 
-def test_pipelined_host_state_machine_without_cuda():
-    """Graph keys, capture snapshot / restore and replay advance of the fused DLRM's host state."""
+def _host_model(pipelined, staleness=1, accum=1):
     from types import SimpleNamespace
 
     from flare_b200.models.dlrm import DLRM
 
-    def model(pipelined):
-        m = object.__new__(DLRM)  # no CUDA: only the host-side bookkeeping is exercised
-        m.pipelined, m._next_slot, m.pending_slot, m.accum = pipelined, 0, None, 1
-        m.dense, m.emb = SimpleNamespace(step=0), SimpleNamespace(step=0, _slot=0, micro_filled=0, _micro=0)
-        return m
+    m = object.__new__(DLRM)  # no CUDA: only the host-side bookkeeping is exercised
+    m.pipelined, m.staleness, m.accum = pipelined, staleness if pipelined else 0, accum
+    m._next_slot, m.pending = 0, []
+    m.dense, m.emb = SimpleNamespace(step=0), SimpleNamespace(step=0, _slot=0, micro_filled=0, _micro=0)
+    return m
 
-    s = model(False)
+
+def test_pipelined_host_state_machine_without_cuda():
+    """Graph keys, capture snapshot / restore and replay advance of the fused DLRM's host state."""
+    s = _host_model(False)
     assert s.graph_key() == 0
     s.advance_host_state()
     assert (s.dense.step, s.emb.step) == (1, 1)
 
-    p = model(True)
+    p = _host_model(True)
     assert p.graph_key() is None  # the first step has no pending update: eager, never captured
-    p._next_slot, p.pending_slot, p.emb._slot = 1, 0, 0  # after one eager step on slot 0
+    p._next_slot, p.pending, p.emb._slot = 1, [0], 0  # after one eager step on slot 0
     keys = []
     for _ in range(4):
         keys.append(p.graph_key())
         snap = p.host_state()
-        p._next_slot, p.pending_slot, p.dense.step = 9, 9, 99  # what a capture may leave behind
+        p._next_slot, p.pending, p.dense.step = 9, [9], 99  # what a capture may leave behind
         p.restore_host_state(snap)
         p.advance_host_state()
-    assert keys == [(1, 0), (0, 1), (1, 0), (0, 1)]  # two graphs, alternating
+    assert keys == [(1, (0,)), (0, (1,)), (1, (0,)), (0, (1,))]  # two graphs, alternating
     assert (p.dense.step, p.emb.step, p.emb._slot, p._next_slot, p.pending_slot) == (4, 4, 0, 1, 0)
+
+
+def test_pipeline_of_depth_two_host_state_machine_without_cuda():
+    """Staleness 2: two updates in flight, three slots in rotation, three graph keys."""
+    p = _host_model(True, staleness=2)
+    assert p.graph_key() is None
+    p._next_slot, p.pending = 2, [0, 1]  # after two eager steps on slots 0 and 1
+    keys = []
+    for _ in range(6):
+        keys.append(p.graph_key())
+        p.advance_host_state()
+    assert keys == [(2, (0, 1)), (0, (1, 2)), (1, (2, 0))] * 2
+    assert (p.dense.step, p.emb.step, p._next_slot, p.pending) == (6, 6, 2, [0, 1])
 
 
 def test_accumulation_window_host_state_machine_without_cuda():
     """A window of 3 micro-steps: one graph per position, optimizer steps only when the window closes."""
-    from types import SimpleNamespace
-
-    from flare_b200.models.dlrm import DLRM
-
-    m = object.__new__(DLRM)
-    m.pipelined, m._next_slot, m.pending_slot, m.accum = False, 0, None, 3
-    m.dense, m.emb = SimpleNamespace(step=0), SimpleNamespace(step=0, _slot=0, micro_filled=0, _micro=0)
+    m = _host_model(False, accum=3)
     keys, steps = [], []
     for _ in range(7):
         keys.append(m.graph_key())

@@ -55,31 +55,33 @@ def test_training_reduces_loss_and_graph_matches_eager(cuda):
         assert abs(a - b) <= tol, (i, a, b)
 
 
-def test_pipelined_policy_matches_stale_emulation(cuda):
-    """Pipelined steps equal sync steps whose lookups read the tables one sparse update behind."""
+@pytest.mark.parametrize("staleness", [1, 2])
+def test_pipelined_policy_matches_stale_emulation(cuda, staleness):
+    """Pipelined steps equal sync steps whose lookups read the tables ``staleness`` sparse updates behind."""
     cfg = _cfg(lr_sparse=0.05)
-    B = 256
+    B, d = 256, staleness
     data = DLRMSyntheticData(B, VOCABS, max_bag=8, device=cuda, seed=11, pos_rate=0.3)
-    batches = [data.next() for _ in range(7)]
-    tr = DLRMTrainer(cfg, B, max_bag_size=8, device=cuda, seed=4, use_graph=True, sparse_policy="pipelined")
+    batches = [data.next() for _ in range(8)]
+    tr = DLRMTrainer(cfg, B, max_bag_size=8, device=cuda, seed=4, use_graph=True, sparse_policy="pipelined",
+                     staleness=d)
     piped = [tr.train_step(b).loss for b in batches]
-    assert tr.model.pending_slot is not None and len(tr.graphs) == 2  # slots alternate: one graph per parity
+    # d updates in flight; the slots rotate over d + 1 buffers: one graph per position
+    assert len(tr.model.pending) == d and len(tr.graphs) == d + 1
     assert tr.flush_pending_updates() and not tr.flush_pending_updates()
     tr.check()
 
     ref = DLRM(cfg, B, max_bag_size=8, device=cuda, seed=4)
-    prev, emulated = None, []
-    for b in batches:
+    hist, emulated = [ref.emb.weights.clone()], []  # hist[k]: tables after the updates of steps < k
+    for t, b in enumerate(batches):
         ref.set_batch(b.dense, b.labels, b.offsets, b.values, non_blocking=False)
-        cur = ref.emb.weights.clone()  # tables with the updates of every earlier step
-        if prev is not None:
-            ref.emb.weights.copy_(prev)  # lookups see the tables before the previous step's update
+        cur = ref.emb.weights.clone()
+        ref.emb.weights.copy_(hist[max(t - d, 0)])  # lookups miss the updates of steps t-d .. t-1
         loss = ref.forward_backward()
         ref.emb.weights.copy_(cur)
         ref.emb.backward()
         ref.dense.apply()
         emulated.append(float(loss.item()) / B)
-        prev = cur
+        hist.append(ref.emb.weights.clone())
     ref.check()
     for a, b in zip(piped, emulated):
         assert abs(a - b) <= 1e-3 * max(1.0, abs(a)), (piped, emulated)
