@@ -4,7 +4,12 @@ Every rank trains the multitask PLE recipe (fused sharded embeddings, flat
 fused optimizer: ZeRO-1 reduce-scatter + Adam + all-gather over NVLink peer
 memory) on its own local batch; rank 0 also trains a one-GPU copy on the
 concatenation of every rank's batch.  The global losses and the final dense
-master weights and tables must agree (fp32 / bf16 tolerance).
+master weights and tables must agree (fp32 / bf16 tolerance).  The tables
+train with SGD here: a row-wise Adagrad step normalises a row's gradient, so
+a row whose summed gradient nearly cancels moves by up to the learning rate
+on bf16 rounding differences alone (the per-sample gradients of a batch of B
+and of 2B come from differently tiled GEMMs), which would hide a routing
+error of the same size.
 
     python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 \\
         -m flare_b200.recipes.multitask_dist_check
@@ -18,6 +23,7 @@ import torch.distributed as dist
 
 from flare_b200.parallel.dist import init_distributed
 from flare_b200.recipes.multitask import MultitaskModelBuilder, MultitaskRankingRecipe, synthetic_multitask_batch
+from flare_b200.sparse.config import SparseOptimizerConfig
 
 
 def _concat(batches, F, B):
@@ -37,7 +43,7 @@ def main(steps: int = 4, B: int = 256) -> int:
     info = init_distributed(timeout_s=120)
     rank, world = info.rank, info.world_size
     dev = torch.device("cuda", torch.cuda.current_device())
-    builder = MultitaskModelBuilder()
+    builder = MultitaskModelBuilder(sparse_optimizer=SparseOptimizerConfig(kind="sgd", learning_rate=0.05))
     recipe = MultitaskRankingRecipe(name="mt", task_name="ranking", batch_size=B, builder=builder)
     data = [[synthetic_multitask_batch(B, builder.vocabs, builder.num_dense, builder.max_bag_size,
                                        seed=1000 * r + s, device=dev) for s in range(steps)] for r in range(world)]

@@ -88,18 +88,28 @@ def test_assembled_training_and_evaluation_graphs(cuda, tmp_path):
     assert set(g["task_graph"].phase_seconds) == set(RANKING_PHASE_ORDER)
     assert losses[-1] < losses[0]
     assert g["metrics"].window.completed or g["metrics"].window.total_steps == 40
-    # a timeline of 12 more steps without per-step loss reads: the host materialises the next step's
-    # batch while the GPU trains this one
+    # a timeline without per-step loss reads, at a batch where the GPU step outlasts the host's work per
+    # step (pre-built device batches, no metric forward): the host materialises the next step's batch
+    # while the GPU trains this one
+    import itertools
+
     from flare_b200.validation.overlap import effective_overlap, phase_overlap
     from flare_b200.validation.perfetto import PerfettoWriter, parse_trace
 
+    big_B = 8192
+    big = MultitaskRankingRecipe(name="mt", task_name="ranking", batch_size=big_B, builder=builder)
+    pool = [synthetic_multitask_batch(big_B, builder.vocabs, builder.num_dense, builder.max_bag_size, seed=50 + i,
+                                      device=cuda) for i in range(4)]
+    tl = assemble_ranking_training_graph(build_pipeline_nodes(big, source=itertools.cycle(pool), device=cuda,
+                                                              seed=1))["task_graph"]
+    tl.run(4)  # eager steps and the graph capture
     w = PerfettoWriter()
-    g["task_graph"].run(12, read_loss_every=0, trace=w)
+    tl.run(12, read_loss_every=0, trace=w)
     path = w.save(tmp_path / "ranking.pftrace")
-    rep = phase_overlap(parse_trace(path), set(range(42, 51)))
-    assert all(r["overlaps"]["materialize_next"]["present"] for r in rep["rows"])
-    assert effective_overlap(rep, relations=("materialize_next",))["relations"]["materialize_next"][
-        "positive_hidden_count"] > 0
+    rep = phase_overlap(parse_trace(path), set(range(5, 15)))
+    assert len(rep["rows"]) == 10 and all(r["overlaps"]["materialize_next"]["present"] for r in rep["rows"])
+    eff = effective_overlap(rep, relations=("materialize_next",))
+    assert eff["relations"]["materialize_next"]["positive_hidden_count"] > 0, eff
     ev_inputs = build_pipeline_nodes(recipe, source=source(10_000), device=cuda, seed=1)
     ev_inputs.trainer = inputs.trainer  # evaluate the trained model
     out = assemble_ranking_evaluation_graph(ev_inputs)["task_graph"].run(4)
