@@ -13,6 +13,7 @@
 #include "embedding.cuh"
 #include "gemm.cuh"
 #include "host_tier.cuh"
+#include "mixing.cuh"
 #include "seqrec.cuh"
 #include "sparse_ops.cuh"
 
@@ -701,6 +702,37 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     flare::dcn_finalize_grad(P<const float>(acc), ld_acc, rows, cols, P<__nv_bfloat16>(grad), ldg, cur_stream());
   });
 
+  m.def("gate_mix", [](const py::dict& d, bool backward) {
+    flare::GateMixParams p{};
+    const auto ys = get<std::vector<uintptr_t>>(d, "ys");
+    FLARE_CHECK(!ys.empty() && ys.size() <= static_cast<size_t>(flare::kMixMaxExperts), "gate_mix: 1..64 experts");
+    p.E = static_cast<int>(ys.size());
+    for (int e = 0; e < p.E; ++e) p.ys[e] = P<const __nv_bfloat16>(ys[e]);
+    p.logits = P<const __nv_bfloat16>(get<uintptr_t>(d, "logits"));
+    p.ld_logits = get<int64_t>(d, "ld_logits");
+    p.probs = P<float>(get<uintptr_t>(d, "probs"));
+    p.ld_y = get<int64_t>(d, "ld_y");
+    p.ld_out = get<int64_t>(d, "ld_out");
+    p.B = get<int>(d, "B");
+    p.D = get<int>(d, "D");
+    if (backward) {
+      const auto dys = get<std::vector<uintptr_t>>(d, "dys");
+      FLARE_CHECK(dys.size() == ys.size(), "gate_mix: one gradient per expert output");
+      for (int e = 0; e < p.E; ++e) p.dys[e] = P<__nv_bfloat16>(dys[e]);
+      p.ld_dy = get<int64_t>(d, "ld_dy");
+      p.dlogits = P<__nv_bfloat16>(get<uintptr_t>(d, "dlogits"));
+      p.dout = P<const __nv_bfloat16>(get<uintptr_t>(d, "dout"));
+      flare::gate_mix_backward(p, cur_stream());
+    } else {
+      p.out = P<__nv_bfloat16>(get<uintptr_t>(d, "out"));
+      flare::gate_mix_forward(p, cur_stream());
+    }
+  });
+  m.def("relu_bwd_colsum", [](uintptr_t g, int64_t ldg, uintptr_t h, int64_t ldh, int64_t rows, int cols,
+                              uintptr_t gout, int64_t ldo, uintptr_t colsum) {
+    flare::relu_bwd_colsum(P<const __nv_bfloat16>(g), ldg, P<const __nv_bfloat16>(h), ldh, rows, cols,
+                           P<__nv_bfloat16>(gout), ldo, P<float>(colsum), cur_stream());
+  });
   m.def("colsum_bf16", [](uintptr_t x, int64_t rows, int cols, int64_t ldx, uintptr_t out) {
     flare::colsum_bf16(P<const __nv_bfloat16>(x), rows, cols, ldx, P<float>(out), cur_stream());
   });

@@ -1,0 +1,301 @@
+// Fused kernels of the multitask layer library.
+//
+// gate_mix: the expert mixing of PLE / CGC gates (softmax over the gate
+// logits in fp32, weighted sum of the expert outputs) in one pass over the
+// expert rows, and its backward (expert-output gradients and the softmax
+// Jacobian-vector product for the gate logits) in one more.  Reference
+// semantics: `_GatedExperts._mix` of src/flare/jax/layers/multitask.py
+// (stack, fp32 softmax, fp32 sum).
+//
+// relu_bwd_colsum: ReLU backward of an MLP layer fused with its bias
+// gradient (column sums in fp32).
+#include "mixing.cuh"
+
+#include <algorithm>
+
+namespace flare {
+namespace {
+
+constexpr int kMixThreads = 256;
+constexpr int kMixWarps = kMixThreads / 32;
+constexpr int kMixMaxChunksPerLane = 4;  // D <= 32 lanes * 4 chunks * 8 = 1024
+
+__device__ __forceinline__ void bf16x8_to_f32(const int4& v, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ int4 f32_to_bf16x8(const float (&f)[8]) {
+  int4 v;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  return v;
+}
+
+// softmax of one row's E (<= 64) logits across the warp; lane l holds entries l and l + 32
+__device__ __forceinline__ void row_softmax(const GateMixParams& p, int64_t row, float& p0, float& p1) {
+  const int lane = lane_id();
+  const __nv_bfloat16* lg = p.logits + row * p.ld_logits;
+  const float x0 = lane < p.E ? __bfloat162float(lg[lane]) : -INFINITY;
+  const float x1 = lane + 32 < p.E ? __bfloat162float(lg[lane + 32]) : -INFINITY;
+  float m = fmaxf(x0, x1);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float e0 = lane < p.E ? __expf(x0 - m) : 0.f;
+  const float e1 = lane + 32 < p.E ? __expf(x1 - m) : 0.f;
+  float s = e0 + e1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float inv = 1.f / s;
+  p0 = e0 * inv;
+  p1 = e1 * inv;
+}
+
+// G lanes per row, 32 / G rows per warp at a time
+template <int G>
+__global__ void __launch_bounds__(kMixThreads) gate_mix_fwd_kernel(GateMixParams p) {
+  constexpr int R = 32 / G;
+  __shared__ float sp[kMixWarps][R][kMixMaxExperts];
+  const int warp = threadIdx.x >> 5, lane = lane_id();
+  const int grp = lane / G, sub = lane % G;
+  const int nchunk = p.D / 8;
+  const int64_t tiles = (static_cast<int64_t>(p.B) + R - 1) / R;
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * kMixWarps + warp; t < tiles;
+       t += static_cast<int64_t>(gridDim.x) * kMixWarps) {
+    const int64_t row0 = t * R;
+    for (int r = 0; r < R; ++r) {
+      const int64_t row = row0 + r;
+      if (row >= p.B) break;
+      float p0, p1;
+      row_softmax(p, row, p0, p1);
+      if (lane < p.E) {
+        sp[warp][r][lane] = p0;
+        p.probs[row * p.E + lane] = p0;
+      }
+      if (lane + 32 < p.E) {
+        sp[warp][r][lane + 32] = p1;
+        p.probs[row * p.E + lane + 32] = p1;
+      }
+    }
+    __syncwarp();
+    const int64_t row = row0 + grp;
+    if (row < p.B) {
+      for (int c = sub; c < nchunk; c += G) {
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        const int64_t off = row * p.ld_y + c * 8;
+        int e = 0;
+        for (; e + 4 <= p.E; e += 4) {  // four expert rows in flight
+          int4 v[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) v[k] = __ldg(reinterpret_cast<const int4*>(p.ys[e + k] + off));
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            float f[8];
+            bf16x8_to_f32(v[k], f);
+            const float pe = sp[warp][grp][e + k];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = fmaf(pe, f[i], acc[i]);
+          }
+        }
+        for (; e < p.E; ++e) {
+          float f[8];
+          bf16x8_to_f32(__ldg(reinterpret_cast<const int4*>(p.ys[e] + off)), f);
+          const float pe = sp[warp][grp][e];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] = fmaf(pe, f[i], acc[i]);
+        }
+        *reinterpret_cast<int4*>(p.out + row * p.ld_out + c * 8) = f32_to_bf16x8(acc);
+      }
+    }
+    __syncwarp();
+  }
+}
+
+template <int G>
+__global__ void __launch_bounds__(kMixThreads) gate_mix_bwd_kernel(GateMixParams p) {
+  constexpr int R = 32 / G;
+  __shared__ float sp[kMixWarps][R][kMixMaxExperts];
+  __shared__ float ss[kMixWarps][R][kMixMaxExperts];
+  const int warp = threadIdx.x >> 5, lane = lane_id();
+  const int grp = lane / G, sub = lane % G;
+  const int nchunk = p.D / 8;
+  const int64_t tiles = (static_cast<int64_t>(p.B) + R - 1) / R;
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * kMixWarps + warp; t < tiles;
+       t += static_cast<int64_t>(gridDim.x) * kMixWarps) {
+    const int64_t row0 = t * R;
+    for (int i = lane; i < R * p.E; i += 32) {
+      const int r = i / p.E, e = i - r * p.E;
+      sp[warp][r][e] = row0 + r < p.B ? p.probs[(row0 + r) * p.E + e] : 0.f;
+    }
+    __syncwarp();
+    const int64_t row = row0 + grp;
+    const bool live = row < p.B;
+    // this lane's chunks of dout, kept in registers across the experts
+    float g[kMixMaxChunksPerLane][8];
+#pragma unroll
+    for (int k = 0; k < kMixMaxChunksPerLane; ++k) {
+      const int c = sub + k * G;
+      if (live && c < nchunk) {
+        bf16x8_to_f32(__ldg(reinterpret_cast<const int4*>(p.dout + row * p.ld_out + c * 8)), g[k]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) g[k][i] = 0.f;
+      }
+    }
+    for (int e = 0; e < p.E; ++e) {
+      const float pe = sp[warp][grp][e];
+      float dot = 0.f;
+#pragma unroll
+      for (int k = 0; k < kMixMaxChunksPerLane; ++k) {
+        const int c = sub + k * G;
+        if (live && c < nchunk) {
+          float f[8], d[8];
+          bf16x8_to_f32(__ldg(reinterpret_cast<const int4*>(p.ys[e] + row * p.ld_y + c * 8)), f);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            dot = fmaf(g[k][i], f[i], dot);
+            d[i] = pe * g[k][i];
+          }
+          *reinterpret_cast<int4*>(p.dys[e] + row * p.ld_dy + c * 8) = f32_to_bf16x8(d);
+        }
+      }
+#pragma unroll
+      for (int o = G / 2; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      if (sub == 0) ss[warp][grp][e] = dot;
+    }
+    __syncwarp();
+    for (int r = 0; r < R; ++r) {
+      const int64_t rr = row0 + r;
+      if (rr >= p.B) break;
+      const float p0 = lane < p.E ? sp[warp][r][lane] : 0.f;
+      const float p1 = lane + 32 < p.E ? sp[warp][r][lane + 32] : 0.f;
+      const float s0 = lane < p.E ? ss[warp][r][lane] : 0.f;
+      const float s1 = lane + 32 < p.E ? ss[warp][r][lane + 32] : 0.f;
+      float tot = p0 * s0 + p1 * s1;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+      __nv_bfloat16* dl = p.dlogits + rr * p.ld_logits;
+      if (lane < p.E) dl[lane] = __float2bfloat16_rn(p0 * (s0 - tot));
+      if (lane + 32 < p.E) dl[lane + 32] = __float2bfloat16_rn(p1 * (s1 - tot));
+    }
+    __syncwarp();
+  }
+}
+
+// block (32, 8): thread x covers 8 consecutive columns, rows strided over the y threads and gridDim.y
+__global__ void relu_bwd_colsum_kernel(const __nv_bfloat16* __restrict__ g, int64_t ldg,
+                                       const __nv_bfloat16* __restrict__ h, int64_t ldh, int64_t rows, int cols,
+                                       __nv_bfloat16* __restrict__ gout, int64_t ldo, float* __restrict__ colsum) {
+  __shared__ float part[8][32][9];
+  const int c8 = (blockIdx.x * 32 + threadIdx.x) * 8;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (c8 < cols) {
+    for (int64_t r = static_cast<int64_t>(blockIdx.y) * 8 + threadIdx.y; r < rows;
+         r += static_cast<int64_t>(gridDim.y) * 8) {
+      float gv[8], hv[8];
+      bf16x8_to_f32(__ldg(reinterpret_cast<const int4*>(g + r * ldg + c8)), gv);
+      bf16x8_to_f32(__ldg(reinterpret_cast<const int4*>(h + r * ldh + c8)), hv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        gv[i] = hv[i] > 0.f ? gv[i] : 0.f;
+      }
+      const int4 o = f32_to_bf16x8(gv);
+      *reinterpret_cast<int4*>(gout + r * ldo + c8) = o;
+      // the bias gradient sums the rounded values the next GEMM consumes
+      float rv[8];
+      bf16x8_to_f32(o, rv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += rv[i];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) part[threadIdx.y][threadIdx.x][i] = acc[i];
+  __syncthreads();
+  if (threadIdx.y == 0 && c8 < cols) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float s = 0.f;
+#pragma unroll
+      for (int y = 0; y < 8; ++y) s += part[y][threadIdx.x][i];
+      atomicAdd(colsum + c8 + i, s);
+    }
+  }
+}
+
+int lanes_per_row(int D) {
+  const int nchunk = D / 8;
+  int G = 4;
+  while (G < 32 && G < nchunk) G <<= 1;
+  return G;
+}
+
+void check_mix(const GateMixParams& p) {
+  FLARE_CHECK(p.E >= 1 && p.E <= kMixMaxExperts, "gate_mix: 1..64 experts");
+  FLARE_CHECK(p.D % 8 == 0 && p.D <= 8 * 32 * kMixMaxChunksPerLane, "gate_mix: width a multiple of 8, <= 1024");
+  FLARE_CHECK(p.ld_y % 8 == 0 && p.ld_out % 8 == 0, "gate_mix: row strides must keep rows 16-byte aligned");
+  for (int e = 0; e < p.E; ++e)
+    FLARE_CHECK((reinterpret_cast<uintptr_t>(p.ys[e]) & 15) == 0, "gate_mix: expert outputs 16-byte aligned");
+}
+
+int mix_grid(int64_t B, int G) {
+  const int64_t tiles = (B + 32 / G - 1) / (32 / G);
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((tiles + kMixWarps - 1) / kMixWarps, 148 * 8)));
+}
+
+}  // namespace
+
+void gate_mix_forward(const GateMixParams& p, cudaStream_t s) {
+  check_mix(p);
+  if (p.B == 0) return;
+  const int G = lanes_per_row(p.D);
+  const int grid = mix_grid(p.B, G);
+  switch (G) {
+    case 4: gate_mix_fwd_kernel<4><<<grid, kMixThreads, 0, s>>>(p); break;
+    case 8: gate_mix_fwd_kernel<8><<<grid, kMixThreads, 0, s>>>(p); break;
+    case 16: gate_mix_fwd_kernel<16><<<grid, kMixThreads, 0, s>>>(p); break;
+    default: gate_mix_fwd_kernel<32><<<grid, kMixThreads, 0, s>>>(p); break;
+  }
+  FLARE_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void gate_mix_backward(const GateMixParams& p, cudaStream_t s) {
+  check_mix(p);
+  FLARE_CHECK(p.ld_dy % 8 == 0, "gate_mix: gradient rows 16-byte aligned");
+  for (int e = 0; e < p.E; ++e)
+    FLARE_CHECK((reinterpret_cast<uintptr_t>(p.dys[e]) & 15) == 0, "gate_mix: gradients 16-byte aligned");
+  if (p.B == 0) return;
+  const int G = lanes_per_row(p.D);
+  const int grid = mix_grid(p.B, G);
+  switch (G) {
+    case 4: gate_mix_bwd_kernel<4><<<grid, kMixThreads, 0, s>>>(p); break;
+    case 8: gate_mix_bwd_kernel<8><<<grid, kMixThreads, 0, s>>>(p); break;
+    case 16: gate_mix_bwd_kernel<16><<<grid, kMixThreads, 0, s>>>(p); break;
+    default: gate_mix_bwd_kernel<32><<<grid, kMixThreads, 0, s>>>(p); break;
+  }
+  FLARE_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+void relu_bwd_colsum(const __nv_bfloat16* g, int64_t ldg, const __nv_bfloat16* h, int64_t ldh, int64_t rows,
+                     int cols, __nv_bfloat16* gout, int64_t ldo, float* colsum, cudaStream_t s) {
+  FLARE_CHECK(cols % 8 == 0 && ldg % 8 == 0 && ldh % 8 == 0 && ldo % 8 == 0,
+              "relu_bwd_colsum: columns and strides must be multiples of 8");
+  FLARE_CHECK(((reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(gout)) &
+               15) == 0,
+              "relu_bwd_colsum: 16-byte aligned rows");
+  if (rows == 0) return;
+  const int gx = ceil_div(cols / 8, 32);
+  const int gy = std::max(1, std::min<int>(ceil_div(rows, 64), std::max(1, 148 * 8 / gx)));
+  relu_bwd_colsum_kernel<<<dim3(gx, gy), dim3(32, 8), 0, s>>>(g, ldg, h, ldh, rows, cols, gout, ldo, colsum);
+  FLARE_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+}  // namespace flare

@@ -12,7 +12,11 @@ numerics helpers.
 ``TcLinear`` is a linear layer whose forward and backward GEMMs run on the
 hand-written tcgen05 kernel when the input is a bf16 CUDA tensor (weight
 gradients accumulate in fp32, as ``fp32_weight_gradient_dot_general`` does in
-the reference); otherwise it is a plain fp32 ``nn.Linear``.
+the reference); otherwise it is a plain fp32 ``nn.Linear``.  A ReLU ``MLP`` on
+bf16 CUDA inputs runs as one autograd node: bias + ReLU in the GEMM
+epilogues, and in the backward each layer's input-gradient GEMM applies the
+previous layer's ReLU mask and sums its bias gradient in the epilogue.  The
+gates' expert mixing is one fused kernel per direction (``ops.mixing``).
 """
 from __future__ import annotations
 
@@ -25,6 +29,7 @@ import torch.nn.functional as F
 
 from ..ops.dense import colsum_
 from ..ops.gemm import gemm
+from ..ops.mixing import gate_mix, relu_bwd_colsum_
 
 
 # ---------------------------------------------------------------- numerics
@@ -89,10 +94,70 @@ class _TcLinearFn(torch.autograd.Function):
 class TcLinear(nn.Linear):
     """nn.Linear that uses the tcgen05 GEMM for bf16 CUDA inputs (dims multiple of 8)."""
 
+    def tc_eligible(self, x: torch.Tensor) -> bool:
+        return x.is_cuda and x.dtype == torch.bfloat16 and self.in_features % 8 == 0 and self.out_features % 8 == 0
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        if x.is_cuda and x.dtype == torch.bfloat16 and self.in_features % 8 == 0 and self.out_features % 8 == 0:
+        if self.tc_eligible(x):
             return _TcLinearFn.apply(x, self.weight, self.bias)
         return F.linear(x, self.weight.to(x.dtype), None if self.bias is None else self.bias.to(x.dtype))
+
+
+class _TcReluMLPFn(torch.autograd.Function):
+    """A stack of TcLinear layers with ReLU between them (and optionally after the last) as one node.
+
+    Forward: bias + ReLU in every GEMM epilogue.  Backward: the last layer's ReLU mask and bias
+    gradient in one pass (``relu_bwd_colsum``); then per layer the weight gradient (fp32, accumulated
+    into the flat buffer when bound) and the input-gradient GEMM whose epilogue applies the previous
+    layer's ReLU mask and adds the previous layer's bias gradient."""
+
+    @staticmethod
+    def forward(ctx, x, last_relu, *params):
+        L = len(params) // 2
+        h = x.reshape(-1, x.shape[-1]).contiguous()
+        hs, wbs = [h], []
+        for i in range(L):
+            w, b = params[2 * i], params[2 * i + 1]
+            wb = w.to(torch.bfloat16).contiguous()
+            h = gemm(h, wb, bias=b.to(torch.bfloat16), relu=i < L - 1 or last_relu)
+            hs.append(h)
+            wbs.append(wb)
+        ctx.save_for_backward(*hs, *wbs)
+        ctx.L, ctx.last_relu, ctx.shape = L, last_relu, x.shape
+        ctx.flat = [getattr(p, "_flare_grad", None) for p in params]
+        ctx.param_shapes = [p.shape for p in params]
+        return h.reshape(*x.shape[:-1], h.shape[-1])
+
+    @staticmethod
+    def backward(ctx, gy):
+        L = ctx.L
+        saved = ctx.saved_tensors
+        hs, wbs = saved[:L + 1], saved[L + 1:]
+        dev = gy.device
+        grads: list[torch.Tensor | None] = [None] * (2 * L)
+
+        def target(k):  # where parameter k's gradient goes: its flat fp32 view, or a fresh fp32 buffer
+            if ctx.flat[k] is not None:
+                return ctx.flat[k]
+            grads[k] = torch.zeros(ctx.param_shapes[k], dtype=torch.float32, device=dev)
+            return grads[k]
+
+        g = gy.reshape(-1, gy.shape[-1]).to(torch.bfloat16).contiguous()
+        db = target(2 * L - 1)
+        if ctx.last_relu:
+            gm = torch.empty_like(g)
+            relu_bwd_colsum_(g, hs[L], gm, db)
+            g = gm
+        else:
+            colsum_(g, db)
+        dx = None
+        for i in reversed(range(L)):
+            gemm(g, hs[i], a_t=True, b_t=True, out=target(2 * i), accumulate=True)
+            if i > 0:
+                g = gemm(g, wbs[i], b_t=True, mask=hs[i], colsum=target(2 * i - 1))
+            elif ctx.needs_input_grad[0]:
+                dx = gemm(g, wbs[0], b_t=True).reshape(ctx.shape)
+        return (dx, None, *grads)
 
 
 _ACTS = {"relu": F.relu, "gelu": F.gelu, "sigmoid": torch.sigmoid, "tanh": torch.tanh,
@@ -121,6 +186,10 @@ class MLP(nn.Module):
         self.last_layer_use_activate = last_layer_use_activate
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if (self.activate is not None and str(self.activate).lower() == "relu" and self.layers
+                and all(layer.bias is not None and layer.tc_eligible(x) for layer in self.layers)):
+            params = [t for layer in self.layers for t in (layer.weight, layer.bias)]
+            return _TcReluMLPFn.apply(x, self.last_layer_use_activate, *params)
         act = get_activation(self.activate)
         for i, layer in enumerate(self.layers):
             x = layer(x)
@@ -193,6 +262,8 @@ class _GatedExperts(nn.Module):
 
     @staticmethod
     def _mix(layers, gate_logits):
+        if gate_logits.dim() == 2 and gate_logits.is_cuda and gate_logits.dtype == torch.bfloat16:
+            return gate_mix(gate_logits, list(layers))  # one fused kernel per direction
         stacked = torch.stack(layers, -1)                     # [B, D, E]
         gate = fp32_softmax(gate_logits, -1).unsqueeze(1)     # [B, 1, E]
         return fp32_sum(stacked * gate, dim=-1)

@@ -82,7 +82,7 @@ def test_window_equals_one_step_on_the_union(cuda, kind, micro, bwd_path):
         for name in ("state_row", "state_m", "state_v"):
             a, b = getattr(win, name), getattr(ref, name)
             if a is not None:
-                torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-8)
+                torch.testing.assert_close(a, b, rtol=1e-4, atol=1e-7)  # fp32 sums in another order
     assert win.step == ref.step == 2
 
 

@@ -1,0 +1,72 @@
+"""Fused multitask-layer kernels against plain PyTorch fp32: gate mixing (forward and backward),
+ReLU backward with bias-gradient column sums, and the one-node ReLU MLP on the tcgen05 GEMM."""
+import pytest
+import torch
+
+from flare_b200.models.layers import MLP
+from flare_b200.ops.mixing import gate_mix, gate_mix_supported, relu_bwd_colsum_
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("B,E,D", [(1, 3, 8), (37, 16, 64), (1000, 24, 128), (257, 64, 512), (64, 5, 1024)])
+def test_gate_mix_matches_fp32_autograd(cuda, B, E, D):
+    torch.manual_seed(B + E + D)
+    logits = (torch.randn(B, E, device=cuda) * 2).to(torch.bfloat16)
+    ys = [torch.randn(B, D, device=cuda).to(torch.bfloat16) for _ in range(E)]
+    assert gate_mix_supported(logits, ys)
+    lg = logits.detach().clone().requires_grad_(True)
+    yy = [y.detach().clone().requires_grad_(True) for y in ys]
+    out = gate_mix(lg, yy)
+    dout = torch.randn(B, D, device=cuda).to(torch.bfloat16)
+    out.backward(dout)
+
+    lr = logits.double().requires_grad_(True)
+    yr = [y.double().requires_grad_(True) for y in ys]
+    ref = (torch.stack(yr, -1) * torch.softmax(lr, -1).unsqueeze(1)).sum(-1)
+    ref.backward(dout.double())
+    torch.testing.assert_close(out.double(), ref, rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(lg.grad.double(), lr.grad, rtol=2e-2, atol=2e-2)
+    for a, b in zip(yy, yr):
+        torch.testing.assert_close(a.grad.double(), b.grad, rtol=1e-2, atol=1e-2)
+
+
+def test_relu_bwd_colsum(cuda):
+    torch.manual_seed(0)
+    g = torch.randn(1000, 136, device=cuda).to(torch.bfloat16)
+    h = torch.relu(torch.randn(1000, 136, device=cuda)).to(torch.bfloat16)
+    out = torch.empty_like(g)
+    cs = torch.full((136,), 0.5, device=cuda)
+    relu_bwd_colsum_(g, h, out, cs)
+    want = torch.where(h > 0, g, torch.zeros_like(g))
+    torch.testing.assert_close(out, want, rtol=0, atol=0)
+    torch.testing.assert_close(cs, 0.5 + want.float().sum(0), rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("last_act", [True, False])
+def test_relu_mlp_one_node_matches_fp32(cuda, last_act):
+    torch.manual_seed(1)
+    mlp = MLP(64, [128, 256, 32], activate="relu", last_layer_use_activate=last_act).to(cuda)
+    ref = [torch.nn.Linear(l.in_features, l.out_features).to(cuda).double() for l in mlp.layers]
+    with torch.no_grad():
+        for r, l in zip(ref, mlp.layers):
+            r.weight.copy_(l.weight.to(torch.bfloat16).double())
+            r.bias.copy_(l.bias.to(torch.bfloat16).double())
+    x = torch.randn(300, 64, device=cuda).to(torch.bfloat16).requires_grad_(True)
+    y = mlp(x)
+    assert y.grad_fn is not None and "TcReluMLP" in type(y.grad_fn).__name__
+    gy = torch.randn_like(y)
+    y.backward(gy)
+
+    xr = x.detach().double().requires_grad_(True)
+    h = xr
+    for i, r in enumerate(ref):
+        h = r(h)
+        if i < len(ref) - 1 or last_act:
+            h = torch.relu(h)
+    h.backward(gy.double())
+    torch.testing.assert_close(y.double(), h, rtol=3e-2, atol=3e-2)
+    torch.testing.assert_close(x.grad.double(), xr.grad, rtol=3e-2, atol=3e-2)
+    for r, l in zip(ref, mlp.layers):
+        torch.testing.assert_close(l.weight.grad.double(), r.weight.grad, rtol=3e-2, atol=5e-2)
+        torch.testing.assert_close(l.bias.grad.double(), r.bias.grad, rtol=3e-2, atol=5e-2)
