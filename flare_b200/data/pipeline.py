@@ -231,10 +231,31 @@ def encode_input(cfg: PipelineConfig, path: str, out: str, proc: FeatureProcesso
     return windows
 
 
+def code_digest() -> str:
+    """SHA-256 of the encoding code (this module and the ETL wrappers): every worker must run the same."""
+    import hashlib
+
+    h = hashlib.sha256()
+    for mod in (__file__, etl.__file__):
+        h.update(Path(mod).read_bytes())
+    return h.hexdigest()
+
+
 def encode_group(cfg: PipelineConfig, paths: list[str], out: str) -> list[tuple[str, list[dict]]]:
     """Worker process: encode a group of inputs (one feature processor for all)."""
     proc = FeatureProcessor(cfg)
     return [(p, encode_input(cfg, p, out, proc)) for p in paths]
+
+
+def encode_group_measured(cfg: PipelineConfig, paths: list[str], out: str) -> tuple[list, dict]:
+    """``encode_group`` plus the worker's wall / CPU seconds, peak RSS, host and code digest."""
+    import resource
+
+    t0, c0 = time.perf_counter(), time.process_time()
+    res = encode_group(cfg, paths, out)
+    return res, {"wall_seconds": time.perf_counter() - t0, "cpu_seconds": time.process_time() - c0,
+                 "max_rss_bytes": resource.getrusage(resource.RUSAGE_SELF).ru_maxrss * 1024,
+                 "node": socket.gethostname(), "code_sha256": code_digest()}
 
 
 def plan_groups(paths: list[str], workers: int) -> list[list[str]]:
@@ -337,8 +358,12 @@ class DataPipeline:
             gone.append(d.name)
         return gone
 
-    def run(self, workers: int = 1) -> dict:
-        """Publish every input not yet in the manifest; ``workers > 1`` encodes in parallel processes."""
+    def run(self, workers: int = 1, *, audit_path: str | Path | None = None) -> dict:
+        """Publish every input not yet in the manifest; ``workers > 1`` encodes in parallel processes.
+
+        With ``audit_path`` the parallel run writes an audit JSON: rows per input, the code digest (every
+        worker must report the same), worker nodes, summed wall / CPU seconds, peak worker RSS, groups
+        and part files (the reference's heap-stream audit, recipes/recsys/data/heap_stream.py:207-226)."""
         self.out.mkdir(parents=True, exist_ok=True)
         lease = Lease(self.out, self.cfg.lease_seconds)
         lease.acquire()
@@ -355,11 +380,31 @@ class DataPipeline:
             import multiprocessing as mp
 
             groups = plan_groups(todo, workers)
+            t0 = time.perf_counter()
+            expected, metrics, rows = code_digest(), [], {}
             with cf.ProcessPoolExecutor(max_workers=len(groups), mp_context=mp.get_context("spawn")) as ex:
-                futs = [ex.submit(encode_group, self.cfg, g, str(self.out)) for g in groups]
+                futs = [ex.submit(encode_group_measured, self.cfg, g, str(self.out)) for g in groups]
                 for fut in futs:  # commit in group order; each group's inputs in order
-                    for path, windows in fut.result():
+                    res, m = fut.result()
+                    if m["code_sha256"] != expected:
+                        raise RuntimeError("encoding code differs across workers")
+                    metrics.append(m)
+                    for path, windows in res:
+                        if path in rows:
+                            raise RuntimeError(f"input {path} encoded by two groups")
+                        rows[path] = sum(w["rows"] for w in windows)
                         self._commit(man, path, windows)
+            if set(rows) != set(todo):
+                raise RuntimeError("group coverage is incomplete")
+            if audit_path is not None:
+                write_json(audit_path, {
+                    "source_rows": rows, "execution_engine": "process_groups", "code_sha256": expected,
+                    "worker_nodes": sorted({m["node"] for m in metrics}), "total_rows": sum(rows.values()),
+                    "groups": len(groups), "worker_seconds": sum(m["wall_seconds"] for m in metrics),
+                    "worker_cpu_seconds": sum(m["cpu_seconds"] for m in metrics),
+                    "max_worker_rss_bytes": max(m["max_rss_bytes"] for m in metrics),
+                    "elapsed_before_commit": time.perf_counter() - t0,
+                    "data_files": sum(w["parts"] for w in man["windows"] if w["input"] in rows)})
             return man
         finally:
             lease.release()
@@ -381,5 +426,5 @@ class DataPipeline:
         return [str(self.out / w["dir"] / f"part-{i:05d}.parquet") for w in man["windows"] for i in range(w["parts"])]
 
 
-__all__ = ["DataPipeline", "DenseSpec", "FeatureProcessor", "Lease", "PipelineConfig", "SparseSpec", "encode_group",
-           "encode_input", "load_category_values", "plan_groups", "plan_workers", "read_chunks"]
+__all__ = ["DataPipeline", "DenseSpec", "FeatureProcessor", "Lease", "PipelineConfig", "SparseSpec", "code_digest",
+           "encode_group", "encode_group_measured", "encode_input", "load_category_values", "plan_groups", "plan_workers", "read_chunks"]

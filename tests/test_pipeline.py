@@ -108,8 +108,11 @@ def test_parallel_workers_and_planning(tmp_path):
     files = sorted(str(p) for p in (tmp_path / "logs").iterdir())
     groups = plan_groups(files, 2)
     assert sorted(f for g in groups for f in g) == files and len(groups) == 2
-    man = DataPipeline(_cfg(tmp_path)).run(workers=2)
+    man = DataPipeline(_cfg(tmp_path)).run(workers=2, audit_path=tmp_path / "audit.json")
     assert sum(w["rows"] for w in man["windows"]) == 550 and len(man["inputs_done"]) == 4
+    audit = json.loads((tmp_path / "audit.json").read_text())
+    assert audit["total_rows"] == 550 and audit["groups"] == 2 and sorted(audit["source_rows"]) == files
+    assert audit["data_files"] >= 4 and audit["max_worker_rss_bytes"] > 0 and len(audit["code_sha256"]) == 64
     assert plan_workers(cpus=64, memory_bytes=256 << 30, cpus_per_worker=4, memory_per_worker=8 << 30) == 15
     with pytest.raises(ValueError):
         plan_workers(cpus=4, memory_bytes=1 << 30, cpus_per_worker=8, memory_per_worker=1 << 20)
@@ -131,3 +134,20 @@ def test_zstd_inputs_encode_like_plain_ones(tmp_path):
         files = sorted((root / "out").rglob("*.parquet"))
         tabs.append(pa.concat_tables([pq.read_table(f) for f in files]))
     assert tabs[0].num_rows == tabs[1].num_rows == 230 and tabs[0].equals(tabs[1])
+
+
+def test_encode_batch_tuning():
+    from flare_b200.data.tuning import MIB, choose_encoded_batch, estimate_row_bytes
+
+    narrow = pa.schema([("label", pa.float32()), ("d0", pa.float32()), ("s0", pa.list_(pa.int32()))])
+    wide = pa.schema([(f"s{i}", pa.list_(pa.int64())) for i in range(600)])
+    assert estimate_row_bytes(narrow) < estimate_row_bytes(wide)
+    assert estimate_row_bytes(wide) >= 32 * 1024
+    t = choose_encoded_batch(narrow, worker_memory_bytes=4 << 30)
+    assert t.batch_bytes == 128 * MIB and t.rows_per_batch == 128 * MIB // t.row_bytes
+    assert choose_encoded_batch(wide, worker_memory_bytes=4 << 30).batch_bytes == 256 * MIB
+    # a smaller worker steps the automatic choice down; a supplied size is kept or refused
+    assert choose_encoded_batch(wide, worker_memory_bytes=512 * MIB).batch_bytes == 64 * MIB
+    assert choose_encoded_batch(narrow, worker_memory_bytes=4 << 30, supplied=32 * MIB).batch_bytes == 32 * MIB
+    with pytest.raises(ValueError, match="fits"):
+        choose_encoded_batch(narrow, worker_memory_bytes=64 * MIB)
