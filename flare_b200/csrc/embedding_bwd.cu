@@ -797,6 +797,120 @@ __global__ void __launch_bounds__(kHThreads, 3) emb_hash_light_kernel(EmbBwdPara
   }
 }
 
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned sa = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// 5b. The light-row pass for fp32 tables with the next batch's weight rows in flight: while a warp
+// reduces and applies batch t, cp.async copies the rows of its batch t + nwarps into shared memory
+// (two buffers per lane), so a warp keeps two batches of random row reads outstanding without the
+// registers of a second batch.  Every row appears in one record only, so reading a later batch's
+// rows early cannot race with an update.
+struct LightCur {
+  long long row;
+  int64_t eoff;
+  int hs, seg, c, ncols;
+  int rec_w;
+  float st_old;
+  bool mine, act, single;
+};
+
+template <typename TG, bool kScale>
+__global__ void __launch_bounds__(kHThreads, 3) emb_hash_light_pf_kernel(EmbBwdParams p, int GL) {
+  constexpr int NVL = 4;
+  __shared__ ShardDesc sd[kMaxShards];
+  __shared__ long long rb[kMaxShards];
+  __shared__ __align__(16) float4 wbuf[2][kHThreads][NVL];
+  for (int i = threadIdx.x; i < p.num_shards; i += blockDim.x) {
+    sd[i] = p.shards[i];
+    rb[i] = p.shards[i].row_base;
+  }
+  __syncthreads();
+  SparseOptParams o = p.opt;
+  resolve_sparse_step(o);
+  const int nsh = p.num_shards;
+  const bool row_state = o.state_row != nullptr && (o.kind == kOptRowwiseAdagrad || o.kind == kOptRowwiseAdam);
+  const TG* gbase = p.grad_direct ? reinterpret_cast<const TG*>(p.peer_grad[p.rank])
+                                  : reinterpret_cast<const TG*>(p.grad_stage);
+  float* const weights = reinterpret_cast<float*>(p.weights);
+  const int lane = lane_id();
+  const int gwarp = static_cast<int>((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
+  const int nwarps = static_cast<int>((static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5);
+  const int S = min(p.num_unique[4], static_cast<int>(p.max_occ));
+  const int N = min(S + p.num_unique[5], static_cast<int>(p.max_occ));
+  const int RPW = 32 / GL;
+  const int NB = (N + RPW - 1) / RPW;
+  const int g = lane / GL, gl = lane - g * GL;
+  const int leader = g * GL;
+  const int col = gl * 4 * NVL;
+
+  auto prepare = [&](int64_t t, LightCur& x, int buf) {
+    const int i = static_cast<int>(t) * RPW + g;
+    x.mine = i < N;
+    const int4 rec = x.mine ? light_rec(p, i, S) : make_int4(0, 0, 0, 0);
+    x.row = static_cast<unsigned>(rec.x);
+    x.hs = rec.y;
+    x.seg = rec.z;
+    x.rec_w = rec.w;
+    x.single = i < S;
+    x.c = x.mine ? (x.single ? 1 : rec.w) : 0;
+    const ShardDesc& d = sd[x.mine ? shard_of_row(rb, nsh, x.row) : 0];
+    x.ncols = d.ncols;
+    x.act = x.mine && col < d.ncols;
+    x.eoff = d.weight_off + (x.row - d.row_base) * d.ncols + col;
+    if (x.act) {
+#pragma unroll
+      for (int v = 0; v < NVL; ++v) cp_async16(&wbuf[buf][threadIdx.x][v], weights + x.eoff + 4 * v);
+    }
+    x.st_old = (row_state && x.mine && gl == 0) ? o.state_row[x.row] : -1.f;
+  };
+
+  int64_t t = gwarp;
+  if (t >= NB) return;
+  LightCur cur, nxt;
+  int buf = 0;
+  prepare(t, cur, 0);
+  cp_async_commit();
+  for (; t < NB; t += nwarps) {
+    const int64_t tn = t + nwarps;
+    if (tn < NB) prepare(tn, nxt, buf ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();  // this batch's rows (this lane's own copies) have landed
+    float4 wv[NVL], acc[NVL];
+#pragma unroll
+    for (int v = 0; v < NVL; ++v) {
+      wv[v] = cur.act ? wbuf[buf][threadIdx.x][v] : make_float4(0.f, 0.f, 0.f, 0.f);
+      acc[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (cur.act && cur.single) {
+      add_grad<TG, NVL, kScale>(gbase + cur.seg + col, acc, kScale ? __int_as_float(cur.rec_w) : 1.f);
+    } else if (cur.act) {
+      int k = 0;
+      for (; k + 2 <= cur.c; k += 2) {
+        const int g0 = p.occ[cur.seg + k], g1 = p.occ[cur.seg + k + 1];
+        const float s0 = kScale ? p.occ_scale[cur.seg + k] : 1.f, s1 = kScale ? p.occ_scale[cur.seg + k + 1] : 1.f;
+        add_grad<TG, NVL, kScale>(gbase + g0 + col, acc, s0);
+        add_grad<TG, NVL, kScale>(gbase + g1 + col, acc, s1);
+      }
+      if (k < cur.c)
+        add_grad<TG, NVL, kScale>(gbase + p.occ[cur.seg + k] + col, acc, kScale ? p.occ_scale[cur.seg + k] : 1.f);
+    }
+    apply_update<float, NVL>(o, weights + cur.eoff, cur.eoff, cur.row, cur.mine, cur.act, cur.ncols, acc, wv,
+                             cur.c, GL, leader, cur.st_old);
+    if (cur.mine && gl == 0) {
+      p.htab[cur.hs] = kHEmpty;
+      if (p.dirty != nullptr) p.dirty[cur.row] = 1;
+    }
+    cur = nxt;
+    buf ^= 1;
+  }
+  cp_async_wait<0>();
+}
+
 template <typename TW, typename TG, bool kScale>
 void hash_apply_launch(const EmbBwdParams& p, int ncols_max, int grid, cudaStream_t s) {
   // chunks: one 16-byte gradient load per lane (two for fp32 rows wider than 128 columns);
@@ -807,6 +921,12 @@ void hash_apply_launch(const EmbBwdParams& p, int ncols_max, int grid, cudaStrea
     emb_hash_chunk_kernel<TW, TG, 2, kScale><<<grid, kHThreads, 0, s>>>(p, ncols_max / 8);
   else
     emb_hash_chunk_kernel<TW, TG, kNvc, kScale><<<grid, kHThreads, 0, s>>>(p, ncols_max / (4 * kNvc));
+  if constexpr (std::is_same<TW, float>::value) {
+    if (p.light_prefetch) {
+      emb_hash_light_pf_kernel<TG, kScale><<<grid, kHThreads, 0, s>>>(p, GL);
+      return;
+    }
+  }
   emb_hash_light_kernel<TW, TG, 4, kScale><<<grid, kHThreads, 0, s>>>(p, GL);
 }
 
