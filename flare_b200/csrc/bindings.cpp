@@ -386,7 +386,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.block_counter = P<unsigned>(get_or<uintptr_t>(d, "block_counter", 0));
     p.status = P<int>(get_or<uintptr_t>(d, "status", 0));
     p.timeout_ns = get_or<uint64_t>(d, "timeout_ns", 2000000000ull);
-    p.light_prefetch = get_or<int>(d, "light_prefetch", 1);
+    p.light_prefetch = get_or<int>(d, "light_prefetch", 0);
     flare::emb_backward(p, get<int>(d, "ncols_max"), get<int>(d, "grid"), cur_stream());
   });
 

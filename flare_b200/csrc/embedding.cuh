@@ -183,7 +183,7 @@ struct EmbBwdParams {
   unsigned* block_counter;
   int* status;
   uint64_t timeout_ns;
-  int light_prefetch;  // fp32 tables: the light-row pass keeps the next batch's rows in flight (cp.async)
+  int light_prefetch;  // fp32 tables: the light-row pass keeps the next batch's rows in flight (cp.async; opt-in)
 };
 
 // Gradient-accumulation window: the staging of micro-step `micro` appended to the window's staging,

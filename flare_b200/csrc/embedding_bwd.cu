@@ -809,7 +809,9 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // reduces and applies batch t, cp.async copies the rows of its batch t + nwarps into shared memory
 // (two buffers per lane), so a warp keeps two batches of random row reads outstanding without the
 // registers of a second batch.  Every row appears in one record only, so reading a later batch's
-// rows early cannot race with an update.
+// rows early cannot race with an update.  Opt-in (FLARE_EMB_LIGHT_PREFETCH=1): on the 26-table
+// DLRM benchmark it measured 0.7 % slower per step than the register version (2.325 vs 2.309 ms),
+// which already keeps the DRAM random-read rate near its ceiling with 24 warps per SM.
 struct LightCur {
   long long row;
   int64_t eoff;

@@ -51,7 +51,7 @@ def test_training_reduces_loss_and_graph_matches_eager(cuda):
     # difference compounds while training overfits the four batches, so later steps get a looser bound
     # (a replay bug shows at once: the first replayed step is step 2)
     for i, (a, b) in enumerate(zip(eager, graph)):
-        tol = 1e-3 * max(1.0, abs(a)) if i < 16 else 3e-2 * abs(a) + 1e-3
+        tol = 3e-3 * max(1.0, abs(a)) if i < 16 else 3e-2 * abs(a) + 1e-3
         assert abs(a - b) <= tol, (i, a, b)
 
 
