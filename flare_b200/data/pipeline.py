@@ -91,6 +91,7 @@ class PipelineConfig:
     rows_per_file: int = 65536
     files_per_window: int = 4
     lease_seconds: float = 3600.0
+    iceberg_table: str | None = None   # also commit every input's windows to this Iceberg table
 
 
 # ------------------------------------------------------------------ reading
@@ -351,12 +352,54 @@ class DataPipeline:
         return read_json(p) if p.exists() else {"windows": [], "inputs_done": []}
 
     def reconcile(self) -> list[str]:
-        """Remove temporary windows of a crashed run; returns their names."""
+        """Remove temporary windows of a crashed run; returns their names.  With an Iceberg table, every
+        input already published gets its snapshot if the crash came between the two commits."""
         gone = []
         for d in self.out.glob(TMP_PREFIX + "*"):
             shutil.rmtree(d, ignore_errors=True)
             gone.append(d.name)
+        if self.cfg.iceberg_table:
+            man = self.manifest()
+            for path in man["inputs_done"]:
+                self._commit_iceberg(man, path)
         return gone
+
+    def _iceberg(self):
+        from .iceberg import IcebergTable
+
+        if getattr(self, "_ice", None) is None:
+            import pyarrow.parquet as pq
+
+            files = self.published_files()
+            if not files:
+                return None
+            schema = pq.read_schema(files[0])
+            self._ice = IcebergTable.create(self.cfg.iceberg_table, schema, exist_ok=True)
+        return self._ice
+
+    def _commit_iceberg(self, man: dict, path: str) -> None:
+        """One append snapshot per input, idempotent by the input's commit id."""
+        import hashlib
+
+        from .iceberg import DataFile
+
+        table = self._iceberg()
+        if table is None:
+            return
+        commit_id = "input:" + hashlib.sha256(path.encode()).hexdigest()[:32]
+        if table.refresh().find_commit(commit_id) is not None:
+            return
+        files = []
+        import pyarrow.parquet as pq
+
+        for w in man["windows"]:
+            if w["input"] != path:
+                continue
+            for i in range(w["parts"]):
+                f = self.out / w["dir"] / f"part-{i:05d}.parquet"
+                files.append(DataFile(str(f.absolute()), pq.ParquetFile(f).metadata.num_rows, f.stat().st_size))
+        if files:
+            table.append(files, commit_id=commit_id)
 
     def run(self, workers: int = 1, *, audit_path: str | Path | None = None) -> dict:
         """Publish every input not yet in the manifest; ``workers > 1`` encodes in parallel processes.
@@ -420,6 +463,8 @@ class DataPipeline:
             write_json(self.out / MANIFEST, man)
         man["inputs_done"].append(path)
         write_json(self.out / MANIFEST, man)
+        if self.cfg.iceberg_table:
+            self._commit_iceberg(man, path)
 
     def published_files(self) -> list[str]:
         man = self.manifest()

@@ -171,13 +171,24 @@ class ParquetSourceFactory:
 class StandardSourceFactory:
     """Factory selection by name with option validation."""
 
-    KINDS = ("parquet", "files")
+    KINDS = ("parquet", "files", "iceberg")
 
     @staticmethod
-    def create(kind: str, options: Mapping[str, Any]) -> ParquetSourceFactory:
+    def create(kind: str, options: Mapping[str, Any]):
         if kind not in StandardSourceFactory.KINDS:
             raise ValueError(f"unsupported source kind {kind!r}; expected one of {StandardSourceFactory.KINDS}")
         opts = dict(options)
+        if kind == "iceberg":
+            from .iceberg import IcebergSourceFactory
+
+            table = opts.pop("table", None)
+            if not table:
+                raise ValueError("source option 'table' is required for iceberg")
+            allowed = {"mode", "snapshot_id", "after_snapshot_id", "columns", "rows_per_item", "max_concurrency"}
+            unknown = set(opts) - allowed
+            if unknown:
+                raise ValueError(f"unknown source options {sorted(unknown)}")
+            return IcebergSourceFactory(table, **opts)
         paths = opts.pop("paths", None)
         if not paths:
             raise ValueError("source option 'paths' is required")
