@@ -387,6 +387,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.status = P<int>(get_or<uintptr_t>(d, "status", 0));
     p.timeout_ns = get_or<uint64_t>(d, "timeout_ns", 2000000000ull);
     p.light_prefetch = get_or<int>(d, "light_prefetch", 0);
+    p.chunk_variant = get_or<int>(d, "chunk_variant", 1);
     flare::emb_backward(p, get<int>(d, "ncols_max"), get<int>(d, "grid"), cur_stream());
   });
 
@@ -737,8 +738,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("colsum_bf16", [](uintptr_t x, int64_t rows, int cols, int64_t ldx, uintptr_t out) {
     flare::colsum_bf16(P<const __nv_bfloat16>(x), rows, cols, ldx, P<float>(out), cur_stream());
   });
-  m.def("cast_pad_bf16", [](uintptr_t x, int64_t rows, int cols, int64_t ldx, uintptr_t y, int ldy) {
-    flare::cast_pad_bf16(P<const float>(x), rows, cols, ldx, P<__nv_bfloat16>(y), ldy, cur_stream());
+  m.def("cast_pad_bf16", [](uintptr_t x, int64_t rows, int cols, int64_t ldx, uintptr_t y, int ldy, uintptr_t zero) {
+    flare::cast_pad_bf16(P<const float>(x), rows, cols, ldx, P<__nv_bfloat16>(y), ldy, cur_stream(), P<float>(zero));
   });
   m.def("init_uniform", [](uintptr_t out, int dtype, int64_t n, float lo, float hi, uint64_t seed, int64_t off,
                            int ncols, int dim, int col_begin, int64_t row_stride, int64_t row_first) {

@@ -707,7 +707,9 @@ __global__ void colsum_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows,
 }
 
 __global__ void cast_pad_kernel(const float* __restrict__ x, int64_t rows, int cols, int64_t ldx,
-                                __nv_bfloat16* __restrict__ y, int ldy) {
+                                __nv_bfloat16* __restrict__ y, int ldy, float* __restrict__ zero) {
+  // the step's first kernel also clears the step's loss accumulator (no separate fill launch)
+  if (zero != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *zero = 0.f;
   const int64_t n = rows * ldy;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -894,8 +896,8 @@ void colsum_bf16(const __nv_bfloat16* x, int64_t rows, int cols, int64_t ldx, fl
 }
 
 void cast_pad_bf16(const float* x, int64_t rows, int cols, int64_t ldx, __nv_bfloat16* y, int ldy,
-                   cudaStream_t s) {
-  cast_pad_kernel<<<grid_for(rows * ldy, 256), 256, 0, s>>>(x, rows, cols, ldx, y, ldy);
+                   cudaStream_t s, float* zero) {
+  cast_pad_kernel<<<grid_for(rows * ldy, 256), 256, 0, s>>>(x, rows, cols, ldx, y, ldy, zero);
   FLARE_CUDA_CHECK(cudaGetLastError());
   count_launch();
 }

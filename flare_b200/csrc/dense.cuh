@@ -93,7 +93,8 @@ void adam_flat(const AdamFlatParams& p, cudaStream_t s);
 void increment_counter(int* p, cudaStream_t s);
 void adam_dp_fused(const AdamDpParams& p, cudaStream_t s);
 void colsum_bf16(const __nv_bfloat16* x, int64_t rows, int cols, int64_t ldx, float* out, cudaStream_t s);
-void cast_pad_bf16(const float* x, int64_t rows, int cols, int64_t ldx, __nv_bfloat16* y, int ldy, cudaStream_t s);
+void cast_pad_bf16(const float* x, int64_t rows, int cols, int64_t ldx, __nv_bfloat16* y, int ldy, cudaStream_t s,
+                   float* zero = nullptr);
 void init_uniform(void* out, int dtype, int64_t n, float lo, float hi, uint64_t seed, int64_t index_offset,
                   int ncols, int dim, int col_begin, int64_t row_stride, int64_t row_first, cudaStream_t s);
 

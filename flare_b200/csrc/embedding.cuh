@@ -184,6 +184,7 @@ struct EmbBwdParams {
   int* status;
   uint64_t timeout_ns;
   int light_prefetch;  // fp32 tables: the light-row pass keeps the next batch's rows in flight (cp.async; opt-in)
+  int chunk_variant;   // chunk pass code variant (see hash_apply_launch; 1 by default)
 };
 
 // Gradient-accumulation window: the staging of micro-step `micro` appended to the window's staging,

@@ -210,12 +210,11 @@ class DLRM:
         dense gradients add up in the flat buffer and the pooled gradients in the window's micro-step
         slot."""
         self._flush_pipelined()
-        cast_pad_bf16(self.dense_in, self.xd)
+        cast_pad_bf16(self.dense_in, self.xd, zero=self.loss_sum)  # also clears the loss accumulator
         bot = self.bottom.forward(self.xd)
         pooled = self.emb.forward()
         interaction_forward(bot, pooled, self.F, self.inter, self.inter_status)
         h = self.top.forward(self.inter)
-        self.loss_sum.zero_()
         head_bce(h, self.head_w, self.head_b, self.labels, grad_scale=1.0 / self.global_B, logits=self.logits,
                  loss_sum=self.loss_sum, dh=self.dh, dw=self.head_dw, db=self.head_db)
         dinter = self.top.backward(self.dh, need_input_grad=True)
@@ -343,7 +342,7 @@ class DLRM:
         slot = self._next_slot
         pend = self.pending[0] if len(self.pending) == self.staleness else None
         comm.wait_stream(main)  # this step's inputs and the previous step's dense reads are ordered before
-        cast_pad_bf16(self.dense_in, self.xd)
+        cast_pad_bf16(self.dense_in, self.xd, zero=self.loss_sum)  # also clears the loss accumulator
         bot = self.bottom.forward(self.xd)
         with torch.cuda.stream(comm):
             pooled = self.emb.forward(slot=slot)
@@ -353,7 +352,6 @@ class DLRM:
         main.wait_event(self._ev_fwd)
         interaction_forward(bot, pooled, self.F, self.inter, self.inter_status)
         h = self.top.forward(self.inter)
-        self.loss_sum.zero_()
         head_bce(h, self.head_w, self.head_b, self.labels, grad_scale=1.0 / self.global_B, logits=self.logits,
                  loss_sum=self.loss_sum, dh=self.dh, dw=self.head_dw, db=self.head_db)
         dinter = self.top.backward(self.dh, need_input_grad=True)

@@ -154,13 +154,19 @@ def colsum_(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
     return out
 
 
-def cast_pad_bf16(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
-    """out[:, :k] = bf16(x); out[:, k:] = 0."""
+def cast_pad_bf16(x: torch.Tensor, out: torch.Tensor, *, zero: torch.Tensor | None = None) -> torch.Tensor:
+    """out[:, :k] = bf16(x); out[:, k:] = 0; ``zero`` (an fp32 scalar, e.g. a step's loss accumulator) is
+    cleared by the same launch."""
     if not on_cuda(x, out):
         out.zero_()
         out[:, : x.shape[1]] = x.to(out.dtype)
+        if zero is not None:
+            zero.zero_()
         return out
-    native().cast_pad_bf16(x.data_ptr(), x.shape[0], x.shape[1], x.stride(0), out.data_ptr(), out.stride(0))
+    if zero is not None and (zero.dtype != torch.float32 or not zero.is_cuda):
+        raise ValueError("zero must be a CUDA fp32 tensor")
+    native().cast_pad_bf16(x.data_ptr(), x.shape[0], x.shape[1], x.stride(0), out.data_ptr(), out.stride(0),
+                           zero.data_ptr() if zero is not None else 0)
     return out
 
 

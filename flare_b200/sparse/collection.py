@@ -548,6 +548,7 @@ class ShardedEmbeddingBagCollection:
             d.update(hash_mode=1, grad_direct=int(self.grad_direct), htab=self.htab.data_ptr(), hcap=h["hcap"],
                      hregion=h["hregion"], hprefetch=0 if os.environ.get("FLARE_EMB_HASH_PREFETCH") == "0" else 1,
                      light_prefetch=1 if os.environ.get("FLARE_EMB_LIGHT_PREFETCH") == "1" else 0,
+                     chunk_variant=int(os.environ.get("FLARE_EMB_CHUNK_VARIANT", "1")),
                      occ_h=self.flags_occ.data_ptr(),
                      occ_rank=self.stage_rank.data_ptr(), max_tiles=h["max_tiles"], max_chunks=h["max_chunks"],
                      max_parts=h["max_parts"],
