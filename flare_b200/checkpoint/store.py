@@ -144,12 +144,12 @@ def save_sparse(dirpath: Path, coll, step: int, *, mode: str = "full", base_step
         prefix = dirpath / _piece_name(s.spec.name, s.col_begin, s.row_index, s.row_shards)
         rows = None
         if mode == "incremental":
-            rows = torch.nonzero(coll.dirty[s.row_base:s.row_base + s.storage_rows]).flatten()
+            rows = coll.dirty_rows(s.row_base, s.storage_rows)
             np.save(f"{prefix}.rows.npy", rows.cpu().numpy().astype(np.int64))
         for field, t in fields.items():
             arr = t if rows is None else t.index_select(0, rows)
             np.save(f"{prefix}.{field}.npy", arr.float().cpu().numpy())
-    coll.dirty.zero_()
+    coll.clear_dirty()
     pieces = [{"table": s.spec.name, "col_begin": s.col_begin, "ncols": s.ncols, "rank": rank,
                "row_index": s.row_index, "row_shards": s.row_shards} for s in coll.shards]
     gathered = [pieces]
@@ -221,7 +221,7 @@ def load_sparse(root: str | os.PathLike, step: int, group: str, coll) -> dict:
     coll.load_local_state(state)
     coll.step = int(last["optimizer_step"])
     coll.step_dev.fill_(coll.step)
-    coll.dirty.zero_()
+    coll.clear_dirty()
     return last
 
 

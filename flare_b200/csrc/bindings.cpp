@@ -349,7 +349,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.heavy_acc = P<float>(get_or<uintptr_t>(d, "heavy_acc", 0));
     p.max_heavy = get_or<int>(d, "max_heavy", 0);
     p.light_max = get_or<int>(d, "light_max", 64);
-    p.dirty = P<uint8_t>(get_or<uintptr_t>(d, "dirty", 0));
+    p.dirty = P<unsigned>(get_or<uintptr_t>(d, "dirty", 0));
     p.max_occ = get<int64_t>(d, "max_occ");
     p.deterministic = get_or<int>(d, "deterministic", 0);
     p.det_first = P<int>(get_or<uintptr_t>(d, "det_first", 0));

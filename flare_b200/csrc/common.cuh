@@ -65,6 +65,12 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// Mark `row` dirty in a bitmap of 32 rows per word (the bitmap of a 200M-row collection is 25 MB and
+// stays in L2, where a byte per row would cost a DRAM sector read-modify-write per touched row).
+__device__ __forceinline__ void mark_dirty(unsigned* bits, long long row) {
+  if (bits != nullptr) atomicOr(bits + (row >> 5), 1u << (row & 31));
+}
+
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 

@@ -1037,7 +1037,7 @@ __global__ void __launch_bounds__(kEmbThreads, MINB) emb_apply_light_kernel(EmbB
     apply_update<TW, NV>(o, w, eoff, row, mine, act, d.ncols, acc, wv, c, G, leader);
     if (mine && gl == 0) {
       p.row_count[row] = 0;
-      if (p.dirty != nullptr) p.dirty[row] = 1;
+      mark_dirty(p.dirty, row);
     }
   }
 }
@@ -1210,7 +1210,7 @@ __global__ void __launch_bounds__(kEmbThreads) emb_heavy_apply_kernel(EmbBwdPara
     apply_update<TW, NV>(o, wp, eoff, row, true, act, d.ncols, acc, wv, p.cnt_u[u], 32, 0);
     if (lane == 0) {
       p.row_count[row] = 0;
-      if (p.dirty != nullptr) p.dirty[row] = 1;
+      mark_dirty(p.dirty, row);
     }
   }
 }

@@ -141,7 +141,7 @@ struct EmbBwdParams {
   float* heavy_acc; // [max_heavy + max_occ / 256 + 2][32*4*NV] fp32 partial sums per (heavy row, chunk)
   int max_heavy;
   int light_max;
-  uint8_t* dirty;   // per-row dirty flags for incremental checkpoints (nullable)
+  unsigned* dirty;  // per-row dirty bits for incremental checkpoints, 32 rows a word (nullable)
   int64_t max_occ;  // capacity of the per-unique arrays
   // deterministic-reduction mode: every row adds its occurrences in staging order (run-to-run
   // bitwise identical results); needs det_keys [2 * max_occ], det_vals [max_occ] and the sort's

@@ -742,7 +742,7 @@ __global__ void __launch_bounds__(kHThreads, 3) emb_hash_chunk_kernel(EmbBwdPara
         apply_update<TW, NVC>(o, w, eoff, row, true, own, d.ncols, acc, wv, c, LG, 0);
         if (lane == 0) {
           p.htab[hs] = kHEmpty;
-          if (p.dirty != nullptr) p.dirty[row] = 1;
+          mark_dirty(p.dirty, row);
           ++heavy_rows;
         }
       }
@@ -813,7 +813,7 @@ __global__ void __launch_bounds__(kHThreads, 3) emb_hash_light_kernel(EmbBwdPara
       apply_update<TW, NVL>(o, w, eoff, row, mine, act, d.ncols, acc, wv, c, GL, leader, st_old);
       if (mine && gl == 0) {
         p.htab[hs] = kHEmpty;
-        if (p.dirty != nullptr) p.dirty[row] = 1;
+        mark_dirty(p.dirty, row);
       }
   }
 }
@@ -926,7 +926,7 @@ __global__ void __launch_bounds__(kHThreads, 3) emb_hash_light_pf_kernel(EmbBwdP
                              cur.c, GL, leader, cur.st_old);
     if (cur.mine && gl == 0) {
       p.htab[cur.hs] = kHEmpty;
-      if (p.dirty != nullptr) p.dirty[cur.row] = 1;
+      mark_dirty(p.dirty, cur.row);
     }
     cur = nxt;
     buf ^= 1;

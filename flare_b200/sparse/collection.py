@@ -244,8 +244,8 @@ class ShardedEmbeddingBagCollection:
         self.lut = (torch.tensor(opt.custom_lut, dtype=torch.float32, device=dev)
                     if opt.dynamic_lr_policy == "custom_lut" else None)
 
-        # rows updated since the last checkpoint (incremental sparse saves)
-        self.dirty = torch.zeros(max(rbase, 4), dtype=torch.uint8, device=dev)
+        # rows updated since the last checkpoint (incremental sparse saves): one bit per local row
+        self.dirty_bits = torch.zeros(max((rbase + 31) // 32, 1), dtype=torch.int32, device=dev)
 
         # ---- staging ----
         ns = max(len(self.shards), 1)
@@ -536,7 +536,7 @@ class ShardedEmbeddingBagCollection:
             stage_cap=self.bwd_cap, weights=self.weights.data_ptr(), w_dtype=dtype_code(self.value_dtype),
             flags=self.flags_occ.data_ptr(), num_unique=self.num_unique.data_ptr(),
             seg_start=self.seg_start.data_ptr(), occ=self.occ.data_ptr(),
-            light_max=self.light_max, max_occ=self.max_occ, opt=op, dirty=self.dirty.data_ptr(),
+            light_max=self.light_max, max_occ=self.max_occ, opt=op, dirty=self.dirty_bits.data_ptr(),
             flags_local=self.flags.local_ptr, peer_flags=self.flags.peer_ptrs.data_ptr(),
             flag_in=self.flags.slots(FLAG_BWD_IN), epoch_ctr=self.flags.epoch_ptr(FLAG_BWD_IN),
             block_counter=self.flags.block_counter_ptr(FLAG_BWD_IN), status=self.status.ptr,
@@ -586,6 +586,28 @@ class ShardedEmbeddingBagCollection:
         if u > 0:
             h["hregion"] = min(self.hash_region_cap, 1 << max(12, int(u * 1.6 - 1).bit_length()))
         h["tuned"] = True
+
+    def dirty_rows(self, row_base: int, rows: int) -> torch.Tensor:
+        """Local row indices in [row_base, row_base + rows) updated since the last ``clear_dirty`` (relative
+        to ``row_base``, ascending)."""
+        if rows <= 0:
+            return torch.zeros(0, dtype=torch.int64, device=self.device)
+        w0, w1 = row_base // 32, (row_base + rows + 31) // 32
+        words = self.dirty_bits[w0:w1].to(torch.int64) & 0xFFFFFFFF
+        bits = (words.unsqueeze(1) >> torch.arange(32, device=words.device)) & 1
+        flags = bits.reshape(-1)[row_base - 32 * w0:row_base - 32 * w0 + rows]
+        return torch.nonzero(flags).flatten()
+
+    @property
+    def dirty(self) -> torch.Tensor:
+        """Per-row dirty flags (uint8, unpacked from the bitmap)."""
+        n = self.num_local_rows
+        out = torch.zeros(max(n, 4), dtype=torch.uint8, device=self.device)
+        out[self.dirty_rows(0, n)] = 1
+        return out
+
+    def clear_dirty(self) -> None:
+        self.dirty_bits.zero_()
 
     def check(self) -> None:
         self.status.check("sharded embedding")

@@ -68,6 +68,12 @@ class CpuTables:
     def shard_fields(self, i: int) -> dict[str, torch.Tensor]:
         return {"weight": self.w[i], "state_row": self.acc[i]}
 
+    def dirty_rows(self, row_base: int, rows: int) -> torch.Tensor:
+        return torch.nonzero(self.dirty[row_base:row_base + rows]).flatten()
+
+    def clear_dirty(self) -> None:
+        self.dirty.zero_()
+
     def load_local_state(self, state: dict) -> None:
         for i, s in enumerate(self.shards):
             st = state[(s.spec.name, s.col_begin, s.row_index)]

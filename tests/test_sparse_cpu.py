@@ -265,3 +265,26 @@ def test_exchange_bytes_account_for_the_pipelined_gradient_buffer():
     sync = ShardedEmbeddingBagCollection.exchange_bytes(tabs, 32, 4)
     piped = ShardedEmbeddingBagCollection.exchange_bytes(tabs, 32, 4, pipelined=True)
     assert piped - sync == 4 * 32 * (16 + 8)  # one more [B, total_dim] pooled-gradient buffer
+
+
+def test_dirty_row_bitmap_unpacking_without_cuda():
+    """Dirty rows live in a bitmap of 32 rows per int32 word (bit 31 included); ranges may start and
+    end inside a word."""
+    import torch
+
+    from flare_b200.sparse.collection import ShardedEmbeddingBagCollection
+
+    c = object.__new__(ShardedEmbeddingBagCollection)
+    c.device = torch.device("cpu")
+    c.num_local_rows = 100
+    c.dirty_bits = torch.zeros(4, dtype=torch.int32)
+    rows = [0, 5, 31, 32, 63, 64, 70, 99]
+    for r in rows:
+        w = int(c.dirty_bits[r // 32]) & 0xFFFFFFFF
+        w |= 1 << (r % 32)
+        c.dirty_bits[r // 32] = w - (1 << 32) if w >= 1 << 31 else w
+    assert c.dirty_rows(0, 100).tolist() == rows
+    assert c.dirty_rows(30, 40).tolist() == [1, 2, 33, 34]  # rows 31, 32, 63, 64 relative to 30
+    assert c.dirty.nonzero().flatten().tolist() == rows
+    c.clear_dirty()
+    assert c.dirty_rows(0, 100).numel() == 0
