@@ -188,24 +188,44 @@ __global__ void __launch_bounds__(kMixThreads) gate_mix_bwd_kernel(GateMixParams
   }
 }
 
-// block (32, 8): thread x covers 8 consecutive columns, rows strided over the y threads and gridDim.y
-__global__ void relu_bwd_colsum_kernel(const __nv_bfloat16* __restrict__ g, int64_t ldg,
-                                       const __nv_bfloat16* __restrict__ h, int64_t ldh, int64_t rows, int cols,
-                                       __nv_bfloat16* __restrict__ gout, int64_t ldo, float* __restrict__ colsum) {
-  __shared__ float part[8][32][9];
-  const int c8 = (blockIdx.x * 32 + threadIdx.x) * 8;
+// 256 threads per block: thread t covers column group t % ncg (8 consecutive columns) of rows
+// t / ncg, t / ncg + rpb, ... (rpb = 256 / ncg rows per block pass), four rows' loads issued before
+// their math; the block then sums each column group over its threads in shared memory and adds one
+// value per column to colsum.
+constexpr int kRbThreads = 256;
+constexpr int kRbMaxGroups = 64;  // cols <= 512
+
+__global__ void __launch_bounds__(kRbThreads) relu_bwd_colsum_kernel(
+    const __nv_bfloat16* __restrict__ g, int64_t ldg, const __nv_bfloat16* __restrict__ h, int64_t ldh,
+    int64_t rows, int ncg, __nv_bfloat16* __restrict__ gout, int64_t ldo, float* __restrict__ colsum) {
+  __shared__ float part[kRbThreads][9];
+  const int t = threadIdx.x;
+  const int rpb = kRbThreads / ncg;
+  const int cg = t % ncg, r0 = t / ncg;
+  const bool on = r0 < rpb;
+  const int c8 = cg * 8;
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  if (c8 < cols) {
-    for (int64_t r = static_cast<int64_t>(blockIdx.y) * 8 + threadIdx.y; r < rows;
-         r += static_cast<int64_t>(gridDim.y) * 8) {
-      float gv[8], hv[8];
-      bf16x8_to_f32(__ldg(reinterpret_cast<const int4*>(g + r * ldg + c8)), gv);
-      bf16x8_to_f32(__ldg(reinterpret_cast<const int4*>(h + r * ldh + c8)), hv);
+  const int64_t step = static_cast<int64_t>(gridDim.x) * rpb;
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * rpb + r0; on && base < rows; base += 4 * step) {
+    int4 gv[4], hv[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        gv[i] = hv[i] > 0.f ? gv[i] : 0.f;
+    for (int u = 0; u < 4; ++u) {
+      const int64_t r = base + u * step;
+      if (r < rows) {
+        gv[u] = __ldg(reinterpret_cast<const int4*>(g + r * ldg + c8));
+        hv[u] = __ldg(reinterpret_cast<const int4*>(h + r * ldh + c8));
       }
-      const int4 o = f32_to_bf16x8(gv);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t r = base + u * step;
+      if (r >= rows) break;
+      float gf[8], hf[8];
+      bf16x8_to_f32(gv[u], gf);
+      bf16x8_to_f32(hv[u], hf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) gf[i] = hf[i] > 0.f ? gf[i] : 0.f;
+      const int4 o = f32_to_bf16x8(gf);
       *reinterpret_cast<int4*>(gout + r * ldo + c8) = o;
       // the bias gradient sums the rounded values the next GEMM consumes
       float rv[8];
@@ -215,16 +235,15 @@ __global__ void relu_bwd_colsum_kernel(const __nv_bfloat16* __restrict__ g, int6
     }
   }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) part[threadIdx.y][threadIdx.x][i] = acc[i];
+  for (int i = 0; i < 8; ++i) part[t][i] = on ? acc[i] : 0.f;
   __syncthreads();
-  if (threadIdx.y == 0 && c8 < cols) {
+  if (t < ncg) {
+    float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int k = t; k < rpb * ncg; k += ncg)
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float s = 0.f;
+      for (int i = 0; i < 8; ++i) sum[i] += part[k][i];
 #pragma unroll
-      for (int y = 0; y < 8; ++y) s += part[y][threadIdx.x][i];
-      atomicAdd(colsum + c8 + i, s);
-    }
+    for (int i = 0; i < 8; ++i) atomicAdd(colsum + c8 + i, sum[i]);
   }
 }
 
@@ -291,11 +310,16 @@ void relu_bwd_colsum(const __nv_bfloat16* g, int64_t ldg, const __nv_bfloat16* h
                15) == 0,
               "relu_bwd_colsum: 16-byte aligned rows");
   if (rows == 0) return;
-  const int gx = ceil_div(cols / 8, 32);
-  const int gy = std::max(1, std::min<int>(ceil_div(rows, 64), std::max(1, 148 * 8 / gx)));
-  relu_bwd_colsum_kernel<<<dim3(gx, gy), dim3(32, 8), 0, s>>>(g, ldg, h, ldh, rows, cols, gout, ldo, colsum);
-  FLARE_CUDA_CHECK(cudaGetLastError());
-  count_launch();
+  // column groups of 8 in chunks of at most 64 groups (512 columns) per launch
+  for (int c0 = 0; c0 < cols; c0 += 8 * kRbMaxGroups) {
+    const int ncg = std::min(kRbMaxGroups, (cols - c0) / 8);
+    const int rpb = kRbThreads / ncg;
+    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((rows + rpb - 1) / rpb, 148 * 4)));
+    relu_bwd_colsum_kernel<<<grid, kRbThreads, 0, s>>>(g + c0, ldg, h + c0, ldh, rows, ncg, gout + c0, ldo,
+                                                      colsum + c0);
+    FLARE_CUDA_CHECK(cudaGetLastError());
+    count_launch();
+  }
 }
 
 }  // namespace flare

@@ -31,16 +31,17 @@ def test_gate_mix_matches_fp32_autograd(cuda, B, E, D):
         torch.testing.assert_close(a.grad.double(), b.grad, rtol=1e-2, atol=1e-2)
 
 
-def test_relu_bwd_colsum(cuda):
+@pytest.mark.parametrize("rows,cols", [(1000, 136), (4096, 128), (37, 8), (3000, 1040)])
+def test_relu_bwd_colsum(cuda, rows, cols):
     torch.manual_seed(0)
-    g = torch.randn(1000, 136, device=cuda).to(torch.bfloat16)
-    h = torch.relu(torch.randn(1000, 136, device=cuda)).to(torch.bfloat16)
+    g = torch.randn(rows, cols, device=cuda).to(torch.bfloat16)
+    h = torch.relu(torch.randn(rows, cols, device=cuda)).to(torch.bfloat16)
     out = torch.empty_like(g)
-    cs = torch.full((136,), 0.5, device=cuda)
+    cs = torch.full((cols,), 0.5, device=cuda)
     relu_bwd_colsum_(g, h, out, cs)
     want = torch.where(h > 0, g, torch.zeros_like(g))
     torch.testing.assert_close(out, want, rtol=0, atol=0)
-    torch.testing.assert_close(cs, 0.5 + want.float().sum(0), rtol=1e-5, atol=1e-4)
+    torch.testing.assert_close(cs, 0.5 + want.float().sum(0), rtol=1e-5, atol=1e-3)
 
 
 @pytest.mark.parametrize("last_act", [True, False])
