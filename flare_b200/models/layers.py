@@ -173,6 +173,76 @@ def get_activation(name: str | None):
         raise ValueError(f"unsupported activation: {name!r}") from exc
 
 
+def _stacked_view(params, attr: str | None, rows: int, cols: int) -> torch.Tensor | None:
+    """One [rows, cols] view over consecutive equal-shaped tensors (``p.data`` or ``p.<attr>``), or None when
+    they are not laid out back to back (flat-buffer parameters registered as a stack group are)."""
+    ts = [getattr(p, attr, None) if attr else p.data for p in params]
+    if any(t is None for t in ts):
+        return None
+    t0 = ts[0]
+    n = t0.numel()
+    es = t0.element_size()
+    for k, t in enumerate(ts):
+        if t.dtype != t0.dtype or t.numel() != n or not t.is_contiguous() or \
+                t.data_ptr() != t0.data_ptr() + k * n * es:
+            return None
+    return t0.as_strided((rows, cols), (cols, 1))
+
+
+class _StackedReluLinearFn(torch.autograd.Function):
+    """n single-layer experts on one input as one GEMM: y = x [W_0; ...; W_{n-1}]^T + [b_0; ...] (ReLU
+    optional), returned as n column views.  Experts whose parameters sit back to back in the flat fused
+    buffers (a stack group of ``FusedDenseParameters``) use those buffers directly: no weight copy in the
+    forward, and the weight / bias gradients land in the flat gradient buffer from the GEMM epilogue and
+    the ReLU-backward column sums."""
+
+    @staticmethod
+    def forward(ctx, x, last_relu, n, *params):
+        Ws, bs = params[:n], params[n:]
+        D, K = Ws[0].shape
+        x2 = x.reshape(-1, K).contiguous()
+        wc = _stacked_view(Ws, None, n * D, K)
+        if wc is None or wc.dtype != torch.bfloat16:
+            wc = torch.cat([w.to(torch.bfloat16) for w in Ws])
+        bc = _stacked_view(bs, None, 1, n * D)
+        bc = bc.reshape(-1) if bc is not None and bc.dtype == torch.bfloat16 else torch.cat(
+            [b.to(torch.bfloat16) for b in bs])
+        y = gemm(x2, wc, bias=bc, relu=bool(last_relu))
+        ctx.save_for_backward(x2, wc, y)
+        ctx.n, ctx.D, ctx.K, ctx.last_relu, ctx.shape = n, D, K, bool(last_relu), x.shape
+        ctx.params = params
+        return tuple(y[:, e * D:(e + 1) * D].reshape(*x.shape[:-1], D) for e in range(n))
+
+    @staticmethod
+    def backward(ctx, *gys):
+        x2, wc, y = ctx.saved_tensors
+        n, D, K = ctx.n, ctx.D, ctx.K
+        Ws, bs = ctx.params[:n], ctx.params[n:]
+        dev = y.device
+        g = torch.cat([(gy if gy is not None else torch.zeros(y.shape[0], D, device=dev)).reshape(-1, D)
+                       .to(torch.bfloat16) for gy in gys], 1)
+        dw = _stacked_view(Ws, "_flare_grad", n * D, K)
+        db = _stacked_view(bs, "_flare_grad", 1, n * D)
+        flat = dw is not None and db is not None
+        if not flat:
+            dw = torch.zeros(n * D, K, dtype=torch.float32, device=dev)
+            db = torch.zeros(n * D, dtype=torch.float32, device=dev)
+        db = db.reshape(-1)
+        if ctx.last_relu:
+            gm = torch.empty_like(g)
+            relu_bwd_colsum_(g, y, gm, db)
+            g = gm
+        else:
+            colsum_(g, db)
+        gemm(g, x2, a_t=True, b_t=True, out=dw, accumulate=True)
+        dx = gemm(g, wc, b_t=True).reshape(ctx.shape) if ctx.needs_input_grad[0] else None
+        if flat:
+            grads = [None] * (2 * n)
+        else:
+            grads = [dw[e * D:(e + 1) * D] for e in range(n)] + [db[e * D:(e + 1) * D] for e in range(n)]
+        return (dx, None, None, *grads)
+
+
 class MLP(nn.Module):
     def __init__(self, in_features: int, dims: Sequence[int], activate: str = "relu",
                  last_layer_use_activate: bool = True):
@@ -252,8 +322,34 @@ class _GatedExperts(nn.Module):
         self.num_experts, self.n_tasks, self.out_dim = num_experts, n_tasks, dims[-1]
         self.experts = nn.ModuleList(MLP(base_dim, dims, activate) for _ in range(n_tasks * num_experts))
         self.gate_layers = nn.ModuleList(TcLinear(gate_in_dim, g) for g in gate_sizes)
+        # single-layer ReLU experts are computed as one stacked GEMM per shared input; their weights
+        # and biases form stack groups, which FusedDenseParameters lays out back to back
+        self.stackable = len(dims) == 1 and str(activate).lower() == "relu" and dims[0] % 8 == 0 \
+            and base_dim % 8 == 0
+        if self.stackable:
+            gid = id(self)
+            for e, m in enumerate(self.experts):
+                m.layers[0].weight._flare_stack = (gid, "w", e)
+                m.layers[0].bias._flare_stack = (gid, "b", e)
 
     def _expert_outputs(self, base_layers):
+        x0 = base_layers[0]
+        if self.stackable and x0.is_cuda and x0.dtype == torch.bfloat16:
+            # consecutive input groups that share one tensor run as one GEMM
+            outs, i, t = [], 0, 0
+            while t < len(base_layers):
+                u = t
+                while u + 1 < len(base_layers) and base_layers[u + 1] is base_layers[t]:
+                    u += 1
+                ex = [self.experts[k].layers[0] for k in range(i, i + (u - t + 1) * self.num_experts)]
+                last = self.experts[i].last_layer_use_activate
+                ys = _StackedReluLinearFn.apply(base_layers[t], last, len(ex), *[l.weight for l in ex],
+                                                *[l.bias for l in ex])
+                for k in range(u - t + 1):
+                    outs.append(list(ys[k * self.num_experts:(k + 1) * self.num_experts]))
+                i += (u - t + 1) * self.num_experts
+                t = u + 1
+            return outs
         outs, i = [], 0
         for t in range(len(base_layers)):
             outs.append([self.experts[i + e](base_layers[t]) for e in range(self.num_experts)])

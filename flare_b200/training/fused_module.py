@@ -37,7 +37,7 @@ class FusedDenseParameters:
         self.names: list[str] = []
         params = FlatParams()
         self._params: list[nn.Parameter] = []
-        for name, p in module.named_parameters():
+        for name, p in _stack_grouped(module.named_parameters()):
             if not p.requires_grad:
                 continue
             params.register(name, tuple(p.shape))
@@ -86,6 +86,27 @@ class FusedDenseParameters:
         if list(st.get("names", self.names)) != self.names:
             raise ValueError("checkpoint parameters do not match this module")
         self.state.load_state_dict(st)
+
+
+def _stack_grouped(named):
+    """Parameters in module order, except that the members of a stack group (``p._flare_stack = (group,
+    kind, index)``, set by layers that run several equal-shaped parameters as one GEMM operand) are
+    registered back to back, in index order, where the group's first member appears."""
+    named = list(named)
+    groups: dict = {}
+    for n, p in named:
+        key = getattr(p, "_flare_stack", None)
+        if key is not None:
+            groups.setdefault(key[:2], []).append((key[2], n, p))
+    out, done = [], set()
+    for n, p in named:
+        key = getattr(p, "_flare_stack", None)
+        if key is None:
+            out.append((n, p))
+        elif key[:2] not in done:
+            done.add(key[:2])
+            out.extend((m, q) for _, m, q in sorted(groups[key[:2]], key=lambda t: t[0]))
+    return out
 
 
 def _accumulate_into_flat(p: torch.Tensor) -> None:

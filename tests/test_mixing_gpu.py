@@ -79,3 +79,42 @@ def test_relu_mlp_one_node_matches_fp32(cuda, last_act):
     for r, l in zip(ref, mlp.layers):
         close(l.weight.grad, r.weight.grad, 3e-2)
         close(l.bias.grad, r.bias.grad, 3e-2)
+
+
+@pytest.mark.parametrize("shared_input", [True, False])
+def test_ple_stacked_experts_match_fp64_eager(cuda, shared_input):
+    """PLE with single-layer ReLU experts: one stacked GEMM per shared input (+ fused gate mixing) on
+    bf16 CUDA inputs against the same module's eager path in fp64 on the CPU."""
+    import copy
+
+    from flare_b200.models.layers import PLE
+
+    torch.manual_seed(3)
+    ple = PLE(64, 64, 4, [32], 3).to(cuda)
+    assert ple.stackable
+    ref = copy.deepcopy(ple).cpu().double()
+    with torch.no_grad():
+        for p, q in zip(ple.parameters(), ref.parameters()):
+            q.copy_(p.to(torch.bfloat16).double())
+    xs = [torch.randn(200, 64, device=cuda).to(torch.bfloat16) for _ in range(3)]
+    if shared_input:
+        xs = [xs[0]] * 3
+    xs = [x.requires_grad_(True) if i == 0 else x for i, x in enumerate(xs)]
+    outs = ple(xs, xs[0])
+    gys = [torch.randn_like(o) for o in outs]
+    torch.autograd.backward(outs, gys)
+    xr = [x.detach().double().cpu().requires_grad_(True) for x in xs]
+    if shared_input:
+        xr = [xr[0]] * 3
+    outs_r = ref(xr, xr[0])
+    torch.autograd.backward(outs_r, [g.double().cpu() for g in gys])
+    for o, r in zip(outs, outs_r):
+        torch.testing.assert_close(o.double().cpu(), r, rtol=3e-2, atol=3e-2)
+
+    def close(a, b, tol=4e-2):
+        err = (a.double().cpu() - b).abs() - tol * (1 + b.abs())
+        assert (err > 0).double().mean() < 5e-3 and bool((err < 10 * tol * (1 + b.abs())).all()), err.max()
+
+    close(xs[0].grad, xr[0].grad)
+    for (n, p), (_, q) in zip(ple.named_parameters(), ref.named_parameters()):
+        close(p.grad, q.grad)
