@@ -314,7 +314,9 @@ void relu_bwd_colsum(const __nv_bfloat16* g, int64_t ldg, const __nv_bfloat16* h
   for (int c0 = 0; c0 < cols; c0 += 8 * kRbMaxGroups) {
     const int ncg = std::min(kRbMaxGroups, (cols - c0) / 8);
     const int rpb = kRbThreads / ncg;
-    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((rows + rpb - 1) / rpb, 148 * 4)));
+    // one block per SM at most: every block adds one value per column, and same-address float atomics
+    // serialise in L2 (592 blocks measured 49 us on 4096 x 512, dominated by the column atomics)
+    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((rows + rpb - 1) / rpb, 148)));
     relu_bwd_colsum_kernel<<<grid, kRbThreads, 0, s>>>(g + c0, ldg, h + c0, ldh, rows, ncg, gout + c0, ldo,
                                                       colsum + c0);
     FLARE_CUDA_CHECK(cudaGetLastError());
