@@ -43,3 +43,22 @@ def test_rank_loss_between_steps_is_detected_on_the_host(mode):
     assert "[rank0] RANK_LOSS_DETECTED ranks=[1] after step 3" in out, out[-4000:]
     assert "[rank1] leaving after step 3" in out, out[-4000:]
     assert "NO_DETECTION" not in out, out[-4000:]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_accumulation_windows_and_staleness_two_on_two_gpus():
+    import os
+    import socket
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=root)
+    cmd = ["timeout", "-k", "30", "400", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={port}",
+           "-m", "flare_b200.testing.dlrm_policy_dist_check"]
+    res = subprocess.run(cmd, cwd=root, env=env, capture_output=True, text=True, timeout=450)
+    assert res.returncode == 0 and "POLICY_DIST_OK" in res.stdout, (res.stdout + res.stderr)[-5000:]
