@@ -1,61 +1,15 @@
 """Run a function on N CPU ranks over gloo (multi-process tests without a GPU)."""
 from __future__ import annotations
 
-import io
-import os
-import socket
-import traceback
-
-import torch
-import torch.distributed as dist
-import torch.multiprocessing as mp
-
-
-def free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
-def _entry(rank, world, port, fn, args, queue):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
-                      LOCAL_RANK=str(rank))
-    try:
-        dist.init_process_group("gloo", rank=rank, world_size=world)
-        out = fn(rank, world, *args)
-        # results travel as bytes: a tensor put on the queue as is would be shared through a file
-        # descriptor that the parent can no longer fetch once this process has exited
-        buf = io.BytesIO()
-        torch.save(out, buf)
-        queue.put((rank, "ok", buf.getvalue()))
-    except BaseException:  # noqa: BLE001 - report any failure to the parent
-        queue.put((rank, "err", traceback.format_exc()))
-    finally:
-        if dist.is_initialized():
-            dist.destroy_process_group()
+from ..runtime.launch import RankFailure, free_port, spawn_ranks
 
 
 def run_ranks(fn, world: int, *args, timeout: float = 120.0):
     """Returns [result of rank 0, ..., rank world-1]; raises if any rank failed."""
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = free_port()
-    procs = [ctx.Process(target=_entry, args=(r, world, port, fn, args, q)) for r in range(world)]
-    for p in procs:
-        p.start()
-    results = {}
     try:
-        for _ in range(world):
-            rank, status, out = q.get(timeout=timeout)
-            if status != "ok":
-                raise RuntimeError(f"rank {rank} failed:\n{out}")
-            results[rank] = torch.load(io.BytesIO(out), weights_only=False)
-    finally:
-        for p in procs:
-            p.join(timeout=10)
-            if p.is_alive():
-                p.kill()
-    return [results[r] for r in range(world)]
+        return spawn_ranks(fn, world, *args, backend="gloo", timeout=timeout)
+    except RankFailure as e:
+        raise RuntimeError(str(e)) from e
 
 
 __all__ = ["free_port", "run_ranks"]
