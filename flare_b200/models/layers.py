@@ -182,9 +182,12 @@ def _stacked_view(params, attr: str | None, rows: int, cols: int) -> torch.Tenso
     t0 = ts[0]
     n = t0.numel()
     es = t0.element_size()
+    base = t0.untyped_storage()
+    if (t0.storage_offset() + rows * cols) * es > base.nbytes():
+        return None  # separate allocations that merely sit next to each other are not one buffer
     for k, t in enumerate(ts):
         if t.dtype != t0.dtype or t.numel() != n or not t.is_contiguous() or \
-                t.data_ptr() != t0.data_ptr() + k * n * es:
+                t.untyped_storage().data_ptr() != base.data_ptr() or t.data_ptr() != t0.data_ptr() + k * n * es:
             return None
     return t0.as_strided((rows, cols), (cols, 1))
 
