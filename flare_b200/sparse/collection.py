@@ -454,7 +454,7 @@ class ShardedEmbeddingBagCollection:
             Bl=self.B, F=self.F, peer_offsets=self._peer["offsets"].data_ptr(),
             peer_values=self._peer["values"].data_ptr(), peer_out=self._peer["out"].data_ptr(),
             out_stride=self.total_dim, weights=self.weights.data_ptr(), w_dtype=dtype_code(self.value_dtype),
-            out_dtype=dtype_code(self.out_dtype), vec=self.bulk_vec if self.bulk else self.vec,
+            out_dtype=dtype_code(self.out_dtype), vec=self.bulk_vec if self.bulk else self._fwd_vec(),
             bulk=1 if self.bulk else 0, stage_ids=st["ids"].data_ptr(),
             slot_map=self.slot_map.data_ptr() if self.slot_map is not None else 0,
             stage_bag=st["bag"].data_ptr(), stage_count=st["count"].data_ptr(),
@@ -487,6 +487,14 @@ class ShardedEmbeddingBagCollection:
                 micro=k, micro_steps=self.accum, stage_cap=self.stage_cap))
             self._micro, self.micro_filled = k, k + 1
         return self.pooled.local
+
+    def _fwd_vec(self) -> int:
+        """float4 vectors per lane in the forward: 1 for rows up to 128 columns (a warp per bag), 2 above;
+        FLARE_EMB_FWD_VEC=2 runs two bags per warp at 128 columns (16 lanes of 8 columns each)."""
+        v = int(os.environ.get("FLARE_EMB_FWD_VEC", "0"))
+        if v == 2 and all(sh.ncols % 8 == 0 and (sh.ncols // 8) & (sh.ncols // 8 - 1) == 0 for sh in self.shards):
+            return 2
+        return self.vec
 
     def backward(self, step: int | None = None, slot: int | None = None) -> None:
         """Consume the pooled gradients of staging ``slot`` (default: the last forward's) and update the owned shards.
