@@ -285,6 +285,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     p.block_counter = P<unsigned>(get_or<uintptr_t>(d, "block_counter", 0));
     p.status = P<int>(get_or<uintptr_t>(d, "status", 0));
     p.timeout_ns = get_or<uint64_t>(d, "timeout_ns", 2000000000ull);
+    p.fwd_minb = get_or<int>(d, "fwd_minb", 4);
     flare::emb_forward(p, get<int>(d, "grid"), cur_stream());
   });
 

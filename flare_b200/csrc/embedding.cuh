@@ -101,6 +101,7 @@ struct EmbFwdParams {
   unsigned* block_counter;
   int* status;
   uint64_t timeout_ns;
+  int fwd_minb;  // resident blocks per SM the forward is compiled for (3 or 4)
 };
 
 struct EmbBwdParams {

@@ -463,6 +463,7 @@ class ShardedEmbeddingBagCollection:
             flag_in=self.flags.slots(FLAG_FWD_IN), flag_out=self.flags.slots(FLAG_FWD_OUT),
             epoch_ctr=self.flags.epoch_ptr(FLAG_FWD_IN), block_counter=self.flags.block_counter_ptr(FLAG_FWD_IN),
             status=self.status.ptr, timeout_ns=self.timeout_ns, grid=self.grid,
+            fwd_minb=int(os.environ.get("FLARE_EMB_FWD_MINB", "4")),
         )
         if self.host_tier is not None:
             self.host_tier.prepare()
