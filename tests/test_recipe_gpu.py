@@ -130,3 +130,40 @@ def test_multitask_recipe_two_gpus_match_one_gpu_on_global_batch():
            "-m", "flare_b200.recipes.multitask_dist_check"]
     res = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=450)
     assert res.returncode == 0 and "RECIPE_DIST_OK" in res.stdout, (res.stdout + res.stderr)[-5000:]
+
+
+def test_user_model_accumulation_window_equals_the_union_step(cuda):
+    """A user model (multitask PLE) with 2-micro-step windows against the same model stepping once on
+    the union of the two micro-batches: equal losses window by window (SGD tables, Adam dense)."""
+    from flare_b200.sparse.config import SparseOptimizerConfig
+
+    builder = MultitaskModelBuilder(sparse_optimizer=SparseOptimizerConfig(kind="sgd", learning_rate=0.05))
+    B = 256
+    win = MultitaskRankingRecipe(name="mt", task_name="ranking", batch_size=B, builder=builder).trainer(
+        device=cuda, use_graph=True, seed=6, accumulation_steps=2)
+    one = MultitaskRankingRecipe(name="mt", task_name="ranking", batch_size=2 * B, builder=builder).trainer(
+        device=cuda, use_graph=True, seed=6)
+    F = len(builder.vocabs)
+
+    def union(a, b):
+        offs, vals, base = [0], [], 0
+        for f in range(F):
+            for x in (a, b):
+                seg = x[2][f * B:(f + 1) * B + 1].long()
+                vals.append(x[3][seg[0]:seg[-1]])
+                offs.extend((seg[1:] - seg[0] + base).tolist())
+                base += int(seg[-1] - seg[0])
+        return (torch.cat([a[0], b[0]]), torch.cat([a[1], b[1]]),
+                torch.tensor(offs, dtype=torch.int32, device=cuda), torch.cat(vals))
+
+    for w in range(6):
+        a, b = [synthetic_multitask_batch(B, builder.vocabs, builder.num_dense, builder.max_bag_size,
+                                          seed=500 + 2 * w + k, device=cuda) for k in range(2)]
+        la = win.train_step(*a).loss
+        lb = win.train_step(*b).loss
+        lu = one.train_step(*union(a, b)).loss
+        assert abs((la + lb) / 2 - lu) <= 0.02 * abs(lu) + 2e-3, (w, la, lb, lu)
+    assert win.coll.step == one.coll.step == 6 and win.coll.micro_filled == 0
+    assert len(win.graphs) == 2  # one graph per micro-step position
+    win.check()
+    one.check()
