@@ -3,7 +3,8 @@ another world size from the last committed checkpoint and ends in exactly the st
 changed world size at that checkpoint without failing."""
 import torch
 
-from flare_b200.runtime.elastic import elastic_cpu_worker, run_elastic
+from flare_b200.recipes.cpu_elastic import elastic_cpu_worker
+from flare_b200.runtime.elastic import run_elastic
 from flare_b200.runtime.launch import spawn_ranks
 
 
