@@ -128,6 +128,26 @@ __all__ = ["DLRMSyntheticData", "SCRAMBLE", "SmallSyntheticData", "SparseBatch",
            "make_jagged", "zipf_ids"]
 
 
+def synthetic_ranking_batch(B: int, vocabs, num_dense: int, max_bag: int, *, seed: int, device=None,
+                            n_labels: int = 3):
+    """(dense [B, num_dense], label ids [B], offsets, values) for a ranking model with multi-class labels.
+
+    Bags are U[1, max_bag] uniform ids of each vocabulary, feature-major (the keyed-jagged layout).  Label
+    id k is given to scores above the k-th of ``n_labels - 1`` thresholds spaced one unit apart (0 and 1
+    for three labels), so higher ids are rarer and predictable from the first dense features."""
+    g = torch.Generator().manual_seed(seed)
+    dense = torch.randn(B, num_dense, generator=g)
+    lens = torch.randint(1, max_bag + 1, (len(vocabs), B), generator=g)
+    vals = torch.cat([torch.randint(0, v, (int(lens[f].sum()),), generator=g) for f, v in enumerate(vocabs)])
+    offs = torch.cat([torch.zeros(1, dtype=torch.long), lens.reshape(-1).cumsum(0)]).int()
+    score = dense[:, 0] + 0.5 * dense[:, 1] + 0.3 * torch.randn(B, generator=g)
+    labels = torch.zeros(B, dtype=torch.long)
+    for k in range(1, n_labels):
+        labels += (score > float(k - 1)).long()
+    out = (dense, labels, offs, vals.int())
+    return tuple(t.to(device) for t in out) if device is not None else out
+
+
 @dataclass
 class SeqBatch:
     """Packed jagged sequences for the sequential model (one rank's share).

@@ -18,6 +18,7 @@ from dataclasses import dataclass, field
 import torch
 import torch.nn as nn
 
+from ..data.synthetic import synthetic_ranking_batch
 from ..models.layers import MLP, PLE
 from ..sparse.config import SparseOptimizerConfig, SparseTableSpec
 from .ranking import BaseRankingRecipe, MultiTargetCrossEntropyLoss, RankingTask
@@ -98,21 +99,21 @@ class MultitaskRankingRecipe(BaseRankingRecipe):
         return RankingTask(label_column="label", group_id_column="user_id", objective=multitask_objective())
 
 
-def synthetic_multitask_batch(B: int, vocabs, num_dense: int, max_bag: int, *, seed: int, device=None):
-    """(dense [B, num_dense], label ids [B], offsets, values) with labels that depend on the dense features."""
-    g = torch.Generator().manual_seed(seed)
-    dense = torch.randn(B, num_dense, generator=g)
-    lens = torch.randint(1, max_bag + 1, (len(vocabs), B), generator=g)
-    vals = torch.cat([torch.randint(0, v, (int(lens[f].sum()),), generator=g) for f, v in enumerate(vocabs)])
-    offs = torch.cat([torch.zeros(1, dtype=torch.long), lens.reshape(-1).cumsum(0)]).int()
-    score = dense[:, 0] + 0.5 * dense[:, 1] + 0.3 * torch.randn(B, generator=g)
-    labels = torch.where(score > 1.0, 2, torch.where(score > 0.0, 1, 0))
-    out = (dense, labels, offs, vals.int())
-    return tuple(t.to(device) for t in out) if device is not None else out
+def synthetic_multitask_batch(B: int, vocabs, num_dense: int, max_bag: int, *, seed: int, device=None,
+                              n_labels: int = 3):
+    """(dense, label ids, offsets, values) of ``data.synthetic.synthetic_ranking_batch`` (labels neg / click /
+    like by default)."""
+    return synthetic_ranking_batch(B, vocabs, num_dense, max_bag, seed=seed, device=device, n_labels=n_labels)
+
+
+def make_recipe(batch_size: int = 4096) -> MultitaskRankingRecipe:
+    """The multitask recipe with the default builder (the command line's ``--recipe`` factory)."""
+    return MultitaskRankingRecipe(name="multitask", task_name="ranking", batch_size=batch_size,
+                                  builder=MultitaskModelBuilder())
 
 
 __all__ = ["LogitHeads", "MultitaskModelBuilder", "MultitaskRankingModel", "MultitaskRankingRecipe",
-           "multitask_objective", "synthetic_multitask_batch"]
+           "make_recipe", "multitask_objective", "synthetic_multitask_batch"]
 
 
 def main(argv=None) -> int:

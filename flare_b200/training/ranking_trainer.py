@@ -193,12 +193,41 @@ class RankingModelTrainer:
         logits = self.module(self.x_dense, pooled, self.emb.split(pooled))
         return torch.sigmoid(logits.float())
 
+    # ------------------------------------------------------------ checkpoints
+    def checkpoint_parts(self) -> "_CheckpointParts":
+        """What ``checkpoint.store.CheckpointManager`` saves and restores: the flat dense state
+        (fp32 master, optimizer moments, step; parameters by name with their logical shapes) and the
+        sparse collection (FULL or INCREMENTAL)."""
+        return _CheckpointParts(self)
+
+    def save_checkpoint(self, manager, step: int, *, incremental: bool | None = None):
+        """Write ``step`` through ``manager``; an open accumulation window is applied first, so a
+        checkpoint is always cut at an optimizer boundary."""
+        torch.cuda.synchronize(self.device)
+        return manager.save(step, self.checkpoint_parts(), incremental=incremental)
+
+    def restore_checkpoint(self, manager, step: int | None = None) -> int:
+        """Load ``step`` (the newest committed one by default) in place: captured graphs stay valid."""
+        step = manager.restore(self.checkpoint_parts(), step)
+        torch.cuda.synchronize(self.device)
+        return step
+
     def check(self) -> None:
         self.coll.check()
 
     def close(self) -> None:
         self.finish_window()
         self.graphs.clear()
+
+
+class _CheckpointParts:
+    def __init__(self, trainer: RankingModelTrainer):
+        self._trainer = trainer
+        self.dense = trainer.dense.state
+        self.emb = trainer.coll
+
+    def flush_pending_updates(self) -> None:
+        self._trainer.finish_window()
 
 
 __all__ = ["RankingModelTrainer", "RankingStepResult"]

@@ -68,3 +68,40 @@ def test_ranking_phase_schedule_contract():
     assert ("update", "train_core", 1) in RANKING_PHASE_DEPENDENCIES
     with pytest.raises(ValueError):
         schedule_order(RANKING_PHASES, RANKING_PHASE_DEPENDENCIES + (("update", "train_core", 0),))
+
+
+def test_cli_loads_recipes_and_builds_their_batches():
+    import pytest
+    import torch
+
+    from flare_b200 import cli
+    from flare_b200.recipes.multitask import make_recipe
+    from flare_b200.recipes.ranking import BaseRankingRecipe
+
+    r = cli.load_recipe("flare_b200.recipes.multitask:make_recipe", 128)
+    assert isinstance(r, BaseRankingRecipe) and r.batch_size == 128
+    import sys
+    import types
+
+    fake = types.ModuleType("_fake_recipe_module")
+    fake.RECIPE = make_recipe(32)
+    sys.modules[fake.__name__] = fake
+    try:
+        inst = cli.load_recipe("_fake_recipe_module:RECIPE", 96)  # an instance: batch size replaced
+        assert inst.batch_size == 96 and fake.RECIPE.batch_size == 32
+    finally:
+        del sys.modules[fake.__name__]
+    args = cli._parser().parse_args(["recipe", "--recipe", "m:f", "--accumulation-steps", "2", "--resume"])
+    assert args.cmd == "recipe" and args.accumulation_steps == 2 and args.resume
+    with pytest.raises(SystemExit):
+        cli.load_recipe("flare_b200.recipes.multitask", 8)
+    with pytest.raises(SystemExit):
+        cli.load_recipe("flare_b200.recipes.multitask:multitask_objective", 8)  # not a recipe factory
+    b = make_recipe(64).model_builder()
+    dense, labels, offs, vals = cli.recipe_batch(b, 3, 64, 7, torch.device("cpu"))
+    F = len(b.vocabs)
+    assert dense.shape == (64, b.num_dense) and offs.shape == (F * 64 + 1,) and int(offs[-1]) == vals.numel()
+    assert int(labels.min()) >= 0 and int(labels.max()) <= 2
+    for f, v in enumerate(b.vocabs):
+        seg = vals[int(offs[f * 64]):int(offs[(f + 1) * 64])]
+        assert int(seg.max()) < v
