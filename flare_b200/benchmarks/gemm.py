@@ -1,6 +1,6 @@
 """GEMM throughput: tcgen05 tile GEMM, persistent tcgen05 GEMM, cuBLAS (torch.matmul).
 
-    python -m flare_b200.benchmarks.gemm [--shapes 8192x2048x6672,...] [--iters 20]
+    python -m flare_b200.benchmarks.gemm [--shapes 8192x2048x6672,...] [--iters 20] [--graph] [--bn 64,128]
 
 Each shape is M x N x K with C = A @ B^T, bf16 in, bf16 out.  Timed with CUDA
 events after warm-up; inputs are rotated over enough copies that the operands
@@ -29,14 +29,31 @@ class _Heap:
         return SymBuffer(t, 0, [t.data_ptr()])
 
 
-def _time(fn, iters):
+def _time(fn, iters, graph: bool = False):
+    """Mean ms per launch.  With ``graph`` the ``iters`` launches are captured in one CUDA graph and the
+    replay is timed, so host launch overhead (which exceeds a small GEMM's device time) is excluded."""
     for _ in range(3):
         fn(0)
     torch.cuda.synchronize()
+    g = None
+    if graph:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for i in range(iters):
+                    fn(i)
+        torch.cuda.current_stream().wait_stream(s)
+        g.replay()
+        torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for i in range(iters):
-        fn(i)
+    if g is not None:
+        g.replay()
+    else:
+        for i in range(iters):
+            fn(i)
     e1.record()
     torch.cuda.synchronize()
     return e0.elapsed_time(e1) / iters
@@ -46,6 +63,9 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--shapes", default="8192x2048x6672,8192x4096x2048,4096x512x6672,4096x6672x512,8192x8192x8192")
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--graph", action="store_true", help="time a CUDA graph of the launches (device time only)")
+    ap.add_argument("--bn", default="", help="also run the tile kernel at these tile widths, e.g. 64,128,256")
+    ap.add_argument("--no-persistent", action="store_true")
     args = ap.parse_args(argv)
     dev = torch.device("cuda", 0)
     ctx = DistGemmContext(_Heap(dev))
@@ -58,14 +78,16 @@ def main(argv=None):
         Cs = [torch.empty(M, N, device=dev, dtype=torch.bfloat16) for _ in range(copies)]
         dg = [DistGemm(ctx, As[i], Bs[i], Cs[i]) for i in range(copies)]
         flops = 2.0 * M * N * K
-        runs = {
-            "tcgen05_tile": lambda i: gemm(As[i % copies], Bs[i % copies], out=Cs[i % copies]),
-            "tcgen05_persistent": lambda i: dg[i % copies](),
-            "cublas": lambda i: torch.matmul(As[i % copies], Bs[i % copies].t(), out=Cs[i % copies]),
-        }
+        runs = {"tcgen05_tile": lambda i: gemm(As[i % copies], Bs[i % copies], out=Cs[i % copies])}
+        for bn in (int(x) for x in args.bn.split(",") if x):
+            runs[f"tcgen05_tile_bn{bn}"] = lambda i, bn=bn: gemm(As[i % copies], Bs[i % copies], out=Cs[i % copies],
+                                                                 bn=bn)
+        if not args.no_persistent:
+            runs["tcgen05_persistent"] = lambda i: dg[i % copies]()
+        runs["cublas"] = lambda i: torch.matmul(As[i % copies], Bs[i % copies].t(), out=Cs[i % copies])
         for name, fn in runs.items():
-            ms = _time(fn, args.iters)
-            print(json.dumps({"shape": shape, "kernel": name, "ms": round(ms, 4),
+            ms = _time(fn, args.iters, graph=args.graph)
+            print(json.dumps({"shape": shape, "kernel": name, "ms": round(ms, 4), "graph": args.graph,
                               "tflops": round(flops / ms / 1e9, 1)}), flush=True)
         ctx.check()
 
