@@ -1,6 +1,6 @@
 """GEMM throughput: tcgen05 tile GEMM, persistent tcgen05 GEMM, cuBLAS (torch.matmul).
 
-    python -m flare_b200.benchmarks.gemm [--shapes 8192x2048x6672,...] [--iters 20] [--graph] [--bn 64,128]
+    python -m flare_b200.benchmarks.gemm [--shapes 8192x2048x6672,...] [--iters 20] [--graph] [--bn 64,128] [--pair]
 
 Each shape is M x N x K with C = A @ B^T, bf16 in, bf16 out.  Timed with CUDA
 events after warm-up; inputs are rotated over enough copies that the operands
@@ -66,6 +66,7 @@ def main(argv=None):
     ap.add_argument("--graph", action="store_true", help="time a CUDA graph of the launches (device time only)")
     ap.add_argument("--bn", default="", help="also run the tile kernel at these tile widths, e.g. 64,128,256")
     ap.add_argument("--no-persistent", action="store_true")
+    ap.add_argument("--pair", action="store_true", help="also run CTA-pair (cta_group::2) tiles at widths 128 and 256")
     args = ap.parse_args(argv)
     dev = torch.device("cuda", 0)
     ctx = DistGemmContext(_Heap(dev))
@@ -82,6 +83,10 @@ def main(argv=None):
         for bn in (int(x) for x in args.bn.split(",") if x):
             runs[f"tcgen05_tile_bn{bn}"] = lambda i, bn=bn: gemm(As[i % copies], Bs[i % copies], out=Cs[i % copies],
                                                                  bn=bn)
+        if args.pair:
+            for bn in (128, 256):
+                runs[f"tcgen05_pair_bn{bn}"] = lambda i, bn=bn: gemm(As[i % copies], Bs[i % copies],
+                                                                     out=Cs[i % copies], bn=bn, pair=True)
         if not args.no_persistent:
             runs["tcgen05_persistent"] = lambda i: dg[i % copies]()
         runs["cublas"] = lambda i: torch.matmul(As[i % copies], Bs[i % copies].t(), out=Cs[i % copies])

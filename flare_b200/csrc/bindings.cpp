@@ -131,7 +131,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       "gemm",
       [](uintptr_t A, int64_t lda, bool a_mn, uintptr_t B, int64_t ldb, bool b_mn, int M, int N, int K, uintptr_t C,
          int64_t ldc, int c_dtype, bool accumulate, uintptr_t bias, int act, float alpha, uintptr_t mask,
-         int64_t ldm, uintptr_t colsum, uintptr_t status, uint64_t timeout_ns, int bn) {
+         int64_t ldm, uintptr_t colsum, uintptr_t status, uint64_t timeout_ns, int bn, int pair) {
         flare::GemmArgs a{};
         a.A = P<const void>(A);
         a.lda = lda;
@@ -154,12 +154,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         a.colsum = P<float>(colsum);
         a.status = P<int>(status);
         a.timeout_ns = timeout_ns;
+        a.pair = pair;
         flare::gemm_bf16_tcgen05(a, bn, cur_stream());
       },
       py::arg("A"), py::arg("lda"), py::arg("a_mn"), py::arg("B"), py::arg("ldb"), py::arg("b_mn"), py::arg("M"),
       py::arg("N"), py::arg("K"), py::arg("C"), py::arg("ldc"), py::arg("c_dtype"), py::arg("accumulate"),
       py::arg("bias"), py::arg("act"), py::arg("alpha"), py::arg("mask"), py::arg("ldm"), py::arg("colsum"),
-      py::arg("status"), py::arg("timeout_ns"), py::arg("bn") = 0);
+      py::arg("status"), py::arg("timeout_ns"), py::arg("bn") = 0, py::arg("pair") = -1);
 
   m.def("gemm_dist", [](const py::dict& d) {
     flare::DistGemmArgs a;

@@ -25,6 +25,7 @@ struct GemmArgs {
   float* colsum;  // fp32 [N]: += column sums of the result; or null
   int* status;
   uint64_t timeout_ns;
+  int pair = -1;  // CTA-pair (cta_group::2) tiles: 1 use, 0 never, -1 as FLARE_GEMM_PAIR says
 };
 
 void gemm_bf16_tcgen05(const GemmArgs& a, int bn_hint, cudaStream_t stream);

@@ -24,6 +24,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 namespace flare {
@@ -95,103 +96,11 @@ struct SmemLayout {
   static constexpr int kAlloc = kBytes + 1024;  // slack for manual 1 KiB alignment
 };
 
-template <int BN, int STAGES, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(kThreads, 1)
-    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                     EpiParams p) {
-  using L = SmemLayout<BN, STAGES>;
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw_addr = smem_u32(smem_raw);
-  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
-  uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* done_bar = empty_bar + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
-
-  const int warp = warp_id();
-  const int lane = lane_id();
-  const int m0 = blockIdx.x * kBM;
-  const int n0 = blockIdx.y * BN;
-  // split-K: this CTA owns k-tiles [kt_begin, kt_end)
-  const int kt_begin = static_cast<int>((static_cast<int64_t>(p.num_k_tiles) * blockIdx.z) / p.splits);
-  const int kt_end = static_cast<int>((static_cast<int64_t>(p.num_k_tiles) * (blockIdx.z + 1)) / p.splits);
-
-  if (threadIdx.x == 0) {
-    sm100::tma_prefetch_desc(&tmap_a);
-    sm100::tma_prefetch_desc(&tmap_b);
-    for (int s = 0; s < STAGES; ++s) {
-      sm100::mbar_init(&full_bar[s], 1);
-      sm100::mbar_init(&empty_bar[s], 1);
-    }
-    sm100::mbar_init(done_bar, 1);
-    sm100::fence_mbar_init();
-  }
-  if (warp == 0) {
-    sm100::tmem_alloc(tmem_slot, BN);
-    sm100::tmem_relinquish();
-  }
-  sm100::tc_fence_before();
-  __syncthreads();
-  sm100::tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-  const int KT = kt_end - kt_begin;
-
-  if (warp == 0 && lane == 0) {
-    // ------------------------------ producer ------------------------------
-    for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % STAGES;
-      if (kt >= STAGES) {
-        if (!sm100::mbar_wait(&empty_bar[s], ((kt / STAGES) - 1) & 1, p.timeout_ns, p.status, 100 + s)) break;
-      }
-      uint8_t* sa = smem + L::kOffA + s * kTileBytesA;
-      uint8_t* sb = smem + L::kOffB + s * L::kTileBytesB;
-      sm100::mbar_arrive_expect_tx(&full_bar[s], kTileBytesA + L::kTileBytesB);
-      const int k0 = (kt_begin + kt) * kBK;
-      if constexpr (!A_MN) {
-        sm100::tma_load_2d(sa, &tmap_a, &full_bar[s], k0, m0);
-      } else {
-#pragma unroll
-        for (int j = 0; j < kBM / 64; ++j) sm100::tma_load_2d(sa + j * 8192, &tmap_a, &full_bar[s], m0 + 64 * j, k0);
-      }
-      if constexpr (!B_MN) {
-        sm100::tma_load_2d(sb, &tmap_b, &full_bar[s], k0, n0);
-      } else {
-#pragma unroll
-        for (int j = 0; j < BN / 64; ++j) sm100::tma_load_2d(sb + j * 8192, &tmap_b, &full_bar[s], n0 + 64 * j, k0);
-      }
-    }
-  } else if (warp == 1 && lane == 0) {
-    // ------------------------------ MMA issuer ----------------------------
-    constexpr uint32_t idesc = sm100::make_idesc_bf16(kBM, BN, A_MN, B_MN);
-    bool ok = true;
-    for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % STAGES;
-      if (!sm100::mbar_wait(&full_bar[s], (kt / STAGES) & 1, p.timeout_ns, p.status, 200 + s)) {
-        ok = false;
-        break;
-      }
-      sm100::tc_fence_after();
-      const uint32_t sa = smem_u32(smem + L::kOffA + s * kTileBytesA);
-      const uint32_t sb = smem_u32(smem + L::kOffB + s * L::kTileBytesB);
-#pragma unroll
-      for (int k = 0; k < kBK / 16; ++k) {
-        // K-major: 16 bf16 = 32 bytes further along the swizzled 128-byte row.
-        // MN-major: 16 K-rows of 128 bytes further down the tile.
-        const uint64_t da = A_MN ? sm100::make_smem_desc(sa + k * 2048, 8192, 1024)
-                                 : sm100::make_smem_desc(sa + k * 32, 16, 1024);
-        const uint64_t db = B_MN ? sm100::make_smem_desc(sb + k * 2048, 8192, 1024)
-                                 : sm100::make_smem_desc(sb + k * 32, 16, 1024);
-        sm100::mma_f16_ss(tmem_base, da, db, idesc, (kt > 0 || k > 0) ? 1u : 0u);
-      }
-      sm100::mma_commit(&empty_bar[s]);
-    }
-    if (ok) sm100::mma_commit(done_bar);
-  }
-  __syncwarp();
-
-  // -------------------------------- epilogue --------------------------------
-  const bool done = sm100::mbar_wait(done_bar, 0, p.timeout_ns, p.status, 300);
-  sm100::tc_fence_after();
+// Epilogue of one 128 x BN accumulator tile in this CTA's TMEM: warp w owns
+// TMEM lanes (= output rows m0 + 32w ..) and walks the columns 32 at a time.
+template <int BN>
+__device__ __forceinline__ void epilogue_rows(const EpiParams& p, uint32_t tmem_base, int m0, int n0, int warp,
+                                              int lane, bool done) {
   const int row = m0 + warp * 32 + lane;
   const bool row_ok = row < p.M;
   if (done) {
@@ -295,23 +204,112 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                     EpiParams p) {
+  using L = SmemLayout<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* done_bar = empty_bar + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int m0 = blockIdx.x * kBM;
+  const int n0 = blockIdx.y * BN;
+  // split-K: this CTA owns k-tiles [kt_begin, kt_end)
+  const int kt_begin = static_cast<int>((static_cast<int64_t>(p.num_k_tiles) * blockIdx.z) / p.splits);
+  const int kt_end = static_cast<int>((static_cast<int64_t>(p.num_k_tiles) * (blockIdx.z + 1)) / p.splits);
+
+  if (threadIdx.x == 0) {
+    sm100::tma_prefetch_desc(&tmap_a);
+    sm100::tma_prefetch_desc(&tmap_b);
+    for (int s = 0; s < STAGES; ++s) {
+      sm100::mbar_init(&full_bar[s], 1);
+      sm100::mbar_init(&empty_bar[s], 1);
+    }
+    sm100::mbar_init(done_bar, 1);
+    sm100::fence_mbar_init();
+  }
+  if (warp == 0) {
+    sm100::tmem_alloc(tmem_slot, BN);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int KT = kt_end - kt_begin;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------ producer ------------------------------
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % STAGES;
+      if (kt >= STAGES) {
+        if (!sm100::mbar_wait(&empty_bar[s], ((kt / STAGES) - 1) & 1, p.timeout_ns, p.status, 100 + s)) break;
+      }
+      uint8_t* sa = smem + L::kOffA + s * kTileBytesA;
+      uint8_t* sb = smem + L::kOffB + s * L::kTileBytesB;
+      sm100::mbar_arrive_expect_tx(&full_bar[s], kTileBytesA + L::kTileBytesB);
+      const int k0 = (kt_begin + kt) * kBK;
+      if constexpr (!A_MN) {
+        sm100::tma_load_2d(sa, &tmap_a, &full_bar[s], k0, m0);
+      } else {
+#pragma unroll
+        for (int j = 0; j < kBM / 64; ++j) sm100::tma_load_2d(sa + j * 8192, &tmap_a, &full_bar[s], m0 + 64 * j, k0);
+      }
+      if constexpr (!B_MN) {
+        sm100::tma_load_2d(sb, &tmap_b, &full_bar[s], k0, n0);
+      } else {
+#pragma unroll
+        for (int j = 0; j < BN / 64; ++j) sm100::tma_load_2d(sb + j * 8192, &tmap_b, &full_bar[s], n0 + 64 * j, k0);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------ MMA issuer ----------------------------
+    constexpr uint32_t idesc = sm100::make_idesc_bf16(kBM, BN, A_MN, B_MN);
+    bool ok = true;
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % STAGES;
+      if (!sm100::mbar_wait(&full_bar[s], (kt / STAGES) & 1, p.timeout_ns, p.status, 200 + s)) {
+        ok = false;
+        break;
+      }
+      sm100::tc_fence_after();
+      const uint32_t sa = smem_u32(smem + L::kOffA + s * kTileBytesA);
+      const uint32_t sb = smem_u32(smem + L::kOffB + s * L::kTileBytesB);
+#pragma unroll
+      for (int k = 0; k < kBK / 16; ++k) {
+        // K-major: 16 bf16 = 32 bytes further along the swizzled 128-byte row.
+        // MN-major: 16 K-rows of 128 bytes further down the tile.
+        const uint64_t da = A_MN ? sm100::make_smem_desc(sa + k * 2048, 8192, 1024)
+                                 : sm100::make_smem_desc(sa + k * 32, 16, 1024);
+        const uint64_t db = B_MN ? sm100::make_smem_desc(sb + k * 2048, 8192, 1024)
+                                 : sm100::make_smem_desc(sb + k * 32, 16, 1024);
+        sm100::mma_f16_ss(tmem_base, da, db, idesc, (kt > 0 || k > 0) ? 1u : 0u);
+      }
+      sm100::mma_commit(&empty_bar[s]);
+    }
+    if (ok) sm100::mma_commit(done_bar);
+  }
+  __syncwarp();
+
+  // -------------------------------- epilogue --------------------------------
+  const bool done = sm100::mbar_wait(done_bar, 0, p.timeout_ns, p.status, 300);
+  sm100::tc_fence_after();
+  epilogue_rows<BN>(p, tmem_base, m0, n0, warp, lane, done);
   sm100::tc_fence_before();
   __syncthreads();
   if (warp == 0) sm100::tmem_dealloc(tmem_base, BN);
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN>
-void launch_cfg(const GemmArgs& a, int splits, cudaStream_t stream) {
-  using L = SmemLayout<BN, STAGES>;
-  auto kern = gemm_bf16_kernel<BN, STAGES, A_MN, B_MN>;
-  static bool attr_set = false;  // one per instantiation; set before first launch
-  if (!attr_set) {
-    FLARE_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc));
-    attr_set = true;
-  }
-  // A: K-major -> inner K, outer M, box rows 128; MN-major -> inner M, outer K, box 64 rows of K.
-  CUtensorMap ta = A_MN ? make_tmap_bf16(a.A, a.M, a.K, a.lda, kBK) : make_tmap_bf16(a.A, a.K, a.M, a.lda, kBM);
-  CUtensorMap tb = B_MN ? make_tmap_bf16(a.B, a.N, a.K, a.ldb, kBK) : make_tmap_bf16(a.B, a.K, a.N, a.ldb, BN);
+EpiParams epi_params(const GemmArgs& a, int splits) {
   EpiParams p;
   p.M = a.M;
   p.N = a.N;
@@ -329,10 +327,181 @@ void launch_cfg(const GemmArgs& a, int splits, cudaStream_t stream) {
   p.timeout_ns = a.timeout_ns;
   p.num_k_tiles = ceil_div(a.K, kBK);
   p.splits = splits;
+  return p;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+void launch_cfg(const GemmArgs& a, int splits, cudaStream_t stream) {
+  using L = SmemLayout<BN, STAGES>;
+  auto kern = gemm_bf16_kernel<BN, STAGES, A_MN, B_MN>;
+  static bool attr_set = false;  // one per instantiation; set before first launch
+  if (!attr_set) {
+    FLARE_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc));
+    attr_set = true;
+  }
+  // A: K-major -> inner K, outer M, box rows 128; MN-major -> inner M, outer K, box 64 rows of K.
+  CUtensorMap ta = A_MN ? make_tmap_bf16(a.A, a.M, a.K, a.lda, kBK) : make_tmap_bf16(a.A, a.K, a.M, a.lda, kBM);
+  CUtensorMap tb = B_MN ? make_tmap_bf16(a.B, a.N, a.K, a.ldb, kBK) : make_tmap_bf16(a.B, a.K, a.N, a.ldb, BN);
+  EpiParams p = epi_params(a, splits);
   dim3 grid(ceil_div(a.M, kBM), ceil_div(a.N, BN), splits);
   kern<<<grid, kThreads, L::kAlloc, stream>>>(ta, tb, p);
   FLARE_CUDA_CHECK(cudaGetLastError());
   count_launch();
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant (cta_group::2).  A cluster of two CTAs computes a 256 x BN
+// tile: CTA r stages rows [128r, 128r + 128) of the tile's A and rows
+// [r BN/2, (r+1) BN/2) of its B (32 KiB per 64-deep stage at BN = 256, against
+// 48 KiB for a 128 x 256 tile on one SM), so the same shared memory holds
+// STAGES = 6 stages in flight and each SM reads a third less per MMA cycle.
+// Both producers count their bytes on the even CTA's full barrier; the even
+// CTA's MMA warp issues the 256-row MMAs and commits to the empty / done
+// barriers of both CTAs (one commit per CTA, addressed through mapa); each CTA
+// runs the epilogue on its own 128 accumulator rows.  Every wait is bounded.
+template <int BN, int STAGES>
+struct PairLayout {
+  static constexpr int kTileBytesB = (BN / 2) * kBK * 2;
+  static constexpr int kStageBytes = kTileBytesA + kTileBytesB;
+  static constexpr int kOffB = STAGES * kTileBytesA;
+  static constexpr int kOffBar = kOffB + STAGES * kTileBytesB;
+  static constexpr int kBytes = kOffBar + (2 * STAGES + 1) * 8 + 16;
+  static constexpr int kAlloc = kBytes + 1024;
+};
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                          EpiParams p) {
+  using L = PairLayout<BN, STAGES>;
+  constexpr int kHalfN = BN / 2;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* done_bar = empty_bar + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const uint32_t rank = sm100::cluster_ctarank();
+  const bool leader = rank == 0;
+  const int m0 = blockIdx.x * kBM;                            // this CTA's 128 rows of the pair's 256
+  const int n0 = blockIdx.y * BN;                             // the pair's BN columns
+  const int nb0 = n0 + static_cast<int>(rank) * kHalfN;       // the B rows this CTA stages
+  const int kt_begin = static_cast<int>((static_cast<int64_t>(p.num_k_tiles) * blockIdx.z) / p.splits);
+  const int kt_end = static_cast<int>((static_cast<int64_t>(p.num_k_tiles) * (blockIdx.z + 1)) / p.splits);
+
+  if (threadIdx.x == 0) {
+    sm100::tma_prefetch_desc(&tmap_a);
+    sm100::tma_prefetch_desc(&tmap_b);
+    for (int s = 0; s < STAGES; ++s) {
+      sm100::mbar_init(&full_bar[s], 1);
+      sm100::mbar_init(&empty_bar[s], 1);
+    }
+    sm100::mbar_init(done_bar, 1);
+    sm100::fence_mbar_init();
+  }
+  if (warp == 0) {
+    sm100::tmem_alloc_pair(tmem_slot, BN);
+    sm100::tmem_relinquish_pair();
+  }
+  sm100::tc_fence_before();
+  sm100::cluster_sync();  // both CTAs: barriers initialised and TMEM allocated before any cross-CTA use
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int KT = kt_end - kt_begin;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------ producer (both CTAs) ------------------------------
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % STAGES;
+      if (kt >= STAGES) {
+        if (!sm100::mbar_wait(&empty_bar[s], ((kt / STAGES) - 1) & 1, p.timeout_ns, p.status, 100 + s)) break;
+      }
+      uint8_t* sa = smem + s * kTileBytesA;
+      uint8_t* sb = smem + L::kOffB + s * L::kTileBytesB;
+      if (leader) sm100::mbar_arrive_expect_tx(&full_bar[s], 2 * L::kStageBytes);
+      const uint32_t bar = sm100::mapa_shared(&full_bar[s], 0);
+      const int k0 = (kt_begin + kt) * kBK;
+      if constexpr (!A_MN) {
+        sm100::tma_load_2d_pair(sa, &tmap_a, bar, k0, m0);
+      } else {
+#pragma unroll
+        for (int j = 0; j < kBM / 64; ++j) sm100::tma_load_2d_pair(sa + j * 8192, &tmap_a, bar, m0 + 64 * j, k0);
+      }
+      if constexpr (!B_MN) {
+        sm100::tma_load_2d_pair(sb, &tmap_b, bar, k0, nb0);
+      } else {
+#pragma unroll
+        for (int j = 0; j < kHalfN / 64; ++j) sm100::tma_load_2d_pair(sb + j * 8192, &tmap_b, bar, nb0 + 64 * j, k0);
+      }
+    }
+  } else if (warp == 1 && lane == 0 && leader) {
+    // ------------------------------ MMA issuer (even CTA) ------------------------------
+    constexpr uint32_t idesc = sm100::make_idesc_bf16(2 * kBM, BN, A_MN, B_MN);
+    bool ok = true;
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % STAGES;
+      if (!sm100::mbar_wait(&full_bar[s], (kt / STAGES) & 1, p.timeout_ns, p.status, 200 + s)) {
+        ok = false;
+        break;
+      }
+      sm100::tc_fence_after();
+      const uint32_t sa = smem_u32(smem + s * kTileBytesA);
+      const uint32_t sb = smem_u32(smem + L::kOffB + s * L::kTileBytesB);
+#pragma unroll
+      for (int k = 0; k < kBK / 16; ++k) {
+        const uint64_t da = A_MN ? sm100::make_smem_desc(sa + k * 2048, 8192, 1024)
+                                 : sm100::make_smem_desc(sa + k * 32, 16, 1024);
+        const uint64_t db = B_MN ? sm100::make_smem_desc(sb + k * 2048, 8192, 1024)
+                                 : sm100::make_smem_desc(sb + k * 32, 16, 1024);
+        sm100::mma_f16_ss_pair(tmem_base, da, db, idesc, (kt > 0 || k > 0) ? 1u : 0u);
+      }
+      sm100::mma_commit_pair(sm100::mapa_shared(&empty_bar[s], 0));
+      sm100::mma_commit_pair(sm100::mapa_shared(&empty_bar[s], 1));
+    }
+    if (ok) {
+      sm100::mma_commit_pair(sm100::mapa_shared(done_bar, 0));
+      sm100::mma_commit_pair(sm100::mapa_shared(done_bar, 1));
+    }
+  }
+  __syncwarp();
+
+  const bool done = sm100::mbar_wait(done_bar, 0, p.timeout_ns, p.status, 300);
+  sm100::tc_fence_after();
+  epilogue_rows<BN>(p, tmem_base, m0, n0, warp, lane, done);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::cluster_sync();  // neither CTA frees the pair's TMEM while the other may still read it
+  if (warp == 0) sm100::tmem_dealloc_pair(tmem_base, BN);
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+void launch_pair_cfg(const GemmArgs& a, int splits, cudaStream_t stream) {
+  using L = PairLayout<BN, STAGES>;
+  auto kern = gemm_bf16_pair_kernel<BN, STAGES, A_MN, B_MN>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    FLARE_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc));
+    attr_set = true;
+  }
+  CUtensorMap ta = A_MN ? make_tmap_bf16(a.A, a.M, a.K, a.lda, kBK) : make_tmap_bf16(a.A, a.K, a.M, a.lda, kBM);
+  CUtensorMap tb = B_MN ? make_tmap_bf16(a.B, a.N, a.K, a.ldb, kBK) : make_tmap_bf16(a.B, a.K, a.N, a.ldb, BN / 2);
+  EpiParams p = epi_params(a, splits);
+  dim3 grid(2 * ceil_div(a.M, 2 * kBM), ceil_div(a.N, BN), splits);
+  kern<<<grid, kThreads, L::kAlloc, stream>>>(ta, tb, p);
+  FLARE_CUDA_CHECK(cudaGetLastError());
+  count_launch();
+}
+
+template <int BN, int STAGES>
+void launch_pair_majors(const GemmArgs& a, int splits, cudaStream_t s) {
+  if (!a.a_mn && !a.b_mn) launch_pair_cfg<BN, STAGES, false, false>(a, splits, s);
+  else if (!a.a_mn && a.b_mn) launch_pair_cfg<BN, STAGES, false, true>(a, splits, s);
+  else if (a.a_mn && !a.b_mn) launch_pair_cfg<BN, STAGES, true, false>(a, splits, s);
+  else launch_pair_cfg<BN, STAGES, true, true>(a, splits, s);
 }
 
 template <int BN, int STAGES>
@@ -354,6 +523,18 @@ int device_sm_count() {
     FLARE_CUDA_CHECK(cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev));
   }
   return count;
+}
+
+// CTA pairs are used for tiles of at least 256 rows and 128 columns when the
+// call asks for them (a.pair = 1) or, with a.pair = -1, when FLARE_GEMM_PAIR=1.
+static bool use_pair(const GemmArgs& a) {
+  static int env = -1;
+  if (env < 0) {
+    const char* v = std::getenv("FLARE_GEMM_PAIR");
+    env = (v != nullptr && v[0] == '1') ? 1 : 0;
+  }
+  const bool want = a.pair > 0 || (a.pair < 0 && env == 1);
+  return want && a.M >= 2 * kBM && a.N >= 128;
 }
 
 void gemm_bf16_tcgen05(const GemmArgs& a, int bn_hint, cudaStream_t stream) {
@@ -381,6 +562,17 @@ void gemm_bf16_tcgen05(const GemmArgs& a, int bn_hint, cudaStream_t stream) {
   // Split-K when the output tiles cannot fill the GPU and K is long (weight
   // gradients: K = batch).  Partials reduce into fp32 C, which therefore must
   // already hold the value to accumulate onto (accumulate semantics).
+  if (use_pair(a)) {
+    // CTA pairs: 256 x bn tiles, two SMs each.
+    const int pbn = (bn_hint == 128 || bn_hint == 256) ? bn_hint : (a.N > 128 ? 256 : 128);
+    const int ctas = 2 * ceil_div(a.M, 2 * kBM) * ceil_div(a.N, pbn);
+    int psplits = 1;
+    if (can_split && ctas < sms && kt >= 16)
+      psplits = std::min(std::min(kt / 8, 16), std::max(1, (2 * sms + ctas - 1) / ctas));
+    if (pbn == 256) launch_pair_majors<256, 6>(a, psplits, stream);
+    else launch_pair_majors<128, 8>(a, psplits, stream);
+    return;
+  }
   int splits = 1;
   const int tiles = ceil_div(a.M, kBM) * ceil_div(a.N, bn);
   if (can_split && tiles < sms && kt >= 16) {

@@ -10,6 +10,10 @@ result is zeroed where ``mask <= 0``, i.e. ReLU backward), ``colsum`` (fp32
 ``[N]`` accumulates the column sums of the result: bias gradient), and fp32
 output with ``accumulate`` (gradient accumulation).
 
+``pair=True`` runs tiles of at least 256 x 128 on CTA pairs (``cta_group::2``:
+two SMs share one 256-row MMA, each staging half of the operands), ``False``
+never, ``None`` as the ``FLARE_GEMM_PAIR`` environment variable says (``1``).
+
 CUDA tensors run the native kernel; CPU tensors run the fp32 reference below
 (also the oracle in the numerics tests).  The reference computes its dense
 layers through XLA/cuBLAS (src/flare/jax/layers/base.py:27 MLP).
@@ -62,6 +66,7 @@ def gemm(
     colsum: torch.Tensor | None = None,
     accumulate: bool = False,
     bn: int = 0,
+    pair: bool | None = None,
 ) -> torch.Tensor:
     M, K, lda = _logical(a, a_t)
     N, Kb, ldb = _logical(b, b_t)
@@ -104,7 +109,7 @@ def gemm(
         act=1 if relu else 0, alpha=float(alpha),
         mask=mask.data_ptr() if mask is not None else 0, ldm=mask.stride(0) if mask is not None else 0,
         colsum=colsum.data_ptr() if colsum is not None else 0,
-        status=st.ptr, timeout_ns=DEFAULT_TIMEOUT_NS, bn=bn,
+        status=st.ptr, timeout_ns=DEFAULT_TIMEOUT_NS, bn=bn, pair=-1 if pair is None else int(bool(pair)),
     )
     return out
 
