@@ -3,18 +3,22 @@
 ``spawn_ranks(fn, world, *args)`` starts ``world`` spawned processes, sets
 the rendezvous environment (127.0.0.1, a free port), initialises the
 process group with a timeout, runs ``fn(rank, world, *args)`` and returns
-the ranks' results in rank order.  A rank that raises makes the call raise
-``RankFailure`` naming the first failed rank and its traceback, after every
-process has ended (the survivors of a lost rank end when their next
-collective times out).  Results travel as ``torch.save`` bytes, so tensors
-do not depend on the sender process staying alive.
+the ranks' results in rank order.  A rank that raises, exits without
+reporting a result (killed, ``os._exit``) or reports nothing before
+``timeout`` makes the call raise ``RankFailure`` naming the first failed rank
+and its traceback (or exit code), after every process has ended (the
+survivors of a lost rank end when their next collective times out).
+Results travel as ``torch.save`` bytes, so tensors do not depend on the
+sender process staying alive.
 """
 from __future__ import annotations
 
 import datetime
 import io
 import os
+import queue
 import socket
+import time
 import traceback
 
 import torch
@@ -64,13 +68,43 @@ def spawn_ranks(fn, world: int, *args, backend: str = "gloo", timeout: float = 1
     for p in procs:
         p.start()
     results, failed = {}, {}
+    pending = set(range(world))
+
+    def take(item):
+        rank, status, out = item
+        pending.discard(rank)
+        if status == "ok":
+            results[rank] = torch.load(io.BytesIO(out), weights_only=False)
+        else:
+            failed[rank] = out
+
+    deadline = time.monotonic() + timeout
     try:
-        for _ in range(world):
-            rank, status, out = q.get(timeout=timeout)
-            if status == "ok":
-                results[rank] = torch.load(io.BytesIO(out), weights_only=False)
-            else:
-                failed[rank] = out
+        while pending:
+            left = deadline - time.monotonic()
+            if left <= 0:
+                for r in sorted(pending):
+                    failed[r] = f"no result within {timeout:.0f} s"
+                break
+            try:
+                take(q.get(timeout=min(1.0, left)))
+                continue
+            except queue.Empty:
+                pass
+            dead = [r for r in sorted(pending) if not procs[r].is_alive()]
+            if not dead:
+                continue
+            # a result is in the pipe before its process exits: drain, then whoever is still missing
+            # exited without reporting (killed, os._exit, a crash below Python)
+            while True:
+                try:
+                    take(q.get_nowait())
+                except queue.Empty:
+                    break
+            for r in dead:
+                if r in pending:
+                    pending.discard(r)
+                    failed[r] = f"exited with code {procs[r].exitcode} without reporting a result"
     finally:
         for p in procs:
             p.join(timeout=10)

@@ -12,4 +12,14 @@ def run_ranks(fn, world: int, *args, timeout: float = 120.0):
         raise RuntimeError(str(e)) from e
 
 
-__all__ = ["free_port", "run_ranks"]
+__all__ = ["exit_silently_worker", "free_port", "run_ranks"]
+
+
+def exit_silently_worker(rank: int, world: int, exit_rank: int = 1, code: int = 3):
+    """Rank ``exit_rank`` leaves with ``os._exit(code)`` (no exception, no result) while a world
+    larger than one; the others return their rank.  Host-side failure for the launcher tests."""
+    import os
+
+    if world > 1 and rank == exit_rank:
+        os._exit(code)
+    return rank

@@ -42,3 +42,22 @@ def test_elastic_restart_resumes_from_the_last_committed_checkpoint(tmp_path):
     _same(got["losses"], want["losses"])
     _same(got["sparse"]["tables"], want["sparse"]["tables"])
     _same(got["dense"], want["dense"])
+
+
+def test_a_rank_that_exits_without_a_result_is_a_rank_failure():
+    import pytest
+
+    from flare_b200.runtime.launch import RankFailure
+    from flare_b200.testing.gloo import exit_silently_worker
+
+    with pytest.raises(RankFailure) as e:
+        spawn_ranks(exit_silently_worker, 2, timeout=60.0)
+    assert e.value.rank == 1 and "exited with code 3" in e.value.detail and set(e.value.failed) == {1}
+
+
+def test_elastic_restart_after_a_silent_exit():
+    from flare_b200.testing.gloo import exit_silently_worker
+
+    res = run_elastic(exit_silently_worker, [2, 1], max_restarts=1, timeout=60.0)
+    assert [a.ok for a in res.attempts] == [False, True] and res.attempts[0].failed_rank == 1
+    assert res.results == [0]
