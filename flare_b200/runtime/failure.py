@@ -3,8 +3,9 @@
 * ``Heartbeat`` publishes ``(timestamp, step)`` for this rank into the
   torch.distributed key-value store from a background thread.
 * ``PeerWatchdog.check()`` reads every peer's heartbeat and raises
-  ``PeerFailure`` naming the ranks that are stale beyond ``timeout_s`` or that
-  published a failure marker; training loops call it between steps, before
+  ``PeerFailure`` naming the ranks that are stale beyond ``timeout_s``, that
+  never published, or that published a failure marker (without blocking on a
+  missing key); training loops call it between steps, before
   launching kernels that wait on peers, so a dead peer is found on the host
   instead of by a device wait running out.
 * Device waits are bounded (see csrc/common.cuh): a wait that runs out records
@@ -78,9 +79,13 @@ class PeerWatchdog:
         for r in range(self.world):
             if r == self.rank:
                 continue
+            # a store's get() waits for a missing key up to the store's own timeout (minutes for a
+            # TCPStore): ask whether it exists first, so a rank that never published is reported now
             try:
-                raw = self.store.get(_key(r)).decode()
-            except Exception:  # noqa: BLE001 - never published
+                raw = self.store.get(_key(r)).decode() if self.store.check([_key(r)]) else None
+            except Exception:  # noqa: BLE001 - store unreachable or key gone
+                raw = None
+            if raw is None:
                 stale.append(r)
                 continue
             ts, _, status = raw.split("|", 2)

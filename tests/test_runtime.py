@@ -103,3 +103,25 @@ def test_device_wait_times_out_and_context_survives(cuda):
     assert st["code"] == 2 and st["count"] == 1 and time.time() - t0 < 10
     x = torch.ones(1000, device=cuda)
     assert float((x * 2).sum()) == 2000.0  # the context is still usable
+
+
+def _never_published(rank, world):
+    store = dist.distributed_c10d._get_default_store()
+    hb = Heartbeat(store, rank, interval_s=0.1) if rank == 0 else None
+    dist.barrier()
+    if rank == 1:
+        return "never beat"
+    t0 = time.monotonic()
+    try:
+        PeerWatchdog(store, world, rank, timeout_s=30).check()
+    except PeerFailure as e:
+        return e.ranks, time.monotonic() - t0
+    finally:
+        hb.stop()
+    return "not detected"
+
+
+def test_watchdog_reports_a_rank_that_never_published_without_waiting():
+    out = run_ranks(_never_published, 2)
+    ranks, seconds = out[0]
+    assert ranks == [1] and seconds < 5.0 and out[1] == "never beat"
