@@ -60,9 +60,13 @@ class S3Options:
     def from_sources(cls, *, config_file: str | os.PathLike | None = None, environ: Mapping[str, str] | None = None,
                      **explicit: str | None) -> "S3Options":
         """Explicit values first, then the JSON file's keys, then ``AWS_*`` variables; empty values count as
-        unset.  Unknown keys (in ``explicit`` or the file) are an error."""
+        unset.  Unknown keys (in ``explicit`` or the file) are an error.  The access key, secret and session
+        token are one credential: all three come from the first layer that sets any of them, so a session
+        token from the environment is never attached to keys given explicitly or in the file."""
         names = {f.name for f in fields(cls)}
+        cred = ("access_key", "secret_key", "session_token")
         merged: dict[str, Any] = {}
+        cred_layer = None
         layers: list[Mapping[str, Any]] = [{k: v for k, v in explicit.items()}]
         if config_file is not None:
             p = Path(config_file)
@@ -75,7 +79,11 @@ class S3Options:
             unknown = sorted(set(layer) - names)
             if unknown:
                 raise ValueError(f"unknown S3 option keys: {unknown}")
+            if cred_layer is None and any(layer.get(k) not in (None, "") for k in cred):
+                cred_layer = layer
             for k, v in layer.items():
+                if k in cred and layer is not cred_layer:
+                    continue
                 if k not in merged and v not in (None, ""):
                     merged[k] = v
         # a profile from the environment yields to keys given explicitly or in the file

@@ -115,3 +115,13 @@ def test_transient_errors_are_retried_and_others_are_not():
     with pytest.raises(OSError, match="Denied"):
         ObjectStoreIO(filesystems={"s3": denied}, backoff_s=0.0).read_bytes("s3://b/k")
     assert denied.calls == 1
+
+
+def test_s3_credentials_come_from_one_layer():
+    from flare_b200.io.objectstore import S3Options
+
+    env = {"AWS_ACCESS_KEY_ID": "ENVKEY", "AWS_SECRET_ACCESS_KEY": "ENVSECRET", "AWS_SESSION_TOKEN": "ENVTOKEN"}
+    o = S3Options.from_sources(environ=env, access_key="a", secret_key="s")
+    assert (o.access_key, o.secret_key, o.session_token) == ("a", "s", None)
+    o = S3Options.from_sources(environ=env)
+    assert (o.access_key, o.secret_key, o.session_token) == ("ENVKEY", "ENVSECRET", "ENVTOKEN")
