@@ -41,6 +41,27 @@ def test_gemm_tile_widths_bf16_out(cuda, bn):
     torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize("bn", [64, 128, 256])
+def test_gemm_bf16_out_tails_strided_and_unaligned_bias(cuda, bn):
+    # row and column tails (a partial last 32-column chunk), an output wider than N, and a bias that
+    # starts one element into its buffer (not 16-byte aligned)
+    torch.manual_seed(4)
+    M, N, K = 300, 200, 320
+    a, b = _rand(M, K, device=cuda), _rand(N, K, device=cuda)
+    bias = (torch.randn(N + 1, device=cuda) * 0.1).to(torch.bfloat16)[1:]
+    out = torch.full((M, 216), 7.0, dtype=torch.bfloat16, device=cuda)
+    gemm(a, b, bias=bias, relu=True, out=out[:, :N], bn=bn)
+    ref = gemm_reference(a, b, bias=bias, relu=True)
+    torch.testing.assert_close(out[:, :N].float(), ref, rtol=2e-2, atol=2e-2)
+    assert bool((out[:, N:] == 7.0).all())  # nothing written past N
+    mask = _rand(M, N, device=cuda)
+    colsum = torch.zeros(N, device=cuda)
+    got = gemm(a, b, mask=mask, colsum=colsum, bn=bn)
+    want = gemm_reference(a, b, mask=mask)
+    torch.testing.assert_close(got.float(), want, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(colsum, want.sum(0), rtol=1e-2, atol=5e-2)
+
+
 def test_gemm_epilogue_mask_colsum_accumulate(cuda):
     torch.manual_seed(2)
     M, N, K = 384, 256, 192
