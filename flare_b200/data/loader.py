@@ -6,7 +6,9 @@ them (bounded depth).  With ``device`` set, a second stage copies each batch to
 the device on a dedicated CUDA stream ahead of use (the device-transfer stage
 that the reference's dataloader leaves as a stub,
 src/flare/data/pipeline/consumption/dataloader/device.py:8).  Iteration yields
-batches that are safe to consume on the current stream.
+batches that are safe to consume on the current stream.  ``close()`` (or
+leaving a ``with`` block) stops the worker when the consumer ends early, so
+the thread does not stay blocked on a full queue holding the source open.
 """
 from __future__ import annotations
 
@@ -31,20 +33,50 @@ class PrefetchLoader:
         self._device = device
         self._stream = torch.cuda.Stream(device=device) if device is not None and device.type == "cuda" else None
         self._error: BaseException | None = None
+        self._stop = threading.Event()
         self._thread = threading.Thread(target=self._work, daemon=True)
         self._thread.start()
+
+    def _put(self, item) -> bool:
+        """Queue ``item`` unless the loader is closed first (False then)."""
+        while not self._stop.is_set():
+            try:
+                self._q.put(item, timeout=0.05)
+                return True
+            except queue.Full:
+                continue
+        return False
 
     def _work(self) -> None:
         try:
             for raw in self._src:
+                if self._stop.is_set():
+                    return
                 b = self._transform(raw)
                 if self._pin:
                     b = b.pin_memory()
-                self._q.put(b)
+                if not self._put(b):
+                    return
         except BaseException as exc:  # noqa: BLE001 - surfaced on the consumer side
             self._error = exc
         finally:
-            self._q.put(_END)
+            self._put(_END)
+
+    def close(self, timeout: float = 5.0) -> None:
+        """Stop the worker and drop the batches it queued."""
+        self._stop.set()
+        while True:
+            try:
+                self._q.get_nowait()
+            except queue.Empty:
+                break
+        self._thread.join(timeout=timeout)
+
+    def __enter__(self) -> "PrefetchLoader":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
 
     def __iter__(self) -> Iterator[SparseBatch]:
         pending = None

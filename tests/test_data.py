@@ -77,3 +77,43 @@ def test_prefetch_loader_cpu():
 
     got = [int(b.values[0]) for b in PrefetchLoader(gen(), depth=2)]
     assert got == [0, 1, 2, 3, 4]
+
+
+def test_prefetch_loader_close_stops_the_worker_early():
+    import itertools
+    import time
+
+    import torch
+
+    made = []
+
+    def endless():
+        for i in itertools.count():
+            made.append(i)
+            yield SparseBatch(torch.zeros(1, 1), torch.zeros(1, 1), torch.tensor([0, 1], dtype=torch.int32),
+                              torch.tensor([i], dtype=torch.int32))
+
+    with PrefetchLoader(endless(), depth=2, pin_memory=False) as loader:
+        it = iter(loader)
+        assert [int(next(it).values[0]) for _ in range(3)] == [0, 1, 2]
+    t0 = time.monotonic()
+    loader._thread.join(timeout=2.0)
+    assert not loader._thread.is_alive() and time.monotonic() - t0 < 2.0
+    n = len(made)
+    time.sleep(0.2)
+    assert len(made) == n  # the source is no longer pulled
+
+
+def test_prefetch_loader_reports_a_source_error():
+    import pytest
+    import torch
+
+    def broken():
+        yield SparseBatch(torch.zeros(1, 1), torch.zeros(1, 1), torch.tensor([0, 1], dtype=torch.int32),
+                          torch.tensor([7], dtype=torch.int32))
+        raise RuntimeError("source failed")
+
+    it = iter(PrefetchLoader(broken(), depth=2, pin_memory=False))
+    assert int(next(it).values[0]) == 7
+    with pytest.raises(RuntimeError, match="source failed"):
+        next(it)
