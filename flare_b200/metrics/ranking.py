@@ -2,8 +2,11 @@
 
 Device path: ``auc_device`` sorts (score[, group]) keys with the framework's
 own stable radix sort and integrates the Mann-Whitney statistic on the GPU
-(csrc/metrics.cu).  Host path: the same statistic from average ranks
-(numpy), used as the oracle and on CPU.  Semantics follow the reference's
+(csrc/metrics.cu).  Host path (CPU tensors): the same statistic from average
+ranks, vectorised over every group at once (``auc_host`` / ``gauc_host``: one
+sort by (group, score), tie runs and group segments from boundary masks).
+``auc_reference`` / ``gauc_reference`` are the plain per-group oracles the
+tests compare both against.  Semantics follow the reference's
 exact AUC/GAUC (recipes/recsys/ranking/metrics/ray_data.py:242-554):
 
 * AUC = (sum over positives of [#neg below + 0.5 * #neg tied]) / (P * N);
@@ -75,10 +78,63 @@ class _AucWorkspace:
         return {k: v.data_ptr() for k, v in self.t.items()}
 
 
+def _grouped_rank_sums(s: np.ndarray, y: np.ndarray, g: np.ndarray):
+    """Per group (in ascending group order): positives, negatives and the sum of the positives'
+    average ranks among the group's scores (ties share the mean of their positions)."""
+    n = s.shape[0]
+    order = np.lexsort((s, g))
+    gs, ss, ys = g[order], s[order], y[order]
+    gnew = np.empty(n, dtype=bool)
+    gnew[0] = True
+    gnew[1:] = gs[1:] != gs[:-1]
+    gstart = np.flatnonzero(gnew)
+    pos = np.arange(n, dtype=np.int64) - gstart[np.cumsum(gnew) - 1]  # 0-based position in the group
+    tnew = gnew.copy()
+    tnew[1:] |= ss[1:] != ss[:-1]
+    tstart = np.flatnonzero(tnew)
+    tend = np.append(tstart[1:], n) - 1
+    run_rank = 0.5 * (pos[tstart] + pos[tend]).astype(np.float64) + 1.0
+    rank = run_rank[np.cumsum(tnew) - 1]
+    P = np.add.reduceat(ys.astype(np.int64), gstart)
+    N = np.diff(np.append(gstart, n)) - P
+    R = np.add.reduceat(np.where(ys, rank, 0.0), gstart)
+    return P, N, R
+
+
+def auc_host(scores, labels) -> float:
+    """Exact AUC on the host (numpy), vectorised; equal to ``auc_reference``."""
+    s = np.asarray(scores, dtype=np.float32).astype(np.float64).reshape(-1)
+    y = (np.asarray(labels).astype(np.float64) > 0.5).reshape(-1)
+    if s.size == 0:
+        return float("nan")
+    P, N, R = _grouped_rank_sums(s, y, np.zeros(s.size, dtype=np.int64))
+    if P[0] == 0 or N[0] == 0:
+        return float("nan")
+    return float((R[0] - P[0] * (P[0] + 1) / 2.0) / (float(P[0]) * float(N[0])))
+
+
+def gauc_host(scores, labels, groups, negative_factor: float = 0.0) -> float:
+    """Exact grouped AUC on the host (numpy), every group in one pass; equal to ``gauc_reference``."""
+    s = np.asarray(scores, dtype=np.float32).astype(np.float64).reshape(-1)
+    y = (np.asarray(labels).astype(np.float64) > 0.5).reshape(-1)
+    g = np.asarray(groups).astype(np.int64).reshape(-1)
+    if s.size == 0:
+        return float("nan")
+    P, N, R = _grouped_rank_sums(s, y, g)
+    ok = (P > 0) & (N > 0)
+    if not ok.any():
+        return float("nan")
+    Pf, Nf = P[ok].astype(np.float64), N[ok].astype(np.float64)
+    a = (R[ok] - Pf * (Pf + 1) / 2.0) / (Pf * Nf)
+    w = Pf + negative_factor * Nf
+    den = float(w.sum())
+    return float((a * w).sum() / den) if den else float("nan")
+
+
 def auc(scores: torch.Tensor, labels: torch.Tensor) -> float:
     """Exact AUC; runs on the GPU for CUDA tensors."""
     if not on_cuda(scores, labels):
-        return auc_reference(scores.detach().float().cpu().numpy(), labels.detach().cpu().numpy())
+        return auc_host(scores.detach().float().cpu().numpy(), labels.detach().cpu().numpy())
     s = scores.detach().reshape(-1).float().contiguous()
     y = labels.detach().reshape(-1).float().contiguous()
     n = s.numel()
@@ -94,8 +150,8 @@ def auc(scores: torch.Tensor, labels: torch.Tensor) -> float:
 def gauc(scores: torch.Tensor, labels: torch.Tensor, groups: torch.Tensor, negative_factor: float = 0.0) -> float:
     """Grouped AUC weighted by positives (+ negative_factor * negatives)."""
     if not on_cuda(scores, labels, groups):
-        return gauc_reference(scores.detach().float().cpu().numpy(), labels.detach().cpu().numpy(),
-                              groups.detach().cpu().numpy(), negative_factor)
+        return gauc_host(scores.detach().float().cpu().numpy(), labels.detach().cpu().numpy(),
+                         groups.detach().cpu().numpy(), negative_factor)
     s = scores.detach().reshape(-1).float().contiguous()
     y = labels.detach().reshape(-1).float().contiguous()
     g = groups.detach().reshape(-1).to(torch.int64).contiguous()
@@ -113,4 +169,4 @@ def calibration(predictions: torch.Tensor, labels: torch.Tensor) -> float:
     return p / y if y else float("nan")
 
 
-__all__ = ["auc", "auc_reference", "calibration", "gauc", "gauc_reference"]
+__all__ = ["auc", "auc_host", "auc_reference", "calibration", "gauc", "gauc_host", "gauc_reference"]

@@ -144,3 +144,25 @@ def test_background_windows_match_synchronous_and_stay_bounded():
     for a, b in zip(got, sync_out):
         assert a["train/auc_ctr"] == b["train/auc_ctr"] and a["train/loss"] == b["train/loss"]
     assert [s for s, _ in bg_sink.rows] == [s for s, _ in sync_sink.rows] == [3, 6, 9]
+
+
+def test_vectorised_host_auc_gauc_equal_the_per_group_oracles():
+    import numpy as np
+
+    from flare_b200.metrics.ranking import auc_host, gauc_host
+
+    rng = np.random.default_rng(5)
+    for n, groups, levels in ((1, 1, 3), (50, 7, 4), (5000, 300, 20), (20000, 5000, 1000)):
+        s = (rng.integers(0, levels, n) / levels).astype(np.float32)  # many ties
+        y = (rng.random(n) < 0.3).astype(np.float32)
+        g = rng.integers(0, groups, n) * 7 - 3  # negative and sparse group ids
+        assert np.isclose(auc_host(s, y), auc_reference(s, y), rtol=0, atol=1e-12, equal_nan=True)
+        for nf in (0.0, 0.5):
+            assert np.isclose(gauc_host(s, y, g, nf), gauc_reference(s, y, g, nf), rtol=0, atol=1e-12,
+                              equal_nan=True)
+    assert np.isnan(auc_host(np.zeros(4, np.float32), np.ones(4, np.float32)))
+    assert np.isnan(gauc_host(np.zeros(0, np.float32), np.zeros(0, np.float32), np.zeros(0, np.int64)))
+    # CPU tensors take the vectorised path
+    s, y, g = torch.rand(3000), (torch.rand(3000) < 0.4).float(), torch.randint(0, 50, (3000,))
+    assert abs(auc(s, y) - auc_reference(s.numpy(), y.numpy())) < 1e-12
+    assert abs(gauc(s, y, g, 0.25) - gauc_reference(s.numpy(), y.numpy(), g.numpy(), 0.25)) < 1e-12
