@@ -25,8 +25,9 @@ from .store import latest_step, step_dir
 FORMAT = "flare_b200.cpu.v1"
 
 
-def save_cpu(root: str | os.PathLike, step: int, engine, emb, *, group: str = "tables") -> Path:
-    """Write step ``step``: ``engine.capture_checkpoint_state()`` and ``emb.state_dict()``."""
+def save_cpu(root: str | os.PathLike, step: int, engine, emb, *, group: str = "tables", reader=None) -> Path:
+    """Write step ``step``: ``engine.capture_checkpoint_state()`` and ``emb.state_dict()``, and with
+    ``reader`` (a ``data.reader.BatchReader``) its cut position, committed by the same rename."""
     final = step_dir(root, step)
     tmp = final.with_name(f"{final.name}.partial")
     if tmp.exists():
@@ -43,14 +44,20 @@ def save_cpu(root: str | os.PathLike, step: int, engine, emb, *, group: str = "t
     (tmp / "sparse" / group / "manifest.json").write_text(json.dumps(
         {"format": FORMAT, "step": int(step), "optimizer_step": int(sparse["step"]),
          "tables": sorted(sparse["tables"]), "dynamic": sorted(sparse["dynamic"])}, indent=1))
+    if reader is not None:
+        from .source_cut import save_reader_cut
+
+        save_reader_cut(tmp, step, reader.capture_state())
     if final.exists():
         shutil.rmtree(final)
     os.replace(tmp, final)
     return final
 
 
-def restore_cpu(root: str | os.PathLike, engine, emb, step: int | None = None, *, group: str = "tables") -> int:
-    """Load step ``step`` (default: the latest complete one) into ``engine`` and ``emb``; returns it."""
+def restore_cpu(root: str | os.PathLike, engine, emb, step: int | None = None, *, group: str = "tables",
+                reader=None) -> int:
+    """Load step ``step`` (default: the latest complete one) into ``engine`` and ``emb`` (and ``reader``'s
+    cut position, when the step has one); returns it."""
     step = latest_step(root) if step is None else step
     if step is None:
         raise FileNotFoundError(f"no checkpoint under {root}")
@@ -61,6 +68,13 @@ def restore_cpu(root: str | os.PathLike, engine, emb, step: int | None = None, *
             raise ValueError(f"{part}: not a CPU-configuration checkpoint")
     engine.restore_checkpoint_state(torch.load(d / "model" / "state.pt", weights_only=False))
     emb.load_state_dict(torch.load(d / "sparse" / group / "state.pt", weights_only=False))
+    if reader is not None:
+        from .source_cut import load_reader_cut
+
+        states = load_reader_cut(d)
+        if not states:
+            raise ValueError(f"step {step} has no reader cut to restore")
+        reader.restore_state(states)
     return step
 
 

@@ -232,9 +232,12 @@ class CheckpointManager:
 
     root: str
 
-    def save(self, step: int, model, *, group: str = "tables", incremental: bool | None = None) -> Path:
+    def save(self, step: int, model, *, group: str = "tables", incremental: bool | None = None,
+             reader=None) -> Path:
         """Write ``steps/<step>`` for every rank's part of ``model``.  A sparse update the model still
-        holds back (pipelined policy) is applied first, so the saved tables include every step."""
+        holds back (pipelined policy) is applied first, so the saved tables include every step.  With
+        ``reader`` (this rank's ``data.reader.BatchReader``) its cut position goes into
+        ``reader/rank<k>.json`` of the same step, committed together with the model."""
         flush = getattr(model, "flush_pending_updates", None)
         if flush is not None:
             flush()
@@ -250,6 +253,10 @@ class CheckpointManager:
         mode = "incremental" if (incremental and prev is not None) else "full"
         save_dense(tmp / "model", model.dense, step)
         save_sparse(tmp / "sparse" / group, model.emb, step, mode=mode, base_step=prev if mode == "incremental" else None)
+        if reader is not None:
+            from .source_cut import save_reader_cut
+
+            save_reader_cut(tmp, step, reader.capture_state())
         _barrier()
         if rank == 0:
             if final.exists():
@@ -258,7 +265,7 @@ class CheckpointManager:
         _barrier()
         return final
 
-    def restore(self, model, step: int | None = None, *, group: str = "tables") -> int:
+    def restore(self, model, step: int | None = None, *, group: str = "tables", reader=None) -> int:
         step = latest_step(self.root) if step is None else step
         if step is None:
             raise FileNotFoundError(f"no checkpoint under {self.root}")
@@ -267,6 +274,13 @@ class CheckpointManager:
             flush()  # a pending update belongs to the state being replaced
         load_dense(step_dir(self.root, step) / "model", model.dense)
         load_sparse(self.root, step, group, model.emb)
+        if reader is not None:  # every saved rank's cut; the remaining items are dealt to this run's ranks
+            from .source_cut import load_reader_cut
+
+            states = load_reader_cut(step_dir(self.root, step))
+            if not states:
+                raise ValueError(f"step {step} has no reader cut to restore")
+            reader.restore_state(states)
         return step
 
 
