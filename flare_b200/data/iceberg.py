@@ -444,11 +444,21 @@ class IcebergTable:
 
 # ------------------------------------------------------------- sink and source
 class IcebergSink:
-    """Writes Arrow tables as Parquet data files of a table and commits them as append snapshots."""
+    """Writes Arrow tables as Parquet data files of a table and commits them as append snapshots.
+
+    The Parquet codec is the table's ``write.parquet.compression-codec`` property (Iceberg's table
+    property for it), zstd when the table does not set one, as Iceberg's own writers default to."""
+
+    CODEC_PROPERTY = "write.parquet.compression-codec"
 
     def __init__(self, table: IcebergTable, *, row_group_size: int = 64 * 1024):
         self.table = table
         self.row_group_size = row_group_size
+
+    @property
+    def codec(self) -> str:
+        props = (self.table.meta or {}).get("properties", {})
+        return str(props.get(self.CODEC_PROPERTY, "zstd")).lower()
 
     def write_files(self, tables: Iterable[pa.Table]) -> list[DataFile]:
         out = []
@@ -462,7 +472,8 @@ class IcebergSink:
             if self.table._local:
                 Path(inner).parent.mkdir(parents=True, exist_ok=True)
             with fs.open_output_stream(inner) as f:
-                pq.write_table(t, f, row_group_size=self.row_group_size)
+                pq.write_table(t, f, row_group_size=self.row_group_size,
+                               compression=None if self.codec == "uncompressed" else self.codec)
             size = fs.get_file_info(inner).size
             out.append(DataFile(path, t.num_rows, int(size)))
         return out

@@ -20,8 +20,12 @@ def test_schema_and_rows_of_a_published_table(tmp_path, capsys):
     assert validate_physical_schema(t, ["a", "b", "_ds"]) == {"files": 2, "columns": 3, "codec": None}
     with pytest.raises(AssertionError, match=r"missing=\['c'\] unexpected=\['_ds'\]"):
         validate_physical_schema(t, ["a", "b", "c"])
-    with pytest.raises(AssertionError, match="ZSTD"):
-        validate_physical_schema(t, ["a", "b", "_ds"], codec="zstd")  # the sink's default codec is not zstd
+    assert validate_physical_schema(t, ["a", "b", "_ds"], codec="zstd")["codec"] == "ZSTD"  # the sink's default
+    snappy = IcebergTable.create(str(tmp_path / "s"), pa.schema([("a", pa.int64())]),
+                                 properties={"write.parquet.compression-codec": "snappy"})
+    IcebergSink(snappy).append([pa.table({"a": [1, 2, 3]})])
+    with pytest.raises(AssertionError, match=r"only ZSTD compression.*SNAPPY"):
+        validate_physical_schema(snappy.refresh(), ["a"], codec="zstd")
     assert validate_rows(t, 100) == {"rows": 100, "unique_data_files": 2}
     with pytest.raises(AssertionError, match="expected=99"):
         validate_rows(t, 99)
