@@ -342,10 +342,15 @@ class Lease:
 
 
 class DataPipeline:
-    def __init__(self, cfg: PipelineConfig):
+    def __init__(self, cfg: PipelineConfig, *, lineage=None):
+        """``lineage``: an optional ``data.lineage.LineageRecorder``; every committed input is recorded
+        as read (``file``), every published window (``parquet``, version = window directory, publication
+        id = window id) and every Iceberg append (``iceberg``, version = snapshot id, publication id =
+        the input's commit id) as published, and the recorder is flushed at the end of ``run``."""
         self.cfg = cfg
         self.out = Path(cfg.output)
         self.proc = FeatureProcessor(cfg)
+        self.lineage = lineage
 
     def manifest(self) -> dict:
         p = self.out / MANIFEST
@@ -399,7 +404,12 @@ class DataPipeline:
                 f = self.out / w["dir"] / f"part-{i:05d}.parquet"
                 files.append(DataFile(str(f.absolute()), pq.ParquetFile(f).metadata.num_rows, f.stat().st_size))
         if files:
-            table.append(files, commit_id=commit_id)
+            snap = table.append(files, commit_id=commit_id)
+            if self.lineage is not None:
+                from .lineage import AssetRef
+
+                self.lineage.output_published([AssetRef("iceberg", table.location, str(snap["snapshot-id"]))],
+                                              commit_id)
 
     def run(self, workers: int = 1, *, audit_path: str | Path | None = None) -> dict:
         """Publish every input not yet in the manifest; ``workers > 1`` encodes in parallel processes.
@@ -418,7 +428,7 @@ class DataPipeline:
             if workers <= 1 or len(todo) <= 1:
                 for path in todo:
                     self._commit(man, path, encode_input(self.cfg, path, str(self.out)))
-                return man
+                return self._finished(man)
             import concurrent.futures as cf
             import multiprocessing as mp
 
@@ -448,9 +458,14 @@ class DataPipeline:
                     "max_worker_rss_bytes": max(m["max_rss_bytes"] for m in metrics),
                     "elapsed_before_commit": time.perf_counter() - t0,
                     "data_files": sum(w["parts"] for w in man["windows"] if w["input"] in rows)})
-            return man
+            return self._finished(man)
         finally:
             lease.release()
+
+    def _finished(self, man: dict) -> dict:
+        if self.lineage is not None:
+            self.lineage.flush()  # a failed export keeps the facts in the recorder and raises
+        return man
 
     def _commit(self, man: dict, path: str, windows: list[dict]) -> None:
         """Rename an input's encoded windows into place and record them (the input is done)."""
@@ -461,8 +476,17 @@ class DataPipeline:
             man["windows"].append({"id": wid, "dir": final.name, "parts": w["parts"], "rows": w["rows"],
                                    "input": path})
             write_json(self.out / MANIFEST, man)
+            if self.lineage is not None:
+                from .lineage import AssetRef
+
+                self.lineage.output_published([AssetRef("parquet", str(self.out.absolute()), final.name)],
+                                              f"window-{wid}")
         man["inputs_done"].append(path)
         write_json(self.out / MANIFEST, man)
+        if self.lineage is not None:
+            from .lineage import AssetRef
+
+            self.lineage.inputs_read([AssetRef("file", str(Path(path).absolute()))])
         if self.cfg.iceberg_table:
             self._commit_iceberg(man, path)
 
