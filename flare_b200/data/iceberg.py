@@ -496,8 +496,12 @@ class IcebergSourceFactory:
 
     def __init__(self, table: IcebergTable | str, *, mode: str = "pinned", snapshot_id: int | None = None,
                  after_snapshot_id: int | None = None, columns: Sequence[str] | None = None,
-                 rows_per_item: int | None = None, max_concurrency: int = 4):
+                 rows_per_item: int | None = None, max_concurrency: int = 4, cache=None):
+        """``cache``: a ``data.file_cache.LocalFileCache`` through which data files on an object store are
+        read (each downloaded once per node, identified by its path and size); local files are read in
+        place."""
         self.table = table if isinstance(table, IcebergTable) else IcebergTable.load(table)
+        self.cache = cache
         if mode not in ("pinned", "continuous"):
             raise ValueError("mode must be 'pinned' or 'continuous'")
         self.mode = mode
@@ -509,16 +513,18 @@ class IcebergSourceFactory:
         else:
             self.snapshot_id = self.cursor
             self.files = self.table.appended_files(after_snapshot_id, self.cursor) if self.cursor is not None else []
-        local = [self._local_path(f.path) for f in self.files]
+        local = [self._local_path(f) for f in self.files]
         self._parquet = ParquetSourceFactory(local, columns=columns, rows_per_item=rows_per_item,
                                              max_concurrency=max_concurrency) if local else None
 
-    def _local_path(self, p: str) -> str:
-        fs, inner, scheme = self.table.io.resolve(p)
-        if scheme != "file":
-            raise ValueError("reading Iceberg data files from an object store goes through a local cache; "
-                             f"got {p}")
-        return inner
+    def _local_path(self, f: DataFile) -> str:
+        fs, inner, scheme = self.table.io.resolve(f.path)
+        if scheme == "file":
+            return inner
+        if self.cache is None:
+            raise ValueError("reading Iceberg data files from an object store needs a local cache "
+                             f"(cache=LocalFileCache(...)); got {f.path}")
+        return self.cache.local_path(f.path, f"size={f.file_size_in_bytes}")
 
     def plan(self) -> list[WorkItem]:
         return self._parquet.plan() if self._parquet else []

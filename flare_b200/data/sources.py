@@ -184,10 +184,16 @@ class StandardSourceFactory:
             table = opts.pop("table", None)
             if not table:
                 raise ValueError("source option 'table' is required for iceberg")
-            allowed = {"mode", "snapshot_id", "after_snapshot_id", "columns", "rows_per_item", "max_concurrency"}
+            allowed = {"mode", "snapshot_id", "after_snapshot_id", "columns", "rows_per_item", "max_concurrency",
+                       "cache_bytes", "cache_dir"}
             unknown = set(opts) - allowed
             if unknown:
                 raise ValueError(f"unknown source options {sorted(unknown)}")
+            cache_bytes, cache_dir = opts.pop("cache_bytes", None), opts.pop("cache_dir", None)
+            if cache_bytes is not None:  # data files on an object store, read through a node-local cache
+                from .file_cache import LocalFileCache
+
+                opts["cache"] = LocalFileCache(int(cache_bytes), cache_dir)
             return IcebergSourceFactory(table, **opts)
         paths = opts.pop("paths", None)
         if not paths:
