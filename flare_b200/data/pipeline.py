@@ -421,6 +421,7 @@ class DataPipeline:
         lease = Lease(self.out, self.cfg.lease_seconds)
         lease.acquire()
         try:
+            self._check_catalog()
             self.reconcile()
             man = self.manifest()
             done = set(man["inputs_done"])
@@ -461,6 +462,19 @@ class DataPipeline:
             return self._finished(man)
         finally:
             lease.release()
+
+    def _check_catalog(self) -> None:
+        """Publish the output's feature catalog, or check that an existing one has this config's digest."""
+        from .feature_catalog import MANIFEST_NAME, FeatureCatalog, catalog_for
+
+        cat = catalog_for(self.cfg)
+        if (self.out / MANIFEST_NAME).exists():
+            have = FeatureCatalog.from_manifest_dir(self.out)
+            if have.config_digest != cat.config_digest:
+                raise ValueError(f"{self.out} holds features of another configuration (digest "
+                                 f"{have.config_digest[:12]}, this one {cat.config_digest[:12]})")
+        else:
+            cat.write_manifest(self.out)
 
     def _finished(self, man: dict) -> dict:
         if self.lineage is not None:

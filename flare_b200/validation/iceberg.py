@@ -9,6 +9,7 @@
   claims.
 
     python -m flare_b200.validation.iceberg schema TABLE_LOCATION --columns a,b,c [--codec ZSTD]
+    python -m flare_b200.validation.iceberg schema TABLE_LOCATION --manifest-dir PIPELINE_OUTPUT
     python -m flare_b200.validation.iceberg rows TABLE_LOCATION EXPECTED_ROWS
 
 Reference behaviour: tools/validation/validate_iceberg.py (the physical schema of every planned data
@@ -80,7 +81,10 @@ def main(argv=None) -> int:
     sub = ap.add_subparsers(dest="cmd", required=True)
     s = sub.add_parser("schema")
     s.add_argument("location")
-    s.add_argument("--columns", required=True, help="comma-separated names, or a file with one name per line")
+    g = s.add_mutually_exclusive_group(required=True)
+    g.add_argument("--columns", help="comma-separated names, or a file with one name per line")
+    g.add_argument("--manifest-dir", help="a directory with the feature pipeline's feature_manifest.json")
+    s.add_argument("--extra-columns", default="", help="columns the publisher adds beyond the catalog")
     s.add_argument("--codec", default=None)
     r = sub.add_parser("rows")
     r.add_argument("location")
@@ -88,7 +92,14 @@ def main(argv=None) -> int:
     args = ap.parse_args(argv)
     table = IcebergTable.load(args.location)
     if args.cmd == "schema":
-        out = validate_physical_schema(table, _columns(args.columns), codec=args.codec)
+        if args.manifest_dir:
+            from ..data.feature_catalog import FeatureCatalog
+
+            cols = list(FeatureCatalog.from_manifest_dir(args.manifest_dir).columns)
+        else:
+            cols = _columns(args.columns)
+        cols += [c for c in args.extra_columns.split(",") if c]
+        out = validate_physical_schema(table, cols, codec=args.codec)
         print(f"physical_schema_files={out['files']} columns={out['columns']} compression={out['codec'] or 'any'}")
     else:
         out = validate_rows(table, args.expected_rows)
