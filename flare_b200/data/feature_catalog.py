@@ -101,6 +101,27 @@ class FeatureCatalog:
             raise ValueError(f"feature name {name!r} is " + ("not declared" if not cols else f"ambiguous: {cols}"))
         return cols[0]
 
+    def table_specs(self, embedding_dim: int, *, columns=None, sizes=None, **spec_kwargs) -> list:
+        """One ``sparse.config.SparseTableSpec`` per sparse column (all of them, or ``columns``), named and
+        fed by the column, with the column's id space (``buckets``) as its rows; ``sizes`` gives the rows
+        of columns whose ids are not bucketed (an error names any column left without a size).  Further
+        keyword arguments go to every spec (pooling, optimizer, shards, ...)."""
+        from ..sparse.config import SparseTableSpec
+
+        sizes = dict(sizes or {})
+        wanted = list(columns) if columns is not None else [d.column for d in self.descriptors if d.kind == "sparse"]
+        specs = []
+        for c in wanted:
+            d = self.require(c)
+            if d.kind != "sparse":
+                raise ValueError(f"column {c!r} is a {d.kind} feature, not a sparse one")
+            rows = int(sizes.get(c, d.buckets))
+            if rows <= 0:
+                raise ValueError(f"sparse column {c!r} has no bounded id space: give its rows in sizes")
+            specs.append(SparseTableSpec(name=c, num_embeddings=rows, embedding_dim=embedding_dim, feature=c,
+                                         **spec_kwargs))
+        return specs
+
     def to_manifest(self) -> dict:
         return {"config_digest": self.config_digest, "features": [d.to_entry() for d in self.descriptors]}
 
@@ -147,8 +168,13 @@ def catalog_for(cfg) -> FeatureCatalog:
     for i, d in enumerate(cfg.dense):
         descs.append(FeatureDescriptor(f"d{i}", f"dense_{d.code}", "dense", d.transform, (d.code,)))
     for i, s in enumerate(cfg.sparse):
+        buckets = int(s.buckets)
+        if s.kind == "category":  # vocabulary indices and the default index
+            buckets = max([int(v) for v in dict(s.vocab).values()] + [int(s.default)]) + 1
+        elif s.kind == "intersect":  # raw ids shared by two lists: no bounded id space
+            buckets = 0
         descs.append(FeatureDescriptor(f"s{i}", f"{s.kind}_" + "_".join(str(c) for c in s.codes), "sparse", s.kind,
-                                       tuple(s.codes), int(s.buckets)))
+                                       tuple(s.codes), buckets))
     return FeatureCatalog(descs, config_digest=config_digest(cfg))
 
 

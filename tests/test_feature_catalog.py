@@ -55,3 +55,21 @@ def test_manifest_round_trip_and_validation(tmp_path):
         FeatureCatalog.from_manifest({"config_digest": "0" * 64, "features": [{"column": "a"}]})
     with pytest.raises(ValueError, match="not declared"):
         back.column_for("nope")
+
+
+def test_table_specs_from_the_catalog(tmp_path):
+    cfg = _run(tmp_path)
+    cat = FeatureCatalog.from_manifest_dir(tmp_path / "out")
+    specs = cat.table_specs(16, pooling="mean")
+    assert [(t.name, t.num_embeddings, t.feature, t.pooling) for t in specs] == [
+        ("s0", 1000, "s0", "mean"), ("s1", 500, "s1", "mean"), ("s2", 777, "s2", "mean")]
+    assert cat.table_specs(8, columns=["s1"], sizes={"s1": 64})[0].num_embeddings == 64
+    with pytest.raises(ValueError, match="not a sparse"):
+        cat.table_specs(8, columns=["d0"])
+    from test_pipeline import _cfg
+
+    inter = catalog_for(_cfg(tmp_path, sparse=({"kind": "intersect", "codes": (30, 31)},
+                                               {"kind": "category", "codes": (21,), "vocab": {"a": 0, "b": 4}})))
+    with pytest.raises(ValueError, match="no bounded id space"):
+        inter.table_specs(8)
+    assert inter.table_specs(8, sizes={"s0": 100})[1].num_embeddings == 5
