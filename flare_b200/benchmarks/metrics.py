@@ -10,7 +10,8 @@ scores, 0/1 labels (one column per target) and group ids.  Two ways of computing
   ``--device`` (the GPU sort kernels for CUDA tensors, the exact CPU reference otherwise);
 * for every P in ``--ranks``: P gloo ranks hold an equal share of the rows each and merge them
   exactly (``metrics.distributed.distributed_metrics``: one all-gather of packed (group, score,
-  positives, negatives) summaries per target), timed between barriers inside the ranks, slowest rank.
+  positives, negatives) summaries per target, or with ``--merge partitioned`` groups and score ranges
+  split over the ranks), timed between barriers inside the ranks, slowest rank.
 
 Each round visits the rank counts in alternating order so that no rank count always runs first
 (cold start); every run must see the same sample count and reach the local values (the merge is
@@ -79,7 +80,7 @@ def local_metrics(scores: torch.Tensor, labels: torch.Tensor, groups: torch.Tens
     return out
 
 
-def _rank_worker(rank: int, world: int, scores, labels, groups) -> dict:
+def _rank_worker(rank: int, world: int, scores, labels, groups, merge: str = "allgather") -> dict:
     """One rank's share of the window: merge with the others, timed between barriers."""
     import torch.distributed as dist
 
@@ -92,7 +93,7 @@ def _rank_worker(rank: int, world: int, scores, labels, groups) -> dict:
     t0 = time.perf_counter()
     out = {}
     for t in range(s.shape[1]):
-        m = distributed_metrics(s[:, t].contiguous(), y[:, t].contiguous(), g)
+        m = distributed_metrics(s[:, t].contiguous(), y[:, t].contiguous(), g, merge=merge)
         for k, v in m.items():
             out[f"{k}_{t}"] = v
     dist.barrier()
@@ -104,7 +105,7 @@ def _rank_worker(rank: int, world: int, scores, labels, groups) -> dict:
 
 def run(*, batches: int = 10, rows_per_batch: int = 20_000, targets: int = 3, group_cardinality: int = 20_000,
         ranks: tuple[int, ...] = (1, 2, 4), rounds: int = 2, device: str = "cpu", seed: int = 1,
-        timeout: float = 600.0) -> dict:
+        timeout: float = 600.0, merge: str = "allgather") -> dict:
     from ..runtime.launch import spawn_ranks
 
     counts = (batches, rows_per_batch, targets, group_cardinality, rounds, *ranks)
@@ -129,7 +130,7 @@ def run(*, batches: int = 10, rows_per_batch: int = 20_000, targets: int = 3, gr
     worst = 0.0
     for r in range(rounds):
         for p in (ranks if r % 2 == 0 else tuple(reversed(ranks))):
-            res = spawn_ranks(_rank_worker, p, scores, labels, groups, timeout=timeout)
+            res = spawn_ranks(_rank_worker, p, scores, labels, groups, merge, timeout=timeout)
             if any(x["samples"] != rows for x in res):
                 raise RuntimeError(f"{p} ranks saw {res[0]['samples']} samples, expected {rows}")
             per_p[p].append(max(x["seconds"] for x in res))
@@ -140,7 +141,7 @@ def run(*, batches: int = 10, rows_per_batch: int = 20_000, targets: int = 3, gr
         raise RuntimeError(f"merged metrics differ from the one-process values by {worst:g}")
     return {
         "samples": rows, "targets": targets, "group_cardinality": group_cardinality, "batches": batches,
-        "rounds": rounds, "device": str(dev),
+        "rounds": rounds, "device": str(dev), "merge": merge,
         "metrics": {k: v for k, v in ref.items()},
         "max_abs_diff_merged_vs_local": worst,
         "local": timing_summary(local_secs, rows),
@@ -159,11 +160,13 @@ def main(argv=None) -> int:
     ap.add_argument("--device", default="cuda" if torch.cuda.is_available() else "cpu",
                     help="device of the one-process computation")
     ap.add_argument("--seed", type=int, default=1)
+    ap.add_argument("--merge", choices=("allgather", "partitioned"), default="allgather",
+                    help="how the ranks merge their windows (metrics.distributed.distributed_metrics)")
     ap.add_argument("--output", type=Path)
     args = ap.parse_args(argv)
     summary = run(batches=args.batches, rows_per_batch=args.rows_per_batch, targets=args.targets,
                   group_cardinality=args.group_cardinality, ranks=tuple(int(x) for x in args.ranks.split(",") if x),
-                  rounds=args.rounds, device=args.device, seed=args.seed)
+                  rounds=args.rounds, device=args.device, seed=args.seed, merge=args.merge)
     text = json.dumps(summary, indent=2)
     if args.output is not None:
         args.output.parent.mkdir(parents=True, exist_ok=True)

@@ -157,6 +157,92 @@ def _max_scalar(val: float, group, device) -> float:
     return float(t.item())
 
 
+def _exchange_rows(rows: torch.Tensor, owner: torch.Tensor, group) -> torch.Tensor:
+    """Send each row of ``rows`` ([n, 4] float64) to rank ``owner[i]``; returns the rows this rank owns."""
+    W = _world(group)
+    home, dev = rows.device, _comm_device(group, rows)
+    order = torch.argsort(owner, stable=True)
+    rows, owner = rows[order].to(dev), owner[order]
+    send = torch.bincount(owner, minlength=W).to(torch.int64)
+    recv = torch.empty_like(send, device=dev)
+    dist.all_to_all_single(recv, send.to(dev), group=group)
+    send_l, recv_l = send.tolist(), recv.tolist()
+    out = torch.empty(sum(recv_l), 4, dtype=torch.float64, device=dev)
+    dist.all_to_all_single(out.view(-1), rows.reshape(-1), [4 * k for k in recv_l], [4 * k for k in send_l],
+                           group=group)
+    return out.to(home)
+
+
+def _rank_of(group) -> int:
+    return dist.get_rank(group) if _world(group) > 1 else 0
+
+
+def partitioned_gauc(summary: torch.Tensor, negative_factor: float = 0.0, group=None) -> float:
+    """Exact GAUC with the groups split over the ranks: group g is merged by rank g mod W only."""
+    W = _world(group)
+    if W == 1:
+        return gauc_from_summary(summary, negative_factor)
+    owner = torch.remainder(summary[:, 0].to(torch.int64), W)
+    mine = merge_summaries([_exchange_rows(summary, owner, group)])
+    num = den = 0.0
+    if mine.numel():
+        g, pos, neg = mine[:, 0], mine[:, 2], mine[:, 3]
+        start = torch.ones(g.numel(), dtype=torch.bool, device=g.device)
+        start[1:] = g[1:] != g[:-1]
+        gid = torch.cumsum(start.to(torch.int64), 0) - 1
+        G = int(gid[-1].item()) + 1
+        Pg = torch.zeros(G, dtype=torch.float64, device=g.device).index_add_(0, gid, pos)
+        Ng = torch.zeros(G, dtype=torch.float64, device=g.device).index_add_(0, gid, neg)
+        cneg = torch.cumsum(neg, 0)
+        base = (cneg - neg)[torch.nonzero(start).reshape(-1)]
+        below = cneg - neg - base[gid]
+        credit = torch.zeros(G, dtype=torch.float64, device=g.device).index_add_(0, gid, pos * (below + 0.5 * neg))
+        ok = (Pg > 0) & (Ng > 0)
+        w = Pg + negative_factor * Ng
+        num = float((credit[ok] / (Pg[ok] * Ng[ok]) * w[ok]).sum())
+        den = float(w[ok].sum())
+    num, den = _sum_scalars([num, den], group, summary.device)
+    return num / den if den else float("nan")
+
+
+def partitioned_auc(summary: torch.Tensor, group=None) -> float:
+    """Exact AUC with the score axis split into one range per rank.
+
+    Every rank proposes W - 1 quantiles of its own distinct scores; the sorted union's every W-th
+    value becomes a global splitter, so rank r owns the scores in [split[r-1], split[r]) and equal
+    scores always meet at one rank.  Each rank merges its range and credits its positives with the
+    negatives below them inside the range plus every negative held by the ranks of lower ranges."""
+    W = _world(group)
+    if W == 1:
+        return auc_from_summary(summary)
+    dev = summary.device
+    s = summary[:, 1].contiguous()
+    k = W - 1
+    if s.numel():
+        ss = torch.sort(s).values
+        q = ss[(torch.arange(1, k + 1, device=dev) * ss.numel()) // (k + 1)]
+    else:
+        q = torch.full((k,), float("inf"), dtype=torch.float64, device=dev)
+    cdev = _comm_device(group, q)
+    props = [torch.empty(k, dtype=torch.float64, device=cdev) for _ in range(W)]
+    dist.all_gather(props, q.to(cdev), group=group)
+    allq = torch.sort(torch.cat(props)).values.to(dev)  # W * (W - 1) proposals
+    split = allq[(torch.arange(1, W, device=dev) * allq.numel()) // W]
+    owner = torch.searchsorted(split, s, right=True)
+    folded = torch.cat([torch.zeros_like(s)[:, None], summary[:, 1:]], 1)
+    mine = merge_summaries([_exchange_rows(folded, owner, group)])
+    pos, neg = (mine[:, 2], mine[:, 3]) if mine.numel() else (torch.zeros(0, dtype=torch.float64, device=dev),) * 2
+    P_r, N_r = float(pos.sum()), float(neg.sum())
+    credit = float((pos * (torch.cumsum(neg, 0) - neg + 0.5 * neg)).sum()) if mine.numel() else 0.0
+    counts = torch.tensor([P_r, N_r], dtype=torch.float64, device=cdev)
+    every = [torch.empty(2, dtype=torch.float64, device=cdev) for _ in range(W)]
+    dist.all_gather(every, counts, group=group)
+    below = sum(float(every[r][1]) for r in range(_rank_of(group)))
+    credit += P_r * below
+    credit, P, N = _sum_scalars([credit, P_r, N_r], group, dev)
+    return credit / (P * N) if P and N else float("nan")
+
+
 def distributed_auc(scores: torch.Tensor, labels: torch.Tensor, group=None) -> float:
     """Exact AUC over the samples of every rank of ``group``."""
     return auc_from_summary(merge_summaries(all_gather_summaries(score_summary(scores, labels), group)))
@@ -175,8 +261,26 @@ def distributed_calibration(predictions: torch.Tensor, labels: torch.Tensor, gro
 
 
 def distributed_metrics(scores: torch.Tensor, labels: torch.Tensor, groups: torch.Tensor | None = None, *,
-                        negative_factor: float = 0.0, group=None) -> dict[str, float]:
-    """AUC, calibration (and GAUC with groups) of every rank's samples from one all-gather."""
+                        negative_factor: float = 0.0, group=None, merge: str = "allgather") -> dict[str, float]:
+    """AUC, calibration (and GAUC with groups) of every rank's samples.
+
+    ``merge="allgather"`` (default): every rank gathers every summary and merges the whole window
+    (one collective; every rank holds all W summaries).  ``merge="partitioned"``: the groups and the
+    score ranges are split over the ranks (``partitioned_gauc`` / ``partitioned_auc``), so each rank
+    holds and merges about 1/W of the window, for windows too large to gather on every rank; it pays
+    two all-to-alls per metric, which on CPU gloo ranks cost more than the all-gather at 200K-row
+    windows (``benchmarks.metrics --merge``).  Both are exact."""
+    if merge not in ("allgather", "partitioned"):
+        raise ValueError(f"merge must be 'allgather' or 'partitioned', got {merge!r}")
+    if merge == "partitioned" and _world(group) > 1:
+        summ = score_summary(scores, labels, groups)
+        out = {"auc": partitioned_auc(summ, group)}
+        p_sum, y_sum = _sum_scalars([float(scores.double().sum()), float(labels.double().sum())], group,
+                                    scores.device)
+        out["calibration"] = p_sum / y_sum if y_sum else float("nan")
+        if groups is not None:
+            out["gauc"] = partitioned_gauc(summ, negative_factor, group)
+        return out
     merged = merge_summaries(all_gather_summaries(score_summary(scores, labels, groups), group))
     out = {"auc": auc_from_summary(merged)}
     p_sum, y_sum = _sum_scalars([float(scores.double().sum()), float(labels.double().sum())], group, scores.device)
@@ -187,4 +291,4 @@ def distributed_metrics(scores: torch.Tensor, labels: torch.Tensor, groups: torc
 
 
 __all__ = ["all_gather_summaries", "auc_from_summary", "distributed_auc", "distributed_calibration",
-           "distributed_gauc", "distributed_metrics", "gauc_from_summary", "merge_summaries", "score_summary"]
+           "distributed_gauc", "distributed_metrics", "gauc_from_summary", "merge_summaries", "partitioned_auc", "partitioned_gauc", "score_summary"]
