@@ -87,10 +87,13 @@ class TensorBoardSink:
 class TrainMetricsWindow:
     def __init__(self, targets: tuple[str, ...] = ("ctr",), window_steps: int = 100, capacity: int = 1 << 22,
                  device: torch.device | None = None, sinks: list | None = None, negative_factor: float = 0.0,
-                 distributed: bool | None = None, group=None, background: bool = False, max_pending: int = 2):
+                 distributed: bool | None = None, group=None, background: bool = False, max_pending: int = 2,
+                 merge: str = "allgather"):
         """``distributed``: merge every rank's window into one exact AUC / GAUC / calibration / loss /
         throughput (default: when a process group of more than one rank is up).  Every rank must then
-        call ``update`` for the same steps, since the flush is a collective.
+        call ``update`` for the same steps, since the flush is a collective.  ``merge`` picks how the
+        ranks' windows are merged (``metrics.distributed.distributed_metrics``: ``"allgather"``, or
+        ``"partitioned"`` for windows too large to hold on every rank).
 
         ``background`` (rank-local windows): a finished window is copied on the device and its metrics
         are computed by one worker thread while training goes on; at most ``max_pending`` windows wait
@@ -99,8 +102,11 @@ class TrainMetricsWindow:
         for all of them.  Reference behaviour: bounded background pending windows of the train
         metrics aggregator (recipes/recsys/ranking/metrics/train_metrics.py:127-326)."""
         self.targets = targets
+        if merge not in ("allgather", "partitioned"):
+            raise ValueError(f"merge must be 'allgather' or 'partitioned', got {merge!r}")
         self.group = group
         self.distributed = distributed
+        self.merge = merge
         self.window_steps = window_steps
         self.device = device or torch.device("cpu")
         T = len(targets)
@@ -155,7 +161,7 @@ class TrainMetricsWindow:
             grouped = self.has_groups
             for t, name in enumerate(self.targets):
                 m = distributed_metrics(self.scores[:n, t], self.labels[:n, t], self.groups[:n] if grouped else None,
-                                        negative_factor=self.negative_factor, group=self.group)
+                                        negative_factor=self.negative_factor, group=self.group, merge=self.merge)
                 for k, v in m.items():
                     out[f"train/{k}_{name}"] = v
             elapsed = self.window.elapsed()
