@@ -315,30 +315,48 @@ def load_category_values(category_files: dict[str, str], category_dir: str | Pat
 
 # ------------------------------------------------------------------ publication state
 class Lease:
-    """Exclusive publisher lease on an output directory (owner + expiry; a stale lease is taken over)."""
+    """Exclusive publisher lease on an output directory (owner + expiry; a stale lease is taken over).
+
+    Every decision (acquire, renew, release) reads and writes the lease file under an exclusive
+    ``flock`` on ``_lease.lock`` in the output directory, so of several publishers that find the same
+    stale lease exactly one takes it over."""
 
     def __init__(self, out: Path, seconds: float):
         self.path = out / LEASE
         self.owner = f"{socket.gethostname()}:{os.getpid()}:{uuid.uuid4().hex[:8]}"
         self.seconds = seconds
 
+    def _locked(self, fn):
+        import fcntl
+
+        with open(self.path.with_name(LEASE + ".lock"), "a+b") as lock:
+            fcntl.flock(lock, fcntl.LOCK_EX)
+            try:
+                return fn(read_json(self.path) if self.path.exists() else None)
+            finally:
+                fcntl.flock(lock, fcntl.LOCK_UN)
+
     def acquire(self) -> None:
-        body = {"owner": self.owner, "expires": time.time() + self.seconds}
-        try:
-            write_json(self.path, body, exclusive=True)
-            return
-        except FileExistsError:
-            cur = read_json(self.path)
-            if cur.get("expires", 0) > time.time():
+        def take(cur):
+            if cur is not None and cur.get("owner") != self.owner and cur.get("expires", 0) > time.time():
                 raise RuntimeError(f"output is leased by {cur.get('owner')} until {cur.get('expires')}")
-        write_json(self.path, body)  # expired: take over
+            write_json(self.path, {"owner": self.owner, "expires": time.time() + self.seconds})
+        self._locked(take)
+
+    def renew(self) -> None:
+        """Extend the expiry of a lease this publisher still owns (called at every commit)."""
+        def extend(cur):
+            if cur is None or cur.get("owner") != self.owner:
+                raise RuntimeError(f"the lease on {self.path.parent} was taken over by "
+                                   f"{cur.get('owner') if cur else 'nobody (released)'}")
+            write_json(self.path, {"owner": self.owner, "expires": time.time() + self.seconds})
+        self._locked(extend)
 
     def release(self) -> None:
-        try:
-            if read_json(self.path).get("owner") == self.owner:
-                self.path.unlink()
-        except FileNotFoundError:
-            pass
+        def drop(cur):
+            if cur is not None and cur.get("owner") == self.owner:
+                self.path.unlink(missing_ok=True)
+        self._locked(drop)
 
 
 class DataPipeline:
@@ -420,6 +438,7 @@ class DataPipeline:
         self.out.mkdir(parents=True, exist_ok=True)
         lease = Lease(self.out, self.cfg.lease_seconds)
         lease.acquire()
+        self._lease = lease
         try:
             self._check_catalog()
             self.reconcile()
@@ -483,6 +502,9 @@ class DataPipeline:
 
     def _commit(self, man: dict, path: str, windows: list[dict]) -> None:
         """Rename an input's encoded windows into place and record them (the input is done)."""
+        lease = getattr(self, "_lease", None)
+        if lease is not None:
+            lease.renew()  # a long run keeps its lease; a publisher that lost it stops before publishing
         for w in windows:
             wid = len(man["windows"])
             final = self.out / f"window-{wid:06d}"

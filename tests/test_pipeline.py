@@ -88,6 +88,35 @@ def test_lease_blocks_second_publisher(tmp_path):
     b.release()
 
 
+def test_stale_lease_takeover_has_one_winner_and_renewal_detects_loss(tmp_path):
+    import threading
+
+    out = tmp_path / "o"
+    out.mkdir()
+    old = Lease(out, -1.0)  # already expired: a crashed publisher's lease
+    old.acquire()
+    contenders = [Lease(out, 60) for _ in range(8)]
+    won, barrier = [], threading.Barrier(len(contenders))
+
+    def take(lease):
+        barrier.wait()
+        try:
+            lease.acquire()
+            won.append(lease)
+        except RuntimeError:
+            pass
+
+    threads = [threading.Thread(target=take, args=(c,)) for c in contenders]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert len(won) == 1
+    won[0].renew()  # still the owner
+    with pytest.raises(RuntimeError, match="taken over"):
+        old.renew()
+
+
 def test_cli(tmp_path, capsys):
     (tmp_path / "logs").mkdir()
     _write_logs(tmp_path / "logs" / "a.txt", 50, 2)
